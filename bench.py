@@ -1,0 +1,354 @@
+"""Benchmark: plans/sec and p50 plan latency of the LeWM iCEM planning hot path.
+
+Workload (one "step" = one full iCEM plan for one env on each GPU):
+  LeWM predictor (width 192, 6 layers, 16 heads x 64, MLP 4x, AdaLN-zero action
+  conditioning, action dim 2 x frameskip 5 = 10), horizon 5, history 1, bucketed
+  iCEM 300 -> 60 samples over 30 iterations (2820 model-cost evaluations), 30
+  elites, brown colored noise (beta 2) over raw time, elite retention 3 (10% of
+  30), bf16 rollout with fp32 costs / ranking, in-kernel Philox noise.
+  Synthetic random-init weights and N(0,1) latents (no checkpoint / dataset).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Multi-GPU: one process per GPU (torchrun); each rank plans its own env (weak
+scaling, no collective on the plan path); time is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import platform
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "plans/sec and p50 plan latency (ms), 300-sample iCEM H=5"
+WORKLOAD = "icem_bucketed_300_1env_bf16"
+# Canonical algorithmic FLOPs per candidate (width 192, 6 layers, H=1, T=5): new window
+# tokens 1+1+1+3+3 = 9 through the 6 blocks, AdaLN for 5 action tokens x 6 layers,
+# Embedder for 5 action tokens.
+D, L, INNER, MLP, A, T = 192, 6, 1024, 768, 10, 5
+F_BLOCK_TOKEN = 2 * (D * 3 * INNER + INNER * D + 2 * D * MLP)  # per token per layer
+F_CANON = 9 * L * F_BLOCK_TOKEN + T * L * 2 * D * 6 * D + T * 2 * (A * A + A * 4 * D + 4 * D * D)
+
+
+def percentile(values, q):
+    """Interpolated percentile (reference tools/benchmarks/metrics.py:64-76)."""
+    xs = sorted(values)
+    if not xs:
+        return None
+    pos = (len(xs) - 1) * q / 100.0
+    lo, hi = int(np.floor(pos)), int(np.ceil(pos))
+    return xs[lo] + (xs[hi] - xs[lo]) * (pos - lo)
+
+
+def plan_options():
+    from lewm_flash_b200.runtime import PlanOptions
+
+    return PlanOptions(num_samples=300, topk=30, n_steps=30, sample_decay=1.25, sample_count_bucket_size=60,
+                       elite_retention=3, beta=2.0, time_axis="raw", action_block=5, seed=0)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                for line in out.stdout.strip().splitlines():
+                    self.rows.append([x.strip() for x in line.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        sms, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sms.append(float(r[1]))
+                mx = float(r[2])
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() in ("active", "1", "yes"):
+                        reasons.add(n)
+            except Exception:
+                continue
+        return {"sm_mhz": percentile(sms, 50) if sms else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+def l2_flush(buf):
+    buf.add_(1.0)  # write 256 MiB (> 126 MB L2) between timed plans
+
+
+def cpu_info():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return platform.processor()
+
+
+def run_cpu_plan(n_plans: int):
+    """The oracle port (numpy) of the reference iCEM chain, on the host cores."""
+    from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
+    from oracle import icem_oracle as io
+    from oracle import lewm_oracle as lo
+
+    desc = ModelDesc()
+    sd = synthetic_state_dict(desc, 0)
+    rng = np.random.default_rng(0)
+    emb = rng.standard_normal((1, 1, desc.dim)).astype(np.float32)
+    goal = rng.standard_normal((1, 1, desc.dim)).astype(np.float32)
+    counts = io.sample_counts(30, 300, 30, 1.25, 60)
+    times = []
+    for _ in range(n_plans):
+        white = [rng.standard_normal((1, c, 2, 25)) for c in counts]
+        noise = [io.color_white_noise(w, 5, 10, 2.0, 5, "raw") for w in white]
+        mean = np.zeros((1, 5, 10), np.float32)
+        var = np.ones_like(mean)
+        t0 = time.perf_counter()
+        io.run_static_icem_chain(lambda e, g, c: lo.get_cost_from_embeddings(e, g, c, sd, desc), emb, goal, mean,
+                                 var, noise, topk=30, elite_retention=3)
+        times.append(time.perf_counter() - t0)
+    return times
+
+
+def reference_arm(args, rank, world):
+    """--impl reference: the reference algorithm's CPU implementation (numpy oracle port) on host cores."""
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    run_cpu_plan(1) if args.warmup > 0 else None
+    times = run_cpu_plan(max(args.steps, 1))
+    per = float(np.mean(times))
+    value = 1.0 / per
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "plans/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3,
+        "p50_plan_ms": percentile([t * 1e3 for t in times], 50), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "envs_per_gpu": 1, "candidates_per_plan": 2820},
+        "cpu_baseline": {"value": value, "unit": "plans/s", "cores": threads, "kind": "port",
+                         "sample": f"{len(times)} full plans (2820 candidates each) on {cpu_info()}"},
+        "e2e": {"value": value, "unit": "plans/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-baseline-plans", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+    if args.warmup < 3:
+        print("warmup must be >= 3", file=sys.stderr)
+        return 2
+
+    import torch
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    from lewm_flash_b200 import _lib
+    from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
+    from lewm_flash_b200.runtime import Runtime
+    from lewm_flash_b200.solver import B200ICEMSolver
+
+    desc = ModelDesc()
+    rt = Runtime(desc, synthetic_state_dict(desc, 0), dev)
+    opts = plan_options()
+    rng = np.random.default_rng(100 + rank)
+    emb = torch.as_tensor(rng.standard_normal((1, 1, desc.dim)), dtype=torch.float32, device=dev)
+    goal = torch.as_tensor(rng.standard_normal((1, 1, desc.dim)), dtype=torch.float32, device=dev)
+    mean = torch.zeros(1, 5, 10, device=dev)
+    std = torch.ones(1, 5, 10, device=dev)
+    flush = torch.zeros(64 * 1024 * 1024, device=dev)  # 256 MiB
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    # ---------------------------------------------------------------- device-resident plans
+    for i in range(args.warmup):
+        rt.plan(opts, emb, goal, mean, std, plan_index=i)
+    rt.sync()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        t_all0 = torch.cuda.Event(enable_timing=True)
+        t_all1 = torch.cuda.Event(enable_timing=True)
+        t_all0.record(stream)
+        for i in range(args.steps):
+            l2_flush(flush)
+            ev[i][0].record(stream)
+            rt.plan(opts, emb, goal, mean, std, plan_index=1000 + i)
+            ev[i][1].record(stream)
+        t_all1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    rt.sync()
+    plan_ms = [a.elapsed_time(b) for a, b in ev]
+    busy_ms = float(sum(plan_ms))
+    worst = torch.tensor([busy_ms], device=dev)
+    if dist is not None:
+        dist.all_reduce(worst, op=dist.ReduceOp.MAX)
+    worst_ms = float(worst.item())
+    value = world * args.steps / (worst_ms / 1e3)
+    p50 = percentile(plan_ms, 50)
+
+    # ---------------------------------------------------------------- per-kernel-class timing pass
+    kinfo = kernel_class_pass(rt, opts, emb, goal, mean, std, dev)
+
+    # ---------------------------------------------------------------- end to end through the solver API
+    solver = B200ICEMSolver(rt, num_samples=300, n_steps=30, topk=30, elite_retention=3, colored_noise="brown",
+                            colored_noise_time="raw", sample_decay=1.25, sample_count_bucket_size=60, seed=0,
+                            device=dev)
+
+    class Box:
+        shape = (1, 2)
+        low = -np.ones((1, 2), np.float32)
+        high = np.ones((1, 2), np.float32)
+
+    class Cfg:
+        horizon, action_block = 5, 5
+
+    solver.configure(action_space=Box(), n_envs=1, config=Cfg())
+    host_emb = emb.cpu().pin_memory()
+    host_goal = goal.cpu().pin_memory()
+    info = {"emb": host_emb, "goal_emb": host_goal}
+    for _ in range(args.warmup):
+        solver.solve(info)
+    barrier()
+    e2e_ms = []
+    for i in range(args.steps):
+        l2_flush(flush)
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        out = solver.solve(info)  # H2D of emb/goal/mean/var, plan, D2H of actions/var/costs
+        e2e_ms.append((time.perf_counter() - t0) * 1e3)
+    worst_e2e = torch.tensor([sum(e2e_ms)], device=dev)
+    if dist is not None:
+        dist.all_reduce(worst_e2e, op=dist.ReduceOp.MAX)
+    e2e_value = world * args.steps / (float(worst_e2e.item()) / 1e3)
+    h2d = host_emb.numel() * 4 + host_goal.numel() * 4 + 2 * 5 * 10 * 4
+    d2h = out["actions"].numel() * 4 + out["var"][0].numel() * 4 + len(out["costs"]) * 4
+
+    per_plan_launches = kinfo["launches_per_plan"]
+    flops_plan = F_CANON * 2820
+    line = {
+        "metric": METRIC, "value": value, "unit": "plans/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": worst_ms / args.steps, "p50_plan_ms": p50,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights, N(0,1) latents)",
+        "config": {"workload": WORKLOAD, "envs_per_gpu": 1, "candidates_per_plan": 2820, "horizon": 5,
+                   "history": 1, "topk": 30, "iterations": 30, "colored_noise": "brown/raw", "elite_retention": 3,
+                   "width": 192, "layers": 6, "parallelism": f"env-sharded x{world}, no collective",
+                   "l2": "256 MiB write between timed plans"},
+        "e2e": {"value": e2e_value, "unit": "plans/s", "p50_ms": percentile(e2e_ms, 50),
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                "api": "B200ICEMSolver.solve with pinned host emb/goal"},
+        "gpu_launches": int(per_plan_launches * args.steps),
+        "plan_roofline": {"bound": "tensor", "achieved": flops_plan / (p50 / 1e3) / 1e12,
+                          "peak": kinfo["peak"], "unit": "TFLOP/s",
+                          "frac": flops_plan / (p50 / 1e3) / 1e12 / kinfo["peak"],
+                          "flops_per_plan": flops_plan},
+        "roofline": kinfo["roofline"],
+        "kernel_classes": kinfo["classes"],
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        times = run_cpu_plan(max(args.cpu_baseline_plans, 1))
+        line["cpu_baseline"] = {"value": 1.0 / float(np.mean(times)), "unit": "plans/s",
+                                "cores": os.cpu_count() or 1, "kind": "port",
+                                "sample": f"{len(times)} full plans (2820 candidates) of the numpy oracle port "
+                                          f"on {cpu_info()}"}
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    rt.close()
+    return 0
+
+
+def kernel_class_pass(rt, opts, emb, goal, mean, std, dev):
+    """Untimed pass: per-kernel-class device time of one plan via the library's event profiler."""
+    import ctypes as C
+
+    import torch
+
+    from lewm_flash_b200 import _lib
+
+    peaks = {}
+    try:
+        peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    peak_kind = "measured" if "bf16_tflops" in peaks else "fallback"
+    res = rt.profile_plan(opts, emb, goal, mean, std)
+    classes = res["classes"]
+    top = max(classes, key=lambda k: classes[k]["ms"])
+    c = classes[top]
+    achieved = c["flops"] / (c["ms"] / 1e3) / 1e12 if c["ms"] > 0 else 0.0
+    roof = {"kernel": top, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
+            "method": "CUDA events around every launch of this class in an untimed plan; "
+                      "algorithmic FLOPs = valid rows x GEMM shape"}
+    return {"roofline": roof, "classes": classes, "launches_per_plan": res["launches"], "peak": peak}
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,198 @@
+/*
+ * lewm_b200.h -- C ABI of the B200 (sm_100a) LeWM iCEM planning hot path.
+ *
+ * Plain pointers and sizes only. Every tensor pointer is a CUDA device pointer
+ * on the context's device unless a comment says otherwise; float tensors are
+ * contiguous row-major float32. Calls are asynchronous on the given stream
+ * (a cudaStream_t passed as void*; NULL = legacy default stream) and the
+ * caller owns every buffer. One context per device; a context is not
+ * thread-safe without external locking.
+ *
+ * The reference (antoinenguyen27/lewm-flash) is pure PyTorch and has no FFI;
+ * each entry point below replaces one Python interface of its planning path,
+ * cited as file:line in that project.
+ */
+#ifndef LEWM_B200_H
+#define LEWM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LEWM_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define LEWM_API __attribute__((visibility("default")))
+#else
+#define LEWM_API
+#endif
+
+typedef enum lewm_status {
+  LEWM_OK = 0,
+  LEWM_INVALID_ARG = 1,       /* bad pointer, size or option (reference: ValueError) */
+  LEWM_UNSUPPORTED_SHAPE = 2, /* a model / plan shape the kernels are not built for */
+  LEWM_DEVICE_TIMEOUT = 3,    /* a bounded device-side wait expired */
+  LEWM_NUMERIC_NAN = 4,       /* NaN in a plan's final costs */
+  LEWM_CUDA_ERROR = 5,        /* CUDA runtime error; see lewm_last_error */
+  LEWM_OUT_OF_MEMORY = 6
+} lewm_status;
+
+typedef struct lewm_ctx lewm_ctx;
+
+/* Predictor + action-encoder shape (reference lewm/module.py:189-285).
+ * Supported: dim in {192, 384}, dim_head == 64, heads <= 16, mlp_dim and
+ * embed_hidden multiples of 128, action_dim and smoothed_dim <= 16,
+ * num_frames <= 8, pred_proj_hidden == 0 (Identity head). */
+typedef struct lewm_model_desc {
+  int32_t dim;
+  int32_t depth;
+  int32_t heads;
+  int32_t dim_head;
+  int32_t mlp_dim;
+  int32_t action_dim;
+  int32_t smoothed_dim;
+  int32_t embed_hidden;
+  int32_t num_frames;
+  int32_t pred_proj_hidden; /* 0: Identity */
+  int32_t pred_proj_norm;   /* 0 none, 1 LayerNorm, 2 BatchNorm1d (eval) */
+} lewm_model_desc;
+
+/* Number of float32 values lewm_create expects for `desc`. The weights are the
+ * reference JEPA state-dict tensors (predictor.*, action_encoder.*, pred_proj.*)
+ * concatenated in this order, each row-major:
+ *   predictor.pos_embedding
+ *   for each layer l: adaLN_modulation.1.weight, .bias, attn.norm.weight, .bias,
+ *     attn.to_qkv.weight, attn.to_out.0.weight, .bias, mlp.net.0.weight, .bias,
+ *     mlp.net.1.weight, .bias, mlp.net.4.weight, .bias
+ *   transformer.norm.weight, .bias
+ *   action_encoder.patch_embed.weight, .bias, embed.0.weight, .bias, embed.2.weight, .bias
+ * (host memory). */
+LEWM_API size_t lewm_weight_count(const lewm_model_desc* desc);
+
+/* Build a context on `device`: validates `desc`, packs `weights` (HOST float32,
+ * `n_floats` values, lewm_weight_count order) into bf16 tensor-core tiles and
+ * uploads them. Replaces loading the reference JEPA predictor onto the GPU
+ * (reference tools/benchmarks/lewm_plan_benchmark.py:1855-1857). */
+LEWM_API lewm_status lewm_create(lewm_ctx** out, const lewm_model_desc* desc, const float* weights, size_t n_floats,
+                        int device);
+LEWM_API void lewm_destroy(lewm_ctx* ctx);
+/* Message of the last failing call on `ctx` ("" if none). NULL ctx: last lewm_create failure. */
+LEWM_API const char* lewm_last_error(const lewm_ctx* ctx);
+
+/* Terminal latent cost of each action candidate.
+ * Replaces JEPA.get_cost_from_embeddings(emb, goal_emb, action_candidates, history_size)
+ * (reference lewm/jepa.py:302-317), i.e. rollout_from_embeddings (:262-300) and
+ * cost_from_rollout (:246-260), computed with bf16 tensor-core GEMMs and fp32
+ * norms/residuals/cost.
+ *   emb   (B,H,D) if emb_per_sample == 0, else (B,S,H,D)
+ *   goal  (B,D)   if goal_per_sample == 0, else (B,S,D): the last goal row
+ *   cand  (B,S,T,A)
+ *   costs_out (B,S)
+ * 1 <= H <= T, 1 <= history_size <= num_frames. */
+LEWM_API lewm_status lewm_model_cost(lewm_ctx* ctx, const float* emb, int32_t emb_per_sample, int32_t H, const float* goal,
+                            int32_t goal_per_sample, const float* cand, int32_t B, int32_t S, int32_t T,
+                            int32_t history_size, float* costs_out, void* stream);
+
+/* iCEM solver options (reference ICEMSolver.__init__, lewm/solvers/icem.py:258-322). */
+typedef struct lewm_plan_desc {
+  int32_t n_envs;           /* B */
+  int32_t horizon;          /* T */
+  int32_t history;          /* H (rows of emb per env) */
+  int32_t history_size;     /* predictor window (JEPA default 3) */
+  int32_t num_samples;      /* S */
+  int32_t topk;             /* k */
+  int32_t n_steps;          /* iCEM iterations */
+  float sample_decay;       /* >= 1 */
+  int32_t bucket;           /* sample_count_bucket_size >= 0 */
+  int32_t elite_retention;  /* >= 0 */
+  float beta;               /* colored-noise exponent: 0 white, 1 pink, 2 brown */
+  int32_t time_axis_raw;    /* 1: color over horizon*action_block raw steps; 0: over horizon */
+  int32_t action_block;     /* >= 1 */
+  float momentum_alpha;     /* [0, 1) */
+  int32_t return_best_elite;
+  int32_t clip_actions;     /* clamp to action_low/high */
+  uint64_t seed;            /* Philox key word 0 */
+  uint64_t plan_index;      /* Philox key word 1: a new stream per plan call */
+} lewm_plan_desc;
+
+/* Per-iteration device outputs for solver callbacks / debugging (any may be NULL).
+ * i = iteration, S = num_samples (rows past the iteration's sample count are unset). */
+typedef struct lewm_plan_trace {
+  float* costs;       /* [n_steps][B][S] */
+  int32_t* topk_idx;  /* [n_steps][B][k] ascending cost */
+  float* topk_val;    /* [n_steps][B][k] */
+  float* mean;        /* [n_steps][B][T][A] after refit */
+  float* std;         /* [n_steps][B][T][A] after refit */
+  float* candidates;  /* [n_steps][B][S][T][A] */
+} lewm_plan_trace;
+
+/* Sample counts of every iteration (reference ICEMSolver.sample_counts,
+ * lewm/solvers/icem.py:377-394). Writes min(n_steps, cap) counts; returns the
+ * total model-cost evaluations per env in *evals_out (may be NULL). HOST memory. */
+LEWM_API lewm_status lewm_sample_counts(const lewm_plan_desc* plan, int32_t* counts_out, int32_t cap, int64_t* evals_out);
+
+/* One full iCEM solve for B independent envs, with no host round trip.
+ * Replaces the per-env-batch iteration loop of ICEMSolver.solve
+ * (lewm/solvers/icem.py:501-588) and the tensor-only run_static_icem_chain
+ * (lewm/solvers/icem_static_compile.py:61-114).
+ *   emb (B,H,D), goal (B,D), init_mean/init_std (B,T,A)
+ *   noise_steps: NULL -> in-kernel Philox colored noise; else n_steps device
+ *     pointers (a HOST array of device pointers), step i of shape
+ *     (B, counts[i], T, A): the reference's post-coloring noise ("injection mode")
+ *   action_low/high (A) device, used when clip_actions
+ *   actions_out (B,T,A): final mean, or the best elite if return_best_elite
+ *   std_out (B,T,A), final_cost_out (B): mean of the last top-k costs
+ *   trace: optional per-iteration outputs. */
+LEWM_API lewm_status lewm_plan(lewm_ctx* ctx, const lewm_plan_desc* plan, const float* emb, const float* goal,
+                      const float* init_mean, const float* init_std, const float* const* noise_steps,
+                      const float* action_low, const float* action_high, float* actions_out, float* std_out,
+                      float* final_cost_out, const lewm_plan_trace* trace, void* stream);
+
+/* One elite selection + refit step on given costs (reference
+ * lewm/solvers/icem.py:543-563, lewm/solvers/icem_static_compile.py:95-107).
+ *   costs (B,S), cand (B,S,T,A), mean/std (B,T,A) updated in place,
+ *   topk_idx (B,k) / topk_val (B,k) ascending (ties: lower index), best (B,T,A),
+ *   final_cost (B). */
+LEWM_API lewm_status lewm_topk_refit(lewm_ctx* ctx, const float* costs, const float* cand, int32_t B, int32_t S, int32_t T,
+                            int32_t A, int32_t k, float momentum_alpha, float* mean, float* std, int32_t* topk_idx,
+                            float* topk_val, float* best, float* final_cost, void* stream);
+
+/* Candidate sampling alone (tests / diagnostics): candidates of iteration
+ * `iter` for the given mean/std, no elite injection. Reference
+ * make_colored_noise (lewm/solvers/icem.py:185-250) + :523-527.
+ * out (B,S,T,A). */
+LEWM_API lewm_status lewm_sample_candidates(lewm_ctx* ctx, const lewm_plan_desc* plan, int32_t S, int32_t iter,
+                                   const float* mean, const float* std, const float* injected_noise,
+                                   const float* action_low, const float* action_high, float* out, void* stream);
+
+/* The real n x n matrix W with irfft(rfft(x) * scale, n) == W x, scale_f = (f/n)^(-beta/2),
+ * scale_0 = scale_1: the temporal coloring of _colored_noise_along_time
+ * (lewm/solvers/icem.py:173-182) as a matrix. HOST memory, row-major. */
+LEWM_API lewm_status lewm_coloring_matrix(int32_t n, double beta, double* out);
+
+/* Kernel classes reported by lewm_profile_plan, in array order. */
+#define LEWM_KERNEL_CLASSES 9 /* embed, adaln, qkv_attn, out_proj, fc1, fc2, final, sample, refit */
+
+/* Run one plan (in-kernel noise) with a CUDA event pair around every kernel
+ * launch, synchronize, and report per kernel class: summed device ms,
+ * algorithmic FLOPs (valid rows x GEMM shape) and launch count. HOST output
+ * arrays of LEWM_KERNEL_CLASSES entries. Diagnostics only: the events
+ * serialize launches, so use lewm_plan for timing whole plans. No reference
+ * counterpart (the reference profiles with torch.profiler,
+ * tools/benchmarks/lewm_plan_benchmark.py:1455-1475). */
+LEWM_API lewm_status lewm_profile_plan(lewm_ctx* ctx, const lewm_plan_desc* plan, const float* emb, const float* goal,
+                                       const float* init_mean, const float* init_std, double* ms_out,
+                                       double* flops_out, int32_t* launches_out, void* stream);
+
+/* Synchronize `stream`, then read and clear the device status word of `ctx`
+ * (LEWM_DEVICE_TIMEOUT if any bounded wait expired since the last call). */
+LEWM_API lewm_status lewm_sync_status(lewm_ctx* ctx, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LEWM_B200_H */

@@ -1,0 +1,24 @@
+"""B200-native LeWM iCEM planning hot path.
+
+Public surface (drop-ins for the reference antoinenguyen27/lewm-flash):
+
+* ``B200ICEMSolver`` -- ``lewm.solvers.icem.ICEMSolver``
+* ``B200CEMSolver`` -- ``lewm.solvers.cem_exact.CEMExactSolver``
+* ``run_static_icem_chain`` -- ``lewm.solvers.icem_static_compile.run_static_icem_chain``
+* ``B200ModelCost`` / ``install_model_cost`` -- ``JEPA.get_cost_from_embeddings``
+* ``Runtime`` -- the C ABI (``include/lewm_b200.h``) on one GPU
+
+The compute path is ``liblewm_b200.so`` (sm_100a CUDA); there is no CPU
+fallback.
+"""
+
+from .model import ModelDesc, STRESS_DESC, synthetic_state_dict
+from .runtime import PlanOptions, Runtime, coloring_matrix, sample_counts
+from .solver import (B200CEMSolver, B200ICEMSolver, B200ModelCost, install_model_cost, prepare_init_action,
+                     run_static_icem_chain)
+
+__all__ = [
+    "ModelDesc", "STRESS_DESC", "synthetic_state_dict", "PlanOptions", "Runtime", "coloring_matrix", "sample_counts",
+    "B200ICEMSolver", "B200CEMSolver", "B200ModelCost", "install_model_cost", "prepare_init_action",
+    "run_static_icem_chain",
+]

@@ -1,0 +1,827 @@
+// C ABI of the LeWM iCEM hot path: argument checks, weight packing, workspace
+// management and the launch sequence of one model-cost call / one plan.
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/lewm_b200.h"
+#include "lewm_internal.h"
+
+using namespace lewm;
+
+namespace {
+
+thread_local std::string g_create_error;
+
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+uint16_t f2bf(float f) {  // round to nearest even
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fc0;
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return static_cast<uint16_t>(u >> 16);
+}
+
+uint32_t sw128(uint32_t r, uint32_t k) { return r * 128u + ((((k >> 3) ^ (r & 7u)) << 4) | ((k & 7u) << 1)); }
+
+struct Workspace {
+  void* base = nullptr;
+  size_t bytes = 0;
+  float* cand = nullptr;
+  __nv_bfloat16* act_a = nullptr;
+  __nv_bfloat16* mod = nullptr;
+  float* x = nullptr;
+  __nv_bfloat16* attn = nullptr;
+  __nv_bfloat16* h = nullptr;
+  float* pred = nullptr;
+  float* costs = nullptr;
+  // plan state
+  float* mean = nullptr;
+  float* stdv = nullptr;
+  float* elites = nullptr;
+  float* best = nullptr;
+  float* fcost = nullptr;
+  float* W = nullptr;
+};
+
+struct WsReq {
+  size_t n_cand, T, A, D, L, tiles, heads, mlp, npred, B, R, ncol;
+  bool operator<=(const WsReq& o) const {
+    return n_cand <= o.n_cand && T <= o.T && tiles <= o.tiles && npred <= o.npred && B <= o.B && R <= o.R &&
+           ncol <= o.ncol;
+  }
+};
+
+}  // namespace
+
+struct lewm_ctx {
+  int device = 0;
+  lewm_model_desc desc{};
+  ModelDims md{};
+  std::string err;
+  void* d_weights = nullptr;
+  DevWeights w{};
+  uint32_t* d_status = nullptr;
+  Workspace ws;
+  WsReq cap{};
+  bool have_ws = false;
+  Prof prof;                  // per-launch event profiler (lewm_profile_plan)
+  std::vector<float> W_host;  // last uploaded coloring matrix
+  int W_n = -1;
+  float W_beta = -1.f;
+};
+
+namespace {
+
+lewm_status fail(lewm_ctx* c, lewm_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (c)
+    c->err = buf;
+  else
+    g_create_error = buf;
+  return s;
+}
+
+#define LEWM_CK(ctx, call)                                                                               \
+  do {                                                                                                   \
+    cudaError_t e_ = (call);                                                                             \
+    if (e_ != cudaSuccess)                                                                               \
+      return fail(ctx, e_ == cudaErrorMemoryAllocation ? LEWM_OUT_OF_MEMORY : LEWM_CUDA_ERROR, "%s: %s", \
+                  #call, cudaGetErrorString(e_));                                                        \
+  } while (0)
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+lewm_status check_desc(const lewm_model_desc* d, ModelDims* md) {
+  if (!d) return fail(nullptr, LEWM_INVALID_ARG, "desc is NULL");
+  if (d->dim <= 0 || d->depth <= 0 || d->heads <= 0 || d->dim_head <= 0 || d->mlp_dim <= 0 || d->action_dim <= 0 ||
+      d->smoothed_dim <= 0 || d->embed_hidden <= 0 || d->num_frames <= 0 || d->pred_proj_hidden < 0)
+    return fail(nullptr, LEWM_INVALID_ARG, "model dimensions must be positive");
+  if (d->dim != 192 && d->dim != 384)
+    return fail(nullptr, LEWM_UNSUPPORTED_SHAPE, "dim=%d unsupported (built for 192, 384)", d->dim);
+  if (d->dim_head != 64) return fail(nullptr, LEWM_UNSUPPORTED_SHAPE, "dim_head=%d unsupported (64)", d->dim_head);
+  if (d->heads > 16) return fail(nullptr, LEWM_UNSUPPORTED_SHAPE, "heads=%d > 16", d->heads);
+  if (d->mlp_dim % 128 || d->embed_hidden % 128)
+    return fail(nullptr, LEWM_UNSUPPORTED_SHAPE, "mlp_dim and embed_hidden must be multiples of 128");
+  if (d->action_dim > 16 || d->smoothed_dim > 16)
+    return fail(nullptr, LEWM_UNSUPPORTED_SHAPE, "action_dim/smoothed_dim must be <= 16");
+  if (d->num_frames > 8) return fail(nullptr, LEWM_UNSUPPORTED_SHAPE, "num_frames must be <= 8");
+  if (d->pred_proj_hidden != 0)
+    return fail(nullptr, LEWM_UNSUPPORTED_SHAPE, "pred_proj MLP head not supported (Identity only)");
+  md->D = d->dim;
+  md->L = d->depth;
+  md->heads = d->heads;
+  md->inner = d->heads * 64;
+  md->mlp = d->mlp_dim;
+  md->A = d->action_dim;
+  md->As = d->smoothed_dim;
+  md->eh = d->embed_hidden;
+  md->frames = d->num_frames;
+  return LEWM_OK;
+}
+
+size_t weight_count(const ModelDims& m) {
+  const size_t D = m.D;
+  size_t n = (size_t)m.frames * D;
+  const size_t per_layer = 6 * D * D + 6 * D + 2 * D + 3 * (size_t)m.inner * D + D * m.inner + D + 2 * D +
+                           (size_t)m.mlp * D + m.mlp + D * m.mlp + D;
+  n += per_layer * m.L;
+  n += 2 * D;
+  n += (size_t)m.As * m.A + m.As + (size_t)m.eh * m.As + m.eh + D * m.eh + D;
+  return n;
+}
+
+// Pack rows `rowmap(r)` (r < nrows) and columns [64*kb, 64*kb+64) of W (rows x K) into a
+// swizzled [nrows x 64] bf16 block.
+template <class RowMap>
+void pack_block(uint8_t* dst, const float* W, int K, int nrows, int kb, RowMap rowmap) {
+  for (int r = 0; r < nrows; ++r) {
+    const float* src = W + (size_t)rowmap(r) * K;
+    for (int k = 0; k < 64; ++k) {
+      const int col = kb * 64 + k;
+      const uint16_t v = col < K ? f2bf(src[col]) : 0;
+      std::memcpy(dst + sw128(r, k), &v, 2);
+    }
+  }
+}
+
+lewm_status pack_weights(lewm_ctx* c, const float* wts, size_t n) {
+  const ModelDims& m = c->md;
+  const int D = m.D, L = m.L, KB = D / 64, NT = D / 4, NKI = m.inner / 64, NKM = m.mlp / 64;
+  const int NT_ADA = (D == 192) ? 192 : 128;
+  // Walk the canonical order.
+  const float* p = wts;
+  auto take = [&](size_t k) {
+    const float* q = p;
+    p += k;
+    return q;
+  };
+  const float* pos = take((size_t)m.frames * D);
+  std::vector<const float*> ada_w(L), ada_b(L), aln_w(L), aln_b(L), qkv_w(L), out_w(L), out_b(L), fln_w(L),
+      fln_b(L), w1(L), b1(L), w2(L), b2(L);
+  for (int l = 0; l < L; ++l) {
+    ada_w[l] = take((size_t)6 * D * D);
+    ada_b[l] = take(6 * D);
+    aln_w[l] = take(D);
+    aln_b[l] = take(D);
+    qkv_w[l] = take((size_t)3 * m.inner * D);
+    out_w[l] = take((size_t)D * m.inner);
+    out_b[l] = take(D);
+    fln_w[l] = take(D);
+    fln_b[l] = take(D);
+    w1[l] = take((size_t)m.mlp * D);
+    b1[l] = take(m.mlp);
+    w2[l] = take((size_t)D * m.mlp);
+    b2[l] = take(D);
+  }
+  const float* fin_w = take(D);
+  const float* fin_b = take(D);
+  const float* conv_w = take((size_t)m.As * m.A);
+  const float* conv_b = take(m.As);
+  const float* e1_w = take((size_t)m.eh * m.As);
+  const float* e1_b = take(m.eh);
+  const float* e2_w = take((size_t)D * m.eh);
+  const float* e2_b = take(D);
+  if ((size_t)(p - wts) != n) return fail(c, LEWM_INVALID_ARG, "weight walk mismatch");
+
+  std::vector<uint8_t> buf;
+  auto alloc = [&](size_t bytes) {
+    const size_t off = round_up(buf.size(), 1024);
+    buf.resize(off + bytes);
+    return off;
+  };
+  const size_t blkA = 128 * 128;  // [128 x 64] block bytes
+  const size_t o_qkv = alloc((size_t)L * m.heads * KB * 192 * 128);
+  const size_t o_wout = alloc((size_t)L * 4 * NKI * NT * 128);
+  const size_t o_w1 = alloc((size_t)L * (m.mlp / 128) * KB * blkA);
+  const size_t o_w2 = alloc((size_t)L * 4 * NKM * NT * 128);
+  const size_t n_ada_tiles = (size_t)L * 6 * D / NT_ADA;
+  const size_t o_wada = alloc(n_ada_tiles * KB * NT_ADA * 128);
+  const size_t o_we2 = alloc((size_t)(m.eh / 128) * 2 * D * 128);
+  auto fvec = [&](const std::vector<const float*>& parts, size_t each) {
+    const size_t off = alloc(parts.size() * each * 4);
+    for (size_t i = 0; i < parts.size(); ++i) std::memcpy(buf.data() + off + i * each * 4, parts[i], each * 4);
+    return off;
+  };
+  const size_t o_pos = fvec({pos}, (size_t)m.frames * D);
+  const size_t o_adab = fvec(ada_b, 6 * D);
+  const size_t o_alnw = fvec(aln_w, D), o_alnb = fvec(aln_b, D);
+  const size_t o_outb = fvec(out_b, D);
+  const size_t o_flnw = fvec(fln_w, D), o_flnb = fvec(fln_b, D);
+  const size_t o_b1 = fvec(b1, m.mlp), o_b2 = fvec(b2, D);
+  const size_t o_finw = fvec({fin_w}, D), o_finb = fvec({fin_b}, D);
+  const size_t o_convw = fvec({conv_w}, (size_t)m.As * m.A), o_convb = fvec({conv_b}, m.As);
+  const size_t o_e1w = fvec({e1_w}, (size_t)m.eh * m.As), o_e1b = fvec({e1_b}, m.eh), o_e2b = fvec({e2_b}, D);
+
+  for (int l = 0; l < L; ++l) {
+    for (int h = 0; h < m.heads; ++h)
+      for (int kb = 0; kb < KB; ++kb) {
+        uint8_t* dst = buf.data() + o_qkv + ((size_t)(l * m.heads + h) * KB + kb) * 192 * 128;
+        pack_block(dst, qkv_w[l], D, 192, kb, [&](int r) { return (r / 64) * m.inner + h * 64 + (r % 64); });
+      }
+    for (int nt = 0; nt < 4; ++nt)
+      for (int kb = 0; kb < NKI; ++kb) {
+        uint8_t* dst = buf.data() + o_wout + ((size_t)(l * 4 + nt) * NKI + kb) * NT * 128;
+        pack_block(dst, out_w[l], m.inner, NT, kb, [&](int r) { return nt * NT + r; });
+      }
+    for (int nt = 0; nt < m.mlp / 128; ++nt)
+      for (int kb = 0; kb < KB; ++kb) {
+        uint8_t* dst = buf.data() + o_w1 + ((size_t)(l * (m.mlp / 128) + nt) * KB + kb) * blkA;
+        pack_block(dst, w1[l], D, 128, kb, [&](int r) { return nt * 128 + r; });
+      }
+    for (int nt = 0; nt < 4; ++nt)
+      for (int kb = 0; kb < NKM; ++kb) {
+        uint8_t* dst = buf.data() + o_w2 + ((size_t)(l * 4 + nt) * NKM + kb) * NT * 128;
+        pack_block(dst, w2[l], m.mlp, NT, kb, [&](int r) { return nt * NT + r; });
+      }
+  }
+  for (size_t t = 0; t < n_ada_tiles; ++t)
+    for (int kb = 0; kb < KB; ++kb) {
+      uint8_t* dst = buf.data() + o_wada + (t * KB + kb) * NT_ADA * 128;
+      for (int r = 0; r < NT_ADA; ++r) {
+        const size_t R = t * NT_ADA + r;
+        const float* src = ada_w[R / (6 * D)] + (R % (6 * D)) * D;
+        for (int k = 0; k < 64; ++k) {
+          const uint16_t v = f2bf(src[kb * 64 + k]);
+          std::memcpy(dst + sw128(r, k), &v, 2);
+        }
+      }
+    }
+  for (int ch = 0; ch < m.eh / 128; ++ch)
+    for (int kb = 0; kb < 2; ++kb) {
+      uint8_t* dst = buf.data() + o_we2 + ((size_t)ch * 2 + kb) * D * 128;
+      for (int r = 0; r < D; ++r)
+        for (int k = 0; k < 64; ++k) {
+          const uint16_t v = f2bf(e2_w[(size_t)r * m.eh + ch * 128 + kb * 64 + k]);
+          std::memcpy(dst + sw128(r, k), &v, 2);
+        }
+    }
+
+  LEWM_CK(c, cudaMalloc(&c->d_weights, buf.size()));
+  LEWM_CK(c, cudaMemcpy(c->d_weights, buf.data(), buf.size(), cudaMemcpyHostToDevice));
+  auto* base = static_cast<uint8_t*>(c->d_weights);
+  auto bf = [&](size_t o) { return reinterpret_cast<const __nv_bfloat16*>(base + o); };
+  auto fl = [&](size_t o) { return reinterpret_cast<const float*>(base + o); };
+  c->w = DevWeights{bf(o_qkv), bf(o_wout), bf(o_w1), bf(o_w2), bf(o_wada), bf(o_we2), fl(o_pos), fl(o_adab),
+                    fl(o_alnw), fl(o_alnb), fl(o_outb), fl(o_flnw), fl(o_flnb), fl(o_b1), fl(o_b2), fl(o_finw),
+                    fl(o_finb), fl(o_convw), fl(o_convb), fl(o_e1w), fl(o_e1b), fl(o_e2b)};
+  return LEWM_OK;
+}
+
+int window_tiles(int n_cand, int w) {
+  const int cpt = 128 / w;
+  return (n_cand + cpt - 1) / cpt;
+}
+
+lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
+  if (c->have_ws && need <= c->cap) return LEWM_OK;
+  WsReq r = need;
+  if (c->have_ws) {  // grow monotonically
+    r.n_cand = std::max(r.n_cand, c->cap.n_cand);
+    r.T = std::max(r.T, c->cap.T);
+    r.tiles = std::max(r.tiles, c->cap.tiles);
+    r.npred = std::max(r.npred, c->cap.npred);
+    r.B = std::max(r.B, c->cap.B);
+    r.R = std::max(r.R, c->cap.R);
+    r.ncol = std::max(r.ncol, c->cap.ncol);
+    cudaFree(c->ws.base);
+    c->ws = Workspace{};
+    c->have_ws = false;
+  }
+  const ModelDims& m = c->md;
+  const size_t rows_e = r.n_cand * r.T;
+  const size_t tiles_e = (rows_e + 127) / 128;
+  size_t off = 0;
+  auto carve = [&](size_t bytes) {
+    const size_t o = off;
+    off = round_up(off + std::max<size_t>(bytes, 16), 1024);
+    return o;
+  };
+  const size_t o_cand = carve(r.n_cand * r.T * m.A * 4);
+  const size_t o_act = carve(tiles_e * (m.D / 64) * 128 * 64 * 2);
+  const size_t o_mod = carve(rows_e * (size_t)m.L * 6 * m.D * 2);
+  const size_t o_x = carve(r.tiles * 128 * (size_t)m.D * 4);
+  const size_t o_attn = carve(r.tiles * (size_t)(m.inner / 64) * 128 * 64 * 2);
+  const size_t o_h = carve(r.tiles * (size_t)(m.mlp / 64) * 128 * 64 * 2);
+  const size_t o_pred = carve(r.n_cand * r.npred * (size_t)m.D * 4);
+  const size_t o_costs = carve(r.n_cand * 4);
+  const size_t ta = r.T * m.A;
+  const size_t o_mean = carve(r.B * ta * 4);
+  const size_t o_std = carve(r.B * ta * 4);
+  const size_t o_el = carve(r.B * std::max<size_t>(r.R, 1) * ta * 4);
+  const size_t o_best = carve(r.B * ta * 4);
+  const size_t o_fc = carve(r.B * 4);
+  const size_t o_W = carve(std::max<size_t>(r.ncol, 1) * std::max<size_t>(r.ncol, 1) * 4);
+  void* base = nullptr;
+  LEWM_CK(c, cudaMalloc(&base, off));
+  auto* b = static_cast<uint8_t*>(base);
+  Workspace& ws = c->ws;
+  ws.base = base;
+  ws.bytes = off;
+  ws.cand = reinterpret_cast<float*>(b + o_cand);
+  ws.act_a = reinterpret_cast<__nv_bfloat16*>(b + o_act);
+  ws.mod = reinterpret_cast<__nv_bfloat16*>(b + o_mod);
+  ws.x = reinterpret_cast<float*>(b + o_x);
+  ws.attn = reinterpret_cast<__nv_bfloat16*>(b + o_attn);
+  ws.h = reinterpret_cast<__nv_bfloat16*>(b + o_h);
+  ws.pred = reinterpret_cast<float*>(b + o_pred);
+  ws.costs = reinterpret_cast<float*>(b + o_costs);
+  ws.mean = reinterpret_cast<float*>(b + o_mean);
+  ws.stdv = reinterpret_cast<float*>(b + o_std);
+  ws.elites = reinterpret_cast<float*>(b + o_el);
+  ws.best = reinterpret_cast<float*>(b + o_best);
+  ws.fcost = reinterpret_cast<float*>(b + o_fc);
+  ws.W = reinterpret_cast<float*>(b + o_W);
+  c->cap = r;
+  c->have_ws = true;
+  c->W_n = -1;
+  return LEWM_OK;
+}
+
+// Launch sequence of one model-cost evaluation over n_cand = B*S candidates.
+lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, const float* goal, int goal_pc,
+                           const float* cand, int B, int S, int T, int HS, float* costs, cudaStream_t st) {
+  const ModelDims& m = c->md;
+  const int NC = B * S;
+  const int rows = NC * T;
+  LEWM_CK(c, launch_embed(m, c->w, cand, rows, c->ws.act_a, c->d_status, st, &c->prof));
+  LEWM_CK(c, launch_adaln(m, c->w, rows, c->ws.act_a, c->ws.mod, c->d_status, st, &c->prof));
+  RolloutBufs b{emb, emb_pc, goal, goal_pc, cand, c->ws.act_a, c->ws.mod, c->ws.x, c->ws.attn, c->ws.h, c->ws.pred,
+                costs};
+  const int n_calls = T - H + 1;
+  for (int k = 0; k < n_calls; ++k) {
+    const int end = H + k;
+    const int start = std::max(0, end - HS);
+    const int w = end - start;
+    CallGeom g{NC, S, T, H, w, start, 128 / w, window_tiles(NC, w), k, k == n_calls - 1};
+    LEWM_CK(c, launch_call(m, c->w, g, b, c->d_status, st, &c->prof));
+  }
+  return LEWM_OK;
+}
+
+int max_call_tiles(int NC, int T, int H, int HS) {
+  int t = 1;
+  for (int k = 0; k < T - H + 1; ++k) {
+    const int end = H + k;
+    t = std::max(t, window_tiles(NC, end - std::max(0, end - HS)));
+  }
+  return t;
+}
+
+void coloring_matrix(int n, double beta, double* W) {
+  // W[t][u] = irfft(rfft(e_u) * scale)[t]; scale_f = (f/n)^(-beta/2) for f >= 1, scale_0 = scale_1.
+  std::vector<double> s(n / 2 + 1);
+  for (int f = 1; f <= n / 2; ++f) s[f] = std::pow((double)f / n, -beta / 2.0);
+  s[0] = (n / 2 >= 1) ? s[1] : 1.0;
+  const double pi = 3.14159265358979323846;
+  for (int t = 0; t < n; ++t)
+    for (int u = 0; u < n; ++u) {
+      const int d = t - u;
+      double acc = s[0];
+      for (int f = 1; f <= n / 2; ++f) {
+        const double wgt = (2 * f == n) ? 1.0 : 2.0;
+        acc += wgt * s[f] * std::cos(2.0 * pi * f * d / n);
+      }
+      W[t * n + u] = acc / n;
+    }
+}
+
+lewm_status check_plan(lewm_ctx* c, const lewm_plan_desc* p) {
+  if (!p) return fail(c, LEWM_INVALID_ARG, "plan desc is NULL");
+  if (p->topk <= 0) return fail(c, LEWM_INVALID_ARG, "topk must be positive, got %d", p->topk);
+  if (p->num_samples < p->topk)
+    return fail(c, LEWM_INVALID_ARG, "num_samples=%d must be >= topk=%d", p->num_samples, p->topk);
+  if (p->n_steps <= 0) return fail(c, LEWM_INVALID_ARG, "n_steps must be positive, got %d", p->n_steps);
+  if (p->elite_retention < 0)
+    return fail(c, LEWM_INVALID_ARG, "elite_retention must be non-negative, got %d", p->elite_retention);
+  if (!(p->momentum_alpha >= 0.f && p->momentum_alpha < 1.f))
+    return fail(c, LEWM_INVALID_ARG, "momentum_alpha must satisfy 0 <= alpha < 1, got %g", p->momentum_alpha);
+  if (!(p->sample_decay >= 1.f)) return fail(c, LEWM_INVALID_ARG, "sample_decay must be >= 1.0, got %g", p->sample_decay);
+  if (p->bucket < 0) return fail(c, LEWM_INVALID_ARG, "sample_count_bucket_size must be non-negative, got %d", p->bucket);
+  if (p->action_block <= 0) return fail(c, LEWM_INVALID_ARG, "action_block must be positive, got %d", p->action_block);
+  if (!(p->beta >= 0.f)) return fail(c, LEWM_INVALID_ARG, "beta must be >= 0");
+  if (p->n_envs <= 0 || p->horizon <= 0 || p->history <= 0 || p->history > p->horizon || p->history_size <= 0)
+    return fail(c, LEWM_INVALID_ARG, "need n_envs > 0 and 1 <= history <= horizon, history_size >= 1");
+  if (c) {
+    if (p->history_size > c->md.frames)
+      return fail(c, LEWM_UNSUPPORTED_SHAPE, "history_size=%d exceeds num_frames=%d", p->history_size, c->md.frames);
+    if (p->horizon * c->md.A > 128) return fail(c, LEWM_UNSUPPORTED_SHAPE, "horizon*action_dim must be <= 128");
+    if (p->beta > 0.f && p->time_axis_raw && p->action_block > 1) {
+      if (c->md.A % p->action_block)
+        return fail(c, LEWM_INVALID_ARG, "action_dim=%d is not divisible by action_block=%d", c->md.A,
+                    p->action_block);
+      if (p->horizon * p->action_block > 128) return fail(c, LEWM_UNSUPPORTED_SHAPE, "horizon*action_block > 128");
+    }
+    if (p->num_samples > 4096) return fail(c, LEWM_UNSUPPORTED_SHAPE, "num_samples must be <= 4096");
+    if (p->topk > 512) return fail(c, LEWM_UNSUPPORTED_SHAPE, "topk must be <= 512");
+  }
+  return LEWM_OK;
+}
+
+std::vector<int> counts_of(const lewm_plan_desc* p) {
+  std::vector<int> out(p->n_steps);
+  for (int s = 0; s < p->n_steps; ++s) {
+    int count;
+    if ((double)p->sample_decay == 1.0) {
+      count = p->num_samples;
+    } else {
+      const int decayed = (int)std::ceil(p->num_samples * std::pow((double)p->sample_decay, (double)-s));
+      count = std::max(decayed, std::min(p->num_samples, 2 * p->topk));
+      if (p->bucket > 0)
+        count = std::min(p->num_samples, (int)std::ceil((double)count / p->bucket) * p->bucket);
+    }
+    out[s] = count;
+  }
+  return out;
+}
+
+// Noise layout of make_colored_noise for this plan: kind and colored length.
+void noise_kind(const lewm_ctx* c, const lewm_plan_desc* p, int* kind, int* ncol) {
+  if (p->beta <= 0.f) {
+    *kind = 0;
+    *ncol = 0;
+    return;
+  }
+  if (p->time_axis_raw && p->action_block > 1) {
+    *kind = 1;
+    *ncol = p->horizon * p->action_block;
+  } else {
+    *kind = 2;
+    *ncol = p->horizon;
+  }
+  if (*ncol <= 1) {
+    *kind = 0;
+    *ncol = 0;
+  }
+  (void)c;
+}
+
+lewm_status upload_W(lewm_ctx* c, const lewm_plan_desc* p, int ncol, cudaStream_t st) {
+  if (ncol <= 1) return LEWM_OK;
+  if (c->W_n == ncol && c->W_beta == p->beta) return LEWM_OK;
+  std::vector<double> Wd((size_t)ncol * ncol);
+  coloring_matrix(ncol, p->beta, Wd.data());
+  c->W_host.assign(Wd.begin(), Wd.end());
+  LEWM_CK(c, cudaMemcpyAsync(c->ws.W, c->W_host.data(), c->W_host.size() * 4, cudaMemcpyHostToDevice, st));
+  LEWM_CK(c, cudaStreamSynchronize(st));  // W_host may be rewritten by a later call
+  c->W_n = ncol;
+  c->W_beta = p->beta;
+  return LEWM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t lewm_weight_count(const lewm_model_desc* desc) {
+  ModelDims md{};
+  if (check_desc(desc, &md) != LEWM_OK) return 0;
+  return weight_count(md);
+}
+
+lewm_status lewm_create(lewm_ctx** out, const lewm_model_desc* desc, const float* weights, size_t n_floats,
+                        int device) {
+  if (!out) return fail(nullptr, LEWM_INVALID_ARG, "out is NULL");
+  *out = nullptr;
+  ModelDims md{};
+  lewm_status s = check_desc(desc, &md);
+  if (s != LEWM_OK) return s;
+  if (!weights) return fail(nullptr, LEWM_INVALID_ARG, "weights is NULL");
+  if (n_floats != weight_count(md))
+    return fail(nullptr, LEWM_INVALID_ARG, "expected %zu weight floats, got %zu", weight_count(md), n_floats);
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+    return fail(nullptr, LEWM_CUDA_ERROR, "no CUDA device %d", device);
+  DeviceGuard g(device);
+  cudaDeviceProp prop{};
+  cudaGetDeviceProperties(&prop, device);
+  if (prop.major != 10) return fail(nullptr, LEWM_UNSUPPORTED_SHAPE, "device %d is sm_%d%d, need sm_100", device, prop.major, prop.minor);
+  auto* c = new lewm_ctx();
+  c->device = device;
+  c->desc = *desc;
+  c->md = md;
+  s = pack_weights(c, weights, n_floats);
+  if (s == LEWM_OK && cudaMalloc(&c->d_status, 4) != cudaSuccess) s = fail(c, LEWM_CUDA_ERROR, "status alloc");
+  if (s == LEWM_OK && cudaMemset(c->d_status, 0, 4) != cudaSuccess) s = fail(c, LEWM_CUDA_ERROR, "status memset");
+  if (s != LEWM_OK) {
+    g_create_error = c->err;
+    lewm_destroy(c);
+    return s;
+  }
+  *out = c;
+  return LEWM_OK;
+}
+
+void lewm_destroy(lewm_ctx* c) {
+  if (!c) return;
+  DeviceGuard g(c->device);
+  if (c->ws.base) cudaFree(c->ws.base);
+  if (c->d_weights) cudaFree(c->d_weights);
+  if (c->d_status) cudaFree(c->d_status);
+  delete c;
+}
+
+const char* lewm_last_error(const lewm_ctx* c) { return c ? c->err.c_str() : g_create_error.c_str(); }
+
+lewm_status lewm_model_cost(lewm_ctx* c, const float* emb, int32_t emb_per_sample, int32_t H, const float* goal,
+                            int32_t goal_per_sample, const float* cand, int32_t B, int32_t S, int32_t T,
+                            int32_t history_size, float* costs_out, void* stream) {
+  if (!c) return fail(nullptr, LEWM_INVALID_ARG, "ctx is NULL");
+  c->err.clear();
+  if (!emb || !goal || !cand || !costs_out) return fail(c, LEWM_INVALID_ARG, "NULL tensor pointer");
+  if (B <= 0 || S <= 0 || T <= 0 || H <= 0 || H > T || history_size <= 0)
+    return fail(c, LEWM_INVALID_ARG, "need B,S,T > 0 and 1 <= H <= T, got B=%d S=%d T=%d H=%d", B, S, T, H);
+  if (history_size > c->md.frames)
+    return fail(c, LEWM_UNSUPPORTED_SHAPE, "history_size=%d exceeds num_frames=%d", history_size, c->md.frames);
+  if ((int64_t)B * S * T > (1ll << 26)) return fail(c, LEWM_UNSUPPORTED_SHAPE, "B*S*T too large");
+  DeviceGuard g(c->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int NC = B * S;
+  WsReq need{(size_t)NC, (size_t)T, (size_t)c->md.A, (size_t)c->md.D, (size_t)c->md.L,
+             (size_t)max_call_tiles(NC, T, H, history_size), (size_t)c->md.heads, (size_t)c->md.mlp,
+             (size_t)(T - H + 1), 1, 0, 0};
+  lewm_status s = ensure_ws(c, need);
+  if (s != LEWM_OK) return s;
+  return run_model_cost(c, emb, emb_per_sample != 0, H, goal, goal_per_sample != 0, cand, B, S, T, history_size,
+                        costs_out, st);
+}
+
+lewm_status lewm_sample_counts(const lewm_plan_desc* plan, int32_t* counts_out, int32_t cap, int64_t* evals_out) {
+  lewm_status s = check_plan(nullptr, plan);
+  if (s != LEWM_OK) return s;
+  const std::vector<int> cs = counts_of(plan);
+  int64_t tot = 0;
+  for (size_t i = 0; i < cs.size(); ++i) {
+    if (counts_out && (int32_t)i < cap) counts_out[i] = cs[i];
+    tot += cs[i];
+  }
+  if (evals_out) *evals_out = tot;
+  return LEWM_OK;
+}
+
+lewm_status lewm_plan(lewm_ctx* c, const lewm_plan_desc* p, const float* emb, const float* goal,
+                      const float* init_mean, const float* init_std, const float* const* noise_steps,
+                      const float* action_low, const float* action_high, float* actions_out, float* std_out,
+                      float* final_cost_out, const lewm_plan_trace* trace, void* stream) {
+  if (!c) return fail(nullptr, LEWM_INVALID_ARG, "ctx is NULL");
+  c->err.clear();
+  lewm_status s = check_plan(c, p);
+  if (s != LEWM_OK) return s;
+  if (!emb || !goal || !init_mean || !init_std || !actions_out || !std_out || !final_cost_out)
+    return fail(c, LEWM_INVALID_ARG, "NULL tensor pointer");
+  if (p->clip_actions && (!action_low || !action_high))
+    return fail(c, LEWM_INVALID_ARG, "clip_actions needs action_low and action_high");
+  if (noise_steps)
+    for (int i = 0; i < p->n_steps; ++i)
+      if (!noise_steps[i]) return fail(c, LEWM_INVALID_ARG, "noise_steps[%d] is NULL", i);
+  DeviceGuard g(c->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const ModelDims& m = c->md;
+  const int B = p->n_envs, T = p->horizon, A = m.A, TA = T * A, k = p->topk;
+  const std::vector<int> counts = counts_of(p);
+  const int Smax = *std::max_element(counts.begin(), counts.end());
+  if ((int64_t)B * Smax * T > (1ll << 26)) return fail(c, LEWM_UNSUPPORTED_SHAPE, "n_envs*num_samples*T too large");
+  int kind, ncol;
+  noise_kind(c, p, &kind, &ncol);
+  const int R = std::min(p->elite_retention, k);
+  const int NC = B * Smax;
+  WsReq need{(size_t)NC, (size_t)T, (size_t)A, (size_t)m.D, (size_t)m.L,
+             (size_t)max_call_tiles(NC, T, p->history, p->history_size), (size_t)m.heads, (size_t)m.mlp,
+             (size_t)(T - p->history + 1), (size_t)B, (size_t)R, (size_t)std::max(ncol, 1)};
+  s = ensure_ws(c, need);
+  if (s != LEWM_OK) return s;
+  Workspace& ws = c->ws;
+  s = upload_W(c, p, ncol, st);
+  if (s != LEWM_OK) return s;
+  LEWM_CK(c, cudaMemcpyAsync(ws.mean, init_mean, (size_t)B * TA * 4, cudaMemcpyDeviceToDevice, st));
+  LEWM_CK(c, cudaMemcpyAsync(ws.stdv, init_std, (size_t)B * TA * 4, cudaMemcpyDeviceToDevice, st));
+  for (int it = 0; it < p->n_steps; ++it) {
+    const int St = counts[it];
+    const int n_inject = (it > 0 && p->elite_retention > 0) ? std::min(std::min(p->elite_retention, k), St - 1) : 0;
+    SampleParams sp{};
+    sp.B = B;
+    sp.S = St;
+    sp.T = T;
+    sp.A = A;
+    sp.noise_kind = kind;
+    sp.raw_block = p->action_block;
+    sp.ncol = ncol;
+    sp.W = ws.W;
+    sp.noise = noise_steps ? noise_steps[it] : nullptr;
+    sp.seed_lo = (uint32_t)(p->seed & 0xffffffffu);
+    sp.plan_id = (uint32_t)(p->plan_index & 0xffffffffu);
+    sp.iter = (uint32_t)it;
+    sp.mean = ws.mean;
+    sp.stdv = ws.stdv;
+    sp.elites = ws.elites;
+    sp.elite_stride = std::max(R, 1);
+    sp.n_inject = std::max(n_inject, 0);
+    sp.low = p->clip_actions ? action_low : nullptr;
+    sp.high = p->clip_actions ? action_high : nullptr;
+    sp.cand = ws.cand;
+    c->prof.begin(st);
+    LEWM_CK(c, launch_sample(sp, st));
+    c->prof.end(KC_SAMPLE, 0.0, st);
+    s = run_model_cost(c, emb, 0, p->history, goal, 0, ws.cand, B, St, T, p->history_size, ws.costs, st);
+    if (s != LEWM_OK) return s;
+    RefitParams rp{};
+    rp.B = B;
+    rp.S = St;
+    rp.T = T;
+    rp.A = A;
+    rp.k = k;
+    rp.R = R;
+    rp.costs = ws.costs;
+    rp.cand = ws.cand;
+    rp.mean = ws.mean;
+    rp.stdv = ws.stdv;
+    rp.alpha = p->momentum_alpha;
+    rp.elites = ws.elites;
+    rp.best = ws.best;
+    rp.final_cost = ws.fcost;
+    rp.topk_idx = (trace && trace->topk_idx) ? trace->topk_idx + (size_t)it * B * k : nullptr;
+    rp.topk_val = (trace && trace->topk_val) ? trace->topk_val + (size_t)it * B * k : nullptr;
+    c->prof.begin(st);
+    LEWM_CK(c, launch_refit(rp, st));
+    c->prof.end(KC_REFIT, 0.0, st);
+    if (trace) {
+      const size_t S = p->num_samples;
+      if (trace->costs)
+        LEWM_CK(c, cudaMemcpy2DAsync(trace->costs + (size_t)it * B * S, S * 4, ws.costs, (size_t)St * 4,
+                                     (size_t)St * 4, B, cudaMemcpyDeviceToDevice, st));
+      if (trace->candidates)
+        LEWM_CK(c, cudaMemcpy2DAsync(trace->candidates + (size_t)it * B * S * TA, S * TA * 4, ws.cand,
+                                     (size_t)St * TA * 4, (size_t)St * TA * 4, B, cudaMemcpyDeviceToDevice, st));
+      if (trace->mean)
+        LEWM_CK(c, cudaMemcpyAsync(trace->mean + (size_t)it * B * TA, ws.mean, (size_t)B * TA * 4,
+                                   cudaMemcpyDeviceToDevice, st));
+      if (trace->std)
+        LEWM_CK(c, cudaMemcpyAsync(trace->std + (size_t)it * B * TA, ws.stdv, (size_t)B * TA * 4,
+                                   cudaMemcpyDeviceToDevice, st));
+    }
+  }
+  LEWM_CK(c, cudaMemcpyAsync(actions_out, p->return_best_elite ? ws.best : ws.mean, (size_t)B * TA * 4,
+                             cudaMemcpyDeviceToDevice, st));
+  LEWM_CK(c, cudaMemcpyAsync(std_out, ws.stdv, (size_t)B * TA * 4, cudaMemcpyDeviceToDevice, st));
+  LEWM_CK(c, cudaMemcpyAsync(final_cost_out, ws.fcost, (size_t)B * 4, cudaMemcpyDeviceToDevice, st));
+  return LEWM_OK;
+}
+
+lewm_status lewm_topk_refit(lewm_ctx* c, const float* costs, const float* cand, int32_t B, int32_t S, int32_t T,
+                            int32_t A, int32_t k, float momentum_alpha, float* mean, float* std, int32_t* topk_idx,
+                            float* topk_val, float* best, float* final_cost, void* stream) {
+  if (!c) return fail(nullptr, LEWM_INVALID_ARG, "ctx is NULL");
+  c->err.clear();
+  if (!costs || !cand || !mean || !std || !best || !final_cost) return fail(c, LEWM_INVALID_ARG, "NULL tensor pointer");
+  if (B <= 0 || S <= 0 || T <= 0 || A <= 0 || k <= 0 || k > S)
+    return fail(c, LEWM_INVALID_ARG, "need B,S,T,A > 0 and 1 <= k <= S");
+  if (S > 4096 || T * A > 128 || k > 512) return fail(c, LEWM_UNSUPPORTED_SHAPE, "S <= 4096, T*A <= 128, k <= 512");
+  if (!(momentum_alpha >= 0.f && momentum_alpha < 1.f)) return fail(c, LEWM_INVALID_ARG, "0 <= momentum_alpha < 1");
+  DeviceGuard g(c->device);
+  RefitParams rp{};
+  rp.B = B;
+  rp.S = S;
+  rp.T = T;
+  rp.A = A;
+  rp.k = k;
+  rp.R = 0;
+  rp.costs = costs;
+  rp.cand = cand;
+  rp.mean = mean;
+  rp.stdv = std;
+  rp.alpha = momentum_alpha;
+  rp.elites = nullptr;
+  rp.best = best;
+  rp.final_cost = final_cost;
+  rp.topk_idx = topk_idx;
+  rp.topk_val = topk_val;
+  LEWM_CK(c, launch_refit(rp, static_cast<cudaStream_t>(stream)));
+  return LEWM_OK;
+}
+
+lewm_status lewm_sample_candidates(lewm_ctx* c, const lewm_plan_desc* p, int32_t S, int32_t iter,
+                                   const float* mean, const float* std, const float* injected_noise,
+                                   const float* action_low, const float* action_high, float* out, void* stream) {
+  if (!c) return fail(nullptr, LEWM_INVALID_ARG, "ctx is NULL");
+  c->err.clear();
+  lewm_status s = check_plan(c, p);
+  if (s != LEWM_OK) return s;
+  if (!mean || !std || !out || S <= 0 || iter < 0) return fail(c, LEWM_INVALID_ARG, "bad sample arguments");
+  if (p->clip_actions && (!action_low || !action_high))
+    return fail(c, LEWM_INVALID_ARG, "clip_actions needs action_low and action_high");
+  DeviceGuard g(c->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int kind, ncol;
+  noise_kind(c, p, &kind, &ncol);
+  WsReq need{1, (size_t)p->horizon, (size_t)c->md.A, (size_t)c->md.D, (size_t)c->md.L, 1, (size_t)c->md.heads,
+             (size_t)c->md.mlp, 1, 1, 0, (size_t)std::max(ncol, 1)};
+  s = ensure_ws(c, need);
+  if (s != LEWM_OK) return s;
+  s = upload_W(c, p, ncol, st);
+  if (s != LEWM_OK) return s;
+  SampleParams sp{};
+  sp.B = p->n_envs;
+  sp.S = S;
+  sp.T = p->horizon;
+  sp.A = c->md.A;
+  sp.noise_kind = kind;
+  sp.raw_block = p->action_block;
+  sp.ncol = ncol;
+  sp.W = c->ws.W;
+  sp.noise = injected_noise;
+  sp.seed_lo = (uint32_t)(p->seed & 0xffffffffu);
+  sp.plan_id = (uint32_t)(p->plan_index & 0xffffffffu);
+  sp.iter = (uint32_t)iter;
+  sp.mean = mean;
+  sp.stdv = std;
+  sp.elites = nullptr;
+  sp.elite_stride = 1;
+  sp.n_inject = 0;
+  sp.low = p->clip_actions ? action_low : nullptr;
+  sp.high = p->clip_actions ? action_high : nullptr;
+  sp.cand = out;
+  LEWM_CK(c, launch_sample(sp, st));
+  return LEWM_OK;
+}
+
+lewm_status lewm_sync_status(lewm_ctx* c, void* stream) {
+  if (!c) return fail(nullptr, LEWM_INVALID_ARG, "ctx is NULL");
+  DeviceGuard g(c->device);
+  LEWM_CK(c, cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  LEWM_CK(c, cudaGetLastError());
+  uint32_t v = 0;
+  LEWM_CK(c, cudaMemcpy(&v, c->d_status, 4, cudaMemcpyDeviceToHost));
+  if (v) {
+    LEWM_CK(c, cudaMemset(c->d_status, 0, 4));
+    return fail(c, LEWM_DEVICE_TIMEOUT, "device status 0x%x: a bounded device wait expired", v);
+  }
+  return LEWM_OK;
+}
+
+lewm_status lewm_profile_plan(lewm_ctx* c, const lewm_plan_desc* p, const float* emb, const float* goal,
+                              const float* init_mean, const float* init_std, double* ms_out, double* flops_out,
+                              int32_t* launches_out, void* stream) {
+  if (!c) return fail(nullptr, LEWM_INVALID_ARG, "ctx is NULL");
+  if (!ms_out || !flops_out || !launches_out) return fail(c, LEWM_INVALID_ARG, "NULL output array");
+  if (!p) return fail(c, LEWM_INVALID_ARG, "plan desc is NULL");
+  DeviceGuard g(c->device);
+  const int B = p->n_envs, TA = p->horizon * c->md.A;
+  float *act = nullptr, *sd = nullptr, *fc = nullptr;
+  LEWM_CK(c, cudaMalloc(&act, (size_t)B * TA * 4 * 2 + (size_t)B * 4));
+  sd = act + (size_t)B * TA;
+  fc = sd + (size_t)B * TA;
+  c->prof.reset();
+  c->prof.on = true;
+  lewm_status s = lewm_plan(c, p, emb, goal, init_mean, init_std, nullptr, nullptr, nullptr, act, sd, fc, nullptr,
+                            stream);
+  c->prof.on = false;
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  cudaFree(act);
+  if (s != LEWM_OK) return s;
+  if (e != cudaSuccess) return fail(c, LEWM_CUDA_ERROR, "profile sync: %s", cudaGetErrorString(e));
+  for (int k = 0; k < KC_COUNT; ++k) {
+    ms_out[k] = 0;
+    flops_out[k] = 0;
+    launches_out[k] = 0;
+  }
+  for (const auto& r : c->prof.recs) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, r.a, r.b);
+    ms_out[r.cls] += ms;
+    flops_out[r.cls] += r.flops;
+    launches_out[r.cls] += 1;
+  }
+  c->prof.reset();
+  return LEWM_OK;
+}
+
+lewm_status lewm_coloring_matrix(int32_t n, double beta, double* out) {
+  if (n <= 0 || !out || !(beta >= 0.0)) return fail(nullptr, LEWM_INVALID_ARG, "bad coloring_matrix arguments");
+  if (beta <= 0.0 || n <= 1) {
+    for (int i = 0; i < n * n; ++i) out[i] = (i / n == i % n) ? 1.0 : 0.0;
+    return LEWM_OK;
+  }
+  coloring_matrix(n, beta, out);
+  return LEWM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,217 @@
+// iCEM sampling and elite refit kernels for sm_100a.
+//
+// k_sample: one thread per (env, candidate) builds the candidate action sequence
+//   cand = noise * std + mean (reference lewm/solvers/icem.py:523), slot 0 = mean
+//   (:524), slots 1..n_inject = previous sorted elites (:421-432), optional clamp
+//   (:526-527). Noise is either injected (the reference's post-coloring noise
+//   tensors) or drawn in-kernel: Philox4x32-10 normals (Box-Muller), colored by
+//   a fixed real matrix W that equals rfft -> scale -> irfft
+//   (lewm/solvers/icem.py:173-182), then divided by the unbiased std over time
+//   (clamped at 1e-8, :148-150), laid out as in make_colored_noise (:185-250).
+// k_refit: one CTA per env sorts (cost, index) keys with a bitonic network in
+//   shared memory (ascending; ties -> lower index; NaN last), gathers the k
+//   elites and refits mean / unbiased std with optional momentum
+//   (lewm/solvers/icem.py:543-563), keeps the best elite (:551) and the mean
+//   of the k smallest costs (:580).
+#include "lewm_common.cuh"
+#include "lewm_internal.h"
+
+namespace lewm {
+namespace {
+
+constexpr int kMaxTA = 128;   // horizon * action_dim
+constexpr int kMaxCol = 128;  // colored time length
+
+struct Philox4 {
+  uint32_t x, y, z, w;
+};
+
+__device__ __forceinline__ Philox4 philox4x32_10(Philox4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+  for (int i = 0; i < 10; ++i) {
+    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
+    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
+    c = Philox4{hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0};
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return c;
+}
+
+// Draw d of (plan, it, env, cand): counter (d/4, cand, env, it), key (seed, plan).
+__device__ __forceinline__ void normals4(uint32_t blk, uint32_t cand, uint32_t env, uint32_t it, uint32_t seed,
+                                         uint32_t plan, float* out) {
+  const Philox4 r = philox4x32_10(Philox4{blk, cand, env, it}, seed, plan);
+  const float u1a = ((float)r.x + 1.0f) * 2.3283064365386963e-10f;  // (0, 1]
+  const float u2a = (float)r.y * 2.3283064365386963e-10f;           // [0, 1)
+  const float u1b = ((float)r.z + 1.0f) * 2.3283064365386963e-10f;
+  const float u2b = (float)r.w * 2.3283064365386963e-10f;
+  const float ra = sqrtf(-2.0f * logf(u1a)), rb = sqrtf(-2.0f * logf(u1b));
+  float sa, ca, sb, cb;
+  sincospif(2.0f * u2a, &sa, &ca);
+  sincospif(2.0f * u2b, &sb, &cb);
+  out[0] = ra * ca;
+  out[1] = ra * sa;
+  out[2] = rb * cb;
+  out[3] = rb * sb;
+}
+
+__global__ void __launch_bounds__(128) k_sample(SampleParams p) {
+  const int gid = blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= p.B * p.S) return;
+  const int env = gid / p.S, c = gid - env * p.S;
+  const int TA = p.T * p.A;
+  const float* mean = p.mean + (size_t)env * TA;
+  const float* sd = p.stdv + (size_t)env * TA;
+  float* out = p.cand + (size_t)gid * TA;
+  float v[kMaxTA];
+  if (c == 0) {
+    for (int i = 0; i < TA; ++i) v[i] = mean[i];
+  } else if (c <= p.n_inject) {
+    const float* e = p.elites + ((size_t)env * p.elite_stride + (c - 1)) * TA;
+    for (int i = 0; i < TA; ++i) v[i] = e[i];
+  } else if (p.noise) {
+    const float* nz = p.noise + (size_t)gid * TA;
+    for (int i = 0; i < TA; ++i) v[i] = nz[i] * sd[i] + mean[i];
+  } else {
+    // White draws in the reference's randn layout: [channel][time].
+    const int chans = (p.noise_kind == 1) ? p.A / p.raw_block : p.A;
+    const int ncol = (p.noise_kind == 0) ? p.T : p.ncol;
+    const int n = chans * ncol;
+    float wn[kMaxTA];
+    for (int d = 0; d < n; d += 4) {
+      float r4[4];
+      normals4((uint32_t)(d >> 2), (uint32_t)c, (uint32_t)env, p.iter, p.seed_lo, p.plan_id, r4);
+      for (int q = 0; q < 4 && d + q < n; ++q) wn[d + q] = r4[q];
+    }
+    if (p.noise_kind == 0) {
+      // white (B,S,T,A): draw d -> (t, a) = (d / A, d % A)
+      for (int i = 0; i < TA; ++i) v[i] = wn[i] * sd[i] + mean[i];
+    } else {
+      for (int ch = 0; ch < chans; ++ch) {
+        float col[kMaxCol];
+        float s = 0.f;
+        for (int t = 0; t < ncol; ++t) {
+          float acc = 0.f;
+          const float* wr = p.W + t * ncol;
+          for (int u = 0; u < ncol; ++u) acc += wr[u] * wn[ch * ncol + u];
+          col[t] = acc;
+          s += acc;
+        }
+        const float mu = s / ncol;
+        float q = 0.f;
+        for (int t = 0; t < ncol; ++t) q += (col[t] - mu) * (col[t] - mu);
+        const float sdv = fmaxf(sqrtf(q / (float)(ncol - 1)), 1e-8f);
+        for (int t = 0; t < ncol; ++t) {
+          int ts, a;
+          if (p.noise_kind == 1) {  // raw time: (t, ch) -> solver step t / block, dim (t % block) * chans + ch
+            ts = t / p.raw_block;
+            a = (t - ts * p.raw_block) * chans + ch;
+          } else {  // block: channel ch is action dim, t is solver step
+            ts = t;
+            a = ch;
+          }
+          const int i = ts * p.A + a;
+          v[i] = (col[t] / sdv) * sd[i] + mean[i];
+        }
+      }
+    }
+  }
+  if (p.low) {
+    for (int i = 0; i < TA; ++i) v[i] = fminf(fmaxf(v[i], p.low[i % p.A]), p.high[i % p.A]);
+  }
+  for (int i = 0; i < TA; ++i) out[i] = v[i];
+}
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  if (isnan(f)) return 0xFFFFFFFFu;
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+constexpr int kRefitThreads = 512;
+constexpr int kMaxSort = 4096;
+
+__global__ void __launch_bounds__(kRefitThreads) k_refit(RefitParams p) {
+  __shared__ unsigned long long keys[kMaxSort];
+  const int env = blockIdx.x, tid = threadIdx.x;
+  int P = 1;
+  while (P < p.S) P <<= 1;
+  const float* costs = p.costs + (size_t)env * p.S;
+  for (int i = tid; i < P; i += kRefitThreads) {
+    const uint32_t k = (i < p.S) ? order_key(costs[i]) : 0xFFFFFFFFu;
+    keys[i] = ((unsigned long long)k << 32) | (unsigned)i;
+  }
+  __syncthreads();
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < P; i += kRefitThreads) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool up = (i & size) == 0;
+          const unsigned long long a = keys[i], b = keys[j];
+          if ((a > b) == up) {
+            keys[i] = b;
+            keys[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  const int TA = p.T * p.A;
+  const float* cand = p.cand + (size_t)env * p.S * TA;
+  if (tid < p.k) {
+    const int idx = (int)(keys[tid] & 0xFFFFFFFFull);
+    if (p.topk_idx) p.topk_idx[(size_t)env * p.k + tid] = idx;
+    if (p.topk_val) p.topk_val[(size_t)env * p.k + tid] = costs[idx];
+  }
+  if (tid == 0) {
+    float s = 0.f;
+    for (int i = 0; i < p.k; ++i) s += costs[(int)(keys[i] & 0xFFFFFFFFull)];
+    p.final_cost[env] = s / (float)p.k;
+  }
+  for (int e = tid; e < p.R * TA; e += kRefitThreads) {
+    const int i = e / TA, d = e - i * TA;
+    const int idx = (int)(keys[i] & 0xFFFFFFFFull);
+    p.elites[((size_t)env * p.R + i) * TA + d] = cand[(size_t)idx * TA + d];
+  }
+  if (tid < TA) {
+    const int d = tid;
+    float s = 0.f;
+    for (int i = 0; i < p.k; ++i) s += cand[(size_t)(keys[i] & 0xFFFFFFFFull) * TA + d];
+    const float mu = s / (float)p.k;
+    float q = 0.f;
+    for (int i = 0; i < p.k; ++i) {
+      const float dv = cand[(size_t)(keys[i] & 0xFFFFFFFFull) * TA + d] - mu;
+      q += dv * dv;
+    }
+    const float sdv = sqrtf(q / (float)(p.k - 1));
+    const size_t o = (size_t)env * TA + d;
+    p.best[o] = cand[(size_t)(keys[0] & 0xFFFFFFFFull) * TA + d];
+    if (p.alpha != 0.f) {
+      p.mean[o] = p.alpha * p.mean[o] + (1.0f - p.alpha) * mu;
+      p.stdv[o] = p.alpha * p.stdv[o] + (1.0f - p.alpha) * sdv;
+    } else {
+      p.mean[o] = mu;
+      p.stdv[o] = sdv;
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_sample(const SampleParams& p, cudaStream_t st) {
+  if (p.T * p.A > kMaxTA || p.ncol > kMaxCol) return cudaErrorInvalidValue;
+  const int n = p.B * p.S;
+  k_sample<<<(n + 127) / 128, 128, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_refit(const RefitParams& p, cudaStream_t st) {
+  if (p.S > kMaxSort || p.T * p.A > kMaxTA || p.k > p.S || p.k < 1 || p.k > kRefitThreads) return cudaErrorInvalidValue;
+  k_refit<<<p.B, kRefitThreads, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace lewm

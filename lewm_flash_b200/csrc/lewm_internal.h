@@ -1,0 +1,181 @@
+// Internal layouts shared by the kernels and the C-ABI layer.
+//
+// Device memory layout (all bf16 operand tiles are K-major, 128-byte
+// swizzled [rows x 64] blocks, so one bulk copy lands a block ready for
+// tcgen05.mma):
+//
+//   weights (read-only, packed once by lewm_create)
+//     qkv  [L][heads][D/64]      blocks of [192 x 64]   rows = q|k|v of one head
+//     wout [L][4][inner/64]      blocks of [D/4 x 64]
+//     w1   [L][mlp/128][D/64]    blocks of [128 x 64]
+//     w2   [L][4][mlp/64]        blocks of [D/4 x 64]
+//     wada [L*6D/NT_ADA][D/64]   blocks of [NT_ADA x 64]   (all layers stacked)
+//     we2  [eh/128][2]           blocks of [D x 64]        (Embedder Linear 2)
+//   activations (per plan / model-cost call)
+//     act_a [ceil(NC*T/128)][D/64] blocks of [128 x 64]  SiLU(action embedding)
+//     mod   [NC*T][L*6D] bf16   AdaLN shift/scale/gate per (candidate, time, layer)
+//     x     [tiles][128][D] fp32  residual stream of one window
+//     attn  [tiles][inner/64] blocks of [128 x 64]  attention output
+//     h     [tiles][mlp/64]   blocks of [128 x 64]  GELU(FFN hidden)
+//     pred  [NC][T-H+1][D] fp32  predicted embeddings appended to the history
+//
+// A window tile holds floor(128 / w) whole candidates (w = window tokens),
+// row = local_candidate * w + position, so attention never crosses tiles.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+namespace lewm {
+
+constexpr int kDimHead = 64;
+constexpr int kTileM = 128;
+
+struct DevWeights {
+  const __nv_bfloat16* qkv;
+  const __nv_bfloat16* wout;
+  const __nv_bfloat16* w1;
+  const __nv_bfloat16* w2;
+  const __nv_bfloat16* wada;
+  const __nv_bfloat16* we2;
+  const float* pos;        // [frames][D]
+  const float* ada_b;      // [L][6D]
+  const float* attn_ln_w;  // [L][D]
+  const float* attn_ln_b;  // [L][D]
+  const float* out_b;      // [L][D]
+  const float* ffn_ln_w;   // [L][D]
+  const float* ffn_ln_b;   // [L][D]
+  const float* b1;         // [L][mlp]
+  const float* b2;         // [L][D]
+  const float* fin_w;      // [D]
+  const float* fin_b;      // [D]
+  const float* conv_w;     // [A'][A]
+  const float* conv_b;     // [A']
+  const float* e1_w;       // [eh][A']
+  const float* e1_b;       // [eh]
+  const float* e2_b;       // [D]
+};
+
+struct ModelDims {
+  int D, L, heads, inner, mlp, A, As, eh, frames;
+};
+
+// One predictor call of the rollout over every candidate.
+struct CallGeom {
+  int n_cand;   // candidates in flight (envs * samples)
+  int S;        // samples per env (candidate -> env mapping)
+  int T, H;     // horizon, history length
+  int w;        // window tokens
+  int start;    // history index of window position 0
+  int cpt;      // candidates per tile
+  int n_tiles;  // window tiles
+  int call;     // prediction slot written by this call
+  int last;     // 1: final call, write costs
+};
+
+struct RolloutBufs {
+  const float* emb;   // (B,H,D) or (NC,H,D)
+  int emb_per_cand;
+  const float* goal;  // (B,D) or (NC,D)
+  int goal_per_cand;
+  const float* cand;  // (NC,T,A)
+  __nv_bfloat16* act_a;
+  __nv_bfloat16* mod;
+  float* x;
+  __nv_bfloat16* attn;
+  __nv_bfloat16* h;
+  float* pred;
+  float* costs;
+};
+
+// Optional per-launch event profiler (host side). When `on`, every launch site
+// records an event pair and the algorithmic FLOPs of that launch under a kernel
+// class; lewm_profile_plan sums them after a synchronize.
+enum KernelClass { KC_EMBED = 0, KC_ADALN, KC_QKV_ATTN, KC_OUT, KC_FC1, KC_FC2, KC_FINAL, KC_SAMPLE, KC_REFIT,
+                   KC_COUNT };
+struct Prof {
+  bool on = false;
+  struct Rec {
+    int cls;
+    double flops;
+    cudaEvent_t a, b;
+  };
+  std::vector<Rec> recs;
+  std::vector<cudaEvent_t> pool;
+  size_t used = 0;
+  cudaEvent_t take() {
+    if (used == pool.size()) {
+      cudaEvent_t e;
+      cudaEventCreate(&e);
+      pool.push_back(e);
+    }
+    return pool[used++];
+  }
+  void begin(cudaStream_t s) {
+    if (!on) return;
+    cur_a = take();
+    cudaEventRecord(cur_a, s);
+  }
+  void end(int cls, double flops, cudaStream_t s) {
+    if (!on) return;
+    cudaEvent_t b = take();
+    cudaEventRecord(b, s);
+    recs.push_back(Rec{cls, flops, cur_a, b});
+  }
+  void reset() {
+    recs.clear();
+    used = 0;
+  }
+  ~Prof() {
+    for (auto e : pool) cudaEventDestroy(e);
+  }
+  cudaEvent_t cur_a = nullptr;
+};
+
+// Launchers (rollout_kernels.cu). All asynchronous on `st`; `prof` may be null.
+cudaError_t launch_embed(const ModelDims& md, const DevWeights& w, const float* cand, int rows,
+                         __nv_bfloat16* act_a, uint32_t* status, cudaStream_t st, Prof* prof);
+cudaError_t launch_adaln(const ModelDims& md, const DevWeights& w, int rows, const __nv_bfloat16* act_a,
+                         __nv_bfloat16* mod, uint32_t* status, cudaStream_t st, Prof* prof);
+cudaError_t launch_call(const ModelDims& md, const DevWeights& w, const CallGeom& g, const RolloutBufs& b,
+                        uint32_t* status, cudaStream_t st, Prof* prof);
+
+// iCEM kernels (icem_kernels.cu).
+struct SampleParams {
+  int B, S, T, A;
+  int noise_kind;     // 0 white, 1 raw-time colored, 2 block colored
+  int raw_block;      // action_block for raw-time coloring
+  int ncol;           // colored time length (T*block or T)
+  const float* W;     // [ncol][ncol] coloring matrix (fp32)
+  const float* noise; // injected noise (B,S,T,A) or null
+  uint32_t seed_lo, plan_id, iter;
+  const float* mean;  // (B,T,A)
+  const float* stdv;  // (B,T,A)
+  const float* elites;  // (B,elite_stride,T,A) previous sorted elites
+  int elite_stride;
+  int n_inject;       // slots 1..n_inject take elites 0..n_inject-1
+  const float* low;   // (A) or null
+  const float* high;
+  float* cand;        // (B,S,T,A)
+};
+cudaError_t launch_sample(const SampleParams& p, cudaStream_t st);
+
+struct RefitParams {
+  int B, S, T, A, k, R;
+  const float* costs;   // (B,S)
+  const float* cand;    // (B,S,T,A)
+  float* mean;          // (B,T,A) in/out
+  float* stdv;          // (B,T,A) in/out
+  float alpha;          // momentum
+  float* elites;        // (B,R,T,A) out: R best elites, ascending cost
+  float* best;          // (B,T,A) out: best elite
+  float* final_cost;    // (B) out: mean of the k smallest costs
+  int32_t* topk_idx;    // (B,k) out or null
+  float* topk_val;      // (B,k) out or null
+};
+cudaError_t launch_refit(const RefitParams& p, cudaStream_t st);
+
+}  // namespace lewm

@@ -1,0 +1,473 @@
+"""Drop-in iCEM / CEM solvers and model-cost helper backed by the B200 kernels.
+
+* ``B200ICEMSolver`` takes exactly the constructor arguments of the reference
+  ``ICEMSolver`` (``lewm/solvers/icem.py:258-322``), raises the same
+  ``ValueError``s, exposes the same properties and ``configure`` /
+  ``sample_counts`` / ``model_cost_evals_per_solve`` / ``solve`` / ``__call__``
+  surface and returns the same ``solve`` dict (CPU ``actions``, ``mean``,
+  ``var``, ``costs`` and, with callbacks, ``callbacks``). A Hydra config swaps
+  ``_target_: lewm.solvers.icem.ICEMSolver`` for
+  ``lewm_flash_b200.solver.B200ICEMSolver``.
+* ``B200CEMSolver`` is ``CEMExactSolver`` (``lewm/solvers/cem_exact.py:54-383``):
+  iCEM with every feature off, plus its receding-horizon warm start.
+* ``run_static_icem_chain`` mirrors the reference tensor-only chain
+  (``lewm/solvers/icem_static_compile.py:61-114``) with injected noise.
+* ``B200ModelCost`` / ``install_model_cost`` replace
+  ``JEPA.get_cost_from_embeddings`` (``lewm/jepa.py:302-317``).
+
+All envs of a ``solve`` run as one batched device plan; ``batch_size`` is
+accepted for interface compatibility. Noise comes from a counter-based Philox
+stream keyed by (seed, solve index, iteration, env, candidate) instead of the
+reference's sequential torch generator, so a given seed gives a different (but
+deterministic) stream than the reference; parity with the reference is checked
+by injecting the reference's noise (``run_static_icem_chain``).
+"""
+
+from __future__ import annotations
+
+import math
+import warnings
+from typing import Any, List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import runtime as rt_mod
+from .runtime import PlanOptions, Runtime
+
+COLORED_NOISE_BETA = {"none": 0.0, "pink": 1.0, "brown": 2.0}
+
+
+def _runtime(model, device) -> Runtime:
+    if isinstance(model, Runtime):
+        return model
+    cache = getattr(model, "_lewm_b200_runtimes", None)
+    if cache is None:
+        cache = {}
+        try:
+            setattr(model, "_lewm_b200_runtimes", cache)
+        except Exception:  # pragma: no cover
+            pass
+    dev = torch.device(device)
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    if key not in cache:
+        from .model import extract_state_dict, infer_desc
+
+        desc = infer_desc(model)
+        cache[key] = Runtime(desc, extract_state_dict(model, desc), torch.device("cuda", key))
+    return cache[key]
+
+
+def prepare_init_action(model: Any, info_dict: dict, init_action: Optional[torch.Tensor], horizon: int, *,
+                        n_envs: int, action_dim: int) -> torch.Tensor:
+    """Warm-start padding of ``prepare_init_action`` (reference ``lewm/solvers/cem_exact.py:13-51``)."""
+    if init_action is not None:
+        assert init_action.shape[0] == n_envs, f"init_action batch size {init_action.shape[0]} != n_envs {n_envs}"
+        assert init_action.shape[2] == action_dim, (
+            f"init_action action_dim {init_action.shape[2]} != action_dim {action_dim}")
+    n_prev = init_action.shape[1] if init_action is not None else 0
+    remaining = horizon - n_prev
+    if remaining <= 0:
+        return init_action
+    if not hasattr(model, "get_action"):
+        device = init_action.device if init_action is not None else "cpu"
+        tail = torch.zeros(n_envs, remaining, action_dim, device=device)
+        return torch.cat([init_action, tail], dim=1) if init_action is not None else tail
+    with torch.no_grad():
+        tail = model.get_action(info_dict, horizon=remaining, prefix_actions=init_action)
+    return torch.cat([init_action.to(tail.device), tail], dim=1) if init_action is not None else tail
+
+
+class B200ICEMSolver:
+    """iCEM solver whose whole iteration loop runs on the B200 plan kernels."""
+
+    defer_cpu_materialization = True
+
+    def __init__(
+        self,
+        model: Any,
+        batch_size: int = 1,
+        num_samples: int = 300,
+        var_scale: float = 1.0,
+        n_steps: int = 30,
+        topk: int = 30,
+        device: str | torch.device = "cuda",
+        seed: int = 1234,
+        elite_retention: int = 0,
+        colored_noise: str = "none",
+        colored_noise_time: str = "raw",
+        momentum_alpha: float = 0.0,
+        sample_decay: float = 1.0,
+        sample_count_bucket_size: int = 0,
+        return_best_elite: bool = False,
+        clip_actions: bool = False,
+        callbacks: list[Any] | None = None,
+        history_size: int = 3,
+    ) -> None:
+        if topk <= 0:
+            raise ValueError(f"topk must be positive, got {topk}")
+        if num_samples < topk:
+            raise ValueError(f"num_samples={num_samples} must be >= topk={topk}")
+        if n_steps <= 0:
+            raise ValueError(f"n_steps must be positive, got {n_steps}")
+        if elite_retention < 0:
+            raise ValueError(f"elite_retention must be non-negative, got {elite_retention}")
+        if colored_noise not in COLORED_NOISE_BETA:
+            raise ValueError(
+                f"colored_noise must be one of {sorted(COLORED_NOISE_BETA)}, got {colored_noise!r}")
+        if not 0.0 <= momentum_alpha < 1.0:
+            raise ValueError(f"momentum_alpha must satisfy 0 <= alpha < 1, got {momentum_alpha}")
+        if sample_decay < 1.0:
+            raise ValueError(f"sample_decay must be >= 1.0, got {sample_decay}")
+        if sample_count_bucket_size < 0:
+            raise ValueError(f"sample_count_bucket_size must be non-negative, got {sample_count_bucket_size}")
+        if colored_noise_time not in ("block", "raw"):
+            raise ValueError(f"colored noise time_axis must be 'block' or 'raw', got {colored_noise_time!r}")
+        self.model = model
+        self.batch_size = batch_size
+        self.var_scale = var_scale
+        self.num_samples = num_samples
+        self.n_steps = n_steps
+        self.topk = topk
+        self.device = torch.device(device)
+        self.seed = int(seed)
+        self.elite_retention = elite_retention
+        self.colored_noise = colored_noise
+        self.colored_noise_time = colored_noise_time
+        self.momentum_alpha = float(momentum_alpha)
+        self.sample_decay = float(sample_decay)
+        self.sample_count_bucket_size = int(sample_count_bucket_size)
+        self.return_best_elite = bool(return_best_elite)
+        self.clip_actions = bool(clip_actions)
+        self.callbacks = list(callbacks) if callbacks else []
+        self.history_size = int(history_size)
+        self._action_low: torch.Tensor | None = None
+        self._action_high: torch.Tensor | None = None
+        self._solves = 0
+        try:
+            self._dtype = next(model.parameters()).dtype
+        except (AttributeError, StopIteration, TypeError):
+            self._dtype = torch.float32
+
+    # ------------------------------------------------------------------ reference surface
+    def configure(self, *, action_space: Any, n_envs: int, config: Any) -> None:
+        self._action_space = action_space
+        self._n_envs = n_envs
+        self._config = config
+        self._action_dim = int(np.prod(action_space.shape[1:]))
+        self._configured = True
+        if "Box" not in type(action_space).__name__:
+            warnings.warn(f"Action space is not Box-like, got {type(action_space)}. "
+                          "ICEMSolver may not work as expected.", RuntimeWarning, stacklevel=2)
+            return
+        if self.clip_actions and hasattr(action_space, "low") and hasattr(action_space, "high"):
+            self._action_low = torch.as_tensor(action_space.low[0], device=self.device,
+                                               dtype=self.dtype).repeat(self._config.action_block)
+            self._action_high = torch.as_tensor(action_space.high[0], device=self.device,
+                                                dtype=self.dtype).repeat(self._config.action_block)
+        for cb in self.callbacks:
+            configure = getattr(cb, "configure", None)
+            if callable(configure):
+                configure(action_low=self._action_low, action_high=self._action_high)
+
+    @property
+    def n_envs(self) -> int:
+        return self._n_envs
+
+    @property
+    def action_dim(self) -> int:
+        return self._action_dim * self._config.action_block
+
+    @property
+    def horizon(self) -> int:
+        return self._config.horizon
+
+    @property
+    def action_block(self) -> int:
+        return int(getattr(self._config, "action_block", 1))
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return self._dtype
+
+    def __call__(self, *args: Any, **kwargs: Any) -> dict[str, Any]:
+        return self.solve(*args, **kwargs)
+
+    def sample_count_for_step(self, step: int) -> int:
+        if self.sample_decay == 1.0:
+            return self.num_samples
+        decayed = int(math.ceil(self.num_samples * (self.sample_decay ** (-step))))
+        count = max(decayed, min(self.num_samples, 2 * self.topk))
+        if self.sample_count_bucket_size > 0:
+            count = min(self.num_samples,
+                        int(math.ceil(count / self.sample_count_bucket_size)) * self.sample_count_bucket_size)
+        return count
+
+    def sample_counts(self) -> list[int]:
+        return [self.sample_count_for_step(step) for step in range(self.n_steps)]
+
+    def model_cost_evals_per_solve(self) -> int:
+        return sum(self.sample_counts())
+
+    def init_action_distrib(self, n_envs: int, actions: torch.Tensor | None = None):
+        var = self.var_scale * torch.ones([n_envs, self.horizon, self.action_dim], dtype=self.dtype)
+        mean = torch.zeros([n_envs, 0, self.action_dim], dtype=self.dtype) if actions is None else actions
+        remaining = self.horizon - mean.shape[1]
+        if remaining > 0:
+            new_mean = torch.zeros([n_envs, remaining, self.action_dim], dtype=self.dtype, device=mean.device)
+            mean = torch.cat([mean, new_mean], dim=1)
+        return mean, var
+
+    # ------------------------------------------------------------------ B200 specifics
+    def plan_options(self) -> PlanOptions:
+        return PlanOptions(
+            num_samples=self.num_samples, topk=self.topk, n_steps=self.n_steps, sample_decay=self.sample_decay,
+            sample_count_bucket_size=self.sample_count_bucket_size, elite_retention=self.elite_retention,
+            beta=COLORED_NOISE_BETA[self.colored_noise], time_axis=self.colored_noise_time,
+            action_block=self.action_block, momentum_alpha=self.momentum_alpha,
+            return_best_elite=self.return_best_elite, clip_actions=self._action_low is not None,
+            history_size=self.history_size, seed=self.seed)
+
+    @property
+    def runtime(self) -> Runtime:
+        return _runtime(self.model, self.device)
+
+    def _cost_embeddings(self, info_dict: dict, total_envs: int):
+        """(emb (B,H,D), goal_emb (B,G,D)) -- cached tensors if given, else the model's encoder.
+
+        The encoder path mirrors ``ICEMStaticCompileSolver._prepare_cost_embeddings``
+        (reference ``lewm/solvers/icem_static_compile.py:212-238``).
+        """
+        emb = info_dict.get("emb")
+        goal = info_dict.get("goal_emb")
+        if torch.is_tensor(emb) and torch.is_tensor(goal) and emb.ndim == 3:
+            return emb, goal
+        expanded = {}
+        for key, value in info_dict.items():
+            if torch.is_tensor(value):
+                tgt = self.dtype if value.is_floating_point() else None
+                expanded[key] = value.to(device=self.device, dtype=tgt).unsqueeze(1)
+            elif isinstance(value, np.ndarray):
+                expanded[key] = value[:, None]
+            else:
+                expanded[key] = value
+        dummy = torch.zeros(total_envs, 1, self.horizon, self.action_dim, device=self.device, dtype=self.dtype)
+        if not hasattr(self.model, "_ensure_cost_embeddings"):
+            raise RuntimeError("B200ICEMSolver needs emb/goal_emb in info_dict or a JEPA with _ensure_cost_embeddings")
+        emb, goal = self.model._ensure_cost_embeddings(expanded, dummy)
+        if emb.ndim == 4:
+            emb = emb[:, 0]
+        if goal.ndim == 4:
+            goal = goal[:, 0]
+        return emb, goal
+
+    def _plan(self, info_dict: dict, mean: torch.Tensor, var: torch.Tensor, trace: bool):
+        total_envs = mean.shape[0]
+        emb, goal = self._cost_embeddings(info_dict, total_envs)
+        rt = self.runtime
+        opts = self.plan_options()
+        plan_index = self._solves
+        self._solves += 1
+        return rt.plan(opts, emb, goal, mean, var, action_low=self._action_low, action_high=self._action_high,
+                       trace=trace, plan_index=plan_index)
+
+    @torch.inference_mode()
+    def solve(self, info_dict: dict, init_action: torch.Tensor | None = None) -> dict[str, Any]:
+        outputs: dict[str, Any] = {"costs": [], "mean": [], "var": []}
+        total_envs = len(next(iter(info_dict.values())))
+        init_action = prepare_init_action(self.model, info_dict, init_action, self.horizon, n_envs=total_envs,
+                                          action_dim=self.action_dim)
+        mean, var = self.init_action_distrib(total_envs, init_action)
+        mean = mean.to(self.device)
+        var = var.to(self.device)
+        for cb in self.callbacks:
+            cb.reset()
+        actions, std, fcost, tr = self._plan(info_dict, mean, var, trace=bool(self.callbacks))
+        if self.callbacks:
+            self._replay_callbacks(tr, mean, var)
+        # One device->host read per solve (reference lewm/solvers/icem.py:589-593).
+        outputs["costs"].extend(fcost.cpu().tolist())
+        self.runtime.sync()
+        actions_cpu = actions.detach().cpu()
+        outputs["actions"] = actions_cpu
+        outputs["mean"] = [actions_cpu.clone()]
+        outputs["var"] = [std.detach().cpu()]
+        if self.callbacks:
+            outputs["callbacks"] = {}
+            for cb in self.callbacks:
+                cb.end_solve()
+                outputs["callbacks"][cb.output_key] = cb.history
+        return outputs
+
+    def _replay_callbacks(self, tr, mean0, var0) -> None:
+        """Feed the per-iteration plan trace to the reference callback protocol (icem.py:565-578)."""
+        for cb in self.callbacks:
+            cb.start_batch()
+        prev_mean, prev_var = mean0, var0
+        for step, n in enumerate(tr["counts"]):
+            cand = tr["candidates"][step][:, :n]
+            costs = tr["costs"][step][:, :n]
+            inds = tr["topk_idx"][step].long()
+            vals = tr["topk_val"][step]
+            topk_cand = torch.gather(cand, 1, inds[:, :, None, None].expand(-1, -1, cand.shape[2], cand.shape[3]))
+            m, v = tr["mean"][step], tr["std"][step]
+            for cb in self.callbacks:
+                cb(step=step, candidates=cand, costs=costs, topk_vals=vals, topk_inds=inds,
+                   topk_candidates=topk_cand, mean=m, var=v, prev_mean=prev_mean, prev_var=prev_var, n_samples=n)
+            prev_mean, prev_var = m, v
+
+
+class B200CEMSolver(B200ICEMSolver):
+    """``CEMExactSolver`` semantics (reference ``lewm/solvers/cem_exact.py:54-383``) on the B200 kernels.
+
+    iCEM with every feature off is CEM (reference ``tests/test_lewm_icem.py:56-96``).
+    ``warm_start`` shifts the previous solve's mean/var by the receding horizon
+    (``_shift_warm_start_distribution``, ``cem_exact.py:193-241``).
+    """
+
+    def __init__(self, model: Any, batch_size: int = 1, num_samples: int = 300, var_scale: float = 1.0,
+                 n_steps: int = 30, topk: int = 30, device: str | torch.device = "cuda", seed: int = 1234,
+                 warm_start: bool = False, callbacks: list[Any] | None = None, history_size: int = 3) -> None:
+        super().__init__(model, batch_size=batch_size, num_samples=num_samples, var_scale=var_scale, n_steps=n_steps,
+                         topk=topk, device=device, seed=seed, callbacks=callbacks, history_size=history_size)
+        self.warm_start = bool(warm_start)
+        self._warm_mean: torch.Tensor | None = None
+        self._warm_var: torch.Tensor | None = None
+        self._last_warm_start_info = {"enabled": self.warm_start, "used": False, "reset": False, "reset_reason": None}
+
+    def configure(self, *, action_space: Any, n_envs: int, config: Any) -> None:
+        super().configure(action_space=action_space, n_envs=n_envs, config=config)
+        self.reset_warm_start_state("configure")
+
+    @property
+    def receding_horizon(self) -> int:
+        return int(getattr(self._config, "receding_horizon", self.horizon))
+
+    @property
+    def last_warm_start_info(self) -> dict:
+        return dict(self._last_warm_start_info)
+
+    def reset_warm_start_state(self, reason: str = "manual") -> None:
+        self._warm_mean = None
+        self._warm_var = None
+        self._last_warm_start_info = {"enabled": self.warm_start, "used": False, "reset": True,
+                                      "reset_reason": reason}
+
+    def _shift(self, mean: torch.Tensor, var: torch.Tensor):
+        info = {"enabled": self.warm_start, "used": False, "reset": False, "reset_reason": None,
+                "receding_horizon": self.receding_horizon}
+        if not self.warm_start:
+            self._last_warm_start_info = info
+            return mean, var
+        shift = self.receding_horizon
+        if shift <= 0 or shift >= self.horizon:
+            info["reset"] = shift >= self.horizon
+            info["reset_reason"] = "no_unexecuted_tail" if shift >= self.horizon else "invalid_shift"
+            self._last_warm_start_info = info
+            return mean, var
+        if self._warm_mean is None or self._warm_mean.shape != mean.shape:
+            had = self._warm_mean is not None
+            self._warm_mean = self._warm_var = None
+            info["reset"] = had
+            info["reset_reason"] = "signature_mismatch" if had else "no_previous_state"
+            self._last_warm_start_info = info
+            return mean, var
+        m = torch.zeros_like(mean)
+        v = self.var_scale * torch.ones_like(var)
+        m[:, :-shift] = self._warm_mean[:, shift:].to(mean)
+        v[:, :-shift] = self._warm_var[:, shift:].to(var)
+        info["used"] = True
+        self._last_warm_start_info = info
+        return m, v
+
+    @torch.inference_mode()
+    def solve(self, info_dict: dict, init_action: torch.Tensor | None = None) -> dict[str, Any]:
+        total_envs = len(next(iter(info_dict.values())))
+        init_action = prepare_init_action(self.model, info_dict, init_action, self.horizon, n_envs=total_envs,
+                                          action_dim=self.action_dim)
+        mean, var = self.init_action_distrib(total_envs, init_action)
+        mean, var = self._shift(mean.to(self.device), var.to(self.device))
+        for cb in self.callbacks:
+            cb.reset()
+        actions, std, fcost, tr = self._plan(info_dict, mean, var, trace=bool(self.callbacks))
+        if self.callbacks:
+            self._replay_callbacks(tr, mean, var)
+        costs = fcost.cpu().tolist()
+        self.runtime.sync()
+        out = {"costs": costs, "actions": actions.cpu(), "mean": [actions.cpu()], "var": [std.cpu()],
+               "warm_start": self.last_warm_start_info}
+        if self.warm_start:
+            self._warm_mean, self._warm_var = actions.detach().clone(), std.detach().clone()
+        if self.callbacks:
+            out["callbacks"] = {}
+            for cb in self.callbacks:
+                cb.end_solve()
+                out["callbacks"][cb.output_key] = cb.history
+        return out
+
+
+def run_static_icem_chain(model, emb: torch.Tensor, goal_emb: torch.Tensor, mean: torch.Tensor, var: torch.Tensor,
+                          noise_steps: Sequence[torch.Tensor], *, topk: int, elite_retention: int = 0,
+                          momentum_alpha: float = 0.0, return_best_elite: bool = False,
+                          action_low: Optional[torch.Tensor] = None, action_high: Optional[torch.Tensor] = None,
+                          history_size: int = 3):
+    """Reference ``run_static_icem_chain`` (``lewm/solvers/icem_static_compile.py:61-114``) as one device plan.
+
+    ``model`` is a reference ``JEPA`` (its predictor replaces ``cost_fn``) or a
+    ``Runtime``. Each noise step is (B, S_i, T, A) post-coloring noise.
+    Returns (actions_or_best_elite, std, final_cost) on the device.
+    """
+    rt = _runtime(model, mean.device if mean.is_cuda else "cuda")
+    counts = [int(n.shape[1]) for n in noise_steps]
+    S = max(counts)
+    # The plan derives per-iteration counts from (S, decay, bucket); encode the given
+    # counts through a schedule that reproduces them exactly.
+    opts = PlanOptions(num_samples=S, topk=topk, n_steps=len(counts), elite_retention=elite_retention,
+                       momentum_alpha=momentum_alpha, return_best_elite=return_best_elite,
+                       clip_actions=action_low is not None and action_high is not None, history_size=history_size)
+    _fit_schedule(opts, counts)
+    actions, std, fcost, _ = rt.plan(opts, emb, goal_emb, mean, var, noise_steps=list(noise_steps),
+                                     action_low=action_low, action_high=action_high)
+    return actions, std, fcost
+
+
+def _fit_schedule(opts: PlanOptions, counts: List[int]) -> None:
+    """Find (sample_decay, bucket) whose schedule equals ``counts`` (fixed S, or an ICEMSolver schedule)."""
+    S = opts.num_samples
+    if all(c == S for c in counts):
+        opts.sample_decay, opts.sample_count_bucket_size = 1.0, 0
+        return
+    from itertools import product
+
+    for decay, bucket in product([1.25, 1.5, 2.0, 1.1, 1.2, 1.3, 1.75, 3.0], [0] + sorted({c for c in counts})):
+        opts.sample_decay, opts.sample_count_bucket_size = decay, bucket
+        got = rt_mod.sample_counts(opts)
+        if got == counts:
+            return
+    raise ValueError(f"noise step sample counts {counts} do not follow an iCEM schedule")
+
+
+class B200ModelCost:
+    """``JEPA.get_cost_from_embeddings`` on the B200 kernels (reference ``lewm/jepa.py:302-317``)."""
+
+    def __init__(self, model, device="cuda"):
+        self.model = model
+        self.device = torch.device(device)
+
+    @property
+    def runtime(self) -> Runtime:
+        return _runtime(self.model, self.device)
+
+    def get_cost_from_embeddings(self, emb: torch.Tensor, goal_emb: torch.Tensor, action_candidates: torch.Tensor,
+                                 history_size: int = 3) -> torch.Tensor:
+        return self.runtime.model_cost(emb, goal_emb, action_candidates, history_size=history_size)
+
+    __call__ = get_cost_from_embeddings
+
+
+def install_model_cost(model, device="cuda"):
+    """Route ``model.get_cost_from_embeddings`` (and so the reference's compile_cost
+    ``JEPA.get_cost`` path, ``lewm/jepa.py:357-359``) through the B200 kernels."""
+    mc = B200ModelCost(model, device)
+    model.get_cost_from_embeddings = mc.get_cost_from_embeddings
+    return mc

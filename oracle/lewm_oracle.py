@@ -60,10 +60,12 @@ def gelu(x):
 
 
 def linear(x, w, b=None):
-    y = x @ w.T
+    """``nn.Linear``; flattened to one 2-D GEMM so numpy hands it to BLAS in one call."""
+    lead = x.shape[:-1]
+    y = np.ascontiguousarray(x, dtype=F32).reshape(-1, x.shape[-1]) @ w.T
     if b is not None:
-        y = y + b
-    return y.astype(F32, copy=False)
+        y += b
+    return y.reshape(*lead, w.shape[0]).astype(F32, copy=False)
 
 
 def embedder(act, sd: Mapping[str, np.ndarray], prefix: str = "action_encoder."):

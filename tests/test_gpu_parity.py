@@ -1,0 +1,289 @@
+"""CUDA path vs the oracle and the reference's golden outputs, through the C ABI.
+
+Tolerances: the rollout computes GEMMs in bf16 with fp32 accumulation, so
+per-candidate costs must match the reference fp32 path within 1e-2 relative
+(the bf16 rollout bound); selection / refit given the same costs is exact on
+indices; sampling given the same noise matches to float32 rounding.
+"""
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from lewm_flash_b200.model import ModelDesc, STRESS_DESC, synthetic_state_dict
+from lewm_flash_b200.runtime import PlanOptions, Runtime
+from oracle import icem_oracle as io
+from oracle import lewm_oracle as lo
+from tests.golden_io import CHAIN_CASES, load, weights_of
+
+pytestmark = pytest.mark.gpu
+
+COST_RTOL = 1e-2  # bf16 rollout vs fp32 reference, relative, per candidate
+
+_RT = {}
+
+
+def runtime(desc: ModelDesc, seed: int) -> Runtime:
+    key = (desc, seed)
+    if key not in _RT:
+        _RT[key] = Runtime(desc, synthetic_state_dict(desc, seed), "cuda:0")
+    return _RT[key]
+
+
+def cuda(x):
+    return torch.as_tensor(np.asarray(x), dtype=torch.float32, device="cuda:0")
+
+
+def rel_err(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    return np.abs(got - want) / np.maximum(np.abs(want), 1e-6)
+
+
+@pytest.mark.parametrize("case", ["model_cost_full_h1.npz", "model_cost_full_h3.npz", "model_cost_stress_h3.npz"])
+def test_model_cost_matches_reference_golden(case):
+    d = load(case)
+    desc, sd = weights_of(d)
+    rt = runtime(desc, int(d["seed"]))
+    got = rt.model_cost(cuda(d["emb"]), cuda(d["goal"]), cuda(d["cand"])).cpu().numpy()
+    rt.sync()
+    err = rel_err(got, d["cost"])
+    assert err.max() <= COST_RTOL, f"max rel err {err.max():.3e}"
+
+
+@pytest.mark.parametrize("H,B,S,emb_rank4", [(1, 2, 300, False), (3, 2, 100, False), (3, 1, 64, True),
+                                              (2, 1, 50, False), (5, 1, 10, False)])
+def test_model_cost_matches_oracle(H, B, S, emb_rank4):
+    desc = ModelDesc()
+    sd = synthetic_state_dict(desc, 0)
+    rt = runtime(desc, 0)
+    rng = np.random.default_rng(H * 100 + S)
+    emb = rng.standard_normal((B, S, H, desc.dim) if emb_rank4 else (B, H, desc.dim)).astype(np.float32)
+    goal = rng.standard_normal((B, 1, desc.dim)).astype(np.float32)
+    cand = rng.standard_normal((B, S, 5, desc.action_dim)).astype(np.float32)
+    want = lo.get_cost_from_embeddings(emb, goal, cand, sd, desc)
+    got = rt.model_cost(cuda(emb), cuda(goal), cuda(cand)).cpu().numpy()
+    rt.sync()
+    err = rel_err(got, want)
+    assert err.max() <= COST_RTOL, f"max rel err {err.max():.3e}, median {np.median(err):.3e}"
+    # ranking quality: the bf16 costs order candidates like the fp32 reference
+    for b in range(B):
+        assert np.corrcoef(got[b], want[b])[0, 1] > 0.99
+
+
+def test_model_cost_per_sample_goal_and_history_window():
+    desc = ModelDesc()
+    sd = synthetic_state_dict(desc, 0)
+    rt = runtime(desc, 0)
+    rng = np.random.default_rng(5)
+    emb = rng.standard_normal((1, 1, desc.dim)).astype(np.float32)
+    goal = rng.standard_normal((1, 7, 2, desc.dim)).astype(np.float32)  # (B,S,G,D): last row per sample
+    cand = rng.standard_normal((1, 7, 5, desc.action_dim)).astype(np.float32)
+    for hs in (1, 2, 3):
+        want = lo.get_cost_from_embeddings(emb, goal, cand, sd, desc, history_size=hs)
+        got = rt.model_cost(cuda(emb), cuda(goal), cuda(cand), history_size=hs).cpu().numpy()
+        assert rel_err(got, want).max() <= COST_RTOL, hs
+
+
+def test_stress_model_cost_matches_oracle():
+    desc = STRESS_DESC
+    sd = synthetic_state_dict(desc, 5)
+    rt = runtime(desc, 5)
+    rng = np.random.default_rng(9)
+    emb = rng.standard_normal((2, 3, desc.dim)).astype(np.float32)
+    goal = rng.standard_normal((2, 1, desc.dim)).astype(np.float32)
+    cand = rng.standard_normal((2, 20, 10, desc.action_dim)).astype(np.float32)
+    want = lo.get_cost_from_embeddings(emb, goal, cand, sd, desc)
+    got = rt.model_cost(cuda(emb), cuda(goal), cuda(cand)).cpu().numpy()
+    rt.sync()
+    assert rel_err(got, want).max() <= COST_RTOL
+
+
+def test_model_cost_is_deterministic_and_batch_independent():
+    desc = ModelDesc()
+    rt = runtime(desc, 0)
+    rng = np.random.default_rng(11)
+    emb = cuda(rng.standard_normal((3, 1, desc.dim)))
+    goal = cuda(rng.standard_normal((3, 1, desc.dim)))
+    cand = cuda(rng.standard_normal((3, 250, 5, desc.action_dim)))
+    a = rt.model_cost(emb, goal, cand)
+    b = rt.model_cost(emb, goal, cand)
+    assert torch.equal(a, b)
+    # each env alone gives the same bits as inside the batch (rows are independent)
+    for e in range(3):
+        single = rt.model_cost(emb[e:e + 1], goal[e:e + 1], cand[e:e + 1])
+        assert torch.equal(single[0], a[e])
+
+
+@pytest.mark.parametrize("case", CHAIN_CASES)
+def test_topk_refit_fed_reference_costs_is_exact(case):
+    d = load(case)
+    kw = json.loads(str(d["solver"]))
+    rt = runtime(ModelDesc(), 0)
+    for i in range(int(d["n_iters"])):
+        costs, cand = d[f"cost_{i}"], d[f"cand_{i}"]
+        B, S, T, A = cand.shape
+        mean = np.zeros((B, T, A), np.float32)
+        std = np.ones((B, T, A), np.float32)
+        out = rt.topk_refit(cuda(costs), cuda(cand), cuda(mean), cuda(std), kw["topk"])
+        assert np.array_equal(out["topk_idx"].cpu().numpy(), d[f"inds_{i}"]), f"iteration {i}"
+        np.testing.assert_array_equal(out["topk_val"].cpu().numpy(), d[f"vals_{i}"])
+        elites = np.take_along_axis(cand, d[f"inds_{i}"][:, :, None, None], 1)
+        em, es = io.refit(elites, mean, std)
+        np.testing.assert_allclose(out["mean"].cpu().numpy(), em, rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(out["std"].cpu().numpy(), es, rtol=1e-5, atol=1e-6)
+        np.testing.assert_array_equal(out["best"].cpu().numpy(), elites[:, 0])
+
+
+@pytest.mark.parametrize("S,k,alpha", [(300, 30, 0.0), (60, 30, 0.3), (3000, 300, 0.0), (7, 1, 0.0), (513, 17, 0.9)])
+def test_topk_refit_matches_oracle(S, k, alpha):
+    rt = runtime(ModelDesc(), 0)
+    rng = np.random.default_rng(S + k)
+    B, T, A = 3, 5, 10
+    costs = rng.standard_normal((B, S)).astype(np.float32) ** 2
+    costs[0, :: 5] = costs[0, 0]          # ties
+    costs[1, 3] = np.nan                   # NaN sorts last
+    cand = rng.standard_normal((B, S, T, A)).astype(np.float32)
+    mean = rng.standard_normal((B, T, A)).astype(np.float32)
+    std = rng.uniform(0.5, 1.5, (B, T, A)).astype(np.float32)
+    out = rt.topk_refit(cuda(costs), cuda(cand), cuda(mean), cuda(std), k, alpha)
+    vals, inds = io.topk_smallest(costs, k)
+    assert np.array_equal(out["topk_idx"].cpu().numpy(), inds)
+    elites = np.take_along_axis(cand, inds[:, :, None, None], 1)
+    em, es = io.refit(elites, mean, std, alpha)
+    if k > 1:
+        np.testing.assert_allclose(out["mean"].cpu().numpy(), em, rtol=1e-5, atol=1e-5)
+        np.testing.assert_allclose(out["std"].cpu().numpy(), es, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(out["final_cost"].cpu().numpy(), vals.mean(1), rtol=1e-5)
+
+
+def test_sampling_injected_noise_matches_reference_formula():
+    rt = runtime(ModelDesc(), 0)
+    rng = np.random.default_rng(3)
+    B, S, T, A = 2, 40, 5, 10
+    mean = rng.standard_normal((B, T, A)).astype(np.float32)
+    std = rng.uniform(0.1, 2.0, (B, T, A)).astype(np.float32)
+    noise = rng.standard_normal((B, S, T, A)).astype(np.float32)
+    lo_, hi_ = -0.8 * np.ones(A, np.float32), 0.8 * np.ones(A, np.float32)
+    for clip in (False, True):
+        opts = PlanOptions(num_samples=S, topk=4, n_steps=1, clip_actions=clip)
+        got = rt.sample_candidates(opts, S, 0, cuda(mean), cuda(std), cuda(noise), cuda(lo_), cuda(hi_))
+        want = noise * std[:, None] + mean[:, None]
+        want[:, 0] = mean
+        if clip:
+            want = np.clip(want, lo_, hi_)
+        np.testing.assert_allclose(got.cpu().numpy(), want, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("beta,time_axis,block", [(0.0, "raw", 5), (2.0, "raw", 5), (1.0, "raw", 5),
+                                                  (2.0, "block", 5), (2.0, "raw", 1)])
+def test_philox_colored_noise_matches_oracle(beta, time_axis, block):
+    rt = runtime(ModelDesc(), 0)
+    B, S, T, A = 2, 33, 5, 10
+    opts = PlanOptions(num_samples=S, topk=4, n_steps=1, beta=beta, time_axis=time_axis, action_block=block,
+                       seed=77)
+    mean = np.zeros((B, T, A), np.float32)
+    std = np.ones((B, T, A), np.float32)
+    got = rt.sample_candidates(opts, S, 4, cuda(mean), cuda(std), plan_index=9).cpu().numpy()
+    shape = io.white_noise_shape(1, 1, T, A, beta, block, time_axis)
+    n = int(np.prod(shape))
+    for e in range(B):
+        for c in range(1, S):
+            white = io.philox_normal(n, c, e, 4, 77, 9).reshape(shape)
+            want = io.color_white_noise(white, T, A, beta, block, time_axis)[0, 0]
+            np.testing.assert_allclose(got[e, c], want, rtol=2e-3, atol=2e-3)
+    # the in-kernel stream is standard normal before coloring
+    white = got[:, 1:].reshape(-1)
+    if beta == 0.0:
+        assert abs(white.mean()) < 0.1 and abs(white.std() - 1) < 0.1
+
+
+@pytest.mark.parametrize("case", CHAIN_CASES)
+def test_plan_with_reference_noise_tracks_reference_chain(case):
+    """Injected reference noise: iteration costs within the bf16 bound, and the whole
+    chain equals the oracle chain replayed on the device's own costs."""
+    d = load(case)
+    desc, sd = weights_of(d)
+    rt = runtime(desc, int(d["seed"]))
+    kw = json.loads(str(d["solver"]))
+    n = int(d["n_iters"])
+    noise = [cuda(d[f"noise_{i}"]) for i in range(n)]
+    counts = [int(d[f"noise_{i}"].shape[1]) for i in range(n)]
+    opts = PlanOptions(num_samples=max(counts), topk=kw["topk"], n_steps=n,
+                       sample_decay=kw.get("sample_decay", 1.0),
+                       sample_count_bucket_size=kw.get("sample_count_bucket_size", 0),
+                       elite_retention=kw.get("elite_retention", 0), momentum_alpha=kw.get("momentum_alpha", 0.0),
+                       return_best_elite=kw.get("return_best_elite", False), clip_actions=bool(d["low"].size))
+    lo_ = cuda(d["low"]) if d["low"].size else None
+    hi_ = cuda(d["high"]) if d["high"].size else None
+    act, std, fcost, tr = rt.plan(opts, cuda(d["emb"]), cuda(d["goal"]), cuda(d["mean0"]), cuda(d["var0"]),
+                                  noise_steps=noise, action_low=lo_, action_high=hi_, trace=True)
+    rt.sync()
+    # iteration 0 sees the reference's exact candidates
+    np.testing.assert_allclose(tr["candidates"][0][:, :counts[0]].cpu().numpy(), d["cand_0"], rtol=1e-6, atol=1e-6)
+    assert rel_err(tr["costs"][0][:, :counts[0]].cpu().numpy(), d["cost_0"]).max() <= COST_RTOL
+    # replay the oracle chain on the device's costs: identical elites and refits
+    costs_dev = [tr["costs"][i][:, :counts[i]].cpu().numpy() for i in range(n)]
+    it = iter(costs_dev)
+    trace = []
+    a_o, s_o, f_o = io.run_static_icem_chain(
+        lambda e, g, c: next(it), d["emb"], d["goal"], d["mean0"], d["var0"], [d[f"noise_{i}"] for i in range(n)],
+        topk=kw["topk"], elite_retention=kw.get("elite_retention", 0), momentum_alpha=kw.get("momentum_alpha", 0.0),
+        return_best_elite=kw.get("return_best_elite", False), action_low=d["low"] if d["low"].size else None,
+        action_high=d["high"] if d["high"].size else None, trace=trace)
+    for i, t in enumerate(trace):
+        assert np.array_equal(tr["topk_idx"][i].cpu().numpy(), t["topk_inds"]), f"elites differ at {i}"
+        np.testing.assert_allclose(tr["candidates"][i][:, :counts[i]].cpu().numpy(), t["candidates"], rtol=1e-5,
+                                   atol=1e-5)
+        # device costs vs the fp32 model on the same candidates
+        want = lo.get_cost_from_embeddings(d["emb"], d["goal"], t["candidates"], sd, desc)
+        assert rel_err(costs_dev[i], want).max() <= COST_RTOL, f"iteration {i}"
+    np.testing.assert_allclose(act.cpu().numpy(), a_o, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(std.cpu().numpy(), s_o, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(fcost.cpu().numpy(), f_o, rtol=1e-5)
+    # and the final cost stays within the bf16 bound of the reference's
+    assert rel_err(fcost.cpu().numpy(), d["final_cost"]).max() <= COST_RTOL
+
+
+def test_plan_philox_is_deterministic_per_plan_index():
+    desc = ModelDesc()
+    rt = runtime(desc, 0)
+    rng = np.random.default_rng(1)
+    B = 2
+    emb, goal = cuda(rng.standard_normal((B, 1, desc.dim))), cuda(rng.standard_normal((B, 1, desc.dim)))
+    mean = torch.zeros(B, 5, 10, device="cuda:0")
+    std = torch.ones(B, 5, 10, device="cuda:0")
+    opts = PlanOptions(num_samples=120, topk=12, n_steps=6, sample_decay=1.25, sample_count_bucket_size=30,
+                       elite_retention=3, beta=2.0, action_block=5)
+    a1 = rt.plan(opts, emb, goal, mean, std, plan_index=3)
+    a2 = rt.plan(opts, emb, goal, mean, std, plan_index=3)
+    a3 = rt.plan(opts, emb, goal, mean, std, plan_index=4)
+    rt.sync()
+    for x, y in zip(a1[:3], a2[:3]):
+        assert torch.equal(x, y)
+    assert not torch.equal(a1[0], a3[0])
+    # each env's plan is independent of the others in the batch
+    s0 = rt.plan(opts, emb[:1], goal[:1], mean[:1], std[:1], plan_index=3)
+    assert torch.equal(s0[0][0], a1[0][0])
+
+
+def test_plan_lowers_cost_over_iterations():
+    desc = ModelDesc()
+    rt = runtime(desc, 0)
+    rng = np.random.default_rng(2)
+    emb, goal = cuda(rng.standard_normal((1, 1, desc.dim))), cuda(rng.standard_normal((1, 1, desc.dim)))
+    mean = torch.zeros(1, 5, 10, device="cuda:0")
+    std = torch.ones(1, 5, 10, device="cuda:0")
+    opts = PlanOptions(num_samples=300, topk=30, n_steps=30, sample_decay=1.25, sample_count_bucket_size=60,
+                       elite_retention=3, beta=2.0, action_block=5)
+    act, std_o, fc, tr = rt.plan(opts, emb, goal, mean, std, trace=True)
+    rt.sync()
+    first = tr["topk_val"][0].mean().item()
+    last = tr["topk_val"][-1].mean().item()
+    assert last < first
+    assert torch.isfinite(act).all() and torch.isfinite(std_o).all()
+    # the returned mean's own cost is close to the best elites' cost
+    c = rt.model_cost(emb, goal, act[:, None])
+    assert c.item() <= first
