@@ -155,6 +155,7 @@ __global__ void __launch_bounds__(256) k_embed(DevWeights w, ModelDims md, const
     mbar_init(bar_mma, 1);
     fence_mbar_init();
   }
+  __syncwarp();
   if (warp == 0) {
     tmem_alloc(tmem_slot, C::TMEM_EMB);
     tmem_relinquish();
@@ -222,6 +223,7 @@ __global__ void __launch_bounds__(256) k_embed(DevWeights w, ModelDims md, const
     }
   }
   ok = mbar_wait(bar_mma, (nch - 1) & 1, status) && ok;
+  __syncwarp();
   tc_fence_after();
   {
     const int r = tid & 127;
@@ -250,6 +252,7 @@ __global__ void __launch_bounds__(256) k_embed(DevWeights w, ModelDims md, const
     bulk_commit();
     bulk_wait_all();
   }
+  __syncwarp();
   if (warp == 0) tmem_dealloc(tmem, C::TMEM_EMB);
 }
 
@@ -279,6 +282,7 @@ __global__ void __launch_bounds__(128) k_adaln(DevWeights w, ModelDims md, int r
       bulk_g2s(sB + kb * NT * 128, w.wada + ((size_t)nt * C::KB + kb) * NT * 64, NT * 128, &bars[0]);
     }
   }
+  __syncwarp();
   if (warp == 0) {
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
@@ -295,6 +299,7 @@ __global__ void __launch_bounds__(128) k_adaln(DevWeights w, ModelDims md, int r
     umma_commit(&bars[1]);
   }
   const bool ok = mbar_wait(&bars[1], 0, status);
+  __syncwarp();
   tc_fence_after();
   const int row = tile * 128 + tid;
   const int ncols = md.L * 6 * D;
@@ -315,6 +320,7 @@ __global__ void __launch_bounds__(128) k_adaln(DevWeights w, ModelDims md, int r
   }
   tc_fence_before();
   __syncthreads();
+  __syncwarp();
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
@@ -357,6 +363,7 @@ __global__ void __launch_bounds__(128) k_qkv_attn(DevWeights w, ModelDims md, Ca
       bulk_g2s(sB + s * B_BLK, wq + (size_t)s * 192 * 64, B_BLK, &full[s]);
     }
   }
+  __syncwarp();
   if (warp == 0) {
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
@@ -414,6 +421,7 @@ __global__ void __launch_bounds__(128) k_qkv_attn(DevWeights w, ModelDims md, Ca
     umma_commit(bar_mma);
   }
   const bool ok = mbar_wait(bar_mma, 0, status);
+  __syncwarp();
   tc_fence_after();
   {  // q|k|v of this head -> scratch rows (fp32)
     const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
@@ -470,6 +478,7 @@ __global__ void __launch_bounds__(128) k_qkv_attn(DevWeights w, ModelDims md, Ca
     bulk_commit();
     bulk_wait_all();
   }
+  __syncwarp();
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
@@ -510,6 +519,7 @@ __global__ void __launch_bounds__(128) k_resid_gemm(const __nv_bfloat16* __restr
       bulk_g2s(sB + s * B_BLK, tB + (size_t)s * NT * 64, B_BLK, &full[s]);
     }
   }
+  __syncwarp();
   if (warp == 0) {
     tmem_alloc(tmem_slot, C::TMEM_OUT);
     tmem_relinquish();
@@ -544,6 +554,7 @@ __global__ void __launch_bounds__(128) k_resid_gemm(const __nv_bfloat16* __restr
     umma_commit(bar_mma);
   }
   const bool ok = mbar_wait(bar_mma, 0, status);
+  __syncwarp();
   tc_fence_after();
   const int r = tid;
   const RowMap m = map_row(g, tile, r);
@@ -569,6 +580,7 @@ __global__ void __launch_bounds__(128) k_resid_gemm(const __nv_bfloat16* __restr
   }
   tc_fence_before();
   __syncthreads();
+  __syncwarp();
   if (warp == 0) tmem_dealloc(tmem, C::TMEM_OUT);
 }
 
@@ -605,6 +617,7 @@ __global__ void __launch_bounds__(128) k_fc1(DevWeights w, ModelDims md, CallGeo
       bulk_g2s(sB + s * kBlk, wb + (size_t)s * kBlkElems, kBlk, &full[s]);
     }
   }
+  __syncwarp();
   if (warp == 0) {
     tmem_alloc(tmem_slot, 128);
     tmem_relinquish();
@@ -646,6 +659,7 @@ __global__ void __launch_bounds__(128) k_fc1(DevWeights w, ModelDims md, CallGeo
     umma_commit(bar_mma);
   }
   const bool ok = mbar_wait(bar_mma, 0, status);
+  __syncwarp();
   tc_fence_after();
   {
     const int r = tid;
@@ -676,6 +690,7 @@ __global__ void __launch_bounds__(128) k_fc1(DevWeights w, ModelDims md, CallGeo
     bulk_commit();
     bulk_wait_all();
   }
+  __syncwarp();
   if (warp == 0) tmem_dealloc(tmem, 128);
 }
 
