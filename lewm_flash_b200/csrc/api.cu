@@ -5,6 +5,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -48,6 +49,10 @@ struct Workspace {
   float* best = nullptr;
   float* fcost = nullptr;
   float* W = nullptr;
+  uint32_t* rng = nullptr;   // [seed, plan index]
+  float* emb_in = nullptr;   // staged plan inputs (graph path)
+  float* goal_in = nullptr;
+  float* lohi = nullptr;     // action low | high
 };
 
 struct WsReq {
@@ -72,6 +77,9 @@ struct lewm_ctx {
   WsReq cap{};
   bool have_ws = false;
   Prof prof;                  // per-launch event profiler (lewm_profile_plan)
+  cudaStream_t cap_stream = nullptr;  // plan graphs are captured and replayed here
+  cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+  std::map<std::vector<double>, cudaGraphExec_t> graphs;  // one executable graph per plan shape
   std::vector<float> W_host;  // last uploaded coloring matrix
   int W_n = -1;
   float W_beta = -1.f;
@@ -292,6 +300,11 @@ int window_tiles(int n_cand, int w) {
   return (n_cand + cpt - 1) / cpt;
 }
 
+void clear_graphs(lewm_ctx* c) {
+  for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+  c->graphs.clear();
+}
+
 lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   if (c->have_ws && need <= c->cap) return LEWM_OK;
   WsReq r = need;
@@ -303,6 +316,7 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
     r.B = std::max(r.B, c->cap.B);
     r.R = std::max(r.R, c->cap.R);
     r.ncol = std::max(r.ncol, c->cap.ncol);
+    clear_graphs(c);
     cudaFree(c->ws.base);
     c->ws = Workspace{};
     c->have_ws = false;
@@ -331,6 +345,10 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   const size_t o_best = carve(r.B * ta * 4);
   const size_t o_fc = carve(r.B * 4);
   const size_t o_W = carve(std::max<size_t>(r.ncol, 1) * std::max<size_t>(r.ncol, 1) * 4);
+  const size_t o_rng = carve(16);
+  const size_t o_embin = carve(r.B * r.T * (size_t)m.D * 4);
+  const size_t o_goalin = carve(r.B * (size_t)m.D * 4);
+  const size_t o_lohi = carve(2 * (size_t)m.A * 4);
   void* base = nullptr;
   LEWM_CK(c, cudaMalloc(&base, off));
   auto* b = static_cast<uint8_t*>(base);
@@ -351,6 +369,10 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   ws.best = reinterpret_cast<float*>(b + o_best);
   ws.fcost = reinterpret_cast<float*>(b + o_fc);
   ws.W = reinterpret_cast<float*>(b + o_W);
+  ws.rng = reinterpret_cast<uint32_t*>(b + o_rng);
+  ws.emb_in = reinterpret_cast<float*>(b + o_embin);
+  ws.goal_in = reinterpret_cast<float*>(b + o_goalin);
+  ws.lohi = reinterpret_cast<float*>(b + o_lohi);
   c->cap = r;
   c->have_ws = true;
   c->W_n = -1;
@@ -488,6 +510,116 @@ lewm_status upload_W(lewm_ctx* c, const lewm_plan_desc* p, int ncol, cudaStream_
   return LEWM_OK;
 }
 
+struct PlanIO {
+  const float* emb;
+  const float* goal;
+  const float* low;
+  const float* high;
+};
+
+bool graphs_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("LEWM_NO_GRAPH");
+    return !(v && v[0] == '1');
+  }();
+  return on;
+}
+
+std::vector<double> plan_key(const lewm_plan_desc* p, int kind, int ncol) {
+  return {(double)p->n_envs, (double)p->horizon, (double)p->history, (double)p->history_size,
+          (double)p->num_samples, (double)p->topk, (double)p->n_steps, (double)p->sample_decay,
+          (double)p->bucket, (double)p->elite_retention, (double)kind, (double)ncol, (double)p->action_block,
+          (double)p->momentum_alpha, (double)p->return_best_elite, (double)p->clip_actions};
+}
+
+// Every launch of one plan: per iteration sample -> model cost -> top-k/refit.
+// Reads the distribution from ws.mean / ws.stdv (set by the caller) and leaves the
+// result there; the Philox key is read from ws.rng at run time.
+lewm_status plan_iterations(lewm_ctx* c, const lewm_plan_desc* p, const std::vector<int>& counts, int kind,
+                            int ncol, const PlanIO& io, const float* const* noise_steps,
+                            const lewm_plan_trace* trace, cudaStream_t st) {
+  const ModelDims& m = c->md;
+  Workspace& ws = c->ws;
+  const int B = p->n_envs, T = p->horizon, A = m.A, TA = T * A, k = p->topk;
+  const int R = std::min(p->elite_retention, k);
+  for (int it = 0; it < p->n_steps; ++it) {
+    const int St = counts[it];
+    const int n_inject = (it > 0 && p->elite_retention > 0) ? std::min(R, St - 1) : 0;
+    SampleParams sp{};
+    sp.B = B;
+    sp.S = St;
+    sp.T = T;
+    sp.A = A;
+    sp.noise_kind = kind;
+    sp.raw_block = p->action_block;
+    sp.ncol = ncol;
+    sp.W = ws.W;
+    sp.noise = noise_steps ? noise_steps[it] : nullptr;
+    sp.rng = ws.rng;
+    sp.iter = (uint32_t)it;
+    sp.mean = ws.mean;
+    sp.stdv = ws.stdv;
+    sp.elites = ws.elites;
+    sp.elite_stride = std::max(R, 1);
+    sp.n_inject = std::max(n_inject, 0);
+    sp.low = io.low;
+    sp.high = io.high;
+    sp.cand = ws.cand;
+    c->prof.begin(st);
+    LEWM_CK(c, launch_sample(sp, st));
+    c->prof.end(KC_SAMPLE, 0.0, st);
+    lewm_status s = run_model_cost(c, io.emb, 0, p->history, io.goal, 0, ws.cand, B, St, T, p->history_size,
+                                   ws.costs, st);
+    if (s != LEWM_OK) return s;
+    RefitParams rp{};
+    rp.B = B;
+    rp.S = St;
+    rp.T = T;
+    rp.A = A;
+    rp.k = k;
+    rp.R = R;
+    rp.costs = ws.costs;
+    rp.cand = ws.cand;
+    rp.mean = ws.mean;
+    rp.stdv = ws.stdv;
+    rp.alpha = p->momentum_alpha;
+    rp.elites = ws.elites;
+    rp.best = ws.best;
+    rp.final_cost = ws.fcost;
+    rp.topk_idx = (trace && trace->topk_idx) ? trace->topk_idx + (size_t)it * B * k : nullptr;
+    rp.topk_val = (trace && trace->topk_val) ? trace->topk_val + (size_t)it * B * k : nullptr;
+    c->prof.begin(st);
+    LEWM_CK(c, launch_refit(rp, st));
+    c->prof.end(KC_REFIT, 0.0, st);
+    if (trace) {
+      const size_t S = p->num_samples;
+      if (trace->costs)
+        LEWM_CK(c, cudaMemcpy2DAsync(trace->costs + (size_t)it * B * S, S * 4, ws.costs, (size_t)St * 4,
+                                     (size_t)St * 4, B, cudaMemcpyDeviceToDevice, st));
+      if (trace->candidates)
+        LEWM_CK(c, cudaMemcpy2DAsync(trace->candidates + (size_t)it * B * S * TA, S * TA * 4, ws.cand,
+                                     (size_t)St * TA * 4, (size_t)St * TA * 4, B, cudaMemcpyDeviceToDevice, st));
+      if (trace->mean)
+        LEWM_CK(c, cudaMemcpyAsync(trace->mean + (size_t)it * B * TA, ws.mean, (size_t)B * TA * 4,
+                                   cudaMemcpyDeviceToDevice, st));
+      if (trace->std)
+        LEWM_CK(c, cudaMemcpyAsync(trace->std + (size_t)it * B * TA, ws.stdv, (size_t)B * TA * 4,
+                                   cudaMemcpyDeviceToDevice, st));
+    }
+  }
+  return LEWM_OK;
+}
+
+lewm_status copy_plan_outputs(lewm_ctx* c, const lewm_plan_desc* p, float* actions_out, float* std_out,
+                              float* final_cost_out, cudaStream_t st) {
+  const size_t bta = (size_t)p->n_envs * p->horizon * c->md.A * 4;
+  LEWM_CK(c, cudaMemcpyAsync(actions_out, p->return_best_elite ? c->ws.best : c->ws.mean, bta,
+                             cudaMemcpyDeviceToDevice, st));
+  LEWM_CK(c, cudaMemcpyAsync(std_out, c->ws.stdv, bta, cudaMemcpyDeviceToDevice, st));
+  LEWM_CK(c, cudaMemcpyAsync(final_cost_out, c->ws.fcost, (size_t)p->n_envs * 4, cudaMemcpyDeviceToDevice, st));
+  return LEWM_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -522,6 +654,10 @@ lewm_status lewm_create(lewm_ctx** out, const lewm_model_desc* desc, const float
   s = pack_weights(c, weights, n_floats);
   if (s == LEWM_OK && cudaMalloc(&c->d_status, 4) != cudaSuccess) s = fail(c, LEWM_CUDA_ERROR, "status alloc");
   if (s == LEWM_OK && cudaMemset(c->d_status, 0, 4) != cudaSuccess) s = fail(c, LEWM_CUDA_ERROR, "status memset");
+  if (s == LEWM_OK && (cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking) != cudaSuccess ||
+                       cudaEventCreateWithFlags(&c->ev_in, cudaEventDisableTiming) != cudaSuccess ||
+                       cudaEventCreateWithFlags(&c->ev_out, cudaEventDisableTiming) != cudaSuccess))
+    s = fail(c, LEWM_CUDA_ERROR, "stream/event creation");
   if (s != LEWM_OK) {
     g_create_error = c->err;
     lewm_destroy(c);
@@ -534,6 +670,11 @@ lewm_status lewm_create(lewm_ctx** out, const lewm_model_desc* desc, const float
 void lewm_destroy(lewm_ctx* c) {
   if (!c) return;
   DeviceGuard g(c->device);
+  if (c->cap_stream) cudaStreamSynchronize(c->cap_stream);
+  clear_graphs(c);
+  if (c->ev_in) cudaEventDestroy(c->ev_in);
+  if (c->ev_out) cudaEventDestroy(c->ev_out);
+  if (c->cap_stream) cudaStreamDestroy(c->cap_stream);
   if (c->ws.base) cudaFree(c->ws.base);
   if (c->d_weights) cudaFree(c->d_weights);
   if (c->d_status) cudaFree(c->d_status);
@@ -596,93 +737,74 @@ lewm_status lewm_plan(lewm_ctx* c, const lewm_plan_desc* p, const float* emb, co
   DeviceGuard g(c->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const ModelDims& m = c->md;
-  const int B = p->n_envs, T = p->horizon, A = m.A, TA = T * A, k = p->topk;
+  const int B = p->n_envs, T = p->horizon, A = m.A, TA = T * A, H = p->history;
   const std::vector<int> counts = counts_of(p);
   const int Smax = *std::max_element(counts.begin(), counts.end());
   if ((int64_t)B * Smax * T > (1ll << 26)) return fail(c, LEWM_UNSUPPORTED_SHAPE, "n_envs*num_samples*T too large");
   int kind, ncol;
   noise_kind(c, p, &kind, &ncol);
-  const int R = std::min(p->elite_retention, k);
+  const int R = std::min(p->elite_retention, p->topk);
   const int NC = B * Smax;
   WsReq need{(size_t)NC, (size_t)T, (size_t)A, (size_t)m.D, (size_t)m.L,
-             (size_t)max_call_tiles(NC, T, p->history, p->history_size), (size_t)m.heads, (size_t)m.mlp,
-             (size_t)(T - p->history + 1), (size_t)B, (size_t)R, (size_t)std::max(ncol, 1)};
+             (size_t)max_call_tiles(NC, T, H, p->history_size), (size_t)m.heads, (size_t)m.mlp,
+             (size_t)(T - H + 1), (size_t)B, (size_t)R, (size_t)std::max(ncol, 1)};
   s = ensure_ws(c, need);
   if (s != LEWM_OK) return s;
   Workspace& ws = c->ws;
   s = upload_W(c, p, ncol, st);
   if (s != LEWM_OK) return s;
-  LEWM_CK(c, cudaMemcpyAsync(ws.mean, init_mean, (size_t)B * TA * 4, cudaMemcpyDeviceToDevice, st));
-  LEWM_CK(c, cudaMemcpyAsync(ws.stdv, init_std, (size_t)B * TA * 4, cudaMemcpyDeviceToDevice, st));
-  for (int it = 0; it < p->n_steps; ++it) {
-    const int St = counts[it];
-    const int n_inject = (it > 0 && p->elite_retention > 0) ? std::min(std::min(p->elite_retention, k), St - 1) : 0;
-    SampleParams sp{};
-    sp.B = B;
-    sp.S = St;
-    sp.T = T;
-    sp.A = A;
-    sp.noise_kind = kind;
-    sp.raw_block = p->action_block;
-    sp.ncol = ncol;
-    sp.W = ws.W;
-    sp.noise = noise_steps ? noise_steps[it] : nullptr;
-    sp.seed_lo = (uint32_t)(p->seed & 0xffffffffu);
-    sp.plan_id = (uint32_t)(p->plan_index & 0xffffffffu);
-    sp.iter = (uint32_t)it;
-    sp.mean = ws.mean;
-    sp.stdv = ws.stdv;
-    sp.elites = ws.elites;
-    sp.elite_stride = std::max(R, 1);
-    sp.n_inject = std::max(n_inject, 0);
-    sp.low = p->clip_actions ? action_low : nullptr;
-    sp.high = p->clip_actions ? action_high : nullptr;
-    sp.cand = ws.cand;
-    c->prof.begin(st);
-    LEWM_CK(c, launch_sample(sp, st));
-    c->prof.end(KC_SAMPLE, 0.0, st);
-    s = run_model_cost(c, emb, 0, p->history, goal, 0, ws.cand, B, St, T, p->history_size, ws.costs, st);
+  const uint32_t seed = (uint32_t)(p->seed & 0xffffffffu), plan = (uint32_t)(p->plan_index & 0xffffffffu);
+  const bool use_graph = !noise_steps && !trace && !c->prof.on && graphs_enabled();
+  if (!use_graph) {
+    LEWM_CK(c, cudaMemcpyAsync(ws.mean, init_mean, (size_t)B * TA * 4, cudaMemcpyDeviceToDevice, st));
+    LEWM_CK(c, cudaMemcpyAsync(ws.stdv, init_std, (size_t)B * TA * 4, cudaMemcpyDeviceToDevice, st));
+    LEWM_CK(c, launch_set_rng(ws.rng, seed, plan, st));
+    PlanIO io{emb, goal, p->clip_actions ? action_low : nullptr, p->clip_actions ? action_high : nullptr};
+    s = plan_iterations(c, p, counts, kind, ncol, io, noise_steps, trace, st);
     if (s != LEWM_OK) return s;
-    RefitParams rp{};
-    rp.B = B;
-    rp.S = St;
-    rp.T = T;
-    rp.A = A;
-    rp.k = k;
-    rp.R = R;
-    rp.costs = ws.costs;
-    rp.cand = ws.cand;
-    rp.mean = ws.mean;
-    rp.stdv = ws.stdv;
-    rp.alpha = p->momentum_alpha;
-    rp.elites = ws.elites;
-    rp.best = ws.best;
-    rp.final_cost = ws.fcost;
-    rp.topk_idx = (trace && trace->topk_idx) ? trace->topk_idx + (size_t)it * B * k : nullptr;
-    rp.topk_val = (trace && trace->topk_val) ? trace->topk_val + (size_t)it * B * k : nullptr;
-    c->prof.begin(st);
-    LEWM_CK(c, launch_refit(rp, st));
-    c->prof.end(KC_REFIT, 0.0, st);
-    if (trace) {
-      const size_t S = p->num_samples;
-      if (trace->costs)
-        LEWM_CK(c, cudaMemcpy2DAsync(trace->costs + (size_t)it * B * S, S * 4, ws.costs, (size_t)St * 4,
-                                     (size_t)St * 4, B, cudaMemcpyDeviceToDevice, st));
-      if (trace->candidates)
-        LEWM_CK(c, cudaMemcpy2DAsync(trace->candidates + (size_t)it * B * S * TA, S * TA * 4, ws.cand,
-                                     (size_t)St * TA * 4, (size_t)St * TA * 4, B, cudaMemcpyDeviceToDevice, st));
-      if (trace->mean)
-        LEWM_CK(c, cudaMemcpyAsync(trace->mean + (size_t)it * B * TA, ws.mean, (size_t)B * TA * 4,
-                                   cudaMemcpyDeviceToDevice, st));
-      if (trace->std)
-        LEWM_CK(c, cudaMemcpyAsync(trace->std + (size_t)it * B * TA, ws.stdv, (size_t)B * TA * 4,
-                                   cudaMemcpyDeviceToDevice, st));
-    }
+    return copy_plan_outputs(c, p, actions_out, std_out, final_cost_out, st);
   }
-  LEWM_CK(c, cudaMemcpyAsync(actions_out, p->return_best_elite ? ws.best : ws.mean, (size_t)B * TA * 4,
-                             cudaMemcpyDeviceToDevice, st));
-  LEWM_CK(c, cudaMemcpyAsync(std_out, ws.stdv, (size_t)B * TA * 4, cudaMemcpyDeviceToDevice, st));
-  LEWM_CK(c, cudaMemcpyAsync(final_cost_out, ws.fcost, (size_t)B * 4, cudaMemcpyDeviceToDevice, st));
+  // Graph path: stage the inputs into workspace buffers so the captured plan is
+  // pointer-stable, replay the cached graph for this plan shape, copy outputs back.
+  cudaStream_t cs = c->cap_stream;
+  LEWM_CK(c, cudaEventRecord(c->ev_in, st));
+  LEWM_CK(c, cudaStreamWaitEvent(cs, c->ev_in, 0));
+  LEWM_CK(c, cudaMemcpyAsync(ws.emb_in, emb, (size_t)B * H * m.D * 4, cudaMemcpyDeviceToDevice, cs));
+  LEWM_CK(c, cudaMemcpyAsync(ws.goal_in, goal, (size_t)B * m.D * 4, cudaMemcpyDeviceToDevice, cs));
+  LEWM_CK(c, cudaMemcpyAsync(ws.mean, init_mean, (size_t)B * TA * 4, cudaMemcpyDeviceToDevice, cs));
+  LEWM_CK(c, cudaMemcpyAsync(ws.stdv, init_std, (size_t)B * TA * 4, cudaMemcpyDeviceToDevice, cs));
+  if (p->clip_actions) {
+    LEWM_CK(c, cudaMemcpyAsync(ws.lohi, action_low, (size_t)A * 4, cudaMemcpyDeviceToDevice, cs));
+    LEWM_CK(c, cudaMemcpyAsync(ws.lohi + A, action_high, (size_t)A * 4, cudaMemcpyDeviceToDevice, cs));
+  }
+  LEWM_CK(c, launch_set_rng(ws.rng, seed, plan, cs));
+  const std::vector<double> key = plan_key(p, kind, ncol);
+  auto it = c->graphs.find(key);
+  if (it == c->graphs.end()) {
+    cudaGraph_t graph = nullptr;
+    LEWM_CK(c, cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+    PlanIO io{ws.emb_in, ws.goal_in, p->clip_actions ? ws.lohi : nullptr, p->clip_actions ? ws.lohi + A : nullptr};
+    s = plan_iterations(c, p, counts, kind, ncol, io, nullptr, nullptr, cs);
+    const cudaError_t ce = cudaStreamEndCapture(cs, &graph);
+    if (s != LEWM_OK) {
+      if (graph) cudaGraphDestroy(graph);
+      return s;
+    }
+    if (ce != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      return fail(c, LEWM_CUDA_ERROR, "plan graph capture: %s", cudaGetErrorString(ce));
+    }
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) return fail(c, LEWM_CUDA_ERROR, "plan graph instantiate: %s", cudaGetErrorString(ie));
+    it = c->graphs.emplace(key, exec).first;
+  }
+  LEWM_CK(c, cudaGraphLaunch(it->second, cs));
+  s = copy_plan_outputs(c, p, actions_out, std_out, final_cost_out, cs);
+  if (s != LEWM_OK) return s;
+  LEWM_CK(c, cudaEventRecord(c->ev_out, cs));
+  LEWM_CK(c, cudaStreamWaitEvent(st, c->ev_out, 0));
   return LEWM_OK;
 }
 
@@ -748,8 +870,9 @@ lewm_status lewm_sample_candidates(lewm_ctx* c, const lewm_plan_desc* p, int32_t
   sp.ncol = ncol;
   sp.W = c->ws.W;
   sp.noise = injected_noise;
-  sp.seed_lo = (uint32_t)(p->seed & 0xffffffffu);
-  sp.plan_id = (uint32_t)(p->plan_index & 0xffffffffu);
+  LEWM_CK(c, launch_set_rng(c->ws.rng, (uint32_t)(p->seed & 0xffffffffu), (uint32_t)(p->plan_index & 0xffffffffu),
+                            st));
+  sp.rng = c->ws.rng;
   sp.iter = (uint32_t)iter;
   sp.mean = mean;
   sp.stdv = std;
@@ -767,6 +890,7 @@ lewm_status lewm_sync_status(lewm_ctx* c, void* stream) {
   if (!c) return fail(nullptr, LEWM_INVALID_ARG, "ctx is NULL");
   DeviceGuard g(c->device);
   LEWM_CK(c, cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  if (c->cap_stream) LEWM_CK(c, cudaStreamSynchronize(c->cap_stream));
   LEWM_CK(c, cudaGetLastError());
   uint32_t v = 0;
   LEWM_CK(c, cudaMemcpy(&v, c->d_status, 4, cudaMemcpyDeviceToHost));

@@ -57,6 +57,8 @@ __device__ __forceinline__ void normals4(uint32_t blk, uint32_t cand, uint32_t e
 }
 
 __global__ void __launch_bounds__(128) k_sample(SampleParams p) {
+  griddep_wait();
+  griddep_launch();
   const int gid = blockIdx.x * blockDim.x + threadIdx.x;
   if (gid >= p.B * p.S) return;
   const int env = gid / p.S, c = gid - env * p.S;
@@ -81,7 +83,7 @@ __global__ void __launch_bounds__(128) k_sample(SampleParams p) {
     float wn[kMaxTA];
     for (int d = 0; d < n; d += 4) {
       float r4[4];
-      normals4((uint32_t)(d >> 2), (uint32_t)c, (uint32_t)env, p.iter, p.seed_lo, p.plan_id, r4);
+      normals4((uint32_t)(d >> 2), (uint32_t)c, (uint32_t)env, p.iter, p.rng[0], p.rng[1], r4);
       for (int q = 0; q < 4 && d + q < n; ++q) wn[d + q] = r4[q];
     }
     if (p.noise_kind == 0) {
@@ -134,6 +136,8 @@ constexpr int kMaxSort = 4096;
 
 __global__ void __launch_bounds__(kRefitThreads) k_refit(RefitParams p) {
   __shared__ unsigned long long keys[kMaxSort];
+  griddep_wait();
+  griddep_launch();
   const int env = blockIdx.x, tid = threadIdx.x;
   int P = 1;
   while (P < p.S) P <<= 1;
@@ -199,19 +203,28 @@ __global__ void __launch_bounds__(kRefitThreads) k_refit(RefitParams p) {
   }
 }
 
+__global__ void k_set_rng(uint32_t* rng, uint32_t seed, uint32_t plan) {
+  griddep_wait();
+  griddep_launch();
+  rng[0] = seed;
+  rng[1] = plan;
+}
+
 }  // namespace
+
+cudaError_t launch_set_rng(uint32_t* rng, uint32_t seed, uint32_t plan, cudaStream_t st) {
+  return launch_k(k_set_rng, dim3(1), dim3(1), 0, st, rng, seed, plan);
+}
 
 cudaError_t launch_sample(const SampleParams& p, cudaStream_t st) {
   if (p.T * p.A > kMaxTA || p.ncol > kMaxCol) return cudaErrorInvalidValue;
   const int n = p.B * p.S;
-  k_sample<<<(n + 127) / 128, 128, 0, st>>>(p);
-  return cudaGetLastError();
+  return launch_k(k_sample, dim3((n + 127) / 128), dim3(128), 0, st, p);
 }
 
 cudaError_t launch_refit(const RefitParams& p, cudaStream_t st) {
   if (p.S > kMaxSort || p.T * p.A > kMaxTA || p.k > p.S || p.k < 1 || p.k > kRefitThreads) return cudaErrorInvalidValue;
-  k_refit<<<p.B, kRefitThreads, 0, st>>>(p);
-  return cudaGetLastError();
+  return launch_k(k_refit, dim3(p.B), dim3(kRefitThreads), 0, st, p);
 }
 
 }  // namespace lewm

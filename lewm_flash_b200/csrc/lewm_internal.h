@@ -27,6 +27,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
+#include <utility>
 #include <vector>
 
 namespace lewm {
@@ -135,6 +137,30 @@ struct Prof {
   cudaEvent_t cur_a = nullptr;
 };
 
+// Launch with programmatic stream serialization (the kernel calls griddep_wait()
+// before touching its predecessor's output). LEWM_NO_PDL=1 turns it off.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("LEWM_NO_PDL");
+    return !(v && v[0] == '1');
+  }();
+  return on;
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // Launchers (rollout_kernels.cu). All asynchronous on `st`; `prof` may be null.
 cudaError_t launch_embed(const ModelDims& md, const DevWeights& w, const float* cand, int rows,
                          __nv_bfloat16* act_a, uint32_t* status, cudaStream_t st, Prof* prof);
@@ -151,7 +177,8 @@ struct SampleParams {
   int ncol;           // colored time length (T*block or T)
   const float* W;     // [ncol][ncol] coloring matrix (fp32)
   const float* noise; // injected noise (B,S,T,A) or null
-  uint32_t seed_lo, plan_id, iter;
+  const uint32_t* rng;  // device [seed, plan index] (Philox key), read at run time
+  uint32_t iter;
   const float* mean;  // (B,T,A)
   const float* stdv;  // (B,T,A)
   const float* elites;  // (B,elite_stride,T,A) previous sorted elites
@@ -162,6 +189,7 @@ struct SampleParams {
   float* cand;        // (B,S,T,A)
 };
 cudaError_t launch_sample(const SampleParams& p, cudaStream_t st);
+cudaError_t launch_set_rng(uint32_t* rng, uint32_t seed, uint32_t plan, cudaStream_t st);
 
 struct RefitParams {
   int B, S, T, A, k, R;

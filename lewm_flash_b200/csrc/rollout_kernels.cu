@@ -9,9 +9,9 @@
 //   per predictor call (lewm/jepa.py:284-298), per layer (lewm/module.py:105-111):
 //     k_qkv_attn  LN1 -> modulate -> attn.norm -> QKV GEMM (one head per CTA)
 //                 -> causal attention over the window (lewm/module.py:75-85)
-//     k_out       out-proj GEMM + bias, * gate_msa, + residual
+//     k_resid_gemm (out-proj) GEMM + bias, * gate_msa, + residual
 //     k_fc1       LN2 -> modulate -> FFN LayerNorm -> FC1 GEMM + bias -> GELU
-//     k_fc2       FC2 GEMM + bias, * gate_mlp, + residual
+//     k_resid_gemm (FC2) GEMM + bias, * gate_mlp, + residual
 //   k_final     final LayerNorm (lewm/module.py:183) on each window's last token,
 //               then append to the history or score against the goal
 //               (cost_from_rollout, lewm/jepa.py:246-260)
@@ -19,6 +19,13 @@
 // GEMMs run on tcgen05 (bf16 in, fp32 accumulate in TMEM); operands arrive in
 // shared memory by bulk copy of pre-swizzled blocks; LayerNorm, modulation,
 // bias, GELU, gates, residuals and the cost are fp32 in prologues/epilogues.
+//
+// Latency structure: every kernel is launched with programmatic stream
+// serialization. Before griddep_wait() a kernel only initialises barriers,
+// allocates TMEM and starts the bulk copies of its weight tiles, so that part
+// overlaps the previous kernel. Row work (LayerNorm prologues, attention) is
+// split over several threads per row and accumulator columns over the four
+// warps that share a TMEM lane quadrant, so no thread walks a long serial chain.
 #include <algorithm>
 
 #include "lewm_common.cuh"
@@ -30,7 +37,8 @@ namespace {
 constexpr int kBlk = 16384;           // bytes of one [128 x 64] bf16 block
 constexpr int kBlkElems = 128 * 64;   // elements of one [128 x 64] block
 constexpr int kMaxWindow = 8;
-constexpr int kScratchStride = 193;   // floats per row of the q|k|v scratch (bank-conflict free)
+constexpr int kScratchStride = 193;   // floats per row of the q|k|v scratch
+constexpr int kThreads = 512;         // 16 warps: 4 per TMEM lane quadrant
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -44,78 +52,10 @@ struct Cfg {
   static constexpr int TMEM_OUT = (NT_OUT <= 64) ? 64 : 128;
   static constexpr int TMEM_EMB = (D <= 256) ? 256 : 512;
   static constexpr int QKV_ST = (KB < 3) ? KB : 3;
+  static constexpr int RES_ST = 6;                // K-ring depth of the streamed-A GEMMs
+  static constexpr int TPR = D / 48;              // LayerNorm threads per row (48 columns each)
+  static constexpr int RPP = kThreads / TPR;      // rows per LayerNorm pass
 };
-
-// ---------------------------------------------------------------- row prologue
-// Warp-per-row: A-row (bf16, swizzled) = LN_affine(LN(x) * (1 + scale) + shift).
-// Lane l holds columns 64*i + 2l, 64*i + 2l + 1. `xout` (optional) receives x.
-template <int D>
-__device__ __forceinline__ void ln_mod_ln_row(const float* __restrict__ xrow, const float* __restrict__ addrow,
-                                              const __nv_bfloat16* __restrict__ shift,
-                                              const __nv_bfloat16* __restrict__ scale,
-                                              const float* __restrict__ g, const float* __restrict__ bb,
-                                              uint8_t* a_smem, int r, int lane, float* __restrict__ xout) {
-  constexpr int NP = D / 64;
-  float2 v[NP];
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    const int c = 64 * i + 2 * lane;
-    float2 t = *reinterpret_cast<const float2*>(xrow + c);
-    if (addrow) {
-      const float2 a = *reinterpret_cast<const float2*>(addrow + c);
-      t.x += a.x;
-      t.y += a.y;
-    }
-    v[i] = t;
-    s += t.x + t.y;
-  }
-  if (xout) {
-#pragma unroll
-    for (int i = 0; i < NP; ++i) *reinterpret_cast<float2*>(xout + 64 * i + 2 * lane) = v[i];
-  }
-  const float mean = warp_sum(s) * (1.0f / D);
-  float q = 0.f;
-#pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    const float dx = v[i].x - mean, dy = v[i].y - mean;
-    q += dx * dx + dy * dy;
-  }
-  const float rstd = rsqrtf(warp_sum(q) * (1.0f / D) + 1e-6f);
-  float s2 = 0.f;
-#pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    const int c = 64 * i + 2 * lane;
-    const float2 sh = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(shift + c));
-    const float2 sc = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(scale + c));
-    v[i].x = (v[i].x - mean) * rstd * (1.0f + sc.x) + sh.x;
-    v[i].y = (v[i].y - mean) * rstd * (1.0f + sc.y) + sh.y;
-    s2 += v[i].x + v[i].y;
-  }
-  const float mean2 = warp_sum(s2) * (1.0f / D);
-  float q2 = 0.f;
-#pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    const float dx = v[i].x - mean2, dy = v[i].y - mean2;
-    q2 += dx * dx + dy * dy;
-  }
-  const float rstd2 = rsqrtf(warp_sum(q2) * (1.0f / D) + 1e-5f);
-#pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    const int c = 64 * i + 2 * lane;
-    const float2 gg = *reinterpret_cast<const float2*>(g + c);
-    const float2 b2 = *reinterpret_cast<const float2*>(bb + c);
-    const float zx = (v[i].x - mean2) * rstd2 * gg.x + b2.x;
-    const float zy = (v[i].y - mean2) * rstd2 * gg.y + b2.y;
-    *reinterpret_cast<uint32_t*>(a_smem + i * kBlk + sw128_off(r, 2 * lane)) = pack_bf16x2(zx, zy);
-  }
-}
-
-template <int D>
-__device__ __forceinline__ void zero_row(uint8_t* a_smem, int r, int lane) {
-#pragma unroll
-  for (int i = 0; i < D / 64; ++i) *reinterpret_cast<uint32_t*>(a_smem + i * kBlk + sw128_off(r, 2 * lane)) = 0u;
-}
 
 struct RowMap {
   bool valid;
@@ -129,6 +69,96 @@ __device__ __forceinline__ RowMap map_row(const CallGeom& g, int tile, int r) {
   m.valid = (cl < g.cpt) && (m.cand < g.n_cand);
   m.tok = m.cand * g.T + g.start + m.pos;
   return m;
+}
+
+// ---------------------------------------------------------------- row prologue
+// TPR threads per row; thread q holds float4 chunks j = q + TPR*i (i < 12), i.e.
+// columns 4j..4j+3. A-row (bf16, swizzled) = LN_affine(LN(x)*(1+scale)+shift).
+// Every lane runs the group shuffles; invalid rows compute on zeros and store zeros.
+template <int D>
+__device__ __forceinline__ void ln_mod_ln_part(bool valid, const float* __restrict__ xrow,
+                                               const float* __restrict__ addrow,
+                                               const __nv_bfloat16* __restrict__ shift,
+                                               const __nv_bfloat16* __restrict__ scale,
+                                               const float* __restrict__ g, const float* __restrict__ bb,
+                                               uint8_t* a_smem, int r, int q, float* __restrict__ xout) {
+  constexpr int TPR = Cfg<D>::TPR;
+  constexpr int NC = 12;
+  float4 v[NC];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = 4 * (q + TPR * i);
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (valid) {
+      t = *reinterpret_cast<const float4*>(xrow + c);
+      if (addrow) {
+        const float4 a = *reinterpret_cast<const float4*>(addrow + c);
+        t.x += a.x;
+        t.y += a.y;
+        t.z += a.z;
+        t.w += a.w;
+      }
+      if (xout) *reinterpret_cast<float4*>(xout + c) = t;
+    }
+    v[i] = t;
+    s += (t.x + t.y) + (t.z + t.w);
+  }
+#pragma unroll
+  for (int o = TPR / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s * (1.0f / D);
+  float q2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+    q2 += (a * a + b * b) + (c * c + d * d);
+  }
+#pragma unroll
+  for (int o = TPR / 2; o > 0; o >>= 1) q2 += __shfl_xor_sync(0xffffffffu, q2, o);
+  const float rstd = rsqrtf(q2 * (1.0f / D) + 1e-6f);
+  float s2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = 4 * (q + TPR * i);
+    float2 sh01 = make_float2(0.f, 0.f), sh23 = sh01, sc01 = sh01, sc23 = sh01;
+    if (valid) {
+      const uint2 sh = *reinterpret_cast<const uint2*>(shift + c);
+      const uint2 sc = *reinterpret_cast<const uint2*>(scale + c);
+      sh01 = unpack_bf16x2(sh.x);
+      sh23 = unpack_bf16x2(sh.y);
+      sc01 = unpack_bf16x2(sc.x);
+      sc23 = unpack_bf16x2(sc.y);
+    }
+    v[i].x = (v[i].x - mean) * rstd * (1.0f + sc01.x) + sh01.x;
+    v[i].y = (v[i].y - mean) * rstd * (1.0f + sc01.y) + sh01.y;
+    v[i].z = (v[i].z - mean) * rstd * (1.0f + sc23.x) + sh23.x;
+    v[i].w = (v[i].w - mean) * rstd * (1.0f + sc23.y) + sh23.y;
+    s2 += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+#pragma unroll
+  for (int o = TPR / 2; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+  const float mean2 = s2 * (1.0f / D);
+  float q3 = 0.f;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const float a = v[i].x - mean2, b = v[i].y - mean2, c = v[i].z - mean2, d = v[i].w - mean2;
+    q3 += (a * a + b * b) + (c * c + d * d);
+  }
+#pragma unroll
+  for (int o = TPR / 2; o > 0; o >>= 1) q3 += __shfl_xor_sync(0xffffffffu, q3, o);
+  const float rstd2 = rsqrtf(q3 * (1.0f / D) + 1e-5f);
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = 4 * (q + TPR * i);
+    uint2 out = make_uint2(0u, 0u);
+    if (valid) {
+      const float4 gg = *reinterpret_cast<const float4*>(g + c);
+      const float4 b4 = *reinterpret_cast<const float4*>(bb + c);
+      out.x = pack_bf16x2((v[i].x - mean2) * rstd2 * gg.x + b4.x, (v[i].y - mean2) * rstd2 * gg.y + b4.y);
+      out.y = pack_bf16x2((v[i].z - mean2) * rstd2 * gg.z + b4.z, (v[i].w - mean2) * rstd2 * gg.w + b4.w);
+    }
+    *reinterpret_cast<uint2*>(a_smem + (c >> 6) * kBlk + sw128_off(r, c & 63)) = out;
+  }
 }
 
 // ---------------------------------------------------------------- Embedder + SiLU
@@ -154,12 +184,17 @@ __global__ void __launch_bounds__(256) k_embed(DevWeights w, ModelDims md, const
     mbar_init(bar_b, 1);
     mbar_init(bar_mma, 1);
     fence_mbar_init();
+    mbar_arrive_expect_tx(bar_b, 2 * D * 128);
+    bulk_g2s(sB, w.we2, D * 128, bar_b);
+    bulk_g2s(sB + D * 128, w.we2 + (size_t)D * 64, D * 128, bar_b);
   }
   __syncwarp();
   if (warp == 0) {
     tmem_alloc(tmem_slot, C::TMEM_EMB);
     tmem_relinquish();
   }
+  griddep_wait();
+  griddep_launch();
   for (int idx = tid; idx < 128 * 16; idx += 256) {
     const int r = idx >> 4, o = idx & 15;
     const int row = row0 + r;
@@ -178,11 +213,13 @@ __global__ void __launch_bounds__(256) k_embed(DevWeights w, ModelDims md, const
   const int nch = md.eh / 128;
   bool ok = true;
   for (int c = 0; c < nch; ++c) {
-    if (c > 0) ok = mbar_wait(bar_mma, (c - 1) & 1, status) && ok;
-    if (tid == 0) {
-      mbar_arrive_expect_tx(bar_b, 2 * D * 128);
-      bulk_g2s(sB, w.we2 + (size_t)(c * 2) * D * 64, D * 128, bar_b);
-      bulk_g2s(sB + D * 128, w.we2 + (size_t)(c * 2 + 1) * D * 64, D * 128, bar_b);
+    if (c > 0) {
+      ok = mbar_wait(bar_mma, (c - 1) & 1, status) && ok;
+      if (tid == 0) {
+        mbar_arrive_expect_tx(bar_b, 2 * D * 128);
+        bulk_g2s(sB, w.we2 + (size_t)(c * 2) * D * 64, D * 128, bar_b);
+        bulk_g2s(sB + D * 128, w.we2 + (size_t)(c * 2 + 1) * D * 64, D * 128, bar_b);
+      }
     }
     {
       const int k = tid & 127;
@@ -233,7 +270,6 @@ __global__ void __launch_bounds__(256) k_embed(DevWeights w, ModelDims md, const
     for (int c0 = half * (D / 2); c0 < (half + 1) * (D / 2); c0 += 16) {
       float v[16];
       tmem_ld16(taddr + c0, v);
-      tmem_ld_wait();
 #pragma unroll
       for (int i = 0; i < 16; i += 2) {
         const int c = c0 + i;
@@ -259,40 +295,47 @@ __global__ void __launch_bounds__(256) k_embed(DevWeights w, ModelDims md, const
 // ---------------------------------------------------------------- AdaLN modulation
 // mod[row, n] = bf16(act_a[row] . Wada[n] + b[n]) for n over all layers' 6*D outputs.
 template <int D>
-__global__ void __launch_bounds__(128) k_adaln(DevWeights w, ModelDims md, int rows,
-                                               const __nv_bfloat16* __restrict__ act_a,
-                                               __nv_bfloat16* __restrict__ mod, uint32_t* status) {
+__global__ void __launch_bounds__(kThreads) k_adaln(DevWeights w, ModelDims md, int rows,
+                                                    const __nv_bfloat16* __restrict__ act_a,
+                                                    __nv_bfloat16* __restrict__ mod, uint32_t* status) {
   using C = Cfg<D>;
   constexpr int NT = C::NT_ADA;
+  constexpr int CW = NT / 4;  // columns per warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::KB * kBlk;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + C::KB * NT * 128);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
-  const int tid = threadIdx.x, warp = tid >> 5;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + C::KB * NT * 128);  // [0] weights, [1] mma, [2] act
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x, nt = blockIdx.y;
   if (tid == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
+    mbar_init(&bars[2], 1);
     fence_mbar_init();
-    mbar_arrive_expect_tx(&bars[0], C::KB * (kBlk + NT * 128));
-    for (int kb = 0; kb < C::KB; ++kb) {
-      bulk_g2s(sA + kb * kBlk, act_a + ((size_t)tile * C::KB + kb) * kBlkElems, kBlk, &bars[0]);
+    mbar_arrive_expect_tx(&bars[0], C::KB * NT * 128);
+    for (int kb = 0; kb < C::KB; ++kb)
       bulk_g2s(sB + kb * NT * 128, w.wada + ((size_t)nt * C::KB + kb) * NT * 64, NT * 128, &bars[0]);
-    }
   }
   __syncwarp();
   if (warp == 0) {
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
+  griddep_wait();
+  griddep_launch();
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bars[2], C::KB * kBlk);
+    for (int kb = 0; kb < C::KB; ++kb)
+      bulk_g2s(sA + kb * kBlk, act_a + ((size_t)tile * C::KB + kb) * kBlkElems, kBlk, &bars[2]);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (tid == 0) {
-    if (mbar_wait(&bars[0], 0, status)) {
+    if (mbar_wait(&bars[0], 0, status) && mbar_wait(&bars[2], 0, status)) {
       tc_fence_after();
       umma_tile(tmem, smem_u32(sA), kBlk, smem_u32(sB), NT * 128, 0, C::KB, idesc_bf16(128, NT), false);
     }
@@ -301,21 +344,23 @@ __global__ void __launch_bounds__(128) k_adaln(DevWeights w, ModelDims md, int r
   const bool ok = mbar_wait(&bars[1], 0, status);
   __syncwarp();
   tc_fence_after();
-  const int row = tile * 128 + tid;
+  const int quad = warp & 3, slice = warp >> 2;
+  const int row = tile * 128 + quad * 32 + lane;
   const int ncols = md.L * 6 * D;
-  const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-  for (int c0 = 0; c0 < NT; c0 += 16) {
-    float v[16];
-    tmem_ld16(taddr + c0, v);
-    tmem_ld_wait();
-    if (ok && row < rows) {
-      const int n0 = nt * NT + c0;
-      uint32_t pk[8];
+  const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * CW;
+  float v[CW];
+  tmem_ld_cols<CW>(taddr, v);
+  if (ok && row < rows) {
+    const int n0 = nt * NT + slice * CW;
+    uint4* dst = reinterpret_cast<uint4*>(mod + (size_t)row * ncols + n0);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) pk[i] = pack_bf16x2(v[2 * i] + w.ada_b[n0 + 2 * i], v[2 * i + 1] + w.ada_b[n0 + 2 * i + 1]);
-      uint4* dst = reinterpret_cast<uint4*>(mod + (size_t)row * ncols + n0);
-      dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+    for (int i = 0; i < CW / 8; ++i) {
+      uint32_t pk[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        pk[k] = pack_bf16x2(v[8 * i + 2 * k] + w.ada_b[n0 + 8 * i + 2 * k],
+                            v[8 * i + 2 * k + 1] + w.ada_b[n0 + 8 * i + 2 * k + 1]);
+      dst[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     }
   }
   tc_fence_before();
@@ -326,8 +371,8 @@ __global__ void __launch_bounds__(128) k_adaln(DevWeights w, ModelDims md, int r
 
 // ---------------------------------------------------------------- QKV + attention
 template <int D>
-__global__ void __launch_bounds__(128) k_qkv_attn(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b, int layer,
-                                                  uint32_t* status) {
+__global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b,
+                                                       int layer, uint32_t* status) {
   using C = Cfg<D>;
   constexpr int KB = C::KB;
   constexpr int ST = C::QKV_ST;
@@ -368,30 +413,31 @@ __global__ void __launch_bounds__(128) k_qkv_attn(DevWeights w, ModelDims md, Ca
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
+  griddep_wait();
+  griddep_launch();
   // Prologue: window rows -> LN1 -> modulate(shift_msa, scale_msa) -> attn.norm -> bf16 A.
-  const int NP = g.T - g.H + 1;
-  for (int r = warp; r < 128; r += 4) {
+  const int NPRED = g.T - g.H + 1;
+  for (int r = tid / C::TPR; r < 128; r += C::RPP) {
+    const int q = tid % C::TPR;
     const RowMap m = map_row(g, tile, r);
-    if (!m.valid) {
-      zero_row<D>(sA, r, lane);
-      continue;
-    }
-    const __nv_bfloat16* mrow = b.mod + (size_t)m.tok * ncols + layer * 6 * D;
+    const __nv_bfloat16* mrow = b.mod + (size_t)(m.valid ? m.tok : 0) * ncols + layer * 6 * D;
     float* xdst = b.x + ((size_t)tile * 128 + r) * D;
     if (layer == 0) {
-      const int j = g.start + m.pos;
-      const float* src;
-      if (j < g.H) {
-        const int e = b.emb_per_cand ? m.cand : (m.cand / g.S);
-        src = b.emb + ((size_t)e * g.H + j) * D;
-      } else {
-        src = b.pred + ((size_t)m.cand * NP + (j - g.H)) * D;
+      const float* src = b.emb;
+      if (m.valid) {
+        const int j = g.start + m.pos;
+        if (j < g.H) {
+          const int e = b.emb_per_cand ? m.cand : (m.cand / g.S);
+          src = b.emb + ((size_t)e * g.H + j) * D;
+        } else {
+          src = b.pred + ((size_t)m.cand * NPRED + (j - g.H)) * D;
+        }
       }
-      ln_mod_ln_row<D>(src, w.pos + m.pos * D, mrow, mrow + D, w.attn_ln_w + layer * D, w.attn_ln_b + layer * D,
-                       sA, r, lane, head == 0 ? xdst : nullptr);
+      ln_mod_ln_part<D>(m.valid, src, w.pos + m.pos * D, mrow, mrow + D, w.attn_ln_w + layer * D,
+                        w.attn_ln_b + layer * D, sA, r, q, head == 0 ? xdst : nullptr);
     } else {
-      ln_mod_ln_row<D>(xdst, nullptr, mrow, mrow + D, w.attn_ln_w + layer * D, w.attn_ln_b + layer * D, sA, r,
-                       lane, nullptr);
+      ln_mod_ln_part<D>(m.valid, xdst, nullptr, mrow, mrow + D, w.attn_ln_w + layer * D, w.attn_ln_b + layer * D,
+                        sA, r, q, nullptr);
     }
   }
   fence_async_smem();
@@ -423,52 +469,65 @@ __global__ void __launch_bounds__(128) k_qkv_attn(DevWeights w, ModelDims md, Ca
   const bool ok = mbar_wait(bar_mma, 0, status);
   __syncwarp();
   tc_fence_after();
-  {  // q|k|v of this head -> scratch rows (fp32)
-    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-    float* srow = scr + tid * kScratchStride;
-    for (int c0 = 0; c0 < 192; c0 += 16) {
-      float v[16];
-      tmem_ld16(taddr + c0, v);
-      tmem_ld_wait();
+  {  // q|k|v of this head -> scratch rows (fp32); warp slice s owns columns [48s, 48s+48)
+    const int quad = warp & 3, slice = warp >> 2;
+    const int r = quad * 32 + lane;
+    const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * 48;
+    float v[48];
+    tmem_ld_cols<48>(taddr, v);
+    float* srow = scr + r * kScratchStride + slice * 48;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) srow[c0 + i] = v[i];
-    }
+    for (int i = 0; i < 48; ++i) srow[i] = v[i];
   }
   __syncthreads();
-  {  // causal softmax(q k^T / 8) v within the candidate's window
-    const int r = tid;
+  {  // causal softmax(q k^T / 8) v within the candidate's window; 4 threads per row, 16 dims each
+    const int r = tid >> 2, part = tid & 3;
     const RowMap m = map_row(g, tile, r);
-    if (ok && m.valid) {
-      const int base = r - m.pos;
-      const float* qr = scr + r * kScratchStride;
-      float sc[kMaxWindow];
-      float mx = -INFINITY;
-      for (int j = 0; j <= m.pos; ++j) {
-        const float* kr = scr + (base + j) * kScratchStride + 64;
-        float d = 0.f;
-#pragma unroll 16
-        for (int t = 0; t < 64; ++t) d += qr[t] * kr[t];
-        sc[j] = d * 0.125f;
-        mx = fmaxf(mx, sc[j]);
+    const bool valid = ok && m.valid;
+    const int base = r - m.pos;
+    const float* qr = scr + r * kScratchStride + part * 16;
+    float sc[kMaxWindow];
+    float mx = -INFINITY;
+    for (int j = 0; j < g.w; ++j) {
+      float d = 0.f;
+      if (valid && j <= m.pos) {
+        const float* kr = scr + (base + j) * kScratchStride + 64 + part * 16;
+#pragma unroll
+        for (int t = 0; t < 16; ++t) d += qr[t] * kr[t];
       }
-      float den = 0.f;
-      for (int j = 0; j <= m.pos; ++j) {
-        sc[j] = expf(sc[j] - mx);
-        den += sc[j];
-      }
-      const float inv = 1.0f / den;
-      for (int t = 0; t < 64; t += 2) {
-        float o0 = 0.f, o1 = 0.f;
-        for (int j = 0; j <= m.pos; ++j) {
-          const float* vr = scr + (base + j) * kScratchStride + 128;
-          o0 += sc[j] * vr[t];
-          o1 += sc[j] * vr[t + 1];
-        }
-        *reinterpret_cast<uint32_t*>(sO + sw128_off(r, t)) = pack_bf16x2(o0 * inv, o1 * inv);
-      }
-    } else {
-      for (int t = 0; t < 64; t += 2) *reinterpret_cast<uint32_t*>(sO + sw128_off(r, t)) = 0u;
+      d += __shfl_xor_sync(0xffffffffu, d, 1);
+      d += __shfl_xor_sync(0xffffffffu, d, 2);
+      sc[j] = d * 0.125f;
+      if (j <= m.pos) mx = fmaxf(mx, sc[j]);
     }
+    float den = 0.f;
+    for (int j = 0; j < g.w; ++j) {
+      sc[j] = (j <= m.pos) ? expf(sc[j] - mx) : 0.f;
+      den += sc[j];
+    }
+    const float inv = 1.0f / den;
+    float o[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) o[t] = 0.f;
+    if (valid) {
+      for (int j = 0; j <= m.pos; ++j) {
+        const float* vr = scr + (base + j) * kScratchStride + 128 + part * 16;
+#pragma unroll
+        for (int t = 0; t < 16; ++t) o[t] += sc[j] * vr[t];
+      }
+    }
+    uint4 lo, hi;
+    lo.x = pack_bf16x2(o[0] * inv, o[1] * inv);
+    lo.y = pack_bf16x2(o[2] * inv, o[3] * inv);
+    lo.z = pack_bf16x2(o[4] * inv, o[5] * inv);
+    lo.w = pack_bf16x2(o[6] * inv, o[7] * inv);
+    hi.x = pack_bf16x2(o[8] * inv, o[9] * inv);
+    hi.y = pack_bf16x2(o[10] * inv, o[11] * inv);
+    hi.z = pack_bf16x2(o[12] * inv, o[13] * inv);
+    hi.w = pack_bf16x2(o[14] * inv, o[15] * inv);
+    if (!valid) lo = hi = make_uint4(0u, 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(sO + sw128_off(r, part * 16)) = lo;
+    *reinterpret_cast<uint4*>(sO + sw128_off(r, part * 16 + 8)) = hi;
   }
   fence_async_smem();
   tc_fence_before();
@@ -486,13 +545,14 @@ __global__ void __launch_bounds__(128) k_qkv_attn(DevWeights w, ModelDims md, Ca
 // x[:, n-tile] += gate * (A . B^T + bias), A streamed from pre-swizzled global tiles.
 // Used for the attention out-projection (gate_msa) and FC2 (gate_mlp).
 template <int D>
-__global__ void __launch_bounds__(128) k_resid_gemm(const __nv_bfloat16* __restrict__ gA, int nkb,
-                                                    const __nv_bfloat16* __restrict__ gB,
-                                                    const float* __restrict__ bias, int gate_chunk, CallGeom g,
-                                                    RolloutBufs b, ModelDims md, int layer, uint32_t* status) {
+__global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __restrict__ gA, int nkb,
+                                                         const __nv_bfloat16* __restrict__ gB,
+                                                         const float* __restrict__ bias, int gate_chunk, CallGeom g,
+                                                         RolloutBufs b, ModelDims md, int layer, uint32_t* status) {
   using C = Cfg<D>;
   constexpr int NT = C::NT_OUT;
-  constexpr int ST = 4;
+  constexpr int CW = NT / 4;
+  constexpr int ST = C::RES_ST;
   constexpr int B_BLK = NT * 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -502,10 +562,11 @@ __global__ void __launch_bounds__(128) k_resid_gemm(const __nv_bfloat16* __restr
   uint64_t* empty = full + ST;
   uint64_t* bar_mma = empty + ST;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x, nt = blockIdx.y;
   const __nv_bfloat16* tA = gA + (size_t)tile * nkb * kBlkElems;
   const __nv_bfloat16* tB = gB + (size_t)nt * nkb * NT * 64;
+  const int pre = ST < nkb ? ST : nkb;
   if (tid == 0) {
     for (int s = 0; s < ST; ++s) {
       mbar_init(&full[s], 1);
@@ -513,9 +574,8 @@ __global__ void __launch_bounds__(128) k_resid_gemm(const __nv_bfloat16* __restr
     }
     mbar_init(bar_mma, 1);
     fence_mbar_init();
-    for (int s = 0; s < ST && s < nkb; ++s) {
+    for (int s = 0; s < pre; ++s) {  // weights first: they do not depend on the previous kernel
       mbar_arrive_expect_tx(&full[s], kBlk + B_BLK);
-      bulk_g2s(sA + s * kBlk, tA + (size_t)s * kBlkElems, kBlk, &full[s]);
       bulk_g2s(sB + s * B_BLK, tB + (size_t)s * NT * 64, B_BLK, &full[s]);
     }
   }
@@ -524,6 +584,10 @@ __global__ void __launch_bounds__(128) k_resid_gemm(const __nv_bfloat16* __restr
     tmem_alloc(tmem_slot, C::TMEM_OUT);
     tmem_relinquish();
   }
+  griddep_wait();
+  griddep_launch();
+  if (tid == 0)
+    for (int s = 0; s < pre; ++s) bulk_g2s(sA + s * kBlk, tA + (size_t)s * kBlkElems, kBlk, &full[s]);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -556,26 +620,29 @@ __global__ void __launch_bounds__(128) k_resid_gemm(const __nv_bfloat16* __restr
   const bool ok = mbar_wait(bar_mma, 0, status);
   __syncwarp();
   tc_fence_after();
-  const int r = tid;
+  const int quad = warp & 3, slice = warp >> 2;
+  const int r = quad * 32 + lane;
   const RowMap m = map_row(g, tile, r);
-  const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-  const int ncols = md.L * 6 * D;
-  float* xrow = b.x + ((size_t)tile * 128 + r) * D + nt * NT;
-  const __nv_bfloat16* gate = b.mod + (size_t)m.tok * ncols + layer * 6 * D + gate_chunk * D + nt * NT;
-  const float* bs = bias + nt * NT;
-  for (int c0 = 0; c0 < NT; c0 += 16) {
-    float v[16];
-    tmem_ld16(taddr + c0, v);
-    tmem_ld_wait();
-    if (ok && m.valid) {
+  const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * CW;
+  float v[CW];
+  tmem_ld_cols<CW>(taddr, v);
+  if (ok && m.valid) {
+    const int ncols = md.L * 6 * D;
+    const int c0 = nt * NT + slice * CW;
+    float* xrow = b.x + ((size_t)tile * 128 + r) * D + c0;
+    const __nv_bfloat16* gate = b.mod + (size_t)m.tok * ncols + layer * 6 * D + gate_chunk * D + c0;
+    const float* bs = bias + c0;
 #pragma unroll
-      for (int i = 0; i < 16; i += 2) {
-        const float2 gt = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(gate + c0 + i));
-        float2 xv = *reinterpret_cast<float2*>(xrow + c0 + i);
-        xv.x += gt.x * (v[i] + bs[c0 + i]);
-        xv.y += gt.y * (v[i + 1] + bs[c0 + i + 1]);
-        *reinterpret_cast<float2*>(xrow + c0 + i) = xv;
-      }
+    for (int i = 0; i < CW; i += 4) {
+      const uint2 gt = *reinterpret_cast<const uint2*>(gate + i);
+      const float2 g01 = unpack_bf16x2(gt.x), g23 = unpack_bf16x2(gt.y);
+      const float4 b4 = *reinterpret_cast<const float4*>(bs + i);
+      float4 xv = *reinterpret_cast<float4*>(xrow + i);
+      xv.x += g01.x * (v[i] + b4.x);
+      xv.y += g01.y * (v[i + 1] + b4.y);
+      xv.z += g23.x * (v[i + 2] + b4.z);
+      xv.w += g23.y * (v[i + 3] + b4.w);
+      *reinterpret_cast<float4*>(xrow + i) = xv;
     }
   }
   tc_fence_before();
@@ -586,8 +653,8 @@ __global__ void __launch_bounds__(128) k_resid_gemm(const __nv_bfloat16* __restr
 
 // ---------------------------------------------------------------- FC1 + GELU
 template <int D>
-__global__ void __launch_bounds__(128) k_fc1(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b, int layer,
-                                             uint32_t* status) {
+__global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b, int layer,
+                                                  uint32_t* status) {
   using C = Cfg<D>;
   constexpr int KB = C::KB;
   constexpr int ST = C::QKV_ST;
@@ -622,15 +689,14 @@ __global__ void __launch_bounds__(128) k_fc1(DevWeights w, ModelDims md, CallGeo
     tmem_alloc(tmem_slot, 128);
     tmem_relinquish();
   }
-  for (int r = warp; r < 128; r += 4) {
+  griddep_wait();
+  griddep_launch();
+  for (int r = tid / C::TPR; r < 128; r += C::RPP) {
+    const int q = tid % C::TPR;
     const RowMap m = map_row(g, tile, r);
-    if (!m.valid) {
-      zero_row<D>(sA, r, lane);
-      continue;
-    }
-    const __nv_bfloat16* mrow = b.mod + (size_t)m.tok * ncols + layer * 6 * D;
-    ln_mod_ln_row<D>(b.x + ((size_t)tile * 128 + r) * D, nullptr, mrow + 3 * D, mrow + 4 * D,
-                     w.ffn_ln_w + layer * D, w.ffn_ln_b + layer * D, sA, r, lane, nullptr);
+    const __nv_bfloat16* mrow = b.mod + (size_t)(m.valid ? m.tok : 0) * ncols + layer * 6 * D;
+    ln_mod_ln_part<D>(m.valid, b.x + ((size_t)tile * 128 + r) * D, nullptr, mrow + 3 * D, mrow + 4 * D,
+                      w.ffn_ln_w + layer * D, w.ffn_ln_b + layer * D, sA, r, q, nullptr);
   }
   fence_async_smem();
   tc_fence_before();
@@ -661,23 +727,26 @@ __global__ void __launch_bounds__(128) k_fc1(DevWeights w, ModelDims md, CallGeo
   const bool ok = mbar_wait(bar_mma, 0, status);
   __syncwarp();
   tc_fence_after();
-  {
-    const int r = tid;
+  {  // warp slice s owns hidden columns [32s, 32s+32) of this 128-wide chunk
+    const int quad = warp & 3, slice = warp >> 2;
+    const int r = quad * 32 + lane;
     const RowMap m = map_row(g, tile, r);
     const bool valid = ok && m.valid;
-    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-    const float* bs = w.b1 + layer * md.mlp + nt * 128;
-    for (int c0 = 0; c0 < 128; c0 += 16) {
-      float v[16];
-      tmem_ld16(taddr + c0, v);
-      tmem_ld_wait();
+    const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * 32;
+    const float* bs = w.b1 + layer * md.mlp + nt * 128 + slice * 32;
+    float v[32];
+    tmem_ld_cols<32>(taddr, v);
 #pragma unroll
-      for (int i = 0; i < 16; i += 2) {
-        const int c = c0 + i;
-        const float a0 = valid ? gelu_f(v[i] + bs[c]) : 0.f;
-        const float a1 = valid ? gelu_f(v[i + 1] + bs[c + 1]) : 0.f;
-        *reinterpret_cast<uint32_t*>(sO + (c >> 6) * kBlk + sw128_off(r, c & 63)) = pack_bf16x2(a0, a1);
+    for (int i = 0; i < 32; i += 8) {
+      uint4 pk = make_uint4(0u, 0u, 0u, 0u);
+      if (valid) {
+        pk.x = pack_bf16x2(gelu_f(v[i] + bs[i]), gelu_f(v[i + 1] + bs[i + 1]));
+        pk.y = pack_bf16x2(gelu_f(v[i + 2] + bs[i + 2]), gelu_f(v[i + 3] + bs[i + 3]));
+        pk.z = pack_bf16x2(gelu_f(v[i + 4] + bs[i + 4]), gelu_f(v[i + 5] + bs[i + 5]));
+        pk.w = pack_bf16x2(gelu_f(v[i + 6] + bs[i + 6]), gelu_f(v[i + 7] + bs[i + 7]));
       }
+      const int c = slice * 32 + i;
+      *reinterpret_cast<uint4*>(sO + (c >> 6) * kBlk + sw128_off(r, c & 63)) = pk;
     }
   }
   fence_async_smem();
@@ -697,6 +766,8 @@ __global__ void __launch_bounds__(128) k_fc1(DevWeights w, ModelDims md, CallGeo
 // ---------------------------------------------------------------- final LayerNorm + history / cost
 template <int D>
 __global__ void __launch_bounds__(128) k_final(DevWeights w, CallGeom g, RolloutBufs b) {
+  griddep_wait();
+  griddep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cand = blockIdx.x * 4 + warp;
   if (cand >= g.n_cand) return;
@@ -758,9 +829,13 @@ constexpr int smem_qkv() {
   return 1024 + R1S + kBlk + 128;
 }
 template <int D>
-constexpr int smem_resid() { return 1024 + 4 * kBlk + 4 * Cfg<D>::NT_OUT * 128 + 128; }
+constexpr int smem_resid() { return 1024 + Cfg<D>::RES_ST * (kBlk + Cfg<D>::NT_OUT * 128) + 128; }
 template <int D>
 constexpr int smem_fc1() { return 1024 + Cfg<D>::KB * kBlk + Cfg<D>::QKV_ST * kBlk + 128; }
+
+static_assert(smem_qkv<192>() <= 232448 && smem_qkv<384>() <= 232448, "qkv smem");
+static_assert(smem_embed<384>() <= 232448 && smem_adaln<384>() <= 232448, "embed/adaln smem");
+static_assert(smem_fc1<384>() <= 232448 && smem_resid<384>() <= 232448, "fc smem");
 
 template <int D>
 cudaError_t set_smem_attrs() {
@@ -777,10 +852,6 @@ cudaError_t set_smem_attrs() {
   return cudaSuccess;
 }
 
-static_assert(smem_qkv<192>() <= 232448 && smem_qkv<384>() <= 232448, "qkv smem");
-static_assert(smem_embed<384>() <= 232448 && smem_adaln<384>() <= 232448, "embed/adaln smem");
-static_assert(smem_fc1<384>() <= 232448 && smem_resid<384>() <= 232448, "fc smem");
-
 template <int D>
 cudaError_t embed_impl(const ModelDims& md, const DevWeights& w, const float* cand, int rows, __nv_bfloat16* act_a,
                        uint32_t* status, cudaStream_t st, Prof* prof) {
@@ -788,9 +859,9 @@ cudaError_t embed_impl(const ModelDims& md, const DevWeights& w, const float* ca
   if (e) return e;
   const int tiles = (rows + 127) / 128;
   if (prof) prof->begin(st);
-  k_embed<D><<<tiles, 256, smem_embed<D>(), st>>>(w, md, cand, rows, act_a, status);
+  e = launch_k(k_embed<D>, dim3(tiles), dim3(256), smem_embed<D>(), st, w, md, cand, rows, act_a, status);
   if (prof) prof->end(KC_EMBED, 2.0 * rows * ((double)md.A * md.As + (double)md.As * md.eh + (double)md.eh * D), st);
-  return cudaGetLastError();
+  return e;
 }
 
 template <int D>
@@ -801,9 +872,9 @@ cudaError_t adaln_impl(const ModelDims& md, const DevWeights& w, int rows, const
   const int tiles = (rows + 127) / 128;
   const int ntiles = md.L * 6 * D / Cfg<D>::NT_ADA;
   if (prof) prof->begin(st);
-  k_adaln<D><<<dim3(tiles, ntiles), 128, smem_adaln<D>(), st>>>(w, md, rows, act_a, mod, status);
+  e = launch_k(k_adaln<D>, dim3(tiles, ntiles), dim3(kThreads), smem_adaln<D>(), st, w, md, rows, act_a, mod, status);
   if (prof) prof->end(KC_ADALN, 2.0 * rows * (double)D * md.L * 6 * D, st);
-  return cudaGetLastError();
+  return e;
 }
 
 template <int D>
@@ -813,27 +884,37 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
   if (e) return e;
   const int nkb_inner = md.inner / 64, nkb_mlp = md.mlp / 64;
   const double rows = (double)g.n_cand * g.w;  // valid window rows
+#define LEWM_TRY(x)                         \
+  do {                                      \
+    if ((e = (x)) != cudaSuccess) return e; \
+  } while (0)
   for (int l = 0; l < md.L; ++l) {
     if (prof) prof->begin(st);
-    k_qkv_attn<D><<<dim3(g.n_tiles, md.heads), 128, smem_qkv<D>(), st>>>(w, md, g, b, l, status);
+    LEWM_TRY(launch_k(k_qkv_attn<D>, dim3(g.n_tiles, md.heads), dim3(kThreads), smem_qkv<D>(), st, w, md, g, b, l,
+                      status));
     if (prof) prof->end(KC_QKV_ATTN, 2.0 * rows * D * 3 * md.inner + 4.0 * rows * g.w * md.inner, st);
     if (prof) prof->begin(st);
-    k_resid_gemm<D><<<dim3(g.n_tiles, 4), 128, smem_resid<D>(), st>>>(
-        b.attn, nkb_inner, w.wout + (size_t)l * 4 * nkb_inner * Cfg<D>::NT_OUT * 64, w.out_b + l * D, 2, g, b, md, l,
-        status);
+    LEWM_TRY(launch_k(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads), smem_resid<D>(), st,
+                      (const __nv_bfloat16*)b.attn, nkb_inner,
+                      (const __nv_bfloat16*)(w.wout + (size_t)l * 4 * nkb_inner * Cfg<D>::NT_OUT * 64),
+                      (const float*)(w.out_b + l * D), 2, g, b, md, l, status));
     if (prof) prof->end(KC_OUT, 2.0 * rows * md.inner * D, st);
     if (prof) prof->begin(st);
-    k_fc1<D><<<dim3(g.n_tiles, md.mlp / 128), 128, smem_fc1<D>(), st>>>(w, md, g, b, l, status);
+    LEWM_TRY(launch_k(k_fc1<D>, dim3(g.n_tiles, md.mlp / 128), dim3(kThreads), smem_fc1<D>(), st, w, md, g, b, l,
+                      status));
     if (prof) prof->end(KC_FC1, 2.0 * rows * D * md.mlp, st);
     if (prof) prof->begin(st);
-    k_resid_gemm<D><<<dim3(g.n_tiles, 4), 128, smem_resid<D>(), st>>>(
-        b.h, nkb_mlp, w.w2 + (size_t)l * 4 * nkb_mlp * Cfg<D>::NT_OUT * 64, w.b2 + l * D, 5, g, b, md, l, status);
+    LEWM_TRY(launch_k(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads), smem_resid<D>(), st,
+                      (const __nv_bfloat16*)b.h, nkb_mlp,
+                      (const __nv_bfloat16*)(w.w2 + (size_t)l * 4 * nkb_mlp * Cfg<D>::NT_OUT * 64),
+                      (const float*)(w.b2 + l * D), 5, g, b, md, l, status));
     if (prof) prof->end(KC_FC2, 2.0 * rows * md.mlp * D, st);
   }
   if (prof) prof->begin(st);
-  k_final<D><<<(g.n_cand + 3) / 4, 128, 0, st>>>(w, g, b);
+  LEWM_TRY(launch_k(k_final<D>, dim3((g.n_cand + 3) / 4), dim3(128), 0, st, w, g, b));
   if (prof) prof->end(KC_FINAL, 0.0, st);
-  return cudaGetLastError();
+#undef LEWM_TRY
+  return cudaSuccess;
 }
 
 }  // namespace

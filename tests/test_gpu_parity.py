@@ -287,3 +287,25 @@ def test_plan_lowers_cost_over_iterations():
     # the returned mean's own cost is close to the best elites' cost
     c = rt.model_cost(emb, goal, act[:, None])
     assert c.item() <= first
+
+
+def test_graph_replay_matches_direct_launch():
+    """The cached CUDA-graph plan and the directly launched plan (trace on) agree bit for bit."""
+    desc = ModelDesc()
+    rt = runtime(desc, 0)
+    rng = np.random.default_rng(4)
+    B = 3
+    emb, goal = cuda(rng.standard_normal((B, 3, desc.dim))), cuda(rng.standard_normal((B, 1, desc.dim)))
+    mean = cuda(rng.standard_normal((B, 5, 10)) * 0.1)
+    std = torch.ones(B, 5, 10, device="cuda:0")
+    lo_, hi_ = -torch.ones(10, device="cuda:0"), torch.ones(10, device="cuda:0")
+    opts = PlanOptions(num_samples=90, topk=9, n_steps=5, sample_decay=1.25, sample_count_bucket_size=30,
+                       elite_retention=2, beta=1.0, action_block=5, momentum_alpha=0.1, clip_actions=True)
+    g1 = rt.plan(opts, emb, goal, mean, std, action_low=lo_, action_high=hi_, plan_index=7)
+    g2 = rt.plan(opts, emb, goal, mean, std, action_low=lo_, action_high=hi_, plan_index=7)  # cached graph
+    d = rt.plan(opts, emb, goal, mean, std, action_low=lo_, action_high=hi_, plan_index=7, trace=True)
+    rt.sync()
+    for a, b_, c in zip(g1[:3], g2[:3], d[:3]):
+        assert torch.equal(a, b_)
+        assert torch.equal(a, c)
+    assert (g1[0].abs() <= 1).all()
