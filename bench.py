@@ -248,9 +248,6 @@ def main() -> int:
     value = world * args.steps / (worst_ms / 1e3)
     p50 = percentile(plan_ms, 50)
 
-    # ---------------------------------------------------------------- per-kernel-class timing pass
-    kinfo = kernel_class_pass(rt, opts, emb, goal, mean, std, dev)
-
     # ---------------------------------------------------------------- end to end through the solver API
     solver = B200ICEMSolver(rt, num_samples=300, n_steps=30, topk=30, elite_retention=3, colored_noise="brown",
                             colored_noise_time="raw", sample_decay=1.25, sample_count_bucket_size=60, seed=0,
@@ -285,6 +282,8 @@ def main() -> int:
     h2d = host_emb.numel() * 4 + host_goal.numel() * 4 + 2 * 5 * 10 * 4
     d2h = out["actions"].numel() * 4 + out["var"][0].numel() * 4 + len(out["costs"]) * 4
 
+    # ---------------------------------------------------------------- per-kernel-class timing pass (diagnostic, last)
+    kinfo = kernel_class_pass(rt, opts, emb, goal, mean, std, dev)
     per_plan_launches = kinfo["launches_per_plan"]
     flops_plan = F_CANON * 2820
     line = {

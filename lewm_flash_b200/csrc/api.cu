@@ -37,7 +37,10 @@ struct Workspace {
   float* cand = nullptr;
   __nv_bfloat16* act_a = nullptr;
   __nv_bfloat16* mod = nullptr;
-  float* x = nullptr;
+  float* x = nullptr;    // two residual buffers: predictor calls alternate between them
+  float* x2 = nullptr;
+  __nv_bfloat16* a_attn = nullptr;
+  __nv_bfloat16* a_ffn = nullptr;
   __nv_bfloat16* attn = nullptr;
   __nv_bfloat16* h = nullptr;
   float* pred = nullptr;
@@ -334,6 +337,9 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   const size_t o_act = carve(tiles_e * (m.D / 64) * 128 * 64 * 2);
   const size_t o_mod = carve(rows_e * (size_t)m.L * 6 * m.D * 2);
   const size_t o_x = carve(r.tiles * 128 * (size_t)m.D * 4);
+  const size_t o_x2 = carve(r.tiles * 128 * (size_t)m.D * 4);
+  const size_t o_aat = carve(r.tiles * (size_t)(m.D / 64) * 128 * 64 * 2);
+  const size_t o_aff = carve(r.tiles * (size_t)(m.D / 64) * 128 * 64 * 2);
   const size_t o_attn = carve(r.tiles * (size_t)(m.inner / 64) * 128 * 64 * 2);
   const size_t o_h = carve(r.tiles * (size_t)(m.mlp / 64) * 128 * 64 * 2);
   const size_t o_pred = carve(r.n_cand * r.npred * (size_t)m.D * 4);
@@ -359,6 +365,9 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   ws.act_a = reinterpret_cast<__nv_bfloat16*>(b + o_act);
   ws.mod = reinterpret_cast<__nv_bfloat16*>(b + o_mod);
   ws.x = reinterpret_cast<float*>(b + o_x);
+  ws.x2 = reinterpret_cast<float*>(b + o_x2);
+  ws.a_attn = reinterpret_cast<__nv_bfloat16*>(b + o_aat);
+  ws.a_ffn = reinterpret_cast<__nv_bfloat16*>(b + o_aff);
   ws.attn = reinterpret_cast<__nv_bfloat16*>(b + o_attn);
   ws.h = reinterpret_cast<__nv_bfloat16*>(b + o_h);
   ws.pred = reinterpret_cast<float*>(b + o_pred);
@@ -387,14 +396,27 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
   const int rows = NC * T;
   LEWM_CK(c, launch_embed(m, c->w, cand, rows, c->ws.act_a, c->d_status, st, &c->prof));
   LEWM_CK(c, launch_adaln(m, c->w, rows, c->ws.act_a, c->ws.mod, c->d_status, st, &c->prof));
-  RolloutBufs b{emb, emb_pc, goal, goal_pc, cand, c->ws.act_a, c->ws.mod, c->ws.x, c->ws.attn, c->ws.h, c->ws.pred,
-                costs};
+  RolloutBufs b{emb, emb_pc, goal, goal_pc, cand, c->ws.act_a, c->ws.mod, c->ws.x, c->ws.x2, c->ws.a_attn,
+                c->ws.a_ffn, c->ws.attn, c->ws.h, c->ws.pred, costs};
   const int n_calls = T - H + 1;
-  for (int k = 0; k < n_calls; ++k) {
+  auto geom = [&](int k) {
     const int end = H + k;
     const int start = std::max(0, end - HS);
     const int w = end - start;
-    CallGeom g{NC, S, T, H, w, start, 128 / w, window_tiles(NC, w), k, k == n_calls - 1};
+    return CallGeom{NC, S, T, H, w, start, 128 / w, window_tiles(NC, w), k, k == n_calls - 1, 1, 0, 128};
+  };
+  for (int k = 0; k < n_calls; ++k) {
+    CallGeom g = geom(k);
+    if (k + 1 < n_calls) {
+      const CallGeom gn = geom(k + 1);
+      g.next_w = gn.w;
+      g.next_start = gn.start;
+      g.next_cpt = gn.cpt;
+    }
+    // Calls alternate residual buffers: k_final of call k writes call k+1's layer-0 rows.
+    b.x = (k & 1) ? c->ws.x2 : c->ws.x;
+    b.xn = (k & 1) ? c->ws.x : c->ws.x2;
+    if (k == 0) LEWM_CK(c, launch_prep0(m, c->w, g, b, st, &c->prof));
     LEWM_CK(c, launch_call(m, c->w, g, b, c->d_status, st, &c->prof));
   }
   return LEWM_OK;
@@ -915,8 +937,10 @@ lewm_status lewm_profile_plan(lewm_ctx* c, const lewm_plan_desc* p, const float*
   fc = sd + (size_t)B * TA;
   c->prof.reset();
   c->prof.on = true;
+  pdl_suppressed() = true;
   lewm_status s = lewm_plan(c, p, emb, goal, init_mean, init_std, nullptr, nullptr, nullptr, act, sd, fc, nullptr,
                             stream);
+  pdl_suppressed() = false;
   c->prof.on = false;
   cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   cudaFree(act);

@@ -80,6 +80,9 @@ __device__ __forceinline__ void bulk_s2g(void* gdst, const void* smem_src, uint3
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Wait until the shared-memory sources of every committed bulk store have been read
+// (the global writes complete on their own and are visible at grid completion).
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // Make generic-proxy shared-memory writes visible to the async proxy (MMA / bulk copy).
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -162,6 +165,20 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float* v) {
     tmem_ld4(taddr + N - 4, v + N - 4);
   }
   tmem_ld_wait();
+}
+
+// ----------------------------------------------------------------- thread-block clusters
+// Barrier over every thread of every CTA in the cluster; orders distributed
+// shared-memory stores before it with loads after it.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Store a float2 into the shared memory of CTA `rank` of this cluster, at the
+// address `local` has in the executing CTA.
+__device__ __forceinline__ void st_dsmem_f2(const void* local, uint32_t rank, float2 v) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(remote), "f"(v.x), "f"(v.y) : "memory");
 }
 
 // ----------------------------------------------------------------- programmatic dependent launch

@@ -76,6 +76,8 @@ struct CallGeom {
   int n_tiles;  // window tiles
   int call;     // prediction slot written by this call
   int last;     // 1: final call, write costs
+  // Window of the next call (k_final prepares its layer-0 inputs); unused when last.
+  int next_w, next_start, next_cpt;
 };
 
 struct RolloutBufs {
@@ -86,7 +88,10 @@ struct RolloutBufs {
   const float* cand;  // (NC,T,A)
   __nv_bfloat16* act_a;
   __nv_bfloat16* mod;
-  float* x;
+  float* x;        // residual stream of this call's window, [tiles][128][D]
+  float* xn;       // residual stream of the next call's window (k_final writes it)
+  __nv_bfloat16* a_attn;  // bf16 A operand of the QKV GEMM, [tiles][D/64][128x64]
+  __nv_bfloat16* a_ffn;   // bf16 A operand of the FC1 GEMM
   __nv_bfloat16* attn;
   __nv_bfloat16* h;
   float* pred;
@@ -97,7 +102,7 @@ struct RolloutBufs {
 // records an event pair and the algorithmic FLOPs of that launch under a kernel
 // class; lewm_profile_plan sums them after a synchronize.
 enum KernelClass { KC_EMBED = 0, KC_ADALN, KC_QKV_ATTN, KC_OUT, KC_FC1, KC_FC2, KC_FINAL, KC_SAMPLE, KC_REFIT,
-                   KC_COUNT };
+                   KC_PREP0, KC_COUNT };
 struct Prof {
   bool on = false;
   struct Rec {
@@ -139,26 +144,49 @@ struct Prof {
 
 // Launch with programmatic stream serialization (the kernel calls griddep_wait()
 // before touching its predecessor's output). LEWM_NO_PDL=1 turns it off.
+// Per-thread switch used while the event profiler is on: events recorded between
+// programmatically dependent launches would break their ordering, so profiled
+// plans launch every kernel with plain stream ordering.
+inline bool& pdl_suppressed() {
+  static thread_local bool off = false;
+  return off;
+}
 inline bool pdl_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("LEWM_NO_PDL");
     return !(v && v[0] == '1');
   }();
-  return on;
+  return on && !pdl_suppressed();
 }
 template <typename... KArgs, typename... Args>
-cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+cudaError_t launch_kc(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, dim3 cluster,
+                      Args&&... args) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute at[2];
+  int n = 0;
+  if (cluster.x * cluster.y * cluster.z > 1) {
+    at[n].id = cudaLaunchAttributeClusterDimension;
+    at[n].val.clusterDim.x = cluster.x;
+    at[n].val.clusterDim.y = cluster.y;
+    at[n].val.clusterDim.z = cluster.z;
+    ++n;
+  }
+  if (pdl_enabled()) {
+    at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
   cfg.attrs = at;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  return launch_kc(kern, grid, block, smem, st, dim3(1, 1, 1), std::forward<Args>(args)...);
 }
 
 // Launchers (rollout_kernels.cu). All asynchronous on `st`; `prof` may be null.
@@ -168,6 +196,10 @@ cudaError_t launch_adaln(const ModelDims& md, const DevWeights& w, int rows, con
                          __nv_bfloat16* mod, uint32_t* status, cudaStream_t st, Prof* prof);
 cudaError_t launch_call(const ModelDims& md, const DevWeights& w, const CallGeom& g, const RolloutBufs& b,
                         uint32_t* status, cudaStream_t st, Prof* prof);
+// Layer-0 inputs (residual x0 = history + position, and its LN1/modulate/LN A
+// operand) of the first predictor call of a rollout.
+cudaError_t launch_prep0(const ModelDims& md, const DevWeights& w, const CallGeom& g, const RolloutBufs& b,
+                         cudaStream_t st, Prof* prof);
 
 // iCEM kernels (icem_kernels.cu).
 struct SampleParams {

@@ -6,30 +6,48 @@
 //   k_adaln   AdaLN modulation Linear (lewm/module.py:98-100) for every layer at once;
 //             it depends only on the actions, so it is hoisted out of the
 //             autoregressive chain and computed once per candidate and time step
+//   k_prep0   first predictor call: layer-0 residual (history + position) and its
+//             LN1 -> modulate -> attn.norm operand
 //   per predictor call (lewm/jepa.py:284-298), per layer (lewm/module.py:105-111):
-//     k_qkv_attn  LN1 -> modulate -> attn.norm -> QKV GEMM (one head per CTA)
-//                 -> causal attention over the window (lewm/module.py:75-85)
-//     k_resid_gemm (out-proj) GEMM + bias, * gate_msa, + residual
-//     k_fc1       LN2 -> modulate -> FFN LayerNorm -> FC1 GEMM + bias -> GELU
-//     k_resid_gemm (FC2) GEMM + bias, * gate_mlp, + residual
-//   k_final     final LayerNorm (lewm/module.py:183) on each window's last token,
-//               then append to the history or score against the goal
-//               (cost_from_rollout, lewm/jepa.py:246-260)
+//     k_qkv_attn   QKV GEMM (one head per CTA) -> causal attention over the window
+//                  (lewm/module.py:75-85)
+//     k_resid_gemm out-proj GEMM + bias, * gate_msa, + residual, then
+//                  LN2 -> modulate -> FFN LayerNorm: the FC1 operand
+//     k_fc1        FC1 GEMM + bias -> GELU
+//     k_resid_gemm FC2 GEMM + bias, * gate_mlp, + residual, then (not after the
+//                  last layer) LN1 -> modulate -> attn.norm: the next QKV operand
+//   k_final   final LayerNorm (lewm/module.py:183) on each window's last token,
+//             then score against the goal (cost_from_rollout, lewm/jepa.py:246-260)
+//             or append to the history and prepare the next call's layer-0 rows
 //
 // GEMMs run on tcgen05 (bf16 in, fp32 accumulate in TMEM); operands arrive in
 // shared memory by bulk copy of pre-swizzled blocks; LayerNorm, modulation,
-// bias, GELU, gates, residuals and the cost are fp32 in prologues/epilogues.
+// bias, GELU, gates, residuals and the cost are fp32.
 //
-// Latency structure: every kernel is launched with programmatic stream
-// serialization. Before griddep_wait() a kernel only initialises barriers,
-// allocates TMEM and starts the bulk copies of its weight tiles, so that part
-// overlaps the previous kernel. Row work (LayerNorm prologues, attention) is
-// split over several threads per row and accumulator columns over the four
-// warps that share a TMEM lane quadrant, so no thread walks a long serial chain.
+// Latency structure (a single-env plan is a chain of thousands of small
+// dependent kernels, so every global-memory round trip on a kernel's critical
+// path counts):
+//   * every kernel is launched with programmatic stream serialization; before
+//     griddep_wait() it only initialises barriers, allocates TMEM and starts
+//     bulk copies of weights and per-layer vectors into shared memory, which
+//     overlaps the previous kernel;
+//   * each LayerNorm is computed once per row, by the kernel that produces the
+//     residual; its consumers bulk-load the finished bf16 operand;
+//   * the residual GEMMs are 4-CTA clusters (one N tile each) that combine the
+//     per-row LayerNorm moments through distributed shared memory;
+//   * accumulator columns are split over the four warps that share a TMEM lane
+//     quadrant, attention rows over four threads each;
+//   * in the streamed-K GEMMs a producer warp refills the operand ring while the
+//     MMA warp issues, so issue never waits for an MMA to retire.
 #include <algorithm>
 
 #include "lewm_common.cuh"
 #include "lewm_internal.h"
+
+// Phase-timing hook for diagnostic builds (no code in the product build).
+#ifndef LEWM_STAMP
+#define LEWM_STAMP(kind, phase)
+#endif
 
 namespace lewm {
 namespace {
@@ -53,8 +71,6 @@ struct Cfg {
   static constexpr int TMEM_EMB = (D <= 256) ? 256 : 512;
   static constexpr int QKV_ST = (KB < 3) ? KB : 3;
   static constexpr int RES_ST = 6;                // K-ring depth of the streamed-A GEMMs
-  static constexpr int TPR = D / 48;              // LayerNorm threads per row (48 columns each)
-  static constexpr int RPP = kThreads / TPR;      // rows per LayerNorm pass
 };
 
 struct RowMap {
@@ -69,96 +85,6 @@ __device__ __forceinline__ RowMap map_row(const CallGeom& g, int tile, int r) {
   m.valid = (cl < g.cpt) && (m.cand < g.n_cand);
   m.tok = m.cand * g.T + g.start + m.pos;
   return m;
-}
-
-// ---------------------------------------------------------------- row prologue
-// TPR threads per row; thread q holds float4 chunks j = q + TPR*i (i < 12), i.e.
-// columns 4j..4j+3. A-row (bf16, swizzled) = LN_affine(LN(x)*(1+scale)+shift).
-// Every lane runs the group shuffles; invalid rows compute on zeros and store zeros.
-template <int D>
-__device__ __forceinline__ void ln_mod_ln_part(bool valid, const float* __restrict__ xrow,
-                                               const float* __restrict__ addrow,
-                                               const __nv_bfloat16* __restrict__ shift,
-                                               const __nv_bfloat16* __restrict__ scale,
-                                               const float* __restrict__ g, const float* __restrict__ bb,
-                                               uint8_t* a_smem, int r, int q, float* __restrict__ xout) {
-  constexpr int TPR = Cfg<D>::TPR;
-  constexpr int NC = 12;
-  float4 v[NC];
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    const int c = 4 * (q + TPR * i);
-    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (valid) {
-      t = *reinterpret_cast<const float4*>(xrow + c);
-      if (addrow) {
-        const float4 a = *reinterpret_cast<const float4*>(addrow + c);
-        t.x += a.x;
-        t.y += a.y;
-        t.z += a.z;
-        t.w += a.w;
-      }
-      if (xout) *reinterpret_cast<float4*>(xout + c) = t;
-    }
-    v[i] = t;
-    s += (t.x + t.y) + (t.z + t.w);
-  }
-#pragma unroll
-  for (int o = TPR / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  const float mean = s * (1.0f / D);
-  float q2 = 0.f;
-#pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
-    q2 += (a * a + b * b) + (c * c + d * d);
-  }
-#pragma unroll
-  for (int o = TPR / 2; o > 0; o >>= 1) q2 += __shfl_xor_sync(0xffffffffu, q2, o);
-  const float rstd = rsqrtf(q2 * (1.0f / D) + 1e-6f);
-  float s2 = 0.f;
-#pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    const int c = 4 * (q + TPR * i);
-    float2 sh01 = make_float2(0.f, 0.f), sh23 = sh01, sc01 = sh01, sc23 = sh01;
-    if (valid) {
-      const uint2 sh = *reinterpret_cast<const uint2*>(shift + c);
-      const uint2 sc = *reinterpret_cast<const uint2*>(scale + c);
-      sh01 = unpack_bf16x2(sh.x);
-      sh23 = unpack_bf16x2(sh.y);
-      sc01 = unpack_bf16x2(sc.x);
-      sc23 = unpack_bf16x2(sc.y);
-    }
-    v[i].x = (v[i].x - mean) * rstd * (1.0f + sc01.x) + sh01.x;
-    v[i].y = (v[i].y - mean) * rstd * (1.0f + sc01.y) + sh01.y;
-    v[i].z = (v[i].z - mean) * rstd * (1.0f + sc23.x) + sh23.x;
-    v[i].w = (v[i].w - mean) * rstd * (1.0f + sc23.y) + sh23.y;
-    s2 += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-  }
-#pragma unroll
-  for (int o = TPR / 2; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-  const float mean2 = s2 * (1.0f / D);
-  float q3 = 0.f;
-#pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    const float a = v[i].x - mean2, b = v[i].y - mean2, c = v[i].z - mean2, d = v[i].w - mean2;
-    q3 += (a * a + b * b) + (c * c + d * d);
-  }
-#pragma unroll
-  for (int o = TPR / 2; o > 0; o >>= 1) q3 += __shfl_xor_sync(0xffffffffu, q3, o);
-  const float rstd2 = rsqrtf(q3 * (1.0f / D) + 1e-5f);
-#pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    const int c = 4 * (q + TPR * i);
-    uint2 out = make_uint2(0u, 0u);
-    if (valid) {
-      const float4 gg = *reinterpret_cast<const float4*>(g + c);
-      const float4 b4 = *reinterpret_cast<const float4*>(bb + c);
-      out.x = pack_bf16x2((v[i].x - mean2) * rstd2 * gg.x + b4.x, (v[i].y - mean2) * rstd2 * gg.y + b4.y);
-      out.y = pack_bf16x2((v[i].z - mean2) * rstd2 * gg.z + b4.z, (v[i].w - mean2) * rstd2 * gg.w + b4.w);
-    }
-    *reinterpret_cast<uint2*>(a_smem + (c >> 6) * kBlk + sw128_off(r, c & 63)) = out;
-  }
 }
 
 // ---------------------------------------------------------------- Embedder + SiLU
@@ -178,7 +104,7 @@ __global__ void __launch_bounds__(256) k_embed(DevWeights w, ModelDims md, const
   uint64_t* bar_mma = bars + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row0 = blockIdx.x * 128;
   if (tid == 0) {
     mbar_init(bar_b, 1);
@@ -240,23 +166,27 @@ __global__ void __launch_bounds__(256) k_embed(DevWeights w, ModelDims md, const
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (tid == 0) {
-      if (mbar_wait(bar_b, c & 1, status)) {
-        tc_fence_after();
-        const uint32_t idesc = idesc_bf16(128, 192);
-        for (int kb = 0; kb < 2; ++kb) {
+    if (warp == 0) {  // whole warp waits, lane 0 issues (keeps the issuing warp converged)
+      const bool got = __all_sync(0xffffffffu, mbar_wait(bar_b, c & 1, status));
+      if (lane == 0) {
+        if (got) {
+          tc_fence_after();
+          const uint32_t idesc = idesc_bf16(128, 192);
+          for (int kb = 0; kb < 2; ++kb) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint64_t ad = sdesc_sw128(smem_u32(sA1) + kb * kBlk + j * 32);
+            for (int j = 0; j < 4; ++j) {
+              const uint64_t ad = sdesc_sw128(smem_u32(sA1) + kb * kBlk + j * 32);
 #pragma unroll
-            for (int nh = 0; nh < D / 192; ++nh) {
-              const uint64_t bd = sdesc_sw128(smem_u32(sB) + kb * D * 128 + nh * 192 * 128 + j * 32);
-              umma_bf16(tmem + nh * 192, ad, bd, idesc, (c | kb | j) ? 1u : 0u);
+              for (int nh = 0; nh < D / 192; ++nh) {
+                const uint64_t bd = sdesc_sw128(smem_u32(sB) + kb * D * 128 + nh * 192 * 128 + j * 32);
+                umma_bf16(tmem + nh * 192, ad, bd, idesc, (c | kb | j) ? 1u : 0u);
+              }
             }
           }
         }
+        umma_commit(bar_mma);
       }
-      umma_commit(bar_mma);
+      __syncwarp();
     }
   }
   ok = mbar_wait(bar_mma, (nch - 1) & 1, status) && ok;
@@ -286,7 +216,7 @@ __global__ void __launch_bounds__(256) k_embed(DevWeights w, ModelDims md, const
     for (int kb = 0; kb < C::KB; ++kb)
       bulk_s2g(act_a + ((size_t)blockIdx.x * C::KB + kb) * kBlkElems, sOut + kb * kBlk, kBlk);
     bulk_commit();
-    bulk_wait_all();
+    bulk_wait_read();
   }
   __syncwarp();
   if (warp == 0) tmem_dealloc(tmem, C::TMEM_EMB);
@@ -305,43 +235,55 @@ __global__ void __launch_bounds__(kThreads) k_adaln(DevWeights w, ModelDims md, 
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::KB * kBlk;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + C::KB * NT * 128);  // [0] weights, [1] mma, [2] act
+  float* sbias = reinterpret_cast<float*>(sB + C::KB * NT * 128);  // NT floats
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sbias + NT);      // [0] weights, [1] mma, [2] act
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x, nt = blockIdx.y;
+  LEWM_STAMP(1, 0);
   if (tid == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
     mbar_init(&bars[2], 1);
     fence_mbar_init();
-    mbar_arrive_expect_tx(&bars[0], C::KB * NT * 128);
+    mbar_arrive_expect_tx(&bars[0], C::KB * NT * 128 + NT * 4);
     for (int kb = 0; kb < C::KB; ++kb)
       bulk_g2s(sB + kb * NT * 128, w.wada + ((size_t)nt * C::KB + kb) * NT * 64, NT * 128, &bars[0]);
+    bulk_g2s(sbias, w.ada_b + nt * NT, NT * 4, &bars[0]);
   }
   __syncwarp();
   if (warp == 0) {
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
+  LEWM_STAMP(1, 1);
   griddep_wait();
+  LEWM_STAMP(1, 2);
   griddep_launch();
   if (tid == 0) {
     mbar_arrive_expect_tx(&bars[2], C::KB * kBlk);
     for (int kb = 0; kb < C::KB; ++kb)
       bulk_g2s(sA + kb * kBlk, act_a + ((size_t)tile * C::KB + kb) * kBlkElems, kBlk, &bars[2]);
   }
+  LEWM_STAMP(1, 5);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (tid == 0) {
-    if (mbar_wait(&bars[0], 0, status) && mbar_wait(&bars[2], 0, status)) {
-      tc_fence_after();
-      umma_tile(tmem, smem_u32(sA), kBlk, smem_u32(sB), NT * 128, 0, C::KB, idesc_bf16(128, NT), false);
+  if (warp == 0) {
+    const bool got = __all_sync(0xffffffffu, mbar_wait(&bars[0], 0, status) && mbar_wait(&bars[2], 0, status));
+    if (lane == 0) {
+      if (got) {
+        tc_fence_after();
+        umma_tile(tmem, smem_u32(sA), kBlk, smem_u32(sB), NT * 128, 0, C::KB, idesc_bf16(128, NT), false);
+      }
+      LEWM_STAMP(1, 3);
+      umma_commit(&bars[1]);
     }
-    umma_commit(&bars[1]);
+    __syncwarp();
   }
   const bool ok = mbar_wait(&bars[1], 0, status);
+  LEWM_STAMP(1, 4);
   __syncwarp();
   tc_fence_after();
   const int quad = warp & 3, slice = warp >> 2;
@@ -351,22 +293,118 @@ __global__ void __launch_bounds__(kThreads) k_adaln(DevWeights w, ModelDims md, 
   float v[CW];
   tmem_ld_cols<CW>(taddr, v);
   if (ok && row < rows) {
-    const int n0 = nt * NT + slice * CW;
-    uint4* dst = reinterpret_cast<uint4*>(mod + (size_t)row * ncols + n0);
+    const float* bs = sbias + slice * CW;
+    uint4* dst = reinterpret_cast<uint4*>(mod + (size_t)row * ncols + nt * NT + slice * CW);
 #pragma unroll
     for (int i = 0; i < CW / 8; ++i) {
       uint32_t pk[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k)
-        pk[k] = pack_bf16x2(v[8 * i + 2 * k] + w.ada_b[n0 + 8 * i + 2 * k],
-                            v[8 * i + 2 * k + 1] + w.ada_b[n0 + 8 * i + 2 * k + 1]);
+        pk[k] = pack_bf16x2(v[8 * i + 2 * k] + bs[8 * i + 2 * k], v[8 * i + 2 * k + 1] + bs[8 * i + 2 * k + 1]);
       dst[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     }
   }
+  LEWM_STAMP(1, 6);
   tc_fence_before();
   __syncthreads();
   __syncwarp();
   if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ---------------------------------------------------------------- warp-level row LayerNorm
+// One warp, one row of D columns (lane l holds columns 64*i + 2l, 64*i + 2l + 1).
+// Writes bf16(LN_affine(LN(x) * (1 + scale) + shift)) into row r of a global
+// pre-swizzled [D/64][128 x 64] A tile.
+template <int D>
+__device__ __forceinline__ void warp_ln_mod_ln_store(const float2 (&x)[D / 64], const __nv_bfloat16* __restrict__ shift,
+                                                     const __nv_bfloat16* __restrict__ scale,
+                                                     const float* __restrict__ g, const float* __restrict__ bb,
+                                                     __nv_bfloat16* __restrict__ a_tile, int r, int lane) {
+  constexpr int NP = D / 64;
+  float2 sh[NP], sc[NP], gg[NP], b2[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int c = 64 * i + 2 * lane;
+    sh[i] = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(shift + c));
+    sc[i] = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(scale + c));
+    gg[i] = *reinterpret_cast<const float2*>(g + c);
+    b2[i] = *reinterpret_cast<const float2*>(bb + c);
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NP; ++i) s += x[i].x + x[i].y;
+  const float mean = warp_sum(s) * (1.0f / D);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const float dx = x[i].x - mean, dy = x[i].y - mean;
+    q += dx * dx + dy * dy;
+  }
+  const float rstd = rsqrtf(warp_sum(q) * (1.0f / D) + 1e-6f);
+  float2 y[NP];
+  float s2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    y[i].x = (x[i].x - mean) * rstd * (1.0f + sc[i].x) + sh[i].x;
+    y[i].y = (x[i].y - mean) * rstd * (1.0f + sc[i].y) + sh[i].y;
+    s2 += y[i].x + y[i].y;
+  }
+  const float mean2 = warp_sum(s2) * (1.0f / D);
+  float q2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const float dx = y[i].x - mean2, dy = y[i].y - mean2;
+    q2 += dx * dx + dy * dy;
+  }
+  const float rstd2 = rsqrtf(warp_sum(q2) * (1.0f / D) + 1e-5f);
+  uint8_t* tile_bytes = reinterpret_cast<uint8_t*>(a_tile);
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const float zx = (y[i].x - mean2) * rstd2 * gg[i].x + b2[i].x;
+    const float zy = (y[i].y - mean2) * rstd2 * gg[i].y + b2[i].y;
+    *reinterpret_cast<uint32_t*>(tile_bytes + i * kBlk + sw128_off(r, 2 * lane)) = pack_bf16x2(zx, zy);
+  }
+}
+
+// Layer-0 residual x0 = history row + position embedding of window position p, and
+// its A operand (LN1, modulate with layer-0 shift/scale of the token, attn.norm).
+template <int D>
+__device__ __forceinline__ void prep_layer0_row(const DevWeights& w, const ModelDims& md, const float* __restrict__ src,
+                                                int p, int tok, float* __restrict__ xdst,
+                                                __nv_bfloat16* __restrict__ a_tile, int r, int lane,
+                                                const __nv_bfloat16* __restrict__ mod) {
+  constexpr int NP = D / 64;
+  float2 x[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int c = 64 * i + 2 * lane;
+    const float2 a = *reinterpret_cast<const float2*>(src + c);
+    const float2 pe = *reinterpret_cast<const float2*>(w.pos + p * D + c);
+    x[i] = make_float2(a.x + pe.x, a.y + pe.y);
+    *reinterpret_cast<float2*>(xdst + c) = x[i];
+  }
+  const __nv_bfloat16* mrow = mod + (size_t)tok * (md.L * 6 * D);
+  warp_ln_mod_ln_store<D>(x, mrow, mrow + D, w.attn_ln_w, w.attn_ln_b, a_tile, r, lane);
+}
+
+// ---------------------------------------------------------------- first-call layer-0 inputs
+// Warp per window row of the first predictor call (its history rows are all
+// observation embeddings).
+template <int D>
+__global__ void __launch_bounds__(128) k_prep0(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b) {
+  griddep_wait();
+  griddep_launch();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 4 + warp;
+  if (row >= g.n_cand * g.w) return;
+  const int cand = row / g.w, p = row - cand * g.w;
+  const int j = g.start + p;  // < H for the first call
+  const int e = b.emb_per_cand ? cand : cand / g.S;
+  const int tile = cand / g.cpt;
+  const int r = (cand - tile * g.cpt) * g.w + p;
+  prep_layer0_row<D>(w, md, b.emb + ((size_t)e * g.H + j) * D, p, cand * g.T + j,
+                     b.x + ((size_t)tile * 128 + r) * D, b.a_attn + (size_t)tile * (D / 64) * kBlkElems, r, lane,
+                     b.mod);
 }
 
 // ---------------------------------------------------------------- QKV + attention
@@ -389,12 +427,13 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   uint64_t* full = reinterpret_cast<uint64_t*>(sO + kBlk);
   uint64_t* empty = full + ST;
   uint64_t* bar_mma = empty + ST;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
+  uint64_t* bar_a = bar_mma + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  LEWM_STAMP(2, 0);
   const int tile = blockIdx.x, head = blockIdx.y;
   const __nv_bfloat16* wq = w.qkv + (size_t)((layer * md.heads + head) * KB) * (192 * 64);
-  const int ncols = md.L * 6 * D;
 
   if (tid == 0) {
     for (int s = 0; s < ST; ++s) {
@@ -402,6 +441,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
       mbar_init(&empty[s], 1);
     }
     mbar_init(bar_mma, 1);
+    mbar_init(bar_a, 1);
     fence_mbar_init();
     for (int s = 0; s < ST; ++s) {
       mbar_arrive_expect_tx(&full[s], B_BLK);
@@ -413,60 +453,52 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
+  LEWM_STAMP(2, 1);
   griddep_wait();
+  LEWM_STAMP(2, 2);
   griddep_launch();
-  // Prologue: window rows -> LN1 -> modulate(shift_msa, scale_msa) -> attn.norm -> bf16 A.
-  const int NPRED = g.T - g.H + 1;
-  for (int r = tid / C::TPR; r < 128; r += C::RPP) {
-    const int q = tid % C::TPR;
-    const RowMap m = map_row(g, tile, r);
-    const __nv_bfloat16* mrow = b.mod + (size_t)(m.valid ? m.tok : 0) * ncols + layer * 6 * D;
-    float* xdst = b.x + ((size_t)tile * 128 + r) * D;
-    if (layer == 0) {
-      const float* src = b.emb;
-      if (m.valid) {
-        const int j = g.start + m.pos;
-        if (j < g.H) {
-          const int e = b.emb_per_cand ? m.cand : (m.cand / g.S);
-          src = b.emb + ((size_t)e * g.H + j) * D;
-        } else {
-          src = b.pred + ((size_t)m.cand * NPRED + (j - g.H)) * D;
-        }
-      }
-      ln_mod_ln_part<D>(m.valid, src, w.pos + m.pos * D, mrow, mrow + D, w.attn_ln_w + layer * D,
-                        w.attn_ln_b + layer * D, sA, r, q, head == 0 ? xdst : nullptr);
-    } else {
-      ln_mod_ln_part<D>(m.valid, xdst, nullptr, mrow, mrow + D, w.attn_ln_w + layer * D, w.attn_ln_b + layer * D,
-                        sA, r, q, nullptr);
-    }
+  if (tid == 0) {  // the A operand was written, normalized and swizzled, by the producer of x
+    mbar_arrive_expect_tx(bar_a, KB * kBlk);
+    for (int kb = 0; kb < KB; ++kb)
+      bulk_g2s(sA + kb * kBlk, b.a_attn + ((size_t)tile * KB + kb) * kBlkElems, kBlk, bar_a);
   }
-  fence_async_smem();
+  LEWM_STAMP(2, 5);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (tid == 0) {
+  if (warp == 0) {  // whole warp waits, lane 0 issues
     const uint32_t idesc = idesc_bf16(128, 192);
-    for (int kb = 0; kb < KB; ++kb) {
+    const bool go = __all_sync(0xffffffffu, mbar_wait(bar_a, 0, status));
+    for (int kb = 0; go && kb < KB; ++kb) {
       const int s = kb % ST;
-      if (!mbar_wait(&full[s], (kb / ST) & 1, status)) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (kb / ST) & 1, status))) break;
       tc_fence_after();
+      if (lane == 0) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint64_t ad = sdesc_sw128(smem_u32(sA) + kb * kBlk + j * 32);
-        const uint64_t bd = sdesc_sw128(smem_u32(sB) + s * B_BLK + j * 32);
-        umma_bf16(tmem, ad, bd, idesc, (kb | j) ? 1u : 0u);
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t ad = sdesc_sw128(smem_u32(sA) + kb * kBlk + j * 32);
+          const uint64_t bd = sdesc_sw128(smem_u32(sB) + s * B_BLK + j * 32);
+          umma_bf16(tmem, ad, bd, idesc, (kb | j) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
       }
-      umma_commit(&empty[s]);
+      __syncwarp();
       if (kb + ST < KB) {
-        if (!mbar_wait(&empty[s], (kb / ST) & 1, status)) break;
-        mbar_arrive_expect_tx(&full[s], B_BLK);
-        bulk_g2s(sB + s * B_BLK, wq + (size_t)(kb + ST) * 192 * 64, B_BLK, &full[s]);
+        if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], (kb / ST) & 1, status))) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[s], B_BLK);
+          bulk_g2s(sB + s * B_BLK, wq + (size_t)(kb + ST) * 192 * 64, B_BLK, &full[s]);
+        }
+        __syncwarp();
       }
     }
-    umma_commit(bar_mma);
+    LEWM_STAMP(2, 3);
+    if (lane == 0) umma_commit(bar_mma);
+    __syncwarp();
   }
   const bool ok = mbar_wait(bar_mma, 0, status);
+  LEWM_STAMP(2, 4);
   __syncwarp();
   tc_fence_after();
   {  // q|k|v of this head -> scratch rows (fp32); warp slice s owns columns [48s, 48s+48)
@@ -480,6 +512,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     for (int i = 0; i < 48; ++i) srow[i] = v[i];
   }
   __syncthreads();
+  LEWM_STAMP(2, 7);
   {  // causal softmax(q k^T / 8) v within the candidate's window; 4 threads per row, 16 dims each
     const int r = tid >> 2, part = tid & 3;
     const RowMap m = map_row(g, tile, r);
@@ -532,22 +565,39 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
+  LEWM_STAMP(2, 8);
   if (tid == 0) {
     bulk_s2g(b.attn + ((size_t)tile * md.heads + head) * kBlkElems, sO, kBlk);
     bulk_commit();
-    bulk_wait_all();
+    bulk_wait_read();
   }
+  LEWM_STAMP(2, 6);
   __syncwarp();
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
-// ---------------------------------------------------------------- streamed-K GEMM with residual epilogue
-// x[:, n-tile] += gate * (A . B^T + bias), A streamed from pre-swizzled global tiles.
-// Used for the attention out-projection (gate_msa) and FC2 (gate_mlp).
+// ---------------------------------------------------------------- streamed-K GEMM, residual + LayerNorm epilogue
+// What the epilogue of an out-projection / FC2 launch does with its N tile.
+struct ResidEpi {
+  const float* bias;      // [D] of this GEMM
+  int gate_chunk;         // mod chunk of the gate (2: gate_msa, 5: gate_mlp) of `layer`
+  __nv_bfloat16* a_out;   // A operand of the next GEMM, or null (last FC2)
+  int ln_layer;           // layer whose shift/scale modulate the next LayerNorm
+  int ln_chunk;           // mod chunk of that shift (scale = chunk + 1)
+  const float* ln_g;      // [D] affine of the second LayerNorm
+  const float* ln_b;
+};
+
+// x[:, n-tile] += gate * (A . B^T + bias); A streamed from pre-swizzled global tiles.
+// Launched as 4-CTA clusters, one per row tile (cluster rank = N tile). When a_out is
+// set, the epilogue also produces the next GEMM's A operand for its columns:
+// LN(x) (eps 1e-6) -> * (1 + scale) + shift -> LN (eps 1e-5) * g + b -> bf16. The
+// per-row moments of the 4 N tiles are combined through distributed shared memory
+// (Chan et al. parallel variance merge), one cluster barrier per LayerNorm.
+// Warp 0 issues MMAs, warp 1 refills the operand ring.
 template <int D>
 __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __restrict__ gA, int nkb,
-                                                         const __nv_bfloat16* __restrict__ gB,
-                                                         const float* __restrict__ bias, int gate_chunk, CallGeom g,
+                                                         const __nv_bfloat16* __restrict__ gB, ResidEpi ep, CallGeom g,
                                                          RolloutBufs b, ModelDims md, int layer, uint32_t* status) {
   using C = Cfg<D>;
   constexpr int NT = C::NT_OUT;
@@ -558,15 +608,20 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
   uint8_t* sB = smem + ST * kBlk;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + ST * B_BLK);
+  float* svec = reinterpret_cast<float*>(sB + ST * B_BLK);  // [bias NT][ln_g NT][ln_b NT]
+  float* red = svec + 3 * NT;                               // [2][4 slices][128]
+  float2* xch = reinterpret_cast<float2*>(red + 2 * 4 * 128);  // [2 rounds][4 ranks][128]
+  uint64_t* full = reinterpret_cast<uint64_t*>(xch + 2 * 4 * 128);
   uint64_t* empty = full + ST;
   uint64_t* bar_mma = empty + ST;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int tile = blockIdx.x, nt = blockIdx.y;
+  LEWM_STAMP(3, 0);
+  const int tile = blockIdx.x, nt = blockIdx.y;  // nt == cluster rank
   const __nv_bfloat16* tA = gA + (size_t)tile * nkb * kBlkElems;
   const __nv_bfloat16* tB = gB + (size_t)nt * nkb * NT * 64;
   const int pre = ST < nkb ? ST : nkb;
+  const bool do_ln = ep.a_out != nullptr;
   if (tid == 0) {
     for (int s = 0; s < ST; ++s) {
       mbar_init(&full[s], 1);
@@ -574,7 +629,15 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
     }
     mbar_init(bar_mma, 1);
     fence_mbar_init();
-    for (int s = 0; s < pre; ++s) {  // weights first: they do not depend on the previous kernel
+    // Weights and vectors first: they do not depend on the previous kernel.
+    mbar_arrive_expect_tx(&full[0], kBlk + B_BLK + (do_ln ? 3 : 1) * NT * 4);
+    bulk_g2s(svec, ep.bias + nt * NT, NT * 4, &full[0]);
+    if (do_ln) {
+      bulk_g2s(svec + NT, ep.ln_g + nt * NT, NT * 4, &full[0]);
+      bulk_g2s(svec + 2 * NT, ep.ln_b + nt * NT, NT * 4, &full[0]);
+    }
+    bulk_g2s(sB, tB, B_BLK, &full[0]);
+    for (int s = 1; s < pre; ++s) {
       mbar_arrive_expect_tx(&full[s], kBlk + B_BLK);
       bulk_g2s(sB + s * B_BLK, tB + (size_t)s * NT * 64, B_BLK, &full[s]);
     }
@@ -584,67 +647,173 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
     tmem_alloc(tmem_slot, C::TMEM_OUT);
     tmem_relinquish();
   }
+  cluster_sync();  // every CTA of the cluster is running before any distributed shared-memory access
+  LEWM_STAMP(3, 1);
   griddep_wait();
+  LEWM_STAMP(3, 2);
   griddep_launch();
   if (tid == 0)
     for (int s = 0; s < pre; ++s) bulk_g2s(sA + s * kBlk, tA + (size_t)s * kBlkElems, kBlk, &full[s]);
+  LEWM_STAMP(3, 5);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (tid == 0) {
+  if (warp == 0) {  // MMA issuer
     const uint32_t idesc = idesc_bf16(128, NT);
     for (int kb = 0; kb < nkb; ++kb) {
       const int s = kb % ST;
-      if (!mbar_wait(&full[s], (kb / ST) & 1, status)) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (kb / ST) & 1, status))) break;
       tc_fence_after();
+      if (lane == 0) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint64_t ad = sdesc_sw128(smem_u32(sA) + s * kBlk + j * 32);
-        const uint64_t bd = sdesc_sw128(smem_u32(sB) + s * B_BLK + j * 32);
-        umma_bf16(tmem, ad, bd, idesc, (kb | j) ? 1u : 0u);
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t ad = sdesc_sw128(smem_u32(sA) + s * kBlk + j * 32);
+          const uint64_t bd = sdesc_sw128(smem_u32(sB) + s * B_BLK + j * 32);
+          umma_bf16(tmem, ad, bd, idesc, (kb | j) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
       }
-      umma_commit(&empty[s]);
-      // Refill the stage the previous MMA group used once that group is done.
-      if (kb >= 1 && kb - 1 + ST < nkb) {
-        const int ps = (kb - 1) % ST;
-        if (!mbar_wait(&empty[ps], ((kb - 1) / ST) & 1, status)) break;
-        const int nk = kb - 1 + ST;
-        mbar_arrive_expect_tx(&full[ps], kBlk + B_BLK);
-        bulk_g2s(sA + ps * kBlk, tA + (size_t)nk * kBlkElems, kBlk, &full[ps]);
-        bulk_g2s(sB + ps * B_BLK, tB + (size_t)nk * NT * 64, B_BLK, &full[ps]);
-      }
+      __syncwarp();
     }
-    umma_commit(bar_mma);
+    LEWM_STAMP(3, 3);
+    if (lane == 0) umma_commit(bar_mma);
+    __syncwarp();
+  } else if (warp == 1) {  // producer: refill a stage once the MMAs that read it are done
+    for (int kb = pre; kb < nkb; ++kb) {
+      const int s = kb % ST;
+      if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ((kb / ST) - 1) & 1, status))) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[s], kBlk + B_BLK);
+        bulk_g2s(sA + s * kBlk, tA + (size_t)kb * kBlkElems, kBlk, &full[s]);
+        bulk_g2s(sB + s * B_BLK, tB + (size_t)kb * NT * 64, B_BLK, &full[s]);
+      }
+      __syncwarp();
+    }
   }
-  const bool ok = mbar_wait(bar_mma, 0, status);
-  __syncwarp();
-  tc_fence_after();
   const int quad = warp & 3, slice = warp >> 2;
   const int r = quad * 32 + lane;
   const RowMap m = map_row(g, tile, r);
+  // Residual, gate and the next LayerNorm's shift/scale do not depend on the MMA:
+  // load them while it runs.
+  const int c0 = nt * NT + slice * CW;
+  float* xrow = b.x + ((size_t)tile * 128 + r) * D + c0;
+  float4 xv[CW / 4];
+  uint2 gt[CW / 4], sh[CW / 4], sc[CW / 4];
+  if (m.valid) {
+    const __nv_bfloat16* mrow = b.mod + (size_t)m.tok * (md.L * 6 * D);
+    const __nv_bfloat16* gate = mrow + layer * 6 * D + ep.gate_chunk * D + c0;
+    const __nv_bfloat16* shp = mrow + ep.ln_layer * 6 * D + ep.ln_chunk * D + c0;
+#pragma unroll
+    for (int i = 0; i < CW / 4; ++i) {
+      xv[i] = *reinterpret_cast<const float4*>(xrow + 4 * i);
+      gt[i] = *reinterpret_cast<const uint2*>(gate + 4 * i);
+      if (do_ln) {
+        sh[i] = *reinterpret_cast<const uint2*>(shp + 4 * i);
+        sc[i] = *reinterpret_cast<const uint2*>(shp + D + 4 * i);
+      } else {
+        sh[i] = sc[i] = make_uint2(0u, 0u);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < CW / 4; ++i) {
+      xv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      gt[i] = sh[i] = sc[i] = make_uint2(0u, 0u);
+    }
+  }
+  const bool ok = mbar_wait(bar_mma, 0, status);
+  LEWM_STAMP(3, 4);
+  __syncwarp();
+  tc_fence_after();
   const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * CW;
   float v[CW];
   tmem_ld_cols<CW>(taddr, v);
-  if (ok && m.valid) {
-    const int ncols = md.L * 6 * D;
-    const int c0 = nt * NT + slice * CW;
-    float* xrow = b.x + ((size_t)tile * 128 + r) * D + c0;
-    const __nv_bfloat16* gate = b.mod + (size_t)m.tok * ncols + layer * 6 * D + gate_chunk * D + c0;
-    const float* bs = bias + c0;
+  LEWM_STAMP(3, 7);
+  {
+    const float* bs = svec + slice * CW;
 #pragma unroll
-    for (int i = 0; i < CW; i += 4) {
-      const uint2 gt = *reinterpret_cast<const uint2*>(gate + i);
-      const float2 g01 = unpack_bf16x2(gt.x), g23 = unpack_bf16x2(gt.y);
-      const float4 b4 = *reinterpret_cast<const float4*>(bs + i);
-      float4 xv = *reinterpret_cast<float4*>(xrow + i);
-      xv.x += g01.x * (v[i] + b4.x);
-      xv.y += g01.y * (v[i + 1] + b4.y);
-      xv.z += g23.x * (v[i + 2] + b4.z);
-      xv.w += g23.y * (v[i + 3] + b4.w);
-      *reinterpret_cast<float4*>(xrow + i) = xv;
+    for (int i = 0; i < CW / 4; ++i) {
+      const float2 g01 = unpack_bf16x2(gt[i].x), g23 = unpack_bf16x2(gt[i].y);
+      const float4 b4 = *reinterpret_cast<const float4*>(bs + 4 * i);
+      xv[i].x += g01.x * (v[4 * i] + b4.x);
+      xv[i].y += g01.y * (v[4 * i + 1] + b4.y);
+      xv[i].z += g23.x * (v[4 * i + 2] + b4.z);
+      xv[i].w += g23.y * (v[4 * i + 3] + b4.w);
+      if (ok && m.valid) *reinterpret_cast<float4*>(xrow + 4 * i) = xv[i];
     }
   }
+  if (do_ln) {
+    float z[CW];
+#pragma unroll
+    for (int i = 0; i < CW / 4; ++i) {
+      z[4 * i] = xv[i].x;
+      z[4 * i + 1] = xv[i].y;
+      z[4 * i + 2] = xv[i].z;
+      z[4 * i + 3] = xv[i].w;
+    }
+    const int rank = nt;
+#pragma unroll
+    for (int round = 0; round < 2; ++round) {
+      // (mean, M2) of this CTA's NT columns of row r: two passes through shared memory.
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < CW; ++i) s += z[i];
+      red[slice * 128 + r] = s;
+      __syncthreads();
+      const float mean_c = (red[r] + red[128 + r] + red[256 + r] + red[384 + r]) * (1.0f / NT);
+      float q = 0.f;
+#pragma unroll
+      for (int i = 0; i < CW; ++i) q += (z[i] - mean_c) * (z[i] - mean_c);
+      red[512 + slice * 128 + r] = q;
+      __syncthreads();
+      if (slice == 0) {
+        const float m2_c = red[512 + r] + red[640 + r] + red[768 + r] + red[896 + r];
+        const float2 mv = make_float2(mean_c, m2_c);
+#pragma unroll
+        for (int peer = 0; peer < 4; ++peer) st_dsmem_f2(xch + (round * 4 + rank) * 128 + r, peer, mv);
+      }
+      cluster_sync();
+      float mean = 0.f;
+      float2 part[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        part[k] = xch[(round * 4 + k) * 128 + r];
+        mean += part[k].x;
+      }
+      mean *= 0.25f;
+      float m2 = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) m2 += part[k].y + NT * (part[k].x - mean) * (part[k].x - mean);
+      const float rstd = rsqrtf(m2 * (1.0f / D) + (round == 0 ? 1e-6f : 1e-5f));
+      if (round == 0) {
+#pragma unroll
+        for (int i = 0; i < CW / 4; ++i) {
+          const float2 s01 = unpack_bf16x2(sh[i].x), s23 = unpack_bf16x2(sh[i].y);
+          const float2 k01 = unpack_bf16x2(sc[i].x), k23 = unpack_bf16x2(sc[i].y);
+          z[4 * i] = (z[4 * i] - mean) * rstd * (1.0f + k01.x) + s01.x;
+          z[4 * i + 1] = (z[4 * i + 1] - mean) * rstd * (1.0f + k01.y) + s01.y;
+          z[4 * i + 2] = (z[4 * i + 2] - mean) * rstd * (1.0f + k23.x) + s23.x;
+          z[4 * i + 3] = (z[4 * i + 3] - mean) * rstd * (1.0f + k23.y) + s23.y;
+        }
+      } else if (ok && m.valid) {
+        const float* gg = svec + NT + slice * CW;
+        const float* bb = svec + 2 * NT + slice * CW;
+        uint8_t* at = reinterpret_cast<uint8_t*>(ep.a_out + (size_t)tile * (D / 64) * kBlkElems);
+#pragma unroll
+        for (int i = 0; i < CW / 4; ++i) {
+          const int c = c0 + 4 * i;
+          uint2 pk;
+          pk.x = pack_bf16x2((z[4 * i] - mean) * rstd * gg[4 * i] + bb[4 * i],
+                             (z[4 * i + 1] - mean) * rstd * gg[4 * i + 1] + bb[4 * i + 1]);
+          pk.y = pack_bf16x2((z[4 * i + 2] - mean) * rstd * gg[4 * i + 2] + bb[4 * i + 2],
+                             (z[4 * i + 3] - mean) * rstd * gg[4 * i + 3] + bb[4 * i + 3]);
+          *reinterpret_cast<uint2*>(at + (c >> 6) * kBlk + sw128_off(r, c & 63)) = pk;
+        }
+      }
+    }
+  }
+  LEWM_STAMP(3, 6);
   tc_fence_before();
   __syncthreads();
   __syncwarp();
@@ -663,23 +832,29 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   uint8_t* sA = smem;
   uint8_t* sB = smem + KB * kBlk;
   uint8_t* sO = smem;  // 2 blocks, aliases sA after the MMA
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + ST * kBlk);
+  float* svec = reinterpret_cast<float*>(sB + ST * kBlk);  // [b1 128]
+  uint64_t* full = reinterpret_cast<uint64_t*>(svec + 128);
   uint64_t* empty = full + ST;
   uint64_t* bar_mma = empty + ST;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
+  uint64_t* bar_a = bar_mma + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  LEWM_STAMP(4, 0);
   const int tile = blockIdx.x, nt = blockIdx.y;
   const int nmlp = md.mlp / 128;
   const __nv_bfloat16* wb = w.w1 + (size_t)((layer * nmlp + nt) * KB) * kBlkElems;
-  const int ncols = md.L * 6 * D;
   if (tid == 0) {
     for (int s = 0; s < ST; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     mbar_init(bar_mma, 1);
+    mbar_init(bar_a, 1);
     fence_mbar_init();
-    for (int s = 0; s < ST; ++s) {
+    mbar_arrive_expect_tx(&full[0], kBlk + 128 * 4);
+    bulk_g2s(svec, w.b1 + layer * md.mlp + nt * 128, 128 * 4, &full[0]);
+    bulk_g2s(sB, wb, kBlk, &full[0]);
+    for (int s = 1; s < ST; ++s) {
       mbar_arrive_expect_tx(&full[s], kBlk);
       bulk_g2s(sB + s * kBlk, wb + (size_t)s * kBlkElems, kBlk, &full[s]);
     }
@@ -689,42 +864,52 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
     tmem_alloc(tmem_slot, 128);
     tmem_relinquish();
   }
+  LEWM_STAMP(4, 1);
   griddep_wait();
+  LEWM_STAMP(4, 2);
   griddep_launch();
-  for (int r = tid / C::TPR; r < 128; r += C::RPP) {
-    const int q = tid % C::TPR;
-    const RowMap m = map_row(g, tile, r);
-    const __nv_bfloat16* mrow = b.mod + (size_t)(m.valid ? m.tok : 0) * ncols + layer * 6 * D;
-    ln_mod_ln_part<D>(m.valid, b.x + ((size_t)tile * 128 + r) * D, nullptr, mrow + 3 * D, mrow + 4 * D,
-                      w.ffn_ln_w + layer * D, w.ffn_ln_b + layer * D, sA, r, q, nullptr);
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar_a, KB * kBlk);
+    for (int kb = 0; kb < KB; ++kb)
+      bulk_g2s(sA + kb * kBlk, b.a_ffn + ((size_t)tile * KB + kb) * kBlkElems, kBlk, bar_a);
   }
-  fence_async_smem();
+  LEWM_STAMP(4, 5);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (tid == 0) {
+  if (warp == 0) {  // whole warp waits, lane 0 issues
     const uint32_t idesc = idesc_bf16(128, 128);
-    for (int kb = 0; kb < KB; ++kb) {
+    const bool go = __all_sync(0xffffffffu, mbar_wait(bar_a, 0, status));
+    for (int kb = 0; go && kb < KB; ++kb) {
       const int s = kb % ST;
-      if (!mbar_wait(&full[s], (kb / ST) & 1, status)) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (kb / ST) & 1, status))) break;
       tc_fence_after();
+      if (lane == 0) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint64_t ad = sdesc_sw128(smem_u32(sA) + kb * kBlk + j * 32);
-        const uint64_t bd = sdesc_sw128(smem_u32(sB) + s * kBlk + j * 32);
-        umma_bf16(tmem, ad, bd, idesc, (kb | j) ? 1u : 0u);
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t ad = sdesc_sw128(smem_u32(sA) + kb * kBlk + j * 32);
+          const uint64_t bd = sdesc_sw128(smem_u32(sB) + s * kBlk + j * 32);
+          umma_bf16(tmem, ad, bd, idesc, (kb | j) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
       }
-      umma_commit(&empty[s]);
+      __syncwarp();
       if (kb + ST < KB) {
-        if (!mbar_wait(&empty[s], (kb / ST) & 1, status)) break;
-        mbar_arrive_expect_tx(&full[s], kBlk);
-        bulk_g2s(sB + s * kBlk, wb + (size_t)(kb + ST) * kBlkElems, kBlk, &full[s]);
+        if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], (kb / ST) & 1, status))) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[s], kBlk);
+          bulk_g2s(sB + s * kBlk, wb + (size_t)(kb + ST) * kBlkElems, kBlk, &full[s]);
+        }
+        __syncwarp();
       }
     }
-    umma_commit(bar_mma);
+    LEWM_STAMP(4, 3);
+    if (lane == 0) umma_commit(bar_mma);
+    __syncwarp();
   }
   const bool ok = mbar_wait(bar_mma, 0, status);
+  LEWM_STAMP(4, 4);
   __syncwarp();
   tc_fence_after();
   {  // warp slice s owns hidden columns [32s, 32s+32) of this 128-wide chunk
@@ -733,7 +918,7 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
     const RowMap m = map_row(g, tile, r);
     const bool valid = ok && m.valid;
     const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * 32;
-    const float* bs = w.b1 + layer * md.mlp + nt * 128 + slice * 32;
+    const float* bs = svec + slice * 32;
     float v[32];
     tmem_ld_cols<32>(taddr, v);
 #pragma unroll
@@ -752,20 +937,25 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
+  LEWM_STAMP(4, 7);
   if (tid == 0) {
     const int nkm = md.mlp / 64;
     bulk_s2g(b.h + ((size_t)tile * nkm + 2 * nt) * kBlkElems, sO, kBlk);
     bulk_s2g(b.h + ((size_t)tile * nkm + 2 * nt + 1) * kBlkElems, sO + kBlk, kBlk);
     bulk_commit();
-    bulk_wait_all();
+    bulk_wait_read();
   }
+  LEWM_STAMP(4, 6);
   __syncwarp();
   if (warp == 0) tmem_dealloc(tmem, 128);
 }
 
 // ---------------------------------------------------------------- final LayerNorm + history / cost
+// Warp per candidate: final LayerNorm of the window's last token. The last call scores
+// it against the goal; earlier calls append it to the history and prepare the next
+// call's layer-0 residual and A operand for every row of the candidate's next window.
 template <int D>
-__global__ void __launch_bounds__(128) k_final(DevWeights w, CallGeom g, RolloutBufs b) {
+__global__ void __launch_bounds__(128) k_final(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b) {
   griddep_wait();
   griddep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -775,11 +965,17 @@ __global__ void __launch_bounds__(128) k_final(DevWeights w, CallGeom g, Rollout
   const int r = (cand - tile * g.cpt) * g.w + (g.w - 1);
   const float* xr = b.x + ((size_t)tile * 128 + r) * D;
   constexpr int NP = D / 64;
-  float2 v[NP];
+  const int e = b.goal_per_cand ? cand : cand / g.S;
+  const float* gr = b.goal + (size_t)e * D;
+  float2 v[NP], gv[NP], fw[NP], fb[NP];
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
-    v[i] = *reinterpret_cast<const float2*>(xr + 64 * i + 2 * lane);
+    const int c = 64 * i + 2 * lane;
+    v[i] = *reinterpret_cast<const float2*>(xr + c);
+    gv[i] = g.last ? *reinterpret_cast<const float2*>(gr + c) : make_float2(0.f, 0.f);
+    fw[i] = *reinterpret_cast<const float2*>(w.fin_w + c);
+    fb[i] = *reinterpret_cast<const float2*>(w.fin_b + c);
     s += v[i].x + v[i].y;
   }
   const float mean = warp_sum(s) * (1.0f / D);
@@ -792,27 +988,33 @@ __global__ void __launch_bounds__(128) k_final(DevWeights w, CallGeom g, Rollout
   const float rstd = rsqrtf(warp_sum(q) * (1.0f / D) + 1e-5f);
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
-    const int c = 64 * i + 2 * lane;
-    v[i].x = (v[i].x - mean) * rstd * w.fin_w[c] + w.fin_b[c];
-    v[i].y = (v[i].y - mean) * rstd * w.fin_w[c + 1] + w.fin_b[c + 1];
+    v[i].x = (v[i].x - mean) * rstd * fw[i].x + fb[i].x;
+    v[i].y = (v[i].y - mean) * rstd * fw[i].y + fb[i].y;
   }
   if (g.last) {
-    const int e = b.goal_per_cand ? cand : cand / g.S;
-    const float* gr = b.goal + (size_t)e * D;
     float acc = 0.f;
 #pragma unroll
     for (int i = 0; i < NP; ++i) {
-      const int c = 64 * i + 2 * lane;
-      const float dx = v[i].x - gr[c], dy = v[i].y - gr[c + 1];
+      const float dx = v[i].x - gv[i].x, dy = v[i].y - gv[i].y;
       acc += dx * dx + dy * dy;
     }
     acc = warp_sum(acc);
     if (lane == 0) b.costs[cand] = acc;
-  } else {
-    const int NPred = g.T - g.H + 1;
-    float* dst = b.pred + ((size_t)cand * NPred + g.call) * D;
+    return;
+  }
+  const int NPred = g.T - g.H + 1;
+  float* pcand = b.pred + (size_t)cand * NPred * D;
 #pragma unroll
-    for (int i = 0; i < NP; ++i) *reinterpret_cast<float2*>(dst + 64 * i + 2 * lane) = v[i];
+  for (int i = 0; i < NP; ++i) *reinterpret_cast<float2*>(pcand + g.call * D + 64 * i + 2 * lane) = v[i];
+  // Next call's window rows of this candidate (each lane reads back only its own columns).
+  const int ntile = cand / g.next_cpt;
+  const int e2 = b.emb_per_cand ? cand : cand / g.S;
+  for (int p = 0; p < g.next_w; ++p) {
+    const int j = g.next_start + p;
+    const float* src = (j < g.H) ? b.emb + ((size_t)e2 * g.H + j) * D : pcand + (size_t)(j - g.H) * D;
+    const int nr = (cand - ntile * g.next_cpt) * g.next_w + p;
+    prep_layer0_row<D>(w, md, src, p, cand * g.T + j, b.xn + ((size_t)ntile * 128 + nr) * D,
+                       b.a_attn + (size_t)ntile * (D / 64) * kBlkElems, nr, lane, b.mod);
   }
 }
 
@@ -820,7 +1022,7 @@ __global__ void __launch_bounds__(128) k_final(DevWeights w, CallGeom g, Rollout
 template <int D>
 constexpr int smem_embed() { return 1024 + 2 * kBlk + 2 * D * 128 + 128 * 16 * 4 + 64; }
 template <int D>
-constexpr int smem_adaln() { return 1024 + Cfg<D>::KB * (kBlk + Cfg<D>::NT_ADA * 128) + 64; }
+constexpr int smem_adaln() { return 1024 + Cfg<D>::KB * (kBlk + Cfg<D>::NT_ADA * 128) + Cfg<D>::NT_ADA * 4 + 64; }
 template <int D>
 constexpr int smem_qkv() {
   constexpr int R1 = Cfg<D>::KB * kBlk + Cfg<D>::QKV_ST * 192 * 128;
@@ -829,9 +1031,12 @@ constexpr int smem_qkv() {
   return 1024 + R1S + kBlk + 128;
 }
 template <int D>
-constexpr int smem_resid() { return 1024 + Cfg<D>::RES_ST * (kBlk + Cfg<D>::NT_OUT * 128) + 128; }
+constexpr int smem_resid() {
+  return 1024 + Cfg<D>::RES_ST * (kBlk + Cfg<D>::NT_OUT * 128) + 3 * Cfg<D>::NT_OUT * 4 + 2 * 4 * 128 * 4 +
+         2 * 4 * 128 * 8 + 128;
+}
 template <int D>
-constexpr int smem_fc1() { return 1024 + Cfg<D>::KB * kBlk + Cfg<D>::QKV_ST * kBlk + 128; }
+constexpr int smem_fc1() { return 1024 + Cfg<D>::KB * kBlk + Cfg<D>::QKV_ST * kBlk + 128 * 4 + 128; }
 
 static_assert(smem_qkv<192>() <= 232448 && smem_qkv<384>() <= 232448, "qkv smem");
 static_assert(smem_embed<384>() <= 232448 && smem_adaln<384>() <= 232448, "embed/adaln smem");
@@ -878,6 +1083,15 @@ cudaError_t adaln_impl(const ModelDims& md, const DevWeights& w, int rows, const
 }
 
 template <int D>
+cudaError_t prep0_impl(const ModelDims& md, const DevWeights& w, const CallGeom& g, const RolloutBufs& b,
+                       cudaStream_t st, Prof* prof) {
+  if (prof) prof->begin(st);
+  const cudaError_t e = launch_k(k_prep0<D>, dim3((g.n_cand * g.w + 3) / 4), dim3(128), 0, st, w, md, g, b);
+  if (prof) prof->end(KC_PREP0, 0.0, st);
+  return e;
+}
+
+template <int D>
 cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& g, const RolloutBufs& b,
                       uint32_t* status, cudaStream_t st, Prof* prof) {
   cudaError_t e = set_smem_attrs<D>();
@@ -893,25 +1107,32 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
     LEWM_TRY(launch_k(k_qkv_attn<D>, dim3(g.n_tiles, md.heads), dim3(kThreads), smem_qkv<D>(), st, w, md, g, b, l,
                       status));
     if (prof) prof->end(KC_QKV_ATTN, 2.0 * rows * D * 3 * md.inner + 4.0 * rows * g.w * md.inner, st);
+    // out-projection: residual with gate_msa, then LN2 / modulate(mlp) / FFN LayerNorm -> FC1 operand
+    const ResidEpi ep_out{w.out_b + l * D, 2, b.a_ffn, l, 3, w.ffn_ln_w + l * D, w.ffn_ln_b + l * D};
     if (prof) prof->begin(st);
-    LEWM_TRY(launch_k(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads), smem_resid<D>(), st,
-                      (const __nv_bfloat16*)b.attn, nkb_inner,
-                      (const __nv_bfloat16*)(w.wout + (size_t)l * 4 * nkb_inner * Cfg<D>::NT_OUT * 64),
-                      (const float*)(w.out_b + l * D), 2, g, b, md, l, status));
+    LEWM_TRY(launch_kc(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads), smem_resid<D>(), st, dim3(1, 4, 1),
+                       (const __nv_bfloat16*)b.attn, nkb_inner,
+                       (const __nv_bfloat16*)(w.wout + (size_t)l * 4 * nkb_inner * Cfg<D>::NT_OUT * 64), ep_out, g,
+                       b, md, l, status));
     if (prof) prof->end(KC_OUT, 2.0 * rows * md.inner * D, st);
     if (prof) prof->begin(st);
     LEWM_TRY(launch_k(k_fc1<D>, dim3(g.n_tiles, md.mlp / 128), dim3(kThreads), smem_fc1<D>(), st, w, md, g, b, l,
                       status));
     if (prof) prof->end(KC_FC1, 2.0 * rows * D * md.mlp, st);
+    // FC2: residual with gate_mlp, then (not after the last layer) LN1 / modulate(msa of l+1) / attn.norm
+    const bool more = l + 1 < md.L;
+    const int nl = more ? l + 1 : l;
+    const ResidEpi ep_fc2{w.b2 + l * D, 5, more ? b.a_attn : nullptr, nl, 0, w.attn_ln_w + nl * D,
+                          w.attn_ln_b + nl * D};
     if (prof) prof->begin(st);
-    LEWM_TRY(launch_k(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads), smem_resid<D>(), st,
-                      (const __nv_bfloat16*)b.h, nkb_mlp,
-                      (const __nv_bfloat16*)(w.w2 + (size_t)l * 4 * nkb_mlp * Cfg<D>::NT_OUT * 64),
-                      (const float*)(w.b2 + l * D), 5, g, b, md, l, status));
+    LEWM_TRY(launch_kc(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads), smem_resid<D>(), st, dim3(1, 4, 1),
+                       (const __nv_bfloat16*)b.h, nkb_mlp,
+                       (const __nv_bfloat16*)(w.w2 + (size_t)l * 4 * nkb_mlp * Cfg<D>::NT_OUT * 64), ep_fc2, g, b,
+                       md, l, status));
     if (prof) prof->end(KC_FC2, 2.0 * rows * md.mlp * D, st);
   }
   if (prof) prof->begin(st);
-  LEWM_TRY(launch_k(k_final<D>, dim3((g.n_cand + 3) / 4), dim3(128), 0, st, w, g, b));
+  LEWM_TRY(launch_k(k_final<D>, dim3((g.n_cand + 3) / 4), dim3(128), 0, st, w, md, g, b));
   if (prof) prof->end(KC_FINAL, 0.0, st);
 #undef LEWM_TRY
   return cudaSuccess;
@@ -930,6 +1151,13 @@ cudaError_t launch_adaln(const ModelDims& md, const DevWeights& w, int rows, con
                          __nv_bfloat16* mod, uint32_t* status, cudaStream_t st, Prof* prof) {
   if (md.D == 192) return adaln_impl<192>(md, w, rows, act_a, mod, status, st, prof);
   if (md.D == 384) return adaln_impl<384>(md, w, rows, act_a, mod, status, st, prof);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_prep0(const ModelDims& md, const DevWeights& w, const CallGeom& g, const RolloutBufs& b,
+                         cudaStream_t st, Prof* prof) {
+  if (md.D == 192) return prep0_impl<192>(md, w, g, b, st, prof);
+  if (md.D == 384) return prep0_impl<384>(md, w, g, b, st, prof);
   return cudaErrorInvalidValue;
 }
 
