@@ -168,6 +168,25 @@ LEWM_API lewm_status lewm_sample_candidates(lewm_ctx* ctx, const lewm_plan_desc*
                                    const float* mean, const float* std, const float* injected_noise,
                                    const float* action_low, const float* action_high, float* out, void* stream);
 
+/* Candidate sampling that allocates nothing. No counterpart in the reference:
+ * it serves callers that cannot allocate device memory where they sample (all
+ * memory handed to their own pool, or no context at hand). Same candidates as
+ * lewm_sample_candidates for the same plan fields, S, iter, mean and std, on
+ * device `device` for an action dimension `action_dim`; no context.
+ *   Scratch: one fixed array of 65,792 bytes per device inside the library
+ *   (a coloring matrix of at most 128 x 128 plus the Philox key); a colored
+ *   time length (horizon*action_block for raw time, else horizon) above 128,
+ *   or horizon*action_dim above 128, returns LEWM_UNSUPPORTED_SHAPE.
+ *   The first call on a device looks up that array's address (and may load
+ *   the module there): make it before any stream capture.
+ *   Calls that overlap on the GPU (unordered streams) share the scratch and
+ *   race; order them on one stream or with events.
+ *   Errors: text from lewm_last_error(NULL). */
+LEWM_API lewm_status lewm_sample_candidates_noalloc(const lewm_plan_desc* plan, int32_t action_dim, int32_t S,
+                                           int32_t iter, const float* mean, const float* std,
+                                           const float* injected_noise, const float* action_low,
+                                           const float* action_high, float* out, int32_t device, void* stream);
+
 /* The real n x n matrix W with irfft(rfft(x) * scale, n) == W x, scale_f = (f/n)^(-beta/2),
  * scale_0 = scale_1: the temporal coloring of _colored_noise_along_time
  * (lewm/solvers/icem.py:173-182) as a matrix. HOST memory, row-major. */

@@ -78,6 +78,9 @@ SIGNATURES = {
                                   C.c_void_p, C.c_void_p]),
     "lewm_sample_candidates": (C.c_int, [C.c_void_p, C.POINTER(PlanDescC), C.c_int32, C.c_int32, C.c_void_p,
                                          C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "lewm_sample_candidates_noalloc": (C.c_int, [C.POINTER(PlanDescC), C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
+                                                 C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                 C.c_int32, C.c_void_p]),
     "lewm_coloring_matrix": (C.c_int, [C.c_int32, C.c_double, C.c_void_p]),
     "lewm_sync_status": (C.c_int, [C.c_void_p, C.c_void_p]),
     "lewm_profile_plan": (C.c_int, [C.c_void_p, C.POINTER(PlanDescC), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,

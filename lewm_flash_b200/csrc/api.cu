@@ -644,6 +644,10 @@ lewm_status copy_plan_outputs(lewm_ctx* c, const lewm_plan_desc* p, float* actio
 
 }  // namespace
 
+namespace lewm {
+void set_noctx_error(const char* msg) { g_create_error = msg; }
+}  // namespace lewm
+
 extern "C" {
 
 size_t lewm_weight_count(const lewm_model_desc* desc) {

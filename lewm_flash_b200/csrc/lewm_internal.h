@@ -223,6 +223,9 @@ struct SampleParams {
 cudaError_t launch_sample(const SampleParams& p, cudaStream_t st);
 cudaError_t launch_set_rng(uint32_t* rng, uint32_t seed, uint32_t plan, cudaStream_t st);
 
+// Sets the thread's error text that lewm_last_error(NULL) returns (context-free calls).
+void set_noctx_error(const char* msg);
+
 struct RefitParams {
   int B, S, T, A, k, R;
   const float* costs;   // (B,S)
