@@ -83,6 +83,7 @@ struct lewm_ctx {
   cudaStream_t cap_stream = nullptr;  // plan graphs are captured and replayed here
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;
   std::map<std::vector<double>, cudaGraphExec_t> graphs;  // one executable graph per plan shape
+  int tile_target = 1;        // row tiles a small predictor call is spread over (SMs / heads)
   std::vector<float> W_host;  // last uploaded coloring matrix
   int W_n = -1;
   float W_beta = -1.f;
@@ -298,9 +299,23 @@ lewm_status pack_weights(lewm_ctx* c, const float* wts, size_t n) {
   return LEWM_OK;
 }
 
-int window_tiles(int n_cand, int w) {
-  const int cpt = 128 / w;
-  return (n_cand + cpt - 1) / cpt;
+// Candidates per row tile and tile count of a predictor call with window w. A tile
+// holds whole candidates (at most 128 rows). A call with few candidates is spread
+// over up to `target` tiles (one wave of the one-head-per-CTA QKV kernel), so each
+// CTA of the streamed-operand GEMMs moves fewer rows; a large call uses full tiles.
+void tile_geom(int n_cand, int w, int target, int* cpt, int* n_tiles) {
+  const int cmax = 128 / w;
+  int nt = (n_cand + cmax - 1) / cmax;
+  nt = std::max(nt, std::min(n_cand, target));
+  const int c = (n_cand + nt - 1) / nt;
+  *cpt = c;
+  *n_tiles = (n_cand + c - 1) / c;
+}
+
+int window_tiles(int n_cand, int w, int target) {
+  int cpt, nt;
+  tile_geom(n_cand, w, target, &cpt, &nt);
+  return nt;
 }
 
 void clear_graphs(lewm_ctx* c) {
@@ -403,7 +418,10 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
     const int end = H + k;
     const int start = std::max(0, end - HS);
     const int w = end - start;
-    return CallGeom{NC, S, T, H, w, start, 128 / w, window_tiles(NC, w), k, k == n_calls - 1, 1, 0, 128};
+    int cpt, nt;
+    tile_geom(NC, w, c->tile_target, &cpt, &nt);
+    const int rows8 = std::min(128, (cpt * w + 7) & ~7);
+    return CallGeom{NC, S, T, H, w, start, cpt, nt, rows8, k, k == n_calls - 1, 1, 0, 128};
   };
   for (int k = 0; k < n_calls; ++k) {
     CallGeom g = geom(k);
@@ -422,11 +440,11 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
   return LEWM_OK;
 }
 
-int max_call_tiles(int NC, int T, int H, int HS) {
+int max_call_tiles(int NC, int T, int H, int HS, int target) {
   int t = 1;
   for (int k = 0; k < T - H + 1; ++k) {
     const int end = H + k;
-    t = std::max(t, window_tiles(NC, end - std::max(0, end - HS)));
+    t = std::max(t, window_tiles(NC, end - std::max(0, end - HS), target));
   }
   return t;
 }
@@ -677,6 +695,7 @@ lewm_status lewm_create(lewm_ctx** out, const lewm_model_desc* desc, const float
   c->device = device;
   c->desc = *desc;
   c->md = md;
+  c->tile_target = std::max(1, prop.multiProcessorCount / md.heads);
   s = pack_weights(c, weights, n_floats);
   if (s == LEWM_OK && cudaMalloc(&c->d_status, 4) != cudaSuccess) s = fail(c, LEWM_CUDA_ERROR, "status alloc");
   if (s == LEWM_OK && cudaMemset(c->d_status, 0, 4) != cudaSuccess) s = fail(c, LEWM_CUDA_ERROR, "status memset");
@@ -724,7 +743,7 @@ lewm_status lewm_model_cost(lewm_ctx* c, const float* emb, int32_t emb_per_sampl
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int NC = B * S;
   WsReq need{(size_t)NC, (size_t)T, (size_t)c->md.A, (size_t)c->md.D, (size_t)c->md.L,
-             (size_t)max_call_tiles(NC, T, H, history_size), (size_t)c->md.heads, (size_t)c->md.mlp,
+             (size_t)max_call_tiles(NC, T, H, history_size, c->tile_target), (size_t)c->md.heads, (size_t)c->md.mlp,
              (size_t)(T - H + 1), 1, 0, 0};
   lewm_status s = ensure_ws(c, need);
   if (s != LEWM_OK) return s;
@@ -772,7 +791,7 @@ lewm_status lewm_plan(lewm_ctx* c, const lewm_plan_desc* p, const float* emb, co
   const int R = std::min(p->elite_retention, p->topk);
   const int NC = B * Smax;
   WsReq need{(size_t)NC, (size_t)T, (size_t)A, (size_t)m.D, (size_t)m.L,
-             (size_t)max_call_tiles(NC, T, H, p->history_size), (size_t)m.heads, (size_t)m.mlp,
+             (size_t)max_call_tiles(NC, T, H, p->history_size, c->tile_target), (size_t)m.heads, (size_t)m.mlp,
              (size_t)(T - H + 1), (size_t)B, (size_t)R, (size_t)std::max(ncol, 1)};
   s = ensure_ws(c, need);
   if (s != LEWM_OK) return s;

@@ -74,6 +74,7 @@ struct CallGeom {
   int start;    // history index of window position 0
   int cpt;      // candidates per tile
   int n_tiles;  // window tiles
+  int rows8;    // rows of a tile that operand copies move: cpt * w rounded up to 8 (<= 128)
   int call;     // prediction slot written by this call
   int last;     // 1: final call, write costs
   // Window of the next call (k_final prepares its layer-0 inputs); unused when last.

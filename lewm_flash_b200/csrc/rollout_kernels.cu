@@ -427,8 +427,8 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   uint64_t* full = reinterpret_cast<uint64_t*>(sO + kBlk);
   uint64_t* empty = full + ST;
   uint64_t* bar_mma = empty + ST;
-  uint64_t* bar_a = bar_mma + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + 1);
+  uint64_t* bar_a = bar_mma + 1;  // [KB]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + KB);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   LEWM_STAMP(2, 0);
@@ -441,7 +441,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
       mbar_init(&empty[s], 1);
     }
     mbar_init(bar_mma, 1);
-    mbar_init(bar_a, 1);
+    for (int kb = 0; kb < KB; ++kb) mbar_init(&bar_a[kb], 1);
     fence_mbar_init();
     for (int s = 0; s < ST; ++s) {
       mbar_arrive_expect_tx(&full[s], B_BLK);
@@ -458,9 +458,10 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   LEWM_STAMP(2, 2);
   griddep_launch();
   if (tid == 0) {  // the A operand was written, normalized and swizzled, by the producer of x
-    mbar_arrive_expect_tx(bar_a, KB * kBlk);
-    for (int kb = 0; kb < KB; ++kb)
-      bulk_g2s(sA + kb * kBlk, b.a_attn + ((size_t)tile * KB + kb) * kBlkElems, kBlk, bar_a);
+    for (int kb = 0; kb < KB; ++kb) {
+      mbar_arrive_expect_tx(&bar_a[kb], g.rows8 * 128);
+      bulk_g2s(sA + kb * kBlk, b.a_attn + ((size_t)tile * KB + kb) * kBlkElems, g.rows8 * 128, &bar_a[kb]);
+    }
   }
   LEWM_STAMP(2, 5);
   tc_fence_before();
@@ -469,10 +470,11 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   const uint32_t tmem = *tmem_slot;
   if (warp == 0) {  // whole warp waits, lane 0 issues
     const uint32_t idesc = idesc_bf16(128, 192);
-    const bool go = __all_sync(0xffffffffu, mbar_wait(bar_a, 0, status));
-    for (int kb = 0; go && kb < KB; ++kb) {
+    for (int kb = 0; kb < KB; ++kb) {
       const int s = kb % ST;
-      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (kb / ST) & 1, status))) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar_a[kb], 0, status) &&
+                                       mbar_wait(&full[s], (kb / ST) & 1, status)))
+        break;
       tc_fence_after();
       if (lane == 0) {
 #pragma unroll
@@ -519,23 +521,33 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     const bool valid = ok && m.valid;
     const int base = r - m.pos;
     const float* qr = scr + r * kScratchStride + part * 16;
+    float q[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) q[t] = qr[t];
+    // Window loops are unrolled to kMaxWindow so the scores stay in registers.
     float sc[kMaxWindow];
     float mx = -INFINITY;
-    for (int j = 0; j < g.w; ++j) {
-      float d = 0.f;
-      if (valid && j <= m.pos) {
-        const float* kr = scr + (base + j) * kScratchStride + 64 + part * 16;
 #pragma unroll
-        for (int t = 0; t < 16; ++t) d += qr[t] * kr[t];
+    for (int j = 0; j < kMaxWindow; ++j) {
+      if (j < g.w) {  // uniform across the four threads of a row (same window)
+        float d = 0.f;
+        if (valid && j <= m.pos) {
+          const float* kr = scr + (base + j) * kScratchStride + 64 + part * 16;
+#pragma unroll
+          for (int t = 0; t < 16; ++t) d += q[t] * kr[t];
+        }
+        d += __shfl_xor_sync(0xffffffffu, d, 1);
+        d += __shfl_xor_sync(0xffffffffu, d, 2);
+        sc[j] = d * 0.125f;
+        if (j <= m.pos) mx = fmaxf(mx, sc[j]);
+      } else {
+        sc[j] = 0.f;
       }
-      d += __shfl_xor_sync(0xffffffffu, d, 1);
-      d += __shfl_xor_sync(0xffffffffu, d, 2);
-      sc[j] = d * 0.125f;
-      if (j <= m.pos) mx = fmaxf(mx, sc[j]);
     }
     float den = 0.f;
-    for (int j = 0; j < g.w; ++j) {
-      sc[j] = (j <= m.pos) ? expf(sc[j] - mx) : 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxWindow; ++j) {
+      sc[j] = (j < g.w && j <= m.pos) ? expf(sc[j] - mx) : 0.f;
       den += sc[j];
     }
     const float inv = 1.0f / den;
@@ -543,10 +555,13 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
 #pragma unroll
     for (int t = 0; t < 16; ++t) o[t] = 0.f;
     if (valid) {
-      for (int j = 0; j <= m.pos; ++j) {
-        const float* vr = scr + (base + j) * kScratchStride + 128 + part * 16;
 #pragma unroll
-        for (int t = 0; t < 16; ++t) o[t] += sc[j] * vr[t];
+      for (int j = 0; j < kMaxWindow; ++j) {
+        if (j <= m.pos) {
+          const float* vr = scr + (base + j) * kScratchStride + 128 + part * 16;
+#pragma unroll
+          for (int t = 0; t < 16; ++t) o[t] += sc[j] * vr[t];
+        }
       }
     }
     uint4 lo, hi;
@@ -567,7 +582,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   __syncthreads();
   LEWM_STAMP(2, 8);
   if (tid == 0) {
-    bulk_s2g(b.attn + ((size_t)tile * md.heads + head) * kBlkElems, sO, kBlk);
+    bulk_s2g(b.attn + ((size_t)tile * md.heads + head) * kBlkElems, sO, g.rows8 * 128);
     bulk_commit();
     bulk_wait_read();
   }
@@ -622,6 +637,7 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
   const __nv_bfloat16* tB = gB + (size_t)nt * nkb * NT * 64;
   const int pre = ST < nkb ? ST : nkb;
   const bool do_ln = ep.a_out != nullptr;
+  const uint32_t ab = (uint32_t)g.rows8 * 128;  // A bytes per K block: the tile's used rows
   if (tid == 0) {
     for (int s = 0; s < ST; ++s) {
       mbar_init(&full[s], 1);
@@ -630,7 +646,7 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
     mbar_init(bar_mma, 1);
     fence_mbar_init();
     // Weights and vectors first: they do not depend on the previous kernel.
-    mbar_arrive_expect_tx(&full[0], kBlk + B_BLK + (do_ln ? 3 : 1) * NT * 4);
+    mbar_arrive_expect_tx(&full[0], ab + B_BLK + (do_ln ? 3 : 1) * NT * 4);
     bulk_g2s(svec, ep.bias + nt * NT, NT * 4, &full[0]);
     if (do_ln) {
       bulk_g2s(svec + NT, ep.ln_g + nt * NT, NT * 4, &full[0]);
@@ -638,7 +654,7 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
     }
     bulk_g2s(sB, tB, B_BLK, &full[0]);
     for (int s = 1; s < pre; ++s) {
-      mbar_arrive_expect_tx(&full[s], kBlk + B_BLK);
+      mbar_arrive_expect_tx(&full[s], ab + B_BLK);
       bulk_g2s(sB + s * B_BLK, tB + (size_t)s * NT * 64, B_BLK, &full[s]);
     }
   }
@@ -653,7 +669,7 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
   LEWM_STAMP(3, 2);
   griddep_launch();
   if (tid == 0)
-    for (int s = 0; s < pre; ++s) bulk_g2s(sA + s * kBlk, tA + (size_t)s * kBlkElems, kBlk, &full[s]);
+    for (int s = 0; s < pre; ++s) bulk_g2s(sA + s * kBlk, tA + (size_t)s * kBlkElems, ab, &full[s]);
   LEWM_STAMP(3, 5);
   tc_fence_before();
   __syncthreads();
@@ -684,8 +700,8 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
       const int s = kb % ST;
       if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ((kb / ST) - 1) & 1, status))) break;
       if (lane == 0) {
-        mbar_arrive_expect_tx(&full[s], kBlk + B_BLK);
-        bulk_g2s(sA + s * kBlk, tA + (size_t)kb * kBlkElems, kBlk, &full[s]);
+        mbar_arrive_expect_tx(&full[s], ab + B_BLK);
+        bulk_g2s(sA + s * kBlk, tA + (size_t)kb * kBlkElems, ab, &full[s]);
         bulk_g2s(sB + s * B_BLK, tB + (size_t)kb * NT * 64, B_BLK, &full[s]);
       }
       __syncwarp();
@@ -821,47 +837,55 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
 }
 
 // ---------------------------------------------------------------- FC1 + GELU
+// One CTA per (row tile, 64 hidden columns): h[:, 64 nt .. 64 nt + 64) = GELU(A . W1^T + b1).
+// The weight operand of an N tile is one half (8 KB, 64 rows) of a pre-swizzled
+// [128 x 64] block; the swizzle repeats every 8 rows, so the half is itself a
+// valid SW128 operand. Each A K-block has its own barrier so the first MMA
+// starts when the first block lands.
 template <int D>
 __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b, int layer,
                                                   uint32_t* status) {
   using C = Cfg<D>;
   constexpr int KB = C::KB;
   constexpr int ST = C::QKV_ST;
+  constexpr int NT = 64;
+  constexpr int B_BLK = NT * 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
   uint8_t* sB = smem + KB * kBlk;
-  uint8_t* sO = smem;  // 2 blocks, aliases sA after the MMA
-  float* svec = reinterpret_cast<float*>(sB + ST * kBlk);  // [b1 128]
-  uint64_t* full = reinterpret_cast<uint64_t*>(svec + 128);
+  uint8_t* sO = smem;  // one block, aliases sA after the MMA
+  float* svec = reinterpret_cast<float*>(sB + ST * B_BLK);  // [b1 NT]
+  uint64_t* full = reinterpret_cast<uint64_t*>(svec + NT);
   uint64_t* empty = full + ST;
   uint64_t* bar_mma = empty + ST;
-  uint64_t* bar_a = bar_mma + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + 1);
+  uint64_t* bar_a = bar_mma + 1;  // [KB]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + KB);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   LEWM_STAMP(4, 0);
   const int tile = blockIdx.x, nt = blockIdx.y;
   const int nmlp = md.mlp / 128;
-  const __nv_bfloat16* wb = w.w1 + (size_t)((layer * nmlp + nt) * KB) * kBlkElems;
+  const __nv_bfloat16* wb =
+      w.w1 + (size_t)((layer * nmlp + (nt >> 1)) * KB) * kBlkElems + (size_t)(nt & 1) * (NT * 64);
   if (tid == 0) {
     for (int s = 0; s < ST; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     mbar_init(bar_mma, 1);
-    mbar_init(bar_a, 1);
+    for (int kb = 0; kb < KB; ++kb) mbar_init(&bar_a[kb], 1);
     fence_mbar_init();
-    mbar_arrive_expect_tx(&full[0], kBlk + 128 * 4);
-    bulk_g2s(svec, w.b1 + layer * md.mlp + nt * 128, 128 * 4, &full[0]);
-    bulk_g2s(sB, wb, kBlk, &full[0]);
+    mbar_arrive_expect_tx(&full[0], B_BLK + NT * 4);
+    bulk_g2s(svec, w.b1 + layer * md.mlp + nt * NT, NT * 4, &full[0]);
+    bulk_g2s(sB, wb, B_BLK, &full[0]);
     for (int s = 1; s < ST; ++s) {
-      mbar_arrive_expect_tx(&full[s], kBlk);
-      bulk_g2s(sB + s * kBlk, wb + (size_t)s * kBlkElems, kBlk, &full[s]);
+      mbar_arrive_expect_tx(&full[s], B_BLK);
+      bulk_g2s(sB + s * B_BLK, wb + (size_t)s * kBlkElems, B_BLK, &full[s]);
     }
   }
   __syncwarp();
   if (warp == 0) {
-    tmem_alloc(tmem_slot, 128);
+    tmem_alloc(tmem_slot, NT);
     tmem_relinquish();
   }
   LEWM_STAMP(4, 1);
@@ -869,9 +893,10 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   LEWM_STAMP(4, 2);
   griddep_launch();
   if (tid == 0) {
-    mbar_arrive_expect_tx(bar_a, KB * kBlk);
-    for (int kb = 0; kb < KB; ++kb)
-      bulk_g2s(sA + kb * kBlk, b.a_ffn + ((size_t)tile * KB + kb) * kBlkElems, kBlk, bar_a);
+    for (int kb = 0; kb < KB; ++kb) {
+      mbar_arrive_expect_tx(&bar_a[kb], g.rows8 * 128);
+      bulk_g2s(sA + kb * kBlk, b.a_ffn + ((size_t)tile * KB + kb) * kBlkElems, g.rows8 * 128, &bar_a[kb]);
+    }
   }
   LEWM_STAMP(4, 5);
   tc_fence_before();
@@ -879,17 +904,18 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (warp == 0) {  // whole warp waits, lane 0 issues
-    const uint32_t idesc = idesc_bf16(128, 128);
-    const bool go = __all_sync(0xffffffffu, mbar_wait(bar_a, 0, status));
-    for (int kb = 0; go && kb < KB; ++kb) {
+    const uint32_t idesc = idesc_bf16(128, NT);
+    for (int kb = 0; kb < KB; ++kb) {
       const int s = kb % ST;
-      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (kb / ST) & 1, status))) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar_a[kb], 0, status) &&
+                                       mbar_wait(&full[s], (kb / ST) & 1, status)))
+        break;
       tc_fence_after();
       if (lane == 0) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const uint64_t ad = sdesc_sw128(smem_u32(sA) + kb * kBlk + j * 32);
-          const uint64_t bd = sdesc_sw128(smem_u32(sB) + s * kBlk + j * 32);
+          const uint64_t bd = sdesc_sw128(smem_u32(sB) + s * B_BLK + j * 32);
           umma_bf16(tmem, ad, bd, idesc, (kb | j) ? 1u : 0u);
         }
         umma_commit(&empty[s]);
@@ -898,8 +924,8 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
       if (kb + ST < KB) {
         if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], (kb / ST) & 1, status))) break;
         if (lane == 0) {
-          mbar_arrive_expect_tx(&full[s], kBlk);
-          bulk_g2s(sB + s * kBlk, wb + (size_t)(kb + ST) * kBlkElems, kBlk, &full[s]);
+          mbar_arrive_expect_tx(&full[s], B_BLK);
+          bulk_g2s(sB + s * B_BLK, wb + (size_t)(kb + ST) * kBlkElems, B_BLK, &full[s]);
         }
         __syncwarp();
       }
@@ -912,17 +938,17 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   LEWM_STAMP(4, 4);
   __syncwarp();
   tc_fence_after();
-  {  // warp slice s owns hidden columns [32s, 32s+32) of this 128-wide chunk
+  {  // warp slice s owns hidden columns [16s, 16s+16) of this 64-wide tile
     const int quad = warp & 3, slice = warp >> 2;
     const int r = quad * 32 + lane;
     const RowMap m = map_row(g, tile, r);
     const bool valid = ok && m.valid;
-    const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * 32;
-    const float* bs = svec + slice * 32;
-    float v[32];
-    tmem_ld_cols<32>(taddr, v);
+    const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * 16;
+    const float* bs = svec + slice * 16;
+    float v[16];
+    tmem_ld_cols<16>(taddr, v);
 #pragma unroll
-    for (int i = 0; i < 32; i += 8) {
+    for (int i = 0; i < 16; i += 8) {
       uint4 pk = make_uint4(0u, 0u, 0u, 0u);
       if (valid) {
         pk.x = pack_bf16x2(gelu_f(v[i] + bs[i]), gelu_f(v[i + 1] + bs[i + 1]));
@@ -930,8 +956,8 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
         pk.z = pack_bf16x2(gelu_f(v[i + 4] + bs[i + 4]), gelu_f(v[i + 5] + bs[i + 5]));
         pk.w = pack_bf16x2(gelu_f(v[i + 6] + bs[i + 6]), gelu_f(v[i + 7] + bs[i + 7]));
       }
-      const int c = slice * 32 + i;
-      *reinterpret_cast<uint4*>(sO + (c >> 6) * kBlk + sw128_off(r, c & 63)) = pk;
+      const int c = slice * 16 + i;
+      *reinterpret_cast<uint4*>(sO + sw128_off(r, c)) = pk;
     }
   }
   fence_async_smem();
@@ -940,14 +966,13 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   LEWM_STAMP(4, 7);
   if (tid == 0) {
     const int nkm = md.mlp / 64;
-    bulk_s2g(b.h + ((size_t)tile * nkm + 2 * nt) * kBlkElems, sO, kBlk);
-    bulk_s2g(b.h + ((size_t)tile * nkm + 2 * nt + 1) * kBlkElems, sO + kBlk, kBlk);
+    bulk_s2g(b.h + ((size_t)tile * nkm + nt) * kBlkElems, sO, g.rows8 * 128);
     bulk_commit();
     bulk_wait_read();
   }
   LEWM_STAMP(4, 6);
   __syncwarp();
-  if (warp == 0) tmem_dealloc(tmem, 128);
+  if (warp == 0) tmem_dealloc(tmem, NT);
 }
 
 // ---------------------------------------------------------------- final LayerNorm + history / cost
@@ -1036,7 +1061,7 @@ constexpr int smem_resid() {
          2 * 4 * 128 * 8 + 128;
 }
 template <int D>
-constexpr int smem_fc1() { return 1024 + Cfg<D>::KB * kBlk + Cfg<D>::QKV_ST * kBlk + 128 * 4 + 128; }
+constexpr int smem_fc1() { return 1024 + Cfg<D>::KB * kBlk + Cfg<D>::QKV_ST * 64 * 128 + 64 * 4 + 8 * (2 * Cfg<D>::QKV_ST + 1 + Cfg<D>::KB) + 16; }
 
 static_assert(smem_qkv<192>() <= 232448 && smem_qkv<384>() <= 232448, "qkv smem");
 static_assert(smem_embed<384>() <= 232448 && smem_adaln<384>() <= 232448, "embed/adaln smem");
@@ -1116,7 +1141,7 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
                        b, md, l, status));
     if (prof) prof->end(KC_OUT, 2.0 * rows * md.inner * D, st);
     if (prof) prof->begin(st);
-    LEWM_TRY(launch_k(k_fc1<D>, dim3(g.n_tiles, md.mlp / 128), dim3(kThreads), smem_fc1<D>(), st, w, md, g, b, l,
+    LEWM_TRY(launch_k(k_fc1<D>, dim3(g.n_tiles, md.mlp / 64), dim3(kThreads), smem_fc1<D>(), st, w, md, g, b, l,
                       status));
     if (prof) prof->end(KC_FC1, 2.0 * rows * D * md.mlp, st);
     // FC2: residual with gate_mlp, then (not after the last layer) LN1 / modulate(msa of l+1) / attn.norm
