@@ -36,6 +36,7 @@ struct Workspace {
   size_t bytes = 0;
   float* cand = nullptr;
   __nv_bfloat16* act_a = nullptr;
+  __nv_bfloat16* eh = nullptr;   // embedder hidden layer, pre-swizzled [row tile][eh/64] blocks
   __nv_bfloat16* mod = nullptr;
   float* x = nullptr;    // two residual buffers: predictor calls alternate between them
   float* x2 = nullptr;
@@ -350,6 +351,7 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   };
   const size_t o_cand = carve(r.n_cand * r.T * m.A * 4);
   const size_t o_act = carve(tiles_e * (m.D / 64) * 128 * 64 * 2);
+  const size_t o_eh = carve(tiles_e * (m.eh / 64) * 128 * 64 * 2);
   const size_t o_mod = carve(rows_e * (size_t)m.L * 6 * m.D * 2);
   const size_t o_x = carve(r.tiles * 128 * (size_t)m.D * 4);
   const size_t o_x2 = carve(r.tiles * 128 * (size_t)m.D * 4);
@@ -378,6 +380,7 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   ws.bytes = off;
   ws.cand = reinterpret_cast<float*>(b + o_cand);
   ws.act_a = reinterpret_cast<__nv_bfloat16*>(b + o_act);
+  ws.eh = reinterpret_cast<__nv_bfloat16*>(b + o_eh);
   ws.mod = reinterpret_cast<__nv_bfloat16*>(b + o_mod);
   ws.x = reinterpret_cast<float*>(b + o_x);
   ws.x2 = reinterpret_cast<float*>(b + o_x2);
@@ -409,7 +412,7 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
   const ModelDims& m = c->md;
   const int NC = B * S;
   const int rows = NC * T;
-  LEWM_CK(c, launch_embed(m, c->w, cand, rows, c->ws.act_a, c->d_status, st, &c->prof));
+  LEWM_CK(c, launch_embed(m, c->w, cand, rows, c->ws.eh, c->ws.act_a, c->d_status, st, &c->prof));
   LEWM_CK(c, launch_adaln(m, c->w, rows, c->ws.act_a, c->ws.mod, c->d_status, st, &c->prof));
   RolloutBufs b{emb, emb_pc, goal, goal_pc, cand, c->ws.act_a, c->ws.mod, c->ws.x, c->ws.x2, c->ws.a_attn,
                 c->ws.a_ffn, c->ws.attn, c->ws.h, c->ws.pred, costs};

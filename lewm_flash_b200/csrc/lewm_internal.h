@@ -191,7 +191,7 @@ cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
 }
 
 // Launchers (rollout_kernels.cu). All asynchronous on `st`; `prof` may be null.
-cudaError_t launch_embed(const ModelDims& md, const DevWeights& w, const float* cand, int rows,
+cudaError_t launch_embed(const ModelDims& md, const DevWeights& w, const float* cand, int rows, __nv_bfloat16* eh,
                          __nv_bfloat16* act_a, uint32_t* status, cudaStream_t st, Prof* prof);
 cudaError_t launch_adaln(const ModelDims& md, const DevWeights& w, int rows, const __nv_bfloat16* act_a,
                          __nv_bfloat16* mod, uint32_t* status, cudaStream_t st, Prof* prof);

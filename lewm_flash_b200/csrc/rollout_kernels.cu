@@ -70,7 +70,7 @@ struct Cfg {
   static constexpr int TMEM_OUT = (NT_OUT <= 64) ? 64 : 128;
   static constexpr int TMEM_EMB = (D <= 256) ? 256 : 512;
   static constexpr int QKV_ST = (KB < 3) ? KB : 3;
-  static constexpr int RES_ST = 6;                // K-ring depth of the streamed-A GEMMs
+  static constexpr int KG = (D == 192) ? 4 : 3;   // K blocks per copy group of the streamed-K GEMMs
 };
 
 struct RowMap {
@@ -87,40 +87,101 @@ __device__ __forceinline__ RowMap map_row(const CallGeom& g, int tile, int r) {
   return m;
 }
 
-// ---------------------------------------------------------------- Embedder + SiLU
-// act_a[row] = bf16(SiLU(Linear2(SiLU(Linear1(Conv1x1(a)))))), rows = candidate*T + t.
-template <int D>
-__global__ void __launch_bounds__(256) k_embed(DevWeights w, ModelDims md, const float* __restrict__ cand, int rows,
-                                               __nv_bfloat16* __restrict__ act_a, uint32_t* status) {
-  using C = Cfg<D>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = align1024(smem_raw);
-  uint8_t* sA1 = smem;                     // 2 blocks [128 x 64]
-  uint8_t* sB = smem + 2 * kBlk;           // 2 blocks [D x 64]
-  uint8_t* sOut = smem;                    // KB blocks, aliases sA1/sB after the last MMA
-  float* actc = reinterpret_cast<float*>(smem + 2 * kBlk + 2 * D * 128);  // [128][16]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(actc + 128 * 16);
-  uint64_t* bar_b = bars;
-  uint64_t* bar_mma = bars + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
+// ---------------------------------------------------------------- streamed-K operand pipeline
+// K blocks travel in groups of G. All copies of a group are issued by the lanes of
+// one warp in a single instruction: 1-D bulk copies issued by separate instructions
+// complete one after another, those issued together overlap. Two groups are in
+// flight (slots [2G]); group g + 2 is issued as soon as the MMAs of group g retire.
+template <int G, int B_BLK>
+struct KStream {
+  uint8_t* sA;                // [2G] slots of kBlk bytes
+  uint8_t* sB;                // [2G] slots of B_BLK bytes
+  uint64_t* full;             // [2] one per slot half
+  uint64_t* empty;            // [2]
+  const __nv_bfloat16* tA;    // A block kb at tA + kb * a_step
+  size_t a_step;
+  const __nv_bfloat16* tB;    // B block kb at tB + kb * b_step
+  size_t b_step;
+  uint32_t ab;                // A bytes per block (the tile's used rows)
+  int nkb;
+  __device__ __forceinline__ int groups() const { return (nkb + G - 1) / G; }
+  __device__ __forceinline__ int blocks(int g) const { return min(G, nkb - g * G); }
+  __device__ __forceinline__ uint32_t bytes(int g) const { return (uint32_t)blocks(g) * (ab + B_BLK); }
+  // Lanes 0 .. 2G-1: block (lane % G) of group lane / G (groups 0 and 1); A or B.
+  __device__ __forceinline__ void issue_first(int lane, bool a_side) const {
+    if (lane >= 2 * G) return;
+    const int g = lane / G, j = lane - g * G;
+    if (g >= groups() || j >= blocks(g)) return;
+    const int kb = g * G + j;
+    if (a_side)
+      bulk_g2s(sA + (size_t)lane * kBlk, tA + (size_t)kb * a_step, ab, &full[g]);
+    else
+      bulk_g2s(sB + (size_t)lane * B_BLK, tB + (size_t)kb * b_step, B_BLK, &full[g]);
+  }
+  // Lanes 0 .. G-1: A blocks of group g, lanes G .. 2G-1: its B blocks.
+  __device__ __forceinline__ void issue_group(int g, int lane) const {
+    if (lane >= 2 * G) return;
+    const int j = lane < G ? lane : lane - G;
+    if (j >= blocks(g)) return;
+    const int kb = g * G + j, slot = (g & 1) * G + j;
+    if (lane < G)
+      bulk_g2s(sA + (size_t)slot * kBlk, tA + (size_t)kb * a_step, ab, &full[g & 1]);
+    else
+      bulk_g2s(sB + (size_t)slot * B_BLK, tB + (size_t)kb * b_step, B_BLK, &full[g & 1]);
+  }
+  // Warp 0: wait for each group, issue its MMAs (lane 0), release its slots.
+  __device__ __forceinline__ bool mma(uint32_t tmem, uint32_t idesc, int lane, uint32_t* status) const {
+    bool ok = true;
+    for (int g = 0; g < groups(); ++g) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[g & 1], (g >> 1) & 1, status))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (lane == 0) {
+        for (int j = 0; j < blocks(g); ++j) {
+          const int slot = (g & 1) * G + j, kb = g * G + j;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint64_t ad = sdesc_sw128(smem_u32(sA) + slot * kBlk + q * 32);
+            const uint64_t bd = sdesc_sw128(smem_u32(sB) + slot * B_BLK + q * 32);
+            umma_bf16(tmem, ad, bd, idesc, (kb | q) ? 1u : 0u);
+          }
+        }
+        umma_commit(&empty[g & 1]);
+      }
+      __syncwarp();
+    }
+    return ok;
+  }
+  // Warp 1: refill a slot half once the MMAs of the group before it retired.
+  __device__ __forceinline__ void produce(int lane, uint32_t* status) const {
+    for (int g = 2; g < groups(); ++g) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&empty[g & 1], ((g >> 1) - 1) & 1, status))) break;
+      if (lane == 0) mbar_arrive_expect_tx(&full[g & 1], bytes(g));
+      __syncwarp();
+      issue_group(g, lane);
+      __syncwarp();
+    }
+  }
+};
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int row0 = blockIdx.x * 128;
-  if (tid == 0) {
-    mbar_init(bar_b, 1);
-    mbar_init(bar_mma, 1);
-    fence_mbar_init();
-    mbar_arrive_expect_tx(bar_b, 2 * D * 128);
-    bulk_g2s(sB, w.we2, D * 128, bar_b);
-    bulk_g2s(sB + D * 128, w.we2 + (size_t)D * 64, D * 128, bar_b);
-  }
-  __syncwarp();
-  if (warp == 0) {
-    tmem_alloc(tmem_slot, C::TMEM_EMB);
-    tmem_relinquish();
-  }
+// ---------------------------------------------------------------- Embedder + SiLU
+// act_a[row] = bf16(SiLU(Linear2(SiLU(Linear1(Conv1x1(a)))))), rows = candidate*T + t,
+// in two kernels so the hidden layer is spread over many SMs:
+//   k_embed_hidden  one CTA per (128-row tile, 64 hidden units): Conv1x1 and Linear1 in
+//                   fp32, SiLU, bf16 into a pre-swizzled [128 x 64] block of `eh`
+//   k_embed_out     Linear2 on tcgen05 (K = embed_hidden streamed, one CTA per N/4
+//                   columns), + bias, SiLU, bf16 into act_a.
+template <int D>
+__global__ void __launch_bounds__(256) k_embed_hidden(DevWeights w, ModelDims md, const float* __restrict__ cand,
+                                                      int rows, __nv_bfloat16* __restrict__ eh) {
+  __shared__ float actc[128 * 16];
+  __shared__ __align__(1024) uint8_t sO[kBlk];
   griddep_wait();
   griddep_launch();
+  const int tid = threadIdx.x;
+  const int row0 = blockIdx.x * 128, hc = blockIdx.y;
   for (int idx = tid; idx < 128 * 16; idx += 256) {
     const int r = idx >> 4, o = idx & 15;
     const int row = row0 + r;
@@ -132,94 +193,113 @@ __global__ void __launch_bounds__(256) k_embed(DevWeights w, ModelDims md, const
     }
     actc[idx] = v;
   }
+  __syncthreads();
+  const int k = tid & 63;
+  const int hk = hc * 64 + k;
+  float wv[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) wv[i] = (i < md.As) ? w.e1_w[hk * md.As + i] : 0.f;
+  const float bias = w.e1_b[hk];
+  for (int r = tid >> 6; r < 128; r += 4) {
+    float acc = bias;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc += wv[i] * actc[r * 16 + i];
+    *reinterpret_cast<__nv_bfloat16*>(sO + sw128_off(r, k)) = __float2bfloat16_rn(silu_f(acc));
+  }
+  fence_async_smem();
+  __syncthreads();
+  if (tid == 0) {
+    bulk_s2g(eh + ((size_t)blockIdx.x * (md.eh / 64) + hc) * kBlkElems, sO, kBlk);
+    bulk_commit();
+    bulk_wait_read();
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) k_embed_out(DevWeights w, ModelDims md, int rows,
+                                                        const __nv_bfloat16* __restrict__ eh,
+                                                        __nv_bfloat16* __restrict__ act_a, uint32_t* status) {
+  using C = Cfg<D>;
+  constexpr int NT = C::NT_OUT;  // D / 4 columns per CTA
+  constexpr int CW = NT / 4;
+  constexpr int G = C::KG;
+  constexpr int B_BLK = NT * 128;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + 2 * G * kBlk;
+  float* sbias = reinterpret_cast<float*>(sB + 2 * G * B_BLK);  // [NT]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sbias + NT);
+  uint64_t* empty = full + 2;
+  uint64_t* bar_mma = empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x, nt = blockIdx.y;
+  const int nkb = md.eh / 64;
+  // we2 K block kb holds all D rows: this CTA's N tile is rows [nt * NT, nt * NT + NT).
+  const KStream<G, B_BLK> ks{sA, sB, full, empty, eh + (size_t)tile * nkb * kBlkElems, (size_t)kBlkElems,
+                             w.we2 + (size_t)nt * NT * 64, (size_t)D * 64, (uint32_t)kBlk, nkb};
+  if (tid == 0) {
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&full[h], 1);
+      mbar_init(&empty[h], 1);
+    }
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&full[0], ks.bytes(0) + NT * 4);
+    if (ks.groups() > 1) mbar_arrive_expect_tx(&full[1], ks.bytes(1));
+  }
+  __syncwarp();
+  if (warp == 0) {  // weights and bias before the wait, one instruction
+    if (lane < 2 * G)
+      ks.issue_first(lane, false);
+    else if (lane == 2 * G)
+      bulk_g2s(sbias, w.e2_b + nt * NT, NT * 4, &full[0]);
+  }
+  __syncwarp();
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, C::TMEM_OUT);
+    tmem_relinquish();
+  }
+  griddep_wait();
+  griddep_launch();
+  if (warp == 0) ks.issue_first(lane, true);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int nch = md.eh / 128;
-  bool ok = true;
-  for (int c = 0; c < nch; ++c) {
-    if (c > 0) {
-      ok = mbar_wait(bar_mma, (c - 1) & 1, status) && ok;
-      if (tid == 0) {
-        mbar_arrive_expect_tx(bar_b, 2 * D * 128);
-        bulk_g2s(sB, w.we2 + (size_t)(c * 2) * D * 64, D * 128, bar_b);
-        bulk_g2s(sB + D * 128, w.we2 + (size_t)(c * 2 + 1) * D * 64, D * 128, bar_b);
-      }
-    }
-    {
-      const int k = tid & 127;
-      const int hk = c * 128 + k;
-      float wv[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) wv[i] = (i < md.As) ? w.e1_w[hk * md.As + i] : 0.f;
-      const float bias = w.e1_b[hk];
-      uint8_t* blk = sA1 + (k >> 6) * kBlk;
-      for (int r = tid >> 7; r < 128; r += 2) {
-        float acc = bias;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc += wv[i] * actc[r * 16 + i];
-        *reinterpret_cast<__nv_bfloat16*>(blk + sw128_off(r, k & 63)) = __float2bfloat16_rn(silu_f(acc));
-      }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (warp == 0) {  // whole warp waits, lane 0 issues (keeps the issuing warp converged)
-      const bool got = __all_sync(0xffffffffu, mbar_wait(bar_b, c & 1, status));
-      if (lane == 0) {
-        if (got) {
-          tc_fence_after();
-          const uint32_t idesc = idesc_bf16(128, 192);
-          for (int kb = 0; kb < 2; ++kb) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint64_t ad = sdesc_sw128(smem_u32(sA1) + kb * kBlk + j * 32);
-#pragma unroll
-              for (int nh = 0; nh < D / 192; ++nh) {
-                const uint64_t bd = sdesc_sw128(smem_u32(sB) + kb * D * 128 + nh * 192 * 128 + j * 32);
-                umma_bf16(tmem + nh * 192, ad, bd, idesc, (c | kb | j) ? 1u : 0u);
-              }
-            }
-          }
-        }
-        umma_commit(bar_mma);
-      }
-      __syncwarp();
-    }
+  if (warp == 0) {  // MMA issuer
+    ks.mma(tmem, idesc_bf16(128, NT), lane, status);
+    if (lane == 0) umma_commit(bar_mma);
+    __syncwarp();
+  } else if (warp == 1) {
+    ks.produce(lane, status);
   }
-  ok = mbar_wait(bar_mma, (nch - 1) & 1, status) && ok;
+  const bool ok = mbar_wait(bar_mma, 0, status);
   __syncwarp();
   tc_fence_after();
-  {
-    const int r = tid & 127;
-    const int half = tid >> 7;
-    const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const bool valid = ok && (row0 + r < rows);
-    for (int c0 = half * (D / 2); c0 < (half + 1) * (D / 2); c0 += 16) {
-      float v[16];
-      tmem_ld16(taddr + c0, v);
+  const int quad = warp & 3, slice = warp >> 2;
+  const int r = quad * 32 + lane;
+  const bool valid = ok && (tile * 128 + r < rows);
+  const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * CW;
+  float v[CW];
+  tmem_ld_cols<CW>(taddr, v);
+  const int c0 = nt * NT + slice * CW;
+  uint8_t* at = reinterpret_cast<uint8_t*>(act_a + (size_t)tile * (D / 64) * kBlkElems);
 #pragma unroll
-      for (int i = 0; i < 16; i += 2) {
-        const int c = c0 + i;
-        const float a0 = valid ? silu_f(v[i] + w.e2_b[c]) : 0.f;
-        const float a1 = valid ? silu_f(v[i + 1] + w.e2_b[c + 1]) : 0.f;
-        *reinterpret_cast<uint32_t*>(sOut + (c >> 6) * kBlk + sw128_off(r, c & 63)) = pack_bf16x2(a0, a1);
-      }
+  for (int i = 0; i < CW; i += 4) {
+    const int c = c0 + i;
+    const float* bs = sbias + slice * CW + i;
+    uint2 pk = make_uint2(0u, 0u);
+    if (valid) {
+      pk.x = pack_bf16x2(silu_f(v[i] + bs[0]), silu_f(v[i + 1] + bs[1]));
+      pk.y = pack_bf16x2(silu_f(v[i + 2] + bs[2]), silu_f(v[i + 3] + bs[3]));
     }
+    *reinterpret_cast<uint2*>(at + (c >> 6) * kBlk + sw128_off(r, c & 63)) = pk;
   }
-  fence_async_smem();
   tc_fence_before();
   __syncthreads();
-  if (tid == 0) {
-    for (int kb = 0; kb < C::KB; ++kb)
-      bulk_s2g(act_a + ((size_t)blockIdx.x * C::KB + kb) * kBlkElems, sOut + kb * kBlk, kBlk);
-    bulk_commit();
-    bulk_wait_read();
-  }
-  __syncwarp();
-  if (warp == 0) tmem_dealloc(tmem, C::TMEM_EMB);
+  if (warp == 0) tmem_dealloc(tmem, C::TMEM_OUT);
 }
 
 // ---------------------------------------------------------------- AdaLN modulation
@@ -247,11 +327,15 @@ __global__ void __launch_bounds__(kThreads) k_adaln(DevWeights w, ModelDims md, 
     mbar_init(&bars[2], 1);
     fence_mbar_init();
     mbar_arrive_expect_tx(&bars[0], C::KB * NT * 128 + NT * 4);
-    for (int kb = 0; kb < C::KB; ++kb)
-      bulk_g2s(sB + kb * NT * 128, w.wada + ((size_t)nt * C::KB + kb) * NT * 64, NT * 128, &bars[0]);
-    bulk_g2s(sbias, w.ada_b + nt * NT, NT * 4, &bars[0]);
   }
   __syncwarp();
+  // One copy per lane: copies issued by one thread complete one after another.
+  if (warp == 0) {
+    if (lane < C::KB)
+      bulk_g2s(sB + lane * NT * 128, w.wada + ((size_t)nt * C::KB + lane) * NT * 64, NT * 128, &bars[0]);
+    else if (lane == C::KB)
+      bulk_g2s(sbias, w.ada_b + nt * NT, NT * 4, &bars[0]);
+  }
   if (warp == 0) {
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
@@ -260,10 +344,10 @@ __global__ void __launch_bounds__(kThreads) k_adaln(DevWeights w, ModelDims md, 
   griddep_wait();
   LEWM_STAMP(1, 2);
   griddep_launch();
-  if (tid == 0) {
-    mbar_arrive_expect_tx(&bars[2], C::KB * kBlk);
-    for (int kb = 0; kb < C::KB; ++kb)
-      bulk_g2s(sA + kb * kBlk, act_a + ((size_t)tile * C::KB + kb) * kBlkElems, kBlk, &bars[2]);
+  if (warp == 0) {
+    if (lane == 0) mbar_arrive_expect_tx(&bars[2], C::KB * kBlk);
+    __syncwarp();
+    if (lane < C::KB) bulk_g2s(sA + lane * kBlk, act_a + ((size_t)tile * C::KB + lane) * kBlkElems, kBlk, &bars[2]);
   }
   LEWM_STAMP(1, 5);
   tc_fence_before();
@@ -443,12 +527,12 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     mbar_init(bar_mma, 1);
     for (int kb = 0; kb < KB; ++kb) mbar_init(&bar_a[kb], 1);
     fence_mbar_init();
-    for (int s = 0; s < ST; ++s) {
-      mbar_arrive_expect_tx(&full[s], B_BLK);
-      bulk_g2s(sB + s * B_BLK, wq + (size_t)s * 192 * 64, B_BLK, &full[s]);
-    }
   }
   __syncwarp();
+  if (warp == 0 && lane < ST) {  // one copy per lane
+    mbar_arrive_expect_tx(&full[lane], B_BLK);
+    bulk_g2s(sB + lane * B_BLK, wq + (size_t)lane * 192 * 64, B_BLK, &full[lane]);
+  }
   if (warp == 0) {
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
@@ -457,11 +541,9 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   griddep_wait();
   LEWM_STAMP(2, 2);
   griddep_launch();
-  if (tid == 0) {  // the A operand was written, normalized and swizzled, by the producer of x
-    for (int kb = 0; kb < KB; ++kb) {
-      mbar_arrive_expect_tx(&bar_a[kb], g.rows8 * 128);
-      bulk_g2s(sA + kb * kBlk, b.a_attn + ((size_t)tile * KB + kb) * kBlkElems, g.rows8 * 128, &bar_a[kb]);
-    }
+  if (warp == 0 && lane < KB) {  // the A operand was written, normalized and swizzled, by the producer of x
+    mbar_arrive_expect_tx(&bar_a[lane], g.rows8 * 128);
+    bulk_g2s(sA + lane * kBlk, b.a_attn + ((size_t)tile * KB + lane) * kBlkElems, g.rows8 * 128, &bar_a[lane]);
   }
   LEWM_STAMP(2, 5);
   tc_fence_before();
@@ -617,46 +699,47 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
   using C = Cfg<D>;
   constexpr int NT = C::NT_OUT;
   constexpr int CW = NT / 4;
-  constexpr int ST = C::RES_ST;
+  constexpr int G = C::KG;
   constexpr int B_BLK = NT * 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
-  uint8_t* sB = smem + ST * kBlk;
-  float* svec = reinterpret_cast<float*>(sB + ST * B_BLK);  // [bias NT][ln_g NT][ln_b NT]
-  float* red = svec + 3 * NT;                               // [2][4 slices][128]
+  uint8_t* sB = smem + 2 * G * kBlk;
+  float* svec = reinterpret_cast<float*>(sB + 2 * G * B_BLK);  // [bias NT][ln_g NT][ln_b NT]
+  float* red = svec + 3 * NT;                                  // [2][4 slices][128]
   float2* xch = reinterpret_cast<float2*>(red + 2 * 4 * 128);  // [2 rounds][4 ranks][128]
   uint64_t* full = reinterpret_cast<uint64_t*>(xch + 2 * 4 * 128);
-  uint64_t* empty = full + ST;
-  uint64_t* bar_mma = empty + ST;
+  uint64_t* empty = full + 2;
+  uint64_t* bar_mma = empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   LEWM_STAMP(3, 0);
   const int tile = blockIdx.x, nt = blockIdx.y;  // nt == cluster rank
-  const __nv_bfloat16* tA = gA + (size_t)tile * nkb * kBlkElems;
-  const __nv_bfloat16* tB = gB + (size_t)nt * nkb * NT * 64;
-  const int pre = ST < nkb ? ST : nkb;
   const bool do_ln = ep.a_out != nullptr;
-  const uint32_t ab = (uint32_t)g.rows8 * 128;  // A bytes per K block: the tile's used rows
+  const KStream<G, B_BLK> ks{sA, sB, full, empty, gA + (size_t)tile * nkb * kBlkElems, (size_t)kBlkElems,
+                             gB + (size_t)nt * nkb * NT * 64, (size_t)NT * 64, (uint32_t)g.rows8 * 128, nkb};
   if (tid == 0) {
-    for (int s = 0; s < ST; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&full[h], 1);
+      mbar_init(&empty[h], 1);
     }
     mbar_init(bar_mma, 1);
     fence_mbar_init();
-    // Weights and vectors first: they do not depend on the previous kernel.
-    mbar_arrive_expect_tx(&full[0], ab + B_BLK + (do_ln ? 3 : 1) * NT * 4);
-    bulk_g2s(svec, ep.bias + nt * NT, NT * 4, &full[0]);
-    if (do_ln) {
+    mbar_arrive_expect_tx(&full[0], ks.bytes(0) + (do_ln ? 3 : 1) * NT * 4);
+    if (ks.groups() > 1) mbar_arrive_expect_tx(&full[1], ks.bytes(1));
+  }
+  __syncwarp();
+  // Weights and vectors first (they do not depend on the previous kernel), in one
+  // instruction of warp 0.
+  if (warp == 0) {
+    if (lane < 2 * G)
+      ks.issue_first(lane, false);
+    else if (lane == 2 * G)
+      bulk_g2s(svec, ep.bias + nt * NT, NT * 4, &full[0]);
+    else if (lane == 2 * G + 1 && do_ln)
       bulk_g2s(svec + NT, ep.ln_g + nt * NT, NT * 4, &full[0]);
+    else if (lane == 2 * G + 2 && do_ln)
       bulk_g2s(svec + 2 * NT, ep.ln_b + nt * NT, NT * 4, &full[0]);
-    }
-    bulk_g2s(sB, tB, B_BLK, &full[0]);
-    for (int s = 1; s < pre; ++s) {
-      mbar_arrive_expect_tx(&full[s], ab + B_BLK);
-      bulk_g2s(sB + s * B_BLK, tB + (size_t)s * NT * 64, B_BLK, &full[s]);
-    }
   }
   __syncwarp();
   if (warp == 0) {
@@ -668,44 +751,19 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
   griddep_wait();
   LEWM_STAMP(3, 2);
   griddep_launch();
-  if (tid == 0)
-    for (int s = 0; s < pre; ++s) bulk_g2s(sA + s * kBlk, tA + (size_t)s * kBlkElems, ab, &full[s]);
+  if (warp == 0) ks.issue_first(lane, true);
   LEWM_STAMP(3, 5);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (warp == 0) {  // MMA issuer
-    const uint32_t idesc = idesc_bf16(128, NT);
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % ST;
-      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (kb / ST) & 1, status))) break;
-      tc_fence_after();
-      if (lane == 0) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint64_t ad = sdesc_sw128(smem_u32(sA) + s * kBlk + j * 32);
-          const uint64_t bd = sdesc_sw128(smem_u32(sB) + s * B_BLK + j * 32);
-          umma_bf16(tmem, ad, bd, idesc, (kb | j) ? 1u : 0u);
-        }
-        umma_commit(&empty[s]);
-      }
-      __syncwarp();
-    }
+    ks.mma(tmem, idesc_bf16(128, NT), lane, status);
     LEWM_STAMP(3, 3);
     if (lane == 0) umma_commit(bar_mma);
     __syncwarp();
-  } else if (warp == 1) {  // producer: refill a stage once the MMAs that read it are done
-    for (int kb = pre; kb < nkb; ++kb) {
-      const int s = kb % ST;
-      if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ((kb / ST) - 1) & 1, status))) break;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&full[s], ab + B_BLK);
-        bulk_g2s(sA + s * kBlk, tA + (size_t)kb * kBlkElems, ab, &full[s]);
-        bulk_g2s(sB + s * B_BLK, tB + (size_t)kb * NT * 64, B_BLK, &full[s]);
-      }
-      __syncwarp();
-    }
+  } else if (warp == 1) {
+    ks.produce(lane, status);
   }
   const int quad = warp & 3, slice = warp >> 2;
   const int r = quad * 32 + lane;
@@ -876,14 +934,15 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
     for (int kb = 0; kb < KB; ++kb) mbar_init(&bar_a[kb], 1);
     fence_mbar_init();
     mbar_arrive_expect_tx(&full[0], B_BLK + NT * 4);
-    bulk_g2s(svec, w.b1 + layer * md.mlp + nt * NT, NT * 4, &full[0]);
-    bulk_g2s(sB, wb, B_BLK, &full[0]);
-    for (int s = 1; s < ST; ++s) {
-      mbar_arrive_expect_tx(&full[s], B_BLK);
-      bulk_g2s(sB + s * B_BLK, wb + (size_t)s * kBlkElems, B_BLK, &full[s]);
-    }
+    for (int s = 1; s < ST; ++s) mbar_arrive_expect_tx(&full[s], B_BLK);
   }
   __syncwarp();
+  if (warp == 0) {  // one copy per lane
+    if (lane < ST)
+      bulk_g2s(sB + lane * B_BLK, wb + (size_t)lane * kBlkElems, B_BLK, &full[lane]);
+    else if (lane == ST)
+      bulk_g2s(svec, w.b1 + layer * md.mlp + nt * NT, NT * 4, &full[0]);
+  }
   if (warp == 0) {
     tmem_alloc(tmem_slot, NT);
     tmem_relinquish();
@@ -892,11 +951,9 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   griddep_wait();
   LEWM_STAMP(4, 2);
   griddep_launch();
-  if (tid == 0) {
-    for (int kb = 0; kb < KB; ++kb) {
-      mbar_arrive_expect_tx(&bar_a[kb], g.rows8 * 128);
-      bulk_g2s(sA + kb * kBlk, b.a_ffn + ((size_t)tile * KB + kb) * kBlkElems, g.rows8 * 128, &bar_a[kb]);
-    }
+  if (warp == 0 && lane < KB) {  // one copy per lane
+    mbar_arrive_expect_tx(&bar_a[lane], g.rows8 * 128);
+    bulk_g2s(sA + lane * kBlk, b.a_ffn + ((size_t)tile * KB + lane) * kBlkElems, g.rows8 * 128, &bar_a[lane]);
   }
   LEWM_STAMP(4, 5);
   tc_fence_before();
@@ -1045,7 +1102,9 @@ __global__ void __launch_bounds__(128) k_final(DevWeights w, ModelDims md, CallG
 
 // ---------------------------------------------------------------- shared-memory sizes
 template <int D>
-constexpr int smem_embed() { return 1024 + 2 * kBlk + 2 * D * 128 + 128 * 16 * 4 + 64; }
+constexpr int smem_embed_out() {
+  return 1024 + 2 * Cfg<D>::KG * (kBlk + Cfg<D>::NT_OUT * 128) + Cfg<D>::NT_OUT * 4 + 8 * 5 + 16;
+}
 template <int D>
 constexpr int smem_adaln() { return 1024 + Cfg<D>::KB * (kBlk + Cfg<D>::NT_ADA * 128) + Cfg<D>::NT_ADA * 4 + 64; }
 template <int D>
@@ -1057,14 +1116,14 @@ constexpr int smem_qkv() {
 }
 template <int D>
 constexpr int smem_resid() {
-  return 1024 + Cfg<D>::RES_ST * (kBlk + Cfg<D>::NT_OUT * 128) + 3 * Cfg<D>::NT_OUT * 4 + 2 * 4 * 128 * 4 +
-         2 * 4 * 128 * 8 + 128;
+  return 1024 + 2 * Cfg<D>::KG * (kBlk + Cfg<D>::NT_OUT * 128) + 3 * Cfg<D>::NT_OUT * 4 + 2 * 4 * 128 * 4 +
+         2 * 4 * 128 * 8 + 8 * 5 + 16;
 }
 template <int D>
 constexpr int smem_fc1() { return 1024 + Cfg<D>::KB * kBlk + Cfg<D>::QKV_ST * 64 * 128 + 64 * 4 + 8 * (2 * Cfg<D>::QKV_ST + 1 + Cfg<D>::KB) + 16; }
 
 static_assert(smem_qkv<192>() <= 232448 && smem_qkv<384>() <= 232448, "qkv smem");
-static_assert(smem_embed<384>() <= 232448 && smem_adaln<384>() <= 232448, "embed/adaln smem");
+static_assert(smem_embed_out<384>() <= 232448 && smem_adaln<384>() <= 232448, "embed/adaln smem");
 static_assert(smem_fc1<384>() <= 232448 && smem_resid<384>() <= 232448, "fc smem");
 
 template <int D>
@@ -1072,7 +1131,8 @@ cudaError_t set_smem_attrs() {
   static bool done = false;  // per process; attributes are per device function
   if (done) return cudaSuccess;
   cudaError_t e;
-  if ((e = cudaFuncSetAttribute(k_embed<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_embed<D>()))) return e;
+  if ((e = cudaFuncSetAttribute(k_embed_out<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_embed_out<D>())))
+    return e;
   if ((e = cudaFuncSetAttribute(k_adaln<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_adaln<D>()))) return e;
   if ((e = cudaFuncSetAttribute(k_qkv_attn<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_qkv<D>()))) return e;
   if ((e = cudaFuncSetAttribute(k_resid_gemm<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_resid<D>())))
@@ -1083,14 +1143,18 @@ cudaError_t set_smem_attrs() {
 }
 
 template <int D>
-cudaError_t embed_impl(const ModelDims& md, const DevWeights& w, const float* cand, int rows, __nv_bfloat16* act_a,
-                       uint32_t* status, cudaStream_t st, Prof* prof) {
+cudaError_t embed_impl(const ModelDims& md, const DevWeights& w, const float* cand, int rows, __nv_bfloat16* eh,
+                       __nv_bfloat16* act_a, uint32_t* status, cudaStream_t st, Prof* prof) {
   cudaError_t e = set_smem_attrs<D>();
   if (e) return e;
   const int tiles = (rows + 127) / 128;
   if (prof) prof->begin(st);
-  e = launch_k(k_embed<D>, dim3(tiles), dim3(256), smem_embed<D>(), st, w, md, cand, rows, act_a, status);
-  if (prof) prof->end(KC_EMBED, 2.0 * rows * ((double)md.A * md.As + (double)md.As * md.eh + (double)md.eh * D), st);
+  e = launch_k(k_embed_hidden<D>, dim3(tiles, md.eh / 64), dim3(256), 0, st, w, md, cand, rows, eh);
+  if (prof) prof->end(KC_EMBED, 2.0 * rows * ((double)md.A * md.As + (double)md.As * md.eh), st);
+  if (e) return e;
+  if (prof) prof->begin(st);
+  e = launch_k(k_embed_out<D>, dim3(tiles, 4), dim3(kThreads), smem_embed_out<D>(), st, w, md, rows, eh, act_a, status);
+  if (prof) prof->end(KC_EMBED, 2.0 * rows * (double)md.eh * D, st);
   return e;
 }
 
@@ -1165,10 +1229,10 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
 
 }  // namespace
 
-cudaError_t launch_embed(const ModelDims& md, const DevWeights& w, const float* cand, int rows,
+cudaError_t launch_embed(const ModelDims& md, const DevWeights& w, const float* cand, int rows, __nv_bfloat16* eh,
                          __nv_bfloat16* act_a, uint32_t* status, cudaStream_t st, Prof* prof) {
-  if (md.D == 192) return embed_impl<192>(md, w, cand, rows, act_a, status, st, prof);
-  if (md.D == 384) return embed_impl<384>(md, w, cand, rows, act_a, status, st, prof);
+  if (md.D == 192) return embed_impl<192>(md, w, cand, rows, eh, act_a, status, st, prof);
+  if (md.D == 384) return embed_impl<384>(md, w, cand, rows, eh, act_a, status, st, prof);
   return cudaErrorInvalidValue;
 }
 
