@@ -55,7 +55,7 @@ namespace {
 constexpr int kBlk = 16384;           // bytes of one [128 x 64] bf16 block
 constexpr int kBlkElems = 128 * 64;   // elements of one [128 x 64] block
 constexpr int kMaxWindow = 8;
-constexpr int kScratchStride = 193;   // floats per row of the q|k|v scratch
+constexpr int kKVStride = 129;        // floats per row of the k|v scratch (128 + 1)
 constexpr int kThreads = 512;         // 16 warps: 4 per TMEM lane quadrant
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -500,13 +500,14 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   constexpr int ST = C::QKV_ST;
   constexpr int B_BLK = 192 * 128;
   constexpr int R1 = KB * kBlk + ST * B_BLK;
-  constexpr int SCR = 128 * kScratchStride * 4;
+  constexpr int SCR = 128 * kKVStride * 4 + 4 * kMaxWindow * 128 * 4;
   constexpr int R1S = ((R1 > SCR ? R1 : SCR) + 1023) & ~1023;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
   uint8_t* sB = smem + KB * kBlk;
-  float* scr = reinterpret_cast<float*>(smem);  // aliases sA/sB after the MMA
+  float* kv = reinterpret_cast<float*>(smem);   // [128][kKVStride], aliases sA/sB after the MMA
+  float* spart = kv + 128 * kKVStride;           // [4 parts][kMaxWindow][128] partial scores
   uint8_t* sO = smem + R1S;
   uint64_t* full = reinterpret_cast<uint64_t*>(sO + kBlk);
   uint64_t* empty = full + ST;
@@ -585,67 +586,73 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   LEWM_STAMP(2, 4);
   __syncwarp();
   tc_fence_after();
-  {  // q|k|v of this head -> scratch rows (fp32); warp slice s owns columns [48s, 48s+48)
-    const int quad = warp & 3, slice = warp >> 2;
+  // Causal softmax(q k^T / 8) v within the candidate's window. Thread (warp w, lane l)
+  // owns window row r = 32 (w & 3) + l, its TMEM lane, and head-dim part p = w >> 2:
+  // dims [8p, 8p + 8) and [32 + 8p, 40 + 8p) of q, k and v, read straight from TMEM.
+  // Only k and v of the other rows of a window go through shared memory (row stride
+  // kKVStride = 129 floats: a warp's rows hit distinct banks), and the four parts of
+  // a row combine their partial scores through `spart`.
+  {
+    const int quad = warp & 3, part = warp >> 2;
     const int r = quad * 32 + lane;
-    const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * 48;
-    float v[48];
-    tmem_ld_cols<48>(taddr, v);
-    float* srow = scr + r * kScratchStride + slice * 48;
-#pragma unroll
-    for (int i = 0; i < 48; ++i) srow[i] = v[i];
-  }
-  __syncthreads();
-  LEWM_STAMP(2, 7);
-  {  // causal softmax(q k^T / 8) v within the candidate's window; 4 threads per row, 16 dims each
-    const int r = tid >> 2, part = tid & 3;
     const RowMap m = map_row(g, tile, r);
     const bool valid = ok && m.valid;
     const int base = r - m.pos;
-    const float* qr = scr + r * kScratchStride + part * 16;
-    float q[16];
+    const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + part * 8;
+    float q[16], kk[16], vv[16];
+    tmem_ld8(trow, q);
+    tmem_ld8(trow + 32, q + 8);
+    tmem_ld8(trow + 64, kk);
+    tmem_ld8(trow + 96, kk + 8);
+    tmem_ld8(trow + 128, vv);
+    tmem_ld8(trow + 160, vv + 8);
+    float* kvr = kv + r * kKVStride + part * 8;
 #pragma unroll
-    for (int t = 0; t < 16; ++t) q[t] = qr[t];
-    // Window loops are unrolled to kMaxWindow so the scores stay in registers.
-    float sc[kMaxWindow];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < kMaxWindow; ++j) {
-      if (j < g.w) {  // uniform across the four threads of a row (same window)
-        float d = 0.f;
-        if (valid && j <= m.pos) {
-          const float* kr = scr + (base + j) * kScratchStride + 64 + part * 16;
-#pragma unroll
-          for (int t = 0; t < 16; ++t) d += q[t] * kr[t];
-        }
-        d += __shfl_xor_sync(0xffffffffu, d, 1);
-        d += __shfl_xor_sync(0xffffffffu, d, 2);
-        sc[j] = d * 0.125f;
-        if (j <= m.pos) mx = fmaxf(mx, sc[j]);
-      } else {
-        sc[j] = 0.f;
-      }
+    for (int t = 0; t < 16; ++t) {
+      kvr[t < 8 ? t : t + 24] = kk[t];
+      kvr[64 + (t < 8 ? t : t + 24)] = vv[t];
     }
-    float den = 0.f;
+    __syncthreads();
+    LEWM_STAMP(2, 7);
+    // Loops over the window stay rolled: each CTA runs this code once, so compact code
+    // (fewer cold instruction fetches) beats unrolling.
+    const int npos = valid ? m.pos : -1;
+#pragma unroll 1
+    for (int j = 0; j < npos; ++j) {
+      const float* kr = kv + (base + j) * kKVStride + part * 8;
+      float d = 0.f;
 #pragma unroll
-    for (int j = 0; j < kMaxWindow; ++j) {
-      sc[j] = (j < g.w && j <= m.pos) ? expf(sc[j] - mx) : 0.f;
-      den += sc[j];
+      for (int t = 0; t < 16; ++t) d += q[t] * kr[t < 8 ? t : t + 24];
+      spart[(part * kMaxWindow + j) * 128 + r] = d;
     }
-    const float inv = 1.0f / den;
+    if (valid) {
+      float d = 0.f;
+#pragma unroll
+      for (int t = 0; t < 16; ++t) d += q[t] * kk[t];
+      spart[(part * kMaxWindow + m.pos) * 128 + r] = d;
+    }
+    __syncthreads();
+    LEWM_STAMP(2, 9);
+    // One pass of online softmax over the window: running max, denominator and output.
+    float mx = -INFINITY, den = 0.f;
     float o[16];
 #pragma unroll
     for (int t = 0; t < 16; ++t) o[t] = 0.f;
-    if (valid) {
+#pragma unroll 1
+    for (int j = 0; j <= npos; ++j) {
+      const float sj = (spart[(0 * kMaxWindow + j) * 128 + r] + spart[(1 * kMaxWindow + j) * 128 + r] +
+                        spart[(2 * kMaxWindow + j) * 128 + r] + spart[(3 * kMaxWindow + j) * 128 + r]) *
+                       0.125f;
+      const float mnew = fmaxf(mx, sj);
+      const float scale = expf(mx - mnew);  // 0 on the first step (mx = -inf)
+      const float pj = expf(sj - mnew);
+      den = den * scale + pj;
+      mx = mnew;
+      const float* vr = (j == npos) ? nullptr : kv + (base + j) * kKVStride + 64 + part * 8;
 #pragma unroll
-      for (int j = 0; j < kMaxWindow; ++j) {
-        if (j <= m.pos) {
-          const float* vr = scr + (base + j) * kScratchStride + 128 + part * 16;
-#pragma unroll
-          for (int t = 0; t < 16; ++t) o[t] += sc[j] * vr[t];
-        }
-      }
+      for (int t = 0; t < 16; ++t) o[t] = o[t] * scale + pj * (vr ? vr[t < 8 ? t : t + 24] : vv[t]);
     }
+    const float inv = valid ? 1.0f / den : 0.f;
     uint4 lo, hi;
     lo.x = pack_bf16x2(o[0] * inv, o[1] * inv);
     lo.y = pack_bf16x2(o[2] * inv, o[3] * inv);
@@ -656,8 +663,8 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     hi.z = pack_bf16x2(o[12] * inv, o[13] * inv);
     hi.w = pack_bf16x2(o[14] * inv, o[15] * inv);
     if (!valid) lo = hi = make_uint4(0u, 0u, 0u, 0u);
-    *reinterpret_cast<uint4*>(sO + sw128_off(r, part * 16)) = lo;
-    *reinterpret_cast<uint4*>(sO + sw128_off(r, part * 16 + 8)) = hi;
+    *reinterpret_cast<uint4*>(sO + sw128_off(r, part * 8)) = lo;
+    *reinterpret_cast<uint4*>(sO + sw128_off(r, 32 + part * 8)) = hi;
   }
   fence_async_smem();
   tc_fence_before();
@@ -895,24 +902,24 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
 }
 
 // ---------------------------------------------------------------- FC1 + GELU
-// One CTA per (row tile, 64 hidden columns): h[:, 64 nt .. 64 nt + 64) = GELU(A . W1^T + b1).
-// The weight operand of an N tile is one half (8 KB, 64 rows) of a pre-swizzled
-// [128 x 64] block; the swizzle repeats every 8 rows, so the half is itself a
+// One CTA per (row tile, 32 hidden columns): h[:, 32 nt .. 32 nt + 32) = GELU(A . W1^T + b1).
+// The weight operand of an N tile is one quarter (4 KB, 32 rows) of a pre-swizzled
+// [128 x 64] block; the swizzle repeats every 8 rows, so the quarter is itself a
 // valid SW128 operand. Each A K-block has its own barrier so the first MMA
-// starts when the first block lands.
+// starts when the first block lands. The 32 columns are half of a swizzled h
+// block, so the epilogue stores them directly (16 bytes per thread).
 template <int D>
 __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b, int layer,
                                                   uint32_t* status) {
   using C = Cfg<D>;
   constexpr int KB = C::KB;
   constexpr int ST = C::QKV_ST;
-  constexpr int NT = 64;
+  constexpr int NT = 32;
   constexpr int B_BLK = NT * 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
   uint8_t* sB = smem + KB * kBlk;
-  uint8_t* sO = smem;  // one block, aliases sA after the MMA
   float* svec = reinterpret_cast<float*>(sB + ST * B_BLK);  // [b1 NT]
   uint64_t* full = reinterpret_cast<uint64_t*>(svec + NT);
   uint64_t* empty = full + ST;
@@ -924,7 +931,7 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   const int tile = blockIdx.x, nt = blockIdx.y;
   const int nmlp = md.mlp / 128;
   const __nv_bfloat16* wb =
-      w.w1 + (size_t)((layer * nmlp + (nt >> 1)) * KB) * kBlkElems + (size_t)(nt & 1) * (NT * 64);
+      w.w1 + (size_t)((layer * nmlp + (nt >> 2)) * KB) * kBlkElems + (size_t)(nt & 3) * (NT * 64);
   if (tid == 0) {
     for (int s = 0; s < ST; ++s) {
       mbar_init(&full[s], 1);
@@ -995,40 +1002,34 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   LEWM_STAMP(4, 4);
   __syncwarp();
   tc_fence_after();
-  {  // warp slice s owns hidden columns [16s, 16s+16) of this 64-wide tile
+  {  // warp slice s owns hidden columns [8s, 8s+8) of this 32-wide tile
     const int quad = warp & 3, slice = warp >> 2;
     const int r = quad * 32 + lane;
     const RowMap m = map_row(g, tile, r);
     const bool valid = ok && m.valid;
-    const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * 16;
-    const float* bs = svec + slice * 16;
-    float v[16];
-    tmem_ld_cols<16>(taddr, v);
-#pragma unroll
-    for (int i = 0; i < 16; i += 8) {
-      uint4 pk = make_uint4(0u, 0u, 0u, 0u);
-      if (valid) {
-        pk.x = pack_bf16x2(gelu_f(v[i] + bs[i]), gelu_f(v[i + 1] + bs[i + 1]));
-        pk.y = pack_bf16x2(gelu_f(v[i + 2] + bs[i + 2]), gelu_f(v[i + 3] + bs[i + 3]));
-        pk.z = pack_bf16x2(gelu_f(v[i + 4] + bs[i + 4]), gelu_f(v[i + 5] + bs[i + 5]));
-        pk.w = pack_bf16x2(gelu_f(v[i + 6] + bs[i + 6]), gelu_f(v[i + 7] + bs[i + 7]));
-      }
-      const int c = slice * 16 + i;
-      *reinterpret_cast<uint4*>(sO + sw128_off(r, c)) = pk;
+    const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * 8;
+    const float* bs = svec + slice * 8;
+    float v[8];
+    tmem_ld_cols<8>(taddr, v);
+    LEWM_STAMP(4, 8);
+    uint4 pk = make_uint4(0u, 0u, 0u, 0u);
+    if (valid) {
+      pk.x = pack_bf16x2(gelu_f(v[0] + bs[0]), gelu_f(v[1] + bs[1]));
+      pk.y = pack_bf16x2(gelu_f(v[2] + bs[2]), gelu_f(v[3] + bs[3]));
+      pk.z = pack_bf16x2(gelu_f(v[4] + bs[4]), gelu_f(v[5] + bs[5]));
+      pk.w = pack_bf16x2(gelu_f(v[6] + bs[6]), gelu_f(v[7] + bs[7]));
+    }
+    LEWM_STAMP(4, 9);
+    if (r < g.rows8) {
+      const int nkm = md.mlp / 64;
+      uint8_t* hb = reinterpret_cast<uint8_t*>(b.h + ((size_t)tile * nkm + (nt >> 1)) * kBlkElems);
+      *reinterpret_cast<uint4*>(hb + sw128_off(r, (nt & 1) * 32 + slice * 8)) = pk;
     }
   }
-  fence_async_smem();
+  LEWM_STAMP(4, 7);
   tc_fence_before();
   __syncthreads();
-  LEWM_STAMP(4, 7);
-  if (tid == 0) {
-    const int nkm = md.mlp / 64;
-    bulk_s2g(b.h + ((size_t)tile * nkm + nt) * kBlkElems, sO, g.rows8 * 128);
-    bulk_commit();
-    bulk_wait_read();
-  }
   LEWM_STAMP(4, 6);
-  __syncwarp();
   if (warp == 0) tmem_dealloc(tmem, NT);
 }
 
@@ -1110,7 +1111,7 @@ constexpr int smem_adaln() { return 1024 + Cfg<D>::KB * (kBlk + Cfg<D>::NT_ADA *
 template <int D>
 constexpr int smem_qkv() {
   constexpr int R1 = Cfg<D>::KB * kBlk + Cfg<D>::QKV_ST * 192 * 128;
-  constexpr int SCR = 128 * kScratchStride * 4;
+  constexpr int SCR = 128 * kKVStride * 4 + 4 * kMaxWindow * 128 * 4;
   constexpr int R1S = ((R1 > SCR ? R1 : SCR) + 1023) & ~1023;
   return 1024 + R1S + kBlk + 128;
 }
@@ -1120,7 +1121,7 @@ constexpr int smem_resid() {
          2 * 4 * 128 * 8 + 8 * 5 + 16;
 }
 template <int D>
-constexpr int smem_fc1() { return 1024 + Cfg<D>::KB * kBlk + Cfg<D>::QKV_ST * 64 * 128 + 64 * 4 + 8 * (2 * Cfg<D>::QKV_ST + 1 + Cfg<D>::KB) + 16; }
+constexpr int smem_fc1() { return 1024 + Cfg<D>::KB * kBlk + Cfg<D>::QKV_ST * 32 * 128 + 32 * 4 + 8 * (2 * Cfg<D>::QKV_ST + 1 + Cfg<D>::KB) + 16; }
 
 static_assert(smem_qkv<192>() <= 232448 && smem_qkv<384>() <= 232448, "qkv smem");
 static_assert(smem_embed_out<384>() <= 232448 && smem_adaln<384>() <= 232448, "embed/adaln smem");
@@ -1205,7 +1206,7 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
                        b, md, l, status));
     if (prof) prof->end(KC_OUT, 2.0 * rows * md.inner * D, st);
     if (prof) prof->begin(st);
-    LEWM_TRY(launch_k(k_fc1<D>, dim3(g.n_tiles, md.mlp / 64), dim3(kThreads), smem_fc1<D>(), st, w, md, g, b, l,
+    LEWM_TRY(launch_k(k_fc1<D>, dim3(g.n_tiles, md.mlp / 32), dim3(kThreads), smem_fc1<D>(), st, w, md, g, b, l,
                       status));
     if (prof) prof->end(KC_FC1, 2.0 * rows * D * md.mlp, st);
     // FC2: residual with gate_mlp, then (not after the last layer) LN1 / modulate(msa of l+1) / attn.norm
