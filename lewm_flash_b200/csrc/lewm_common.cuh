@@ -62,6 +62,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   }
 }
 
+// Wait for the MMA-completion barrier in warp 0 only; every other thread blocks on the
+// CTA barrier instead of polling the mbarrier, whose shared-memory word the tensor
+// core's operand reads would otherwise share with hundreds of pollers. `flag` is a
+// spare shared word that carries warp 0's result.
+__device__ __forceinline__ bool cta_wait_mma(uint64_t* bar, uint32_t* status, uint32_t* flag) {
+  if (threadIdx.x < 32) {
+    const bool ok = mbar_wait(bar, 0, status);
+    if (threadIdx.x == 0) *flag = ok ? 1u : 0u;
+  }
+  __syncthreads();
+  return *flag != 0u;
+}
+
 // ----------------------------------------------------------------- bulk copies (TMA engine, 1-D)
 // global -> shared, completes `bytes` of transaction count on `bar`.
 // dst/src 16-byte aligned, bytes a multiple of 16.
@@ -165,6 +178,12 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float* v) {
     tmem_ld4(taddr + N - 4, v + N - 4);
   }
   tmem_ld_wait();
+}
+
+// Barrier over `nthreads` threads (whole warps) that use barrier `id` (1..15; 0 is
+// __syncthreads).
+__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // ----------------------------------------------------------------- thread-block clusters

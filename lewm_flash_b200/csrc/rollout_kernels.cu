@@ -70,7 +70,8 @@ struct Cfg {
   static constexpr int TMEM_OUT = (NT_OUT <= 64) ? 64 : 128;
   static constexpr int TMEM_EMB = (D <= 256) ? 256 : 512;
   static constexpr int QKV_ST = (KB < 3) ? KB : 3;
-  static constexpr int KG = (D == 192) ? 4 : 3;   // K blocks per copy group of the streamed-K GEMMs
+  // K blocks per copy group of the streamed-K GEMMs (two groups in flight).
+  static constexpr int KG = (D == 192) ? 4 : 3;
 };
 
 struct RowMap {
@@ -90,12 +91,16 @@ __device__ __forceinline__ RowMap map_row(const CallGeom& g, int tile, int r) {
 // ---------------------------------------------------------------- streamed-K operand pipeline
 // K blocks travel in groups of G. All copies of a group are issued by the lanes of
 // one warp in a single instruction: 1-D bulk copies issued by separate instructions
-// complete one after another, those issued together overlap. Two groups are in
-// flight (slots [2G]); group g + 2 is issued as soon as the MMAs of group g retire.
-template <int G, int B_BLK>
+// complete one after another, those issued together overlap. When every K block fits
+// in shared memory at once (G >= nkb) there is one group and no refill; otherwise two
+// groups are in flight (slots [2G]) and group g + 2 is issued as soon as the MMAs of
+// group g retire. A slots are `as` bytes apart: the tile's used rows (packed) or a
+// full block; the MMA reads 128 rows from each slot, so the A region keeps a tail of
+// (kBlk - as) bytes after its last slot.
+template <int B_BLK>
 struct KStream {
-  uint8_t* sA;                // [2G] slots of kBlk bytes
-  uint8_t* sB;                // [2G] slots of B_BLK bytes
+  uint8_t* sA;
+  uint8_t* sB;                // slots of B_BLK bytes
   uint64_t* full;             // [2] one per slot half
   uint64_t* empty;            // [2]
   const __nv_bfloat16* tA;    // A block kb at tA + kb * a_step
@@ -103,7 +108,9 @@ struct KStream {
   const __nv_bfloat16* tB;    // B block kb at tB + kb * b_step
   size_t b_step;
   uint32_t ab;                // A bytes per block (the tile's used rows)
+  uint32_t as;                // A slot stride, a multiple of 1024
   int nkb;
+  int G;                      // K blocks per group (<= 16)
   __device__ __forceinline__ int groups() const { return (nkb + G - 1) / G; }
   __device__ __forceinline__ int blocks(int g) const { return min(G, nkb - g * G); }
   __device__ __forceinline__ uint32_t bytes(int g) const { return (uint32_t)blocks(g) * (ab + B_BLK); }
@@ -114,7 +121,7 @@ struct KStream {
     if (g >= groups() || j >= blocks(g)) return;
     const int kb = g * G + j;
     if (a_side)
-      bulk_g2s(sA + (size_t)lane * kBlk, tA + (size_t)kb * a_step, ab, &full[g]);
+      bulk_g2s(sA + (size_t)lane * as, tA + (size_t)kb * a_step, ab, &full[g]);
     else
       bulk_g2s(sB + (size_t)lane * B_BLK, tB + (size_t)kb * b_step, B_BLK, &full[g]);
   }
@@ -125,7 +132,7 @@ struct KStream {
     if (j >= blocks(g)) return;
     const int kb = g * G + j, slot = (g & 1) * G + j;
     if (lane < G)
-      bulk_g2s(sA + (size_t)slot * kBlk, tA + (size_t)kb * a_step, ab, &full[g & 1]);
+      bulk_g2s(sA + (size_t)slot * as, tA + (size_t)kb * a_step, ab, &full[g & 1]);
     else
       bulk_g2s(sB + (size_t)slot * B_BLK, tB + (size_t)kb * b_step, B_BLK, &full[g & 1]);
   }
@@ -139,14 +146,21 @@ struct KStream {
       }
       tc_fence_after();
       if (lane == 0) {
-        for (int j = 0; j < blocks(g); ++j) {
-          const int slot = (g & 1) * G + j, kb = g * G + j;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint64_t ad = sdesc_sw128(smem_u32(sA) + slot * kBlk + q * 32);
-            const uint64_t bd = sdesc_sw128(smem_u32(sB) + slot * B_BLK + q * 32);
-            umma_bf16(tmem, ad, bd, idesc, (kb | q) ? 1u : 0u);
-          }
+        // Descriptors are built once and stepped: the start-address field (bits 0-13,
+        // address >> 4) advances by 2 per 32-byte K step and by the slot stride per block
+        // (shared addresses stay below 256 KB, so the field never carries).
+        const int slot0 = (g & 1) * G;
+        uint64_t ad = sdesc_sw128(smem_u32(sA) + slot0 * as);
+        uint64_t bd = sdesc_sw128(smem_u32(sB) + slot0 * B_BLK);
+        const uint64_t astep = as >> 4, bstep = B_BLK >> 4;
+        const int nb = blocks(g);
+        for (int j = 0; j < nb; ++j) {
+          umma_bf16(tmem, ad, bd, idesc, (g | j) ? 1u : 0u);
+          umma_bf16(tmem, ad + 2, bd + 2, idesc, 1u);
+          umma_bf16(tmem, ad + 4, bd + 4, idesc, 1u);
+          umma_bf16(tmem, ad + 6, bd + 6, idesc, 1u);
+          ad += astep;
+          bd += bstep;
         }
         umma_commit(&empty[g & 1]);
       }
@@ -165,6 +179,31 @@ struct KStream {
     }
   }
 };
+
+// Shared-memory layout of a residual-GEMM launch: one group holding every K block when
+// it fits in the 227 KB a CTA may use, else two groups of kg blocks; A slots packed
+// at the tile's used rows. The host sizes the launch with the same function.
+struct ResidLayout {
+  int G;          // K blocks per group
+  int a_stride;   // bytes between A slots
+  int b_off;      // offset of the B slots
+  int v_off;      // offset of the vectors / reduction scratch / barriers
+  int bytes;      // dynamic shared memory to request (includes 1024 alignment slack)
+};
+__host__ __device__ inline ResidLayout resid_layout(int rows8, int nkb, int b_blk, int kg, int extra) {
+  ResidLayout L{};
+  L.a_stride = rows8 * 128;
+  for (int pass = 0; pass < 2; ++pass) {
+    L.G = pass == 0 ? nkb : kg;
+    const int slots = L.G >= nkb ? nkb : 2 * L.G;
+    const int a_bytes = ((slots * L.a_stride + (kBlk - L.a_stride)) + 1023) & ~1023;
+    L.b_off = a_bytes;
+    L.v_off = (a_bytes + slots * b_blk + 1023) & ~1023;
+    L.bytes = 1024 + L.v_off + extra;
+    if (L.G <= 16 && L.bytes <= 232448) break;
+  }
+  return L;
+}
 
 // ---------------------------------------------------------------- Embedder + SiLU
 // act_a[row] = bf16(SiLU(Linear2(SiLU(Linear1(Conv1x1(a)))))), rows = candidate*T + t,
@@ -237,8 +276,8 @@ __global__ void __launch_bounds__(kThreads) k_embed_out(DevWeights w, ModelDims 
   const int tile = blockIdx.x, nt = blockIdx.y;
   const int nkb = md.eh / 64;
   // we2 K block kb holds all D rows: this CTA's N tile is rows [nt * NT, nt * NT + NT).
-  const KStream<G, B_BLK> ks{sA, sB, full, empty, eh + (size_t)tile * nkb * kBlkElems, (size_t)kBlkElems,
-                             w.we2 + (size_t)nt * NT * 64, (size_t)D * 64, (uint32_t)kBlk, nkb};
+  const KStream<B_BLK> ks{sA, sB, full, empty, eh + (size_t)tile * nkb * kBlkElems, (size_t)kBlkElems,
+                          w.we2 + (size_t)nt * NT * 64, (size_t)D * 64, (uint32_t)kBlk, (uint32_t)kBlk, nkb, G};
   if (tid == 0) {
     for (int h = 0; h < 2; ++h) {
       mbar_init(&full[h], 1);
@@ -275,7 +314,7 @@ __global__ void __launch_bounds__(kThreads) k_embed_out(DevWeights w, ModelDims 
   } else if (warp == 1) {
     ks.produce(lane, status);
   }
-  const bool ok = mbar_wait(bar_mma, 0, status);
+  const bool ok = cta_wait_mma(bar_mma, status, tmem_slot + 1);
   __syncwarp();
   tc_fence_after();
   const int quad = warp & 3, slice = warp >> 2;
@@ -366,7 +405,7 @@ __global__ void __launch_bounds__(kThreads) k_adaln(DevWeights w, ModelDims md, 
     }
     __syncwarp();
   }
-  const bool ok = mbar_wait(&bars[1], 0, status);
+  const bool ok = cta_wait_mma(&bars[1], status, tmem_slot + 1);
   LEWM_STAMP(1, 4);
   __syncwarp();
   tc_fence_after();
@@ -508,15 +547,17 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   uint8_t* sB = smem + KB * kBlk;
   float* kv = reinterpret_cast<float*>(smem);   // [128][kKVStride], aliases sA/sB after the MMA
   float* spart = kv + 128 * kKVStride;           // [4 parts][kMaxWindow][128] partial scores
-  uint8_t* sO = smem + R1S;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sO + kBlk);
+  // The output block also lives in the operand region when it fits after the scratch.
+  constexpr int SO_OFF = (((SCR + 1023) & ~1023) + kBlk <= R1) ? ((SCR + 1023) & ~1023) : R1S;
+  constexpr int BAR_OFF = (SO_OFF + kBlk > R1S) ? SO_OFF + kBlk : R1S;
+  uint8_t* sO = smem + SO_OFF;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
   uint64_t* empty = full + ST;
   uint64_t* bar_mma = empty + ST;
   uint64_t* bar_a = bar_mma + 1;  // [KB]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + KB);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  LEWM_STAMP(2, 0);
   const int tile = blockIdx.x, head = blockIdx.y;
   const __nv_bfloat16* wq = w.qkv + (size_t)((layer * md.heads + head) * KB) * (192 * 64);
 
@@ -582,7 +623,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     if (lane == 0) umma_commit(bar_mma);
     __syncwarp();
   }
-  const bool ok = mbar_wait(bar_mma, 0, status);
+  const bool ok = cta_wait_mma(bar_mma, status, tmem_slot + 1);
   LEWM_STAMP(2, 4);
   __syncwarp();
   tc_fence_after();
@@ -634,12 +675,13 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     __syncthreads();
     LEWM_STAMP(2, 9);
     // One pass of online softmax over the window: running max, denominator and output.
+    // Window rows before this one come from shared memory, this row from registers.
     float mx = -INFINITY, den = 0.f;
     float o[16];
 #pragma unroll
     for (int t = 0; t < 16; ++t) o[t] = 0.f;
 #pragma unroll 1
-    for (int j = 0; j <= npos; ++j) {
+    for (int j = 0; j < npos; ++j) {
       const float sj = (spart[(0 * kMaxWindow + j) * 128 + r] + spart[(1 * kMaxWindow + j) * 128 + r] +
                         spart[(2 * kMaxWindow + j) * 128 + r] + spart[(3 * kMaxWindow + j) * 128 + r]) *
                        0.125f;
@@ -648,11 +690,25 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
       const float pj = expf(sj - mnew);
       den = den * scale + pj;
       mx = mnew;
-      const float* vr = (j == npos) ? nullptr : kv + (base + j) * kKVStride + 64 + part * 8;
+      const float* vr = kv + (base + j) * kKVStride + 64 + part * 8;
 #pragma unroll
-      for (int t = 0; t < 16; ++t) o[t] = o[t] * scale + pj * (vr ? vr[t < 8 ? t : t + 24] : vv[t]);
+      for (int t = 0; t < 16; ++t) o[t] = o[t] * scale + pj * vr[t < 8 ? t : t + 24];
     }
-    const float inv = valid ? 1.0f / den : 0.f;
+    float inv = 0.f;
+    if (valid) {
+      const int j = npos;
+      const float sj = (spart[(0 * kMaxWindow + j) * 128 + r] + spart[(1 * kMaxWindow + j) * 128 + r] +
+                        spart[(2 * kMaxWindow + j) * 128 + r] + spart[(3 * kMaxWindow + j) * 128 + r]) *
+                       0.125f;
+      const float mnew = fmaxf(mx, sj);
+      const float scale = expf(mx - mnew);
+      const float pj = expf(sj - mnew);
+      den = den * scale + pj;
+#pragma unroll
+      for (int t = 0; t < 16; ++t) o[t] = o[t] * scale + pj * vv[t];
+      inv = 1.0f / den;
+    }
+    LEWM_STAMP(2, 0);
     uint4 lo, hi;
     lo.x = pack_bf16x2(o[0] * inv, o[1] * inv);
     lo.y = pack_bf16x2(o[2] * inv, o[3] * inv);
@@ -681,6 +737,10 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
 }
 
 // ---------------------------------------------------------------- streamed-K GEMM, residual + LayerNorm epilogue
+// Bytes after the operand slots: vectors [3][NT], per-slice moments [4][128] float2,
+// cluster exchange [2][4][128] float2, 5 barriers, the TMEM slot.
+template <int D>
+__host__ __device__ constexpr int resid_extra() { return 3 * Cfg<D>::NT_OUT * 4 + 4 * 128 * 8 + 2 * 4 * 128 * 8 + 8 * 5 + 16; }
 // What the epilogue of an out-projection / FC2 launch does with its N tile.
 struct ResidEpi {
   const float* bias;      // [D] of this GEMM
@@ -706,25 +766,28 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
   using C = Cfg<D>;
   constexpr int NT = C::NT_OUT;
   constexpr int CW = NT / 4;
-  constexpr int G = C::KG;
   constexpr int B_BLK = NT * 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
+  const ResidLayout lay = resid_layout(g.rows8, nkb, B_BLK, C::KG, resid_extra<D>());
+  const int G = lay.G;
   uint8_t* sA = smem;
-  uint8_t* sB = smem + 2 * G * kBlk;
-  float* svec = reinterpret_cast<float*>(sB + 2 * G * B_BLK);  // [bias NT][ln_g NT][ln_b NT]
-  float* red = svec + 3 * NT;                                  // [2][4 slices][128]
-  float2* xch = reinterpret_cast<float2*>(red + 2 * 4 * 128);  // [2 rounds][4 ranks][128]
+  uint8_t* sB = smem + lay.b_off;
+  float* svec = reinterpret_cast<float*>(smem + lay.v_off);  // [bias NT][ln_g NT][ln_b NT]
+  float2* red2 = reinterpret_cast<float2*>(svec + 3 * NT);     // [4 slices][128] (mean, M2)
+  float2* xch = red2 + 4 * 128;                                // [2 rounds][4 ranks][128]
   uint64_t* full = reinterpret_cast<uint64_t*>(xch + 2 * 4 * 128);
   uint64_t* empty = full + 2;
   uint64_t* bar_mma = empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  LEWM_STAMP(3, 0);
+  const int skind = ep.gate_chunk == 2 ? 5 : 3;  // diagnostic stamp stream: out-proj / FC2
+  (void)skind;
   const int tile = blockIdx.x, nt = blockIdx.y;  // nt == cluster rank
   const bool do_ln = ep.a_out != nullptr;
-  const KStream<G, B_BLK> ks{sA, sB, full, empty, gA + (size_t)tile * nkb * kBlkElems, (size_t)kBlkElems,
-                             gB + (size_t)nt * nkb * NT * 64, (size_t)NT * 64, (uint32_t)g.rows8 * 128, nkb};
+  const KStream<B_BLK> ks{sA, sB, full, empty, gA + (size_t)tile * nkb * kBlkElems, (size_t)kBlkElems,
+                          gB + (size_t)nt * nkb * NT * 64, (size_t)NT * 64, (uint32_t)g.rows8 * 128,
+                          (uint32_t)lay.a_stride, nkb, G};
   if (tid == 0) {
     for (int h = 0; h < 2; ++h) {
       mbar_init(&full[h], 1);
@@ -737,16 +800,18 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
   }
   __syncwarp();
   // Weights and vectors first (they do not depend on the previous kernel), in one
-  // instruction of warp 0.
+  // instruction of warp 0 (K blocks on lanes below 2G <= 32, vectors on lanes 29-31,
+  // which K blocks never use when 2G > 29 because then G >= nkb and one group
+  // covers lanes below nkb <= 16).
   if (warp == 0) {
-    if (lane < 2 * G)
-      ks.issue_first(lane, false);
-    else if (lane == 2 * G)
+    if (lane == 29)
       bulk_g2s(svec, ep.bias + nt * NT, NT * 4, &full[0]);
-    else if (lane == 2 * G + 1 && do_ln)
+    else if (lane == 30 && do_ln)
       bulk_g2s(svec + NT, ep.ln_g + nt * NT, NT * 4, &full[0]);
-    else if (lane == 2 * G + 2 && do_ln)
+    else if (lane == 31 && do_ln)
       bulk_g2s(svec + 2 * NT, ep.ln_b + nt * NT, NT * 4, &full[0]);
+    else
+      ks.issue_first(lane, false);
   }
   __syncwarp();
   if (warp == 0) {
@@ -754,19 +819,19 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
     tmem_relinquish();
   }
   cluster_sync();  // every CTA of the cluster is running before any distributed shared-memory access
-  LEWM_STAMP(3, 1);
+  LEWM_STAMP(skind, 1);
   griddep_wait();
-  LEWM_STAMP(3, 2);
+  LEWM_STAMP(skind, 2);
   griddep_launch();
   if (warp == 0) ks.issue_first(lane, true);
-  LEWM_STAMP(3, 5);
+  LEWM_STAMP(skind, 5);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (warp == 0) {  // MMA issuer
     ks.mma(tmem, idesc_bf16(128, NT), lane, status);
-    LEWM_STAMP(3, 3);
+    LEWM_STAMP(skind, 3);
     if (lane == 0) umma_commit(bar_mma);
     __syncwarp();
   } else if (warp == 1) {
@@ -803,14 +868,14 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
       gt[i] = sh[i] = sc[i] = make_uint2(0u, 0u);
     }
   }
-  const bool ok = mbar_wait(bar_mma, 0, status);
-  LEWM_STAMP(3, 4);
+  const bool ok = cta_wait_mma(bar_mma, status, tmem_slot + 1);
+  LEWM_STAMP(skind, 4);
   __syncwarp();
   tc_fence_after();
   const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * CW;
   float v[CW];
   tmem_ld_cols<CW>(taddr, v);
-  LEWM_STAMP(3, 7);
+  LEWM_STAMP(skind, 7);
   {
     const float* bs = svec + slice * CW;
 #pragma unroll
@@ -836,25 +901,31 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
     const int rank = nt;
 #pragma unroll
     for (int round = 0; round < 2; ++round) {
-      // (mean, M2) of this CTA's NT columns of row r: two passes through shared memory.
-      float s = 0.f;
+      // (mean, M2) of this thread's CW columns in registers, then of the CTA's NT columns
+      // of row r: Chan merge of the four column slices, which live in the four warps
+      // sharing this TMEM lane quadrant, behind a named barrier of those 128 threads.
+      float mt = 0.f;
 #pragma unroll
-      for (int i = 0; i < CW; ++i) s += z[i];
-      red[slice * 128 + r] = s;
-      __syncthreads();
-      const float mean_c = (red[r] + red[128 + r] + red[256 + r] + red[384 + r]) * (1.0f / NT);
-      float q = 0.f;
+      for (int i = 0; i < CW; ++i) mt += z[i];
+      mt *= 1.0f / CW;
+      float qt = 0.f;
 #pragma unroll
-      for (int i = 0; i < CW; ++i) q += (z[i] - mean_c) * (z[i] - mean_c);
-      red[512 + slice * 128 + r] = q;
-      __syncthreads();
+      for (int i = 0; i < CW; ++i) qt += (z[i] - mt) * (z[i] - mt);
+      red2[slice * 128 + r] = make_float2(mt, qt);
+      named_barrier_sync(1 + quad, 128);
       if (slice == 0) {
-        const float m2_c = red[512 + r] + red[640 + r] + red[768 + r] + red[896 + r];
+        const float2 p0 = red2[r], p1 = red2[128 + r], p2 = red2[256 + r], p3 = red2[384 + r];
+        const float mean_c = (p0.x + p1.x + p2.x + p3.x) * 0.25f;
+        const float m2_c = p0.y + p1.y + p2.y + p3.y +
+                           CW * ((p0.x - mean_c) * (p0.x - mean_c) + (p1.x - mean_c) * (p1.x - mean_c) +
+                                 (p2.x - mean_c) * (p2.x - mean_c) + (p3.x - mean_c) * (p3.x - mean_c));
         const float2 mv = make_float2(mean_c, m2_c);
 #pragma unroll
         for (int peer = 0; peer < 4; ++peer) st_dsmem_f2(xch + (round * 4 + rank) * 128 + r, peer, mv);
       }
+      LEWM_STAMP(skind, round == 0 ? 9 : 0);
       cluster_sync();
+      if (round == 0) LEWM_STAMP(skind, 8);
       float mean = 0.f;
       float2 part[4];
 #pragma unroll
@@ -894,7 +965,7 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
       }
     }
   }
-  LEWM_STAMP(3, 6);
+  LEWM_STAMP(skind, 6);
   tc_fence_before();
   __syncthreads();
   __syncwarp();
@@ -998,7 +1069,7 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
     if (lane == 0) umma_commit(bar_mma);
     __syncwarp();
   }
-  const bool ok = mbar_wait(bar_mma, 0, status);
+  const bool ok = cta_wait_mma(bar_mma, status, tmem_slot + 1);
   LEWM_STAMP(4, 4);
   __syncwarp();
   tc_fence_after();
@@ -1113,13 +1184,12 @@ constexpr int smem_qkv() {
   constexpr int R1 = Cfg<D>::KB * kBlk + Cfg<D>::QKV_ST * 192 * 128;
   constexpr int SCR = 128 * kKVStride * 4 + 4 * kMaxWindow * 128 * 4;
   constexpr int R1S = ((R1 > SCR ? R1 : SCR) + 1023) & ~1023;
-  return 1024 + R1S + kBlk + 128;
+  constexpr int SO_OFF = (((SCR + 1023) & ~1023) + kBlk <= R1) ? ((SCR + 1023) & ~1023) : R1S;
+  constexpr int BAR_OFF = (SO_OFF + kBlk > R1S) ? SO_OFF + kBlk : R1S;
+  return 1024 + BAR_OFF + 128;
 }
 template <int D>
-constexpr int smem_resid() {
-  return 1024 + 2 * Cfg<D>::KG * (kBlk + Cfg<D>::NT_OUT * 128) + 3 * Cfg<D>::NT_OUT * 4 + 2 * 4 * 128 * 4 +
-         2 * 4 * 128 * 8 + 8 * 5 + 16;
-}
+constexpr int smem_resid() { return 232448; }  // per launch: resid_layout(...).bytes
 template <int D>
 constexpr int smem_fc1() { return 1024 + Cfg<D>::KB * kBlk + Cfg<D>::QKV_ST * 32 * 128 + 32 * 4 + 8 * (2 * Cfg<D>::QKV_ST + 1 + Cfg<D>::KB) + 16; }
 
@@ -1200,8 +1270,9 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
     // out-projection: residual with gate_msa, then LN2 / modulate(mlp) / FFN LayerNorm -> FC1 operand
     const ResidEpi ep_out{w.out_b + l * D, 2, b.a_ffn, l, 3, w.ffn_ln_w + l * D, w.ffn_ln_b + l * D};
     if (prof) prof->begin(st);
-    LEWM_TRY(launch_kc(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads), smem_resid<D>(), st, dim3(1, 4, 1),
-                       (const __nv_bfloat16*)b.attn, nkb_inner,
+    LEWM_TRY(launch_kc(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads),
+                       resid_layout(g.rows8, nkb_inner, Cfg<D>::NT_OUT * 128, Cfg<D>::KG, resid_extra<D>()).bytes, st,
+                       dim3(1, 4, 1), (const __nv_bfloat16*)b.attn, nkb_inner,
                        (const __nv_bfloat16*)(w.wout + (size_t)l * 4 * nkb_inner * Cfg<D>::NT_OUT * 64), ep_out, g,
                        b, md, l, status));
     if (prof) prof->end(KC_OUT, 2.0 * rows * md.inner * D, st);
@@ -1215,8 +1286,9 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
     const ResidEpi ep_fc2{w.b2 + l * D, 5, more ? b.a_attn : nullptr, nl, 0, w.attn_ln_w + nl * D,
                           w.attn_ln_b + nl * D};
     if (prof) prof->begin(st);
-    LEWM_TRY(launch_kc(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads), smem_resid<D>(), st, dim3(1, 4, 1),
-                       (const __nv_bfloat16*)b.h, nkb_mlp,
+    LEWM_TRY(launch_kc(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads),
+                       resid_layout(g.rows8, nkb_mlp, Cfg<D>::NT_OUT * 128, Cfg<D>::KG, resid_extra<D>()).bytes, st,
+                       dim3(1, 4, 1), (const __nv_bfloat16*)b.h, nkb_mlp,
                        (const __nv_bfloat16*)(w.w2 + (size_t)l * 4 * nkb_mlp * Cfg<D>::NT_OUT * 64), ep_fc2, g, b,
                        md, l, status));
     if (prof) prof->end(KC_FC2, 2.0 * rows * md.mlp * D, st);
