@@ -41,6 +41,17 @@ F_BLOCK_TOKEN = 2 * (D * 3 * INNER + INNER * D + 2 * D * MLP)  # per token per l
 F_CANON = 9 * L * F_BLOCK_TOKEN + T * L * 2 * D * 6 * D + T * 2 * (A * A + A * 4 * D + 4 * D * D)
 
 
+# DRAM bytes (read + write) of one launch of the dominant kernel classes, from the ncu
+# captures summarised in profiles/k_resid_gemm_outproj_fc2_w3_9tiles.md and
+# profiles/k_qkv_attn_w3_9tiles.md (ncu flushes L2 between passes, so these are
+# cold-cache first-touch bytes; the timed run keeps weights in L2).
+NCU_TRAFFIC = {
+    "out_proj": {"bytes": 4148736, "launch": "out-proj, 900 rows (300 candidates x window 3), 9 tiles"},
+    "fc2": {"bytes": 3571200, "launch": "FC2, 900 rows (300 candidates x window 3), 9 tiles"},
+    "qkv_attn": {"bytes": 1316096, "launch": "QKV + attention, 900 rows, 9 tiles x 16 heads"},
+}
+
+
 def percentile(values, q):
     """Interpolated percentile (reference tools/benchmarks/metrics.py:64-76)."""
     xs = sorted(values)
@@ -342,8 +353,10 @@ def kernel_class_pass(rt, opts, emb, goal, mean, std, dev):
     top = max(classes, key=lambda k: classes[k]["ms"])
     c = classes[top]
     achieved = c["flops"] / (c["ms"] / 1e3) / 1e12 if c["ms"] > 0 else 0.0
+    ncu = NCU_TRAFFIC.get(top)
     roof = {"kernel": top, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-            "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
+            "frac": achieved / peak, "traffic": ncu["bytes"] if ncu else None,
+            "traffic_launch": ncu["launch"] if ncu else None, "peak_source": peak_kind,
             "method": "CUDA events around every launch of this class in an untimed plan; "
                       "algorithmic FLOPs = valid rows x GEMM shape"}
     return {"roofline": roof, "classes": classes, "launches_per_plan": res["launches"], "peak": peak}
