@@ -57,6 +57,7 @@ constexpr int kBlkElems = 128 * 64;   // elements of one [128 x 64] block
 constexpr int kMaxWindow = 8;
 constexpr int kKVStride = 129;        // floats per row of the k|v scratch (128 + 1)
 constexpr int kThreads = 512;         // 16 warps: 4 per TMEM lane quadrant
+constexpr int kFc1N = 32;             // hidden columns per FC1 CTA (N of its MMA)
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -979,13 +980,15 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
 // valid SW128 operand. Each A K-block has its own barrier so the first MMA
 // starts when the first block lands. The 32 columns are half of a swizzled h
 // block, so the epilogue stores them directly (16 bytes per thread).
-template <int D>
+template <int D, int NT>
 __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b, int layer,
                                                   uint32_t* status) {
   using C = Cfg<D>;
   constexpr int KB = C::KB;
   constexpr int ST = C::QKV_ST;
-  constexpr int NT = 32;
+  constexpr int CW = NT / 4;     // columns per warp slice
+  constexpr int PER128 = 128 / NT;  // N tiles per packed 128-row weight block
+  constexpr int PER64 = 64 / NT;    // N tiles per 64-column h block
   constexpr int B_BLK = NT * 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -1002,7 +1005,7 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   const int tile = blockIdx.x, nt = blockIdx.y;
   const int nmlp = md.mlp / 128;
   const __nv_bfloat16* wb =
-      w.w1 + (size_t)((layer * nmlp + (nt >> 2)) * KB) * kBlkElems + (size_t)(nt & 3) * (NT * 64);
+      w.w1 + (size_t)((layer * nmlp + nt / PER128) * KB) * kBlkElems + (size_t)(nt % PER128) * (NT * 64);
   if (tid == 0) {
     for (int s = 0; s < ST; ++s) {
       mbar_init(&full[s], 1);
@@ -1073,29 +1076,30 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   LEWM_STAMP(4, 4);
   __syncwarp();
   tc_fence_after();
-  {  // warp slice s owns hidden columns [8s, 8s+8) of this 32-wide tile
+  {  // warp slice s owns hidden columns [CW s, CW s + CW) of this NT-wide tile
     const int quad = warp & 3, slice = warp >> 2;
     const int r = quad * 32 + lane;
     const RowMap m = map_row(g, tile, r);
     const bool valid = ok && m.valid;
-    const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * 8;
-    const float* bs = svec + slice * 8;
-    float v[8];
-    tmem_ld_cols<8>(taddr, v);
+    const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * CW;
+    const float* bs = svec + slice * CW;
+    float v[CW];
+    tmem_ld_cols<CW>(taddr, v);
     LEWM_STAMP(4, 8);
-    uint4 pk = make_uint4(0u, 0u, 0u, 0u);
-    if (valid) {
-      pk.x = pack_bf16x2(gelu_f(v[0] + bs[0]), gelu_f(v[1] + bs[1]));
-      pk.y = pack_bf16x2(gelu_f(v[2] + bs[2]), gelu_f(v[3] + bs[3]));
-      pk.z = pack_bf16x2(gelu_f(v[4] + bs[4]), gelu_f(v[5] + bs[5]));
-      pk.w = pack_bf16x2(gelu_f(v[6] + bs[6]), gelu_f(v[7] + bs[7]));
+    const int nkm = md.mlp / 64;
+    uint8_t* hb = reinterpret_cast<uint8_t*>(b.h + ((size_t)tile * nkm + nt / PER64) * kBlkElems);
+#pragma unroll
+    for (int i = 0; i < CW; i += 8) {
+      uint4 pk = make_uint4(0u, 0u, 0u, 0u);
+      if (valid) {
+        pk.x = pack_bf16x2(gelu_f(v[i] + bs[i]), gelu_f(v[i + 1] + bs[i + 1]));
+        pk.y = pack_bf16x2(gelu_f(v[i + 2] + bs[i + 2]), gelu_f(v[i + 3] + bs[i + 3]));
+        pk.z = pack_bf16x2(gelu_f(v[i + 4] + bs[i + 4]), gelu_f(v[i + 5] + bs[i + 5]));
+        pk.w = pack_bf16x2(gelu_f(v[i + 6] + bs[i + 6]), gelu_f(v[i + 7] + bs[i + 7]));
+      }
+      if (r < g.rows8) *reinterpret_cast<uint4*>(hb + sw128_off(r, (nt % PER64) * NT + slice * CW + i)) = pk;
     }
     LEWM_STAMP(4, 9);
-    if (r < g.rows8) {
-      const int nkm = md.mlp / 64;
-      uint8_t* hb = reinterpret_cast<uint8_t*>(b.h + ((size_t)tile * nkm + (nt >> 1)) * kBlkElems);
-      *reinterpret_cast<uint4*>(hb + sw128_off(r, (nt & 1) * 32 + slice * 8)) = pk;
-    }
   }
   LEWM_STAMP(4, 7);
   tc_fence_before();
@@ -1190,12 +1194,12 @@ constexpr int smem_qkv() {
 }
 template <int D>
 constexpr int smem_resid() { return 232448; }  // per launch: resid_layout(...).bytes
-template <int D>
-constexpr int smem_fc1() { return 1024 + Cfg<D>::KB * kBlk + Cfg<D>::QKV_ST * 32 * 128 + 32 * 4 + 8 * (2 * Cfg<D>::QKV_ST + 1 + Cfg<D>::KB) + 16; }
+template <int D, int NT>
+constexpr int smem_fc1() { return 1024 + Cfg<D>::KB * kBlk + Cfg<D>::QKV_ST * NT * 128 + NT * 4 + 8 * (2 * Cfg<D>::QKV_ST + 1 + Cfg<D>::KB) + 16; }
 
 static_assert(smem_qkv<192>() <= 232448 && smem_qkv<384>() <= 232448, "qkv smem");
 static_assert(smem_embed_out<384>() <= 232448 && smem_adaln<384>() <= 232448, "embed/adaln smem");
-static_assert(smem_fc1<384>() <= 232448 && smem_resid<384>() <= 232448, "fc smem");
+static_assert(smem_fc1<384, kFc1N>() <= 232448 && smem_resid<384>() <= 232448, "fc smem");
 
 template <int D>
 cudaError_t set_smem_attrs() {
@@ -1208,7 +1212,8 @@ cudaError_t set_smem_attrs() {
   if ((e = cudaFuncSetAttribute(k_qkv_attn<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_qkv<D>()))) return e;
   if ((e = cudaFuncSetAttribute(k_resid_gemm<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_resid<D>())))
     return e;
-  if ((e = cudaFuncSetAttribute(k_fc1<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_fc1<D>()))) return e;
+  if ((e = cudaFuncSetAttribute(k_fc1<D, kFc1N>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_fc1<D, kFc1N>())))
+    return e;
   done = true;
   return cudaSuccess;
 }
@@ -1277,7 +1282,8 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
                        b, md, l, status));
     if (prof) prof->end(KC_OUT, 2.0 * rows * md.inner * D, st);
     if (prof) prof->begin(st);
-    LEWM_TRY(launch_k(k_fc1<D>, dim3(g.n_tiles, md.mlp / 32), dim3(kThreads), smem_fc1<D>(), st, w, md, g, b, l,
+    LEWM_TRY(launch_k(k_fc1<D, kFc1N>, dim3(g.n_tiles, md.mlp / kFc1N), dim3(kThreads), smem_fc1<D, kFc1N>(), st, w,
+                      md, g, b, l,
                       status));
     if (prof) prof->end(KC_FC1, 2.0 * rows * D * md.mlp, st);
     // FC2: residual with gate_mlp, then (not after the last layer) LN1 / modulate(msa of l+1) / attn.norm
