@@ -1,6 +1,6 @@
 // iCEM sampling and elite refit kernels for sm_100a.
 //
-// k_sample: one thread per (env, candidate) builds the candidate action sequence
+// k_sample: one warp per (env, candidate) builds the candidate action sequence
 //   cand = noise * std + mean (reference lewm/solvers/icem.py:523), slot 0 = mean
 //   (:524), slots 1..n_inject = previous sorted elites (:421-432), optional clamp
 //   (:526-527). Noise is either injected (the reference's post-coloring noise
@@ -56,73 +56,96 @@ __device__ __forceinline__ void normals4(uint32_t blk, uint32_t cand, uint32_t e
   out[3] = rb * sb;
 }
 
-__global__ void __launch_bounds__(128) k_sample(SampleParams p) {
+// One warp per candidate: lane k draws Philox block k (normals 4k .. 4k+3, the same
+// counter layout as a single thread would use), lanes split the coloring matvec over
+// time steps, and the unbiased std over time is a warp reduction.
+constexpr int kSampleWarps = 4;  // candidates per 128-thread CTA
+
+__global__ void __launch_bounds__(32 * kSampleWarps) k_sample(SampleParams p) {
+  __shared__ float wn_s[kSampleWarps][kMaxTA];
+  __shared__ float v_s[kSampleWarps][kMaxTA];
   griddep_wait();
   griddep_launch();
-  const int gid = blockIdx.x * blockDim.x + threadIdx.x;
-  if (gid >= p.B * p.S) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = blockIdx.x * kSampleWarps + warp;
+  if (gid >= p.B * p.S) return;  // whole warp
   const int env = gid / p.S, c = gid - env * p.S;
   const int TA = p.T * p.A;
   const float* mean = p.mean + (size_t)env * TA;
   const float* sd = p.stdv + (size_t)env * TA;
   float* out = p.cand + (size_t)gid * TA;
-  float v[kMaxTA];
+  float* wn = wn_s[warp];
+  float* v = v_s[warp];
   if (c == 0) {
-    for (int i = 0; i < TA; ++i) v[i] = mean[i];
+    for (int i = lane; i < TA; i += 32) v[i] = mean[i];
   } else if (c <= p.n_inject) {
     const float* e = p.elites + ((size_t)env * p.elite_stride + (c - 1)) * TA;
-    for (int i = 0; i < TA; ++i) v[i] = e[i];
+    for (int i = lane; i < TA; i += 32) v[i] = e[i];
   } else if (p.noise) {
     const float* nz = p.noise + (size_t)gid * TA;
-    for (int i = 0; i < TA; ++i) v[i] = nz[i] * sd[i] + mean[i];
+    for (int i = lane; i < TA; i += 32) v[i] = nz[i] * sd[i] + mean[i];
   } else {
     // White draws in the reference's randn layout: [channel][time].
     const int chans = (p.noise_kind == 1) ? p.A / p.raw_block : p.A;
     const int ncol = (p.noise_kind == 0) ? p.T : p.ncol;
     const int n = chans * ncol;
-    float wn[kMaxTA];
-    for (int d = 0; d < n; d += 4) {
+    for (int blk = lane; 4 * blk < n; blk += 32) {
       float r4[4];
-      normals4((uint32_t)(d >> 2), (uint32_t)c, (uint32_t)env, p.iter, p.rng[0], p.rng[1], r4);
-      for (int q = 0; q < 4 && d + q < n; ++q) wn[d + q] = r4[q];
+      normals4((uint32_t)blk, (uint32_t)c, (uint32_t)env, p.iter, p.rng[0], p.rng[1], r4);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (4 * blk + q < n) wn[4 * blk + q] = r4[q];
     }
+    __syncwarp();
     if (p.noise_kind == 0) {
       // white (B,S,T,A): draw d -> (t, a) = (d / A, d % A)
-      for (int i = 0; i < TA; ++i) v[i] = wn[i] * sd[i] + mean[i];
+      for (int i = lane; i < TA; i += 32) v[i] = wn[i] * sd[i] + mean[i];
     } else {
       for (int ch = 0; ch < chans; ++ch) {
-        float col[kMaxCol];
+        float colv[kMaxCol / 32];
         float s = 0.f;
-        for (int t = 0; t < ncol; ++t) {
+#pragma unroll
+        for (int k = 0; k < kMaxCol / 32; ++k) {
+          const int t = lane + 32 * k;
           float acc = 0.f;
-          const float* wr = p.W + t * ncol;
-          for (int u = 0; u < ncol; ++u) acc += wr[u] * wn[ch * ncol + u];
-          col[t] = acc;
+          if (t < ncol) {
+            const float* wr = p.W + t * ncol;
+            for (int u = 0; u < ncol; ++u) acc += wr[u] * wn[ch * ncol + u];
+          }
+          colv[k] = acc;
           s += acc;
         }
-        const float mu = s / ncol;
+        const float mu = warp_sum(s) / ncol;
         float q = 0.f;
-        for (int t = 0; t < ncol; ++t) q += (col[t] - mu) * (col[t] - mu);
-        const float sdv = fmaxf(sqrtf(q / (float)(ncol - 1)), 1e-8f);
-        for (int t = 0; t < ncol; ++t) {
-          int ts, a;
-          if (p.noise_kind == 1) {  // raw time: (t, ch) -> solver step t / block, dim (t % block) * chans + ch
-            ts = t / p.raw_block;
-            a = (t - ts * p.raw_block) * chans + ch;
-          } else {  // block: channel ch is action dim, t is solver step
-            ts = t;
-            a = ch;
+#pragma unroll
+        for (int k = 0; k < kMaxCol / 32; ++k)
+          if (lane + 32 * k < ncol) q += (colv[k] - mu) * (colv[k] - mu);
+        const float sdv = fmaxf(sqrtf(warp_sum(q) / (float)(ncol - 1)), 1e-8f);
+#pragma unroll
+        for (int k = 0; k < kMaxCol / 32; ++k) {
+          const int t = lane + 32 * k;
+          if (t < ncol) {
+            int ts, a;
+            if (p.noise_kind == 1) {  // raw time: (t, ch) -> solver step t / block, dim (t % block) * chans + ch
+              ts = t / p.raw_block;
+              a = (t - ts * p.raw_block) * chans + ch;
+            } else {  // block: channel ch is action dim, t is solver step
+              ts = t;
+              a = ch;
+            }
+            const int i = ts * p.A + a;
+            v[i] = (colv[k] / sdv) * sd[i] + mean[i];
           }
-          const int i = ts * p.A + a;
-          v[i] = (col[t] / sdv) * sd[i] + mean[i];
         }
       }
     }
   }
-  if (p.low) {
-    for (int i = 0; i < TA; ++i) v[i] = fminf(fmaxf(v[i], p.low[i % p.A]), p.high[i % p.A]);
+  __syncwarp();
+  for (int i = lane; i < TA; i += 32) {
+    float x = v[i];
+    if (p.low) x = fminf(fmaxf(x, p.low[i % p.A]), p.high[i % p.A]);
+    out[i] = x;
   }
-  for (int i = 0; i < TA; ++i) out[i] = v[i];
 }
 
 __device__ __forceinline__ uint32_t order_key(float f) {
@@ -219,7 +242,7 @@ cudaError_t launch_set_rng(uint32_t* rng, uint32_t seed, uint32_t plan, cudaStre
 cudaError_t launch_sample(const SampleParams& p, cudaStream_t st) {
   if (p.T * p.A > kMaxTA || p.ncol > kMaxCol) return cudaErrorInvalidValue;
   const int n = p.B * p.S;
-  return launch_k(k_sample, dim3((n + 127) / 128), dim3(128), 0, st, p);
+  return launch_k(k_sample, dim3((n + kSampleWarps - 1) / kSampleWarps), dim3(32 * kSampleWarps), 0, st, p);
 }
 
 cudaError_t launch_refit(const RefitParams& p, cudaStream_t st) {

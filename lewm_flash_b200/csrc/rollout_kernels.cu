@@ -1109,71 +1109,79 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
 }
 
 // ---------------------------------------------------------------- final LayerNorm + history / cost
-// Warp per candidate: final LayerNorm of the window's last token. The last call scores
-// it against the goal; earlier calls append it to the history and prepare the next
-// call's layer-0 residual and A operand for every row of the candidate's next window.
+// The last call: warp per candidate, final LayerNorm of the window's last token and its
+// squared distance to the goal. Earlier calls: warp per (candidate, row p of the next
+// call's window). The warp of the last row, the new prediction, computes the final
+// LayerNorm of this call's last token, appends it to the history and prepares its row;
+// the other warps prepare their rows from the history (observation embeddings or
+// earlier predictions), which this call does not change.
 template <int D>
 __global__ void __launch_bounds__(128) k_final(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b) {
   griddep_wait();
   griddep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cand = blockIdx.x * 4 + warp;
-  if (cand >= g.n_cand) return;
-  const int tile = cand / g.cpt;
-  const int r = (cand - tile * g.cpt) * g.w + (g.w - 1);
-  const float* xr = b.x + ((size_t)tile * 128 + r) * D;
+  const int rows_per_cand = g.last ? 1 : g.next_w;
+  const int item = blockIdx.x * 4 + warp;
+  if (item >= g.n_cand * rows_per_cand) return;
+  const int cand = item / rows_per_cand, p = item - cand * rows_per_cand;
   constexpr int NP = D / 64;
-  const int e = b.goal_per_cand ? cand : cand / g.S;
-  const float* gr = b.goal + (size_t)e * D;
-  float2 v[NP], gv[NP], fw[NP], fb[NP];
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    const int c = 64 * i + 2 * lane;
-    v[i] = *reinterpret_cast<const float2*>(xr + c);
-    gv[i] = g.last ? *reinterpret_cast<const float2*>(gr + c) : make_float2(0.f, 0.f);
-    fw[i] = *reinterpret_cast<const float2*>(w.fin_w + c);
-    fb[i] = *reinterpret_cast<const float2*>(w.fin_b + c);
-    s += v[i].x + v[i].y;
-  }
-  const float mean = warp_sum(s) * (1.0f / D);
-  float q = 0.f;
-#pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    const float dx = v[i].x - mean, dy = v[i].y - mean;
-    q += dx * dx + dy * dy;
-  }
-  const float rstd = rsqrtf(warp_sum(q) * (1.0f / D) + 1e-5f);
-#pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    v[i].x = (v[i].x - mean) * rstd * fw[i].x + fb[i].x;
-    v[i].y = (v[i].y - mean) * rstd * fw[i].y + fb[i].y;
-  }
-  if (g.last) {
-    float acc = 0.f;
-#pragma unroll
-    for (int i = 0; i < NP; ++i) {
-      const float dx = v[i].x - gv[i].x, dy = v[i].y - gv[i].y;
-      acc += dx * dx + dy * dy;
-    }
-    acc = warp_sum(acc);
-    if (lane == 0) b.costs[cand] = acc;
-    return;
-  }
   const int NPred = g.T - g.H + 1;
   float* pcand = b.pred + (size_t)cand * NPred * D;
+  const int j = g.next_start + p;  // history index of this row (unused when last)
+  const bool new_pred = g.last || (j - g.H == g.call);
+  float2 v[NP];
+  if (new_pred) {
+    const int tile = cand / g.cpt;
+    const int r = (cand - tile * g.cpt) * g.w + (g.w - 1);
+    const float* xr = b.x + ((size_t)tile * 128 + r) * D;
+    float2 fw[NP], fb[NP];
+    float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < NP; ++i) *reinterpret_cast<float2*>(pcand + g.call * D + 64 * i + 2 * lane) = v[i];
-  // Next call's window rows of this candidate (each lane reads back only its own columns).
+    for (int i = 0; i < NP; ++i) {
+      const int c = 64 * i + 2 * lane;
+      v[i] = *reinterpret_cast<const float2*>(xr + c);
+      fw[i] = *reinterpret_cast<const float2*>(w.fin_w + c);
+      fb[i] = *reinterpret_cast<const float2*>(w.fin_b + c);
+      s += v[i].x + v[i].y;
+    }
+    const float mean = warp_sum(s) * (1.0f / D);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      const float dx = v[i].x - mean, dy = v[i].y - mean;
+      q += dx * dx + dy * dy;
+    }
+    const float rstd = rsqrtf(warp_sum(q) * (1.0f / D) + 1e-5f);
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      v[i].x = (v[i].x - mean) * rstd * fw[i].x + fb[i].x;
+      v[i].y = (v[i].y - mean) * rstd * fw[i].y + fb[i].y;
+    }
+    if (g.last) {
+      const int e = b.goal_per_cand ? cand : cand / g.S;
+      const float* gr = b.goal + (size_t)e * D;
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        const float2 gv = *reinterpret_cast<const float2*>(gr + 64 * i + 2 * lane);
+        const float dx = v[i].x - gv.x, dy = v[i].y - gv.y;
+        acc += dx * dx + dy * dy;
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) b.costs[cand] = acc;
+      return;
+    }
+#pragma unroll
+    for (int i = 0; i < NP; ++i) *reinterpret_cast<float2*>(pcand + g.call * D + 64 * i + 2 * lane) = v[i];
+  }
+  // Row p of the candidate's next window (each lane reads back only its own columns).
   const int ntile = cand / g.next_cpt;
   const int e2 = b.emb_per_cand ? cand : cand / g.S;
-  for (int p = 0; p < g.next_w; ++p) {
-    const int j = g.next_start + p;
-    const float* src = (j < g.H) ? b.emb + ((size_t)e2 * g.H + j) * D : pcand + (size_t)(j - g.H) * D;
-    const int nr = (cand - ntile * g.next_cpt) * g.next_w + p;
-    prep_layer0_row<D>(w, md, src, p, cand * g.T + j, b.xn + ((size_t)ntile * 128 + nr) * D,
-                       b.a_attn + (size_t)ntile * (D / 64) * kBlkElems, nr, lane, b.mod);
-  }
+  const float* src = new_pred ? pcand + (size_t)g.call * D
+                              : ((j < g.H) ? b.emb + ((size_t)e2 * g.H + j) * D : pcand + (size_t)(j - g.H) * D);
+  const int nr = (cand - ntile * g.next_cpt) * g.next_w + p;
+  prep_layer0_row<D>(w, md, src, p, cand * g.T + j, b.xn + ((size_t)ntile * 128 + nr) * D,
+                     b.a_attn + (size_t)ntile * (D / 64) * kBlkElems, nr, lane, b.mod);
 }
 
 // ---------------------------------------------------------------- shared-memory sizes
@@ -1300,7 +1308,8 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
     if (prof) prof->end(KC_FC2, 2.0 * rows * md.mlp * D, st);
   }
   if (prof) prof->begin(st);
-  LEWM_TRY(launch_k(k_final<D>, dim3((g.n_cand + 3) / 4), dim3(128), 0, st, w, md, g, b));
+  const int final_items = g.n_cand * (g.last ? 1 : g.next_w);
+  LEWM_TRY(launch_k(k_final<D>, dim3((final_items + 3) / 4), dim3(128), 0, st, w, md, g, b));
   if (prof) prof->end(KC_FINAL, 0.0, st);
 #undef LEWM_TRY
   return cudaSuccess;
