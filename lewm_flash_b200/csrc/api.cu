@@ -41,8 +41,6 @@ struct Workspace {
   __nv_bfloat16* mod = nullptr;
   float* x = nullptr;    // two residual buffers: predictor calls alternate between them
   float* x2 = nullptr;
-  __nv_bfloat16* a_attn = nullptr;
-  __nv_bfloat16* a_ffn = nullptr;
   __nv_bfloat16* attn = nullptr;
   __nv_bfloat16* h = nullptr;
   float* pred = nullptr;
@@ -356,8 +354,6 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   const size_t o_mod = carve(rows_e * (size_t)m.L * 6 * m.D * 2);
   const size_t o_x = carve(r.tiles * 128 * (size_t)m.D * 4);
   const size_t o_x2 = carve(r.tiles * 128 * (size_t)m.D * 4);
-  const size_t o_aat = carve(r.tiles * (size_t)(m.D / 64) * 128 * 64 * 2);
-  const size_t o_aff = carve(r.tiles * (size_t)(m.D / 64) * 128 * 64 * 2);
   const size_t o_attn = carve(r.tiles * (size_t)(m.inner / 64) * 128 * 64 * 2);
   const size_t o_h = carve(r.tiles * (size_t)(m.mlp / 64) * 128 * 64 * 2);
   const size_t o_pred = carve(r.n_cand * r.npred * (size_t)m.D * 4);
@@ -385,8 +381,6 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   ws.mod = reinterpret_cast<__nv_bfloat16*>(b + o_mod);
   ws.x = reinterpret_cast<float*>(b + o_x);
   ws.x2 = reinterpret_cast<float*>(b + o_x2);
-  ws.a_attn = reinterpret_cast<__nv_bfloat16*>(b + o_aat);
-  ws.a_ffn = reinterpret_cast<__nv_bfloat16*>(b + o_aff);
   ws.attn = reinterpret_cast<__nv_bfloat16*>(b + o_attn);
   ws.h = reinterpret_cast<__nv_bfloat16*>(b + o_h);
   ws.pred = reinterpret_cast<float*>(b + o_pred);
@@ -415,8 +409,8 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
   const int rows = NC * T;
   LEWM_CK(c, launch_embed(m, c->w, cand, rows, c->ws.eh, c->ws.act_a, c->d_status, st, &c->prof));
   LEWM_CK(c, launch_adaln(m, c->w, rows, c->ws.act_a, c->ws.mod, c->d_status, st, &c->prof));
-  RolloutBufs b{emb, emb_pc, goal, goal_pc, cand, c->ws.act_a, c->ws.mod, c->ws.x, c->ws.x2, c->ws.a_attn,
-                c->ws.a_ffn, c->ws.attn, c->ws.h, c->ws.pred, costs};
+  RolloutBufs b{emb, emb_pc, goal, goal_pc, cand, c->ws.act_a, c->ws.mod, c->ws.x, c->ws.x2, c->ws.attn, c->ws.h,
+                c->ws.pred, costs};
   const int n_calls = T - H + 1;
   auto geom = [&](int k) {
     const int end = H + k;

@@ -91,8 +91,6 @@ struct RolloutBufs {
   __nv_bfloat16* mod;
   float* x;        // residual stream of this call's window, [tiles][128][D]
   float* xn;       // residual stream of the next call's window (k_final writes it)
-  __nv_bfloat16* a_attn;  // bf16 A operand of the QKV GEMM, [tiles][D/64][128x64]
-  __nv_bfloat16* a_ffn;   // bf16 A operand of the FC1 GEMM
   __nv_bfloat16* attn;
   __nv_bfloat16* h;
   float* pred;

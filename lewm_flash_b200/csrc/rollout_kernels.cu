@@ -2,27 +2,26 @@
 //
 // One model-cost evaluation (reference JEPA.get_cost_from_embeddings,
 // lewm/jepa.py:302-317) is:
-//   k_embed   Embedder (lewm/module.py:205-214) + SiLU for every (candidate, time)
+//   k_embed_hidden, k_embed_out
+//             Embedder (lewm/module.py:205-214) + SiLU for every (candidate, time)
 //   k_adaln   AdaLN modulation Linear (lewm/module.py:98-100) for every layer at once;
 //             it depends only on the actions, so it is hoisted out of the
 //             autoregressive chain and computed once per candidate and time step
-//   k_prep0   first predictor call: layer-0 residual (history + position) and its
-//             LN1 -> modulate -> attn.norm operand
+//   k_prep0   first predictor call: layer-0 residual rows (history + position)
 //   per predictor call (lewm/jepa.py:284-298), per layer (lewm/module.py:105-111):
-//     k_qkv_attn   QKV GEMM (one head per CTA) -> causal attention over the window
-//                  (lewm/module.py:75-85)
-//     k_resid_gemm out-proj GEMM + bias, * gate_msa, + residual, then
-//                  LN2 -> modulate -> FFN LayerNorm: the FC1 operand
-//     k_fc1        FC1 GEMM + bias -> GELU
-//     k_resid_gemm FC2 GEMM + bias, * gate_mlp, + residual, then (not after the
-//                  last layer) LN1 -> modulate -> attn.norm: the next QKV operand
+//     k_qkv_attn   LN1 -> modulate -> attn.norm of the residual rows, QKV GEMM (one
+//                  head per CTA), causal attention over the window (lewm/module.py:75-85)
+//     k_resid_gemm out-proj GEMM + bias, * gate_msa, + residual
+//     k_fc1        LN2 -> modulate -> FFN LayerNorm of the residual rows, FC1 GEMM
+//                  + bias -> GELU
+//     k_resid_gemm FC2 GEMM + bias, * gate_mlp, + residual
 //   k_final   final LayerNorm (lewm/module.py:183) on each window's last token,
 //             then score against the goal (cost_from_rollout, lewm/jepa.py:246-260)
-//             or append to the history and prepare the next call's layer-0 rows
+//             or append to the history and write the next call's layer-0 rows
 //
-// GEMMs run on tcgen05 (bf16 in, fp32 accumulate in TMEM); operands arrive in
-// shared memory by bulk copy of pre-swizzled blocks; LayerNorm, modulation,
-// bias, GELU, gates, residuals and the cost are fp32.
+// GEMMs run on tcgen05 (bf16 in, fp32 accumulate in TMEM); weight operands arrive in
+// shared memory by bulk copy of pre-swizzled blocks; LayerNorm, modulation, bias,
+// GELU, gates, residuals and the cost are fp32.
 //
 // Latency structure (a single-env plan is a chain of thousands of small
 // dependent kernels, so every global-memory round trip on a kernel's critical
@@ -31,14 +30,13 @@
 //     griddep_wait() it only initialises barriers, allocates TMEM and starts
 //     bulk copies of weights and per-layer vectors into shared memory, which
 //     overlaps the previous kernel;
-//   * each LayerNorm is computed once per row, by the kernel that produces the
-//     residual; its consumers bulk-load the finished bf16 operand;
-//   * the residual GEMMs are 4-CTA clusters (one N tile each) that combine the
-//     per-row LayerNorm moments through distributed shared memory;
+//   * the LayerNorms of a GEMM operand run in that GEMM's kernel, four threads per
+//     row reducing through shuffles, straight into the swizzled shared-memory tile:
+//     the residual GEMMs need no cross-CTA exchange;
 //   * accumulator columns are split over the four warps that share a TMEM lane
-//     quadrant, attention rows over four threads each;
-//   * in the streamed-K GEMMs a producer warp refills the operand ring while the
-//     MMA warp issues, so issue never waits for an MMA to retire.
+//     quadrant;
+//   * copies are issued one per lane of one warp instruction, and streamed-K GEMMs
+//     move their K blocks in as few instruction rounds as shared memory allows.
 #include <algorithm>
 
 #include "lewm_common.cuh"
@@ -435,80 +433,120 @@ __global__ void __launch_bounds__(kThreads) k_adaln(DevWeights w, ModelDims md, 
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
-// ---------------------------------------------------------------- warp-level row LayerNorm
-// One warp, one row of D columns (lane l holds columns 64*i + 2l, 64*i + 2l + 1).
-// Writes bf16(LN_affine(LN(x) * (1 + scale) + shift)) into row r of a global
-// pre-swizzled [D/64][128 x 64] A tile.
-template <int D>
-__device__ __forceinline__ void warp_ln_mod_ln_store(const float2 (&x)[D / 64], const __nv_bfloat16* __restrict__ shift,
-                                                     const __nv_bfloat16* __restrict__ scale,
-                                                     const float* __restrict__ g, const float* __restrict__ bb,
-                                                     __nv_bfloat16* __restrict__ a_tile, int r, int lane) {
-  constexpr int NP = D / 64;
-  float2 sh[NP], sc[NP], gg[NP], b2[NP];
+// ---------------------------------------------------------------- GEMM operand from the residual
+// A operand of the QKV / FC1 GEMM, built in shared memory from the fp32 residual rows:
+// bf16(LN_{g,b}(LN(x) * (1 + scale) + shift)) with the first LayerNorm at eps 1e-6 and
+// no affine (AdaLN modulate, lewm/module.py:105-111) and the second the attention /
+// feed-forward block's own LayerNorm at eps 1e-5. TPR consecutive threads share a row
+// (a warp covers 32 / TPR rows), D / TPR columns each in 4-column chunks; the row
+// moments reduce through shuffles among them. Rows at or past rows8 are skipped (whole
+// warps: rows8 is a multiple of 8 >= 32 / TPR); window slots without a candidate get
+// zeros.
+template <int D, int TPR>
+__device__ __forceinline__ void build_ln_operand_t(const float* __restrict__ x_tile, const CallGeom& g, int tile,
+                                                   const __nv_bfloat16* __restrict__ mod, int mod_cols, int shift_col,
+                                                   const float* __restrict__ lg, const float* __restrict__ lb,
+                                                   uint8_t* sA, int tid) {
+  constexpr int NPER = D / TPR;   // columns per thread, a multiple of 4
+  constexpr int NCH = NPER / 4;   // 4-column chunks per thread
+  static_assert(NPER % 4 == 0, "4-column chunks");
+  const int part = tid % TPR;
+  for (int r = tid / TPR; r < g.rows8; r += kThreads / TPR) {
+    const RowMap m = map_row(g, tile, r);
+    float xv[NPER];
+    uint2 shv[NCH], scv[NCH];
+    const __nv_bfloat16* mrow = mod + (m.valid ? (size_t)m.tok * mod_cols + shift_col : 0);
+    // chunk k of this thread: columns 4 (part + TPR k) .. + 4 (chunks interleaved over the row)
 #pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    const int c = 64 * i + 2 * lane;
-    sh[i] = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(shift + c));
-    sc[i] = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(scale + c));
-    gg[i] = *reinterpret_cast<const float2*>(g + c);
-    b2[i] = *reinterpret_cast<const float2*>(bb + c);
-  }
-  float s = 0.f;
+    for (int k = 0; k < NCH; ++k) {
+      const int c = 4 * (part + TPR * k);
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      uint2 h = make_uint2(0u, 0u), a = make_uint2(0u, 0u);
+      if (m.valid) {
+        t = *reinterpret_cast<const float4*>(x_tile + (size_t)r * D + c);
+        h = *reinterpret_cast<const uint2*>(mrow + c);
+        a = *reinterpret_cast<const uint2*>(mrow + D + c);
+      }
+      xv[4 * k] = t.x;
+      xv[4 * k + 1] = t.y;
+      xv[4 * k + 2] = t.z;
+      xv[4 * k + 3] = t.w;
+      shv[k] = h;
+      scv[k] = a;
+    }
+    float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < NP; ++i) s += x[i].x + x[i].y;
-  const float mean = warp_sum(s) * (1.0f / D);
-  float q = 0.f;
+    for (int i = 0; i < NPER; ++i) s += xv[i];
 #pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    const float dx = x[i].x - mean, dy = x[i].y - mean;
-    q += dx * dx + dy * dy;
-  }
-  const float rstd = rsqrtf(warp_sum(q) * (1.0f / D) + 1e-6f);
-  float2 y[NP];
-  float s2 = 0.f;
+    for (int o = 1; o < TPR; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s * (1.0f / D);
+    float q = 0.f;
 #pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    y[i].x = (x[i].x - mean) * rstd * (1.0f + sc[i].x) + sh[i].x;
-    y[i].y = (x[i].y - mean) * rstd * (1.0f + sc[i].y) + sh[i].y;
-    s2 += y[i].x + y[i].y;
-  }
-  const float mean2 = warp_sum(s2) * (1.0f / D);
-  float q2 = 0.f;
+    for (int i = 0; i < NPER; ++i) q += (xv[i] - mean) * (xv[i] - mean);
 #pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    const float dx = y[i].x - mean2, dy = y[i].y - mean2;
-    q2 += dx * dx + dy * dy;
-  }
-  const float rstd2 = rsqrtf(warp_sum(q2) * (1.0f / D) + 1e-5f);
-  uint8_t* tile_bytes = reinterpret_cast<uint8_t*>(a_tile);
+    for (int o = 1; o < TPR; o <<= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    const float rstd = rsqrtf(q * (1.0f / D) + 1e-6f);
+    float s2 = 0.f;
 #pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    const float zx = (y[i].x - mean2) * rstd2 * gg[i].x + b2[i].x;
-    const float zy = (y[i].y - mean2) * rstd2 * gg[i].y + b2[i].y;
-    *reinterpret_cast<uint32_t*>(tile_bytes + i * kBlk + sw128_off(r, 2 * lane)) = pack_bf16x2(zx, zy);
+    for (int k = 0; k < NCH; ++k) {
+      const float2 h01 = unpack_bf16x2(shv[k].x), h23 = unpack_bf16x2(shv[k].y);
+      const float2 a01 = unpack_bf16x2(scv[k].x), a23 = unpack_bf16x2(scv[k].y);
+      float* y = xv + 4 * k;
+      y[0] = (y[0] - mean) * rstd * (1.0f + a01.x) + h01.x;
+      y[1] = (y[1] - mean) * rstd * (1.0f + a01.y) + h01.y;
+      y[2] = (y[2] - mean) * rstd * (1.0f + a23.x) + h23.x;
+      y[3] = (y[3] - mean) * rstd * (1.0f + a23.y) + h23.y;
+      s2 += (y[0] + y[1]) + (y[2] + y[3]);
+    }
+#pragma unroll
+    for (int o = 1; o < TPR; o <<= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    const float mean2 = s2 * (1.0f / D);
+    float q2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NPER; ++i) q2 += (xv[i] - mean2) * (xv[i] - mean2);
+#pragma unroll
+    for (int o = 1; o < TPR; o <<= 1) q2 += __shfl_xor_sync(0xffffffffu, q2, o);
+    const float rstd2 = rsqrtf(q2 * (1.0f / D) + 1e-5f);
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      const int c = 4 * (part + TPR * k);
+      const float4 g4 = *reinterpret_cast<const float4*>(lg + c);
+      const float4 b4 = *reinterpret_cast<const float4*>(lb + c);
+      const float* y = xv + 4 * k;
+      uint2 pk = make_uint2(0u, 0u);
+      if (m.valid) {
+        pk.x = pack_bf16x2((y[0] - mean2) * rstd2 * g4.x + b4.x, (y[1] - mean2) * rstd2 * g4.y + b4.y);
+        pk.y = pack_bf16x2((y[2] - mean2) * rstd2 * g4.z + b4.z, (y[3] - mean2) * rstd2 * g4.w + b4.w);
+      }
+      *reinterpret_cast<uint2*>(sA + (c >> 6) * kBlk + sw128_off(r, c & 63)) = pk;
+    }
   }
 }
 
-// Layer-0 residual x0 = history row + position embedding of window position p, and
-// its A operand (LN1, modulate with layer-0 shift/scale of the token, attn.norm).
+// Sixteen threads per row for every tile size: all 16 warps work on the first 32 used
+// rows, and larger tiles loop over further 32-row passes. The reduction order of the row
+// moments is then the same for every tile geometry, so an env's results do not depend
+// on how many candidates share its call.
 template <int D>
-__device__ __forceinline__ void prep_layer0_row(const DevWeights& w, const ModelDims& md, const float* __restrict__ src,
-                                                int p, int tok, float* __restrict__ xdst,
-                                                __nv_bfloat16* __restrict__ a_tile, int r, int lane,
-                                                const __nv_bfloat16* __restrict__ mod) {
+__device__ __forceinline__ void build_ln_operand(const float* __restrict__ x_tile, const CallGeom& g, int tile,
+                                                 const __nv_bfloat16* __restrict__ mod, int mod_cols, int shift_col,
+                                                 const float* __restrict__ lg, const float* __restrict__ lb,
+                                                 uint8_t* sA, int tid) {
+  build_ln_operand_t<D, 16>(x_tile, g, tile, mod, mod_cols, shift_col, lg, lb, sA, tid);
+}
+
+// Layer-0 residual row x0 = history row + position embedding of window position p.
+template <int D>
+__device__ __forceinline__ void prep_layer0_row(const DevWeights& w, const float* __restrict__ src, int p,
+                                                float* __restrict__ xdst, int lane) {
   constexpr int NP = D / 64;
-  float2 x[NP];
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
     const int c = 64 * i + 2 * lane;
     const float2 a = *reinterpret_cast<const float2*>(src + c);
     const float2 pe = *reinterpret_cast<const float2*>(w.pos + p * D + c);
-    x[i] = make_float2(a.x + pe.x, a.y + pe.y);
-    *reinterpret_cast<float2*>(xdst + c) = x[i];
+    *reinterpret_cast<float2*>(xdst + c) = make_float2(a.x + pe.x, a.y + pe.y);
   }
-  const __nv_bfloat16* mrow = mod + (size_t)tok * (md.L * 6 * D);
-  warp_ln_mod_ln_store<D>(x, mrow, mrow + D, w.attn_ln_w, w.attn_ln_b, a_tile, r, lane);
 }
 
 // ---------------------------------------------------------------- first-call layer-0 inputs
@@ -526,9 +564,7 @@ __global__ void __launch_bounds__(128) k_prep0(DevWeights w, ModelDims md, CallG
   const int e = b.emb_per_cand ? cand : cand / g.S;
   const int tile = cand / g.cpt;
   const int r = (cand - tile * g.cpt) * g.w + p;
-  prep_layer0_row<D>(w, md, b.emb + ((size_t)e * g.H + j) * D, p, cand * g.T + j,
-                     b.x + ((size_t)tile * 128 + r) * D, b.a_attn + (size_t)tile * (D / 64) * kBlkElems, r, lane,
-                     b.mod);
+  prep_layer0_row<D>(w, b.emb + ((size_t)e * g.H + j) * D, p, b.x + ((size_t)tile * 128 + r) * D, lane);
 }
 
 // ---------------------------------------------------------------- QKV + attention
@@ -555,8 +591,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
   uint64_t* empty = full + ST;
   uint64_t* bar_mma = empty + ST;
-  uint64_t* bar_a = bar_mma + 1;  // [KB]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + KB);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x, head = blockIdx.y;
@@ -568,7 +603,6 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
       mbar_init(&empty[s], 1);
     }
     mbar_init(bar_mma, 1);
-    for (int kb = 0; kb < KB; ++kb) mbar_init(&bar_a[kb], 1);
     fence_mbar_init();
   }
   __syncwarp();
@@ -584,10 +618,10 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   griddep_wait();
   LEWM_STAMP(2, 2);
   griddep_launch();
-  if (warp == 0 && lane < KB) {  // the A operand was written, normalized and swizzled, by the producer of x
-    mbar_arrive_expect_tx(&bar_a[lane], g.rows8 * 128);
-    bulk_g2s(sA + lane * kBlk, b.a_attn + ((size_t)tile * KB + lane) * kBlkElems, g.rows8 * 128, &bar_a[lane]);
-  }
+  // A operand: LN1 -> modulate (shift/scale_msa of this layer) -> attn.norm of the residual rows.
+  build_ln_operand<D>(b.x + (size_t)tile * 128 * D, g, tile, b.mod, md.L * 6 * D, layer * 6 * D, w.attn_ln_w + layer * D,
+                      w.attn_ln_b + layer * D, sA, tid);
+  fence_async_smem();
   LEWM_STAMP(2, 5);
   tc_fence_before();
   __syncthreads();
@@ -597,9 +631,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     const uint32_t idesc = idesc_bf16(128, 192);
     for (int kb = 0; kb < KB; ++kb) {
       const int s = kb % ST;
-      if (!__all_sync(0xffffffffu, mbar_wait(&bar_a[kb], 0, status) &&
-                                       mbar_wait(&full[s], (kb / ST) & 1, status)))
-        break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (kb / ST) & 1, status))) break;
       tc_fence_after();
       if (lane == 0) {
 #pragma unroll
@@ -741,25 +773,17 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
 // Bytes after the operand slots: vectors [3][NT], per-slice moments [4][128] float2,
 // cluster exchange [2][4][128] float2, 5 barriers, the TMEM slot.
 template <int D>
-__host__ __device__ constexpr int resid_extra() { return 3 * Cfg<D>::NT_OUT * 4 + 4 * 128 * 8 + 2 * 4 * 128 * 8 + 8 * 5 + 16; }
+__host__ __device__ constexpr int resid_extra() { return Cfg<D>::NT_OUT * 4 + 8 * 5 + 16; }
 // What the epilogue of an out-projection / FC2 launch does with its N tile.
 struct ResidEpi {
   const float* bias;      // [D] of this GEMM
   int gate_chunk;         // mod chunk of the gate (2: gate_msa, 5: gate_mlp) of `layer`
-  __nv_bfloat16* a_out;   // A operand of the next GEMM, or null (last FC2)
-  int ln_layer;           // layer whose shift/scale modulate the next LayerNorm
-  int ln_chunk;           // mod chunk of that shift (scale = chunk + 1)
-  const float* ln_g;      // [D] affine of the second LayerNorm
-  const float* ln_b;
 };
 
 // x[:, n-tile] += gate * (A . B^T + bias); A streamed from pre-swizzled global tiles.
-// Launched as 4-CTA clusters, one per row tile (cluster rank = N tile). When a_out is
-// set, the epilogue also produces the next GEMM's A operand for its columns:
-// LN(x) (eps 1e-6) -> * (1 + scale) + shift -> LN (eps 1e-5) * g + b -> bf16. The
-// per-row moments of the 4 N tiles are combined through distributed shared memory
-// (Chan et al. parallel variance merge), one cluster barrier per LayerNorm.
-// Warp 0 issues MMAs, warp 1 refills the operand ring.
+// Four CTAs per row tile (one N tile each), independent: the LayerNorm of the next
+// GEMM's operand is built by that GEMM's kernel from the updated rows. Warp 0 issues
+// MMAs, warp 1 refills the operand slots.
 template <int D>
 __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __restrict__ gA, int nkb,
                                                          const __nv_bfloat16* __restrict__ gB, ResidEpi ep, CallGeom g,
@@ -774,18 +798,15 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
   const int G = lay.G;
   uint8_t* sA = smem;
   uint8_t* sB = smem + lay.b_off;
-  float* svec = reinterpret_cast<float*>(smem + lay.v_off);  // [bias NT][ln_g NT][ln_b NT]
-  float2* red2 = reinterpret_cast<float2*>(svec + 3 * NT);     // [4 slices][128] (mean, M2)
-  float2* xch = red2 + 4 * 128;                                // [2 rounds][4 ranks][128]
-  uint64_t* full = reinterpret_cast<uint64_t*>(xch + 2 * 4 * 128);
+  float* svec = reinterpret_cast<float*>(smem + lay.v_off);  // [bias NT]
+  uint64_t* full = reinterpret_cast<uint64_t*>(svec + NT);
   uint64_t* empty = full + 2;
   uint64_t* bar_mma = empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int skind = ep.gate_chunk == 2 ? 5 : 3;  // diagnostic stamp stream: out-proj / FC2
   (void)skind;
-  const int tile = blockIdx.x, nt = blockIdx.y;  // nt == cluster rank
-  const bool do_ln = ep.a_out != nullptr;
+  const int tile = blockIdx.x, nt = blockIdx.y;
   const KStream<B_BLK> ks{sA, sB, full, empty, gA + (size_t)tile * nkb * kBlkElems, (size_t)kBlkElems,
                           gB + (size_t)nt * nkb * NT * 64, (size_t)NT * 64, (uint32_t)g.rows8 * 128,
                           (uint32_t)lay.a_stride, nkb, G};
@@ -796,21 +817,17 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
     }
     mbar_init(bar_mma, 1);
     fence_mbar_init();
-    mbar_arrive_expect_tx(&full[0], ks.bytes(0) + (do_ln ? 3 : 1) * NT * 4);
+    mbar_arrive_expect_tx(&full[0], ks.bytes(0) + NT * 4);
     if (ks.groups() > 1) mbar_arrive_expect_tx(&full[1], ks.bytes(1));
   }
   __syncwarp();
-  // Weights and vectors first (they do not depend on the previous kernel), in one
-  // instruction of warp 0 (K blocks on lanes below 2G <= 32, vectors on lanes 29-31,
-  // which K blocks never use when 2G > 29 because then G >= nkb and one group
-  // covers lanes below nkb <= 16).
+  // Weights and bias first (they do not depend on the previous kernel), in one
+  // instruction of warp 0 (K blocks on lanes below 2G <= 32, the bias on lane 31, which
+  // K blocks never use because 2G > 31 only when G >= nkb and one group covers lanes
+  // below nkb <= 16).
   if (warp == 0) {
-    if (lane == 29)
+    if (lane == 31)
       bulk_g2s(svec, ep.bias + nt * NT, NT * 4, &full[0]);
-    else if (lane == 30 && do_ln)
-      bulk_g2s(svec + NT, ep.ln_g + nt * NT, NT * 4, &full[0]);
-    else if (lane == 31 && do_ln)
-      bulk_g2s(svec + 2 * NT, ep.ln_b + nt * NT, NT * 4, &full[0]);
     else
       ks.issue_first(lane, false);
   }
@@ -819,7 +836,6 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
     tmem_alloc(tmem_slot, C::TMEM_OUT);
     tmem_relinquish();
   }
-  cluster_sync();  // every CTA of the cluster is running before any distributed shared-memory access
   LEWM_STAMP(skind, 1);
   griddep_wait();
   LEWM_STAMP(skind, 2);
@@ -841,32 +857,23 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
   const int quad = warp & 3, slice = warp >> 2;
   const int r = quad * 32 + lane;
   const RowMap m = map_row(g, tile, r);
-  // Residual, gate and the next LayerNorm's shift/scale do not depend on the MMA:
-  // load them while it runs.
+  // Residual and gate do not depend on the MMA: load them while it runs.
   const int c0 = nt * NT + slice * CW;
   float* xrow = b.x + ((size_t)tile * 128 + r) * D + c0;
   float4 xv[CW / 4];
-  uint2 gt[CW / 4], sh[CW / 4], sc[CW / 4];
+  uint2 gt[CW / 4];
   if (m.valid) {
-    const __nv_bfloat16* mrow = b.mod + (size_t)m.tok * (md.L * 6 * D);
-    const __nv_bfloat16* gate = mrow + layer * 6 * D + ep.gate_chunk * D + c0;
-    const __nv_bfloat16* shp = mrow + ep.ln_layer * 6 * D + ep.ln_chunk * D + c0;
+    const __nv_bfloat16* gate = b.mod + (size_t)m.tok * (md.L * 6 * D) + layer * 6 * D + ep.gate_chunk * D + c0;
 #pragma unroll
     for (int i = 0; i < CW / 4; ++i) {
       xv[i] = *reinterpret_cast<const float4*>(xrow + 4 * i);
       gt[i] = *reinterpret_cast<const uint2*>(gate + 4 * i);
-      if (do_ln) {
-        sh[i] = *reinterpret_cast<const uint2*>(shp + 4 * i);
-        sc[i] = *reinterpret_cast<const uint2*>(shp + D + 4 * i);
-      } else {
-        sh[i] = sc[i] = make_uint2(0u, 0u);
-      }
     }
   } else {
 #pragma unroll
     for (int i = 0; i < CW / 4; ++i) {
       xv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-      gt[i] = sh[i] = sc[i] = make_uint2(0u, 0u);
+      gt[i] = make_uint2(0u, 0u);
     }
   }
   const bool ok = cta_wait_mma(bar_mma, status, tmem_slot + 1);
@@ -877,7 +884,7 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
   float v[CW];
   tmem_ld_cols<CW>(taddr, v);
   LEWM_STAMP(skind, 7);
-  {
+  if (ok && m.valid) {
     const float* bs = svec + slice * CW;
 #pragma unroll
     for (int i = 0; i < CW / 4; ++i) {
@@ -887,89 +894,12 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
       xv[i].y += g01.y * (v[4 * i + 1] + b4.y);
       xv[i].z += g23.x * (v[4 * i + 2] + b4.z);
       xv[i].w += g23.y * (v[4 * i + 3] + b4.w);
-      if (ok && m.valid) *reinterpret_cast<float4*>(xrow + 4 * i) = xv[i];
-    }
-  }
-  if (do_ln) {
-    float z[CW];
-#pragma unroll
-    for (int i = 0; i < CW / 4; ++i) {
-      z[4 * i] = xv[i].x;
-      z[4 * i + 1] = xv[i].y;
-      z[4 * i + 2] = xv[i].z;
-      z[4 * i + 3] = xv[i].w;
-    }
-    const int rank = nt;
-#pragma unroll
-    for (int round = 0; round < 2; ++round) {
-      // (mean, M2) of this thread's CW columns in registers, then of the CTA's NT columns
-      // of row r: Chan merge of the four column slices, which live in the four warps
-      // sharing this TMEM lane quadrant, behind a named barrier of those 128 threads.
-      float mt = 0.f;
-#pragma unroll
-      for (int i = 0; i < CW; ++i) mt += z[i];
-      mt *= 1.0f / CW;
-      float qt = 0.f;
-#pragma unroll
-      for (int i = 0; i < CW; ++i) qt += (z[i] - mt) * (z[i] - mt);
-      red2[slice * 128 + r] = make_float2(mt, qt);
-      named_barrier_sync(1 + quad, 128);
-      if (slice == 0) {
-        const float2 p0 = red2[r], p1 = red2[128 + r], p2 = red2[256 + r], p3 = red2[384 + r];
-        const float mean_c = (p0.x + p1.x + p2.x + p3.x) * 0.25f;
-        const float m2_c = p0.y + p1.y + p2.y + p3.y +
-                           CW * ((p0.x - mean_c) * (p0.x - mean_c) + (p1.x - mean_c) * (p1.x - mean_c) +
-                                 (p2.x - mean_c) * (p2.x - mean_c) + (p3.x - mean_c) * (p3.x - mean_c));
-        const float2 mv = make_float2(mean_c, m2_c);
-#pragma unroll
-        for (int peer = 0; peer < 4; ++peer) st_dsmem_f2(xch + (round * 4 + rank) * 128 + r, peer, mv);
-      }
-      LEWM_STAMP(skind, round == 0 ? 9 : 0);
-      cluster_sync();
-      if (round == 0) LEWM_STAMP(skind, 8);
-      float mean = 0.f;
-      float2 part[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        part[k] = xch[(round * 4 + k) * 128 + r];
-        mean += part[k].x;
-      }
-      mean *= 0.25f;
-      float m2 = 0.f;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) m2 += part[k].y + NT * (part[k].x - mean) * (part[k].x - mean);
-      const float rstd = rsqrtf(m2 * (1.0f / D) + (round == 0 ? 1e-6f : 1e-5f));
-      if (round == 0) {
-#pragma unroll
-        for (int i = 0; i < CW / 4; ++i) {
-          const float2 s01 = unpack_bf16x2(sh[i].x), s23 = unpack_bf16x2(sh[i].y);
-          const float2 k01 = unpack_bf16x2(sc[i].x), k23 = unpack_bf16x2(sc[i].y);
-          z[4 * i] = (z[4 * i] - mean) * rstd * (1.0f + k01.x) + s01.x;
-          z[4 * i + 1] = (z[4 * i + 1] - mean) * rstd * (1.0f + k01.y) + s01.y;
-          z[4 * i + 2] = (z[4 * i + 2] - mean) * rstd * (1.0f + k23.x) + s23.x;
-          z[4 * i + 3] = (z[4 * i + 3] - mean) * rstd * (1.0f + k23.y) + s23.y;
-        }
-      } else if (ok && m.valid) {
-        const float* gg = svec + NT + slice * CW;
-        const float* bb = svec + 2 * NT + slice * CW;
-        uint8_t* at = reinterpret_cast<uint8_t*>(ep.a_out + (size_t)tile * (D / 64) * kBlkElems);
-#pragma unroll
-        for (int i = 0; i < CW / 4; ++i) {
-          const int c = c0 + 4 * i;
-          uint2 pk;
-          pk.x = pack_bf16x2((z[4 * i] - mean) * rstd * gg[4 * i] + bb[4 * i],
-                             (z[4 * i + 1] - mean) * rstd * gg[4 * i + 1] + bb[4 * i + 1]);
-          pk.y = pack_bf16x2((z[4 * i + 2] - mean) * rstd * gg[4 * i + 2] + bb[4 * i + 2],
-                             (z[4 * i + 3] - mean) * rstd * gg[4 * i + 3] + bb[4 * i + 3]);
-          *reinterpret_cast<uint2*>(at + (c >> 6) * kBlk + sw128_off(r, c & 63)) = pk;
-        }
-      }
+      *reinterpret_cast<float4*>(xrow + 4 * i) = xv[i];
     }
   }
   LEWM_STAMP(skind, 6);
   tc_fence_before();
   __syncthreads();
-  __syncwarp();
   if (warp == 0) tmem_dealloc(tmem, C::TMEM_OUT);
 }
 
@@ -998,8 +928,7 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   uint64_t* full = reinterpret_cast<uint64_t*>(svec + NT);
   uint64_t* empty = full + ST;
   uint64_t* bar_mma = empty + ST;
-  uint64_t* bar_a = bar_mma + 1;  // [KB]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + KB);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   LEWM_STAMP(4, 0);
   const int tile = blockIdx.x, nt = blockIdx.y;
@@ -1012,7 +941,6 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
       mbar_init(&empty[s], 1);
     }
     mbar_init(bar_mma, 1);
-    for (int kb = 0; kb < KB; ++kb) mbar_init(&bar_a[kb], 1);
     fence_mbar_init();
     mbar_arrive_expect_tx(&full[0], B_BLK + NT * 4);
     for (int s = 1; s < ST; ++s) mbar_arrive_expect_tx(&full[s], B_BLK);
@@ -1032,10 +960,10 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   griddep_wait();
   LEWM_STAMP(4, 2);
   griddep_launch();
-  if (warp == 0 && lane < KB) {  // one copy per lane
-    mbar_arrive_expect_tx(&bar_a[lane], g.rows8 * 128);
-    bulk_g2s(sA + lane * kBlk, b.a_ffn + ((size_t)tile * KB + lane) * kBlkElems, g.rows8 * 128, &bar_a[lane]);
-  }
+  // A operand: LN2 -> modulate (shift/scale_mlp of this layer) -> ffn.norm of the residual rows.
+  build_ln_operand<D>(b.x + (size_t)tile * 128 * D, g, tile, b.mod, md.L * 6 * D, layer * 6 * D + 3 * D,
+                      w.ffn_ln_w + layer * D, w.ffn_ln_b + layer * D, sA, tid);
+  fence_async_smem();
   LEWM_STAMP(4, 5);
   tc_fence_before();
   __syncthreads();
@@ -1045,9 +973,7 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
     const uint32_t idesc = idesc_bf16(128, NT);
     for (int kb = 0; kb < KB; ++kb) {
       const int s = kb % ST;
-      if (!__all_sync(0xffffffffu, mbar_wait(&bar_a[kb], 0, status) &&
-                                       mbar_wait(&full[s], (kb / ST) & 1, status)))
-        break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (kb / ST) & 1, status))) break;
       tc_fence_after();
       if (lane == 0) {
 #pragma unroll
@@ -1180,8 +1106,7 @@ __global__ void __launch_bounds__(128) k_final(DevWeights w, ModelDims md, CallG
   const float* src = new_pred ? pcand + (size_t)g.call * D
                               : ((j < g.H) ? b.emb + ((size_t)e2 * g.H + j) * D : pcand + (size_t)(j - g.H) * D);
   const int nr = (cand - ntile * g.next_cpt) * g.next_w + p;
-  prep_layer0_row<D>(w, md, src, p, cand * g.T + j, b.xn + ((size_t)ntile * 128 + nr) * D,
-                     b.a_attn + (size_t)ntile * (D / 64) * kBlkElems, nr, lane, b.mod);
+  prep_layer0_row<D>(w, src, p, b.xn + ((size_t)ntile * 128 + nr) * D, lane);
 }
 
 // ---------------------------------------------------------------- shared-memory sizes
@@ -1281,11 +1206,11 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
                       status));
     if (prof) prof->end(KC_QKV_ATTN, 2.0 * rows * D * 3 * md.inner + 4.0 * rows * g.w * md.inner, st);
     // out-projection: residual with gate_msa, then LN2 / modulate(mlp) / FFN LayerNorm -> FC1 operand
-    const ResidEpi ep_out{w.out_b + l * D, 2, b.a_ffn, l, 3, w.ffn_ln_w + l * D, w.ffn_ln_b + l * D};
+    const ResidEpi ep_out{w.out_b + l * D, 2};
     if (prof) prof->begin(st);
-    LEWM_TRY(launch_kc(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads),
-                       resid_layout(g.rows8, nkb_inner, Cfg<D>::NT_OUT * 128, Cfg<D>::KG, resid_extra<D>()).bytes, st,
-                       dim3(1, 4, 1), (const __nv_bfloat16*)b.attn, nkb_inner,
+    LEWM_TRY(launch_k(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads),
+                      resid_layout(g.rows8, nkb_inner, Cfg<D>::NT_OUT * 128, Cfg<D>::KG, resid_extra<D>()).bytes, st,
+                      (const __nv_bfloat16*)b.attn, nkb_inner,
                        (const __nv_bfloat16*)(w.wout + (size_t)l * 4 * nkb_inner * Cfg<D>::NT_OUT * 64), ep_out, g,
                        b, md, l, status));
     if (prof) prof->end(KC_OUT, 2.0 * rows * md.inner * D, st);
@@ -1295,14 +1220,11 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
                       status));
     if (prof) prof->end(KC_FC1, 2.0 * rows * D * md.mlp, st);
     // FC2: residual with gate_mlp, then (not after the last layer) LN1 / modulate(msa of l+1) / attn.norm
-    const bool more = l + 1 < md.L;
-    const int nl = more ? l + 1 : l;
-    const ResidEpi ep_fc2{w.b2 + l * D, 5, more ? b.a_attn : nullptr, nl, 0, w.attn_ln_w + nl * D,
-                          w.attn_ln_b + nl * D};
+    const ResidEpi ep_fc2{w.b2 + l * D, 5};
     if (prof) prof->begin(st);
-    LEWM_TRY(launch_kc(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads),
-                       resid_layout(g.rows8, nkb_mlp, Cfg<D>::NT_OUT * 128, Cfg<D>::KG, resid_extra<D>()).bytes, st,
-                       dim3(1, 4, 1), (const __nv_bfloat16*)b.h, nkb_mlp,
+    LEWM_TRY(launch_k(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads),
+                      resid_layout(g.rows8, nkb_mlp, Cfg<D>::NT_OUT * 128, Cfg<D>::KG, resid_extra<D>()).bytes, st,
+                      (const __nv_bfloat16*)b.h, nkb_mlp,
                        (const __nv_bfloat16*)(w.w2 + (size_t)l * 4 * nkb_mlp * Cfg<D>::NT_OUT * 64), ep_fc2, g, b,
                        md, l, status));
     if (prof) prof->end(KC_FC2, 2.0 * rows * md.mlp * D, st);
