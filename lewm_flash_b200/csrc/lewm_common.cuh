@@ -180,26 +180,6 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float* v) {
   tmem_ld_wait();
 }
 
-// Barrier over `nthreads` threads (whole warps) that use barrier `id` (1..15; 0 is
-// __syncthreads).
-__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-
-// ----------------------------------------------------------------- thread-block clusters
-// Barrier over every thread of every CTA in the cluster; orders distributed
-// shared-memory stores before it with loads after it.
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// Store a float2 into the shared memory of CTA `rank` of this cluster, at the
-// address `local` has in the executing CTA.
-__device__ __forceinline__ void st_dsmem_f2(const void* local, uint32_t rank, float2 v) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(remote), "f"(v.x), "f"(v.y) : "memory");
-}
-
 // ----------------------------------------------------------------- programmatic dependent launch
 // Kernels launched with programmatic stream serialization may start before their
 // predecessor finishes; everything that reads the predecessor's output must come

@@ -157,23 +157,16 @@ inline bool pdl_enabled() {
   }();
   return on && !pdl_suppressed();
 }
+// Launch with programmatic stream serialization (unless disabled or profiling).
 template <typename... KArgs, typename... Args>
-cudaError_t launch_kc(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, dim3 cluster,
-                      Args&&... args) {
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute at[2];
+  cudaLaunchAttribute at[1];
   int n = 0;
-  if (cluster.x * cluster.y * cluster.z > 1) {
-    at[n].id = cudaLaunchAttributeClusterDimension;
-    at[n].val.clusterDim.x = cluster.x;
-    at[n].val.clusterDim.y = cluster.y;
-    at[n].val.clusterDim.z = cluster.z;
-    ++n;
-  }
   if (pdl_enabled()) {
     at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[n].val.programmaticStreamSerializationAllowed = 1;
@@ -183,10 +176,6 @@ cudaError_t launch_kc(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
   cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
-template <typename... KArgs, typename... Args>
-cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
-  return launch_kc(kern, grid, block, smem, st, dim3(1, 1, 1), std::forward<Args>(args)...);
-}
 
 // Launchers (rollout_kernels.cu). All asynchronous on `st`; `prof` may be null.
 cudaError_t launch_embed(const ModelDims& md, const DevWeights& w, const float* cand, int rows, __nv_bfloat16* eh,
@@ -195,8 +184,7 @@ cudaError_t launch_adaln(const ModelDims& md, const DevWeights& w, int rows, con
                          __nv_bfloat16* mod, uint32_t* status, cudaStream_t st, Prof* prof);
 cudaError_t launch_call(const ModelDims& md, const DevWeights& w, const CallGeom& g, const RolloutBufs& b,
                         uint32_t* status, cudaStream_t st, Prof* prof);
-// Layer-0 inputs (residual x0 = history + position, and its LN1/modulate/LN A
-// operand) of the first predictor call of a rollout.
+// Layer-0 residual rows (history + position) of the first predictor call of a rollout.
 cudaError_t launch_prep0(const ModelDims& md, const DevWeights& w, const CallGeom& g, const RolloutBufs& b,
                          cudaStream_t st, Prof* prof);
 

@@ -769,9 +769,8 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
-// ---------------------------------------------------------------- streamed-K GEMM, residual + LayerNorm epilogue
-// Bytes after the operand slots: vectors [3][NT], per-slice moments [4][128] float2,
-// cluster exchange [2][4][128] float2, 5 barriers, the TMEM slot.
+// ---------------------------------------------------------------- streamed-K GEMM, residual epilogue
+// Bytes after the operand slots: the bias [NT], 5 barriers, the TMEM slot and a flag.
 template <int D>
 __host__ __device__ constexpr int resid_extra() { return Cfg<D>::NT_OUT * 4 + 8 * 5 + 16; }
 // What the epilogue of an out-projection / FC2 launch does with its N tile.
