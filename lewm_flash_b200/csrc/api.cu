@@ -41,6 +41,9 @@ struct Workspace {
   __nv_bfloat16* mod = nullptr;
   float* x = nullptr;    // two residual buffers: predictor calls alternate between them
   float* x2 = nullptr;
+  float* xs = nullptr;   // residual after the attention half of a layer
+  float* part = nullptr; // K-split partial sums of the residual-branch GEMMs, two halves
+  size_t part_stride = 0;
   __nv_bfloat16* attn = nullptr;
   __nv_bfloat16* h = nullptr;
   float* pred = nullptr;
@@ -354,6 +357,8 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   const size_t o_mod = carve(rows_e * (size_t)m.L * 6 * m.D * 2);
   const size_t o_x = carve(r.tiles * 128 * (size_t)m.D * 4);
   const size_t o_x2 = carve(r.tiles * 128 * (size_t)m.D * 4);
+  const size_t o_xs = carve(r.tiles * 128 * (size_t)m.D * 4);
+  const size_t o_part = carve(2 * r.tiles * 128 * (size_t)m.D * 4);
   const size_t o_attn = carve(r.tiles * (size_t)(m.inner / 64) * 128 * 64 * 2);
   const size_t o_h = carve(r.tiles * (size_t)(m.mlp / 64) * 128 * 64 * 2);
   const size_t o_pred = carve(r.n_cand * r.npred * (size_t)m.D * 4);
@@ -381,6 +386,9 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   ws.mod = reinterpret_cast<__nv_bfloat16*>(b + o_mod);
   ws.x = reinterpret_cast<float*>(b + o_x);
   ws.x2 = reinterpret_cast<float*>(b + o_x2);
+  ws.xs = reinterpret_cast<float*>(b + o_xs);
+  ws.part = reinterpret_cast<float*>(b + o_part);
+  ws.part_stride = r.tiles * 128 * (size_t)m.D;
   ws.attn = reinterpret_cast<__nv_bfloat16*>(b + o_attn);
   ws.h = reinterpret_cast<__nv_bfloat16*>(b + o_h);
   ws.pred = reinterpret_cast<float*>(b + o_pred);
@@ -409,7 +417,8 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
   const int rows = NC * T;
   LEWM_CK(c, launch_embed(m, c->w, cand, rows, c->ws.eh, c->ws.act_a, c->d_status, st, &c->prof));
   LEWM_CK(c, launch_adaln(m, c->w, rows, c->ws.act_a, c->ws.mod, c->d_status, st, &c->prof));
-  RolloutBufs b{emb, emb_pc, goal, goal_pc, cand, c->ws.act_a, c->ws.mod, c->ws.x, c->ws.x2, c->ws.attn, c->ws.h,
+  RolloutBufs b{emb,        emb_pc,    goal,      goal_pc, cand,      c->ws.act_a, c->ws.mod,
+                c->ws.x,    c->ws.x2,  c->ws.xs,  c->ws.part, c->ws.part_stride, c->ws.attn, c->ws.h,
                 c->ws.pred, costs};
   const int n_calls = T - H + 1;
   auto geom = [&](int k) {

@@ -89,8 +89,11 @@ struct RolloutBufs {
   const float* cand;  // (NC,T,A)
   __nv_bfloat16* act_a;
   __nv_bfloat16* mod;
-  float* x;        // residual stream of this call's window, [tiles][128][D]
+  float* x;        // residual stream of this call's window before each layer, [tiles][128][D]
   float* xn;       // residual stream of the next call's window (k_final writes it)
+  float* xs;       // residual after the attention half of a layer, [tiles][128][D]
+  float* part;     // K-split partial sums of the last residual GEMM, [2][tiles][128][D]
+  size_t part_stride;  // floats between the two K halves of `part`
   __nv_bfloat16* attn;
   __nv_bfloat16* h;
   float* pred;

@@ -11,10 +11,11 @@
 //   per predictor call (lewm/jepa.py:284-298), per layer (lewm/module.py:105-111):
 //     k_qkv_attn   LN1 -> modulate -> attn.norm of the residual rows, QKV GEMM (one
 //                  head per CTA), causal attention over the window (lewm/module.py:75-85)
-//     k_resid_gemm out-proj GEMM + bias, * gate_msa, + residual
-//     k_fc1        LN2 -> modulate -> FFN LayerNorm of the residual rows, FC1 GEMM
-//                  + bias -> GELU
-//     k_resid_gemm FC2 GEMM + bias, * gate_mlp, + residual
+//     k_partial_gemm  out-proj GEMM, two K halves written as partial sums
+//     k_fc1        residual update r + gate_msa * (out-proj + bias), then LN2 -> modulate
+//                  -> FFN LayerNorm, FC1 GEMM + bias -> GELU
+//     k_partial_gemm  FC2 GEMM partial sums; its residual update is applied by the next
+//                  layer's k_qkv_attn (or by k_final after the last layer)
 //   k_final   final LayerNorm (lewm/module.py:183) on each window's last token,
 //             then score against the goal (cost_from_rollout, lewm/jepa.py:246-260)
 //             or append to the history and write the next call's layer-0 rows
@@ -442,8 +443,20 @@ __global__ void __launch_bounds__(kThreads) k_adaln(DevWeights w, ModelDims md, 
 // moments reduce through shuffles among them. Rows at or past rows8 are skipped (whole
 // warps: rows8 is a multiple of 8 >= 32 / TPR); window slots without a candidate get
 // zeros.
+// A residual update still pending when a GEMM operand is built: the K-split residual
+// GEMM wrote two partial sums P0, P1, and the residual is r = src + gate * ((P0 + P1) +
+// bias). With bias == nullptr the rows of src are used as they are.
+struct ResidUpdate {
+  const float* src;     // [tile rows][D] residual before the update (or the final rows)
+  const float* part;    // partial sums of the tile, K half 1 at + part_stride
+  size_t part_stride;
+  const float* bias;    // [D] bias of that GEMM, or null: no pending update
+  int gate_off;         // mod column of its gate (layer * 6D + chunk * D)
+  float* dst;           // [tile rows][D] where the updated rows are written, or null
+};
+
 template <int D, int TPR>
-__device__ __forceinline__ void build_ln_operand_t(const float* __restrict__ x_tile, const CallGeom& g, int tile,
+__device__ __forceinline__ void build_ln_operand_t(const ResidUpdate& u, const CallGeom& g, int tile,
                                                    const __nv_bfloat16* __restrict__ mod, int mod_cols, int shift_col,
                                                    const float* __restrict__ lg, const float* __restrict__ lb,
                                                    uint8_t* sA, int tid) {
@@ -455,17 +468,31 @@ __device__ __forceinline__ void build_ln_operand_t(const float* __restrict__ x_t
     const RowMap m = map_row(g, tile, r);
     float xv[NPER];
     uint2 shv[NCH], scv[NCH];
-    const __nv_bfloat16* mrow = mod + (m.valid ? (size_t)m.tok * mod_cols + shift_col : 0);
-    // chunk k of this thread: columns 4 (part + TPR k) .. + 4 (chunks interleaved over the row)
+    const size_t mbase = m.valid ? (size_t)m.tok * mod_cols : 0;
+    const __nv_bfloat16* mrow = mod + (m.valid ? mbase + shift_col : 0);
+    // All loads of the row first, through the read-only path (none of these buffers is
+    // written by this kernel: the updated rows go to u.dst, never u.src), then the
+    // update and its write-back, so no load waits behind a store.
+    float4 pa[NCH], pb[NCH], bb[NCH];
+    uint2 gw[NCH];
 #pragma unroll
     for (int k = 0; k < NCH; ++k) {
       const int c = 4 * (part + TPR * k);
       float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
       uint2 h = make_uint2(0u, 0u), a = make_uint2(0u, 0u);
+      pa[k] = pb[k] = bb[k] = t;
+      gw[k] = h;
       if (m.valid) {
-        t = *reinterpret_cast<const float4*>(x_tile + (size_t)r * D + c);
-        h = *reinterpret_cast<const uint2*>(mrow + c);
-        a = *reinterpret_cast<const uint2*>(mrow + D + c);
+        const size_t o = (size_t)r * D + c;
+        t = __ldg(reinterpret_cast<const float4*>(u.src + o));
+        h = __ldg(reinterpret_cast<const uint2*>(mrow + c));
+        a = __ldg(reinterpret_cast<const uint2*>(mrow + D + c));
+        if (u.bias) {
+          pa[k] = __ldg(reinterpret_cast<const float4*>(u.part + o));
+          pb[k] = __ldg(reinterpret_cast<const float4*>(u.part + u.part_stride + o));
+          bb[k] = __ldg(reinterpret_cast<const float4*>(u.bias + c));
+          gw[k] = __ldg(reinterpret_cast<const uint2*>(mod + mbase + u.gate_off + c));
+        }
       }
       xv[4 * k] = t.x;
       xv[4 * k + 1] = t.y;
@@ -473,6 +500,25 @@ __device__ __forceinline__ void build_ln_operand_t(const float* __restrict__ x_t
       xv[4 * k + 3] = t.w;
       shv[k] = h;
       scv[k] = a;
+    }
+    if (u.bias && m.valid) {
+#pragma unroll
+      for (int k = 0; k < NCH; ++k) {
+        const float2 g01 = unpack_bf16x2(gw[k].x), g23 = unpack_bf16x2(gw[k].y);
+        float* t = xv + 4 * k;
+        t[0] += g01.x * ((pa[k].x + pb[k].x) + bb[k].x);
+        t[1] += g01.y * ((pa[k].y + pb[k].y) + bb[k].y);
+        t[2] += g23.x * ((pa[k].z + pb[k].z) + bb[k].z);
+        t[3] += g23.y * ((pa[k].w + pb[k].w) + bb[k].w);
+      }
+      if (u.dst) {
+#pragma unroll
+        for (int k = 0; k < NCH; ++k) {
+          const int c = 4 * (part + TPR * k);
+          *reinterpret_cast<float4*>(u.dst + (size_t)r * D + c) =
+              make_float4(xv[4 * k], xv[4 * k + 1], xv[4 * k + 2], xv[4 * k + 3]);
+        }
+      }
     }
     float s = 0.f;
 #pragma unroll
@@ -510,8 +556,8 @@ __device__ __forceinline__ void build_ln_operand_t(const float* __restrict__ x_t
 #pragma unroll
     for (int k = 0; k < NCH; ++k) {
       const int c = 4 * (part + TPR * k);
-      const float4 g4 = *reinterpret_cast<const float4*>(lg + c);
-      const float4 b4 = *reinterpret_cast<const float4*>(lb + c);
+      const float4 g4 = __ldg(reinterpret_cast<const float4*>(lg + c));
+      const float4 b4 = __ldg(reinterpret_cast<const float4*>(lb + c));
       const float* y = xv + 4 * k;
       uint2 pk = make_uint2(0u, 0u);
       if (m.valid) {
@@ -528,11 +574,11 @@ __device__ __forceinline__ void build_ln_operand_t(const float* __restrict__ x_t
 // moments is then the same for every tile geometry, so an env's results do not depend
 // on how many candidates share its call.
 template <int D>
-__device__ __forceinline__ void build_ln_operand(const float* __restrict__ x_tile, const CallGeom& g, int tile,
+__device__ __forceinline__ void build_ln_operand(const ResidUpdate& u, const CallGeom& g, int tile,
                                                  const __nv_bfloat16* __restrict__ mod, int mod_cols, int shift_col,
                                                  const float* __restrict__ lg, const float* __restrict__ lb,
                                                  uint8_t* sA, int tid) {
-  build_ln_operand_t<D, 16>(x_tile, g, tile, mod, mod_cols, shift_col, lg, lb, sA, tid);
+  build_ln_operand_t<D, 16>(u, g, tile, mod, mod_cols, shift_col, lg, lb, sA, tid);
 }
 
 // Layer-0 residual row x0 = history row + position embedding of window position p.
@@ -618,9 +664,18 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   griddep_wait();
   LEWM_STAMP(2, 2);
   griddep_launch();
-  // A operand: LN1 -> modulate (shift/scale_msa of this layer) -> attn.norm of the residual rows.
-  build_ln_operand<D>(b.x + (size_t)tile * 128 * D, g, tile, b.mod, md.L * 6 * D, layer * 6 * D, w.attn_ln_w + layer * D,
-                      w.attn_ln_b + layer * D, sA, tid);
+  // A operand: LN1 -> modulate (shift/scale_msa of this layer) -> attn.norm of the residual
+  // rows. After layer 0 the previous layer's FC2 update is still pending: r = s + gate_mlp *
+  // (P0 + P1 + b2); the head-0 CTAs write r back for this layer's FC1.
+  {
+    const size_t t0 = (size_t)tile * 128 * D;
+    ResidUpdate u{b.x + t0, nullptr, 0, nullptr, 0, nullptr};
+    if (layer > 0)
+      u = ResidUpdate{b.xs + t0, b.part + t0, b.part_stride, w.b2 + (layer - 1) * D, (layer - 1) * 6 * D + 5 * D,
+                      head == 0 ? b.x + t0 : nullptr};
+    build_ln_operand<D>(u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D, w.attn_ln_w + layer * D,
+                        w.attn_ln_b + layer * D, sA, tid);
+  }
   fence_async_smem();
   LEWM_STAMP(2, 5);
   tc_fence_before();
@@ -769,46 +824,43 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
-// ---------------------------------------------------------------- streamed-K GEMM, residual epilogue
-// Bytes after the operand slots: the bias [NT], 5 barriers, the TMEM slot and a flag.
+// ---------------------------------------------------------------- K-split residual-branch GEMM
+// Bytes after the operand slots: 5 barriers, the TMEM slot and a flag.
+constexpr int kKSplit = 2;  // K halves of the out-projection / FC2 GEMMs
 template <int D>
-__host__ __device__ constexpr int resid_extra() { return Cfg<D>::NT_OUT * 4 + 8 * 5 + 16; }
-// What the epilogue of an out-projection / FC2 launch does with its N tile.
-struct ResidEpi {
-  const float* bias;      // [D] of this GEMM
-  int gate_chunk;         // mod chunk of the gate (2: gate_msa, 5: gate_mlp) of `layer`
-};
+__host__ __device__ constexpr int resid_extra() { return 8 * 5 + 16; }
 
-// x[:, n-tile] += gate * (A . B^T + bias); A streamed from pre-swizzled global tiles.
-// Four CTAs per row tile (one N tile each), independent: the LayerNorm of the next
-// GEMM's operand is built by that GEMM's kernel from the updated rows. Warp 0 issues
-// MMAs, warp 1 refills the operand slots.
+// part[kh][rows][n-tile] = A[:, K half kh] . B[n-tile, K half kh]^T for the out-projection
+// or FC2 of a layer. Grid (tiles, 4 N tiles, 2 K halves): each CTA issues half the MMAs
+// and all its operand blocks fit one copy round. The bias, gate and residual add are
+// applied by the consumer of the sum (the next GEMM's operand builder, or k_final),
+// which adds the two halves in a fixed order. Warp 0 issues MMAs, warp 1 refills the
+// operand slots when they do not all fit.
 template <int D>
-__global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __restrict__ gA, int nkb,
-                                                         const __nv_bfloat16* __restrict__ gB, ResidEpi ep, CallGeom g,
-                                                         RolloutBufs b, ModelDims md, int layer, uint32_t* status) {
+__global__ void __launch_bounds__(kThreads) k_partial_gemm(const __nv_bfloat16* __restrict__ gA, int nkb,
+                                                           const __nv_bfloat16* __restrict__ gB, CallGeom g,
+                                                           float* __restrict__ part, size_t part_stride, int skind,
+                                                           uint32_t* status) {
   using C = Cfg<D>;
   constexpr int NT = C::NT_OUT;
   constexpr int CW = NT / 4;
   constexpr int B_BLK = NT * 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  const ResidLayout lay = resid_layout(g.rows8, nkb, B_BLK, C::KG, resid_extra<D>());
-  const int G = lay.G;
+  const int tile = blockIdx.x, nt = blockIdx.y, kh = blockIdx.z;
+  const int kcount = nkb / kKSplit, kb0 = kh * kcount;
+  const ResidLayout lay = resid_layout(g.rows8, kcount, B_BLK, C::KG, resid_extra<D>());
   uint8_t* sA = smem;
   uint8_t* sB = smem + lay.b_off;
-  float* svec = reinterpret_cast<float*>(smem + lay.v_off);  // [bias NT]
-  uint64_t* full = reinterpret_cast<uint64_t*>(svec + NT);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + lay.v_off);
   uint64_t* empty = full + 2;
   uint64_t* bar_mma = empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int skind = ep.gate_chunk == 2 ? 5 : 3;  // diagnostic stamp stream: out-proj / FC2
-  (void)skind;
-  const int tile = blockIdx.x, nt = blockIdx.y;
-  const KStream<B_BLK> ks{sA, sB, full, empty, gA + (size_t)tile * nkb * kBlkElems, (size_t)kBlkElems,
-                          gB + (size_t)nt * nkb * NT * 64, (size_t)NT * 64, (uint32_t)g.rows8 * 128,
-                          (uint32_t)lay.a_stride, nkb, G};
+  (void)skind;  // diagnostic stamp stream
+  const KStream<B_BLK> ks{sA, sB, full, empty, gA + ((size_t)tile * nkb + kb0) * kBlkElems, (size_t)kBlkElems,
+                          gB + ((size_t)nt * nkb + kb0) * NT * 64, (size_t)NT * 64, (uint32_t)g.rows8 * 128,
+                          (uint32_t)lay.a_stride, kcount, lay.G};
   if (tid == 0) {
     for (int h = 0; h < 2; ++h) {
       mbar_init(&full[h], 1);
@@ -816,20 +868,11 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
     }
     mbar_init(bar_mma, 1);
     fence_mbar_init();
-    mbar_arrive_expect_tx(&full[0], ks.bytes(0) + NT * 4);
+    mbar_arrive_expect_tx(&full[0], ks.bytes(0));
     if (ks.groups() > 1) mbar_arrive_expect_tx(&full[1], ks.bytes(1));
   }
   __syncwarp();
-  // Weights and bias first (they do not depend on the previous kernel), in one
-  // instruction of warp 0 (K blocks on lanes below 2G <= 32, the bias on lane 31, which
-  // K blocks never use because 2G > 31 only when G >= nkb and one group covers lanes
-  // below nkb <= 16).
-  if (warp == 0) {
-    if (lane == 31)
-      bulk_g2s(svec, ep.bias + nt * NT, NT * 4, &full[0]);
-    else
-      ks.issue_first(lane, false);
-  }
+  if (warp == 0) ks.issue_first(lane, false);  // weights before the wait, one instruction
   __syncwarp();
   if (warp == 0) {
     tmem_alloc(tmem_slot, C::TMEM_OUT);
@@ -853,48 +896,21 @@ __global__ void __launch_bounds__(kThreads) k_resid_gemm(const __nv_bfloat16* __
   } else if (warp == 1) {
     ks.produce(lane, status);
   }
-  const int quad = warp & 3, slice = warp >> 2;
-  const int r = quad * 32 + lane;
-  const RowMap m = map_row(g, tile, r);
-  // Residual and gate do not depend on the MMA: load them while it runs.
-  const int c0 = nt * NT + slice * CW;
-  float* xrow = b.x + ((size_t)tile * 128 + r) * D + c0;
-  float4 xv[CW / 4];
-  uint2 gt[CW / 4];
-  if (m.valid) {
-    const __nv_bfloat16* gate = b.mod + (size_t)m.tok * (md.L * 6 * D) + layer * 6 * D + ep.gate_chunk * D + c0;
-#pragma unroll
-    for (int i = 0; i < CW / 4; ++i) {
-      xv[i] = *reinterpret_cast<const float4*>(xrow + 4 * i);
-      gt[i] = *reinterpret_cast<const uint2*>(gate + 4 * i);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < CW / 4; ++i) {
-      xv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-      gt[i] = make_uint2(0u, 0u);
-    }
-  }
   const bool ok = cta_wait_mma(bar_mma, status, tmem_slot + 1);
   LEWM_STAMP(skind, 4);
   __syncwarp();
   tc_fence_after();
+  const int quad = warp & 3, slice = warp >> 2;
+  const int r = quad * 32 + lane;
   const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * CW;
   float v[CW];
   tmem_ld_cols<CW>(taddr, v);
   LEWM_STAMP(skind, 7);
-  if (ok && m.valid) {
-    const float* bs = svec + slice * CW;
+  if (ok && r < g.rows8) {
+    float4* dst = reinterpret_cast<float4*>(part + kh * part_stride + ((size_t)tile * 128 + r) * D + nt * NT +
+                                            slice * CW);
 #pragma unroll
-    for (int i = 0; i < CW / 4; ++i) {
-      const float2 g01 = unpack_bf16x2(gt[i].x), g23 = unpack_bf16x2(gt[i].y);
-      const float4 b4 = *reinterpret_cast<const float4*>(bs + 4 * i);
-      xv[i].x += g01.x * (v[4 * i] + b4.x);
-      xv[i].y += g01.y * (v[4 * i + 1] + b4.y);
-      xv[i].z += g23.x * (v[4 * i + 2] + b4.z);
-      xv[i].w += g23.y * (v[4 * i + 3] + b4.w);
-      *reinterpret_cast<float4*>(xrow + 4 * i) = xv[i];
-    }
+    for (int i = 0; i < CW / 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
   }
   LEWM_STAMP(skind, 6);
   tc_fence_before();
@@ -959,9 +975,15 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   griddep_wait();
   LEWM_STAMP(4, 2);
   griddep_launch();
-  // A operand: LN2 -> modulate (shift/scale_mlp of this layer) -> ffn.norm of the residual rows.
-  build_ln_operand<D>(b.x + (size_t)tile * 128 * D, g, tile, b.mod, md.L * 6 * D, layer * 6 * D + 3 * D,
-                      w.ffn_ln_w + layer * D, w.ffn_ln_b + layer * D, sA, tid);
+  // A operand: LN2 -> modulate (shift/scale_mlp of this layer) -> ffn.norm of s = r +
+  // gate_msa * (P0 + P1 + out_b), the out-projection update; the N-tile-0 CTAs write s back.
+  {
+    const size_t t0 = (size_t)tile * 128 * D;
+    const ResidUpdate u{b.x + t0, b.part + t0, b.part_stride, w.out_b + layer * D, layer * 6 * D + 2 * D,
+                        nt == 0 ? b.xs + t0 : nullptr};
+    build_ln_operand<D>(u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D + 3 * D, w.ffn_ln_w + layer * D,
+                        w.ffn_ln_b + layer * D, sA, tid);
+  }
   fence_async_smem();
   LEWM_STAMP(4, 5);
   tc_fence_before();
@@ -1056,15 +1078,25 @@ __global__ void __launch_bounds__(128) k_final(DevWeights w, ModelDims md, CallG
   const bool new_pred = g.last || (j - g.H == g.call);
   float2 v[NP];
   if (new_pred) {
+    // Output of the last layer for the window's last token: s + gate_mlp * ((P0 + P1) + b2),
+    // the FC2 update of the last layer still pending.
     const int tile = cand / g.cpt;
     const int r = (cand - tile * g.cpt) * g.w + (g.w - 1);
-    const float* xr = b.x + ((size_t)tile * 128 + r) * D;
+    const size_t o = ((size_t)tile * 128 + r) * D;
+    const int tok = cand * g.T + g.start + g.w - 1;
+    const __nv_bfloat16* gate = b.mod + (size_t)tok * (md.L * 6 * D) + (md.L - 1) * 6 * D + 5 * D;
+    const float* b2 = w.b2 + (md.L - 1) * D;
     float2 fw[NP], fb[NP];
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < NP; ++i) {
       const int c = 64 * i + 2 * lane;
-      v[i] = *reinterpret_cast<const float2*>(xr + c);
+      const float2 xs = *reinterpret_cast<const float2*>(b.xs + o + c);
+      const float2 p0 = *reinterpret_cast<const float2*>(b.part + o + c);
+      const float2 p1 = *reinterpret_cast<const float2*>(b.part + b.part_stride + o + c);
+      const float2 bb = *reinterpret_cast<const float2*>(b2 + c);
+      const float2 gg = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(gate + c));
+      v[i] = make_float2(xs.x + gg.x * ((p0.x + p1.x) + bb.x), xs.y + gg.y * ((p0.y + p1.y) + bb.y));
       fw[i] = *reinterpret_cast<const float2*>(w.fin_w + c);
       fb[i] = *reinterpret_cast<const float2*>(w.fin_b + c);
       s += v[i].x + v[i].y;
@@ -1142,7 +1174,7 @@ cudaError_t set_smem_attrs() {
     return e;
   if ((e = cudaFuncSetAttribute(k_adaln<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_adaln<D>()))) return e;
   if ((e = cudaFuncSetAttribute(k_qkv_attn<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_qkv<D>()))) return e;
-  if ((e = cudaFuncSetAttribute(k_resid_gemm<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_resid<D>())))
+  if ((e = cudaFuncSetAttribute(k_partial_gemm<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_resid<D>())))
     return e;
   if ((e = cudaFuncSetAttribute(k_fc1<D, kFc1N>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_fc1<D, kFc1N>())))
     return e;
@@ -1204,28 +1236,29 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
     LEWM_TRY(launch_k(k_qkv_attn<D>, dim3(g.n_tiles, md.heads), dim3(kThreads), smem_qkv<D>(), st, w, md, g, b, l,
                       status));
     if (prof) prof->end(KC_QKV_ATTN, 2.0 * rows * D * 3 * md.inner + 4.0 * rows * g.w * md.inner, st);
-    // out-projection: residual with gate_msa, then LN2 / modulate(mlp) / FFN LayerNorm -> FC1 operand
-    const ResidEpi ep_out{w.out_b + l * D, 2};
+    // out-projection partial sums (bias, gate_msa and residual applied by FC1's operand builder)
     if (prof) prof->begin(st);
-    LEWM_TRY(launch_k(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads),
-                      resid_layout(g.rows8, nkb_inner, Cfg<D>::NT_OUT * 128, Cfg<D>::KG, resid_extra<D>()).bytes, st,
-                      (const __nv_bfloat16*)b.attn, nkb_inner,
-                       (const __nv_bfloat16*)(w.wout + (size_t)l * 4 * nkb_inner * Cfg<D>::NT_OUT * 64), ep_out, g,
-                       b, md, l, status));
+    LEWM_TRY(launch_k(k_partial_gemm<D>, dim3(g.n_tiles, 4, kKSplit), dim3(kThreads),
+                      resid_layout(g.rows8, nkb_inner / kKSplit, Cfg<D>::NT_OUT * 128, Cfg<D>::KG, resid_extra<D>())
+                          .bytes,
+                      st, (const __nv_bfloat16*)b.attn, nkb_inner,
+                      (const __nv_bfloat16*)(w.wout + (size_t)l * 4 * nkb_inner * Cfg<D>::NT_OUT * 64), g, b.part,
+                      b.part_stride, 5, status));
     if (prof) prof->end(KC_OUT, 2.0 * rows * md.inner * D, st);
     if (prof) prof->begin(st);
     LEWM_TRY(launch_k(k_fc1<D, kFc1N>, dim3(g.n_tiles, md.mlp / kFc1N), dim3(kThreads), smem_fc1<D, kFc1N>(), st, w,
                       md, g, b, l,
                       status));
     if (prof) prof->end(KC_FC1, 2.0 * rows * D * md.mlp, st);
-    // FC2: residual with gate_mlp, then (not after the last layer) LN1 / modulate(msa of l+1) / attn.norm
-    const ResidEpi ep_fc2{w.b2 + l * D, 5};
+    // FC2 partial sums (bias, gate_mlp and residual applied by the next QKV operand builder
+    // or, after the last layer, by k_final)
     if (prof) prof->begin(st);
-    LEWM_TRY(launch_k(k_resid_gemm<D>, dim3(g.n_tiles, 4), dim3(kThreads),
-                      resid_layout(g.rows8, nkb_mlp, Cfg<D>::NT_OUT * 128, Cfg<D>::KG, resid_extra<D>()).bytes, st,
-                      (const __nv_bfloat16*)b.h, nkb_mlp,
-                       (const __nv_bfloat16*)(w.w2 + (size_t)l * 4 * nkb_mlp * Cfg<D>::NT_OUT * 64), ep_fc2, g, b,
-                       md, l, status));
+    LEWM_TRY(launch_k(k_partial_gemm<D>, dim3(g.n_tiles, 4, kKSplit), dim3(kThreads),
+                      resid_layout(g.rows8, nkb_mlp / kKSplit, Cfg<D>::NT_OUT * 128, Cfg<D>::KG, resid_extra<D>())
+                          .bytes,
+                      st, (const __nv_bfloat16*)b.h, nkb_mlp,
+                      (const __nv_bfloat16*)(w.w2 + (size_t)l * 4 * nkb_mlp * Cfg<D>::NT_OUT * 64), g, b.part,
+                      b.part_stride, 3, status));
     if (prof) prof->end(KC_FC2, 2.0 * rows * md.mlp * D, st);
   }
   if (prof) prof->begin(st);
