@@ -569,16 +569,16 @@ __device__ __forceinline__ void build_ln_operand_t(const ResidUpdate& u, const C
   }
 }
 
-// Sixteen threads per row for every tile size: all 16 warps work on the first 32 used
-// rows, and larger tiles loop over further 32-row passes. The reduction order of the row
-// moments is then the same for every tile geometry, so an env's results do not depend
-// on how many candidates share its call.
+// D / 12 threads per row (12 columns each: 16 threads at width 192, 32 at 384) for every
+// tile size: all 16 warps work on the first rows, and larger tiles loop over further
+// passes. The reduction order of the row moments is then the same for every tile
+// geometry, so an env's results do not depend on how many candidates share its call.
 template <int D>
 __device__ __forceinline__ void build_ln_operand(const ResidUpdate& u, const CallGeom& g, int tile,
                                                  const __nv_bfloat16* __restrict__ mod, int mod_cols, int shift_col,
                                                  const float* __restrict__ lg, const float* __restrict__ lb,
                                                  uint8_t* sA, int tid) {
-  build_ln_operand_t<D, 16>(u, g, tile, mod, mod_cols, shift_col, lg, lb, sA, tid);
+  build_ln_operand_t<D, D / 12>(u, g, tile, mod, mod_cols, shift_col, lg, lb, sA, tid);
 }
 
 // Layer-0 residual row x0 = history row + position embedding of window position p.
