@@ -44,6 +44,7 @@ struct Workspace {
   float* xs = nullptr;   // residual after the attention half of a layer
   float* part = nullptr; // K-split partial sums of the residual-branch GEMMs, two halves
   size_t part_stride = 0;
+  __nv_bfloat16* a_op = nullptr;  // QKV / FC1 operand built once per tile
   __nv_bfloat16* attn = nullptr;
   __nv_bfloat16* h = nullptr;
   float* pred = nullptr;
@@ -359,6 +360,7 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   const size_t o_x2 = carve(r.tiles * 128 * (size_t)m.D * 4);
   const size_t o_xs = carve(r.tiles * 128 * (size_t)m.D * 4);
   const size_t o_part = carve(2 * r.tiles * 128 * (size_t)m.D * 4);
+  const size_t o_aop = carve(r.tiles * 128 * (size_t)m.D * 2);
   const size_t o_attn = carve(r.tiles * (size_t)(m.inner / 64) * 128 * 64 * 2);
   const size_t o_h = carve(r.tiles * (size_t)(m.mlp / 64) * 128 * 64 * 2);
   const size_t o_pred = carve(r.n_cand * r.npred * (size_t)m.D * 4);
@@ -389,6 +391,7 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   ws.xs = reinterpret_cast<float*>(b + o_xs);
   ws.part = reinterpret_cast<float*>(b + o_part);
   ws.part_stride = r.tiles * 128 * (size_t)m.D;
+  ws.a_op = reinterpret_cast<__nv_bfloat16*>(b + o_aop);
   ws.attn = reinterpret_cast<__nv_bfloat16*>(b + o_attn);
   ws.h = reinterpret_cast<__nv_bfloat16*>(b + o_h);
   ws.pred = reinterpret_cast<float*>(b + o_pred);
@@ -418,7 +421,7 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
   LEWM_CK(c, launch_embed(m, c->w, cand, rows, c->ws.eh, c->ws.act_a, c->d_status, st, &c->prof));
   LEWM_CK(c, launch_adaln(m, c->w, rows, c->ws.act_a, c->ws.mod, c->d_status, st, &c->prof));
   RolloutBufs b{emb,        emb_pc,    goal,      goal_pc, cand,      c->ws.act_a, c->ws.mod,
-                c->ws.x,    c->ws.x2,  c->ws.xs,  c->ws.part, c->ws.part_stride, c->ws.attn, c->ws.h,
+                c->ws.x,    c->ws.x2,  c->ws.xs,  c->ws.part, c->ws.part_stride, c->ws.a_op, c->ws.attn, c->ws.h,
                 c->ws.pred, costs};
   const int n_calls = T - H + 1;
   auto geom = [&](int k) {
@@ -428,7 +431,10 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
     int cpt, nt;
     tile_geom(NC, w, c->tile_target, &cpt, &nt);
     const int rows8 = std::min(128, (cpt * w + 7) & ~7);
-    return CallGeom{NC, S, T, H, w, start, cpt, nt, rows8, k, k == n_calls - 1, 1, 0, 128};
+    // Operands of tiles with more rows than one pass of the in-kernel build (512 threads,
+    // D/12 per row) are built once per tile by a separate kernel.
+    const int ln_prebuilt = rows8 > 512 / (m.D / 12) ? 1 : 0;
+    return CallGeom{NC, S, T, H, w, start, cpt, nt, rows8, ln_prebuilt, k, k == n_calls - 1, 1, 0, 128};
   };
   for (int k = 0; k < n_calls; ++k) {
     CallGeom g = geom(k);

@@ -75,6 +75,7 @@ struct CallGeom {
   int cpt;      // candidates per tile
   int n_tiles;  // window tiles
   int rows8;    // rows of a tile that operand copies move: cpt * w rounded up to 8 (<= 128)
+  int ln_prebuilt;  // 1: QKV / FC1 operands are built by k_ln_operand and bulk-copied
   int call;     // prediction slot written by this call
   int last;     // 1: final call, write costs
   // Window of the next call (k_final prepares its layer-0 inputs); unused when last.
@@ -94,6 +95,7 @@ struct RolloutBufs {
   float* xs;       // residual after the attention half of a layer, [tiles][128][D]
   float* part;     // K-split partial sums of the last residual GEMM, [2][tiles][128][D]
   size_t part_stride;  // floats between the two K halves of `part`
+  __nv_bfloat16* a_op; // GEMM operand built by k_ln_operand, [tiles][D/64][128x64] pre-swizzled
   __nv_bfloat16* attn;
   __nv_bfloat16* h;
   float* pred;

@@ -441,7 +441,7 @@ __global__ void __launch_bounds__(kThreads) k_adaln(DevWeights w, ModelDims md, 
 // feed-forward block's own LayerNorm at eps 1e-5. TPR consecutive threads share a row
 // (a warp covers 32 / TPR rows), D / TPR columns each in 4-column chunks; the row
 // moments reduce through shuffles among them. Rows at or past rows8 are skipped (whole
-// warps: rows8 is a multiple of 8 >= 32 / TPR); window slots without a candidate get
+// warps: the row range bounds are multiples of 8 >= 32 / TPR); window slots without a candidate get
 // zeros.
 // A residual update still pending when a GEMM operand is built: the K-split residual
 // GEMM wrote two partial sums P0, P1, and the residual is r = src + gate * ((P0 + P1) +
@@ -459,12 +459,12 @@ template <int D, int TPR>
 __device__ __forceinline__ void build_ln_operand_t(const ResidUpdate& u, const CallGeom& g, int tile,
                                                    const __nv_bfloat16* __restrict__ mod, int mod_cols, int shift_col,
                                                    const float* __restrict__ lg, const float* __restrict__ lb,
-                                                   uint8_t* sA, int tid) {
+                                                   uint8_t* sA, int tid, int r_begin, int r_end) {
   constexpr int NPER = D / TPR;   // columns per thread, a multiple of 4
   constexpr int NCH = NPER / 4;   // 4-column chunks per thread
   static_assert(NPER % 4 == 0, "4-column chunks");
   const int part = tid % TPR;
-  for (int r = tid / TPR; r < g.rows8; r += kThreads / TPR) {
+  for (int r = r_begin + tid / TPR; r < r_end; r += kThreads / TPR) {
     const RowMap m = map_row(g, tile, r);
     float xv[NPER];
     uint2 shv[NCH], scv[NCH];
@@ -578,7 +578,7 @@ __device__ __forceinline__ void build_ln_operand(const ResidUpdate& u, const Cal
                                                  const __nv_bfloat16* __restrict__ mod, int mod_cols, int shift_col,
                                                  const float* __restrict__ lg, const float* __restrict__ lb,
                                                  uint8_t* sA, int tid) {
-  build_ln_operand_t<D, D / 12>(u, g, tile, mod, mod_cols, shift_col, lg, lb, sA, tid);
+  build_ln_operand_t<D, D / 12>(u, g, tile, mod, mod_cols, shift_col, lg, lb, sA, tid, 0, g.rows8);
 }
 
 // Layer-0 residual row x0 = history row + position embedding of window position p.
@@ -593,6 +593,32 @@ __device__ __forceinline__ void prep_layer0_row(const DevWeights& w, const float
     const float2 pe = *reinterpret_cast<const float2*>(w.pos + p * D + c);
     *reinterpret_cast<float2*>(xdst + c) = make_float2(a.x + pe.x, a.y + pe.y);
   }
+}
+
+// ---------------------------------------------------------------- GEMM operand, one CTA per 32 rows
+// For tiles of more than 32 used rows the operand of a QKV / FC1 GEMM is built once per
+// tile by this kernel (grid: tiles x 32-row groups) into the pre-swizzled global
+// [tile][D/64][128 x 64] layout, which the GEMM's CTAs then bulk-copy; building it in
+// each of the GEMM's 16-24 CTAs per tile would repeat several passes per CTA. Same
+// device code as the in-kernel build, so the results are identical either way; every
+// CTA writes back the updated residual rows it owns.
+template <int D>
+__global__ void __launch_bounds__(kThreads) k_ln_operand(ResidUpdate u, CallGeom g, const __nv_bfloat16* mod,
+                                                         int mod_cols, int shift_col, const float* lg, const float* lb,
+                                                         __nv_bfloat16* a_op) {
+  griddep_wait();
+  griddep_launch();
+  const int tile = blockIdx.x;
+  const int r0 = blockIdx.y * (kThreads / (D / 12));
+  const int r1 = min(r0 + kThreads / (D / 12), g.rows8);
+  const size_t t0 = (size_t)tile * 128 * D;
+  ResidUpdate ut = u;
+  ut.src += t0;
+  if (ut.part) ut.part += t0;
+  if (ut.dst) ut.dst += t0;
+  build_ln_operand_t<D, D / 12>(ut, g, tile, mod, mod_cols, shift_col, lg, lb,
+                                reinterpret_cast<uint8_t*>(a_op + (size_t)tile * (D / 64) * kBlkElems), threadIdx.x,
+                                r0, r1);
 }
 
 // ---------------------------------------------------------------- first-call layer-0 inputs
@@ -637,7 +663,8 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
   uint64_t* empty = full + ST;
   uint64_t* bar_mma = empty + ST;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
+  uint64_t* bar_a = bar_mma + 1;  // [KB], operand bulk copies when prebuilt
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + KB);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x, head = blockIdx.y;
@@ -649,6 +676,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
       mbar_init(&empty[s], 1);
     }
     mbar_init(bar_mma, 1);
+    for (int kb = 0; kb < KB; ++kb) mbar_init(&bar_a[kb], 1);
     fence_mbar_init();
   }
   __syncwarp();
@@ -667,7 +695,12 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   // A operand: LN1 -> modulate (shift/scale_msa of this layer) -> attn.norm of the residual
   // rows. After layer 0 the previous layer's FC2 update is still pending: r = s + gate_mlp *
   // (P0 + P1 + b2); the head-0 CTAs write r back for this layer's FC1.
-  {
+  if (g.ln_prebuilt) {  // built once per tile by k_ln_operand: one copy per lane
+    if (warp == 0 && lane < KB) {
+      mbar_arrive_expect_tx(&bar_a[lane], g.rows8 * 128);
+      bulk_g2s(sA + lane * kBlk, b.a_op + ((size_t)tile * KB + lane) * kBlkElems, g.rows8 * 128, &bar_a[lane]);
+    }
+  } else {
     const size_t t0 = (size_t)tile * 128 * D;
     ResidUpdate u{b.x + t0, nullptr, 0, nullptr, 0, nullptr};
     if (layer > 0)
@@ -686,7 +719,9 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     const uint32_t idesc = idesc_bf16(128, 192);
     for (int kb = 0; kb < KB; ++kb) {
       const int s = kb % ST;
-      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (kb / ST) & 1, status))) break;
+      if (!__all_sync(0xffffffffu, (!g.ln_prebuilt || mbar_wait(&bar_a[kb], 0, status)) &&
+                                       mbar_wait(&full[s], (kb / ST) & 1, status)))
+        break;
       tc_fence_after();
       if (lane == 0) {
 #pragma unroll
@@ -943,7 +978,8 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   uint64_t* full = reinterpret_cast<uint64_t*>(svec + NT);
   uint64_t* empty = full + ST;
   uint64_t* bar_mma = empty + ST;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
+  uint64_t* bar_a = bar_mma + 1;  // [KB], operand bulk copies when prebuilt
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + KB);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   LEWM_STAMP(4, 0);
   const int tile = blockIdx.x, nt = blockIdx.y;
@@ -956,6 +992,7 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
       mbar_init(&empty[s], 1);
     }
     mbar_init(bar_mma, 1);
+    for (int kb = 0; kb < KB; ++kb) mbar_init(&bar_a[kb], 1);
     fence_mbar_init();
     mbar_arrive_expect_tx(&full[0], B_BLK + NT * 4);
     for (int s = 1; s < ST; ++s) mbar_arrive_expect_tx(&full[s], B_BLK);
@@ -977,7 +1014,12 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   griddep_launch();
   // A operand: LN2 -> modulate (shift/scale_mlp of this layer) -> ffn.norm of s = r +
   // gate_msa * (P0 + P1 + out_b), the out-projection update; the N-tile-0 CTAs write s back.
-  {
+  if (g.ln_prebuilt) {  // built once per tile by k_ln_operand: one copy per lane
+    if (warp == 0 && lane < KB) {
+      mbar_arrive_expect_tx(&bar_a[lane], g.rows8 * 128);
+      bulk_g2s(sA + lane * kBlk, b.a_op + ((size_t)tile * KB + lane) * kBlkElems, g.rows8 * 128, &bar_a[lane]);
+    }
+  } else {
     const size_t t0 = (size_t)tile * 128 * D;
     const ResidUpdate u{b.x + t0, b.part + t0, b.part_stride, w.out_b + layer * D, layer * 6 * D + 2 * D,
                         nt == 0 ? b.xs + t0 : nullptr};
@@ -994,7 +1036,9 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
     const uint32_t idesc = idesc_bf16(128, NT);
     for (int kb = 0; kb < KB; ++kb) {
       const int s = kb % ST;
-      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (kb / ST) & 1, status))) break;
+      if (!__all_sync(0xffffffffu, (!g.ln_prebuilt || mbar_wait(&bar_a[kb], 0, status)) &&
+                                       mbar_wait(&full[s], (kb / ST) & 1, status)))
+        break;
       tc_fence_after();
       if (lane == 0) {
 #pragma unroll
@@ -1231,7 +1275,18 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
   do {                                      \
     if ((e = (x)) != cudaSuccess) return e; \
   } while (0)
+  const int op_rows = kThreads / (D / 12);  // rows per k_ln_operand CTA
+  const dim3 op_grid(g.n_tiles, (g.rows8 + op_rows - 1) / op_rows);
+  const int mcols = md.L * 6 * D;
   for (int l = 0; l < md.L; ++l) {
+    if (g.ln_prebuilt) {  // QKV operand of every tile: LN1 -> modulate -> attn.norm (+ pending FC2 update)
+      ResidUpdate u{b.x, nullptr, 0, nullptr, 0, nullptr};
+      if (l > 0) u = ResidUpdate{b.xs, b.part, b.part_stride, w.b2 + (l - 1) * D, (l - 1) * 6 * D + 5 * D, b.x};
+      if (prof) prof->begin(st);
+      LEWM_TRY(launch_k(k_ln_operand<D>, op_grid, dim3(kThreads), 0, st, u, g, (const __nv_bfloat16*)b.mod, mcols,
+                        l * 6 * D, w.attn_ln_w + l * D, w.attn_ln_b + l * D, b.a_op));
+      if (prof) prof->end(KC_QKV_ATTN, 0.0, st);
+    }
     if (prof) prof->begin(st);
     LEWM_TRY(launch_k(k_qkv_attn<D>, dim3(g.n_tiles, md.heads), dim3(kThreads), smem_qkv<D>(), st, w, md, g, b, l,
                       status));
@@ -1245,6 +1300,13 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
                       (const __nv_bfloat16*)(w.wout + (size_t)l * 4 * nkb_inner * Cfg<D>::NT_OUT * 64), g, b.part,
                       b.part_stride, 5, status));
     if (prof) prof->end(KC_OUT, 2.0 * rows * md.inner * D, st);
+    if (g.ln_prebuilt) {  // FC1 operand: s = r + gate_msa * (out-proj + bias), LN2 -> modulate -> ffn.norm
+      const ResidUpdate u{b.x, b.part, b.part_stride, w.out_b + l * D, l * 6 * D + 2 * D, b.xs};
+      if (prof) prof->begin(st);
+      LEWM_TRY(launch_k(k_ln_operand<D>, op_grid, dim3(kThreads), 0, st, u, g, (const __nv_bfloat16*)b.mod, mcols,
+                        l * 6 * D + 3 * D, w.ffn_ln_w + l * D, w.ffn_ln_b + l * D, b.a_op));
+      if (prof) prof->end(KC_FC1, 0.0, st);
+    }
     if (prof) prof->begin(st);
     LEWM_TRY(launch_k(k_fc1<D, kFc1N>, dim3(g.n_tiles, md.mlp / kFc1N), dim3(kThreads), smem_fc1<D, kFc1N>(), st, w,
                       md, g, b, l,
