@@ -433,7 +433,11 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
     const int rows8 = std::min(128, (cpt * w + 7) & ~7);
     // Operands of tiles with more rows than one pass of the in-kernel build (512 threads,
     // D/12 per row) are built once per tile by a separate kernel.
-    const int ln_prebuilt = rows8 > 512 / (m.D / 12) ? 1 : 0;
+    static const int pre_rows = [] {
+      const char* v = std::getenv("LEWM_PREBUILT_ROWS");
+      return v ? std::atoi(v) : -1;
+    }();
+    const int ln_prebuilt = rows8 > (pre_rows >= 0 ? pre_rows : 512 / (m.D / 12)) ? 1 : 0;
     return CallGeom{NC, S, T, H, w, start, cpt, nt, rows8, ln_prebuilt, k, k == n_calls - 1, 1, 0, 128};
   };
   for (int k = 0; k < n_calls; ++k) {
