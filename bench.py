@@ -42,13 +42,13 @@ F_CANON = 9 * L * F_BLOCK_TOKEN + T * L * 2 * D * 6 * D + T * 2 * (A * A + A * 4
 
 
 # DRAM bytes (read + write) of one launch of the dominant kernel classes, from the ncu
-# captures summarised in profiles/k_resid_gemm_outproj_fc2_w3_9tiles.md and
-# profiles/k_qkv_attn_w3_9tiles.md (ncu flushes L2 between passes, so these are
-# cold-cache first-touch bytes; the timed run keeps weights in L2).
+# captures summarised in profiles/k_qkv_attn_w1_6tiles.md and
+# profiles/k_partial_gemm_outproj_fc2_w3_8tiles.md (ncu flushes L2 between passes, so
+# these are cold-cache first-touch bytes; the timed run keeps weights in L2).
 NCU_TRAFFIC = {
-    "out_proj": {"bytes": 4148736, "launch": "out-proj, 900 rows (300 candidates x window 3), 9 tiles"},
-    "fc2": {"bytes": 3571200, "launch": "FC2, 900 rows (300 candidates x window 3), 9 tiles"},
-    "qkv_attn": {"bytes": 1316096, "launch": "QKV + attention, 900 rows, 9 tiles x 16 heads"},
+    "qkv_attn": {"bytes": 1308416, "launch": "QKV + attention, 240 rows (window 1), 6 tiles x 16 heads"},
+    "out_proj": {"bytes": 2381056, "launch": "out-proj K halves, 900 rows (300 candidates x window 3), 8 tiles"},
+    "fc2": {"bytes": 1791488, "launch": "FC2 K halves, 900 rows (300 candidates x window 3), 8 tiles"},
 }
 
 
