@@ -42,7 +42,8 @@ struct Workspace {
   float* x = nullptr;    // two residual buffers: predictor calls alternate between them
   float* x2 = nullptr;
   float* xs = nullptr;   // residual after the attention half of a layer
-  float* part = nullptr; // K-split partial sums of the residual-branch GEMMs, two halves
+  float* part_a = nullptr;  // out-proj partial sums (two K halves)
+  float* part_b = nullptr;  // FC2 partial sums (CallGeom::fc2_parts K parts: 2 halves or 4 hidden quarters)
   size_t part_stride = 0;
   __nv_bfloat16* a_op = nullptr;  // QKV / FC1 operand built once per tile
   __nv_bfloat16* attn = nullptr;
@@ -359,7 +360,8 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   const size_t o_x = carve(r.tiles * 128 * (size_t)m.D * 4);
   const size_t o_x2 = carve(r.tiles * 128 * (size_t)m.D * 4);
   const size_t o_xs = carve(r.tiles * 128 * (size_t)m.D * 4);
-  const size_t o_part = carve(2 * r.tiles * 128 * (size_t)m.D * 4);
+  const size_t o_part_a = carve(2 * r.tiles * 128 * (size_t)m.D * 4);
+  const size_t o_part_b = carve(4 * r.tiles * 128 * (size_t)m.D * 4);
   const size_t o_aop = carve(r.tiles * 128 * (size_t)m.D * 2);
   const size_t o_attn = carve(r.tiles * (size_t)(m.inner / 64) * 128 * 64 * 2);
   const size_t o_h = carve(r.tiles * (size_t)(m.mlp / 64) * 128 * 64 * 2);
@@ -389,7 +391,8 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   ws.x = reinterpret_cast<float*>(b + o_x);
   ws.x2 = reinterpret_cast<float*>(b + o_x2);
   ws.xs = reinterpret_cast<float*>(b + o_xs);
-  ws.part = reinterpret_cast<float*>(b + o_part);
+  ws.part_a = reinterpret_cast<float*>(b + o_part_a);
+  ws.part_b = reinterpret_cast<float*>(b + o_part_b);
   ws.part_stride = r.tiles * 128 * (size_t)m.D;
   ws.a_op = reinterpret_cast<__nv_bfloat16*>(b + o_aop);
   ws.attn = reinterpret_cast<__nv_bfloat16*>(b + o_attn);
@@ -421,7 +424,8 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
   LEWM_CK(c, launch_embed(m, c->w, cand, rows, c->ws.eh, c->ws.act_a, c->d_status, st, &c->prof));
   LEWM_CK(c, launch_adaln(m, c->w, rows, c->ws.act_a, c->ws.mod, c->d_status, st, &c->prof));
   RolloutBufs b{emb,        emb_pc,    goal,      goal_pc, cand,      c->ws.act_a, c->ws.mod,
-                c->ws.x,    c->ws.x2,  c->ws.xs,  c->ws.part, c->ws.part_stride, c->ws.a_op, c->ws.attn, c->ws.h,
+                c->ws.x,    c->ws.x2,  c->ws.xs,  c->ws.part_a, c->ws.part_b, c->ws.part_stride, c->ws.a_op,
+                c->ws.attn, c->ws.h,
                 c->ws.pred, costs};
   const int n_calls = T - H + 1;
   auto geom = [&](int k) {
@@ -438,7 +442,18 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
       return v ? std::atoi(v) : -1;
     }();
     const int ln_prebuilt = rows8 > (pre_rows >= 0 ? pre_rows : 512 / (m.D / 12)) ? 1 : 0;
-    return CallGeom{NC, S, T, H, w, start, cpt, nt, rows8, ln_prebuilt, k, k == n_calls - 1, 1, 0, 128};
+    // FC1 + GELU + FC2 fused into one kernel when the operand is built in-kernel (small
+    // tiles) at width 192 / MLP 768: one CTA per (tile, 192 hidden units), whose FC1
+    // accumulator is staged through the 72 KB of FC1 weight slots (at most 64 rows).
+    // LEWM_FFN_FUSED=0 keeps the two-kernel path.
+    static const int ffn_env = [] {
+      const char* v = std::getenv("LEWM_FFN_FUSED");
+      return v ? std::atoi(v) : 1;
+    }();
+    const int fc2_parts = (m.D == 192 && m.mlp == 4 * 192) ? 4 : 2;
+    const int ffn_fused = (ffn_env != 0 && !ln_prebuilt && rows8 <= 64 && fc2_parts == 4) ? 1 : 0;
+    return CallGeom{NC,        S, T, H, w, start, cpt, nt, rows8, ln_prebuilt, ffn_fused,
+                    fc2_parts, k, k == n_calls - 1, 1, 0, 128};
   };
   for (int k = 0; k < n_calls; ++k) {
     CallGeom g = geom(k);

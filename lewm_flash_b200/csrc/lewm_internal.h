@@ -76,6 +76,9 @@ struct CallGeom {
   int n_tiles;  // window tiles
   int rows8;    // rows of a tile that operand copies move: cpt * w rounded up to 8 (<= 128)
   int ln_prebuilt;  // 1: QKV / FC1 operands are built by k_ln_operand and bulk-copied
+  int ffn_fused;    // 1: FC1 + GELU + FC2 run as one kernel per (tile, hidden quarter)
+  int fc2_parts;    // K parts of FC2's partial sums (4 hidden quarters at D 192 / MLP 768, else 2),
+                    // the same on both FFN paths so a row's result does not depend on the batch
   int call;     // prediction slot written by this call
   int last;     // 1: final call, write costs
   // Window of the next call (k_final prepares its layer-0 inputs); unused when last.
@@ -93,8 +96,9 @@ struct RolloutBufs {
   float* x;        // residual stream of this call's window before each layer, [tiles][128][D]
   float* xn;       // residual stream of the next call's window (k_final writes it)
   float* xs;       // residual after the attention half of a layer, [tiles][128][D]
-  float* part;     // K-split partial sums of the last residual GEMM, [2][tiles][128][D]
-  size_t part_stride;  // floats between the two K halves of `part`
+  float* part_a;   // out-proj partial sums, [2][tiles][128][D]
+  float* part_b;   // FC2 partial sums, [2 or 4][tiles][128][D]
+  size_t part_stride;  // floats between consecutive partials of part_a / part_b
   __nv_bfloat16* a_op; // GEMM operand built by k_ln_operand, [tiles][D/64][128x64] pre-swizzled
   __nv_bfloat16* attn;
   __nv_bfloat16* h;

@@ -443,19 +443,49 @@ __global__ void __launch_bounds__(kThreads) k_adaln(DevWeights w, ModelDims md, 
 // moments reduce through shuffles among them. Rows at or past rows8 are skipped (whole
 // warps: the row range bounds are multiples of 8 >= 32 / TPR); window slots without a candidate get
 // zeros.
-// A residual update still pending when a GEMM operand is built: the K-split residual
-// GEMM wrote two partial sums P0, P1, and the residual is r = src + gate * ((P0 + P1) +
-// bias). With bias == nullptr the rows of src are used as they are.
+// A residual update still pending when a GEMM operand is built: the residual-branch GEMM
+// wrote partial sums P0 .. P(n-1) (two K halves, or four hidden quarters of a fused
+// FFN), and the residual is r = src + gate * (sum + bias), the sum taken as (P0 + P1)
+// or ((P0 + P1) + (P2 + P3)). With bias == nullptr the rows of src are used as they are.
 struct ResidUpdate {
   const float* src;     // [tile rows][D] residual before the update (or the final rows)
-  const float* part;    // partial sums of the tile, K half 1 at + part_stride
+  const float* part;    // partial sums of the tile, partial i at + i * part_stride
   size_t part_stride;
+  int nparts;           // 2 or 4
   const float* bias;    // [D] bias of that GEMM, or null: no pending update
   int gate_off;         // mod column of its gate (layer * 6D + chunk * D)
   float* dst;           // [tile rows][D] where the updated rows are written, or null
 };
 
-template <int D, int TPR>
+// Partial sums of a residual-branch GEMM (out-projection, FC2): a tile's block of
+// 128 x D floats holds one slab of 128 rows x D/4 floats per N piece (the columns one
+// CTA computes), so each piece leaves its CTA as a single bulk copy. Within a slab row
+// the 4-float chunks are rotated by part_rot(r): the row-per-thread staging stores in
+// shared memory then hit distinct banks (D/16 chunks a row).
+template <int D>
+__device__ __forceinline__ int part_rot(int r) {
+  return ((D / 16) % 8 == 4) ? (r >> 1) : r;
+}
+// Offset in floats of (row r, column c) inside a tile's partial block.
+template <int D>
+__device__ __forceinline__ int part_off(int r, int c) {
+  constexpr int NT = D / 4, NCH = D / 16;
+  const int piece = c / NT, ch = (c - piece * NT) >> 2;
+  return (piece * 128 + r) * NT + ((ch + part_rot<D>(r)) % NCH) * 4 + (c & 3);
+}
+// Stage a row's chunks [chunk0, chunk0 + N/4) of N piece-local columns into a slab of
+// shared memory laid out like a global partial slab.
+template <int D, int N>
+__device__ __forceinline__ void stage_part_row(float* slab, int r, int chunk0, const float* v) {
+  constexpr int NT = D / 4, NCH = D / 16;
+  const int rot = part_rot<D>(r);
+#pragma unroll
+  for (int i = 0; i < N / 4; ++i)
+    *reinterpret_cast<float4*>(slab + r * NT + ((chunk0 + i + rot) % NCH) * 4) =
+        make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+template <int D, int TPR, int SK = 0>
 __device__ __forceinline__ void build_ln_operand_t(const ResidUpdate& u, const CallGeom& g, int tile,
                                                    const __nv_bfloat16* __restrict__ mod, int mod_cols, int shift_col,
                                                    const float* __restrict__ lg, const float* __restrict__ lb,
@@ -473,8 +503,10 @@ __device__ __forceinline__ void build_ln_operand_t(const ResidUpdate& u, const C
     // All loads of the row first, through the read-only path (none of these buffers is
     // written by this kernel: the updated rows go to u.dst, never u.src), then the
     // update and its write-back, so no load waits behind a store.
-    float4 pa[NCH], pb[NCH], bb[NCH];
+    float4 pa[NCH], pb[NCH], bb[NCH], lgv[NCH], lbv[NCH];
     uint2 gw[NCH];
+    const bool four = u.nparts == 4;
+    LEWM_STAMP(SK, 1);
 #pragma unroll
     for (int k = 0; k < NCH; ++k) {
       const int c = 4 * (part + TPR * k);
@@ -488,12 +520,21 @@ __device__ __forceinline__ void build_ln_operand_t(const ResidUpdate& u, const C
         h = __ldg(reinterpret_cast<const uint2*>(mrow + c));
         a = __ldg(reinterpret_cast<const uint2*>(mrow + D + c));
         if (u.bias) {
+          const int o = part_off<D>(r, c);
           pa[k] = __ldg(reinterpret_cast<const float4*>(u.part + o));
           pb[k] = __ldg(reinterpret_cast<const float4*>(u.part + u.part_stride + o));
+          if (four) {  // (P0 + P1) + (P2 + P3), kept in pa / pb
+            const float4 pc = __ldg(reinterpret_cast<const float4*>(u.part + 2 * u.part_stride + o));
+            const float4 pd = __ldg(reinterpret_cast<const float4*>(u.part + 3 * u.part_stride + o));
+            pa[k] = make_float4(pa[k].x + pb[k].x, pa[k].y + pb[k].y, pa[k].z + pb[k].z, pa[k].w + pb[k].w);
+            pb[k] = make_float4(pc.x + pd.x, pc.y + pd.y, pc.z + pd.z, pc.w + pd.w);
+          }
           bb[k] = __ldg(reinterpret_cast<const float4*>(u.bias + c));
           gw[k] = __ldg(reinterpret_cast<const uint2*>(mod + mbase + u.gate_off + c));
         }
       }
+      lgv[k] = __ldg(reinterpret_cast<const float4*>(lg + c));
+      lbv[k] = __ldg(reinterpret_cast<const float4*>(lb + c));
       xv[4 * k] = t.x;
       xv[4 * k + 1] = t.y;
       xv[4 * k + 2] = t.z;
@@ -523,6 +564,7 @@ __device__ __forceinline__ void build_ln_operand_t(const ResidUpdate& u, const C
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < NPER; ++i) s += xv[i];
+    LEWM_STAMP(SK, 2);
 #pragma unroll
     for (int o = 1; o < TPR; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     const float mean = s * (1.0f / D);
@@ -532,6 +574,7 @@ __device__ __forceinline__ void build_ln_operand_t(const ResidUpdate& u, const C
 #pragma unroll
     for (int o = 1; o < TPR; o <<= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
     const float rstd = rsqrtf(q * (1.0f / D) + 1e-6f);
+    LEWM_STAMP(SK, 3);
     float s2 = 0.f;
 #pragma unroll
     for (int k = 0; k < NCH; ++k) {
@@ -553,11 +596,11 @@ __device__ __forceinline__ void build_ln_operand_t(const ResidUpdate& u, const C
 #pragma unroll
     for (int o = 1; o < TPR; o <<= 1) q2 += __shfl_xor_sync(0xffffffffu, q2, o);
     const float rstd2 = rsqrtf(q2 * (1.0f / D) + 1e-5f);
+    LEWM_STAMP(SK, 4);
 #pragma unroll
     for (int k = 0; k < NCH; ++k) {
       const int c = 4 * (part + TPR * k);
-      const float4 g4 = __ldg(reinterpret_cast<const float4*>(lg + c));
-      const float4 b4 = __ldg(reinterpret_cast<const float4*>(lb + c));
+      const float4 g4 = lgv[k], b4 = lbv[k];
       const float* y = xv + 4 * k;
       uint2 pk = make_uint2(0u, 0u);
       if (m.valid) {
@@ -566,6 +609,7 @@ __device__ __forceinline__ void build_ln_operand_t(const ResidUpdate& u, const C
       }
       *reinterpret_cast<uint2*>(sA + (c >> 6) * kBlk + sw128_off(r, c & 63)) = pk;
     }
+    LEWM_STAMP(SK, 5);
   }
 }
 
@@ -573,12 +617,12 @@ __device__ __forceinline__ void build_ln_operand_t(const ResidUpdate& u, const C
 // tile size: all 16 warps work on the first rows, and larger tiles loop over further
 // passes. The reduction order of the row moments is then the same for every tile
 // geometry, so an env's results do not depend on how many candidates share its call.
-template <int D>
+template <int D, int SK = 0>
 __device__ __forceinline__ void build_ln_operand(const ResidUpdate& u, const CallGeom& g, int tile,
                                                  const __nv_bfloat16* __restrict__ mod, int mod_cols, int shift_col,
                                                  const float* __restrict__ lg, const float* __restrict__ lb,
                                                  uint8_t* sA, int tid) {
-  build_ln_operand_t<D, D / 12>(u, g, tile, mod, mod_cols, shift_col, lg, lb, sA, tid, 0, g.rows8);
+  build_ln_operand_t<D, D / 12, SK>(u, g, tile, mod, mod_cols, shift_col, lg, lb, sA, tid, 0, g.rows8);
 }
 
 // Layer-0 residual row x0 = history row + position embedding of window position p.
@@ -702,11 +746,11 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     }
   } else {
     const size_t t0 = (size_t)tile * 128 * D;
-    ResidUpdate u{b.x + t0, nullptr, 0, nullptr, 0, nullptr};
+    ResidUpdate u{b.x + t0, nullptr, 0, 2, nullptr, 0, nullptr};
     if (layer > 0)
-      u = ResidUpdate{b.xs + t0, b.part + t0, b.part_stride, w.b2 + (layer - 1) * D, (layer - 1) * 6 * D + 5 * D,
-                      head == 0 ? b.x + t0 : nullptr};
-    build_ln_operand<D>(u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D, w.attn_ln_w + layer * D,
+      u = ResidUpdate{b.xs + t0, b.part_b + t0, b.part_stride, g.fc2_parts, w.b2 + (layer - 1) * D,
+                      (layer - 1) * 6 * D + 5 * D, head == 0 ? b.x + t0 : nullptr};
+    build_ln_operand<D, 6>(u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D, w.attn_ln_w + layer * D,
                         w.attn_ln_b + layer * D, sA, tid);
   }
   fence_async_smem();
@@ -861,15 +905,15 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
 
 // ---------------------------------------------------------------- K-split residual-branch GEMM
 // Bytes after the operand slots: 5 barriers, the TMEM slot and a flag.
-constexpr int kKSplit = 2;  // K halves of the out-projection / FC2 GEMMs
+constexpr int kKSplit = 2;  // K halves of the out-projection GEMM (FC2: CallGeom::fc2_parts)
 template <int D>
 __host__ __device__ constexpr int resid_extra() { return 8 * 5 + 16; }
 
-// part[kh][rows][n-tile] = A[:, K half kh] . B[n-tile, K half kh]^T for the out-projection
-// or FC2 of a layer. Grid (tiles, 4 N tiles, 2 K halves): each CTA issues half the MMAs
-// and all its operand blocks fit one copy round. The bias, gate and residual add are
-// applied by the consumer of the sum (the next GEMM's operand builder, or k_final),
-// which adds the two halves in a fixed order. Warp 0 issues MMAs, warp 1 refills the
+// part[kh][rows][n-tile] = A[:, K part kh] . B[n-tile, K part kh]^T for the out-projection
+// or FC2 of a layer. Grid (tiles, 4 N tiles, K parts): each CTA issues 1 / gridDim.z of
+// the MMAs and all its operand blocks fit one copy round. The bias, gate and residual
+// add are applied by the consumer of the sum (the next GEMM's operand builder, or
+// k_final), which adds the parts in a fixed order. Warp 0 issues MMAs, warp 1 refills the
 // operand slots when they do not all fit.
 template <int D>
 __global__ void __launch_bounds__(kThreads) k_partial_gemm(const __nv_bfloat16* __restrict__ gA, int nkb,
@@ -883,7 +927,7 @@ __global__ void __launch_bounds__(kThreads) k_partial_gemm(const __nv_bfloat16* 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const int tile = blockIdx.x, nt = blockIdx.y, kh = blockIdx.z;
-  const int kcount = nkb / kKSplit, kb0 = kh * kcount;
+  const int kcount = nkb / (int)gridDim.z, kb0 = kh * kcount;
   const ResidLayout lay = resid_layout(g.rows8, kcount, B_BLK, C::KG, resid_extra<D>());
   uint8_t* sA = smem;
   uint8_t* sB = smem + lay.b_off;
@@ -941,11 +985,23 @@ __global__ void __launch_bounds__(kThreads) k_partial_gemm(const __nv_bfloat16* 
   float v[CW];
   tmem_ld_cols<CW>(taddr, v);
   LEWM_STAMP(skind, 7);
-  if (ok && r < g.rows8) {
-    float4* dst = reinterpret_cast<float4*>(part + kh * part_stride + ((size_t)tile * 128 + r) * D + nt * NT +
-                                            slice * CW);
-#pragma unroll
-    for (int i = 0; i < CW / 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  // Slab of this piece staged in the operand slots (dead once the MMAs retired), then
+  // one bulk copy. The slab (rows8 x NT floats) fits below the barriers: the A slots
+  // alone hold rows8 x 128 bytes per K block plus a 16 KB tail.
+  float* slab = reinterpret_cast<float*>(smem);
+  const bool fits = g.rows8 * NT * 4 <= lay.v_off;
+  if (fits && r < g.rows8) stage_part_row<D, CW>(slab, r, slice * (CW / 4), v);
+  fence_async_smem();
+  __syncthreads();
+  LEWM_STAMP(skind, 9);
+  if (tid == 0) {
+    if (ok && fits) {
+      bulk_s2g(part + kh * part_stride + ((size_t)tile * 4 + nt) * 128 * NT, slab, g.rows8 * NT * 4);
+      bulk_commit();
+      bulk_wait_read();
+    } else if (!fits) {
+      atomicOr(status, LEWM_DEV_BADARG);
+    }
   }
   LEWM_STAMP(skind, 6);
   tc_fence_before();
@@ -1021,7 +1077,7 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
     }
   } else {
     const size_t t0 = (size_t)tile * 128 * D;
-    const ResidUpdate u{b.x + t0, b.part + t0, b.part_stride, w.out_b + layer * D, layer * 6 * D + 2 * D,
+    const ResidUpdate u{b.x + t0, b.part_a + t0, b.part_stride, 2, w.out_b + layer * D, layer * 6 * D + 2 * D,
                         nt == 0 ? b.xs + t0 : nullptr};
     build_ln_operand<D>(u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D + 3 * D, w.ffn_ln_w + layer * D,
                         w.ffn_ln_b + layer * D, sA, tid);
@@ -1099,6 +1155,190 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
   if (warp == 0) tmem_dealloc(tmem, NT);
 }
 
+// ---------------------------------------------------------------- fused feed-forward (small tiles)
+// One CTA per (row tile, hidden quarter q of 192 units), for tiles whose operand is built
+// in-kernel (at most 32 rows) at width 192: the FC1 operand (s = r + gate_msa *
+// (out-proj + bias), LN2 -> modulate -> ffn.norm; the q == 0 CTAs write s back), FC1 on
+// the quarter's 192 hidden units (N = 192, K = D) + bias -> GELU into shared memory, then
+// the quarter's FC2 contribution to all D outputs (N = 192, K = 192) as the fp32 partial
+// P_q. The consumer adds the four quarters in a fixed order. Replaces k_fc1 and the FC2
+// k_partial_gemm: one kernel boundary and the global round trip of h fewer per layer.
+// The FC1 accumulator is staged through shared memory so all 16 warps share the GELUs
+// (TMEM lanes 0-31, the tile's rows, belong to 4 warps).
+constexpr int kFfnQ = 192;  // hidden units per fused-FFN CTA
+template <int D>
+constexpr int smem_ffn() {
+  return 1024 + (D / 64) * kBlk + (D / 64) * kFfnQ * 128 + (kFfnQ / 64) * D * 128 + kFfnQ * 4 + 8 * 4 + 16;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) k_ffn(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b, int layer,
+                                                  uint32_t* status) {
+  constexpr int KB = D / 64;          // K blocks of FC1
+  constexpr int HB = kFfnQ / 64;      // K blocks of FC2 (this quarter's hidden units)
+  constexpr int W1_BLK = kFfnQ * 128; // [192 hidden x 64] bf16
+  constexpr int W2_BLK = D * 128;     // [D x 64] bf16
+  constexpr int NT2 = Cfg<D>::NT_OUT; // rows of one packed FC2 weight piece (N tile)
+  constexpr int kStage = kFfnQ + 1;   // floats per staged accumulator row
+  static_assert(HB == KB, "h reuses the operand blocks");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sA = smem;                                  // FC1 operand, then h (FC2 operand)
+  uint8_t* sW1 = smem + KB * kBlk;                     // FC1 weights, then the staged accumulator
+  uint8_t* sW2 = sW1 + KB * W1_BLK;
+  float* sb1 = reinterpret_cast<float*>(sW2 + HB * W2_BLK);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sb1 + kFfnQ);  // [0] W1+b1, [1] W2, [2] FC1 done, [3] FC2 done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+  float* stage = reinterpret_cast<float*>(sW1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x, q = blockIdx.y;
+  const int nmlp = md.mlp / 128, nkm = md.mlp / 64;
+  if (tid == 0) {
+    for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&bars[0], KB * W1_BLK + kFfnQ * 4);
+    mbar_arrive_expect_tx(&bars[1], HB * W2_BLK);
+  }
+  __syncwarp();
+  if (warp == 0) {  // weights before the wait: 2 x KB + 4 x HB + 1 copies in one instruction
+    const int h0 = kFfnQ * q;                 // first hidden unit
+    const int hb0 = h0 / 128, r0 = h0 % 128;  // its packed 128-row block and row (0 or 64)
+    if (lane < 2 * KB) {
+      // FC1 block kb: rows [r0, 128) of block hb0, then rows [0, 64 + r0) of block hb0 + 1
+      const int kb = lane >> 1, second = lane & 1;
+      const __nv_bfloat16* src =
+          w.w1 + ((size_t)(layer * nmlp + hb0 + second) * KB + kb) * kBlkElems + (second ? 0 : (size_t)r0 * 64);
+      const uint32_t bytes = second ? (64 + r0) * 128 : (128 - r0) * 128;
+      bulk_g2s(sW1 + kb * W1_BLK + (second ? (128 - r0) * 128 : 0), src, bytes, &bars[0]);
+    } else if (lane < 2 * KB + 4 * HB) {
+      // FC2 block j: the four packed N-tile pieces [NT2 x 64] of hidden K block 3q + j
+      const int i = lane - 2 * KB, j = i >> 2, nt = i & 3;
+      const __nv_bfloat16* src =
+          w.w2 + (((size_t)layer * 4 + nt) * nkm + HB * q + j) * NT2 * 64;
+      bulk_g2s(sW2 + j * W2_BLK + nt * NT2 * 128, src, NT2 * 128, &bars[1]);
+    } else if (lane == 2 * KB + 4 * HB) {
+      bulk_g2s(sb1, w.b1 + layer * md.mlp + kFfnQ * q, kFfnQ * 4, &bars[0]);
+    }
+  }
+  __syncwarp();
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  LEWM_STAMP(4, 1);
+  griddep_wait();
+  LEWM_STAMP(4, 2);
+  griddep_launch();
+  {  // FC1 operand from the residual rows with the out-projection update pending
+    const size_t t0 = (size_t)tile * 128 * D;
+    const ResidUpdate u{b.x + t0, b.part_a + t0, b.part_stride, 2, w.out_b + layer * D, layer * 6 * D + 2 * D,
+                        q == 0 ? b.xs + t0 : nullptr};
+    build_ln_operand<D, 7>(u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D + 3 * D, w.ffn_ln_w + layer * D,
+                        w.ffn_ln_b + layer * D, sA, tid);
+  }
+  fence_async_smem();
+  LEWM_STAMP(4, 5);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t idesc = idesc_bf16(128, 192);
+  if (warp == 0) {  // FC1: D[0, 192) = A . W1^T
+    const bool got = __all_sync(0xffffffffu, mbar_wait(&bars[0], 0, status));
+    tc_fence_after();
+    if (lane == 0) {
+      if (got) {
+        uint64_t ad = sdesc_sw128(smem_u32(sA)), bd = sdesc_sw128(smem_u32(sW1));
+        for (int kb = 0; kb < KB; ++kb) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) umma_bf16(tmem, ad + 2 * j, bd + 2 * j, idesc, (kb | j) ? 1u : 0u);
+          ad += kBlk >> 4;
+          bd += W1_BLK >> 4;
+        }
+      }
+      umma_commit(&bars[2]);
+    }
+    __syncwarp();
+  }
+  const bool ok1 = cta_wait_mma(&bars[2], status, tmem_slot + 1);
+  LEWM_STAMP(4, 3);
+  tc_fence_after();
+  const int quad = warp & 3, slice = warp >> 2;
+  const int r = quad * 32 + lane;
+  if (quad * 32 < g.rows8) {  // stage the accumulator rows of the tile (whole warps load)
+    float v[48];
+    tmem_ld_cols<48>(tmem + ((uint32_t)(quad * 32) << 16) + slice * 48, v);
+    if (r < g.rows8) {
+      float* sr = stage + r * kStage + slice * 48;
+#pragma unroll
+      for (int i = 0; i < 48; ++i) sr[i] = v[i];
+    }
+  }
+  __syncthreads();
+  LEWM_STAMP(4, 0);
+  // bias + GELU over all threads, 4 columns per item, into h (the FC2 operand, in sA)
+  for (int it = tid; it < g.rows8 * (kFfnQ / 4); it += kThreads) {
+    const int rr = it / (kFfnQ / 4), c = (it - rr * (kFfnQ / 4)) * 4;
+    const float* sr = stage + rr * kStage + c;
+    uint2 pk = make_uint2(0u, 0u);
+    if (ok1 && map_row(g, tile, rr).valid) {  // window slots without a candidate stay zero
+      pk.x = pack_bf16x2(gelu_f(sr[0] + sb1[c]), gelu_f(sr[1] + sb1[c + 1]));
+      pk.y = pack_bf16x2(gelu_f(sr[2] + sb1[c + 2]), gelu_f(sr[3] + sb1[c + 3]));
+    }
+    *reinterpret_cast<uint2*>(sA + (c >> 6) * kBlk + sw128_off(rr, c & 63)) = pk;
+  }
+  fence_async_smem();
+  LEWM_STAMP(4, 9);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) {  // FC2 partial: D[0, 192) = h . W2^T over this quarter's hidden units (FC1's
+                    // columns: every thread's loads of them completed before the barrier)
+    const bool got = __all_sync(0xffffffffu, mbar_wait(&bars[1], 0, status));
+    tc_fence_after();
+    if (lane == 0) {
+      if (got) {
+        uint64_t ad = sdesc_sw128(smem_u32(sA)), bd = sdesc_sw128(smem_u32(sW2));
+        for (int kb = 0; kb < HB; ++kb) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) umma_bf16(tmem, ad + 2 * j, bd + 2 * j, idesc, (kb | j) ? 1u : 0u);
+          ad += kBlk >> 4;
+          bd += W2_BLK >> 4;
+        }
+      }
+      umma_commit(&bars[3]);
+    }
+    __syncwarp();
+  }
+  const bool ok2 = cta_wait_mma(&bars[3], status, tmem_slot + 1);
+  LEWM_STAMP(4, 4);
+  tc_fence_after();
+  // Warp slice s holds N piece s (D/4 = 48 columns): staged as four slabs of rows8 x 48
+  // floats in the FC1 weight region (free since FC1 retired; the staged FC1 rows were
+  // read before the barrier above), then one bulk copy per piece.
+  static_assert(D / 4 == 48, "one N piece per warp slice");
+  float* slabs = stage;
+  if (quad * 32 < g.rows8) {
+    float v[48];
+    tmem_ld_cols<48>(tmem + ((uint32_t)(quad * 32) << 16) + slice * 48, v);
+    LEWM_STAMP(4, 8);
+    if (r < g.rows8) stage_part_row<D, 48>(slabs + slice * g.rows8 * 48, r, 0, v);
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  LEWM_STAMP(4, 7);
+  if (warp == 0 && lane < 4) {  // each issuing lane waits for its own copy's reads
+    if (ok1 && ok2)
+      bulk_s2g(b.part_b + q * b.part_stride + ((size_t)tile * 4 + lane) * 128 * 48, slabs + lane * g.rows8 * 48,
+               g.rows8 * 48 * 4);
+    bulk_commit();
+    bulk_wait_read();
+  }
+  LEWM_STAMP(4, 6);
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
 // ---------------------------------------------------------------- final LayerNorm + history / cost
 // The last call: warp per candidate, final LayerNorm of the window's last token and its
 // squared distance to the goal. Earlier calls: warp per (candidate, row p of the next
@@ -1127,6 +1367,7 @@ __global__ void __launch_bounds__(128) k_final(DevWeights w, ModelDims md, CallG
     const int tile = cand / g.cpt;
     const int r = (cand - tile * g.cpt) * g.w + (g.w - 1);
     const size_t o = ((size_t)tile * 128 + r) * D;
+    const float* pt = b.part_b + (size_t)tile * 128 * D;  // the tile's partial block
     const int tok = cand * g.T + g.start + g.w - 1;
     const __nv_bfloat16* gate = b.mod + (size_t)tok * (md.L * 6 * D) + (md.L - 1) * 6 * D + 5 * D;
     const float* b2 = w.b2 + (md.L - 1) * D;
@@ -1136,8 +1377,15 @@ __global__ void __launch_bounds__(128) k_final(DevWeights w, ModelDims md, CallG
     for (int i = 0; i < NP; ++i) {
       const int c = 64 * i + 2 * lane;
       const float2 xs = *reinterpret_cast<const float2*>(b.xs + o + c);
-      const float2 p0 = *reinterpret_cast<const float2*>(b.part + o + c);
-      const float2 p1 = *reinterpret_cast<const float2*>(b.part + b.part_stride + o + c);
+      const int po = part_off<D>(r, c);
+      float2 p0 = *reinterpret_cast<const float2*>(pt + po);
+      float2 p1 = *reinterpret_cast<const float2*>(pt + b.part_stride + po);
+      if (g.fc2_parts == 4) {  // four hidden-quarter partials: (P0 + P1) + (P2 + P3)
+        const float2 p2 = *reinterpret_cast<const float2*>(pt + 2 * b.part_stride + po);
+        const float2 p3 = *reinterpret_cast<const float2*>(pt + 3 * b.part_stride + po);
+        p0 = make_float2(p0.x + p1.x, p0.y + p1.y);
+        p1 = make_float2(p2.x + p3.x, p2.y + p3.y);
+      }
       const float2 bb = *reinterpret_cast<const float2*>(b2 + c);
       const float2 gg = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(gate + c));
       v[i] = make_float2(xs.x + gg.x * ((p0.x + p1.x) + bb.x), xs.y + gg.y * ((p0.y + p1.y) + bb.y));
@@ -1208,6 +1456,7 @@ constexpr int smem_fc1() { return 1024 + Cfg<D>::KB * kBlk + Cfg<D>::QKV_ST * NT
 static_assert(smem_qkv<192>() <= 232448 && smem_qkv<384>() <= 232448, "qkv smem");
 static_assert(smem_embed_out<384>() <= 232448 && smem_adaln<384>() <= 232448, "embed/adaln smem");
 static_assert(smem_fc1<384, kFc1N>() <= 232448 && smem_resid<384>() <= 232448, "fc smem");
+static_assert(smem_ffn<192>() <= 232448, "ffn smem");
 
 template <int D>
 cudaError_t set_smem_attrs() {
@@ -1218,6 +1467,8 @@ cudaError_t set_smem_attrs() {
     return e;
   if ((e = cudaFuncSetAttribute(k_adaln<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_adaln<D>()))) return e;
   if ((e = cudaFuncSetAttribute(k_qkv_attn<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_qkv<D>()))) return e;
+  if constexpr (D == 192)
+    if ((e = cudaFuncSetAttribute(k_ffn<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_ffn<D>()))) return e;
   if ((e = cudaFuncSetAttribute(k_partial_gemm<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_resid<D>())))
     return e;
   if ((e = cudaFuncSetAttribute(k_fc1<D, kFc1N>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_fc1<D, kFc1N>())))
@@ -1280,8 +1531,10 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
   const int mcols = md.L * 6 * D;
   for (int l = 0; l < md.L; ++l) {
     if (g.ln_prebuilt) {  // QKV operand of every tile: LN1 -> modulate -> attn.norm (+ pending FC2 update)
-      ResidUpdate u{b.x, nullptr, 0, nullptr, 0, nullptr};
-      if (l > 0) u = ResidUpdate{b.xs, b.part, b.part_stride, w.b2 + (l - 1) * D, (l - 1) * 6 * D + 5 * D, b.x};
+      ResidUpdate u{b.x, nullptr, 0, 2, nullptr, 0, nullptr};
+      if (l > 0)
+        u = ResidUpdate{b.xs, b.part_b, b.part_stride, g.fc2_parts, w.b2 + (l - 1) * D,
+                        (l - 1) * 6 * D + 5 * D, b.x};
       if (prof) prof->begin(st);
       LEWM_TRY(launch_k(k_ln_operand<D>, op_grid, dim3(kThreads), 0, st, u, g, (const __nv_bfloat16*)b.mod, mcols,
                         l * 6 * D, w.attn_ln_w + l * D, w.attn_ln_b + l * D, b.a_op));
@@ -1297,29 +1550,39 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
                       resid_layout(g.rows8, nkb_inner / kKSplit, Cfg<D>::NT_OUT * 128, Cfg<D>::KG, resid_extra<D>())
                           .bytes,
                       st, (const __nv_bfloat16*)b.attn, nkb_inner,
-                      (const __nv_bfloat16*)(w.wout + (size_t)l * 4 * nkb_inner * Cfg<D>::NT_OUT * 64), g, b.part,
+                      (const __nv_bfloat16*)(w.wout + (size_t)l * 4 * nkb_inner * Cfg<D>::NT_OUT * 64), g, b.part_a,
                       b.part_stride, 5, status));
     if (prof) prof->end(KC_OUT, 2.0 * rows * md.inner * D, st);
     if (g.ln_prebuilt) {  // FC1 operand: s = r + gate_msa * (out-proj + bias), LN2 -> modulate -> ffn.norm
-      const ResidUpdate u{b.x, b.part, b.part_stride, w.out_b + l * D, l * 6 * D + 2 * D, b.xs};
+      const ResidUpdate u{b.x, b.part_a, b.part_stride, 2, w.out_b + l * D, l * 6 * D + 2 * D, b.xs};
       if (prof) prof->begin(st);
       LEWM_TRY(launch_k(k_ln_operand<D>, op_grid, dim3(kThreads), 0, st, u, g, (const __nv_bfloat16*)b.mod, mcols,
                         l * 6 * D + 3 * D, w.ffn_ln_w + l * D, w.ffn_ln_b + l * D, b.a_op));
       if (prof) prof->end(KC_FC1, 0.0, st);
+    }
+    if (g.ffn_fused) {  // FC1 + GELU + FC2 quarter partials in one kernel
+      if constexpr (D == 192) {
+        if (prof) prof->begin(st);
+        LEWM_TRY(launch_k(k_ffn<D>, dim3(g.n_tiles, md.mlp / kFfnQ), dim3(kThreads), smem_ffn<D>(), st, w, md, g, b,
+                          l, status));
+        if (prof) prof->end(KC_FC1, 4.0 * rows * D * md.mlp, st);
+        continue;
+      }
+      return cudaErrorInvalidValue;
     }
     if (prof) prof->begin(st);
     LEWM_TRY(launch_k(k_fc1<D, kFc1N>, dim3(g.n_tiles, md.mlp / kFc1N), dim3(kThreads), smem_fc1<D, kFc1N>(), st, w,
                       md, g, b, l,
                       status));
     if (prof) prof->end(KC_FC1, 2.0 * rows * D * md.mlp, st);
-    // FC2 partial sums (bias, gate_mlp and residual applied by the next QKV operand builder
-    // or, after the last layer, by k_final)
+    // FC2 partial sums over fc2_parts K parts (bias, gate_mlp and residual applied by the
+    // next QKV operand builder or, after the last layer, by k_final)
     if (prof) prof->begin(st);
-    LEWM_TRY(launch_k(k_partial_gemm<D>, dim3(g.n_tiles, 4, kKSplit), dim3(kThreads),
-                      resid_layout(g.rows8, nkb_mlp / kKSplit, Cfg<D>::NT_OUT * 128, Cfg<D>::KG, resid_extra<D>())
+    LEWM_TRY(launch_k(k_partial_gemm<D>, dim3(g.n_tiles, 4, g.fc2_parts), dim3(kThreads),
+                      resid_layout(g.rows8, nkb_mlp / g.fc2_parts, Cfg<D>::NT_OUT * 128, Cfg<D>::KG, resid_extra<D>())
                           .bytes,
                       st, (const __nv_bfloat16*)b.h, nkb_mlp,
-                      (const __nv_bfloat16*)(w.w2 + (size_t)l * 4 * nkb_mlp * Cfg<D>::NT_OUT * 64), g, b.part,
+                      (const __nv_bfloat16*)(w.w2 + (size_t)l * 4 * nkb_mlp * Cfg<D>::NT_OUT * 64), g, b.part_b,
                       b.part_stride, 3, status));
     if (prof) prof->end(KC_FC2, 2.0 * rows * md.mlp * D, st);
   }
