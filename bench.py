@@ -42,13 +42,14 @@ F_CANON = 9 * L * F_BLOCK_TOKEN + T * L * 2 * D * 6 * D + T * 2 * (A * A + A * 4
 
 
 # DRAM bytes (read + write) of one launch of the dominant kernel classes, from the ncu
-# captures summarised in profiles/k_qkv_attn_w1_6tiles.md and
-# profiles/k_partial_gemm_outproj_fc2_w3_8tiles.md (ncu flushes L2 between passes, so
-# these are cold-cache first-touch bytes; the timed run keeps weights in L2).
+# captures summarised in profiles/k_qkv_attn_s60_w3_6tiles.md, profiles/k_ffn_s60_w3_6tiles.md
+# and profiles/k_partial_gemm_outproj_fc2_s300_w3_8tiles.md (ncu flushes L2 between passes,
+# so these are cold-cache first-touch bytes; the timed run keeps weights in L2).
 NCU_TRAFFIC = {
-    "qkv_attn": {"bytes": 1308416, "launch": "QKV + attention, 240 rows (window 1), 6 tiles x 16 heads"},
-    "out_proj": {"bytes": 2381056, "launch": "out-proj K halves, 900 rows (300 candidates x window 3), 8 tiles"},
-    "fc2": {"bytes": 1791488, "launch": "FC2 K halves, 900 rows (300 candidates x window 3), 8 tiles"},
+    "qkv_attn": {"bytes": 2118912, "launch": "QKV + attention, 180 rows (60 candidates x window 3), 6 tiles x 16 heads"},
+    "ffn": {"bytes": 1252608, "launch": "fused FFN, 180 rows (60 candidates x window 3), 6 tiles x 4 hidden quarters"},
+    "out_proj": {"bytes": 2381824, "launch": "out-proj K halves, 900 rows (300 candidates x window 3), 8 tiles"},
+    "fc2": {"bytes": 1792256, "launch": "FC2 hidden quarters, 900 rows (300 candidates x window 3), 8 tiles"},
 }
 
 
@@ -179,6 +180,35 @@ def reference_arm(args, rank, world):
     return 0
 
 
+def model_cost_case(S, repeat):
+    """R predictor rollouts of S candidates (5 calls x 6 layers each, windows 1, 2, 3, 3, 3):
+    a fixed launch sequence for ncu captures of one kernel at a known geometry."""
+    import torch
+
+    from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
+    from lewm_flash_b200.runtime import Runtime
+
+    dev = torch.device("cuda", 0)
+    desc = ModelDesc()
+    rt = Runtime(desc, synthetic_state_dict(desc, 0), dev)
+    rng = np.random.default_rng(7)
+    emb = torch.as_tensor(rng.standard_normal((1, 1, desc.dim)), dtype=torch.float32, device=dev)
+    goal = torch.as_tensor(rng.standard_normal((1, 1, desc.dim)), dtype=torch.float32, device=dev)
+    cand = torch.as_tensor(rng.standard_normal((1, S, 5, desc.action_dim)), dtype=torch.float32, device=dev)
+    ms = []
+    for _ in range(repeat):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        costs = rt.model_cost(emb, goal, cand)
+        b.record()
+        torch.cuda.synchronize(dev)
+        ms.append(a.elapsed_time(b))
+    rt.sync()
+    print(json.dumps({"case": "model_cost", "samples": S, "ms": ms, "cost0": float(costs[0, 0])}))
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -187,7 +217,13 @@ def main() -> int:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-baseline-plans", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--model-cost", type=int, default=0, metavar="S",
+                    help="profiling case: time R model-cost calls of S candidates (1 env, horizon 5, "
+                         "history 1, window 3) and exit; no bench line")
+    ap.add_argument("--repeat", type=int, default=3)
     args = ap.parse_args()
+    if args.model_cost:
+        return model_cost_case(args.model_cost, args.repeat)
 
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

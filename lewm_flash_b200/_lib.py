@@ -86,7 +86,8 @@ SIGNATURES = {
     "lewm_profile_plan": (C.c_int, [C.c_void_p, C.POINTER(PlanDescC), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
 }
-KERNEL_CLASSES = ("embed", "adaln", "qkv_attn", "out_proj", "fc1", "fc2", "final", "sample", "refit", "prep0")
+KERNEL_CLASSES = ("embed", "adaln", "qkv_attn", "out_proj", "fc1", "fc2", "final", "sample", "refit", "prep0", "ffn",
+                  "ln_operand")
 
 
 def lib():

@@ -16,6 +16,8 @@
 
 using namespace lewm;
 
+static_assert(KC_COUNT == LEWM_KERNEL_CLASSES, "kernel classes of lewm_profile_plan");
+
 namespace {
 
 thread_local std::string g_create_error;

@@ -110,7 +110,7 @@ struct RolloutBufs {
 // records an event pair and the algorithmic FLOPs of that launch under a kernel
 // class; lewm_profile_plan sums them after a synchronize.
 enum KernelClass { KC_EMBED = 0, KC_ADALN, KC_QKV_ATTN, KC_OUT, KC_FC1, KC_FC2, KC_FINAL, KC_SAMPLE, KC_REFIT,
-                   KC_PREP0, KC_COUNT };
+                   KC_PREP0, KC_FFN, KC_LN_OP, KC_COUNT };
 struct Prof {
   bool on = false;
   struct Rec {

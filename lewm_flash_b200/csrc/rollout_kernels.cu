@@ -1538,7 +1538,7 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
       if (prof) prof->begin(st);
       LEWM_TRY(launch_k(k_ln_operand<D>, op_grid, dim3(kThreads), 0, st, u, g, (const __nv_bfloat16*)b.mod, mcols,
                         l * 6 * D, w.attn_ln_w + l * D, w.attn_ln_b + l * D, b.a_op));
-      if (prof) prof->end(KC_QKV_ATTN, 0.0, st);
+      if (prof) prof->end(KC_LN_OP, 0.0, st);
     }
     if (prof) prof->begin(st);
     LEWM_TRY(launch_k(k_qkv_attn<D>, dim3(g.n_tiles, md.heads), dim3(kThreads), smem_qkv<D>(), st, w, md, g, b, l,
@@ -1558,14 +1558,14 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
       if (prof) prof->begin(st);
       LEWM_TRY(launch_k(k_ln_operand<D>, op_grid, dim3(kThreads), 0, st, u, g, (const __nv_bfloat16*)b.mod, mcols,
                         l * 6 * D + 3 * D, w.ffn_ln_w + l * D, w.ffn_ln_b + l * D, b.a_op));
-      if (prof) prof->end(KC_FC1, 0.0, st);
+      if (prof) prof->end(KC_LN_OP, 0.0, st);
     }
     if (g.ffn_fused) {  // FC1 + GELU + FC2 quarter partials in one kernel
       if constexpr (D == 192) {
         if (prof) prof->begin(st);
         LEWM_TRY(launch_k(k_ffn<D>, dim3(g.n_tiles, md.mlp / kFfnQ), dim3(kThreads), smem_ffn<D>(), st, w, md, g, b,
                           l, status));
-        if (prof) prof->end(KC_FC1, 4.0 * rows * D * md.mlp, st);
+        if (prof) prof->end(KC_FFN, 4.0 * rows * D * md.mlp, st);
         continue;
       }
       return cudaErrorInvalidValue;
