@@ -485,40 +485,86 @@ __device__ __forceinline__ void stage_part_row(float* slab, int r, int chunk0, c
         make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
 }
 
+// Loads of one builder row (D / TPR columns of this thread, in 4-column chunks) that
+// come from kernels at least two launches back: the modulation rows (written by k_adaln
+// at the start of the rollout) and — where the caller says so — the residual rows. A
+// kernel's CTAs start only after every CTA of the kernel before it passed
+// griddepcontrol.wait (each kernel waits before it triggers its dependents), so by then
+// the kernel two back has completed: these loads may be issued before this kernel's own
+// wait. They bypass L1 (ld.global.cg) and read the coherent L2.
+template <int D, int TPR>
+struct LnEarly {
+  static constexpr int NCH = D / TPR / 4;
+  float4 src[NCH];
+  uint2 shift[NCH], scale[NCH], gate[NCH];
+  bool src_loaded;
+};
+
+template <int D, int TPR>
+__device__ __forceinline__ void ln_row_early(LnEarly<D, TPR>& E, const ResidUpdate& u, const RowMap& m, int r,
+                                             int part, const __nv_bfloat16* __restrict__ mod, int mod_cols,
+                                             int shift_col, bool with_src) {
+  constexpr int NCH = LnEarly<D, TPR>::NCH;
+  const size_t mbase = m.valid ? (size_t)m.tok * mod_cols : 0;
+  const __nv_bfloat16* mrow = mod + mbase + shift_col;
+  E.src_loaded = with_src;
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) {
+    const int c = 4 * (part + TPR * k);
+    E.src[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    E.shift[k] = E.scale[k] = E.gate[k] = make_uint2(0u, 0u);
+    if (m.valid) {
+      E.shift[k] = __ldcg(reinterpret_cast<const uint2*>(mrow + c));
+      E.scale[k] = __ldcg(reinterpret_cast<const uint2*>(mrow + D + c));
+      if (u.bias) E.gate[k] = __ldcg(reinterpret_cast<const uint2*>(mod + mbase + u.gate_off + c));
+      if (with_src) E.src[k] = __ldcg(reinterpret_cast<const float4*>(u.src + (size_t)r * D + c));
+    }
+  }
+}
+
+// Early loads of this thread's first-pass row, issued before griddepcontrol.wait.
+template <int D>
+__device__ __forceinline__ void prefetch_ln_operand(LnEarly<D, D / 12>& pf, const ResidUpdate& u, const CallGeom& g,
+                                                    int tile, const __nv_bfloat16* __restrict__ mod, int mod_cols,
+                                                    int shift_col, int tid, int r_begin, int r_end, bool with_src) {
+  constexpr int TPR = D / 12;
+  const int r = r_begin + tid / TPR;
+  const RowMap m = map_row(g, tile, r);  // rows at or past rows8 map to no candidate
+  ln_row_early<D, TPR>(pf, u, m, r, tid % TPR, mod, mod_cols, shift_col, with_src && r < r_end);
+}
+
 template <int D, int TPR, int SK = 0>
 __device__ __forceinline__ void build_ln_operand_t(const ResidUpdate& u, const CallGeom& g, int tile,
                                                    const __nv_bfloat16* __restrict__ mod, int mod_cols, int shift_col,
                                                    const float* __restrict__ lg, const float* __restrict__ lb,
-                                                   uint8_t* sA, int tid, int r_begin, int r_end) {
+                                                   uint8_t* sA, int tid, int r_begin, int r_end,
+                                                   const LnEarly<D, TPR>* pre = nullptr) {
   constexpr int NPER = D / TPR;   // columns per thread, a multiple of 4
   constexpr int NCH = NPER / 4;   // 4-column chunks per thread
   static_assert(NPER % 4 == 0, "4-column chunks");
   const int part = tid % TPR;
-  for (int r = r_begin + tid / TPR; r < r_end; r += kThreads / TPR) {
+  const int r_first = r_begin + tid / TPR;
+  for (int r = r_first; r < r_end; r += kThreads / TPR) {
     const RowMap m = map_row(g, tile, r);
+    LnEarly<D, TPR> E;
+    if (pre && r == r_first)
+      E = *pre;
+    else
+      ln_row_early<D, TPR>(E, u, m, r, part, mod, mod_cols, shift_col, false);
+    // The loads that depend on the kernel just before this one (the residual rows
+    // unless prefetched, the partial sums) and the bias, through the read-only path (none of these buffers is written by this kernel: the updated rows
+    // go to u.dst, never u.src), all issued before the update and its write-back.
     float xv[NPER];
-    uint2 shv[NCH], scv[NCH];
-    const size_t mbase = m.valid ? (size_t)m.tok * mod_cols : 0;
-    const __nv_bfloat16* mrow = mod + (m.valid ? mbase + shift_col : 0);
-    // All loads of the row first, through the read-only path (none of these buffers is
-    // written by this kernel: the updated rows go to u.dst, never u.src), then the
-    // update and its write-back, so no load waits behind a store.
-    float4 pa[NCH], pb[NCH], bb[NCH], lgv[NCH], lbv[NCH];
-    uint2 gw[NCH];
+    float4 pa[NCH], pb[NCH], bb[NCH];
     const bool four = u.nparts == 4;
     LEWM_STAMP(SK, 1);
 #pragma unroll
     for (int k = 0; k < NCH; ++k) {
       const int c = 4 * (part + TPR * k);
-      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-      uint2 h = make_uint2(0u, 0u), a = make_uint2(0u, 0u);
-      pa[k] = pb[k] = bb[k] = t;
-      gw[k] = h;
+      float4 t = E.src[k];
+      pa[k] = pb[k] = bb[k] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (m.valid) {
-        const size_t o = (size_t)r * D + c;
-        t = __ldg(reinterpret_cast<const float4*>(u.src + o));
-        h = __ldg(reinterpret_cast<const uint2*>(mrow + c));
-        a = __ldg(reinterpret_cast<const uint2*>(mrow + D + c));
+        if (!E.src_loaded) t = __ldg(reinterpret_cast<const float4*>(u.src + (size_t)r * D + c));
         if (u.bias) {
           const int o = part_off<D>(r, c);
           pa[k] = __ldg(reinterpret_cast<const float4*>(u.part + o));
@@ -530,22 +576,17 @@ __device__ __forceinline__ void build_ln_operand_t(const ResidUpdate& u, const C
             pb[k] = make_float4(pc.x + pd.x, pc.y + pd.y, pc.z + pd.z, pc.w + pd.w);
           }
           bb[k] = __ldg(reinterpret_cast<const float4*>(u.bias + c));
-          gw[k] = __ldg(reinterpret_cast<const uint2*>(mod + mbase + u.gate_off + c));
         }
       }
-      lgv[k] = __ldg(reinterpret_cast<const float4*>(lg + c));
-      lbv[k] = __ldg(reinterpret_cast<const float4*>(lb + c));
       xv[4 * k] = t.x;
       xv[4 * k + 1] = t.y;
       xv[4 * k + 2] = t.z;
       xv[4 * k + 3] = t.w;
-      shv[k] = h;
-      scv[k] = a;
     }
     if (u.bias && m.valid) {
 #pragma unroll
       for (int k = 0; k < NCH; ++k) {
-        const float2 g01 = unpack_bf16x2(gw[k].x), g23 = unpack_bf16x2(gw[k].y);
+        const float2 g01 = unpack_bf16x2(E.gate[k].x), g23 = unpack_bf16x2(E.gate[k].y);
         float* t = xv + 4 * k;
         t[0] += g01.x * ((pa[k].x + pb[k].x) + bb[k].x);
         t[1] += g01.y * ((pa[k].y + pb[k].y) + bb[k].y);
@@ -578,8 +619,8 @@ __device__ __forceinline__ void build_ln_operand_t(const ResidUpdate& u, const C
     float s2 = 0.f;
 #pragma unroll
     for (int k = 0; k < NCH; ++k) {
-      const float2 h01 = unpack_bf16x2(shv[k].x), h23 = unpack_bf16x2(shv[k].y);
-      const float2 a01 = unpack_bf16x2(scv[k].x), a23 = unpack_bf16x2(scv[k].y);
+      const float2 h01 = unpack_bf16x2(E.shift[k].x), h23 = unpack_bf16x2(E.shift[k].y);
+      const float2 a01 = unpack_bf16x2(E.scale[k].x), a23 = unpack_bf16x2(E.scale[k].y);
       float* y = xv + 4 * k;
       y[0] = (y[0] - mean) * rstd * (1.0f + a01.x) + h01.x;
       y[1] = (y[1] - mean) * rstd * (1.0f + a01.y) + h01.y;
@@ -600,7 +641,8 @@ __device__ __forceinline__ void build_ln_operand_t(const ResidUpdate& u, const C
 #pragma unroll
     for (int k = 0; k < NCH; ++k) {
       const int c = 4 * (part + TPR * k);
-      const float4 g4 = lgv[k], b4 = lbv[k];
+      const float4 g4 = __ldg(reinterpret_cast<const float4*>(lg + c));
+      const float4 b4 = __ldg(reinterpret_cast<const float4*>(lb + c));
       const float* y = xv + 4 * k;
       uint2 pk = make_uint2(0u, 0u);
       if (m.valid) {
@@ -621,8 +663,8 @@ template <int D, int SK = 0>
 __device__ __forceinline__ void build_ln_operand(const ResidUpdate& u, const CallGeom& g, int tile,
                                                  const __nv_bfloat16* __restrict__ mod, int mod_cols, int shift_col,
                                                  const float* __restrict__ lg, const float* __restrict__ lb,
-                                                 uint8_t* sA, int tid) {
-  build_ln_operand_t<D, D / 12, SK>(u, g, tile, mod, mod_cols, shift_col, lg, lb, sA, tid, 0, g.rows8);
+                                                 uint8_t* sA, int tid, const LnEarly<D, D / 12>* pre = nullptr) {
+  build_ln_operand_t<D, D / 12, SK>(u, g, tile, mod, mod_cols, shift_col, lg, lb, sA, tid, 0, g.rows8, pre);
 }
 
 // Layer-0 residual row x0 = history row + position embedding of window position p.
@@ -646,12 +688,12 @@ __device__ __forceinline__ void prep_layer0_row(const DevWeights& w, const float
 // each of the GEMM's 16-24 CTAs per tile would repeat several passes per CTA. Same
 // device code as the in-kernel build, so the results are identical either way; every
 // CTA writes back the updated residual rows it owns.
+// src_early: the residual rows come from a kernel at least two launches back and are
+// loaded with the modulation before griddepcontrol.wait.
 template <int D>
 __global__ void __launch_bounds__(kThreads) k_ln_operand(ResidUpdate u, CallGeom g, const __nv_bfloat16* mod,
                                                          int mod_cols, int shift_col, const float* lg, const float* lb,
-                                                         __nv_bfloat16* a_op) {
-  griddep_wait();
-  griddep_launch();
+                                                         __nv_bfloat16* a_op, int src_early) {
   const int tile = blockIdx.x;
   const int r0 = blockIdx.y * (kThreads / (D / 12));
   const int r1 = min(r0 + kThreads / (D / 12), g.rows8);
@@ -660,9 +702,13 @@ __global__ void __launch_bounds__(kThreads) k_ln_operand(ResidUpdate u, CallGeom
   ut.src += t0;
   if (ut.part) ut.part += t0;
   if (ut.dst) ut.dst += t0;
+  LnEarly<D, D / 12> pf;
+  prefetch_ln_operand<D>(pf, ut, g, tile, mod, mod_cols, shift_col, threadIdx.x, r0, r1, src_early != 0);
+  griddep_wait();
+  griddep_launch();
   build_ln_operand_t<D, D / 12>(ut, g, tile, mod, mod_cols, shift_col, lg, lb,
                                 reinterpret_cast<uint8_t*>(a_op + (size_t)tile * (D / 64) * kBlkElems), threadIdx.x,
-                                r0, r1);
+                                r0, r1, &pf);
 }
 
 // ---------------------------------------------------------------- first-call layer-0 inputs
@@ -732,26 +778,31 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
+  // A operand: LN1 -> modulate (shift/scale_msa of this layer) -> attn.norm of the residual
+  // rows. After layer 0 the previous layer's FC2 update is still pending: r = s + gate_mlp *
+  // (sum of the FC2 partials + b2); the head-0 CTAs write r back for this layer's FC1. The
+  // modulation rows are loaded before the wait (the residual rows come from the kernel
+  // just before this one).
+  const size_t t0 = (size_t)tile * 128 * D;
+  ResidUpdate u{b.x + t0, nullptr, 0, 2, nullptr, 0, nullptr};
+  if (layer > 0)
+    u = ResidUpdate{b.xs + t0, b.part_b + t0, b.part_stride, g.fc2_parts, w.b2 + (layer - 1) * D,
+                    (layer - 1) * 6 * D + 5 * D, head == 0 ? b.x + t0 : nullptr};
+  LnEarly<D, D / 12> pf;
+  if (!g.ln_prebuilt)
+    prefetch_ln_operand<D>(pf, u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D, tid, 0, g.rows8, false);
   LEWM_STAMP(2, 1);
   griddep_wait();
   LEWM_STAMP(2, 2);
   griddep_launch();
-  // A operand: LN1 -> modulate (shift/scale_msa of this layer) -> attn.norm of the residual
-  // rows. After layer 0 the previous layer's FC2 update is still pending: r = s + gate_mlp *
-  // (P0 + P1 + b2); the head-0 CTAs write r back for this layer's FC1.
   if (g.ln_prebuilt) {  // built once per tile by k_ln_operand: one copy per lane
     if (warp == 0 && lane < KB) {
       mbar_arrive_expect_tx(&bar_a[lane], g.rows8 * 128);
       bulk_g2s(sA + lane * kBlk, b.a_op + ((size_t)tile * KB + lane) * kBlkElems, g.rows8 * 128, &bar_a[lane]);
     }
   } else {
-    const size_t t0 = (size_t)tile * 128 * D;
-    ResidUpdate u{b.x + t0, nullptr, 0, 2, nullptr, 0, nullptr};
-    if (layer > 0)
-      u = ResidUpdate{b.xs + t0, b.part_b + t0, b.part_stride, g.fc2_parts, w.b2 + (layer - 1) * D,
-                      (layer - 1) * 6 * D + 5 * D, head == 0 ? b.x + t0 : nullptr};
     build_ln_operand<D, 6>(u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D, w.attn_ln_w + layer * D,
-                        w.attn_ln_b + layer * D, sA, tid);
+                           w.attn_ln_b + layer * D, sA, tid, &pf);
   }
   fence_async_smem();
   LEWM_STAMP(2, 5);
@@ -1064,23 +1115,28 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
     tmem_alloc(tmem_slot, NT);
     tmem_relinquish();
   }
+  // A operand: LN2 -> modulate (shift/scale_mlp of this layer) -> ffn.norm of s = r +
+  // gate_msa * (P0 + P1 + out_b), the out-projection update; the N-tile-0 CTAs write s back.
+  // The residual rows r (written by k_qkv_attn, two launches back) and the modulation are
+  // loaded before the wait.
+  const size_t t0 = (size_t)tile * 128 * D;
+  const ResidUpdate u{b.x + t0, b.part_a + t0, b.part_stride, 2, w.out_b + layer * D, layer * 6 * D + 2 * D,
+                      nt == 0 ? b.xs + t0 : nullptr};
+  LnEarly<D, D / 12> pf;
+  if (!g.ln_prebuilt)
+    prefetch_ln_operand<D>(pf, u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D + 3 * D, tid, 0, g.rows8, true);
   LEWM_STAMP(4, 1);
   griddep_wait();
   LEWM_STAMP(4, 2);
   griddep_launch();
-  // A operand: LN2 -> modulate (shift/scale_mlp of this layer) -> ffn.norm of s = r +
-  // gate_msa * (P0 + P1 + out_b), the out-projection update; the N-tile-0 CTAs write s back.
   if (g.ln_prebuilt) {  // built once per tile by k_ln_operand: one copy per lane
     if (warp == 0 && lane < KB) {
       mbar_arrive_expect_tx(&bar_a[lane], g.rows8 * 128);
       bulk_g2s(sA + lane * kBlk, b.a_op + ((size_t)tile * KB + lane) * kBlkElems, g.rows8 * 128, &bar_a[lane]);
     }
   } else {
-    const size_t t0 = (size_t)tile * 128 * D;
-    const ResidUpdate u{b.x + t0, b.part_a + t0, b.part_stride, 2, w.out_b + layer * D, layer * 6 * D + 2 * D,
-                        nt == 0 ? b.xs + t0 : nullptr};
     build_ln_operand<D>(u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D + 3 * D, w.ffn_ln_w + layer * D,
-                        w.ffn_ln_b + layer * D, sA, tid);
+                        w.ffn_ln_b + layer * D, sA, tid, &pf);
   }
   fence_async_smem();
   LEWM_STAMP(4, 5);
@@ -1225,17 +1281,19 @@ __global__ void __launch_bounds__(kThreads) k_ffn(DevWeights w, ModelDims md, Ca
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
+  // FC1 operand from the residual rows with the out-projection update pending; the rows
+  // (written by k_qkv_attn, two launches back) and the modulation are loaded before the wait.
+  const size_t t0 = (size_t)tile * 128 * D;
+  const ResidUpdate u{b.x + t0, b.part_a + t0, b.part_stride, 2, w.out_b + layer * D, layer * 6 * D + 2 * D,
+                      q == 0 ? b.xs + t0 : nullptr};
+  LnEarly<D, D / 12> pf;
+  prefetch_ln_operand<D>(pf, u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D + 3 * D, tid, 0, g.rows8, true);
   LEWM_STAMP(4, 1);
   griddep_wait();
   LEWM_STAMP(4, 2);
   griddep_launch();
-  {  // FC1 operand from the residual rows with the out-projection update pending
-    const size_t t0 = (size_t)tile * 128 * D;
-    const ResidUpdate u{b.x + t0, b.part_a + t0, b.part_stride, 2, w.out_b + layer * D, layer * 6 * D + 2 * D,
-                        q == 0 ? b.xs + t0 : nullptr};
-    build_ln_operand<D, 7>(u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D + 3 * D, w.ffn_ln_w + layer * D,
-                        w.ffn_ln_b + layer * D, sA, tid);
-  }
+  build_ln_operand<D, 7>(u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D + 3 * D, w.ffn_ln_w + layer * D,
+                         w.ffn_ln_b + layer * D, sA, tid, &pf);
   fence_async_smem();
   LEWM_STAMP(4, 5);
   tc_fence_before();
@@ -1537,7 +1595,7 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
                         (l - 1) * 6 * D + 5 * D, b.x};
       if (prof) prof->begin(st);
       LEWM_TRY(launch_k(k_ln_operand<D>, op_grid, dim3(kThreads), 0, st, u, g, (const __nv_bfloat16*)b.mod, mcols,
-                        l * 6 * D, w.attn_ln_w + l * D, w.attn_ln_b + l * D, b.a_op));
+                        l * 6 * D, w.attn_ln_w + l * D, w.attn_ln_b + l * D, b.a_op, l > 0 ? 1 : 0));
       if (prof) prof->end(KC_LN_OP, 0.0, st);
     }
     if (prof) prof->begin(st);
@@ -1557,7 +1615,7 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
       const ResidUpdate u{b.x, b.part_a, b.part_stride, 2, w.out_b + l * D, l * 6 * D + 2 * D, b.xs};
       if (prof) prof->begin(st);
       LEWM_TRY(launch_k(k_ln_operand<D>, op_grid, dim3(kThreads), 0, st, u, g, (const __nv_bfloat16*)b.mod, mcols,
-                        l * 6 * D + 3 * D, w.ffn_ln_w + l * D, w.ffn_ln_b + l * D, b.a_op));
+                        l * 6 * D + 3 * D, w.ffn_ln_w + l * D, w.ffn_ln_b + l * D, b.a_op, 1));
       if (prof) prof->end(KC_LN_OP, 0.0, st);
     }
     if (g.ffn_fused) {  // FC1 + GELU + FC2 quarter partials in one kernel
