@@ -1334,16 +1334,26 @@ __global__ void __launch_bounds__(kThreads) k_ffn(DevWeights w, ModelDims md, Ca
   }
   __syncthreads();
   LEWM_STAMP(4, 0);
-  // bias + GELU over all threads, 4 columns per item, into h (the FC2 operand, in sA)
-  for (int it = tid; it < g.rows8 * (kFfnQ / 4); it += kThreads) {
-    const int rr = it / (kFfnQ / 4), c = (it - rr * (kFfnQ / 4)) * 4;
+  // bias + GELU over all threads into h (the FC2 operand, in sA): 12 columns of one row
+  // per item, loaded first so the 12 GELUs overlap (one item per thread at 32 rows).
+  constexpr int kCpi = 12;
+  static_assert(kFfnQ == 16 * kCpi, "16 items per row");
+  for (int it = tid; it < g.rows8 * 16; it += kThreads) {
+    const int rr = it >> 4, c = (it & 15) * kCpi;
     const float* sr = stage + rr * kStage + c;
-    uint2 pk = make_uint2(0u, 0u);
-    if (ok1 && map_row(g, tile, rr).valid) {  // window slots without a candidate stay zero
-      pk.x = pack_bf16x2(gelu_f(sr[0] + sb1[c]), gelu_f(sr[1] + sb1[c + 1]));
-      pk.y = pack_bf16x2(gelu_f(sr[2] + sb1[c + 2]), gelu_f(sr[3] + sb1[c + 3]));
+    float hv[kCpi];
+#pragma unroll
+    for (int i = 0; i < kCpi; ++i) hv[i] = sr[i] + sb1[c + i];
+    const bool valid = ok1 && map_row(g, tile, rr).valid;  // window slots without a candidate stay zero
+#pragma unroll
+    for (int i = 0; i < kCpi; i += 4) {
+      uint2 pk = make_uint2(0u, 0u);
+      if (valid) {
+        pk.x = pack_bf16x2(gelu_f(hv[i]), gelu_f(hv[i + 1]));
+        pk.y = pack_bf16x2(gelu_f(hv[i + 2]), gelu_f(hv[i + 3]));
+      }
+      *reinterpret_cast<uint2*>(sA + ((c + i) >> 6) * kBlk + sw128_off(rr, (c + i) & 63)) = pk;
     }
-    *reinterpret_cast<uint2*>(sA + (c >> 6) * kBlk + sw128_off(rr, c & 63)) = pk;
   }
   fence_async_smem();
   LEWM_STAMP(4, 9);
