@@ -1235,7 +1235,7 @@ __global__ void __launch_bounds__(kThreads) k_ffn(DevWeights w, ModelDims md, Ca
   constexpr int W1_BLK = kFfnQ * 128; // [192 hidden x 64] bf16
   constexpr int W2_BLK = D * 128;     // [D x 64] bf16
   constexpr int NT2 = Cfg<D>::NT_OUT; // rows of one packed FC2 weight piece (N tile)
-  constexpr int kStage = kFfnQ + 1;   // floats per staged accumulator row
+  constexpr int kStage = kFfnQ + 4;   // floats per staged row: 16-byte rows, float4 accesses conflict-free
   static_assert(HB == KB, "h reuses the operand blocks");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -1327,9 +1327,9 @@ __global__ void __launch_bounds__(kThreads) k_ffn(DevWeights w, ModelDims md, Ca
     float v[48];
     tmem_ld_cols<48>(tmem + ((uint32_t)(quad * 32) << 16) + slice * 48, v);
     if (r < g.rows8) {
-      float* sr = stage + r * kStage + slice * 48;
+      float4* sr = reinterpret_cast<float4*>(stage + r * kStage + slice * 48);
 #pragma unroll
-      for (int i = 0; i < 48; ++i) sr[i] = v[i];
+      for (int i = 0; i < 12; ++i) sr[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     }
   }
   __syncthreads();
@@ -1340,10 +1340,17 @@ __global__ void __launch_bounds__(kThreads) k_ffn(DevWeights w, ModelDims md, Ca
   static_assert(kFfnQ == 16 * kCpi, "16 items per row");
   for (int it = tid; it < g.rows8 * 16; it += kThreads) {
     const int rr = it >> 4, c = (it & 15) * kCpi;
-    const float* sr = stage + rr * kStage + c;
+    const float4* sr = reinterpret_cast<const float4*>(stage + rr * kStage + c);
+    const float4* sb = reinterpret_cast<const float4*>(sb1 + c);
     float hv[kCpi];
 #pragma unroll
-    for (int i = 0; i < kCpi; ++i) hv[i] = sr[i] + sb1[c + i];
+    for (int i = 0; i < kCpi / 4; ++i) {
+      const float4 a = sr[i], bq = sb[i];
+      hv[4 * i] = a.x + bq.x;
+      hv[4 * i + 1] = a.y + bq.y;
+      hv[4 * i + 2] = a.z + bq.z;
+      hv[4 * i + 3] = a.w + bq.w;
+    }
     const bool valid = ok1 && map_row(g, tile, rr).valid;  // window slots without a candidate stay zero
 #pragma unroll
     for (int i = 0; i < kCpi; i += 4) {
