@@ -54,7 +54,8 @@ namespace {
 constexpr int kBlk = 16384;           // bytes of one [128 x 64] bf16 block
 constexpr int kBlkElems = 128 * 64;   // elements of one [128 x 64] block
 constexpr int kMaxWindow = 8;
-constexpr int kKVStride = 129;        // floats per row of the k|v scratch (128 + 1)
+constexpr int kKVStride = 132;        // floats per row of the k|v scratch: 16-byte rows, and
+                                       // float4 accesses of 8 consecutive rows hit distinct banks
 constexpr int kThreads = 512;         // 16 warps: 4 per TMEM lane quadrant
 constexpr int kFc1N = 32;             // hidden columns per FC1 CTA (N of its MMA)
 
@@ -849,7 +850,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   // owns window row r = 32 (w & 3) + l, its TMEM lane, and head-dim part p = w >> 2:
   // dims [8p, 8p + 8) and [32 + 8p, 40 + 8p) of q, k and v, read straight from TMEM.
   // Only k and v of the other rows of a window go through shared memory (row stride
-  // kKVStride = 129 floats: a warp's rows hit distinct banks), and the four parts of
+  // kKVStride = 132 floats, float4 accesses conflict-free), and the four parts of
   // a row combine their partial scores through `spart`.
   {
     const int quad = warp & 3, part = warp >> 2;
@@ -865,11 +866,13 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     tmem_ld8(trow + 96, kk + 8);
     tmem_ld8(trow + 128, vv);
     tmem_ld8(trow + 160, vv + 8);
-    float* kvr = kv + r * kKVStride + part * 8;
+    float4* kvr = reinterpret_cast<float4*>(kv + r * kKVStride + part * 8);
+    // dims [8p, 8p + 8) at float4 0-1, [32 + 8p, 40 + 8p) at 8-9; v 16 float4 further
 #pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      kvr[t < 8 ? t : t + 24] = kk[t];
-      kvr[64 + (t < 8 ? t : t + 24)] = vv[t];
+    for (int t = 0; t < 4; ++t) {
+      const int o = (t & 1) + (t >> 1) * 8;
+      kvr[o] = make_float4(kk[4 * t], kk[4 * t + 1], kk[4 * t + 2], kk[4 * t + 3]);
+      kvr[16 + o] = make_float4(vv[4 * t], vv[4 * t + 1], vv[4 * t + 2], vv[4 * t + 3]);
     }
     __syncthreads();
     LEWM_STAMP(2, 7);
@@ -878,10 +881,16 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     const int npos = valid ? m.pos : -1;
 #pragma unroll 1
     for (int j = 0; j < npos; ++j) {
-      const float* kr = kv + (base + j) * kKVStride + part * 8;
+      const float4* kr = reinterpret_cast<const float4*>(kv + (base + j) * kKVStride + part * 8);
       float d = 0.f;
 #pragma unroll
-      for (int t = 0; t < 16; ++t) d += q[t] * kr[t < 8 ? t : t + 24];
+      for (int t = 0; t < 4; ++t) {
+        const float4 k4 = kr[(t & 1) + (t >> 1) * 8];
+        d += q[4 * t] * k4.x;
+        d += q[4 * t + 1] * k4.y;
+        d += q[4 * t + 2] * k4.z;
+        d += q[4 * t + 3] * k4.w;
+      }
       spart[(part * kMaxWindow + j) * 128 + r] = d;
     }
     if (valid) {
@@ -908,9 +917,15 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
       const float pj = expf(sj - mnew);
       den = den * scale + pj;
       mx = mnew;
-      const float* vr = kv + (base + j) * kKVStride + 64 + part * 8;
+      const float4* vr = reinterpret_cast<const float4*>(kv + (base + j) * kKVStride + 64 + part * 8);
 #pragma unroll
-      for (int t = 0; t < 16; ++t) o[t] = o[t] * scale + pj * vr[t < 8 ? t : t + 24];
+      for (int t = 0; t < 4; ++t) {
+        const float4 v4 = vr[(t & 1) + (t >> 1) * 8];
+        o[4 * t] = o[4 * t] * scale + pj * v4.x;
+        o[4 * t + 1] = o[4 * t + 1] * scale + pj * v4.y;
+        o[4 * t + 2] = o[4 * t + 2] * scale + pj * v4.z;
+        o[4 * t + 3] = o[4 * t + 3] * scale + pj * v4.w;
+      }
     }
     float inv = 0.f;
     if (valid) {
