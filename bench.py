@@ -157,6 +157,102 @@ def run_cpu_plan(n_plans: int):
     return times
 
 
+def reference_gpu_arm(args):
+    """--impl reference-gpu: the reference's own PyTorch path for the same plan on this GPU.
+
+    ICEMSolver.solve (lewm/solvers/icem.py) from the installed reference package in
+    baseline/_ref, with the same solver settings, bf16 model-cost autocast and
+    float32 matmul precision "high", timed end to end per plan (CUDA events around
+    solve, batch of one env) eager and with get_cost_from_embeddings under
+    torch.compile(mode="reduce-overhead"), prewarmed on the bucket sizes
+    300/240/180/120/60 as the reference's benchmark does
+    (tools/benchmarks/lewm_plan_benchmark.py:596-700). A comparator for the
+    single-env latency target; the driver's reference arm is the CPU path
+    (--impl reference). Same synthetic weights and latents as the main arm."""
+    ref = REPO / "baseline" / "_ref"
+    if not (ref / "lewm" / "jepa.py").is_file():
+        print(json.dumps({"impl": "reference_gpu", "unavailable": "reference not installed in baseline/_ref"}))
+        return 0
+    sys.path.insert(0, str(ref))
+    from types import SimpleNamespace
+
+    import torch
+    from lewm.jepa import JEPA
+    from lewm.module import ARPredictor, Embedder
+    from lewm.solvers.icem import ICEMSolver
+
+    from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    desc = ModelDesc()
+    pred = ARPredictor(num_frames=desc.num_frames, depth=desc.depth, heads=desc.heads, mlp_dim=desc.mlp_dim,
+                       input_dim=desc.dim, hidden_dim=desc.dim, dim_head=desc.dim_head)
+    enc = Embedder(input_dim=desc.action_dim, smoothed_dim=desc.smoothed_dim, emb_dim=desc.dim,
+                   mlp_scale=desc.embed_hidden // desc.dim)
+    model = JEPA(encoder=torch.nn.Identity(), predictor=pred, action_encoder=enc, pred_proj=None)
+    model.load_state_dict({k: torch.from_numpy(v) for k, v in synthetic_state_dict(desc, 0).items()}, strict=True)
+    model = model.to(dev).eval()
+    torch.set_float32_matmul_precision("high")
+    model.set_model_cost_autocast("bf16")
+    # cached latents: get_cost goes straight to get_cost_from_embeddings
+    model.set_embedding_cache(True).set_compile_cost(True)
+
+    class Box:
+        def __init__(self, shape):
+            self.shape = shape
+            self.low = -np.inf * np.ones(shape, dtype=np.float32)
+            self.high = np.inf * np.ones(shape, dtype=np.float32)
+
+    solver = ICEMSolver(model=model, batch_size=1, num_samples=300, n_steps=30, topk=30, device=dev, seed=0,
+                        elite_retention=3, colored_noise="brown", colored_noise_time="raw", sample_decay=1.25,
+                        sample_count_bucket_size=60)
+    solver.configure(action_space=Box((1, desc.action_dim // 5)), n_envs=1,
+                     config=SimpleNamespace(horizon=5, action_block=5))
+    rng = np.random.default_rng(100)
+    emb = torch.as_tensor(rng.standard_normal((1, 1, desc.dim)), dtype=torch.float32, device=dev)
+    goal = torch.as_tensor(rng.standard_normal((1, 1, desc.dim)), dtype=torch.float32, device=dev)
+
+    def plans(n):
+        ms = []
+        for _ in range(n):
+            info = {"emb": emb, "goal_emb": goal, "pixels": torch.zeros(1, 1, device=dev),
+                    "goal": torch.zeros(1, 1, device=dev)}
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            with torch.inference_mode():
+                solver.solve(info)
+            b.record()
+            torch.cuda.synchronize(dev)
+            ms.append(a.elapsed_time(b))
+        return ms
+
+    steps = max(1, min(args.steps, 5))
+    plans(max(args.warmup, 2))
+    eager = plans(steps)
+    out = {"impl": "reference_gpu", "metric": "p50 plan latency (ms), 300-sample iCEM H=5, 1 env",
+           "unit": "ms", "higher_is_better": False, "steps": steps, "warmup": max(args.warmup, 2),
+           "eager_ms": eager, "eager_p50_ms": percentile(eager, 50),
+           "settings": "ICEMSolver.solve, bf16 model-cost autocast, matmul precision high, cached latents"}
+    try:
+        model.get_cost_from_embeddings = torch.compile(model.get_cost_from_embeddings, mode="reduce-overhead",
+                                                       fullgraph=False)
+        for n in (300, 240, 180, 120, 60):
+            with torch.inference_mode():
+                model.get_cost_from_embeddings(torch.zeros(1, 1, desc.dim, device=dev),
+                                               torch.zeros(1, 1, desc.dim, device=dev),
+                                               torch.zeros(1, n, 5, desc.action_dim, device=dev))
+        torch.cuda.synchronize(dev)
+        plans(max(args.warmup, 2))
+        comp = plans(steps)
+        out.update({"compiled_ms": comp, "compiled_p50_ms": percentile(comp, 50)})
+    except Exception as exc:  # torch.compile unavailable or failing on the box: say so
+        out["compiled"] = f"failed: {type(exc).__name__}: {str(exc)[:200]}"
+    print(json.dumps(out))
+    return 0
+
+
 def reference_arm(args, rank, world):
     """--impl reference: the reference algorithm's CPU implementation (numpy oracle port) on host cores."""
     if rank != 0:
@@ -214,7 +310,7 @@ def main() -> int:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-gpu"])
     ap.add_argument("--cpu-baseline-plans", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--model-cost", type=int, default=0, metavar="S",
@@ -230,6 +326,8 @@ def main() -> int:
     local = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         return reference_arm(args, rank, world)
+    if args.impl == "reference-gpu":
+        return reference_gpu_arm(args)
     if args.warmup < 3:
         print("warmup must be >= 3", file=sys.stderr)
         return 2
