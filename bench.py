@@ -163,7 +163,7 @@ def reference_gpu_arm(args):
     ICEMSolver.solve (lewm/solvers/icem.py) from the installed reference package in
     baseline/_ref, with the same solver settings, bf16 model-cost autocast and
     float32 matmul precision "high", timed end to end per plan (CUDA events around
-    solve, batch of one env) eager and with get_cost_from_embeddings under
+    solve, batch of one env, p50 over at least 50 plans) eager and with get_cost_from_embeddings under
     torch.compile(mode="reduce-overhead"), prewarmed on the bucket sizes
     300/240/180/120/60 as the reference's benchmark does
     (tools/benchmarks/lewm_plan_benchmark.py:596-700). A comparator for the
@@ -228,7 +228,7 @@ def reference_gpu_arm(args):
             ms.append(a.elapsed_time(b))
         return ms
 
-    steps = max(1, min(args.steps, 5))
+    steps = max(args.steps, 50)  # p50 over at least 50 plans
     plans(max(args.warmup, 2))
     eager = plans(steps)
     out = {"impl": "reference_gpu", "metric": "p50 plan latency (ms), 300-sample iCEM H=5, 1 env",
