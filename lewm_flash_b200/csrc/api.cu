@@ -91,6 +91,7 @@ struct lewm_ctx {
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;
   std::map<std::vector<double>, cudaGraphExec_t> graphs;  // one executable graph per plan shape
   int tile_target = 1;        // row tiles a small predictor call is spread over
+  int sm_count = 148;         // streaming multiprocessors of the device
   std::vector<float> W_host;  // last uploaded coloring matrix
   int W_n = -1;
   float W_beta = -1.f;
@@ -444,16 +445,21 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
       return v ? std::atoi(v) : -1;
     }();
     const int ln_prebuilt = rows8 > (pre_rows >= 0 ? pre_rows : 512 / (m.D / 12)) ? 1 : 0;
-    // FC1 + GELU + FC2 fused into one kernel when the operand is built in-kernel (small
-    // tiles) at width 192 / MLP 768: one CTA per (tile, 192 hidden units), whose FC1
-    // accumulator is staged through the 72 KB of FC1 weight slots (at most 64 rows).
-    // LEWM_FFN_FUSED=0 keeps the two-kernel path.
+    // FC1 + GELU + FC2 fused into one kernel at width 192 / MLP 768: one CTA per (tile,
+    // 192 hidden units). Used where it is fastest: tiles of at most 32 rows (operand built
+    // in the kernel), and calls with enough tiles to fill the SMs (4 CTAs per tile;
+    // throughput-bound, measured 387 -> 499 plans/s at 64 envs). A few large tiles keep
+    // the two-kernel path (FC1 over 24 CTAs per tile, then the FC2 partial GEMM): more
+    // CTAs in flight for a latency-bound call. LEWM_FFN_FUSED=0 keeps the two-kernel
+    // path everywhere.
     static const int ffn_env = [] {
       const char* v = std::getenv("LEWM_FFN_FUSED");
       return v ? std::atoi(v) : 1;
     }();
     const int fc2_parts = (m.D == 192 && m.mlp == 4 * 192) ? 4 : 2;
-    const int ffn_fused = (ffn_env != 0 && !ln_prebuilt && rows8 <= 64 && fc2_parts == 4) ? 1 : 0;
+    const bool ffn_small = !ln_prebuilt && rows8 <= 64;
+    const bool ffn_many = nt * 4 >= c->sm_count;
+    const int ffn_fused = (ffn_env != 0 && fc2_parts == 4 && (ffn_small || ffn_many)) ? 1 : 0;
     return CallGeom{NC,        S, T, H, w, start, cpt, nt, rows8, ln_prebuilt, ffn_fused,
                     fc2_parts, k, k == n_calls - 1, 1, 0, 128};
   };
@@ -733,6 +739,7 @@ lewm_status lewm_create(lewm_ctx** out, const lewm_model_desc* desc, const float
   // left free let the next kernel's CTAs launch early and prefetch their weights
   // (measured on B200: 6 tiles 24.2 ms/plan, 9 tiles 25.6 ms, 3 tiles 24.9 ms).
   c->tile_target = std::max(1, prop.multiProcessorCount / md.heads * 2 / 3);
+  c->sm_count = prop.multiProcessorCount;
   if (const char* tt = std::getenv("LEWM_TILE_TARGET")) {  // tuning override
     const int v = std::atoi(tt);
     if (v > 0) c->tile_target = v;

@@ -1239,7 +1239,7 @@ __global__ void __launch_bounds__(kThreads) k_fc1(DevWeights w, ModelDims md, Ca
 constexpr int kFfnQ = 192;  // hidden units per fused-FFN CTA
 template <int D>
 constexpr int smem_ffn() {
-  return 1024 + (D / 64) * kBlk + (D / 64) * kFfnQ * 128 + (kFfnQ / 64) * D * 128 + kFfnQ * 4 + 8 * 4 + 16;
+  return 1024 + (D / 64) * kBlk + (D / 64) * kFfnQ * 128 + (kFfnQ / 64) * D * 128 + kFfnQ * 4 + 8 * 5 + 16;
 }
 
 template <int D>
@@ -1258,14 +1258,15 @@ __global__ void __launch_bounds__(kThreads) k_ffn(DevWeights w, ModelDims md, Ca
   uint8_t* sW1 = smem + KB * kBlk;                     // FC1 weights, then the staged accumulator
   uint8_t* sW2 = sW1 + KB * W1_BLK;
   float* sb1 = reinterpret_cast<float*>(sW2 + HB * W2_BLK);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sb1 + kFfnQ);  // [0] W1+b1, [1] W2, [2] FC1 done, [3] FC2 done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+  // [0] W1+b1, [1] W2, [2] FC1 done, [3] FC2 done, [4] prebuilt operand
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sb1 + kFfnQ);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5);
   float* stage = reinterpret_cast<float*>(sW1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x, q = blockIdx.y;
   const int nmlp = md.mlp / 128, nkm = md.mlp / 64;
   if (tid == 0) {
-    for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < 5; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
     mbar_arrive_expect_tx(&bars[0], KB * W1_BLK + kFfnQ * 4);
     mbar_arrive_expect_tx(&bars[1], HB * W2_BLK);
@@ -1296,19 +1297,31 @@ __global__ void __launch_bounds__(kThreads) k_ffn(DevWeights w, ModelDims md, Ca
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
-  // FC1 operand from the residual rows with the out-projection update pending; the rows
-  // (written by k_qkv_attn, two launches back) and the modulation are loaded before the wait.
+  // FC1 operand: on tiles of more than 32 rows built once per tile by k_ln_operand and
+  // bulk-copied (one copy per lane); otherwise built here from the residual rows with the
+  // out-projection update pending (rows written by k_qkv_attn two launches back and the
+  // modulation are loaded before the wait; the q == 0 CTAs write the updated rows back).
   const size_t t0 = (size_t)tile * 128 * D;
   const ResidUpdate u{b.x + t0, b.part_a + t0, b.part_stride, 2, w.out_b + layer * D, layer * 6 * D + 2 * D,
                       q == 0 ? b.xs + t0 : nullptr};
   LnEarly<D, D / 12> pf;
-  prefetch_ln_operand<D>(pf, u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D + 3 * D, tid, 0, g.rows8, true);
+  if (!g.ln_prebuilt)
+    prefetch_ln_operand<D>(pf, u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D + 3 * D, tid, 0, g.rows8, true);
   LEWM_STAMP(4, 1);
   griddep_wait();
   LEWM_STAMP(4, 2);
   griddep_launch();
-  build_ln_operand<D, 7>(u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D + 3 * D, w.ffn_ln_w + layer * D,
-                         w.ffn_ln_b + layer * D, sA, tid, &pf);
+  if (g.ln_prebuilt) {
+    if (warp == 0) {
+      if (lane == 0) mbar_arrive_expect_tx(&bars[4], KB * g.rows8 * 128);
+      __syncwarp();
+      if (lane < KB)
+        bulk_g2s(sA + lane * kBlk, b.a_op + ((size_t)tile * KB + lane) * kBlkElems, g.rows8 * 128, &bars[4]);
+    }
+  } else {
+    build_ln_operand<D, 7>(u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D + 3 * D, w.ffn_ln_w + layer * D,
+                           w.ffn_ln_b + layer * D, sA, tid, &pf);
+  }
   fence_async_smem();
   LEWM_STAMP(4, 5);
   tc_fence_before();
@@ -1317,7 +1330,8 @@ __global__ void __launch_bounds__(kThreads) k_ffn(DevWeights w, ModelDims md, Ca
   const uint32_t tmem = *tmem_slot;
   const uint32_t idesc = idesc_bf16(128, 192);
   if (warp == 0) {  // FC1: D[0, 192) = A . W1^T
-    const bool got = __all_sync(0xffffffffu, mbar_wait(&bars[0], 0, status));
+    const bool got = __all_sync(0xffffffffu, mbar_wait(&bars[0], 0, status) &&
+                                                 (!g.ln_prebuilt || mbar_wait(&bars[4], 0, status)));
     tc_fence_after();
     if (lane == 0) {
       if (got) {
@@ -1338,43 +1352,70 @@ __global__ void __launch_bounds__(kThreads) k_ffn(DevWeights w, ModelDims md, Ca
   tc_fence_after();
   const int quad = warp & 3, slice = warp >> 2;
   const int r = quad * 32 + lane;
-  if (quad * 32 < g.rows8) {  // stage the accumulator rows of the tile (whole warps load)
-    float v[48];
-    tmem_ld_cols<48>(tmem + ((uint32_t)(quad * 32) << 16) + slice * 48, v);
-    if (r < g.rows8) {
-      float4* sr = reinterpret_cast<float4*>(stage + r * kStage + slice * 48);
+  if (g.rows8 > 64) {
+    // Every TMEM lane quadrant holds rows: each warp applies bias + GELU to its 32 rows x
+    // 48 hidden columns straight from TMEM, 16 at a time, into h (the FC2 operand, in sA).
+    if (quad * 32 < g.rows8) {
+      const bool valid = ok1 && r < g.rows8 && map_row(g, tile, r).valid;  // empty window slots stay zero
+      LEWM_STAMP(4, 0);
+#pragma unroll 1
+      for (int cc = 0; cc < 48; cc += 16) {
+        float v[16];
+        tmem_ld_cols<16>(tmem + ((uint32_t)(quad * 32) << 16) + slice * 48 + cc, v);
+        const int c0 = slice * 48 + cc;  // multiple of 16: two 8-column chunks of one 64-column block
+        uint32_t pk[8];
 #pragma unroll
-      for (int i = 0; i < 12; ++i) sr[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-    }
-  }
-  __syncthreads();
-  LEWM_STAMP(4, 0);
-  // bias + GELU over all threads into h (the FC2 operand, in sA): 12 columns of one row
-  // per item, loaded first so the 12 GELUs overlap (one item per thread at 32 rows).
-  constexpr int kCpi = 12;
-  static_assert(kFfnQ == 16 * kCpi, "16 items per row");
-  for (int it = tid; it < g.rows8 * 16; it += kThreads) {
-    const int rr = it >> 4, c = (it & 15) * kCpi;
-    const float4* sr = reinterpret_cast<const float4*>(stage + rr * kStage + c);
-    const float4* sb = reinterpret_cast<const float4*>(sb1 + c);
-    float hv[kCpi];
-#pragma unroll
-    for (int i = 0; i < kCpi / 4; ++i) {
-      const float4 a = sr[i], bq = sb[i];
-      hv[4 * i] = a.x + bq.x;
-      hv[4 * i + 1] = a.y + bq.y;
-      hv[4 * i + 2] = a.z + bq.z;
-      hv[4 * i + 3] = a.w + bq.w;
-    }
-    const bool valid = ok1 && map_row(g, tile, rr).valid;  // window slots without a candidate stay zero
-#pragma unroll
-    for (int i = 0; i < kCpi; i += 4) {
-      uint2 pk = make_uint2(0u, 0u);
-      if (valid) {
-        pk.x = pack_bf16x2(gelu_f(hv[i]), gelu_f(hv[i + 1]));
-        pk.y = pack_bf16x2(gelu_f(hv[i + 2]), gelu_f(hv[i + 3]));
+        for (int i = 0; i < 8; ++i)
+          pk[i] = valid ? pack_bf16x2(gelu_f(v[2 * i] + sb1[c0 + 2 * i]), gelu_f(v[2 * i + 1] + sb1[c0 + 2 * i + 1]))
+                        : 0u;
+        if (r < g.rows8) {
+          uint8_t* blk = sA + (c0 >> 6) * kBlk;
+          *reinterpret_cast<uint4*>(blk + sw128_off(r, c0 & 63)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4*>(blk + sw128_off(r, (c0 & 63) + 8)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
       }
-      *reinterpret_cast<uint2*>(sA + ((c + i) >> 6) * kBlk + sw128_off(rr, (c + i) & 63)) = pk;
+    }
+  } else {
+    // At most two quadrants hold rows: stage the accumulator through the dead W1 slots
+    // so all 16 warps share the GELUs.
+    if (quad * 32 < g.rows8) {  // stage the accumulator rows of the tile (whole warps load)
+      float v[48];
+      tmem_ld_cols<48>(tmem + ((uint32_t)(quad * 32) << 16) + slice * 48, v);
+      if (r < g.rows8) {
+        float4* sr = reinterpret_cast<float4*>(stage + r * kStage + slice * 48);
+#pragma unroll
+        for (int i = 0; i < 12; ++i) sr[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+    }
+    __syncthreads();
+    LEWM_STAMP(4, 0);
+    // bias + GELU over all threads into h (the FC2 operand, in sA): 12 columns of one row
+    // per item, loaded first so the 12 GELUs overlap (one item per thread at 32 rows).
+    constexpr int kCpi = 12;
+    static_assert(kFfnQ == 16 * kCpi, "16 items per row");
+    for (int it = tid; it < g.rows8 * 16; it += kThreads) {
+      const int rr = it >> 4, c = (it & 15) * kCpi;
+      const float4* sr = reinterpret_cast<const float4*>(stage + rr * kStage + c);
+      const float4* sb = reinterpret_cast<const float4*>(sb1 + c);
+      float hv[kCpi];
+#pragma unroll
+      for (int i = 0; i < kCpi / 4; ++i) {
+        const float4 a = sr[i], bq = sb[i];
+        hv[4 * i] = a.x + bq.x;
+        hv[4 * i + 1] = a.y + bq.y;
+        hv[4 * i + 2] = a.z + bq.z;
+        hv[4 * i + 3] = a.w + bq.w;
+      }
+      const bool valid = ok1 && map_row(g, tile, rr).valid;  // window slots without a candidate stay zero
+#pragma unroll
+      for (int i = 0; i < kCpi; i += 4) {
+        uint2 pk = make_uint2(0u, 0u);
+        if (valid) {
+          pk.x = pack_bf16x2(gelu_f(hv[i]), gelu_f(hv[i + 1]));
+          pk.y = pack_bf16x2(gelu_f(hv[i + 2]), gelu_f(hv[i + 3]));
+        }
+        *reinterpret_cast<uint2*>(sA + ((c + i) >> 6) * kBlk + sw128_off(rr, (c + i) & 63)) = pk;
+      }
     }
   }
   fence_async_smem();
@@ -1404,8 +1445,8 @@ __global__ void __launch_bounds__(kThreads) k_ffn(DevWeights w, ModelDims md, Ca
   LEWM_STAMP(4, 4);
   tc_fence_after();
   // Warp slice s holds N piece s (D/4 = 48 columns): staged as four slabs of rows8 x 48
-  // floats in the FC1 weight region (free since FC1 retired; the staged FC1 rows were
-  // read before the barrier above), then one bulk copy per piece.
+  // floats (up to 96 KB) in the W1 + W2 region (free since FC2 retired; the staged FC1
+  // rows were read before the barrier above), then one bulk copy per piece.
   static_assert(D / 4 == 48, "one N piece per warp slice");
   float* slabs = stage;
   if (quad * 32 < g.rows8) {

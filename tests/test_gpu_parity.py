@@ -101,6 +101,27 @@ def test_stress_model_cost_matches_oracle():
     assert rel_err(got, want).max() <= COST_RTOL
 
 
+def test_many_tile_fused_ffn_equals_single_env_bits():
+    # 48 envs x 250 samples at window 3: 286 row tiles of 126 rows, enough to fill the SMs,
+    # so the FFN runs fused with GELU read straight from TMEM; one env alone (6 tiles)
+    # takes the two-kernel FFN. Same FC2 hidden quarters on both paths: same bits.
+    desc = ModelDesc()
+    sd = synthetic_state_dict(desc, 0)
+    rt = runtime(desc, 0)
+    rng = np.random.default_rng(21)
+    B, S = 48, 250
+    emb = rng.standard_normal((B, 3, desc.dim)).astype(np.float32)
+    goal = rng.standard_normal((B, 1, desc.dim)).astype(np.float32)
+    cand = rng.standard_normal((B, S, 5, desc.action_dim)).astype(np.float32)
+    big = rt.model_cost(cuda(emb), cuda(goal), cuda(cand))
+    for e in (0, 17, B - 1):
+        single = rt.model_cost(cuda(emb[e:e + 1]), cuda(goal[e:e + 1]), cuda(cand[e:e + 1]))
+        assert torch.equal(single[0], big[e]), e
+    want = lo.get_cost_from_embeddings(emb[:1], goal[:1], cand[:1, :40], sd, desc)
+    rt.sync()
+    assert rel_err(big[:1, :40].cpu().numpy(), want).max() <= COST_RTOL
+
+
 def test_model_cost_is_deterministic_and_batch_independent():
     desc = ModelDesc()
     rt = runtime(desc, 0)
