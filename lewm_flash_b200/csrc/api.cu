@@ -232,6 +232,7 @@ lewm_status pack_weights(lewm_ctx* c, const float* wts, size_t n) {
   const size_t blkA = 128 * 128;  // [128 x 64] block bytes
   const size_t o_qkv = alloc((size_t)L * m.heads * KB * 192 * 128);
   const size_t o_wout = alloc((size_t)L * 4 * NKI * NT * 128);
+  const size_t o_wout_w = D == 192 ? alloc((size_t)L * NKI * D * 128) : 0;
   const size_t o_w1 = alloc((size_t)L * (m.mlp / 128) * KB * blkA);
   const size_t o_w2 = alloc((size_t)L * 4 * NKM * NT * 128);
   const size_t n_ada_tiles = (size_t)L * 6 * D / NT_ADA;
@@ -262,6 +263,11 @@ lewm_status pack_weights(lewm_ctx* c, const float* wts, size_t n) {
       for (int kb = 0; kb < NKI; ++kb) {
         uint8_t* dst = buf.data() + o_wout + ((size_t)(l * 4 + nt) * NKI + kb) * NT * 128;
         pack_block(dst, out_w[l], m.inner, NT, kb, [&](int r) { return nt * NT + r; });
+      }
+    if (D == 192)
+      for (int kb = 0; kb < NKI; ++kb) {
+        uint8_t* dst = buf.data() + o_wout_w + ((size_t)l * NKI + kb) * D * 128;
+        pack_block(dst, out_w[l], m.inner, D, kb, [&](int r) { return r; });
       }
     for (int nt = 0; nt < m.mlp / 128; ++nt)
       for (int kb = 0; kb < KB; ++kb) {
@@ -301,7 +307,7 @@ lewm_status pack_weights(lewm_ctx* c, const float* wts, size_t n) {
   auto* base = static_cast<uint8_t*>(c->d_weights);
   auto bf = [&](size_t o) { return reinterpret_cast<const __nv_bfloat16*>(base + o); };
   auto fl = [&](size_t o) { return reinterpret_cast<const float*>(base + o); };
-  c->w = DevWeights{bf(o_qkv), bf(o_wout), bf(o_w1), bf(o_w2), bf(o_wada), bf(o_we2), fl(o_pos), fl(o_adab),
+  c->w = DevWeights{bf(o_qkv), bf(o_wout), D == 192 ? bf(o_wout_w) : nullptr, bf(o_w1), bf(o_w2), bf(o_wada), bf(o_we2), fl(o_pos), fl(o_adab),
                     fl(o_alnw), fl(o_alnb), fl(o_outb), fl(o_flnw), fl(o_flnb), fl(o_b1), fl(o_b2), fl(o_finw),
                     fl(o_finb), fl(o_convw), fl(o_convb), fl(o_e1w), fl(o_e1b), fl(o_e2b)};
   return LEWM_OK;
@@ -460,8 +466,13 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
     const bool ffn_small = !ln_prebuilt && rows8 <= 64;
     const bool ffn_many = nt * 4 >= c->sm_count;
     const int ffn_fused = (ffn_env != 0 && fc2_parts == 4 && (ffn_small || ffn_many)) ? 1 : 0;
+    // Out-projection: 4 N pieces of D/4 x 2 K halves per tile (8 CTAs: latency), or, once
+    // the calls' tiles fill the SMs with 2 CTAs each, all D columns per CTA (N = 192 runs
+    // at the tensor pipe's peak rate, N = 48 on its per-instruction floor). Same K order
+    // per output element either way, so the same bits.
+    const int outproj_wide = (m.D == 192 && nt * 2 >= c->sm_count) ? 1 : 0;
     return CallGeom{NC,        S, T, H, w, start, cpt, nt, rows8, ln_prebuilt, ffn_fused,
-                    fc2_parts, k, k == n_calls - 1, 1, 0, 128};
+                    fc2_parts, outproj_wide, k, k == n_calls - 1, 1, 0, 128};
   };
   for (int k = 0; k < n_calls; ++k) {
     CallGeom g = geom(k);

@@ -39,6 +39,7 @@ constexpr int kTileM = 128;
 struct DevWeights {
   const __nv_bfloat16* qkv;
   const __nv_bfloat16* wout;
+  const __nv_bfloat16* wout_wide;  // out-proj [L][inner/64][D x 64] (all outputs per K block; D 192 only)
   const __nv_bfloat16* w1;
   const __nv_bfloat16* w2;
   const __nv_bfloat16* wada;
@@ -79,6 +80,7 @@ struct CallGeom {
   int ffn_fused;    // 1: FC1 + GELU + FC2 run as one kernel per (tile, hidden quarter)
   int fc2_parts;    // K parts of FC2's partial sums (4 hidden quarters at D 192 / MLP 768, else 2),
                     // the same on both FFN paths so a row's result does not depend on the batch
+  int outproj_wide; // 1: out-proj CTAs compute all D columns (N = D) of one K half
   int call;     // prediction slot written by this call
   int last;     // 1: final call, write costs
   // Window of the next call (k_final prepares its layer-0 inputs); unused when last.

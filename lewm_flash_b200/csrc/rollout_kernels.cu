@@ -901,7 +901,8 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     }
     __syncthreads();
     LEWM_STAMP(2, 9);
-    // One pass of online softmax over the window: running max, denominator and output.
+    // One pass of online softmax over the window: running max, denominator and output
+    // (exponentials on the special-function unit, __expf: ~2^-21 relative).
     // Window rows before this one come from shared memory, this row from registers.
     float mx = -INFINITY, den = 0.f;
     float o[16];
@@ -913,8 +914,8 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
                         spart[(2 * kMaxWindow + j) * 128 + r] + spart[(3 * kMaxWindow + j) * 128 + r]) *
                        0.125f;
       const float mnew = fmaxf(mx, sj);
-      const float scale = expf(mx - mnew);  // 0 on the first step (mx = -inf)
-      const float pj = expf(sj - mnew);
+      const float scale = __expf(mx - mnew);  // 0 on the first step (mx = -inf)
+      const float pj = __expf(sj - mnew);
       den = den * scale + pj;
       mx = mnew;
       const float4* vr = reinterpret_cast<const float4*>(kv + (base + j) * kKVStride + 64 + part * 8);
@@ -934,8 +935,8 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
                         spart[(2 * kMaxWindow + j) * 128 + r] + spart[(3 * kMaxWindow + j) * 128 + r]) *
                        0.125f;
       const float mnew = fmaxf(mx, sj);
-      const float scale = expf(mx - mnew);
-      const float pj = expf(sj - mnew);
+      const float scale = __expf(mx - mnew);
+      const float pj = __expf(sj - mnew);
       den = den * scale + pj;
 #pragma unroll
       for (int t = 0; t < 16; ++t) o[t] = o[t] * scale + pj * vv[t];
@@ -974,6 +975,10 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
 constexpr int kKSplit = 2;  // K halves of the out-projection GEMM (FC2: CallGeom::fc2_parts)
 template <int D>
 __host__ __device__ constexpr int resid_extra() { return 8 * 5 + 16; }
+// K blocks per copy group: the N = D/4 pieces stream KG blocks; the N = D (192) tile's
+// 24 KB weight blocks stream two at a time (2 groups x 2 x (A + B) in shared memory).
+template <int D, int NT>
+__host__ __device__ constexpr int partial_kg() { return NT == Cfg<D>::NT_OUT ? Cfg<D>::KG : 2; }
 
 // part[kh][rows][n-tile] = A[:, K part kh] . B[n-tile, K part kh]^T for the out-projection
 // or FC2 of a layer. Grid (tiles, 4 N tiles, K parts): each CTA issues 1 / gridDim.z of
@@ -981,20 +986,23 @@ __host__ __device__ constexpr int resid_extra() { return 8 * 5 + 16; }
 // add are applied by the consumer of the sum (the next GEMM's operand builder, or
 // k_final), which adds the parts in a fixed order. Warp 0 issues MMAs, warp 1 refills the
 // operand slots when they do not all fit.
-template <int D>
+template <int D, int NT>
 __global__ void __launch_bounds__(kThreads) k_partial_gemm(const __nv_bfloat16* __restrict__ gA, int nkb,
                                                            const __nv_bfloat16* __restrict__ gB, CallGeom g,
                                                            float* __restrict__ part, size_t part_stride, int skind,
                                                            uint32_t* status) {
   using C = Cfg<D>;
-  constexpr int NT = C::NT_OUT;
-  constexpr int CW = NT / 4;
+  constexpr int CW = NT / 4;          // columns per warp slice
   constexpr int B_BLK = NT * 128;
+  constexpr int PW = D / 4;           // columns of one partial-sum piece
+  constexpr int NLP = NT / PW;        // pieces this CTA writes (1, or 4 when N = D)
+  constexpr int TMEM_COLS = NT <= 64 ? 64 : (NT <= 128 ? 128 : 256);
+  static_assert(NT % PW == 0 && NT <= 256, "N tile");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const int tile = blockIdx.x, nt = blockIdx.y, kh = blockIdx.z;
   const int kcount = nkb / (int)gridDim.z, kb0 = kh * kcount;
-  const ResidLayout lay = resid_layout(g.rows8, kcount, B_BLK, C::KG, resid_extra<D>());
+  const ResidLayout lay = resid_layout(g.rows8, kcount, B_BLK, partial_kg<D, NT>(), resid_extra<D>());
   uint8_t* sA = smem;
   uint8_t* sB = smem + lay.b_off;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + lay.v_off);
@@ -1020,7 +1028,7 @@ __global__ void __launch_bounds__(kThreads) k_partial_gemm(const __nv_bfloat16* 
   if (warp == 0) ks.issue_first(lane, false);  // weights before the wait, one instruction
   __syncwarp();
   if (warp == 0) {
-    tmem_alloc(tmem_slot, C::TMEM_OUT);
+    tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
   LEWM_STAMP(skind, 1);
@@ -1051,28 +1059,29 @@ __global__ void __launch_bounds__(kThreads) k_partial_gemm(const __nv_bfloat16* 
   float v[CW];
   tmem_ld_cols<CW>(taddr, v);
   LEWM_STAMP(skind, 7);
-  // Slab of this piece staged in the operand slots (dead once the MMAs retired), then
-  // one bulk copy. The slab (rows8 x NT floats) fits below the barriers: the A slots
-  // alone hold rows8 x 128 bytes per K block plus a 16 KB tail.
+  // The CTA's pieces staged as slabs in the operand slots (dead once the MMAs retired),
+  // then one bulk copy per piece. The slabs (rows8 x NT floats) fit below the barriers
+  // (checked; the A slots alone hold rows8 x 128 bytes per K block plus a 16 KB tail).
   float* slab = reinterpret_cast<float*>(smem);
   const bool fits = g.rows8 * NT * 4 <= lay.v_off;
-  if (fits && r < g.rows8) stage_part_row<D, CW>(slab, r, slice * (CW / 4), v);
+  const int col0 = slice * CW;  // CTA-local first column of this warp slice
+  if (fits && r < g.rows8)
+    stage_part_row<D, CW>(slab + (col0 / PW) * g.rows8 * PW, r, (col0 % PW) / 4, v);
   fence_async_smem();
   __syncthreads();
   LEWM_STAMP(skind, 9);
-  if (tid == 0) {
-    if (ok && fits) {
-      bulk_s2g(part + kh * part_stride + ((size_t)tile * 4 + nt) * 128 * NT, slab, g.rows8 * NT * 4);
-      bulk_commit();
-      bulk_wait_read();
-    } else if (!fits) {
-      atomicOr(status, LEWM_DEV_BADARG);
-    }
+  if (warp == 0 && lane < NLP) {  // each issuing lane waits for its own copy's reads
+    if (ok && fits)
+      bulk_s2g(part + kh * part_stride + ((size_t)tile * 4 + nt * NLP + lane) * 128 * PW,
+               slab + lane * g.rows8 * PW, g.rows8 * PW * 4);
+    bulk_commit();
+    bulk_wait_read();
   }
+  if (tid == 0 && !fits) atomicOr(status, LEWM_DEV_BADARG);
   LEWM_STAMP(skind, 6);
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, C::TMEM_OUT);
+  if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 // ---------------------------------------------------------------- FC1 + GELU
@@ -1600,7 +1609,12 @@ cudaError_t set_smem_attrs() {
   if ((e = cudaFuncSetAttribute(k_qkv_attn<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_qkv<D>()))) return e;
   if constexpr (D == 192)
     if ((e = cudaFuncSetAttribute(k_ffn<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_ffn<D>()))) return e;
-  if ((e = cudaFuncSetAttribute(k_partial_gemm<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_resid<D>())))
+  if constexpr (D == 192)
+    if ((e = cudaFuncSetAttribute(k_partial_gemm<D, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  smem_resid<D>())))
+      return e;
+  if ((e = cudaFuncSetAttribute(k_partial_gemm<D, Cfg<D>::NT_OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                smem_resid<D>())))
     return e;
   if ((e = cudaFuncSetAttribute(k_fc1<D, kFc1N>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_fc1<D, kFc1N>())))
     return e;
@@ -1677,12 +1691,23 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
     if (prof) prof->end(KC_QKV_ATTN, 2.0 * rows * D * 3 * md.inner + 4.0 * rows * g.w * md.inner, st);
     // out-projection partial sums (bias, gate_msa and residual applied by FC1's operand builder)
     if (prof) prof->begin(st);
-    LEWM_TRY(launch_k(k_partial_gemm<D>, dim3(g.n_tiles, 4, kKSplit), dim3(kThreads),
-                      resid_layout(g.rows8, nkb_inner / kKSplit, Cfg<D>::NT_OUT * 128, Cfg<D>::KG, resid_extra<D>())
-                          .bytes,
-                      st, (const __nv_bfloat16*)b.attn, nkb_inner,
-                      (const __nv_bfloat16*)(w.wout + (size_t)l * 4 * nkb_inner * Cfg<D>::NT_OUT * 64), g, b.part_a,
-                      b.part_stride, 5, status));
+    if constexpr (D == 192) {
+      if (g.outproj_wide)
+        LEWM_TRY(launch_k(k_partial_gemm<D, D>, dim3(g.n_tiles, 1, kKSplit), dim3(kThreads),
+                          resid_layout(g.rows8, nkb_inner / kKSplit, D * 128, partial_kg<D, D>(), resid_extra<D>())
+                              .bytes,
+                          st, (const __nv_bfloat16*)b.attn, nkb_inner,
+                          (const __nv_bfloat16*)(w.wout_wide + (size_t)l * nkb_inner * D * 64), g, b.part_a,
+                          b.part_stride, 5, status));
+    }
+    if (!g.outproj_wide)
+      LEWM_TRY(launch_k(k_partial_gemm<D, Cfg<D>::NT_OUT>, dim3(g.n_tiles, 4, kKSplit), dim3(kThreads),
+                        resid_layout(g.rows8, nkb_inner / kKSplit, Cfg<D>::NT_OUT * 128, Cfg<D>::KG,
+                                     resid_extra<D>())
+                            .bytes,
+                        st, (const __nv_bfloat16*)b.attn, nkb_inner,
+                        (const __nv_bfloat16*)(w.wout + (size_t)l * 4 * nkb_inner * Cfg<D>::NT_OUT * 64), g,
+                        b.part_a, b.part_stride, 5, status));
     if (prof) prof->end(KC_OUT, 2.0 * rows * md.inner * D, st);
     if (g.ln_prebuilt) {  // FC1 operand: s = r + gate_msa * (out-proj + bias), LN2 -> modulate -> ffn.norm
       const ResidUpdate u{b.x, b.part_a, b.part_stride, 2, w.out_b + l * D, l * 6 * D + 2 * D, b.xs};
@@ -1709,7 +1734,7 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
     // FC2 partial sums over fc2_parts K parts (bias, gate_mlp and residual applied by the
     // next QKV operand builder or, after the last layer, by k_final)
     if (prof) prof->begin(st);
-    LEWM_TRY(launch_k(k_partial_gemm<D>, dim3(g.n_tiles, 4, g.fc2_parts), dim3(kThreads),
+    LEWM_TRY(launch_k(k_partial_gemm<D, Cfg<D>::NT_OUT>, dim3(g.n_tiles, 4, g.fc2_parts), dim3(kThreads),
                       resid_layout(g.rows8, nkb_mlp / g.fc2_parts, Cfg<D>::NT_OUT * 128, Cfg<D>::KG, resid_extra<D>())
                           .bytes,
                       st, (const __nv_bfloat16*)b.h, nkb_mlp,
