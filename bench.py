@@ -276,9 +276,10 @@ def reference_arm(args, rank, world):
     return 0
 
 
-def model_cost_case(S, repeat):
-    """R predictor rollouts of S candidates (5 calls x 6 layers each, windows 1, 2, 3, 3, 3):
-    a fixed launch sequence for ncu captures of one kernel at a known geometry."""
+def model_cost_case(S, repeat, envs=1):
+    """R predictor rollouts of S candidates per env: 1 env with history 1 (5 calls x 6 layers,
+    windows 1, 2, 3, 3, 3), or B envs with history 3 (3 calls x 6 layers, windows 3, 3, 3).
+    A fixed launch sequence for ncu captures of one kernel at a known geometry."""
     import torch
 
     from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
@@ -288,9 +289,10 @@ def model_cost_case(S, repeat):
     desc = ModelDesc()
     rt = Runtime(desc, synthetic_state_dict(desc, 0), dev)
     rng = np.random.default_rng(7)
-    emb = torch.as_tensor(rng.standard_normal((1, 1, desc.dim)), dtype=torch.float32, device=dev)
-    goal = torch.as_tensor(rng.standard_normal((1, 1, desc.dim)), dtype=torch.float32, device=dev)
-    cand = torch.as_tensor(rng.standard_normal((1, S, 5, desc.action_dim)), dtype=torch.float32, device=dev)
+    hist = 1 if envs == 1 else 3
+    emb = torch.as_tensor(rng.standard_normal((envs, hist, desc.dim)), dtype=torch.float32, device=dev)
+    goal = torch.as_tensor(rng.standard_normal((envs, 1, desc.dim)), dtype=torch.float32, device=dev)
+    cand = torch.as_tensor(rng.standard_normal((envs, S, 5, desc.action_dim)), dtype=torch.float32, device=dev)
     ms = []
     for _ in range(repeat):
         a = torch.cuda.Event(enable_timing=True)
@@ -301,7 +303,7 @@ def model_cost_case(S, repeat):
         torch.cuda.synchronize(dev)
         ms.append(a.elapsed_time(b))
     rt.sync()
-    print(json.dumps({"case": "model_cost", "samples": S, "ms": ms, "cost0": float(costs[0, 0])}))
+    print(json.dumps({"case": "model_cost", "envs": envs, "samples": S, "ms": ms, "cost0": float(costs[0, 0])}))
     return 0
 
 
@@ -314,12 +316,13 @@ def main() -> int:
     ap.add_argument("--cpu-baseline-plans", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--model-cost", type=int, default=0, metavar="S",
-                    help="profiling case: time R model-cost calls of S candidates (1 env, horizon 5, "
-                         "history 1, window 3) and exit; no bench line")
+                    help="profiling case: time R model-cost calls of S candidates per env (horizon 5; 1 env "
+                         "with history 1, or --envs B with history 3) and exit; no bench line")
+    ap.add_argument("--envs", type=int, default=1)
     ap.add_argument("--repeat", type=int, default=3)
     args = ap.parse_args()
     if args.model_cost:
-        return model_cost_case(args.model_cost, args.repeat)
+        return model_cost_case(args.model_cost, args.repeat, args.envs)
 
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
