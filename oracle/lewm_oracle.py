@@ -52,7 +52,9 @@ def layer_norm(x, weight=None, bias=None, eps=1e-5):
 
 
 def silu(x):
-    return (x / (F32(1) + np.exp(-x))).astype(F32, copy=False)
+    # exp(-x) overflows to inf for x below about -88: x / inf = -0, the limit of SiLU.
+    with np.errstate(over="ignore"):
+        return (x / (F32(1) + np.exp(-x))).astype(F32, copy=False)
 
 
 def gelu(x):
