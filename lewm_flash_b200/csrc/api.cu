@@ -52,6 +52,7 @@ struct Workspace {
   __nv_bfloat16* h = nullptr;
   float* pred = nullptr;
   float* costs = nullptr;
+  float* kvc = nullptr;      // growing-window key / value cache (RolloutBufs::kvc)
   // plan state
   float* mean = nullptr;
   float* stdv = nullptr;
@@ -66,12 +67,27 @@ struct Workspace {
 };
 
 struct WsReq {
-  size_t n_cand, T, A, D, L, tiles, heads, mlp, npred, B, R, ncol;
+  size_t n_cand, T, A, D, L, tiles, heads, mlp, npred, B, R, ncol, kvpos;
   bool operator<=(const WsReq& o) const {
     return n_cand <= o.n_cand && T <= o.T && tiles <= o.tiles && npred <= o.npred && B <= o.B && R <= o.R &&
-           ncol <= o.ncol;
+           ncol <= o.ncol && kvpos <= o.kvpos;
   }
 };
+
+// Growing-window key / value cache (CallGeom::kv_read); LEWM_KV_CACHE=0 recomputes every
+// window position in every call instead.
+bool kv_cache_on() {
+  static const bool on = [] {
+    const char* v = std::getenv("LEWM_KV_CACHE");
+    return v ? std::atoi(v) != 0 : true;
+  }();
+  return on;
+}
+
+// Positions per candidate the cache holds for a rollout with history H and window HS: the
+// calls before the window first slides write positions 0 .. HS - 2; none when the first
+// call's window is already full.
+int kv_positions(int H, int HS) { return (kv_cache_on() && H + 1 <= HS) ? HS - 1 : 0; }
 
 }  // namespace
 
@@ -348,6 +364,7 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
     r.B = std::max(r.B, c->cap.B);
     r.R = std::max(r.R, c->cap.R);
     r.ncol = std::max(r.ncol, c->cap.ncol);
+    r.kvpos = std::max(r.kvpos, c->cap.kvpos);
     clear_graphs(c);
     cudaFree(c->ws.base);
     c->ws = Workspace{};
@@ -376,6 +393,7 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   const size_t o_h = carve(r.tiles * (size_t)(m.mlp / 64) * 128 * 64 * 2);
   const size_t o_pred = carve(r.n_cand * r.npred * (size_t)m.D * 4);
   const size_t o_costs = carve(r.n_cand * 4);
+  const size_t o_kvc = carve((size_t)m.L * r.n_cand * r.kvpos * m.heads * 128 * 4);
   const size_t ta = r.T * m.A;
   const size_t o_mean = carve(r.B * ta * 4);
   const size_t o_std = carve(r.B * ta * 4);
@@ -408,6 +426,7 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   ws.h = reinterpret_cast<__nv_bfloat16*>(b + o_h);
   ws.pred = reinterpret_cast<float*>(b + o_pred);
   ws.costs = reinterpret_cast<float*>(b + o_costs);
+  ws.kvc = reinterpret_cast<float*>(b + o_kvc);
   ws.mean = reinterpret_cast<float*>(b + o_mean);
   ws.stdv = reinterpret_cast<float*>(b + o_std);
   ws.elites = reinterpret_cast<float*>(b + o_el);
@@ -435,15 +454,22 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
   RolloutBufs b{emb,        emb_pc,    goal,      goal_pc, cand,      c->ws.act_a, c->ws.mod,
                 c->ws.x,    c->ws.x2,  c->ws.xs,  c->ws.part_a, c->ws.part_b, c->ws.part_stride, c->ws.a_op,
                 c->ws.attn, c->ws.h,
-                c->ws.pred, costs};
+                c->ws.pred, costs, c->ws.kvc, kv_positions(H, HS)};
   const int n_calls = T - H + 1;
   auto geom = [&](int k) {
     const int end = H + k;
     const int start = std::max(0, end - HS);
     const int w = end - start;
+    // While the window only grows (start stays 0) a call's earlier positions are those of
+    // the call before, with the same inputs and outputs: such a call runs only its new last
+    // position, its attention reading the earlier keys / values from the cache that the
+    // calls before wrote.
+    const bool kv_read = kv_cache_on() && k >= 1 && end <= HS;
+    const bool kv_write = kv_cache_on() && k + 1 < n_calls && end + 1 <= HS;
+    const int rpc = kv_read ? 1 : w;
     int cpt, nt;
-    tile_geom(NC, w, c->tile_target, &cpt, &nt);
-    const int rows8 = std::min(128, (cpt * w + 7) & ~7);
+    tile_geom(NC, rpc, c->tile_target, &cpt, &nt);
+    const int rows8 = std::min(128, (cpt * rpc + 7) & ~7);
     // Operands of tiles with more rows than one pass of the in-kernel build (512 threads,
     // D/12 per row) are built once per tile by a separate kernel.
     static const int pre_rows = [] {
@@ -471,8 +497,15 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
     // at the tensor pipe's peak rate, N = 48 on its per-instruction floor). Same K order
     // per output element either way, so the same bits.
     const int outproj_wide = (m.D == 192 && nt * 2 >= c->sm_count) ? 1 : 0;
-    return CallGeom{NC,        S, T, H, w, start, cpt, nt, rows8, ln_prebuilt, ffn_fused,
-                    fc2_parts, outproj_wide, k, k == n_calls - 1, 1, 0, 128};
+    CallGeom g{NC,        S, T, H, w, start, cpt, nt, rows8, ln_prebuilt, ffn_fused,
+               fc2_parts, outproj_wide, k, k == n_calls - 1, 1, 0, 128};
+    g.rpc = rpc;
+    g.pos0 = w - rpc;
+    g.kv_read = kv_read ? 1 : 0;
+    g.kv_write = kv_write ? 1 : 0;
+    g.next_rpc = 1;
+    g.next_pos0 = 0;
+    return g;
   };
   for (int k = 0; k < n_calls; ++k) {
     CallGeom g = geom(k);
@@ -481,6 +514,8 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
       g.next_w = gn.w;
       g.next_start = gn.start;
       g.next_cpt = gn.cpt;
+      g.next_rpc = gn.rpc;
+      g.next_pos0 = gn.pos0;
     }
     // Calls alternate residual buffers: k_final of call k writes call k+1's layer-0 rows.
     b.x = (k & 1) ? c->ws.x2 : c->ws.x;
@@ -803,7 +838,7 @@ lewm_status lewm_model_cost(lewm_ctx* c, const float* emb, int32_t emb_per_sampl
   const int NC = B * S;
   WsReq need{(size_t)NC, (size_t)T, (size_t)c->md.A, (size_t)c->md.D, (size_t)c->md.L,
              (size_t)max_call_tiles(NC, T, H, history_size, c->tile_target), (size_t)c->md.heads, (size_t)c->md.mlp,
-             (size_t)(T - H + 1), 1, 0, 0};
+             (size_t)(T - H + 1), 1, 0, 0, (size_t)kv_positions(H, history_size)};
   lewm_status s = ensure_ws(c, need);
   if (s != LEWM_OK) return s;
   return run_model_cost(c, emb, emb_per_sample != 0, H, goal, goal_per_sample != 0, cand, B, S, T, history_size,
@@ -851,7 +886,8 @@ lewm_status lewm_plan(lewm_ctx* c, const lewm_plan_desc* p, const float* emb, co
   const int NC = B * Smax;
   WsReq need{(size_t)NC, (size_t)T, (size_t)A, (size_t)m.D, (size_t)m.L,
              (size_t)max_call_tiles(NC, T, H, p->history_size, c->tile_target), (size_t)m.heads, (size_t)m.mlp,
-             (size_t)(T - H + 1), (size_t)B, (size_t)R, (size_t)std::max(ncol, 1)};
+             (size_t)(T - H + 1), (size_t)B, (size_t)R, (size_t)std::max(ncol, 1),
+             (size_t)kv_positions(H, p->history_size)};
   s = ensure_ws(c, need);
   if (s != LEWM_OK) return s;
   Workspace& ws = c->ws;
@@ -959,7 +995,7 @@ lewm_status lewm_sample_candidates(lewm_ctx* c, const lewm_plan_desc* p, int32_t
   int kind, ncol;
   noise_kind(c, p, &kind, &ncol);
   WsReq need{1, (size_t)p->horizon, (size_t)c->md.A, (size_t)c->md.D, (size_t)c->md.L, 1, (size_t)c->md.heads,
-             (size_t)c->md.mlp, 1, 1, 0, (size_t)std::max(ncol, 1)};
+             (size_t)c->md.mlp, 1, 1, 0, (size_t)std::max(ncol, 1), 0};
   s = ensure_ws(c, need);
   if (s != LEWM_OK) return s;
   s = upload_W(c, p, ncol, st);

@@ -85,6 +85,15 @@ struct CallGeom {
   int last;     // 1: final call, write costs
   // Window of the next call (k_final prepares its layer-0 inputs); unused when last.
   int next_w, next_start, next_cpt;
+  // Rows of each candidate this call processes: the whole window (rpc = w, pos0 = 0) or, on
+  // a growing-window call whose earlier positions the calls before already ran through the
+  // layers (their inputs and outputs do not change while the window only grows: causal
+  // attention, fixed positions), just the new last position (rpc = 1, pos0 = w - 1), whose
+  // attention reads the earlier positions' keys and values from the cache (kv_read).
+  int rpc, pos0;
+  int kv_read;   // 1: keys / values of positions < pos0 come from RolloutBufs::kvc
+  int kv_write;  // 1: this call's rows store their keys / values there (the next call reads them)
+  int next_rpc, next_pos0;
 };
 
 struct RolloutBufs {
@@ -106,6 +115,11 @@ struct RolloutBufs {
   __nv_bfloat16* h;
   float* pred;
   float* costs;
+  // Keys and values of growing-window positions per layer, candidate, position, head:
+  // [L][n_cand][kvc_pos][heads][k 64 | v 64] fp32 (the row format of the attention's
+  // shared k/v scratch). Null with kvc_pos 0 when no call of the rollout reads it.
+  float* kvc;
+  int kvc_pos;
 };
 
 // Optional per-launch event profiler (host side). When `on`, every launch site

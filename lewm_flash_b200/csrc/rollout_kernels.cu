@@ -81,8 +81,8 @@ struct RowMap {
 };
 __device__ __forceinline__ RowMap map_row(const CallGeom& g, int tile, int r) {
   RowMap m;
-  const int cl = r / g.w;
-  m.pos = r - cl * g.w;
+  const int cl = r / g.rpc;  // g.rpc rows per candidate, window positions pos0 ..
+  m.pos = g.pos0 + (r - cl * g.rpc);
   m.cand = tile * g.cpt + cl;
   m.valid = (cl < g.cpt) && (m.cand < g.n_cand);
   m.tok = m.cand * g.T + g.start + m.pos;
@@ -857,7 +857,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     const int r = quad * 32 + lane;
     const RowMap m = map_row(g, tile, r);
     const bool valid = ok && m.valid;
-    const int base = r - m.pos;
+    const int base = r - (m.pos - g.pos0);  // tile row of window position pos0 of the candidate
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16) + part * 8;
     float q[16], kk[16], vv[16];
     tmem_ld8(trow, q);
@@ -874,6 +874,23 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
       kvr[o] = make_float4(kk[4 * t], kk[4 * t + 1], kk[4 * t + 2], kk[4 * t + 3]);
       kvr[16 + o] = make_float4(vv[4 * t], vv[4 * t + 1], vv[4 * t + 2], vv[4 * t + 3]);
     }
+    // Key / value rows of the growing-window positions a later call reads instead of
+    // recomputing them (same row format, row stride heads x 128 floats).
+    const size_t kv_cand = ((size_t)layer * g.n_cand + m.cand) * b.kvc_pos;
+    if (g.kv_write && valid && m.pos < b.kvc_pos) {
+      float4* cw = reinterpret_cast<float4*>(b.kvc + ((kv_cand + m.pos) * md.heads + head) * 128 + part * 8);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int o = (t & 1) + (t >> 1) * 8;
+        cw[o] = make_float4(kk[4 * t], kk[4 * t + 1], kk[4 * t + 2], kk[4 * t + 3]);
+        cw[16 + o] = make_float4(vv[4 * t], vv[4 * t + 1], vv[4 * t + 2], vv[4 * t + 3]);
+      }
+    }
+    // Rows of the earlier window positions: this tile's rows in shared memory, or, on a
+    // call that runs only the new position, the cache (positions 0 .. pos - 1).
+    const float* kvb = g.kv_read ? b.kvc + (kv_cand * md.heads + head) * 128 + part * 8
+                                 : kv + (size_t)base * kKVStride + part * 8;
+    const int kvs = g.kv_read ? md.heads * 128 : kKVStride;  // floats between window positions
     __syncthreads();
     LEWM_STAMP(2, 7);
     // Loops over the window stay rolled: each CTA runs this code once, so compact code
@@ -881,7 +898,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     const int npos = valid ? m.pos : -1;
 #pragma unroll 1
     for (int j = 0; j < npos; ++j) {
-      const float4* kr = reinterpret_cast<const float4*>(kv + (base + j) * kKVStride + part * 8);
+      const float4* kr = reinterpret_cast<const float4*>(kvb + (size_t)j * kvs);
       float d = 0.f;
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
@@ -918,7 +935,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
       const float pj = __expf(sj - mnew);
       den = den * scale + pj;
       mx = mnew;
-      const float4* vr = reinterpret_cast<const float4*>(kv + (base + j) * kKVStride + 64 + part * 8);
+      const float4* vr = reinterpret_cast<const float4*>(kvb + (size_t)j * kvs + 64);
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         const float4 v4 = vr[(t & 1) + (t >> 1) * 8];
@@ -1491,10 +1508,11 @@ __global__ void __launch_bounds__(128) k_final(DevWeights w, ModelDims md, CallG
   griddep_wait();
   griddep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rows_per_cand = g.last ? 1 : g.next_w;
+  const int rows_per_cand = g.last ? 1 : g.next_rpc;  // rows the next call processes per candidate
   const int item = blockIdx.x * 4 + warp;
   if (item >= g.n_cand * rows_per_cand) return;
-  const int cand = item / rows_per_cand, p = item - cand * rows_per_cand;
+  const int cand = item / rows_per_cand, pi = item - cand * rows_per_cand;
+  const int p = g.last ? pi : g.next_pos0 + pi;  // window position in the next call
   constexpr int NP = D / 64;
   const int NPred = g.T - g.H + 1;
   float* pcand = b.pred + (size_t)cand * NPred * D;
@@ -1505,7 +1523,7 @@ __global__ void __launch_bounds__(128) k_final(DevWeights w, ModelDims md, CallG
     // Output of the last layer for the window's last token: s + gate_mlp * ((P0 + P1) + b2),
     // the FC2 update of the last layer still pending.
     const int tile = cand / g.cpt;
-    const int r = (cand - tile * g.cpt) * g.w + (g.w - 1);
+    const int r = (cand - tile * g.cpt) * g.rpc + (g.rpc - 1);  // window position w - 1
     const size_t o = ((size_t)tile * 128 + r) * D;
     const float* pt = b.part_b + (size_t)tile * 128 * D;  // the tile's partial block
     const int tok = cand * g.T + g.start + g.w - 1;
@@ -1568,7 +1586,7 @@ __global__ void __launch_bounds__(128) k_final(DevWeights w, ModelDims md, CallG
   const int e2 = b.emb_per_cand ? cand : cand / g.S;
   const float* src = new_pred ? pcand + (size_t)g.call * D
                               : ((j < g.H) ? b.emb + ((size_t)e2 * g.H + j) * D : pcand + (size_t)(j - g.H) * D);
-  const int nr = (cand - ntile * g.next_cpt) * g.next_w + p;
+  const int nr = (cand - ntile * g.next_cpt) * g.next_rpc + pi;
   prep_layer0_row<D>(w, src, p, b.xn + ((size_t)ntile * 128 + nr) * D, lane);
 }
 
@@ -1666,7 +1684,7 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
   cudaError_t e = set_smem_attrs<D>();
   if (e) return e;
   const int nkb_inner = md.inner / 64, nkb_mlp = md.mlp / 64;
-  const double rows = (double)g.n_cand * g.w;  // valid window rows
+  const double rows = (double)g.n_cand * g.rpc;  // valid rows this call processes
 #define LEWM_TRY(x)                         \
   do {                                      \
     if ((e = (x)) != cudaSuccess) return e; \
@@ -1743,7 +1761,7 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
     if (prof) prof->end(KC_FC2, 2.0 * rows * md.mlp * D, st);
   }
   if (prof) prof->begin(st);
-  const int final_items = g.n_cand * (g.last ? 1 : g.next_w);
+  const int final_items = g.n_cand * (g.last ? 1 : g.next_rpc);
   LEWM_TRY(launch_k(k_final<D>, dim3((final_items + 3) / 4), dim3(128), 0, st, w, md, g, b));
   if (prof) prof->end(KC_FINAL, 0.0, st);
 #undef LEWM_TRY

@@ -73,6 +73,44 @@ def test_model_cost_matches_oracle(H, B, S, emb_rank4):
         assert np.corrcoef(got[b], want[b])[0, 1] > 0.99
 
 
+_RECOMPUTE = """
+import sys, numpy as np, torch
+from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
+from lewm_flash_b200.runtime import Runtime
+d = np.load(sys.argv[1])
+desc = ModelDesc()
+rt = Runtime(desc, synthetic_state_dict(desc, 0), "cuda:0")
+t = lambda x: torch.as_tensor(x, device="cuda:0")
+np.save(sys.argv[2], rt.model_cost(t(d["emb"]), t(d["goal"]), t(d["cand"])).cpu().numpy())
+"""
+
+
+def test_growing_window_cache_equals_full_recompute_bits(tmp_path):
+    # With history 1 and window 3, calls 1 and 2 run only their new window position and read
+    # the earlier positions' keys / values from the cache; a process with LEWM_KV_CACHE=0
+    # recomputes every position in every call. Rows do not depend on the tile geometry, so
+    # both give the same bits.
+    import os
+    import subprocess
+    import sys
+
+    desc = ModelDesc()
+    rt = runtime(desc, 0)
+    rng = np.random.default_rng(41)
+    emb = rng.standard_normal((2, 1, desc.dim)).astype(np.float32)
+    goal = rng.standard_normal((2, 1, desc.dim)).astype(np.float32)
+    cand = rng.standard_normal((2, 150, 5, desc.action_dim)).astype(np.float32)
+    got = rt.model_cost(cuda(emb), cuda(goal), cuda(cand)).cpu().numpy()
+    np.savez(tmp_path / "in.npz", emb=emb, goal=goal, cand=cand)
+    env = dict(os.environ, LEWM_KV_CACHE="0")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env["PYTHONPATH"] = root + os.pathsep + env.get("PYTHONPATH", "")
+    subprocess.run([sys.executable, "-c", _RECOMPUTE, str(tmp_path / "in.npz"), str(tmp_path / "out.npy")],
+                   env=env, cwd=root, check=True, timeout=600)
+    want = np.load(tmp_path / "out.npy")
+    assert np.array_equal(got, want)
+
+
 def test_model_cost_per_sample_goal_and_history_window():
     desc = ModelDesc()
     sd = synthetic_state_dict(desc, 0)
