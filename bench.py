@@ -48,8 +48,8 @@ F_CANON = 9 * L * F_BLOCK_TOKEN + T * L * 2 * D * 6 * D + T * 2 * (A * A + A * 4
 NCU_TRAFFIC = {
     "qkv_attn": {"bytes": 2121728, "launch": "QKV + attention, 180 rows (60 candidates x window 3), 6 tiles x 16 heads"},
     "ffn": {"bytes": 1268480, "launch": "fused FFN, 180 rows (60 candidates x window 3), 6 tiles x 4 hidden quarters"},
-    "out_proj": {"bytes": 2381824, "launch": "out-proj K halves, 900 rows (300 candidates x window 3), 8 tiles"},
-    "fc2": {"bytes": 1792256, "launch": "FC2 hidden quarters, 900 rows (300 candidates x window 3), 8 tiles"},
+    "out_proj": {"bytes": 2382592, "launch": "out-proj K halves, 900 rows (300 candidates x window 3), 8 tiles"},
+    "fc2": {"bytes": 1792768, "launch": "FC2 hidden quarters, 900 rows (300 candidates x window 3), 8 tiles"},
 }
 
 
