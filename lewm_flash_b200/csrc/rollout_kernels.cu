@@ -416,17 +416,32 @@ __global__ void __launch_bounds__(kThreads) k_adaln(DevWeights w, ModelDims md, 
   const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + slice * CW;
   float v[CW];
   tmem_ld_cols<CW>(taddr, v);
-  if (ok && row < rows) {
+  // The tile's rows staged as bf16 in the operand / weight slots (dead once the MMAs
+  // retired; rows padded to SROW bytes, so 8 consecutive rows' 16-byte stores hit distinct
+  // banks), then one bulk copy per row: the NT columns of a row are contiguous in mod
+  // (row-per-thread global stores would touch 32 lines per warp instruction).
+  constexpr int SROW = NT * 2 + 16;
+  static_assert(128 * SROW <= C::KB * (kBlk + NT * 128), "staging fits the operand slots");
+  uint8_t* stg = smem;
+  const int r = quad * 32 + lane;
+  if (ok) {
     const float* bs = sbias + slice * CW;
-    uint4* dst = reinterpret_cast<uint4*>(mod + (size_t)row * ncols + nt * NT + slice * CW);
+    uint4* sr = reinterpret_cast<uint4*>(stg + r * SROW + slice * CW * 2);
 #pragma unroll
     for (int i = 0; i < CW / 8; ++i) {
       uint32_t pk[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k)
         pk[k] = pack_bf16x2(v[8 * i + 2 * k] + bs[8 * i + 2 * k], v[8 * i + 2 * k + 1] + bs[8 * i + 2 * k + 1]);
-      dst[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      sr[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     }
+  }
+  fence_async_smem();
+  __syncthreads();
+  if (warp < 4 && ok) {  // lane of warp q copies row 32 q + lane and waits for its own copy's reads
+    if (row < rows) bulk_s2g(mod + (size_t)row * ncols + nt * NT, stg + r * SROW, NT * 2);
+    bulk_commit();
+    bulk_wait_read();
   }
   LEWM_STAMP(1, 6);
   tc_fence_before();
