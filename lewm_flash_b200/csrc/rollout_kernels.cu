@@ -450,6 +450,152 @@ __global__ void __launch_bounds__(kThreads) k_adaln(DevWeights w, ModelDims md, 
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
+// ---------------------------------------------------------------- AdaLN modulation, persistent
+// The same product as k_adaln for calls with many row tiles (width 192): one CTA per
+// (192-column N tile, row-tile group) keeps its weight slice in shared memory and runs its
+// row tiles through a pipeline, so the tensor pipe works on tile i + 1 while the epilogue
+// drains tile i. Warp 0 streams the tiles' operands into two buffers, warp 1 issues each
+// tile's 12 MMAs into one of two TMEM accumulators, warps 4-15 apply the bias, convert to
+// bf16, stage the rows and bulk-copy them to mod. Hand-offs are mbarriers: full_a (operand
+// landed), empty_a and mma_done (the tile's MMAs retired), tmem_empty (the epilogue read the
+// accumulator). Every wait is bounded; after a timeout every role stops at its next wait,
+// and the epilogue's decisions come from one thread through shared memory, so its named
+// barriers are always reached by all 384 threads. Per tile the MMAs and the epilogue
+// arithmetic are those of k_adaln: the same bits.
+constexpr int kAdaGroups = 4;  // row-tile groups per N tile (36 N tiles x 4 = 144 CTAs at width 192)
+template <int D>
+constexpr int smem_adaln_ps() {
+  constexpr int NT = Cfg<D>::NT_ADA;
+  return 1024 + Cfg<D>::KB * NT * 128 + 2 * Cfg<D>::KB * kBlk + 128 * (NT * 2 + 16) + NT * 4 + 8 * 9 + 16;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) k_adaln_ps(DevWeights w, ModelDims md, int rows,
+                                                       const __nv_bfloat16* __restrict__ act_a,
+                                                       __nv_bfloat16* __restrict__ mod, uint32_t* status) {
+  using C = Cfg<D>;
+  constexpr int NT = C::NT_ADA;
+  constexpr int KB = C::KB;
+  constexpr int SROW = NT * 2 + 16;  // staged row bytes (16-byte stores of 8 consecutive rows hit distinct banks)
+  constexpr int CWE = NT / 3;        // columns per epilogue warp (3 warps per TMEM lane quadrant)
+  static_assert(NT == 192 && CWE % 8 == 0, "width 192");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sB = smem;                                  // weights of this N tile, [KB][NT x 64]
+  uint8_t* sA = sB + KB * NT * 128;                    // two operand buffers, [2][KB][128 x 64]
+  uint8_t* stg = sA + 2 * KB * kBlk;                   // staged output rows, [128][SROW]
+  float* sbias = reinterpret_cast<float*>(stg + 128 * SROW);
+  uint64_t* bar_w = reinterpret_cast<uint64_t*>(sbias + NT);
+  uint64_t* full_a = bar_w + 1;      // [2]
+  uint64_t* empty_a = full_a + 2;    // [2]
+  uint64_t* mma_done = empty_a + 2;  // [2]
+  uint64_t* tmem_empty = mma_done + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+  volatile uint32_t* eflag = tmem_slot + 1;  // epilogue leader's verdict
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nt = blockIdx.x, grp = blockIdx.y, ngrp = gridDim.y;
+  const int ntile_rows = (rows + 127) / 128;
+  if (tid == 0) {
+    mbar_init(bar_w, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&full_a[i], 1);
+      mbar_init(&empty_a[i], 1);
+      mbar_init(&mma_done[i], 1);
+      mbar_init(&tmem_empty[i], 1);
+    }
+    fence_mbar_init();
+    mbar_arrive_expect_tx(bar_w, KB * NT * 128 + NT * 4);
+  }
+  __syncwarp();
+  if (warp == 0) {  // weights and bias before the wait, one copy per lane
+    if (lane < KB)
+      bulk_g2s(sB + lane * NT * 128, w.wada + ((size_t)nt * KB + lane) * NT * 64, NT * 128, bar_w);
+    else if (lane == KB)
+      bulk_g2s(sbias, w.ada_b + nt * NT, NT * 4, bar_w);
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  griddep_wait();
+  griddep_launch();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp == 0) {  // producer: operand of tile i into buffer i & 1
+    for (int i = 0;; ++i) {
+      const int t = grp + i * ngrp;
+      if (t >= ntile_rows) break;
+      const int bi = i & 1;
+      if (i >= 2 && !__all_sync(0xffffffffu, mbar_wait(&empty_a[bi], ((i >> 1) - 1) & 1, status))) break;
+      if (lane == 0) mbar_arrive_expect_tx(&full_a[bi], KB * kBlk);
+      __syncwarp();
+      if (lane < KB)
+        bulk_g2s(sA + (bi * KB + lane) * kBlk, act_a + ((size_t)t * KB + lane) * kBlkElems, kBlk, &full_a[bi]);
+      __syncwarp();
+    }
+  } else if (warp == 1) {  // MMA issuer: tile i into accumulator i & 1 (TMEM columns 256 (i & 1) ..)
+    const uint32_t idesc = idesc_bf16(128, NT);
+    bool ok = __all_sync(0xffffffffu, mbar_wait(bar_w, 0, status));
+    for (int i = 0; ok; ++i) {
+      const int t = grp + i * ngrp;
+      if (t >= ntile_rows) break;
+      const int bi = i & 1;
+      if (i >= 2 && !__all_sync(0xffffffffu, mbar_wait(&tmem_empty[bi], ((i >> 1) - 1) & 1, status))) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full_a[bi], (i >> 1) & 1, status))) break;
+      tc_fence_after();
+      if (lane == 0) {
+        umma_tile(tmem + bi * 256, smem_u32(sA + bi * KB * kBlk), kBlk, smem_u32(sB), NT * 128, 0, KB, idesc, false);
+        umma_commit(&mma_done[bi]);
+        umma_commit(&empty_a[bi]);
+      }
+      __syncwarp();
+    }
+  } else if (warp >= 4) {  // epilogue: 12 warps, warp (quad, slice) = 32 rows x CWE columns
+    const int e = tid - 128;
+    const int quad = warp & 3, slice = (warp - 4) >> 2;
+    const int r = quad * 32 + lane;
+    const int ncols = md.L * 6 * D;
+    for (int i = 0;; ++i) {
+      const int t = grp + i * ngrp;
+      if (t >= ntile_rows) break;
+      const int bi = i & 1;
+      if (e == 0) {
+        const bool ok = (i > 0 || mbar_wait(bar_w, 0, status)) && mbar_wait(&mma_done[bi], (i >> 1) & 1, status);
+        *eflag = ok ? 1u : 0u;
+      }
+      if (warp < 8) bulk_wait_read();  // the previous tile's copies have read the staged rows
+      named_bar(1, 384);
+      if (*eflag == 0u) break;
+      tc_fence_after();
+      float v[CWE];
+      tmem_ld_cols<CWE>(tmem + bi * 256 + ((uint32_t)(quad * 32) << 16) + slice * CWE, v);
+      tc_fence_before();
+      const float* bs = sbias + slice * CWE;
+      uint4* sr = reinterpret_cast<uint4*>(stg + r * SROW + slice * CWE * 2);
+#pragma unroll
+      for (int k = 0; k < CWE / 8; ++k) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+          pk[m] = pack_bf16x2(v[8 * k + 2 * m] + bs[8 * k + 2 * m], v[8 * k + 2 * m + 1] + bs[8 * k + 2 * m + 1]);
+        sr[k] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+      fence_async_smem();
+      named_bar(1, 384);
+      if (e == 0) mbar_arrive(&tmem_empty[bi]);  // every thread's loads of accumulator bi completed
+      if (warp < 8) {  // warps 4-7: lane copies row 32 quad + lane of the tile
+        const int row = t * 128 + r;
+        if (row < rows) bulk_s2g(mod + (size_t)row * ncols + nt * NT, stg + r * SROW, NT * 2);
+        bulk_commit();
+      }
+    }
+    if (warp < 8) bulk_wait_read();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
 // ---------------------------------------------------------------- GEMM operand from the residual
 // A operand of the QKV / FC1 GEMM, built in shared memory from the fp32 residual rows:
 // bf16(LN_{g,b}(LN(x) * (1 + scale) + shift)) with the first LayerNorm at eps 1e-6 and
@@ -1630,6 +1776,7 @@ static_assert(smem_qkv<192>() <= 232448 && smem_qkv<384>() <= 232448, "qkv smem"
 static_assert(smem_embed_out<384>() <= 232448 && smem_adaln<384>() <= 232448, "embed/adaln smem");
 static_assert(smem_fc1<384, kFc1N>() <= 232448 && smem_resid<384>() <= 232448, "fc smem");
 static_assert(smem_ffn<192>() <= 232448, "ffn smem");
+static_assert(smem_adaln_ps<192>() <= 232448, "persistent adaln smem");
 
 template <int D>
 cudaError_t set_smem_attrs() {
@@ -1640,8 +1787,11 @@ cudaError_t set_smem_attrs() {
     return e;
   if ((e = cudaFuncSetAttribute(k_adaln<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_adaln<D>()))) return e;
   if ((e = cudaFuncSetAttribute(k_qkv_attn<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_qkv<D>()))) return e;
-  if constexpr (D == 192)
+  if constexpr (D == 192) {
     if ((e = cudaFuncSetAttribute(k_ffn<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_ffn<D>()))) return e;
+    if ((e = cudaFuncSetAttribute(k_adaln_ps<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_adaln_ps<D>())))
+      return e;
+  }
   if constexpr (D == 192)
     if ((e = cudaFuncSetAttribute(k_partial_gemm<D, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   smem_resid<D>())))
@@ -1679,7 +1829,21 @@ cudaError_t adaln_impl(const ModelDims& md, const DevWeights& w, int rows, const
   const int tiles = (rows + 127) / 128;
   const int ntiles = md.L * 6 * D / Cfg<D>::NT_ADA;
   if (prof) prof->begin(st);
-  e = launch_k(k_adaln<D>, dim3(tiles, ntiles), dim3(kThreads), smem_adaln<D>(), st, w, md, rows, act_a, mod, status);
+  // Calls with at least 4 row tiles per CTA group run the persistent pipeline (the same bits).
+  static const int ps_env = [] {
+    const char* v = std::getenv("LEWM_ADALN_PERSISTENT");
+    return v ? std::atoi(v) : 1;
+  }();
+  bool ps = false;
+  if constexpr (D == 192) {
+    ps = ps_env != 0 && tiles >= 4 * kAdaGroups;
+    if (ps)
+      e = launch_k(k_adaln_ps<D>, dim3(ntiles, kAdaGroups), dim3(kThreads), smem_adaln_ps<D>(), st, w, md, rows,
+                   act_a, mod, status);
+  }
+  if (!ps)
+    e = launch_k(k_adaln<D>, dim3(tiles, ntiles), dim3(kThreads), smem_adaln<D>(), st, w, md, rows, act_a, mod,
+                 status);
   if (prof) prof->end(KC_ADALN, 2.0 * rows * (double)D * md.L * 6 * D, st);
   return e;
 }
