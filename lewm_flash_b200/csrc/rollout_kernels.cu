@@ -40,6 +40,8 @@
 //     move their K blocks in as few instruction rounds as shared memory allows.
 #include <algorithm>
 
+#include <cuda.h>  // CUtensorMap (tiled TMA store of the AdaLN output)
+
 #include "lewm_common.cuh"
 #include "lewm_internal.h"
 
@@ -456,7 +458,9 @@ __global__ void __launch_bounds__(kThreads) k_adaln(DevWeights w, ModelDims md, 
 // row tiles through a pipeline, so the tensor pipe works on tile i + 1 while the epilogue
 // drains tile i. Warp 0 streams the tiles' operands into two buffers, warp 1 issues each
 // tile's 12 MMAs into one of two TMEM accumulators, warps 4-15 apply the bias, convert to
-// bf16, stage the rows and bulk-copy them to mod. Hand-offs are mbarriers: full_a (operand
+// bf16 and stage the tile as three 128-byte-swizzled [128 x 64] blocks, which one thread
+// writes to mod with three tiled TMA stores (the tensor map clips rows past the end; 384-byte
+// bulk copies per row cost ~2x more per tile). Hand-offs are mbarriers: full_a (operand
 // landed), empty_a and mma_done (the tile's MMAs retired), tmem_empty (the epilogue read the
 // accumulator). Every wait is bounded; after a timeout every role stops at its next wait,
 // and the epilogue's decisions come from one thread through shared memory, so its named
@@ -466,25 +470,25 @@ constexpr int kAdaGroups = 4;  // row-tile groups per N tile (36 N tiles x 4 = 1
 template <int D>
 constexpr int smem_adaln_ps() {
   constexpr int NT = Cfg<D>::NT_ADA;
-  return 1024 + Cfg<D>::KB * NT * 128 + 2 * Cfg<D>::KB * kBlk + 128 * (NT * 2 + 16) + NT * 4 + 8 * 9 + 16;
+  return 1024 + Cfg<D>::KB * NT * 128 + 2 * Cfg<D>::KB * kBlk + (NT / 64) * kBlk + NT * 4 + 8 * 9 + 16;
 }
 
 template <int D>
 __global__ void __launch_bounds__(kThreads) k_adaln_ps(DevWeights w, ModelDims md, int rows,
                                                        const __nv_bfloat16* __restrict__ act_a,
-                                                       __nv_bfloat16* __restrict__ mod, uint32_t* status) {
+                                                       const __grid_constant__ CUtensorMap mod_map,
+                                                       uint32_t* status) {
   using C = Cfg<D>;
   constexpr int NT = C::NT_ADA;
   constexpr int KB = C::KB;
-  constexpr int SROW = NT * 2 + 16;  // staged row bytes (16-byte stores of 8 consecutive rows hit distinct banks)
   constexpr int CWE = NT / 3;        // columns per epilogue warp (3 warps per TMEM lane quadrant)
-  static_assert(NT == 192 && CWE % 8 == 0, "width 192");
+  static_assert(NT == 192 && CWE == 64, "width 192: one staged 64-column block per epilogue warp");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sB = smem;                                  // weights of this N tile, [KB][NT x 64]
   uint8_t* sA = sB + KB * NT * 128;                    // two operand buffers, [2][KB][128 x 64]
-  uint8_t* stg = sA + 2 * KB * kBlk;                   // staged output rows, [128][SROW]
-  float* sbias = reinterpret_cast<float*>(stg + 128 * SROW);
+  uint8_t* stg = sA + 2 * KB * kBlk;                   // staged output tile, [NT/64][128 x 64] SW128
+  float* sbias = reinterpret_cast<float*>(stg + (NT / 64) * kBlk);
   uint64_t* bar_w = reinterpret_cast<uint64_t*>(sbias + NT);
   uint64_t* full_a = bar_w + 1;      // [2]
   uint64_t* empty_a = full_a + 2;    // [2]
@@ -554,7 +558,6 @@ __global__ void __launch_bounds__(kThreads) k_adaln_ps(DevWeights w, ModelDims m
     const int e = tid - 128;
     const int quad = warp & 3, slice = (warp - 4) >> 2;
     const int r = quad * 32 + lane;
-    const int ncols = md.L * 6 * D;
     for (int i = 0;; ++i) {
       const int t = grp + i * ngrp;
       if (t >= ntile_rows) break;
@@ -563,7 +566,7 @@ __global__ void __launch_bounds__(kThreads) k_adaln_ps(DevWeights w, ModelDims m
         const bool ok = (i > 0 || mbar_wait(bar_w, 0, status)) && mbar_wait(&mma_done[bi], (i >> 1) & 1, status);
         *eflag = ok ? 1u : 0u;
       }
-      if (warp < 8) bulk_wait_read();  // the previous tile's copies have read the staged rows
+      if (e == 0) bulk_wait_read();  // the previous tile's stores have read the staged blocks
       named_bar(1, 384);
       if (*eflag == 0u) break;
       tc_fence_after();
@@ -571,25 +574,29 @@ __global__ void __launch_bounds__(kThreads) k_adaln_ps(DevWeights w, ModelDims m
       tmem_ld_cols<CWE>(tmem + bi * 256 + ((uint32_t)(quad * 32) << 16) + slice * CWE, v);
       tc_fence_before();
       const float* bs = sbias + slice * CWE;
-      uint4* sr = reinterpret_cast<uint4*>(stg + r * SROW + slice * CWE * 2);
+      uint8_t* blk = stg + slice * kBlk;  // this warp's 64 columns: one swizzled block
 #pragma unroll
       for (int k = 0; k < CWE / 8; ++k) {
         uint32_t pk[4];
 #pragma unroll
         for (int m = 0; m < 4; ++m)
           pk[m] = pack_bf16x2(v[8 * k + 2 * m] + bs[8 * k + 2 * m], v[8 * k + 2 * m + 1] + bs[8 * k + 2 * m + 1]);
-        sr[k] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(blk + sw128_off(r, 8 * k)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       fence_async_smem();
       named_bar(1, 384);
-      if (e == 0) mbar_arrive(&tmem_empty[bi]);  // every thread's loads of accumulator bi completed
-      if (warp < 8) {  // warps 4-7: lane copies row 32 quad + lane of the tile
-        const int row = t * 128 + r;
-        if (row < rows) bulk_s2g(mod + (size_t)row * ncols + nt * NT, stg + r * SROW, NT * 2);
+      if (e == 0) {
+        mbar_arrive(&tmem_empty[bi]);  // every thread's loads of accumulator bi completed
+#pragma unroll
+        for (int j = 0; j < NT / 64; ++j)  // x: column (a multiple of 64), y: first row of the tile
+          asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                           reinterpret_cast<uint64_t>(&mod_map)),
+                       "r"(nt * NT + 64 * j), "r"(t * 128), "r"(smem_u32(stg + j * kBlk))
+                       : "memory");
         bulk_commit();
       }
     }
-    if (warp < 8) bulk_wait_read();
+    if (e == 0) bulk_wait_read();
   }
   tc_fence_before();
   __syncthreads();
@@ -1821,6 +1828,32 @@ cudaError_t embed_impl(const ModelDims& md, const DevWeights& w, const float* ca
   return e;
 }
 
+// Tensor map of mod ([rows][ncols] bf16, row-major) for 128-byte-swizzled [128 x 64] TMA
+// stores. cuTensorMapEncodeTiled comes from the driver through the runtime's entry-point
+// query (no link against libcuda). False when it is unavailable or rejects the map: the
+// caller then uses the one-tile kernel.
+bool mod_tensor_map(CUtensorMap* map, void* mod, int rows, int ncols) {
+  using Encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static Encode encode = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      fn = nullptr;
+    return reinterpret_cast<Encode>(fn);
+  }();
+  if (!encode || rows <= 0) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)ncols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ncols * 2};
+  const cuuint32_t box[2] = {64, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, mod, dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int D>
 cudaError_t adaln_impl(const ModelDims& md, const DevWeights& w, int rows, const __nv_bfloat16* act_a,
                        __nv_bfloat16* mod, uint32_t* status, cudaStream_t st, Prof* prof) {
@@ -1836,10 +1869,11 @@ cudaError_t adaln_impl(const ModelDims& md, const DevWeights& w, int rows, const
   }();
   bool ps = false;
   if constexpr (D == 192) {
-    ps = ps_env != 0 && tiles >= 4 * kAdaGroups;
+    CUtensorMap map;
+    ps = ps_env != 0 && tiles >= 4 * kAdaGroups && mod_tensor_map(&map, mod, rows, md.L * 6 * D);
     if (ps)
       e = launch_k(k_adaln_ps<D>, dim3(ntiles, kAdaGroups), dim3(kThreads), smem_adaln_ps<D>(), st, w, md, rows,
-                   act_a, mod, status);
+                   act_a, map, status);
   }
   if (!ps)
     e = launch_k(k_adaln<D>, dim3(tiles, ntiles), dim3(kThreads), smem_adaln<D>(), st, w, md, rows, act_a, mod,
