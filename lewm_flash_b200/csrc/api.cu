@@ -497,8 +497,33 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
     // at the tensor pipe's peak rate, N = 48 on its per-instruction floor). Same K order
     // per output element either way, so the same bits.
     const int outproj_wide = (m.D == 192 && nt * 2 >= c->sm_count) ? 1 : 0;
-    CallGeom g{NC,        S, T, H, w, start, cpt, nt, rows8, ln_prebuilt, ffn_fused,
-               fc2_parts, outproj_wide, k, k == n_calls - 1, 1, 0, 128};
+    CallGeom g{};  // fields by name: a field added to CallGeom cannot shift the others
+    g.n_cand = NC;
+    g.S = S;
+    g.T = T;
+    g.H = H;
+    g.w = w;
+    g.start = start;
+    g.cpt = cpt;
+    g.n_tiles = nt;
+    g.rows8 = rows8;
+    g.ln_prebuilt = ln_prebuilt;
+    g.ffn_fused = ffn_fused;
+    g.fc2_parts = fc2_parts;
+    g.outproj_wide = outproj_wide;
+    g.call = k;
+    g.last = k == n_calls - 1 ? 1 : 0;
+    g.next_w = 1;
+    g.next_start = 0;
+    g.next_cpt = 128;
+    // QKV + attention by head-resident CTAs (16 heads x kQkvGroups tile groups) once the
+    // operands are prebuilt and every group has at least 4 tiles; LEWM_QKV_PERSISTENT=0 keeps
+    // one CTA per (tile, head) everywhere.
+    static const int qkv_env = [] {
+      const char* v = std::getenv("LEWM_QKV_PERSISTENT");
+      return v ? std::atoi(v) : 1;
+    }();
+    g.qkv_persistent = (qkv_env != 0 && m.D == 192 && m.heads == 16 && ln_prebuilt && nt >= 4 * kQkvGroups) ? 1 : 0;
     g.rpc = rpc;
     g.pos0 = w - rpc;
     g.kv_read = kv_read ? 1 : 0;

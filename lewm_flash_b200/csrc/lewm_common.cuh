@@ -73,9 +73,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
 // CTA barrier instead of polling the mbarrier, whose shared-memory word the tensor
 // core's operand reads would otherwise share with hundreds of pollers. `flag` is a
 // spare shared word that carries warp 0's result.
-__device__ __forceinline__ bool cta_wait_mma(uint64_t* bar, uint32_t* status, uint32_t* flag) {
+__device__ __forceinline__ bool cta_wait_mma(uint64_t* bar, uint32_t* status, uint32_t* flag,
+                                             uint32_t parity = 0) {
   if (threadIdx.x < 32) {
-    const bool ok = mbar_wait(bar, 0, status);
+    const bool ok = mbar_wait(bar, parity, status);
     if (threadIdx.x == 0) *flag = ok ? 1u : 0u;
   }
   __syncthreads();

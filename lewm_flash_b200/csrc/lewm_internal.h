@@ -67,6 +67,9 @@ struct ModelDims {
 };
 
 // One predictor call of the rollout over every candidate.
+// Tile groups per head of the persistent QKV + attention kernel (16 heads x 9 = 144 CTAs).
+constexpr int kQkvGroups = 9;
+
 struct CallGeom {
   int n_cand;   // candidates in flight (envs * samples)
   int S;        // samples per env (candidate -> env mapping)
@@ -81,6 +84,7 @@ struct CallGeom {
   int fc2_parts;    // K parts of FC2's partial sums (4 hidden quarters at D 192 / MLP 768, else 2),
                     // the same on both FFN paths so a row's result does not depend on the batch
   int outproj_wide; // 1: out-proj CTAs compute all D columns (N = D) of one K half
+  int qkv_persistent;  // 1: QKV + attention by head-resident CTAs looping over prebuilt tiles
   int call;     // prediction slot written by this call
   int last;     // 1: final call, write costs
   // Window of the next call (k_final prepares its layer-0 inputs); unused when last.

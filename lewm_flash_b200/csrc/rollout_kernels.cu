@@ -899,121 +899,14 @@ __global__ void __launch_bounds__(128) k_prep0(DevWeights w, ModelDims md, CallG
 }
 
 // ---------------------------------------------------------------- QKV + attention
+// Attention epilogue of one (row tile, head) of k_qkv_attn / k_qkv_attn_ps: q, k, v in TMEM
+// columns [0, 192) of `tmem`; the head's output block is staged in sO and bulk-stored to
+// b.attn (thread 0 waits until the copy has read sO). `kv` / `spart` / `sO` are shared scratch.
 template <int D>
-__global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b,
-                                                       int layer, uint32_t* status) {
-  using C = Cfg<D>;
-  constexpr int KB = C::KB;
-  constexpr int ST = C::QKV_ST;
-  constexpr int B_BLK = 192 * 128;
-  constexpr int R1 = KB * kBlk + ST * B_BLK;
-  constexpr int SCR = 128 * kKVStride * 4 + 4 * kMaxWindow * 128 * 4;
-  constexpr int R1S = ((R1 > SCR ? R1 : SCR) + 1023) & ~1023;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = align1024(smem_raw);
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + KB * kBlk;
-  float* kv = reinterpret_cast<float*>(smem);   // [128][kKVStride], aliases sA/sB after the MMA
-  float* spart = kv + 128 * kKVStride;           // [4 parts][kMaxWindow][128] partial scores
-  // The output block also lives in the operand region when it fits after the scratch.
-  constexpr int SO_OFF = (((SCR + 1023) & ~1023) + kBlk <= R1) ? ((SCR + 1023) & ~1023) : R1S;
-  constexpr int BAR_OFF = (SO_OFF + kBlk > R1S) ? SO_OFF + kBlk : R1S;
-  uint8_t* sO = smem + SO_OFF;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
-  uint64_t* empty = full + ST;
-  uint64_t* bar_mma = empty + ST;
-  uint64_t* bar_a = bar_mma + 1;  // [KB], operand bulk copies when prebuilt
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + KB);
-
+__device__ __forceinline__ void qkv_attn_epilogue(const ModelDims& md, const CallGeom& g, const RolloutBufs& b,
+                                                  int layer, int head, int tile, uint32_t tmem, bool ok,
+                                                  float* kv, float* spart, uint8_t* sO) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int tile = blockIdx.x, head = blockIdx.y;
-  const __nv_bfloat16* wq = w.qkv + (size_t)((layer * md.heads + head) * KB) * (192 * 64);
-
-  if (tid == 0) {
-    for (int s = 0; s < ST; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    mbar_init(bar_mma, 1);
-    for (int kb = 0; kb < KB; ++kb) mbar_init(&bar_a[kb], 1);
-    fence_mbar_init();
-  }
-  __syncwarp();
-  if (warp == 0 && lane < ST) {  // one copy per lane
-    mbar_arrive_expect_tx(&full[lane], B_BLK);
-    bulk_g2s(sB + lane * B_BLK, wq + (size_t)lane * 192 * 64, B_BLK, &full[lane]);
-  }
-  if (warp == 0) {
-    tmem_alloc(tmem_slot, 256);
-    tmem_relinquish();
-  }
-  // A operand: LN1 -> modulate (shift/scale_msa of this layer) -> attn.norm of the residual
-  // rows. After layer 0 the previous layer's FC2 update is still pending: r = s + gate_mlp *
-  // (sum of the FC2 partials + b2); the head-0 CTAs write r back for this layer's FC1. The
-  // modulation rows are loaded before the wait (the residual rows come from the kernel
-  // just before this one).
-  const size_t t0 = (size_t)tile * 128 * D;
-  ResidUpdate u{b.x + t0, nullptr, 0, 2, nullptr, 0, nullptr};
-  if (layer > 0)
-    u = ResidUpdate{b.xs + t0, b.part_b + t0, b.part_stride, g.fc2_parts, w.b2 + (layer - 1) * D,
-                    (layer - 1) * 6 * D + 5 * D, head == 0 ? b.x + t0 : nullptr};
-  LnEarly<D, D / 12> pf;
-  if (!g.ln_prebuilt)
-    prefetch_ln_operand<D>(pf, u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D, tid, 0, g.rows8, false);
-  LEWM_STAMP(2, 1);
-  griddep_wait();
-  LEWM_STAMP(2, 2);
-  griddep_launch();
-  if (g.ln_prebuilt) {  // built once per tile by k_ln_operand: one copy per lane
-    if (warp == 0 && lane < KB) {
-      mbar_arrive_expect_tx(&bar_a[lane], g.rows8 * 128);
-      bulk_g2s(sA + lane * kBlk, b.a_op + ((size_t)tile * KB + lane) * kBlkElems, g.rows8 * 128, &bar_a[lane]);
-    }
-  } else {
-    build_ln_operand<D, 6>(u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D, w.attn_ln_w + layer * D,
-                           w.attn_ln_b + layer * D, sA, tid, &pf);
-  }
-  fence_async_smem();
-  LEWM_STAMP(2, 5);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  if (warp == 0) {  // whole warp waits, lane 0 issues
-    const uint32_t idesc = idesc_bf16(128, 192);
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % ST;
-      if (!__all_sync(0xffffffffu, (!g.ln_prebuilt || mbar_wait(&bar_a[kb], 0, status)) &&
-                                       mbar_wait(&full[s], (kb / ST) & 1, status)))
-        break;
-      tc_fence_after();
-      if (lane == 0) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint64_t ad = sdesc_sw128(smem_u32(sA) + kb * kBlk + j * 32);
-          const uint64_t bd = sdesc_sw128(smem_u32(sB) + s * B_BLK + j * 32);
-          umma_bf16(tmem, ad, bd, idesc, (kb | j) ? 1u : 0u);
-        }
-        umma_commit(&empty[s]);
-      }
-      __syncwarp();
-      if (kb + ST < KB) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], (kb / ST) & 1, status))) break;
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&full[s], B_BLK);
-          bulk_g2s(sB + s * B_BLK, wq + (size_t)(kb + ST) * 192 * 64, B_BLK, &full[s]);
-        }
-        __syncwarp();
-      }
-    }
-    LEWM_STAMP(2, 3);
-    if (lane == 0) umma_commit(bar_mma);
-    __syncwarp();
-  }
-  const bool ok = cta_wait_mma(bar_mma, status, tmem_slot + 1);
-  LEWM_STAMP(2, 4);
-  __syncwarp();
-  tc_fence_after();
   // Causal softmax(q k^T / 8) v within the candidate's window. Thread (warp w, lane l)
   // owns window row r = 32 (w & 3) + l, its TMEM lane, and head-dim part p = w >> 2:
   // dims [8p, 8p + 8) and [32 + 8p, 40 + 8p) of q, k and v, read straight from TMEM.
@@ -1150,8 +1043,219 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
     bulk_commit();
     bulk_wait_read();
   }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b,
+                                                       int layer, uint32_t* status) {
+  using C = Cfg<D>;
+  constexpr int KB = C::KB;
+  constexpr int ST = C::QKV_ST;
+  constexpr int B_BLK = 192 * 128;
+  constexpr int R1 = KB * kBlk + ST * B_BLK;
+  constexpr int SCR = 128 * kKVStride * 4 + 4 * kMaxWindow * 128 * 4;
+  constexpr int R1S = ((R1 > SCR ? R1 : SCR) + 1023) & ~1023;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + KB * kBlk;
+  float* kv = reinterpret_cast<float*>(smem);   // [128][kKVStride], aliases sA/sB after the MMA
+  float* spart = kv + 128 * kKVStride;           // [4 parts][kMaxWindow][128] partial scores
+  // The output block also lives in the operand region when it fits after the scratch.
+  constexpr int SO_OFF = (((SCR + 1023) & ~1023) + kBlk <= R1) ? ((SCR + 1023) & ~1023) : R1S;
+  constexpr int BAR_OFF = (SO_OFF + kBlk > R1S) ? SO_OFF + kBlk : R1S;
+  uint8_t* sO = smem + SO_OFF;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
+  uint64_t* empty = full + ST;
+  uint64_t* bar_mma = empty + ST;
+  uint64_t* bar_a = bar_mma + 1;  // [KB], operand bulk copies when prebuilt
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_a + KB);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x, head = blockIdx.y;
+  const __nv_bfloat16* wq = w.qkv + (size_t)((layer * md.heads + head) * KB) * (192 * 64);
+
+  if (tid == 0) {
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(bar_mma, 1);
+    for (int kb = 0; kb < KB; ++kb) mbar_init(&bar_a[kb], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (warp == 0 && lane < ST) {  // one copy per lane
+    mbar_arrive_expect_tx(&full[lane], B_BLK);
+    bulk_g2s(sB + lane * B_BLK, wq + (size_t)lane * 192 * 64, B_BLK, &full[lane]);
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  // A operand: LN1 -> modulate (shift/scale_msa of this layer) -> attn.norm of the residual
+  // rows. After layer 0 the previous layer's FC2 update is still pending: r = s + gate_mlp *
+  // (sum of the FC2 partials + b2); the head-0 CTAs write r back for this layer's FC1. The
+  // modulation rows are loaded before the wait (the residual rows come from the kernel
+  // just before this one).
+  const size_t t0 = (size_t)tile * 128 * D;
+  ResidUpdate u{b.x + t0, nullptr, 0, 2, nullptr, 0, nullptr};
+  if (layer > 0)
+    u = ResidUpdate{b.xs + t0, b.part_b + t0, b.part_stride, g.fc2_parts, w.b2 + (layer - 1) * D,
+                    (layer - 1) * 6 * D + 5 * D, head == 0 ? b.x + t0 : nullptr};
+  LnEarly<D, D / 12> pf;
+  if (!g.ln_prebuilt)
+    prefetch_ln_operand<D>(pf, u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D, tid, 0, g.rows8, false);
+  LEWM_STAMP(2, 1);
+  griddep_wait();
+  LEWM_STAMP(2, 2);
+  griddep_launch();
+  if (g.ln_prebuilt) {  // built once per tile by k_ln_operand: one copy per lane
+    if (warp == 0 && lane < KB) {
+      mbar_arrive_expect_tx(&bar_a[lane], g.rows8 * 128);
+      bulk_g2s(sA + lane * kBlk, b.a_op + ((size_t)tile * KB + lane) * kBlkElems, g.rows8 * 128, &bar_a[lane]);
+    }
+  } else {
+    build_ln_operand<D, 6>(u, g, tile, b.mod, md.L * 6 * D, layer * 6 * D, w.attn_ln_w + layer * D,
+                           w.attn_ln_b + layer * D, sA, tid, &pf);
+  }
+  fence_async_smem();
+  LEWM_STAMP(2, 5);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp == 0) {  // whole warp waits, lane 0 issues
+    const uint32_t idesc = idesc_bf16(128, 192);
+    for (int kb = 0; kb < KB; ++kb) {
+      const int s = kb % ST;
+      if (!__all_sync(0xffffffffu, (!g.ln_prebuilt || mbar_wait(&bar_a[kb], 0, status)) &&
+                                       mbar_wait(&full[s], (kb / ST) & 1, status)))
+        break;
+      tc_fence_after();
+      if (lane == 0) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t ad = sdesc_sw128(smem_u32(sA) + kb * kBlk + j * 32);
+          const uint64_t bd = sdesc_sw128(smem_u32(sB) + s * B_BLK + j * 32);
+          umma_bf16(tmem, ad, bd, idesc, (kb | j) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      __syncwarp();
+      if (kb + ST < KB) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], (kb / ST) & 1, status))) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[s], B_BLK);
+          bulk_g2s(sB + s * B_BLK, wq + (size_t)(kb + ST) * 192 * 64, B_BLK, &full[s]);
+        }
+        __syncwarp();
+      }
+    }
+    LEWM_STAMP(2, 3);
+    if (lane == 0) umma_commit(bar_mma);
+    __syncwarp();
+  }
+  const bool ok = cta_wait_mma(bar_mma, status, tmem_slot + 1);
+  LEWM_STAMP(2, 4);
+  __syncwarp();
+  tc_fence_after();
+  qkv_attn_epilogue<D>(md, g, b, layer, head, tile, tmem, ok, kv, spart, sO);
   LEWM_STAMP(2, 6);
   __syncwarp();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ---------------------------------------------------------------- QKV + attention, persistent
+// k_qkv_attn for calls with many row tiles whose operands k_ln_operand prebuilt (width
+// 192): one CTA per (head, tile group) keeps the head's QKV weights in shared memory for
+// the whole launch (the one-tile kernel reloads 72 KB per tile) and loops over its tiles;
+// as soon as a tile's MMAs retire it issues the next tile's operand copy, which lands
+// during the attention epilogue. The k / v scratch has its own space instead of aliasing
+// the operand and weights. Per tile the MMAs and the epilogue are those of k_qkv_attn: the
+// same bits. A timed-out wait ends the CTA's loop (the flag comes from one warp through
+// shared memory, so every thread leaves at the same tile).
+template <int D>
+constexpr int smem_qkv_ps() {
+  constexpr int SCR = 128 * kKVStride * 4 + 4 * kMaxWindow * 128 * 4;
+  constexpr int W = Cfg<D>::KB * 192 * 128, A = Cfg<D>::KB * kBlk;
+  return 1024 + W + A + ((SCR + 1023) & ~1023) + kBlk + 8 * 8 + 16;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) k_qkv_attn_ps(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b,
+                                                          int layer, uint32_t* status) {
+  constexpr int KB = Cfg<D>::KB;
+  constexpr int B_BLK = 192 * 128;
+  constexpr int SCR = 128 * kKVStride * 4 + 4 * kMaxWindow * 128 * 4;
+  static_assert(Cfg<D>::QKV_ST == KB, "every weight block resident");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sB = smem;                      // the head's QKV weights, [KB][192 x 64]
+  uint8_t* sA = sB + KB * B_BLK;           // operand of the current tile, [KB][128 x 64]
+  float* kv = reinterpret_cast<float*>(sA + KB * kBlk);  // [128][kKVStride] k | v of the tile's rows
+  float* spart = kv + 128 * kKVStride;                    // [4 parts][kMaxWindow][128] partial scores
+  uint8_t* sO = reinterpret_cast<uint8_t*>(kv) + ((SCR + 1023) & ~1023);  // output block [128 x 64]
+  uint64_t* bar_w = reinterpret_cast<uint64_t*>(sO + kBlk);  // [KB] weights
+  uint64_t* bar_a = bar_w + KB;                               // operand of a tile (one phase per tile)
+  uint64_t* bar_mma = bar_a + 1;                              // MMAs of a tile retired (one phase per tile)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int head = blockIdx.x, grp = blockIdx.y, ngrp = gridDim.y;
+  const __nv_bfloat16* wq = w.qkv + (size_t)((layer * md.heads + head) * KB) * (192 * 64);
+  if (tid == 0) {
+    for (int kb = 0; kb < KB; ++kb) mbar_init(&bar_w[kb], 1);
+    mbar_init(bar_a, 1);
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (warp == 0) {
+    if (lane < KB) {  // weights before the wait, one copy per lane
+      mbar_arrive_expect_tx(&bar_w[lane], B_BLK);
+      bulk_g2s(sB + lane * B_BLK, wq + (size_t)lane * 192 * 64, B_BLK, &bar_w[lane]);
+    }
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  griddep_wait();
+  griddep_launch();
+  auto issue_operand = [&](int t) {  // warp 0: the prebuilt operand of tile t, one copy per lane
+    if (lane == 0) mbar_arrive_expect_tx(bar_a, KB * g.rows8 * 128);
+    __syncwarp();
+    if (lane < KB)
+      bulk_g2s(sA + lane * kBlk, b.a_op + ((size_t)t * KB + lane) * kBlkElems, g.rows8 * 128, bar_a);
+    __syncwarp();
+  };
+  if (warp == 0 && grp < g.n_tiles) issue_operand(grp);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t idesc = idesc_bf16(128, 192);
+  for (int i = 0, t = grp; t < g.n_tiles; ++i, t += ngrp) {
+    if (warp == 0) {  // whole warp waits, lane 0 issues the tile's 4 x KB MMAs
+      bool got = mbar_wait(bar_a, i & 1, status);
+      for (int kb = 0; kb < KB; ++kb) got = got && mbar_wait(&bar_w[kb], 0, status);
+      got = __all_sync(0xffffffffu, got);
+      tc_fence_after();
+      if (lane == 0) {
+        if (got) umma_tile(tmem, smem_u32(sA), kBlk, smem_u32(sB), B_BLK, 0, KB, idesc, false);
+        umma_commit(bar_mma);
+      }
+      __syncwarp();
+    }
+    const bool ok = cta_wait_mma(bar_mma, status, tmem_slot + 1, i & 1);
+    if (!ok) break;  // the same verdict in every thread
+    tc_fence_after();
+    if (warp == 0 && t + ngrp < g.n_tiles) issue_operand(t + ngrp);  // sA is free: the MMAs retired
+    qkv_attn_epilogue<D>(md, g, b, layer, head, t, tmem, ok, kv, spart, sO);
+    tc_fence_before();
+    __syncthreads();  // every TMEM read and shared-scratch use of tile t done before the next MMAs
+    tc_fence_after();
+  }
+  tc_fence_before();
+  __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
@@ -1784,6 +1888,7 @@ static_assert(smem_embed_out<384>() <= 232448 && smem_adaln<384>() <= 232448, "e
 static_assert(smem_fc1<384, kFc1N>() <= 232448 && smem_resid<384>() <= 232448, "fc smem");
 static_assert(smem_ffn<192>() <= 232448, "ffn smem");
 static_assert(smem_adaln_ps<192>() <= 232448, "persistent adaln smem");
+static_assert(smem_qkv_ps<192>() <= 232448, "persistent qkv smem");
 
 template <int D>
 cudaError_t set_smem_attrs() {
@@ -1797,6 +1902,8 @@ cudaError_t set_smem_attrs() {
   if constexpr (D == 192) {
     if ((e = cudaFuncSetAttribute(k_ffn<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_ffn<D>()))) return e;
     if ((e = cudaFuncSetAttribute(k_adaln_ps<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_adaln_ps<D>())))
+      return e;
+    if ((e = cudaFuncSetAttribute(k_qkv_attn_ps<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_qkv_ps<D>())))
       return e;
   }
   if constexpr (D == 192)
@@ -1917,8 +2024,17 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
       if (prof) prof->end(KC_LN_OP, 0.0, st);
     }
     if (prof) prof->begin(st);
-    LEWM_TRY(launch_k(k_qkv_attn<D>, dim3(g.n_tiles, md.heads), dim3(kThreads), smem_qkv<D>(), st, w, md, g, b, l,
-                      status));
+    bool qkv_done = false;
+    if constexpr (D == 192) {
+      if (g.qkv_persistent) {
+        LEWM_TRY(launch_k(k_qkv_attn_ps<D>, dim3(md.heads, kQkvGroups), dim3(kThreads), smem_qkv_ps<D>(), st, w, md,
+                          g, b, l, status));
+        qkv_done = true;
+      }
+    }
+    if (!qkv_done)
+      LEWM_TRY(launch_k(k_qkv_attn<D>, dim3(g.n_tiles, md.heads), dim3(kThreads), smem_qkv<D>(), st, w, md, g, b, l,
+                        status));
     if (prof) prof->end(KC_QKV_ATTN, 2.0 * rows * D * 3 * md.inner + 4.0 * rows * g.w * md.inner, st);
     // out-projection partial sums (bias, gate_msa and residual applied by FC1's operand builder)
     if (prof) prof->begin(st);
