@@ -902,10 +902,12 @@ __global__ void __launch_bounds__(128) k_prep0(DevWeights w, ModelDims md, CallG
 // Attention epilogue of one (row tile, head) of k_qkv_attn / k_qkv_attn_ps: q, k, v in TMEM
 // columns [0, 192) of `tmem`; the head's output block is staged in sO and bulk-stored to
 // b.attn (thread 0 waits until the copy has read sO). `kv` / `spart` / `sO` are shared scratch.
-template <int D>
+// Every thread calls `mid()` once the tile's TMEM reads are done (after the partial scores'
+// CTA barrier): the persistent kernel issues the next tile's MMAs there.
+template <int D, typename Mid>
 __device__ __forceinline__ void qkv_attn_epilogue(const ModelDims& md, const CallGeom& g, const RolloutBufs& b,
                                                   int layer, int head, int tile, uint32_t tmem, bool ok,
-                                                  float* kv, float* spart, uint8_t* sO) {
+                                                  float* kv, float* spart, uint8_t* sO, const Mid& mid) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // Causal softmax(q k^T / 8) v within the candidate's window. Thread (warp w, lane l)
   // owns window row r = 32 (w & 3) + l, its TMEM lane, and head-dim part p = w >> 2:
@@ -979,6 +981,7 @@ __device__ __forceinline__ void qkv_attn_epilogue(const ModelDims& md, const Cal
     }
     __syncthreads();
     LEWM_STAMP(2, 9);
+    mid();
     // One pass of online softmax over the window: running max, denominator and output
     // (exponentials on the special-function unit, __expf: ~2^-21 relative).
     // Window rows before this one come from shared memory, this row from registers.
@@ -1160,7 +1163,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
   LEWM_STAMP(2, 4);
   __syncwarp();
   tc_fence_after();
-  qkv_attn_epilogue<D>(md, g, b, layer, head, tile, tmem, ok, kv, spart, sO);
+  qkv_attn_epilogue<D>(md, g, b, layer, head, tile, tmem, ok, kv, spart, sO, [] {});
   LEWM_STAMP(2, 6);
   __syncwarp();
   if (warp == 0) tmem_dealloc(tmem, 256);
@@ -1171,7 +1174,9 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn(DevWeights w, ModelDims m
 // 192): one CTA per (head, tile group) keeps the head's QKV weights in shared memory for
 // the whole launch (the one-tile kernel reloads 72 KB per tile) and loops over its tiles;
 // as soon as a tile's MMAs retire it issues the next tile's operand copy, which lands
-// during the attention epilogue. The k / v scratch has its own space instead of aliasing
+// during the attention epilogue, and part-way through that epilogue thread 0 issues the
+// next tile's MMAs into the second of two TMEM accumulators, so the tensor pipe works
+// while the epilogue runs. The k / v scratch has its own space instead of aliasing
 // the operand and weights. Per tile the MMAs and the epilogue are those of k_qkv_attn: the
 // same bits. A timed-out wait ends the CTA's loop (the flag comes from one warp through
 // shared memory, so every thread leaves at the same tile).
@@ -1215,7 +1220,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn_ps(DevWeights w, ModelDim
       mbar_arrive_expect_tx(&bar_w[lane], B_BLK);
       bulk_g2s(sB + lane * B_BLK, wq + (size_t)lane * 192 * 64, B_BLK, &bar_w[lane]);
     }
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   griddep_wait();
@@ -1233,30 +1238,32 @@ __global__ void __launch_bounds__(kThreads) k_qkv_attn_ps(DevWeights w, ModelDim
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t idesc = idesc_bf16(128, 192);
+  // Thread 0: the MMAs of the i-th tile of this CTA into accumulator i & 1 (TMEM columns
+  // 256 (i & 1) ..), once its operand landed; commits bar_mma even when a wait gave up.
+  auto issue_mma = [&](int i) {
+    bool got = mbar_wait(bar_a, i & 1, status);
+    for (int kb = 0; kb < KB; ++kb) got = got && mbar_wait(&bar_w[kb], 0, status);
+    tc_fence_after();
+    if (got) umma_tile(tmem + (i & 1) * 256, smem_u32(sA), kBlk, smem_u32(sB), B_BLK, 0, KB, idesc, false);
+    umma_commit(bar_mma);
+  };
+  if (tid == 0 && grp < g.n_tiles) issue_mma(0);
   for (int i = 0, t = grp; t < g.n_tiles; ++i, t += ngrp) {
-    if (warp == 0) {  // whole warp waits, lane 0 issues the tile's 4 x KB MMAs
-      bool got = mbar_wait(bar_a, i & 1, status);
-      for (int kb = 0; kb < KB; ++kb) got = got && mbar_wait(&bar_w[kb], 0, status);
-      got = __all_sync(0xffffffffu, got);
-      tc_fence_after();
-      if (lane == 0) {
-        if (got) umma_tile(tmem, smem_u32(sA), kBlk, smem_u32(sB), B_BLK, 0, KB, idesc, false);
-        umma_commit(bar_mma);
-      }
-      __syncwarp();
-    }
     const bool ok = cta_wait_mma(bar_mma, status, tmem_slot + 1, i & 1);
     if (!ok) break;  // the same verdict in every thread
     tc_fence_after();
-    if (warp == 0 && t + ngrp < g.n_tiles) issue_operand(t + ngrp);  // sA is free: the MMAs retired
-    qkv_attn_epilogue<D>(md, g, b, layer, head, t, tmem, ok, kv, spart, sO);
+    const bool more = t + ngrp < g.n_tiles;
+    if (warp == 0 && more) issue_operand(t + ngrp);  // sA is free: the MMAs retired
+    qkv_attn_epilogue<D>(md, g, b, layer, head, t, tmem + (i & 1) * 256, ok, kv, spart, sO, [&] {
+      if (tid == 0 && more) issue_mma(i + 1);  // accumulator (i + 1) & 1 was drained last iteration
+    });
     tc_fence_before();
     __syncthreads();  // every TMEM read and shared-scratch use of tile t done before the next MMAs
     tc_fence_after();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 256);
+  if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
 // ---------------------------------------------------------------- K-split residual-branch GEMM
