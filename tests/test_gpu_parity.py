@@ -125,12 +125,13 @@ def test_model_cost_per_sample_goal_and_history_window():
         assert rel_err(got, want).max() <= COST_RTOL, hs
 
 
-def test_stress_model_cost_matches_oracle():
+@pytest.mark.parametrize("H", [3, 1])  # history 1: growing windows, key / value cache at width 384
+def test_stress_model_cost_matches_oracle(H):
     desc = STRESS_DESC
     sd = synthetic_state_dict(desc, 5)
     rt = runtime(desc, 5)
     rng = np.random.default_rng(9)
-    emb = rng.standard_normal((2, 3, desc.dim)).astype(np.float32)
+    emb = rng.standard_normal((2, H, desc.dim)).astype(np.float32)
     goal = rng.standard_normal((2, 1, desc.dim)).astype(np.float32)
     cand = rng.standard_normal((2, 20, 10, desc.action_dim)).astype(np.float32)
     want = lo.get_cost_from_embeddings(emb, goal, cand, sd, desc)
