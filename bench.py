@@ -71,28 +71,60 @@ def plan_options():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """SM clocks and clock-event (throttle) reasons sampled while the timed region runs.
+
+    NVML is polled every 10 ms (read-only queries on the device matched by UUID, so the
+    index is right under CUDA_VISIBLE_DEVICES); without NVML, nvidia-smi every 200 ms.
+    """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, uuid: str | None = None):
         self.gpu = gpu_index
-        self.rows = []
+        self.uuid = uuid
+        self.rows = []  # (sm_mhz, max_mhz, {reason: active})
+        self.source = "nvidia-smi"
         self._stop = threading.Event()
+        self._nvml = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = (pynvml.nvmlDeviceGetHandleByUUID(self.uuid) if self.uuid
+                 else pynvml.nvmlDeviceGetHandleByIndex(self.gpu))
+            self._nvml = (pynvml, h)
+            self.source = "nvml"
+        except Exception:
+            self._nvml = None
         self._t = threading.Thread(target=self._run, daemon=True)
 
+    def _sample_nvml(self):
+        nv, h = self._nvml
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        masks = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                 nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+        self.rows.append((float(sm), float(mx), {n: bool(bits & m) for n, m in zip(self.REASONS, masks)}))
+
+    def _sample_smi(self):
+        out = subprocess.run(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                              "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+        for line in out.stdout.strip().splitlines():
+            r = [x.strip() for x in line.split(",")]
+            self.rows.append((float(r[1]), float(r[2]),
+                              {n: v.lower() in ("active", "1", "yes") for n, v in zip(self.REASONS, r[5:9])}))
+
     def _run(self):
+        period = 0.01 if self._nvml else 0.2
         while not self._stop.is_set():
             try:
-                out = subprocess.run(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
-                for line in out.stdout.strip().splitlines():
-                    self.rows.append([x.strip() for x in line.split(",")])
+                self._sample_nvml() if self._nvml else self._sample_smi()
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(period)
 
     def __enter__(self):
         self._t.start()
@@ -103,19 +135,19 @@ class ClockSampler:
         self._t.join(timeout=10)
 
     def summary(self):
-        sms, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            try:
-                sms.append(float(r[1]))
-                mx = float(r[2])
-                for n, v in zip(names, r[5:9]):
-                    if v.strip().lower() in ("active", "1", "yes"):
-                        reasons.add(n)
-            except Exception:
-                continue
-        return {"sm_mhz": percentile(sms, 50) if sms else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sms)}
+        sms = [r[0] for r in self.rows]
+        mx = self.rows[-1][1] if self.rows else None
+        reasons = sorted({n for r in self.rows for n, on in r[2].items() if on})
+        return {"sm_mhz": percentile(sms, 50) if sms else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(sms), "source": self.source}
+
+
+def measured_peak_tflops() -> float:
+    """Dense bf16 TFLOP/s measured on this pool's B200s (burst), else the earlier fallback."""
+    try:
+        return float(json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
+    except Exception:
+        return 1590.0
 
 
 def l2_flush(buf):
@@ -307,6 +339,31 @@ def model_cost_case(S, repeat, envs=1):
     return 0
 
 
+def encoder_case(n_img: int, repeat: int) -> int:
+    """``--encoder N``: N images through the observation encoder, `repeat` times (for ncu)."""
+    import torch
+
+    from lewm_flash_b200.encoder import B200Encoder, EncoderDesc, flat_weights, synthetic_weights
+
+    dev = torch.device("cuda", 0)
+    desc = EncoderDesc()
+    vit, proj = synthetic_weights(desc, 0)
+    enc = B200Encoder(desc, flat_weights(vit, proj, desc), dev)
+    pix = torch.as_tensor(np.random.default_rng(17).standard_normal((n_img, 3, 224, 224), dtype=np.float32),
+                          device=dev)
+    ms = []
+    for _ in range(repeat):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        out = enc.encode_pixels(pix)
+        b.record()
+        enc.sync()
+        ms.append(a.elapsed_time(b))
+    print(json.dumps({"case": "encoder", "images": n_img, "ms": ms, "emb0": float(out[0, 0])}))
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -318,11 +375,16 @@ def main() -> int:
     ap.add_argument("--model-cost", type=int, default=0, metavar="S",
                     help="profiling case: time R model-cost calls of S candidates per env (horizon 5; 1 env "
                          "with history 1, or --envs B with history 3) and exit; no bench line")
+    ap.add_argument("--encoder", type=int, default=0, metavar="N",
+                    help="profiling case: run the observation encoder R times on N 224 px images and exit; "
+                         "no bench line")
     ap.add_argument("--envs", type=int, default=1)
     ap.add_argument("--repeat", type=int, default=3)
     args = ap.parse_args()
     if args.model_cost:
         return model_cost_case(args.model_cost, args.repeat, args.envs)
+    if args.encoder:
+        return encoder_case(args.encoder, args.repeat)
 
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -374,7 +436,7 @@ def main() -> int:
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize(dev)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(local, "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)) as clocks:
         t_all0 = torch.cuda.Event(enable_timing=True)
         t_all1 = torch.cuda.Event(enable_timing=True)
         t_all0.record(stream)
@@ -433,6 +495,9 @@ def main() -> int:
     # ---------------------------------------------------------------- batched planning (64 envs, history 3)
     batched = batched_pass(rt, dev, args.steps, args.warmup, flush)
 
+    # ---------------------------------------------------------------- observation encoder (64 images, 224 px)
+    encoder = encoder_pass(dev, args.steps, args.warmup, flush)
+
     # ---------------------------------------------------------------- per-kernel-class timing pass (diagnostic, last)
     kinfo = kernel_class_pass(rt, opts, emb, goal, mean, std, dev)
     per_plan_launches = kinfo["launches_per_plan"]
@@ -457,6 +522,7 @@ def main() -> int:
         "roofline": kinfo["roofline"],
         "kernel_classes": kinfo["classes"],
         "batched": batched,
+        "encoder": encoder,
         "clocks": clocks.summary(),
     }
     if rank == 0 and not args.no_cpu_baseline:
@@ -504,6 +570,90 @@ def batched_pass(rt, dev, steps, warmup, flush, n_envs=64, history=3):
     return {"workload": f"icem_bucketed_300_{n_envs}env_h{history}_bf16", "envs": n_envs, "history": history,
             "plans_per_s": n_envs / (p50 / 1e3), "p50_call_ms": p50, "calls": n,
             "note": "one plan call solves all envs; per-GPU throughput, device-resident inputs"}
+
+
+def encoder_pass(dev, steps, warmup, flush, n_img=64):
+    """Observation encoder (ViT-tiny 224 px / patch 14, 12 layers, 2048-wide BatchNorm projector)
+    on one observation per env of the 64-env batch: device-timed with resident pixels, end to
+    end from pinned host pixels, and the same modules in eager PyTorch (transformers ViTModel)
+    on the same GPU for comparison."""
+    import torch
+
+    from lewm_flash_b200.encoder import (B200Encoder, EncoderDesc, encoder_flops, encoder_launches, flat_weights,
+                                         synthetic_weights)
+
+    desc = EncoderDesc()
+    vit, proj = synthetic_weights(desc, 0)
+    enc = B200Encoder(desc, flat_weights(vit, proj, desc), dev)
+    rng = np.random.default_rng(17)
+    host = torch.as_tensor(rng.standard_normal((n_img, 3, 224, 224), dtype=np.float32)).pin_memory()
+    pix = host.to(dev)
+    out_host = torch.empty(n_img, desc.proj_out).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(warmup, 1)):
+        enc.encode_pixels(pix)
+    enc.sync()
+    n = max(5, min(steps, 20))
+
+    def timed(fn):
+        ms = []
+        for _ in range(n):
+            l2_flush(flush)
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            ms.append(a.elapsed_time(b))
+        return percentile(ms, 50)
+
+    out = torch.empty(n_img, desc.proj_out, device=dev)
+    dev_ms = timed(lambda: enc.encode_pixels(pix, out))
+
+    def e2e():
+        p = host.to(dev, non_blocking=True)
+        enc.encode_pixels(p, out)
+        out_host.copy_(out, non_blocking=True)
+
+    e2e_ms = timed(e2e)
+    enc.sync()
+    flops = encoder_flops(desc) * n_img
+    peak = measured_peak_tflops()
+    res = {"workload": f"vit_tiny_224_p14_12l_proj2048bn_{n_img}img", "images": n_img,
+           "images_per_s": n_img / (dev_ms / 1e3), "ms_per_batch": dev_ms,
+           "e2e": {"images_per_s": n_img / (e2e_ms / 1e3), "ms_per_batch": e2e_ms,
+                   "h2d_bytes_per_step": int(host.numel() * 4), "d2h_bytes_per_step": int(out_host.numel() * 4)},
+           "roofline": {"bound": "tensor", "achieved": flops / (dev_ms / 1e3) / 1e12, "peak": peak,
+                        "unit": "TFLOP/s", "frac": flops / (dev_ms / 1e3) / 1e12 / peak,
+                        "flops_per_image": encoder_flops(desc)},
+           "gpu_launches_per_batch": encoder_launches(desc), "l2": "256 MiB write between timed batches"}
+    try:  # the same modules in eager PyTorch: transformers ViTModel + Linear/BatchNorm/GELU/Linear
+        import transformers
+
+        cfg = transformers.ViTConfig(hidden_size=192, num_hidden_layers=12, num_attention_heads=3,
+                                     intermediate_size=768, image_size=224, patch_size=14, layer_norm_eps=1e-12)
+        vm = transformers.ViTModel(cfg, add_pooling_layer=False).eval()
+        vm.load_state_dict({k: torch.from_numpy(v) for k, v in vit.items()}, strict=True)
+        pj = torch.nn.Sequential(torch.nn.Linear(192, 2048), torch.nn.BatchNorm1d(2048), torch.nn.GELU(),
+                                 torch.nn.Linear(2048, 192)).eval()
+        pj.load_state_dict({k.replace("net.", ""): torch.from_numpy(v) for k, v in proj.items()}, strict=False)
+        vm, pj = vm.to(dev), pj.to(dev)
+
+        def torch_fwd(autocast):
+            with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast):
+                pj(vm(pix, interpolate_pos_encoding=True).last_hidden_state[:, 0])
+
+        for ac in (False, True):
+            for _ in range(max(warmup, 1)):
+                torch_fwd(ac)
+        res["torch_eager_fp32_ms"] = timed(lambda: torch_fwd(False))
+        res["torch_eager_bf16_autocast_ms"] = timed(lambda: torch_fwd(True))
+        del vm, pj
+    except Exception as exc:  # pragma: no cover - transformers is in the image
+        res["torch_eager"] = f"unavailable: {exc}"
+    del enc
+    return res
 
 
 def kernel_class_pass(rt, opts, emb, goal, mean, std, dev):

@@ -211,6 +211,65 @@ LEWM_API lewm_status lewm_profile_plan(lewm_ctx* ctx, const lewm_plan_desc* plan
  * (LEWM_DEVICE_TIMEOUT if any bounded wait expired since the last call). */
 LEWM_API lewm_status lewm_sync_status(lewm_ctx* ctx, void* stream);
 
+/* ------------------------------------------------------------------ observation encoder
+ * The pixels -> embedding step in front of planning: JEPA.encode
+ * (lewm/jepa.py:88-104), i.e. the CLS row of a transformers ViTModel
+ * (stable-pretraining 0.1.7 `vit_hf`, tools/benchmarks/stage_lewm_weights.py:72-78)
+ * followed by the projector MLP (lewm/module.py:217-240). Reached by the planner
+ * through JEPA._ensure_cost_embeddings (lewm/jepa.py:319-345). */
+typedef struct lewm_encoder lewm_encoder;
+
+/* Supported: hidden == 192 with heads == hidden / 64, image_size a multiple of
+ * patch_size, (image_size / patch_size)^2 + 1 <= 272 tokens, channels x patch^2
+ * <= 2048, mlp_dim a multiple of 192 or 256, proj_hidden a positive multiple of
+ * 256, proj_out == 192. */
+typedef struct lewm_encoder_desc {
+  int32_t image_size;  /* ViTConfig.image_size (224) */
+  int32_t patch_size;  /* ViTConfig.patch_size (14) */
+  int32_t channels;    /* ViTConfig.num_channels (3) */
+  int32_t hidden;      /* ViTConfig.hidden_size (192) */
+  int32_t depth;       /* ViTConfig.num_hidden_layers (12) */
+  int32_t heads;       /* ViTConfig.num_attention_heads (3) */
+  int32_t mlp_dim;     /* ViTConfig.intermediate_size (768) */
+  float ln_eps;        /* ViTConfig.layer_norm_eps (1e-12) */
+  int32_t proj_hidden; /* projector MLP hidden width (2048) */
+  int32_t proj_out;    /* projector output width (192) */
+  int32_t proj_norm;   /* projector norm: 0 none, 1 LayerNorm, 2 BatchNorm1d (eval) */
+  float proj_eps;      /* projector norm eps (1e-5) */
+} lewm_encoder_desc;
+
+/* Float32 values lewm_encoder_create expects (0 for an unsupported desc): the
+ * ViTModel and projector state-dict tensors concatenated in this order, each
+ * row-major:
+ *   embeddings.cls_token, embeddings.position_embeddings,
+ *   embeddings.patch_embeddings.projection.weight, .bias
+ *   for each layer l (encoder.layer.l.): layernorm_before.weight, .bias,
+ *     attention.attention.query.weight, .bias, .key.weight, .bias, .value.weight, .bias,
+ *     attention.output.dense.weight, .bias, layernorm_after.weight, .bias,
+ *     intermediate.dense.weight, .bias, output.dense.weight, .bias
+ *   layernorm.weight, .bias
+ *   projector net.0.weight, .bias; norm (LayerNorm: weight, bias; BatchNorm1d:
+ *     weight, bias, running_mean, running_var; none: nothing); net.3.weight, .bias */
+LEWM_API size_t lewm_encoder_weight_count(const lewm_encoder_desc* desc);
+
+/* Validate `desc`, pack `weights` (HOST float32) into bf16 tensor-core tiles on
+ * `device` (BatchNorm folded into the first projector Linear). Replaces building
+ * and loading the reference encoder + projector (tools/benchmarks/stage_lewm_weights.py:61-103). */
+LEWM_API lewm_status lewm_encoder_create(lewm_encoder** out, const lewm_encoder_desc* desc, const float* weights,
+                                         size_t n_floats, int device);
+
+/* emb_out[n_images][proj_out] = projector(ViT(pixels)[:, 0]) for pixels
+ * [n_images][channels][image_size][image_size] (already normalized, as JEPA.encode
+ * receives them). Device pointers; emb_out 16-byte aligned. Asynchronous on
+ * `stream`; grows the encoder's workspace on first use of a larger batch. */
+LEWM_API lewm_status lewm_encode(lewm_encoder* enc, const float* pixels, int32_t n_images, float* emb_out,
+                                 void* stream);
+
+/* Synchronize `stream`, then read and clear the encoder's device status word. */
+LEWM_API lewm_status lewm_encoder_sync_status(lewm_encoder* enc, void* stream);
+LEWM_API const char* lewm_encoder_last_error(const lewm_encoder* enc);
+LEWM_API void lewm_encoder_destroy(lewm_encoder* enc);
+
 #ifdef __cplusplus
 }
 #endif

@@ -54,6 +54,13 @@ class PlanDescC(C.Structure):
     ]
 
 
+class EncoderDescC(C.Structure):
+    _fields_ = [("image_size", C.c_int32), ("patch_size", C.c_int32), ("channels", C.c_int32),
+                ("hidden", C.c_int32), ("depth", C.c_int32), ("heads", C.c_int32), ("mlp_dim", C.c_int32),
+                ("ln_eps", C.c_float), ("proj_hidden", C.c_int32), ("proj_out", C.c_int32),
+                ("proj_norm", C.c_int32), ("proj_eps", C.c_float)]
+
+
 class PlanTraceC(C.Structure):
     _fields_ = [("costs", C.c_void_p), ("topk_idx", C.c_void_p), ("topk_val", C.c_void_p),
                 ("mean", C.c_void_p), ("std", C.c_void_p), ("candidates", C.c_void_p)]
@@ -85,6 +92,13 @@ SIGNATURES = {
     "lewm_sync_status": (C.c_int, [C.c_void_p, C.c_void_p]),
     "lewm_profile_plan": (C.c_int, [C.c_void_p, C.POINTER(PlanDescC), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "lewm_encoder_weight_count": (C.c_size_t, [C.POINTER(EncoderDescC)]),
+    "lewm_encoder_create": (C.c_int, [C.POINTER(C.c_void_p), C.POINTER(EncoderDescC), C.c_void_p, C.c_size_t,
+                                      C.c_int]),
+    "lewm_encode": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p]),
+    "lewm_encoder_sync_status": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "lewm_encoder_last_error": (C.c_char_p, [C.c_void_p]),
+    "lewm_encoder_destroy": (None, [C.c_void_p]),
 }
 KERNEL_CLASSES = ("embed", "adaln", "qkv_attn", "out_proj", "fc1", "fc2", "final", "sample", "refit", "prep0", "ffn",
                   "ln_operand")
@@ -112,6 +126,17 @@ def check(status: int, ctx=None) -> None:
     if status == 0:
         return
     msg = lib().lewm_last_error(ctx)
+    text = msg.decode() if msg else ""
+    if status == 1:
+        raise LewmInvalidArgument(status, text)
+    raise LewmError(status, text)
+
+
+def check_encoder(status: int, enc=None) -> None:
+    """``check`` for the encoder entry points (their error text lives on the encoder)."""
+    if status == 0:
+        return
+    msg = lib().lewm_encoder_last_error(enc)
     text = msg.decode() if msg else ""
     if status == 1:
         raise LewmInvalidArgument(status, text)

@@ -1,0 +1,961 @@
+// ViT observation encoder + projector on sm_100a: the observation / goal embedding
+// step in front of LeWM planning (reference lewm/jepa.py:88-104, JEPA.encode).
+//
+// The reference encoder is a transformers ViTModel built by stable-pretraining 0.1.7
+// `vit_hf` (reference tools/benchmarks/stage_lewm_weights.py:72-78): patch embedding
+// (Conv2d, stride = kernel = patch), CLS token, learned position embedding, pre-norm
+// encoder layers (LayerNorm eps 1e-12, QKV with bias, softmax attention over all
+// tokens, output dense, GELU MLP), final LayerNorm. JEPA.encode keeps the CLS row of
+// last_hidden_state and applies the projector MLP (reference lewm/module.py:217-240:
+// Linear, LayerNorm / BatchNorm1d / none, GELU, Linear).
+//
+// Rows are (image, token) pairs, 128 to a tile. Every GEMM runs on tcgen05 from
+// K-major SW128 operand blocks and fuses its elementwise tail:
+//   k_vit_patch_op   pixels -> patch operand (CLS rows and K padding are zeros)
+//   k_vit_gemm       C = A . W^T over a ring of K blocks with one of five epilogues:
+//                    PATCH   + bias, CLS / position embedding -> fp32 residual rows
+//                    QKV     + bias, scattered to per-head Q rows, K rows and V^T blocks
+//                    RESID   + bias, added into the fp32 residual rows
+//                    GELU_OP GELU(acc * scale + shift) -> bf16 operand of the next GEMM
+//                    F32     + bias -> fp32 rows
+//   k_vit_ln_op      LayerNorm (+ optional GELU) of fp32 rows -> bf16 operand blocks
+//   k_vit_attn       one CTA per (head, image): S = Q K^T into TMEM, softmax in
+//                    registers, P V on the tensor core, written as the out-proj operand
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "lewm_b200.h"
+#include "lewm_common.cuh"
+
+namespace lewm {
+namespace vit {
+
+constexpr int kD = 192;                // hidden width the kernels are built for (ViT-tiny)
+constexpr int kHB = kD / 64;           // heads (dim_head 64) = K blocks of one hidden row
+constexpr int kMaxTok = 272;           // tokens one attention CTA holds (S in 272 TMEM columns)
+constexpr int kBlk = 128 * 64;         // elements of a [128 x 64] operand block
+constexpr int kBlkBytes = kBlk * 2;
+constexpr int kMaxStages = 4;
+
+enum Epi { EPI_PATCH = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GELU_OP = 3, EPI_F32 = 4 };
+
+struct EpiArgs {
+  float* x;             // PATCH / RESID: fp32 residual rows [rows][kD]; F32: output rows [rows][n_total]
+  const float* bias;    // per output column over all N chunks
+  const float* scale;   // GELU_OP: per-column multiplier (null = 1)
+  const float* pos;     // PATCH: position embedding [tokens][kD]
+  const float* cls;     // PATCH: CLS token [kD]
+  __nv_bfloat16* op;    // GELU_OP: operand blocks [tiles][n_total / 64][128 x 64]
+  __nv_bfloat16* q;     // QKV: [image][head][q_rows x 64] swizzled rows
+  __nv_bfloat16* k;     // QKV: [image][head][kv_rows x 64]
+  __nv_bfloat16* vt;    // QKV: [image][head][kv_rows / 64][64 x 64], row = d, column = key
+  int rows;             // valid rows
+  int tokens;           // tokens per image
+  int n_total;          // output columns over all chunks (GELU_OP, F32)
+  int q_rows, kv_rows;
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+__device__ __forceinline__ uint4 pack8(const float* v) {
+  return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                    pack_bf16x2(v[6], v[7]));
+}
+
+template <int NC>
+constexpr int gemm_stage_bytes() { return kBlkBytes + NC * 128; }
+template <int NC>
+size_t gemm_smem(int stages) { return 1024 + (size_t)stages * gemm_stage_bytes<NC>() + 128; }
+
+// Epilogue of 16 accumulator columns [c0, c0 + 16) of tile row r.
+template <int NC, int EPI>
+__device__ __forceinline__ void gemm_epilogue(const EpiArgs& ea, int tile, int chunk, int r, int c0, float* v) {
+  const int grow = tile * 128 + r;
+  if (grow >= ea.rows) return;
+  const int col = chunk * NC + c0;  // first output column over all chunks
+  if constexpr (EPI == EPI_PATCH) {
+    const int tok = grow % ea.tokens;
+    float* xr = ea.x + (size_t)grow * kD + c0;
+    const float* pr = ea.pos + (size_t)tok * kD + c0;
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      float4 o;
+      const float4 p = *reinterpret_cast<const float4*>(pr + i);
+      if (tok == 0) {
+        const float4 c = *reinterpret_cast<const float4*>(ea.cls + c0 + i);
+        o = make_float4(c.x + p.x, c.y + p.y, c.z + p.z, c.w + p.w);
+      } else {
+        const float4 b = *reinterpret_cast<const float4*>(ea.bias + c0 + i);
+        o = make_float4(v[i] + b.x + p.x, v[i + 1] + b.y + p.y, v[i + 2] + b.z + p.z, v[i + 3] + b.w + p.w);
+      }
+      *reinterpret_cast<float4*>(xr + i) = o;
+    }
+  } else if constexpr (EPI == EPI_RESID) {
+    float* xr = ea.x + (size_t)grow * kD + c0;
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      float4 o = *reinterpret_cast<float4*>(xr + i);
+      const float4 b = *reinterpret_cast<const float4*>(ea.bias + col + i);
+      o.x += v[i] + b.x;
+      o.y += v[i + 1] + b.y;
+      o.z += v[i + 2] + b.z;
+      o.w += v[i + 3] + b.w;
+      *reinterpret_cast<float4*>(xr + i) = o;
+    }
+  } else if constexpr (EPI == EPI_F32) {
+    float* xr = ea.x + (size_t)grow * ea.n_total + col;
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      const float4 b = *reinterpret_cast<const float4*>(ea.bias + col + i);
+      *reinterpret_cast<float4*>(xr + i) = make_float4(v[i] + b.x, v[i + 1] + b.y, v[i + 2] + b.z, v[i + 3] + b.w);
+    }
+  } else if constexpr (EPI == EPI_GELU_OP) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float s = ea.scale ? ea.scale[col + i] : 1.0f;
+      v[i] = gelu_f(fmaf(v[i], s, ea.bias[col + i]));
+    }
+    uint8_t* blk = reinterpret_cast<uint8_t*>(ea.op) + ((size_t)tile * (ea.n_total / 64) + col / 64) * kBlkBytes;
+    *reinterpret_cast<uint4*>(blk + sw128_off(r, col % 64)) = pack8(v);
+    *reinterpret_cast<uint4*>(blk + sw128_off(r, col % 64 + 8)) = pack8(v + 8);
+  } else {  // EPI_QKV: chunk 0 = Q, 1 = K, 2 = V; NC == kD
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] += ea.bias[col + i];
+    const int img = grow / ea.tokens, tok = grow % ea.tokens;
+    const int head = c0 / 64, d0 = c0 % 64;
+    const size_t hi = (size_t)img * kHB + head;
+    if (chunk < 2) {
+      const int nrow = chunk == 0 ? ea.q_rows : ea.kv_rows;
+      uint8_t* base = reinterpret_cast<uint8_t*>(chunk == 0 ? ea.q : ea.k) + hi * nrow * 128;
+      *reinterpret_cast<uint4*>(base + sw128_off(tok, d0)) = pack8(v);
+      *reinterpret_cast<uint4*>(base + sw128_off(tok, d0 + 8)) = pack8(v + 8);
+    } else {
+      uint8_t* base = reinterpret_cast<uint8_t*>(ea.vt) + (hi * (ea.kv_rows / 64) + tok / 64) * 8192;
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        *reinterpret_cast<__nv_bfloat16*>(base + sw128_off(d0 + i, tok % 64)) = __float2bfloat16_rn(v[i]);
+    }
+  }
+}
+
+// C[tile, chunk] = A[tile] . W[chunk]^T, K = 64 * kb_n, streamed through `stages`
+// shared-memory slots (A block + W block each). Thread 0 issues the copies and the
+// MMAs; all four warps run the epilogue, one tile row per thread (its TMEM lane).
+template <int NC, int EPI>
+__global__ void __launch_bounds__(128) k_vit_gemm(const __nv_bfloat16* __restrict__ A, int kb_n,
+                                                  const __nv_bfloat16* __restrict__ W, int stages, EpiArgs ea,
+                                                  uint32_t* status) {
+  constexpr int STG = gemm_stage_bytes<NC>();
+  constexpr int TCOLS = NC <= 128 ? 128 : 256;
+  static_assert(NC % 64 == 0 && NC <= 256, "N chunk");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * STG);
+  uint64_t* freed = full + kMaxStages;
+  uint64_t* done = freed + kMaxStages;
+  uint32_t* slot = reinterpret_cast<uint32_t*>(done + 1);  // [0] TMEM base, [1] wait flag
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tile = blockIdx.x, chunk = blockIdx.y;
+  const __nv_bfloat16* a_src = A + (size_t)tile * kb_n * kBlk;
+  const __nv_bfloat16* w_src = W + (size_t)chunk * kb_n * NC * 64;
+  if (tid == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&freed[s], 1);
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(slot, TCOLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = slot[0];
+  if (tid == 0) {
+    int loaded = 0, used = 0;
+    auto load = [&](int kb) {
+      const int s = kb % stages;
+      mbar_arrive_expect_tx(&full[s], STG);
+      bulk_g2s(smem + s * STG, a_src + (size_t)kb * kBlk, kBlkBytes, &full[s]);
+      bulk_g2s(smem + s * STG + kBlkBytes, w_src + (size_t)kb * NC * 64, NC * 128, &full[s]);
+    };
+    for (; loaded < stages && loaded < kb_n; ++loaded) load(loaded);
+    const uint32_t idesc = idesc_bf16(128, NC);
+    for (int kb = 0; kb < kb_n; ++kb) {
+      const int s = kb % stages;
+      const uint32_t ph = (uint32_t)(kb / stages) & 1u;
+      if (!mbar_wait(&full[s], ph, status)) break;
+      used = kb + 1;
+      tc_fence_after();
+      umma_tile(tmem, smem_u32(smem + s * STG), kBlkBytes, smem_u32(smem + s * STG + kBlkBytes), NC * 128, 0, 1,
+                idesc, kb > 0);
+      umma_commit(&freed[s]);
+      if (loaded < kb_n) {  // loaded == kb + stages: refill this slot once its MMAs retired
+        if (!mbar_wait(&freed[s], ph, status)) break;
+        load(loaded++);
+      }
+    }
+    umma_commit(done);
+    // After an expired wait, let the copies still in flight land before the CTA exits.
+    for (int kb = used; kb < loaded; ++kb) mbar_wait(&full[kb % stages], (uint32_t)(kb / stages) & 1u, status);
+  }
+  const bool ok = cta_wait_mma(done, status, slot + 1);
+  tc_fence_after();
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  if (ok) {
+#pragma unroll 1
+    for (int c0 = 0; c0 < NC; c0 += 16) {
+      float v[16];
+      tmem_ld16(trow + c0, v);
+      gemm_epilogue<NC, EPI>(ea, tile, chunk, tid, c0, v);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, TCOLS);
+}
+
+// LayerNorm over C columns of fp32 rows (row r reads src + r * src_stride * C), optional
+// affine and GELU, written as bf16 operand blocks [out_rows / 128][C / 64][128 x 64].
+// Rows at or past n_valid are written as zeros. One warp per row.
+template <int C>
+__global__ void __launch_bounds__(256) k_vit_ln_op(const float* __restrict__ src, int src_stride, int n_valid,
+                                                   int out_rows, float eps, const float* __restrict__ gamma,
+                                                   const float* __restrict__ beta, int gelu,
+                                                   __nv_bfloat16* __restrict__ out) {
+  constexpr int NCH = C / 8;             // 16-byte output chunks per row
+  constexpr int PER = (NCH + 31) / 32;   // chunks per lane
+  constexpr int KB = C / 64;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + warp;
+  if (r >= out_rows) return;
+  uint8_t* ob = reinterpret_cast<uint8_t*>(out) + (size_t)(r / 128) * KB * kBlkBytes;
+  const int rr = r % 128;
+  if (r >= n_valid) {
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int q = lane + 32 * j;
+      if (q < NCH) *reinterpret_cast<uint4*>(ob + (q / 8) * kBlkBytes + sw128_off(rr, (q % 8) * 8)) = make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+  const float* row = src + (size_t)r * src_stride * C;
+  float v[PER][8];
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int q = lane + 32 * j;
+    if (q < NCH) {
+      const float4 a = *reinterpret_cast<const float4*>(row + q * 8);
+      const float4 b = *reinterpret_cast<const float4*>(row + q * 8 + 4);
+      v[j][0] = a.x; v[j][1] = a.y; v[j][2] = a.z; v[j][3] = a.w;
+      v[j][4] = b.x; v[j][5] = b.y; v[j][6] = b.z; v[j][7] = b.w;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s += v[j][e];
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[j][e] = 0.f;
+    }
+  }
+  const float mean = warp_sum(s) * (1.0f / C);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    if (lane + 32 * j < NCH) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = v[j][e] - mean;
+        ss += d * d;
+      }
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(ss) * (1.0f / C) + eps);
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int q = lane + 32 * j;
+    if (q >= NCH) continue;
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int k = q * 8 + e;
+      float t = (v[j][e] - mean) * rstd;
+      if (gamma) t = fmaf(t, gamma[k], beta[k]);
+      y[e] = gelu ? gelu_f(t) : t;
+    }
+    *reinterpret_cast<uint4*>(ob + (q / 8) * kBlkBytes + sw128_off(rr, (q % 8) * 8)) = pack8(y);
+  }
+}
+
+// Patch operand: row (image, token) holds the token's C x p x p pixels in Conv2d weight
+// order (channel, ky, kx), zero-padded to kbp * 64; CLS rows and rows past the last image
+// are zeros. One thread per 16-byte chunk.
+__global__ void __launch_bounds__(256) k_vit_patch_op(const float* __restrict__ pix, int n_img, int img, int p,
+                                                      int ch, int tokens, int kbp, int total_rows,
+                                                      __nv_bfloat16* __restrict__ out) {
+  const int nchunk = kbp * 8;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)total_rows * nchunk) return;
+  const int r = (int)(idx / nchunk), q = (int)(idx % nchunk);
+  const int gw = img / p, pp2 = p * p, K = ch * pp2;
+  const int im = r / tokens, tok = r % tokens;
+  const bool valid = im < n_img && tok > 0;
+  const int py = valid ? (tok - 1) / gw : 0, px = valid ? (tok - 1) % gw : 0;
+  float v[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int k = q * 8 + e;
+    float x = 0.f;
+    if (valid && k < K) {
+      const int c = k / pp2, rem = k % pp2, ky = rem / p, kx = rem % p;
+      x = pix[(((size_t)im * ch + c) * img + (size_t)(py * p + ky)) * img + px * p + kx];
+    }
+    v[e] = x;
+  }
+  uint8_t* blk = reinterpret_cast<uint8_t*>(out) + ((size_t)(r / 128) * kbp + q / 8) * kBlkBytes;
+  *reinterpret_cast<uint4*>(blk + sw128_off(r % 128, (q % 8) * 8)) = pack8(v);
+}
+
+struct AttnGeom {
+  int tokens;    // keys = queries per image
+  int ns;        // tokens rounded up to 16: S columns
+  int q_tiles;   // 128-row query tiles
+  int kv_rows;   // key rows held (kvb * 64)
+  int kvb;       // 64-key blocks of P and V^T
+};
+
+inline size_t attn_smem(const AttnGeom& g) {
+  return 1024 + (size_t)g.q_tiles * kBlkBytes + (size_t)g.kv_rows * 128 + (size_t)g.kvb * 8192 +
+         (size_t)g.kvb * kBlkBytes + 64;
+}
+
+// Softmax attention of one (head, image): all Q tiles, K and V^T are loaded once; per
+// query tile S = Q K^T (M 128, N <= 256 + a 16-column remainder) lands in TMEM, each
+// thread turns its row into bf16 probabilities in shared memory (masked past the last
+// token), and O = P V (N 64, K over the key blocks) lands in TMEM columns 384..447.
+// O / sum is written straight into the out-projection operand block of its row.
+__global__ void __launch_bounds__(128) k_vit_attn(const __nv_bfloat16* __restrict__ q,
+                                                  const __nv_bfloat16* __restrict__ k,
+                                                  const __nv_bfloat16* __restrict__ vt, AttnGeom ag,
+                                                  __nv_bfloat16* __restrict__ attn_op, uint32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  const int head = blockIdx.x, img = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const uint32_t qb = (uint32_t)ag.q_tiles * kBlkBytes, kbytes = (uint32_t)ag.kv_rows * 128,
+                 vb = (uint32_t)ag.kvb * 8192, pb = (uint32_t)ag.kvb * kBlkBytes;
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + qb;
+  uint8_t* sV = sK + kbytes;
+  uint8_t* sP = sV + vb;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sP + pb);  // [0] loads, [1] S, [2] O
+  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 3);  // [0] TMEM base, [1] wait flag
+  const size_t hi = (size_t)img * kHB + head;
+  if (tid == 0) {
+    for (int i = 0; i < 3; ++i) mbar_init(&bar[i], 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&bar[0], qb + kbytes + vb);
+    bulk_g2s(sQ, reinterpret_cast<const uint8_t*>(q) + hi * qb, qb, &bar[0]);
+    bulk_g2s(sK, reinterpret_cast<const uint8_t*>(k) + hi * kbytes, kbytes, &bar[0]);
+    bulk_g2s(sV, reinterpret_cast<const uint8_t*>(vt) + hi * vb, vb, &bar[0]);
+  }
+  if (warp == 0) {
+    tmem_alloc(slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = slot[0];
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  bool ok = cta_wait_mma(&bar[0], status, slot + 1);
+  const int n1 = ag.ns < 256 ? ag.ns : 256, n2 = ag.ns - n1;
+  const float c = 0.125f * 1.44269504088896341f;  // dim_head^-1/2 * log2(e)
+  for (int qt = 0; qt < ag.q_tiles && ok; ++qt) {
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t a = smem_u32(sQ + qt * kBlkBytes);
+      umma_tile(tmem, a, kBlkBytes, smem_u32(sK), 0, 0, 1, idesc_bf16(128, n1), false);
+      if (n2 > 0) umma_tile(tmem + 256, a, kBlkBytes, smem_u32(sK + 256 * 128), 0, 0, 1, idesc_bf16(128, n2), false);
+      umma_commit(&bar[1]);
+    }
+    ok = cta_wait_mma(&bar[1], status, slot + 1, (uint32_t)qt & 1u);
+    if (!ok) break;
+    tc_fence_after();
+    const int qi = qt * 128 + tid;
+    const bool valid = qi < ag.tokens;
+    float m = -INFINITY;
+#pragma unroll 1
+    for (int j0 = 0; j0 < ag.ns; j0 += 16) {
+      float v[16];
+      tmem_ld16(trow + j0, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (j0 + i < ag.tokens) m = fmaxf(m, v[i]);
+    }
+    const float mc = m * c;
+    float sum = 0.f;
+#pragma unroll 1
+    for (int j0 = 0; j0 < ag.kvb * 64; j0 += 16) {
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = 0.f;
+      if (j0 < ag.ns) tmem_ld16(trow + j0, v);
+      float pr[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float e = (valid && j0 + i < ag.tokens) ? exp2f(fmaf(v[i], c, -mc)) : 0.f;
+        pr[i] = __bfloat162float(__float2bfloat16_rn(e));  // the value the P V MMA sees
+        sum += pr[i];
+      }
+      uint8_t* blk = sP + (j0 / 64) * kBlkBytes;
+      *reinterpret_cast<uint4*>(blk + sw128_off(tid, j0 % 64)) = pack8(pr);
+      *reinterpret_cast<uint4*>(blk + sw128_off(tid, j0 % 64 + 8)) = pack8(pr + 8);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      umma_tile(tmem + 384, smem_u32(sP), kBlkBytes, smem_u32(sV), 8192, 0, ag.kvb, idesc_bf16(128, 64), false);
+      umma_commit(&bar[2]);
+    }
+    ok = cta_wait_mma(&bar[2], status, slot + 1, (uint32_t)qt & 1u);
+    if (!ok) break;
+    tc_fence_after();
+    float o[64];
+    tmem_ld_cols<64>(trow + 384, o);
+    if (valid) {
+      const float inv = 1.0f / sum;
+#pragma unroll
+      for (int d = 0; d < 64; ++d) o[d] *= inv;
+      const int grow = img * ag.tokens + qi;
+      uint8_t* dst = reinterpret_cast<uint8_t*>(attn_op) + ((size_t)(grow / 128) * kHB + head) * kBlkBytes;
+#pragma unroll
+      for (int d0 = 0; d0 < 64; d0 += 8) *reinterpret_cast<uint4*>(dst + sw128_off(grow % 128, d0)) = pack8(o + d0);
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// ----------------------------------------------------------------- host side
+
+uint16_t bf16_bits(float f) {  // round to nearest even; NaN stays NaN
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fc0;
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+// W [N x K] row-major -> [N / nc chunks][ceil(K / 64)][nc x 64] swizzled blocks, K zero-padded.
+void pack_blocks(const float* w, int N, int K, int nc, std::vector<uint16_t>& out, size_t at) {
+  const int kb_n = (K + 63) / 64;
+  for (int n = 0; n < N; ++n)
+    for (int kk = 0; kk < kb_n * 64; ++kk) {
+      const float val = kk < K ? w[(size_t)n * K + kk] : 0.f;
+      const int chunk = n / nc, nn = n % nc, kb = kk / 64;
+      const size_t blk = at + ((size_t)chunk * kb_n + kb) * nc * 64;
+      out[blk + sw128_off(nn, kk % 64) / 2] = bf16_bits(val);
+    }
+}
+
+struct Geo {
+  int tokens, kbp, fc1_nc, q_tiles, kv_rows, kvb, ns;
+};
+
+Geo geo_of(const lewm_encoder_desc& d) {
+  Geo g{};
+  const int gw = d.image_size / d.patch_size;
+  g.tokens = gw * gw + 1;
+  g.kbp = (d.channels * d.patch_size * d.patch_size + 63) / 64;
+  g.fc1_nc = d.mlp_dim % 256 == 0 ? 256 : 192;
+  g.ns = (g.tokens + 15) / 16 * 16;
+  g.q_tiles = (g.tokens + 127) / 128;
+  g.kvb = (g.ns + 63) / 64;
+  g.kv_rows = g.kvb * 64;
+  return g;
+}
+
+}  // namespace vit
+}  // namespace lewm
+
+using namespace lewm;
+using namespace lewm::vit;
+
+namespace {
+std::string g_enc_create_error;
+}
+
+struct lewm_encoder {
+  int device = 0;
+  lewm_encoder_desc desc{};
+  Geo geo{};
+  std::string err;
+  void* d_w = nullptr;       // bf16 blocks then fp32 vectors
+  uint32_t* d_status = nullptr;
+  // weight views
+  const __nv_bfloat16 *w_patch = nullptr, *w_p1 = nullptr, *w_p2 = nullptr;
+  std::vector<const __nv_bfloat16*> w_qkv, w_out, w_fc1, w_fc2;
+  const float *b_patch = nullptr, *cls = nullptr, *pos = nullptr, *lnf_g = nullptr, *lnf_b = nullptr;
+  const float *p1_scale = nullptr, *p1_shift = nullptr, *pn_g = nullptr, *pn_b = nullptr, *b_p2 = nullptr;
+  std::vector<const float*> ln1_g, ln1_b, b_qkv, b_out, ln2_g, ln2_b, b_fc1, b_fc2;
+  // workspace
+  void* d_ws = nullptr;
+  size_t ws_bytes = 0;
+  int ws_images = 0;
+  __nv_bfloat16 *patch_a = nullptr, *ln_a = nullptr, *attn_a = nullptr, *h_a = nullptr, *cls_a = nullptr,
+                *ph_a = nullptr, *q = nullptr, *k = nullptr, *vt = nullptr;
+  float *x = nullptr, *ph32 = nullptr;
+};
+
+namespace {
+
+lewm_status efail(lewm_encoder* e, lewm_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (e)
+    e->err = buf;
+  else
+    g_enc_create_error = buf;
+  return s;
+}
+
+#define ENC_CK(enc, call)                                                                                \
+  do {                                                                                                   \
+    cudaError_t e_ = (call);                                                                             \
+    if (e_ != cudaSuccess)                                                                               \
+      return efail(enc, e_ == cudaErrorMemoryAllocation ? LEWM_OUT_OF_MEMORY : LEWM_CUDA_ERROR, "%s: %s", \
+                   #call, cudaGetErrorString(e_));                                                       \
+  } while (0)
+
+struct EncDeviceGuard {
+  int prev = -1;
+  explicit EncDeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    cudaSetDevice(dev);
+  }
+  ~EncDeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+lewm_status check_enc_desc(const lewm_encoder_desc* d) {
+  if (!d) return efail(nullptr, LEWM_INVALID_ARG, "desc is NULL");
+  if (d->image_size <= 0 || d->patch_size <= 0 || d->channels <= 0 || d->depth <= 0 || d->heads <= 0 ||
+      d->mlp_dim <= 0 || d->proj_hidden < 0 || d->proj_out <= 0 || !(d->ln_eps > 0.f) || !(d->proj_eps > 0.f))
+    return efail(nullptr, LEWM_INVALID_ARG, "encoder desc has a non-positive size or eps");
+  if (d->proj_norm < 0 || d->proj_norm > 2) return efail(nullptr, LEWM_INVALID_ARG, "proj_norm must be 0, 1 or 2");
+  if (d->hidden != kD || d->heads * 64 != d->hidden)
+    return efail(nullptr, LEWM_UNSUPPORTED_SHAPE, "encoder kernels are built for hidden %d with dim_head 64", kD);
+  if (d->image_size % d->patch_size != 0)
+    return efail(nullptr, LEWM_UNSUPPORTED_SHAPE, "image_size must be a multiple of patch_size");
+  const Geo g = geo_of(*d);
+  if (g.tokens > kMaxTok)
+    return efail(nullptr, LEWM_UNSUPPORTED_SHAPE, "%d tokens per image; at most %d", g.tokens, kMaxTok);
+  if (g.kbp > 32) return efail(nullptr, LEWM_UNSUPPORTED_SHAPE, "channels x patch^2 above 2048");
+  if (d->mlp_dim % 256 != 0 && d->mlp_dim % 192 != 0)
+    return efail(nullptr, LEWM_UNSUPPORTED_SHAPE, "mlp_dim must be a multiple of 192 or 256");
+  if (d->proj_hidden == 0 || d->proj_hidden % 256 != 0)
+    return efail(nullptr, LEWM_UNSUPPORTED_SHAPE, "proj_hidden must be a positive multiple of 256");
+  if (d->proj_out != kD) return efail(nullptr, LEWM_UNSUPPORTED_SHAPE, "proj_out must be %d", kD);
+  return LEWM_OK;
+}
+
+size_t weight_count(const lewm_encoder_desc& d) {
+  const Geo g = geo_of(d);
+  const size_t D = d.hidden, M = d.mlp_dim, P = d.proj_hidden;
+  size_t n = D + (size_t)g.tokens * D + D * d.channels * d.patch_size * d.patch_size + D;
+  n += (size_t)d.depth * (2 * D + 3 * (D * D + D) + D * D + D + 2 * D + M * D + M + D * M + D);
+  n += 2 * D;
+  n += P * D + P + (d.proj_norm == 1 ? 2 * P : d.proj_norm == 2 ? 4 * P : 0) + (size_t)d.proj_out * P + d.proj_out;
+  return n;
+}
+
+template <int NC, int EPI>
+cudaError_t set_gemm_smem() {
+  return cudaFuncSetAttribute(k_vit_gemm<NC, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)gemm_smem<NC>(kMaxStages));
+}
+
+template <int NC, int EPI>
+void launch_gemm(const __nv_bfloat16* A, int kb_n, const __nv_bfloat16* W, int tiles, int chunks, const EpiArgs& ea,
+                 uint32_t* status, cudaStream_t st) {
+  const int stages = kb_n < kMaxStages ? kb_n : kMaxStages;
+  k_vit_gemm<NC, EPI><<<dim3(tiles, chunks), 128, gemm_smem<NC>(stages), st>>>(A, kb_n, W, stages, ea, status);
+}
+
+template <int C>
+void launch_ln(const float* src, int src_stride, int n_valid, int out_rows, float eps, const float* g,
+               const float* b, int gelu, __nv_bfloat16* out, cudaStream_t st) {
+  k_vit_ln_op<C><<<(out_rows + 7) / 8, 256, 0, st>>>(src, src_stride, n_valid, out_rows, eps, g, b, gelu, out);
+}
+
+lewm_status ensure_enc_ws(lewm_encoder* e, int n_img, cudaStream_t st) {
+  if (e->d_ws && n_img <= e->ws_images) return LEWM_OK;
+  const lewm_encoder_desc& d = e->desc;
+  const Geo& g = e->geo;
+  const size_t rows = (size_t)n_img * g.tokens, mt = (rows + 127) / 128, mi = ((size_t)n_img + 127) / 128;
+  size_t off = 0;
+  auto carve = [&](size_t bytes) {
+    const size_t at = off;
+    off += (bytes + 1023) / 1024 * 1024;
+    return at;
+  };
+  const size_t o_patch = carve(mt * g.kbp * kBlkBytes);
+  const size_t o_x = carve(mt * 128 * kD * 4);
+  const size_t o_ln = carve(mt * kHB * kBlkBytes);
+  const size_t o_attn = carve(mt * kHB * kBlkBytes);
+  const size_t o_h = carve(mt * (d.mlp_dim / 64) * kBlkBytes);
+  const size_t o_q = carve((size_t)n_img * kHB * g.q_tiles * kBlkBytes);
+  const size_t o_k = carve((size_t)n_img * kHB * g.kv_rows * 128);
+  const size_t o_vt = carve((size_t)n_img * kHB * g.kvb * 8192);
+  const size_t o_cls = carve(mi * kHB * kBlkBytes);
+  const size_t o_ph = carve(mi * (d.proj_hidden / 64) * kBlkBytes);
+  const size_t o_ph32 = carve(d.proj_norm == 1 ? mi * 128 * d.proj_hidden * 4 : 0);
+  if (e->d_ws) {
+    cudaFree(e->d_ws);
+    e->d_ws = nullptr;
+    e->ws_images = 0;
+  }
+  ENC_CK(e, cudaMalloc(&e->d_ws, off));
+  // Padding rows and key slots are never written by the kernels and must read as zero.
+  ENC_CK(e, cudaMemsetAsync(e->d_ws, 0, off, st));
+  uint8_t* base = static_cast<uint8_t*>(e->d_ws);
+  e->patch_a = reinterpret_cast<__nv_bfloat16*>(base + o_patch);
+  e->x = reinterpret_cast<float*>(base + o_x);
+  e->ln_a = reinterpret_cast<__nv_bfloat16*>(base + o_ln);
+  e->attn_a = reinterpret_cast<__nv_bfloat16*>(base + o_attn);
+  e->h_a = reinterpret_cast<__nv_bfloat16*>(base + o_h);
+  e->q = reinterpret_cast<__nv_bfloat16*>(base + o_q);
+  e->k = reinterpret_cast<__nv_bfloat16*>(base + o_k);
+  e->vt = reinterpret_cast<__nv_bfloat16*>(base + o_vt);
+  e->cls_a = reinterpret_cast<__nv_bfloat16*>(base + o_cls);
+  e->ph_a = reinterpret_cast<__nv_bfloat16*>(base + o_ph);
+  e->ph32 = reinterpret_cast<float*>(base + o_ph32);
+  e->ws_bytes = off;
+  e->ws_images = n_img;
+  return LEWM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t lewm_encoder_weight_count(const lewm_encoder_desc* desc) {
+  if (check_enc_desc(desc) != LEWM_OK) return 0;
+  return weight_count(*desc);
+}
+
+lewm_status lewm_encoder_create(lewm_encoder** out, const lewm_encoder_desc* desc, const float* weights,
+                                size_t n_floats, int device) {
+  if (!out) return efail(nullptr, LEWM_INVALID_ARG, "out is NULL");
+  *out = nullptr;
+  lewm_status s = check_enc_desc(desc);
+  if (s != LEWM_OK) return s;
+  if (!weights) return efail(nullptr, LEWM_INVALID_ARG, "weights is NULL");
+  const lewm_encoder_desc d = *desc;
+  if (n_floats != weight_count(d))
+    return efail(nullptr, LEWM_INVALID_ARG, "expected %zu weight floats, got %zu", weight_count(d), n_floats);
+  const Geo g = geo_of(d);
+  const int D = kD, M = d.mlp_dim, P = d.proj_hidden, L = d.depth;
+  const int KP = d.channels * d.patch_size * d.patch_size;
+
+  // Layout of the device weight buffer: bf16 blocks first, then fp32 vectors.
+  std::vector<size_t> bf_at;
+  size_t bf = 0;
+  auto bf_take = [&](size_t elems) {
+    bf_at.push_back(bf);
+    bf += (elems + 511) / 512 * 512;  // 1 KB granules keep every block base 1024-byte aligned
+    return bf_at.back();
+  };
+  const size_t a_patch = bf_take((size_t)D * g.kbp * 64);
+  std::vector<size_t> a_qkv(L), a_out(L), a_fc1(L), a_fc2(L);
+  for (int l = 0; l < L; ++l) {
+    a_qkv[l] = bf_take((size_t)3 * D * D);
+    a_out[l] = bf_take((size_t)D * D);
+    a_fc1[l] = bf_take((size_t)M * D);
+    a_fc2[l] = bf_take((size_t)D * M);
+  }
+  const size_t a_p1 = bf_take((size_t)P * D);
+  const size_t a_p2 = bf_take((size_t)d.proj_out * P);
+  std::vector<uint16_t> hb(bf, 0);
+  std::vector<float> fv;
+  auto f_take = [&](const float* src, size_t n) {
+    const size_t at = fv.size();
+    fv.insert(fv.end(), src, src + n);
+    fv.resize((fv.size() + 3) / 4 * 4, 0.f);  // 16-byte alignment of every vector
+    return at;
+  };
+  const float* w = weights;
+  const size_t f_cls = f_take(w, D);
+  w += D;
+  const size_t f_pos = f_take(w, (size_t)g.tokens * D);
+  w += (size_t)g.tokens * D;
+  pack_blocks(w, D, KP, D, hb, a_patch);
+  w += (size_t)D * KP;
+  const size_t f_bpatch = f_take(w, D);
+  w += D;
+  std::vector<size_t> f_ln1g(L), f_ln1b(L), f_bqkv(L), f_bout(L), f_ln2g(L), f_ln2b(L), f_bfc1(L), f_bfc2(L);
+  for (int l = 0; l < L; ++l) {
+    f_ln1g[l] = f_take(w, D);
+    w += D;
+    f_ln1b[l] = f_take(w, D);
+    w += D;
+    std::vector<float> qkv_w((size_t)3 * D * D), qkv_b((size_t)3 * D);
+    for (int t = 0; t < 3; ++t) {  // query, key, value: weight then bias
+      std::memcpy(qkv_w.data() + (size_t)t * D * D, w, sizeof(float) * D * D);
+      w += (size_t)D * D;
+      std::memcpy(qkv_b.data() + (size_t)t * D, w, sizeof(float) * D);
+      w += D;
+    }
+    pack_blocks(qkv_w.data(), 3 * D, D, D, hb, a_qkv[l]);
+    f_bqkv[l] = f_take(qkv_b.data(), 3 * D);
+    pack_blocks(w, D, D, D, hb, a_out[l]);
+    w += (size_t)D * D;
+    f_bout[l] = f_take(w, D);
+    w += D;
+    f_ln2g[l] = f_take(w, D);
+    w += D;
+    f_ln2b[l] = f_take(w, D);
+    w += D;
+    pack_blocks(w, M, D, g.fc1_nc, hb, a_fc1[l]);
+    w += (size_t)M * D;
+    f_bfc1[l] = f_take(w, M);
+    w += M;
+    pack_blocks(w, D, M, D, hb, a_fc2[l]);
+    w += (size_t)D * M;
+    f_bfc2[l] = f_take(w, D);
+    w += D;
+  }
+  const size_t f_lnfg = f_take(w, D);
+  w += D;
+  const size_t f_lnfb = f_take(w, D);
+  w += D;
+  pack_blocks(w, P, D, 256, hb, a_p1);
+  w += (size_t)P * D;
+  const float* p1_bias = w;
+  w += P;
+  // Projector hidden: BatchNorm1d (eval) folds into a per-column scale and shift of the
+  // first Linear's accumulator; LayerNorm runs as its own row pass after the bias.
+  std::vector<float> scale(P, 1.f), shift(p1_bias, p1_bias + P);
+  size_t f_png = 0, f_pnb = 0;
+  if (d.proj_norm == 1) {
+    f_png = f_take(w, P);
+    w += P;
+    f_pnb = f_take(w, P);
+    w += P;
+  } else if (d.proj_norm == 2) {
+    const float *gam = w, *bet = w + P, *rm = w + 2 * P, *rv = w + 3 * P;
+    for (int i = 0; i < P; ++i) {
+      const double sc = (double)gam[i] / std::sqrt((double)rv[i] + (double)d.proj_eps);
+      scale[i] = (float)sc;
+      shift[i] = (float)(((double)p1_bias[i] - (double)rm[i]) * sc + (double)bet[i]);
+    }
+    w += 4 * P;
+  }
+  const size_t f_scale = f_take(scale.data(), P);
+  const size_t f_shift = f_take(shift.data(), P);
+  pack_blocks(w, d.proj_out, P, d.proj_out, hb, a_p2);
+  w += (size_t)d.proj_out * P;
+  const size_t f_bp2 = f_take(w, d.proj_out);
+  w += d.proj_out;
+
+  lewm_encoder* e = new lewm_encoder();
+  e->device = device;
+  e->desc = d;
+  e->geo = g;
+  {
+    EncDeviceGuard guard(device);
+    const size_t bf_bytes = bf * 2, total = bf_bytes + fv.size() * 4;
+    cudaError_t ce = cudaMalloc(&e->d_w, total);
+    if (ce == cudaSuccess) ce = cudaMemcpy(e->d_w, hb.data(), bf_bytes, cudaMemcpyHostToDevice);
+    if (ce == cudaSuccess)
+      ce = cudaMemcpy(static_cast<uint8_t*>(e->d_w) + bf_bytes, fv.data(), fv.size() * 4, cudaMemcpyHostToDevice);
+    if (ce == cudaSuccess) ce = cudaMalloc(&e->d_status, 4);
+    if (ce == cudaSuccess) ce = cudaMemset(e->d_status, 0, 4);
+    if (ce == cudaSuccess) ce = set_gemm_smem<192, EPI_PATCH>();
+    if (ce == cudaSuccess) ce = set_gemm_smem<192, EPI_QKV>();
+    if (ce == cudaSuccess) ce = set_gemm_smem<192, EPI_RESID>();
+    if (ce == cudaSuccess) ce = set_gemm_smem<192, EPI_GELU_OP>();
+    if (ce == cudaSuccess) ce = set_gemm_smem<256, EPI_GELU_OP>();
+    if (ce == cudaSuccess) ce = set_gemm_smem<256, EPI_F32>();
+    if (ce == cudaSuccess) ce = set_gemm_smem<192, EPI_F32>();
+    if (ce == cudaSuccess) {
+      AttnGeom ag{g.tokens, g.ns, g.q_tiles, g.kv_rows, g.kvb};
+      ce = cudaFuncSetAttribute(k_vit_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(ag));
+    }
+    if (ce != cudaSuccess) {
+      efail(nullptr, ce == cudaErrorMemoryAllocation ? LEWM_OUT_OF_MEMORY : LEWM_CUDA_ERROR, "encoder create: %s",
+            cudaGetErrorString(ce));
+      if (e->d_w) cudaFree(e->d_w);
+      if (e->d_status) cudaFree(e->d_status);
+      delete e;
+      return ce == cudaErrorMemoryAllocation ? LEWM_OUT_OF_MEMORY : LEWM_CUDA_ERROR;
+    }
+  }
+  const __nv_bfloat16* wb = static_cast<const __nv_bfloat16*>(e->d_w);
+  const float* wf = reinterpret_cast<const float*>(static_cast<const uint8_t*>(e->d_w) + bf * 2);
+  e->w_patch = wb + a_patch;
+  e->w_p1 = wb + a_p1;
+  e->w_p2 = wb + a_p2;
+  e->b_patch = wf + f_bpatch;
+  e->cls = wf + f_cls;
+  e->pos = wf + f_pos;
+  e->lnf_g = wf + f_lnfg;
+  e->lnf_b = wf + f_lnfb;
+  e->p1_scale = wf + f_scale;
+  e->p1_shift = wf + f_shift;
+  e->pn_g = d.proj_norm == 1 ? wf + f_png : nullptr;
+  e->pn_b = d.proj_norm == 1 ? wf + f_pnb : nullptr;
+  e->b_p2 = wf + f_bp2;
+  for (int l = 0; l < L; ++l) {
+    e->w_qkv.push_back(wb + a_qkv[l]);
+    e->w_out.push_back(wb + a_out[l]);
+    e->w_fc1.push_back(wb + a_fc1[l]);
+    e->w_fc2.push_back(wb + a_fc2[l]);
+    e->ln1_g.push_back(wf + f_ln1g[l]);
+    e->ln1_b.push_back(wf + f_ln1b[l]);
+    e->b_qkv.push_back(wf + f_bqkv[l]);
+    e->b_out.push_back(wf + f_bout[l]);
+    e->ln2_g.push_back(wf + f_ln2g[l]);
+    e->ln2_b.push_back(wf + f_ln2b[l]);
+    e->b_fc1.push_back(wf + f_bfc1[l]);
+    e->b_fc2.push_back(wf + f_bfc2[l]);
+  }
+  *out = e;
+  return LEWM_OK;
+}
+
+lewm_status lewm_encode(lewm_encoder* e, const float* pixels, int32_t n_images, float* emb_out, void* stream) {
+  if (!e) return efail(nullptr, LEWM_INVALID_ARG, "encoder is NULL");
+  if (n_images < 0) return efail(e, LEWM_INVALID_ARG, "n_images < 0");
+  if (n_images == 0) return LEWM_OK;
+  if (!pixels || !emb_out) return efail(e, LEWM_INVALID_ARG, "pixels / emb_out is NULL");
+  if ((reinterpret_cast<uintptr_t>(emb_out) & 15u) != 0)
+    return efail(e, LEWM_INVALID_ARG, "emb_out must be 16-byte aligned");
+  EncDeviceGuard guard(e->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  lewm_status s = ensure_enc_ws(e, n_images, st);
+  if (s != LEWM_OK) return s;
+  const lewm_encoder_desc& d = e->desc;
+  const Geo& g = e->geo;
+  const int rows = n_images * g.tokens, mt = (rows + 127) / 128, mi = (n_images + 127) / 128;
+  const float eps = d.ln_eps;
+  {
+    const long long total = (long long)mt * 128 * g.kbp * 8;
+    k_vit_patch_op<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(pixels, n_images, d.image_size, d.patch_size,
+                                                                    d.channels, g.tokens, g.kbp, mt * 128,
+                                                                    e->patch_a);
+  }
+  EpiArgs ea{};
+  ea.rows = rows;
+  ea.tokens = g.tokens;
+  ea.q_rows = g.q_tiles * 128;
+  ea.kv_rows = g.kv_rows;
+  ea.x = e->x;
+  ea.bias = e->b_patch;
+  ea.pos = e->pos;
+  ea.cls = e->cls;
+  launch_gemm<192, EPI_PATCH>(e->patch_a, g.kbp, e->w_patch, mt, 1, ea, e->d_status, st);
+  const AttnGeom ag{g.tokens, g.ns, g.q_tiles, g.kv_rows, g.kvb};
+  const size_t asm_bytes = attn_smem(ag);
+  for (int l = 0; l < d.depth; ++l) {
+    launch_ln<kD>(e->x, 1, rows, mt * 128, eps, e->ln1_g[l], e->ln1_b[l], 0, e->ln_a, st);
+    EpiArgs qa = ea;
+    qa.bias = e->b_qkv[l];
+    qa.q = e->q;
+    qa.k = e->k;
+    qa.vt = e->vt;
+    launch_gemm<192, EPI_QKV>(e->ln_a, kHB, e->w_qkv[l], mt, 3, qa, e->d_status, st);
+    k_vit_attn<<<dim3(kHB, n_images), 128, asm_bytes, st>>>(e->q, e->k, e->vt, ag, e->attn_a, e->d_status);
+    EpiArgs ra = ea;
+    ra.bias = e->b_out[l];
+    launch_gemm<192, EPI_RESID>(e->attn_a, kHB, e->w_out[l], mt, 1, ra, e->d_status, st);
+    launch_ln<kD>(e->x, 1, rows, mt * 128, eps, e->ln2_g[l], e->ln2_b[l], 0, e->ln_a, st);
+    EpiArgs ha = ea;
+    ha.bias = e->b_fc1[l];
+    ha.scale = nullptr;
+    ha.op = e->h_a;
+    ha.n_total = d.mlp_dim;
+    if (g.fc1_nc == 256)
+      launch_gemm<256, EPI_GELU_OP>(e->ln_a, kHB, e->w_fc1[l], mt, d.mlp_dim / 256, ha, e->d_status, st);
+    else
+      launch_gemm<192, EPI_GELU_OP>(e->ln_a, kHB, e->w_fc1[l], mt, d.mlp_dim / 192, ha, e->d_status, st);
+    EpiArgs fa = ea;
+    fa.bias = e->b_fc2[l];
+    launch_gemm<192, EPI_RESID>(e->h_a, d.mlp_dim / 64, e->w_fc2[l], mt, 1, fa, e->d_status, st);
+  }
+  // Final LayerNorm of the CLS rows only (row image * tokens), then the projector.
+  launch_ln<kD>(e->x, g.tokens, n_images, mi * 128, eps, e->lnf_g, e->lnf_b, 0, e->cls_a, st);
+  EpiArgs pa{};
+  pa.rows = n_images;
+  pa.n_total = d.proj_hidden;
+  if (d.proj_norm == 1) {
+    pa.x = e->ph32;
+    pa.bias = e->p1_shift;  // the Linear bias (scale is 1 without BatchNorm)
+    launch_gemm<256, EPI_F32>(e->cls_a, kHB, e->w_p1, mi, d.proj_hidden / 256, pa, e->d_status, st);
+    launch_ln<2048>(e->ph32, 1, n_images, mi * 128, d.proj_eps, e->pn_g, e->pn_b, 1, e->ph_a, st);
+  } else {
+    pa.op = e->ph_a;
+    pa.scale = e->p1_scale;
+    pa.bias = e->p1_shift;
+    launch_gemm<256, EPI_GELU_OP>(e->cls_a, kHB, e->w_p1, mi, d.proj_hidden / 256, pa, e->d_status, st);
+  }
+  EpiArgs oa{};
+  oa.rows = n_images;
+  oa.n_total = d.proj_out;
+  oa.x = emb_out;
+  oa.bias = e->b_p2;
+  launch_gemm<192, EPI_F32>(e->ph_a, d.proj_hidden / 64, e->w_p2, mi, 1, oa, e->d_status, st);
+  ENC_CK(e, cudaGetLastError());
+  return LEWM_OK;
+}
+
+lewm_status lewm_encoder_sync_status(lewm_encoder* e, void* stream) {
+  if (!e) return efail(nullptr, LEWM_INVALID_ARG, "encoder is NULL");
+  EncDeviceGuard guard(e->device);
+  ENC_CK(e, cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  ENC_CK(e, cudaGetLastError());
+  uint32_t v = 0;
+  ENC_CK(e, cudaMemcpy(&v, e->d_status, 4, cudaMemcpyDeviceToHost));
+  if (v) {
+    ENC_CK(e, cudaMemset(e->d_status, 0, 4));
+    return efail(e, LEWM_DEVICE_TIMEOUT, "device status 0x%x: a bounded device wait expired", v);
+  }
+  return LEWM_OK;
+}
+
+const char* lewm_encoder_last_error(const lewm_encoder* e) { return e ? e->err.c_str() : g_enc_create_error.c_str(); }
+
+void lewm_encoder_destroy(lewm_encoder* e) {
+  if (!e) return;
+  {
+    EncDeviceGuard guard(e->device);
+    if (e->d_ws) cudaFree(e->d_ws);
+    if (e->d_w) cudaFree(e->d_w);
+    if (e->d_status) cudaFree(e->d_status);
+  }
+  delete e;
+}
+
+}  // extern "C"
