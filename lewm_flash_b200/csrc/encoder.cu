@@ -299,6 +299,49 @@ __global__ void __launch_bounds__(256) k_vit_ln_op(const float* __restrict__ src
   }
 }
 
+// LayerNorm (+ optional GELU) over a runtime width C (a multiple of 64) of fp32 rows
+// [n][C], written as bf16 operand blocks [out_rows / 128][C / 64][128 x 64]: the
+// projector hidden, a few rows per batch. Three passes over the row (mean, variance,
+// output); rows at or past n_valid are written as zeros. One warp per row.
+__global__ void __launch_bounds__(256) k_vit_ln_wide(const float* __restrict__ src, int C, int n_valid,
+                                                     int out_rows, float eps, const float* __restrict__ gamma,
+                                                     const float* __restrict__ beta, int gelu,
+                                                     __nv_bfloat16* __restrict__ out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + warp;
+  if (r >= out_rows) return;
+  const int nch = C / 8, kb_n = C / 64;
+  uint8_t* ob = reinterpret_cast<uint8_t*>(out) + (size_t)(r / 128) * kb_n * kBlkBytes;
+  const int rr = r % 128;
+  if (r >= n_valid) {
+    for (int q = lane; q < nch; q += 32)
+      *reinterpret_cast<uint4*>(ob + (q / 8) * kBlkBytes + sw128_off(rr, (q % 8) * 8)) = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const float* row = src + (size_t)r * C;
+  float s = 0.f;
+  for (int q = lane; q < nch; q += 32)
+    for (int e = 0; e < 8; ++e) s += row[q * 8 + e];
+  const float mean = warp_sum(s) / (float)C;
+  float ss = 0.f;
+  for (int q = lane; q < nch; q += 32)
+    for (int e = 0; e < 8; ++e) {
+      const float d = row[q * 8 + e] - mean;
+      ss += d * d;
+    }
+  const float rstd = rsqrtf(warp_sum(ss) / (float)C + eps);
+  for (int q = lane; q < nch; q += 32) {
+    float y[8];
+    for (int e = 0; e < 8; ++e) {
+      const int k = q * 8 + e;
+      float t = (row[k] - mean) * rstd;
+      if (gamma) t = fmaf(t, gamma[k], beta[k]);
+      y[e] = gelu ? gelu_f(t) : t;
+    }
+    *reinterpret_cast<uint4*>(ob + (q / 8) * kBlkBytes + sw128_off(rr, (q % 8) * 8)) = pack8(y);
+  }
+}
+
 // Patch operand: row (image, token) holds the token's C x p x p pixels in Conv2d weight
 // order (channel, ky, kx), zero-padded to kbp * 64; CLS rows and rows past the last image
 // are zeros. One thread per 16-byte chunk.
@@ -914,7 +957,8 @@ lewm_status lewm_encode(lewm_encoder* e, const float* pixels, int32_t n_images, 
     pa.x = e->ph32;
     pa.bias = e->p1_shift;  // the Linear bias (scale is 1 without BatchNorm)
     launch_gemm<256, EPI_F32>(e->cls_a, kHB, e->w_p1, mi, d.proj_hidden / 256, pa, e->d_status, st);
-    launch_ln<2048>(e->ph32, 1, n_images, mi * 128, d.proj_eps, e->pn_g, e->pn_b, 1, e->ph_a, st);
+    k_vit_ln_wide<<<mi * 16, 256, 0, st>>>(e->ph32, d.proj_hidden, n_images, mi * 128, d.proj_eps, e->pn_g, e->pn_b,
+                                           1, e->ph_a);
   } else {
     pa.op = e->ph_a;
     pa.scale = e->p1_scale;
