@@ -74,8 +74,61 @@ __device__ __forceinline__ uint4 pack8(const float* v) {
 
 template <int NC>
 constexpr int gemm_stage_bytes() { return kBlkBytes + NC * 128; }
+// Operand slots, reused after the MMAs retire as the fp32 staging tile [128][NC + 4] of
+// the row-wise epilogues; the mbarriers sit after the larger of the two.
 template <int NC>
-size_t gemm_smem(int stages) { return 1024 + (size_t)stages * gemm_stage_bytes<NC>() + 128; }
+__host__ __device__ constexpr int gemm_area(int stages) {
+  return stages * gemm_stage_bytes<NC>() > 128 * (NC + 4) * 4 ? stages * gemm_stage_bytes<NC>() : 128 * (NC + 4) * 4;
+}
+template <int NC>
+size_t gemm_smem(int stages) { return 1024 + (size_t)gemm_area<NC>(stages) + 128; }
+
+constexpr bool staged_epi(int epi) { return epi == EPI_PATCH || epi == EPI_RESID || epi == EPI_F32; }
+
+// Row-wise epilogues from the staging tile, consecutive threads on consecutive float4s of
+// a row (coalesced, and no thread re-reads a sector it has just written): PATCH writes
+// acc + bias + position (CLS + position on token 0) into the residual rows, RESID adds
+// acc + bias into them, F32 writes acc + bias.
+template <int NC, int EPI>
+__device__ __forceinline__ void staged_epilogue(const EpiArgs& ea, int tile, int chunk, const float* __restrict__ stage) {
+  constexpr int NV = NC / 4, SROW = NC + 4;
+  const float* __restrict__ bias = ea.bias;
+  float* __restrict__ x = ea.x;
+#pragma unroll 4
+  for (int idx = threadIdx.x; idx < 128 * NV; idx += 128) {
+    const int row = idx / NV, q = idx % NV;
+    const int grow = tile * 128 + row;
+    if (grow >= ea.rows) continue;
+    const float4 a = *reinterpret_cast<const float4*>(stage + row * SROW + q * 4);
+    const int col = chunk * NC + q * 4;
+    if constexpr (EPI == EPI_PATCH) {
+      const int tok = grow % ea.tokens;
+      const float4 p = *reinterpret_cast<const float4*>(ea.pos + (size_t)tok * kD + q * 4);
+      float4 o;
+      if (tok == 0) {
+        const float4 c = *reinterpret_cast<const float4*>(ea.cls + q * 4);
+        o = make_float4(c.x + p.x, c.y + p.y, c.z + p.z, c.w + p.w);
+      } else {
+        const float4 b = *reinterpret_cast<const float4*>(bias + q * 4);
+        o = make_float4(a.x + b.x + p.x, a.y + b.y + p.y, a.z + b.z + p.z, a.w + b.w + p.w);
+      }
+      *reinterpret_cast<float4*>(x + (size_t)grow * kD + q * 4) = o;
+    } else if constexpr (EPI == EPI_RESID) {
+      const float4 b = *reinterpret_cast<const float4*>(bias + col);
+      float4* xp = reinterpret_cast<float4*>(x + (size_t)grow * kD + col);
+      float4 o = *xp;
+      o.x += a.x + b.x;
+      o.y += a.y + b.y;
+      o.z += a.z + b.z;
+      o.w += a.w + b.w;
+      *xp = o;
+    } else {
+      const float4 b = *reinterpret_cast<const float4*>(bias + col);
+      *reinterpret_cast<float4*>(x + (size_t)grow * ea.n_total + col) =
+          make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+    }
+  }
+}
 
 // Epilogue of 16 accumulator columns [c0, c0 + 16) of tile row r.
 template <int NC, int EPI>
@@ -160,7 +213,7 @@ __global__ void __launch_bounds__(128) k_vit_gemm(const __nv_bfloat16* __restric
   static_assert(NC % 64 == 0 && NC <= 256, "N chunk");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * STG);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + gemm_area<NC>(stages));
   uint64_t* freed = full + kMaxStages;
   uint64_t* done = freed + kMaxStages;
   uint32_t* slot = reinterpret_cast<uint32_t*>(done + 1);  // [0] TMEM base, [1] wait flag
@@ -215,7 +268,21 @@ __global__ void __launch_bounds__(128) k_vit_gemm(const __nv_bfloat16* __restric
   const bool ok = cta_wait_mma(done, status, slot + 1);
   tc_fence_after();
   const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-  if (ok) {
+  if constexpr (staged_epi(EPI)) {
+    float* stage = reinterpret_cast<float*>(smem);  // operand slots are dead once the MMAs retired
+    if (ok) {
+#pragma unroll 1
+      for (int c0 = 0; c0 < NC; c0 += 16) {
+        float v[16];
+        tmem_ld16(trow + c0, v);
+        float* dst = stage + tid * (NC + 4) + c0;
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      }
+    }
+    __syncthreads();
+    if (ok) staged_epilogue<NC, EPI>(ea, tile, chunk, stage);
+  } else if (ok) {
 #pragma unroll 1
     for (int c0 = 0; c0 < NC; c0 += 16) {
       float v[16];
