@@ -19,7 +19,7 @@
 //                    GELU_OP GELU(acc * scale + shift) -> bf16 operand of the next GEMM
 //                    F32     + bias -> fp32 rows
 //   k_vit_ln_op      LayerNorm (+ optional GELU) of fp32 rows -> bf16 operand blocks
-//   k_vit_attn       one CTA per (head, image): S = Q K^T into TMEM, softmax in
+//   k_vit_attn       one CTA per (query tile, head, image): S = Q K^T into TMEM, softmax in
 //                    registers, P V on the tensor core, written as the out-proj operand
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -44,6 +44,7 @@ constexpr int kMaxTok = 272;           // tokens one attention CTA holds (S in 2
 constexpr int kBlk = 128 * 64;         // elements of a [128 x 64] operand block
 constexpr int kBlkBytes = kBlk * 2;
 constexpr int kMaxStages = 4;
+constexpr int kGemmThreads = 256;      // two warpgroups: each reads half of the accumulator columns
 
 enum Epi { EPI_PATCH = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GELU_OP = 3, EPI_F32 = 4 };
 
@@ -57,6 +58,10 @@ struct EpiArgs {
   __nv_bfloat16* q;     // QKV: [image][head][q_rows x 64] swizzled rows
   __nv_bfloat16* k;     // QKV: [image][head][kv_rows x 64]
   __nv_bfloat16* vt;    // QKV: [image][head][kv_rows / 64][64 x 64], row = d, column = key
+  const float* ln_g;    // PATCH / RESID: LayerNorm of the updated rows for the next GEMM
+  const float* ln_b;    //   (affine), written as bf16 operand blocks to ln_out (null = none)
+  __nv_bfloat16* ln_out;
+  float ln_eps;
   int rows;             // valid rows
   int tokens;           // tokens per image
   int n_total;          // output columns over all chunks (GELU_OP, F32)
@@ -88,14 +93,16 @@ constexpr bool staged_epi(int epi) { return epi == EPI_PATCH || epi == EPI_RESID
 // Row-wise epilogues from the staging tile, consecutive threads on consecutive float4s of
 // a row (coalesced, and no thread re-reads a sector it has just written): PATCH writes
 // acc + bias + position (CLS + position on token 0) into the residual rows, RESID adds
-// acc + bias into them, F32 writes acc + bias.
+// acc + bias into them, F32 writes acc + bias. With ln_out set (PATCH / RESID, whose
+// tile holds whole rows) the new residual rows go back into the staging tile and are
+// layer-normalized into the next GEMM's operand, the same arithmetic as k_vit_ln_op<kD>.
 template <int NC, int EPI>
-__device__ __forceinline__ void staged_epilogue(const EpiArgs& ea, int tile, int chunk, const float* __restrict__ stage) {
+__device__ __forceinline__ void staged_epilogue(const EpiArgs& ea, int tile, int chunk, float* __restrict__ stage) {
   constexpr int NV = NC / 4, SROW = NC + 4;
   const float* __restrict__ bias = ea.bias;
   float* __restrict__ x = ea.x;
 #pragma unroll 4
-  for (int idx = threadIdx.x; idx < 128 * NV; idx += 128) {
+  for (int idx = threadIdx.x; idx < 128 * NV; idx += kGemmThreads) {
     const int row = idx / NV, q = idx % NV;
     const int grow = tile * 128 + row;
     if (grow >= ea.rows) continue;
@@ -113,6 +120,7 @@ __device__ __forceinline__ void staged_epilogue(const EpiArgs& ea, int tile, int
         o = make_float4(a.x + b.x + p.x, a.y + b.y + p.y, a.z + b.z + p.z, a.w + b.w + p.w);
       }
       *reinterpret_cast<float4*>(x + (size_t)grow * kD + q * 4) = o;
+      if (ea.ln_out) *reinterpret_cast<float4*>(stage + row * SROW + q * 4) = o;
     } else if constexpr (EPI == EPI_RESID) {
       const float4 b = *reinterpret_cast<const float4*>(bias + col);
       float4* xp = reinterpret_cast<float4*>(x + (size_t)grow * kD + col);
@@ -122,10 +130,51 @@ __device__ __forceinline__ void staged_epilogue(const EpiArgs& ea, int tile, int
       o.z += a.z + b.z;
       o.w += a.w + b.w;
       *xp = o;
+      if (ea.ln_out) *reinterpret_cast<float4*>(stage + row * SROW + q * 4) = o;
     } else {
       const float4 b = *reinterpret_cast<const float4*>(bias + col);
       *reinterpret_cast<float4*>(x + (size_t)grow * ea.n_total + col) =
           make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+    }
+  }
+  if constexpr (EPI == EPI_PATCH || EPI == EPI_RESID) {
+    static_assert(NC == kD, "row LayerNorm needs whole rows");
+    if (!ea.ln_out) return;
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int row = warp; row < 128; row += kGemmThreads / 32) {
+      const int grow = tile * 128 + row;
+      if (grow >= ea.rows) break;  // rows past the last stay as zero-initialized
+      float v[8];
+      float s = 0.f;
+      if (lane < kD / 8) {
+        const float4 lo = *reinterpret_cast<const float4*>(stage + row * SROW + lane * 8);
+        const float4 hi = *reinterpret_cast<const float4*>(stage + row * SROW + lane * 8 + 4);
+        v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
+        v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s += v[e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = 0.f;
+      }
+      const float mean = warp_sum(s) * (1.0f / kD);
+      float ss = 0.f;
+      if (lane < kD / 8) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = v[e] - mean;
+          ss += d * d;
+        }
+      }
+      const float rstd = rsqrtf(warp_sum(ss) * (1.0f / kD) + ea.ln_eps);
+      if (lane < kD / 8) {
+        float y[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = fmaf((v[e] - mean) * rstd, ea.ln_g[lane * 8 + e], ea.ln_b[lane * 8 + e]);
+        uint8_t* blk = reinterpret_cast<uint8_t*>(ea.ln_out) + ((size_t)tile * kHB + lane / 8) * kBlkBytes;
+        *reinterpret_cast<uint4*>(blk + sw128_off(row, (lane % 8) * 8)) = pack8(y);
+      }
     }
   }
 }
@@ -203,9 +252,10 @@ __device__ __forceinline__ void gemm_epilogue(const EpiArgs& ea, int tile, int c
 
 // C[tile, chunk] = A[tile] . W[chunk]^T, K = 64 * kb_n, streamed through `stages`
 // shared-memory slots (A block + W block each). Thread 0 issues the copies and the
-// MMAs; all four warps run the epilogue, one tile row per thread (its TMEM lane).
+// MMAs; all eight warps run the epilogue: warp w reads the TMEM lanes of rows
+// 32 (w % 4) .. + 31 and the accumulator columns of half w / 4.
 template <int NC, int EPI>
-__global__ void __launch_bounds__(128) k_vit_gemm(const __nv_bfloat16* __restrict__ A, int kb_n,
+__global__ void __launch_bounds__(kGemmThreads) k_vit_gemm(const __nv_bfloat16* __restrict__ A, int kb_n,
                                                   const __nv_bfloat16* __restrict__ W, int stages, EpiArgs ea,
                                                   uint32_t* status) {
   constexpr int STG = gemm_stage_bytes<NC>();
@@ -267,15 +317,16 @@ __global__ void __launch_bounds__(128) k_vit_gemm(const __nv_bfloat16* __restric
   }
   const bool ok = cta_wait_mma(done, status, slot + 1);
   tc_fence_after();
-  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+  const int row = tid & 127, cbeg = (tid >> 7) * (NC / 2), cend = cbeg + NC / 2;
   if constexpr (staged_epi(EPI)) {
     float* stage = reinterpret_cast<float*>(smem);  // operand slots are dead once the MMAs retired
     if (ok) {
 #pragma unroll 1
-      for (int c0 = 0; c0 < NC; c0 += 16) {
+      for (int c0 = cbeg; c0 < cend; c0 += 16) {
         float v[16];
         tmem_ld16(trow + c0, v);
-        float* dst = stage + tid * (NC + 4) + c0;
+        float* dst = stage + row * (NC + 4) + c0;
 #pragma unroll
         for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
       }
@@ -284,10 +335,10 @@ __global__ void __launch_bounds__(128) k_vit_gemm(const __nv_bfloat16* __restric
     if (ok) staged_epilogue<NC, EPI>(ea, tile, chunk, stage);
   } else if (ok) {
 #pragma unroll 1
-    for (int c0 = 0; c0 < NC; c0 += 16) {
+    for (int c0 = cbeg; c0 < cend; c0 += 16) {
       float v[16];
       tmem_ld16(trow + c0, v);
-      gemm_epilogue<NC, EPI>(ea, tile, chunk, tid, c0, v);
+      gemm_epilogue<NC, EPI>(ea, tile, chunk, row, c0, v);
     }
   }
   tc_fence_before();
@@ -447,27 +498,28 @@ struct AttnGeom {
 };
 
 inline size_t attn_smem(const AttnGeom& g) {
-  return 1024 + (size_t)g.q_tiles * kBlkBytes + (size_t)g.kv_rows * 128 + (size_t)g.kvb * 8192 +
-         (size_t)g.kvb * kBlkBytes + 64;
+  return 1024 + (size_t)kBlkBytes + (size_t)g.kv_rows * 128 + (size_t)g.kvb * 8192 + (size_t)g.kvb * kBlkBytes + 64;
 }
 
-// Softmax attention of one (head, image): all Q tiles, K and V^T are loaded once; per
-// query tile S = Q K^T (M 128, N <= 256 + a 16-column remainder) lands in TMEM, each
-// thread turns its row into bf16 probabilities in shared memory (masked past the last
-// token), and O = P V (N 64, K over the key blocks) lands in TMEM columns 384..447.
-// O / sum is written straight into the out-projection operand block of its row.
+// Softmax attention of one (query tile, head, image): the Q tile, K and V^T are loaded
+// once; S = Q K^T (M 128, N <= 256 + a 16-column remainder) lands in TMEM, each thread
+// turns its row into bf16 probabilities in shared memory (masked past the last token),
+// and O = P V (N 64, K over the key blocks) lands in TMEM columns 384..447. O / sum is
+// written straight into the out-projection operand block of its row. Warps without a
+// valid query row (the tail tile holds one token) skip the softmax: their P rows only
+// feed their own O rows, which are never written.
 __global__ void __launch_bounds__(128) k_vit_attn(const __nv_bfloat16* __restrict__ q,
                                                   const __nv_bfloat16* __restrict__ k,
                                                   const __nv_bfloat16* __restrict__ vt, AttnGeom ag,
                                                   __nv_bfloat16* __restrict__ attn_op, uint32_t* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  const int head = blockIdx.x, img = blockIdx.y;
+  const int head = blockIdx.x / ag.q_tiles, qt = blockIdx.x % ag.q_tiles, img = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5;
   const uint32_t qb = (uint32_t)ag.q_tiles * kBlkBytes, kbytes = (uint32_t)ag.kv_rows * 128,
                  vb = (uint32_t)ag.kvb * 8192, pb = (uint32_t)ag.kvb * kBlkBytes;
   uint8_t* sQ = smem;
-  uint8_t* sK = sQ + qb;
+  uint8_t* sK = sQ + kBlkBytes;
   uint8_t* sV = sK + kbytes;
   uint8_t* sP = sV + vb;
   uint64_t* bar = reinterpret_cast<uint64_t*>(sP + pb);  // [0] loads, [1] S, [2] O
@@ -476,8 +528,8 @@ __global__ void __launch_bounds__(128) k_vit_attn(const __nv_bfloat16* __restric
   if (tid == 0) {
     for (int i = 0; i < 3; ++i) mbar_init(&bar[i], 1);
     fence_mbar_init();
-    mbar_arrive_expect_tx(&bar[0], qb + kbytes + vb);
-    bulk_g2s(sQ, reinterpret_cast<const uint8_t*>(q) + hi * qb, qb, &bar[0]);
+    mbar_arrive_expect_tx(&bar[0], kBlkBytes + kbytes + vb);
+    bulk_g2s(sQ, reinterpret_cast<const uint8_t*>(q) + hi * qb + (size_t)qt * kBlkBytes, kBlkBytes, &bar[0]);
     bulk_g2s(sK, reinterpret_cast<const uint8_t*>(k) + hi * kbytes, kbytes, &bar[0]);
     bulk_g2s(sV, reinterpret_cast<const uint8_t*>(vt) + hi * vb, vb, &bar[0]);
   }
@@ -493,46 +545,49 @@ __global__ void __launch_bounds__(128) k_vit_attn(const __nv_bfloat16* __restric
   bool ok = cta_wait_mma(&bar[0], status, slot + 1);
   const int n1 = ag.ns < 256 ? ag.ns : 256, n2 = ag.ns - n1;
   const float c = 0.125f * 1.44269504088896341f;  // dim_head^-1/2 * log2(e)
-  for (int qt = 0; qt < ag.q_tiles && ok; ++qt) {
+  if (ok) {
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t a = smem_u32(sQ + qt * kBlkBytes);
+      const uint32_t a = smem_u32(sQ);
       umma_tile(tmem, a, kBlkBytes, smem_u32(sK), 0, 0, 1, idesc_bf16(128, n1), false);
       if (n2 > 0) umma_tile(tmem + 256, a, kBlkBytes, smem_u32(sK + 256 * 128), 0, 0, 1, idesc_bf16(128, n2), false);
       umma_commit(&bar[1]);
     }
-    ok = cta_wait_mma(&bar[1], status, slot + 1, (uint32_t)qt & 1u);
-    if (!ok) break;
+    ok = cta_wait_mma(&bar[1], status, slot + 1);
+  }
+  const int qi = qt * 128 + tid;
+  const bool valid = qi < ag.tokens;
+  float sum = 0.f;
+  if (ok) {
     tc_fence_after();
-    const int qi = qt * 128 + tid;
-    const bool valid = qi < ag.tokens;
-    float m = -INFINITY;
+    if (qt * 128 + warp * 32 < ag.tokens) {  // warp-uniform: some row of this warp is a token
+      float m = -INFINITY;
 #pragma unroll 1
-    for (int j0 = 0; j0 < ag.ns; j0 += 16) {
-      float v[16];
-      tmem_ld16(trow + j0, v);
+      for (int j0 = 0; j0 < ag.ns; j0 += 16) {
+        float v[16];
+        tmem_ld16(trow + j0, v);
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
-        if (j0 + i < ag.tokens) m = fmaxf(m, v[i]);
-    }
-    const float mc = m * c;
-    float sum = 0.f;
-#pragma unroll 1
-    for (int j0 = 0; j0 < ag.kvb * 64; j0 += 16) {
-      float v[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = 0.f;
-      if (j0 < ag.ns) tmem_ld16(trow + j0, v);
-      float pr[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float e = (valid && j0 + i < ag.tokens) ? exp2f(fmaf(v[i], c, -mc)) : 0.f;
-        pr[i] = __bfloat162float(__float2bfloat16_rn(e));  // the value the P V MMA sees
-        sum += pr[i];
+        for (int i = 0; i < 16; ++i)
+          if (j0 + i < ag.tokens) m = fmaxf(m, v[i]);
       }
-      uint8_t* blk = sP + (j0 / 64) * kBlkBytes;
-      *reinterpret_cast<uint4*>(blk + sw128_off(tid, j0 % 64)) = pack8(pr);
-      *reinterpret_cast<uint4*>(blk + sw128_off(tid, j0 % 64 + 8)) = pack8(pr + 8);
+      const float mc = m * c;
+#pragma unroll 1
+      for (int j0 = 0; j0 < ag.kvb * 64; j0 += 16) {
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = 0.f;
+        if (j0 < ag.ns) tmem_ld16(trow + j0, v);
+        float pr[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float e = (valid && j0 + i < ag.tokens) ? exp2f(fmaf(v[i], c, -mc)) : 0.f;
+          pr[i] = __bfloat162float(__float2bfloat16_rn(e));  // the value the P V MMA sees
+          sum += pr[i];
+        }
+        uint8_t* blk = sP + (j0 / 64) * kBlkBytes;
+        *reinterpret_cast<uint4*>(blk + sw128_off(tid, j0 % 64)) = pack8(pr);
+        *reinterpret_cast<uint4*>(blk + sw128_off(tid, j0 % 64 + 8)) = pack8(pr + 8);
+      }
     }
     fence_async_smem();
     tc_fence_before();
@@ -542,8 +597,9 @@ __global__ void __launch_bounds__(128) k_vit_attn(const __nv_bfloat16* __restric
       umma_tile(tmem + 384, smem_u32(sP), kBlkBytes, smem_u32(sV), 8192, 0, ag.kvb, idesc_bf16(128, 64), false);
       umma_commit(&bar[2]);
     }
-    ok = cta_wait_mma(&bar[2], status, slot + 1, (uint32_t)qt & 1u);
-    if (!ok) break;
+    ok = cta_wait_mma(&bar[2], status, slot + 1);
+  }
+  if (ok) {
     tc_fence_after();
     float o[64];
     tmem_ld_cols<64>(trow + 384, o);
@@ -556,8 +612,6 @@ __global__ void __launch_bounds__(128) k_vit_attn(const __nv_bfloat16* __restric
 #pragma unroll
       for (int d0 = 0; d0 < 64; d0 += 8) *reinterpret_cast<uint4*>(dst + sw128_off(grow % 128, d0)) = pack8(o + d0);
     }
-    tc_fence_before();
-    __syncthreads();
   }
   tc_fence_before();
   __syncthreads();
@@ -711,7 +765,8 @@ template <int NC, int EPI>
 void launch_gemm(const __nv_bfloat16* A, int kb_n, const __nv_bfloat16* W, int tiles, int chunks, const EpiArgs& ea,
                  uint32_t* status, cudaStream_t st) {
   const int stages = kb_n < kMaxStages ? kb_n : kMaxStages;
-  k_vit_gemm<NC, EPI><<<dim3(tiles, chunks), 128, gemm_smem<NC>(stages), st>>>(A, kb_n, W, stages, ea, status);
+  k_vit_gemm<NC, EPI><<<dim3(tiles, chunks), kGemmThreads, gemm_smem<NC>(stages), st>>>(A, kb_n, W, stages, ea,
+                                                                                      status);
 }
 
 template <int C>
@@ -983,25 +1038,33 @@ lewm_status lewm_encode(lewm_encoder* e, const float* pixels, int32_t n_images, 
   ea.q_rows = g.q_tiles * 128;
   ea.kv_rows = g.kv_rows;
   ea.x = e->x;
-  ea.bias = e->b_patch;
-  ea.pos = e->pos;
-  ea.cls = e->cls;
-  launch_gemm<192, EPI_PATCH>(e->patch_a, g.kbp, e->w_patch, mt, 1, ea, e->d_status, st);
+  ea.ln_eps = eps;
+  EpiArgs pe = ea;
+  pe.bias = e->b_patch;
+  pe.pos = e->pos;
+  pe.cls = e->cls;
+  pe.ln_g = e->ln1_g[0];  // layer 0's first LayerNorm, fused
+  pe.ln_b = e->ln1_b[0];
+  pe.ln_out = e->ln_a;
+  launch_gemm<192, EPI_PATCH>(e->patch_a, g.kbp, e->w_patch, mt, 1, pe, e->d_status, st);
   const AttnGeom ag{g.tokens, g.ns, g.q_tiles, g.kv_rows, g.kvb};
   const size_t asm_bytes = attn_smem(ag);
   for (int l = 0; l < d.depth; ++l) {
-    launch_ln<kD>(e->x, 1, rows, mt * 128, eps, e->ln1_g[l], e->ln1_b[l], 0, e->ln_a, st);
+    // ln_a holds LN_before(x) of layer l, written by the previous residual epilogue.
     EpiArgs qa = ea;
     qa.bias = e->b_qkv[l];
     qa.q = e->q;
     qa.k = e->k;
     qa.vt = e->vt;
     launch_gemm<192, EPI_QKV>(e->ln_a, kHB, e->w_qkv[l], mt, 3, qa, e->d_status, st);
-    k_vit_attn<<<dim3(kHB, n_images), 128, asm_bytes, st>>>(e->q, e->k, e->vt, ag, e->attn_a, e->d_status);
+    k_vit_attn<<<dim3(g.q_tiles * kHB, n_images), 128, asm_bytes, st>>>(e->q, e->k, e->vt, ag, e->attn_a,
+                                                                        e->d_status);
     EpiArgs ra = ea;
     ra.bias = e->b_out[l];
+    ra.ln_g = e->ln2_g[l];  // LN_after of this layer, fused
+    ra.ln_b = e->ln2_b[l];
+    ra.ln_out = e->ln_a;
     launch_gemm<192, EPI_RESID>(e->attn_a, kHB, e->w_out[l], mt, 1, ra, e->d_status, st);
-    launch_ln<kD>(e->x, 1, rows, mt * 128, eps, e->ln2_g[l], e->ln2_b[l], 0, e->ln_a, st);
     EpiArgs ha = ea;
     ha.bias = e->b_fc1[l];
     ha.scale = nullptr;
@@ -1013,6 +1076,11 @@ lewm_status lewm_encode(lewm_encoder* e, const float* pixels, int32_t n_images, 
       launch_gemm<192, EPI_GELU_OP>(e->ln_a, kHB, e->w_fc1[l], mt, d.mlp_dim / 192, ha, e->d_status, st);
     EpiArgs fa = ea;
     fa.bias = e->b_fc2[l];
+    if (l + 1 < d.depth) {  // LN_before of the next layer, fused
+      fa.ln_g = e->ln1_g[l + 1];
+      fa.ln_b = e->ln1_b[l + 1];
+      fa.ln_out = e->ln_a;
+    }
     launch_gemm<192, EPI_RESID>(e->h_a, d.mlp_dim / 64, e->w_fc2[l], mt, 1, fa, e->d_status, st);
   }
   // Final LayerNorm of the CLS rows only (row image * tokens), then the projector.

@@ -161,7 +161,7 @@ def encoder_flops(desc: EncoderDesc) -> float:
 
 def encoder_launches(desc: EncoderDesc) -> int:
     """Kernel launches of one ``lewm_encode`` call."""
-    return 2 + 7 * desc.depth + 1 + (3 if desc.proj_norm == "layernorm" else 2)
+    return 2 + 5 * desc.depth + 1 + (3 if desc.proj_norm == "layernorm" else 2)
 
 
 def weight_count(desc: EncoderDesc) -> int:
