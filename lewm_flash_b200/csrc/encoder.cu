@@ -101,6 +101,36 @@ __device__ __forceinline__ void staged_epilogue(const EpiArgs& ea, int tile, int
   constexpr int NV = NC / 4, SROW = NC + 4;
   const float* __restrict__ bias = ea.bias;
   float* __restrict__ x = ea.x;
+  if constexpr (EPI == EPI_RESID) {
+    // All of this thread's residual float4s are loaded before any is written back, so
+    // the loads overlap instead of forming a chain of memory round trips.
+    constexpr int PER = 128 * NV / kGemmThreads;
+    static_assert(128 * NV % kGemmThreads == 0, "residual float4s per thread");
+    float4 xa[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int idx = threadIdx.x + i * kGemmThreads, row = idx / NV, q = idx % NV;
+      const int grow = tile * 128 + row;
+      xa[i] = grow < ea.rows ? *reinterpret_cast<const float4*>(x + (size_t)grow * kD + chunk * NC + q * 4)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int idx = threadIdx.x + i * kGemmThreads, row = idx / NV, q = idx % NV;
+      const int grow = tile * 128 + row;
+      if (grow >= ea.rows) continue;
+      const float4 a = *reinterpret_cast<const float4*>(stage + row * SROW + q * 4);
+      const int col = chunk * NC + q * 4;
+      const float4 b = *reinterpret_cast<const float4*>(bias + col);
+      float4 o = xa[i];
+      o.x += a.x + b.x;
+      o.y += a.y + b.y;
+      o.z += a.z + b.z;
+      o.w += a.w + b.w;
+      *reinterpret_cast<float4*>(x + (size_t)grow * kD + col) = o;
+      if (ea.ln_out) *reinterpret_cast<float4*>(stage + row * SROW + q * 4) = o;
+    }
+  } else
 #pragma unroll 4
   for (int idx = threadIdx.x; idx < 128 * NV; idx += kGemmThreads) {
     const int row = idx / NV, q = idx % NV;
@@ -121,16 +151,6 @@ __device__ __forceinline__ void staged_epilogue(const EpiArgs& ea, int tile, int
       }
       *reinterpret_cast<float4*>(x + (size_t)grow * kD + q * 4) = o;
       if (ea.ln_out) *reinterpret_cast<float4*>(stage + row * SROW + q * 4) = o;
-    } else if constexpr (EPI == EPI_RESID) {
-      const float4 b = *reinterpret_cast<const float4*>(bias + col);
-      float4* xp = reinterpret_cast<float4*>(x + (size_t)grow * kD + col);
-      float4 o = *xp;
-      o.x += a.x + b.x;
-      o.y += a.y + b.y;
-      o.z += a.z + b.z;
-      o.w += a.w + b.w;
-      *xp = o;
-      if (ea.ln_out) *reinterpret_cast<float4*>(stage + row * SROW + q * 4) = o;
     } else {
       const float4 b = *reinterpret_cast<const float4*>(bias + col);
       *reinterpret_cast<float4*>(x + (size_t)grow * ea.n_total + col) =
@@ -142,36 +162,50 @@ __device__ __forceinline__ void staged_epilogue(const EpiArgs& ea, int tile, int
     if (!ea.ln_out) return;
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int row = warp; row < 128; row += kGemmThreads / 32) {
-      const int grow = tile * 128 + row;
-      if (grow >= ea.rows) break;  // rows past the last stay as zero-initialized
-      float v[8];
-      float s = 0.f;
-      if (lane < kD / 8) {
-        const float4 lo = *reinterpret_cast<const float4*>(stage + row * SROW + lane * 8);
-        const float4 hi = *reinterpret_cast<const float4*>(stage + row * SROW + lane * 8 + 4);
-        v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
-        v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
+    constexpr int WARPS = kGemmThreads / 32, U = 4;  // rows in flight per warp
+    for (int r0 = warp; r0 < 128; r0 += WARPS * U) {
+      float v[U][8], mean[U], rstd[U], s[U], ss[U];
+      bool live[U];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) s += v[e];
-      } else {
+      for (int u = 0; u < U; ++u) {
+        const int row = r0 + u * WARPS;
+        live[u] = row < 128 && tile * 128 + row < ea.rows;  // rows past the last stay zero
+        s[u] = 0.f;
+        if (live[u] && lane < kD / 8) {
+          const float4 lo = *reinterpret_cast<const float4*>(stage + row * SROW + lane * 8);
+          const float4 hi = *reinterpret_cast<const float4*>(stage + row * SROW + lane * 8 + 4);
+          v[u][0] = lo.x; v[u][1] = lo.y; v[u][2] = lo.z; v[u][3] = lo.w;
+          v[u][4] = hi.x; v[u][5] = hi.y; v[u][6] = hi.z; v[u][7] = hi.w;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = 0.f;
-      }
-      const float mean = warp_sum(s) * (1.0f / kD);
-      float ss = 0.f;
-      if (lane < kD / 8) {
+          for (int e = 0; e < 8; ++e) s[u] += v[u][e];
+        } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float d = v[e] - mean;
-          ss += d * d;
+          for (int e = 0; e < 8; ++e) v[u][e] = 0.f;
         }
       }
-      const float rstd = rsqrtf(warp_sum(ss) * (1.0f / kD) + ea.ln_eps);
-      if (lane < kD / 8) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) mean[u] = warp_sum(s[u]) * (1.0f / kD);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        ss[u] = 0.f;
+        if (lane < kD / 8) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float d = v[u][e] - mean[u];
+            ss[u] += d * d;
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) rstd[u] = rsqrtf(warp_sum(ss[u]) * (1.0f / kD) + ea.ln_eps);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int row = r0 + u * WARPS;
+        if (!live[u] || lane >= kD / 8) continue;
         float y[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) y[e] = fmaf((v[e] - mean) * rstd, ea.ln_g[lane * 8 + e], ea.ln_b[lane * 8 + e]);
+        for (int e = 0; e < 8; ++e)
+          y[e] = fmaf((v[u][e] - mean[u]) * rstd[u], ea.ln_g[lane * 8 + e], ea.ln_b[lane * 8 + e]);
         uint8_t* blk = reinterpret_cast<uint8_t*>(ea.ln_out) + ((size_t)tile * kHB + lane / 8) * kBlkBytes;
         *reinterpret_cast<uint4*>(blk + sw128_off(row, (lane % 8) * 8)) = pack8(y);
       }
@@ -222,11 +256,16 @@ __device__ __forceinline__ void gemm_epilogue(const EpiArgs& ea, int tile, int c
       *reinterpret_cast<float4*>(xr + i) = make_float4(v[i] + b.x, v[i + 1] + b.y, v[i + 2] + b.z, v[i + 3] + b.w);
     }
   } else if constexpr (EPI == EPI_GELU_OP) {
+    float bb[16], sc[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float s = ea.scale ? ea.scale[col + i] : 1.0f;
-      v[i] = gelu_f(fmaf(v[i], s, ea.bias[col + i]));
+    for (int i = 0; i < 16; i += 4) {
+      const float4 b4 = *reinterpret_cast<const float4*>(ea.bias + col + i);
+      const float4 s4 = ea.scale ? *reinterpret_cast<const float4*>(ea.scale + col + i) : make_float4(1.f, 1.f, 1.f, 1.f);
+      bb[i] = b4.x; bb[i + 1] = b4.y; bb[i + 2] = b4.z; bb[i + 3] = b4.w;
+      sc[i] = s4.x; sc[i + 1] = s4.y; sc[i + 2] = s4.z; sc[i + 3] = s4.w;
     }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = gelu_f(fmaf(v[i], sc[i], bb[i]));
     uint8_t* blk = reinterpret_cast<uint8_t*>(ea.op) + ((size_t)tile * (ea.n_total / 64) + col / 64) * kBlkBytes;
     *reinterpret_cast<uint4*>(blk + sw128_off(r, col % 64)) = pack8(v);
     *reinterpret_cast<uint4*>(blk + sw128_off(r, col % 64 + 8)) = pack8(v + 8);
@@ -497,33 +536,41 @@ struct AttnGeom {
   int kvb;       // 64-key blocks of P and V^T
 };
 
+constexpr int kAttnThreads = 256;  // two warpgroups split each row's key columns
+constexpr int kAttnSplit = 144;    // first key column of the second warpgroup (multiple of 16)
+
 inline size_t attn_smem(const AttnGeom& g) {
-  return 1024 + (size_t)kBlkBytes + (size_t)g.kv_rows * 128 + (size_t)g.kvb * 8192 + (size_t)g.kvb * kBlkBytes + 64;
+  return 1024 + (size_t)kBlkBytes + (size_t)g.kv_rows * 128 + (size_t)g.kvb * 8192 + (size_t)g.kvb * kBlkBytes +
+         4 * 128 * 4 + 64;
 }
 
 // Softmax attention of one (query tile, head, image): the Q tile, K and V^T are loaded
-// once; S = Q K^T (M 128, N <= 256 + a 16-column remainder) lands in TMEM, each thread
-// turns its row into bf16 probabilities in shared memory (masked past the last token),
-// and O = P V (N 64, K over the key blocks) lands in TMEM columns 384..447. O / sum is
-// written straight into the out-projection operand block of its row. Warps without a
-// valid query row (the tail tile holds one token) skip the softmax: their P rows only
-// feed their own O rows, which are never written.
-__global__ void __launch_bounds__(128) k_vit_attn(const __nv_bfloat16* __restrict__ q,
-                                                  const __nv_bfloat16* __restrict__ k,
-                                                  const __nv_bfloat16* __restrict__ vt, AttnGeom ag,
-                                                  __nv_bfloat16* __restrict__ attn_op, uint32_t* status) {
+// once; S = Q K^T (M 128, N <= 256 + a 16-column remainder) lands in TMEM. Warpgroup g
+// (warps 4g .. 4g + 3, TMEM lanes by warp % 4) owns key columns [0, 144) or [144, end):
+// each finds its part of the row maximum, the two parts are exchanged through shared
+// memory, and each writes its keys' bf16 probabilities into P (masked past the last
+// token) and a partial row sum. O = P V (N 64, K over the key blocks) lands in TMEM
+// columns 384..447; each warpgroup scales 32 of its columns by 1 / (sum0 + sum1) and
+// writes them into the out-projection operand block of the row. Warps without a valid
+// query row (the tail tile holds one token) skip the softmax: their P rows only feed
+// their own O rows, which are never written.
+__global__ void __launch_bounds__(kAttnThreads) k_vit_attn(const __nv_bfloat16* __restrict__ q,
+                                                           const __nv_bfloat16* __restrict__ k,
+                                                           const __nv_bfloat16* __restrict__ vt, AttnGeom ag,
+                                                           __nv_bfloat16* __restrict__ attn_op, uint32_t* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const int head = blockIdx.x / ag.q_tiles, qt = blockIdx.x % ag.q_tiles, img = blockIdx.y;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, wg = warp >> 2, row = tid & 127;
   const uint32_t qb = (uint32_t)ag.q_tiles * kBlkBytes, kbytes = (uint32_t)ag.kv_rows * 128,
                  vb = (uint32_t)ag.kvb * 8192, pb = (uint32_t)ag.kvb * kBlkBytes;
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + kBlkBytes;
   uint8_t* sV = sK + kbytes;
   uint8_t* sP = sV + vb;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sP + pb);  // [0] loads, [1] S, [2] O
-  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 3);  // [0] TMEM base, [1] wait flag
+  float* red = reinterpret_cast<float*>(sP + pb);  // [0..1][128] partial max, [2..3][128] partial sum
+  uint64_t* bar = reinterpret_cast<uint64_t*>(red + 4 * 128);  // [0] loads, [1] S, [2] O
+  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 3);        // [0] TMEM base, [1] wait flag
   const size_t hi = (size_t)img * kHB + head;
   if (tid == 0) {
     for (int i = 0; i < 3; ++i) mbar_init(&bar[i], 1);
@@ -541,7 +588,7 @@ __global__ void __launch_bounds__(128) k_vit_attn(const __nv_bfloat16* __restric
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = slot[0];
-  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);
   bool ok = cta_wait_mma(&bar[0], status, slot + 1);
   const int n1 = ag.ns < 256 ? ag.ns : 256, n2 = ag.ns - n1;
   const float c = 0.125f * 1.44269504088896341f;  // dim_head^-1/2 * log2(e)
@@ -555,28 +602,37 @@ __global__ void __launch_bounds__(128) k_vit_attn(const __nv_bfloat16* __restric
     }
     ok = cta_wait_mma(&bar[1], status, slot + 1);
   }
-  const int qi = qt * 128 + tid;
+  const int qi = qt * 128 + row;
   const bool valid = qi < ag.tokens;
-  float sum = 0.f;
+  const bool warp_rows = qt * 128 + (warp & 3) * 32 < ag.tokens;  // warp-uniform
+  // This warpgroup's S columns [s_beg, s_end) and P key columns [p_beg, p_end).
+  const int s_beg = wg == 0 ? 0 : kAttnSplit, s_end = wg == 0 ? min(kAttnSplit, ag.ns) : ag.ns;
+  const int p_beg = s_beg, p_end = wg == 0 ? min(kAttnSplit, ag.kvb * 64) : ag.kvb * 64;
   if (ok) {
     tc_fence_after();
-    if (qt * 128 + warp * 32 < ag.tokens) {  // warp-uniform: some row of this warp is a token
-      float m = -INFINITY;
+    float m = -INFINITY;
+    if (warp_rows) {
 #pragma unroll 1
-      for (int j0 = 0; j0 < ag.ns; j0 += 16) {
+      for (int j0 = s_beg; j0 < s_end; j0 += 16) {
         float v[16];
         tmem_ld16(trow + j0, v);
 #pragma unroll
         for (int i = 0; i < 16; ++i)
           if (j0 + i < ag.tokens) m = fmaxf(m, v[i]);
       }
-      const float mc = m * c;
+    }
+    red[wg * 128 + row] = m;
+    __syncthreads();
+    m = fmaxf(red[row], red[128 + row]);
+    const float mc = m * c;
+    float sum = 0.f;
+    if (warp_rows) {
 #pragma unroll 1
-      for (int j0 = 0; j0 < ag.kvb * 64; j0 += 16) {
+      for (int j0 = p_beg; j0 < p_end; j0 += 16) {
         float v[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = 0.f;
-        if (j0 < ag.ns) tmem_ld16(trow + j0, v);
+        if (j0 < s_end) tmem_ld16(trow + j0, v);
         float pr[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -585,10 +641,11 @@ __global__ void __launch_bounds__(128) k_vit_attn(const __nv_bfloat16* __restric
           sum += pr[i];
         }
         uint8_t* blk = sP + (j0 / 64) * kBlkBytes;
-        *reinterpret_cast<uint4*>(blk + sw128_off(tid, j0 % 64)) = pack8(pr);
-        *reinterpret_cast<uint4*>(blk + sw128_off(tid, j0 % 64 + 8)) = pack8(pr + 8);
+        *reinterpret_cast<uint4*>(blk + sw128_off(row, j0 % 64)) = pack8(pr);
+        *reinterpret_cast<uint4*>(blk + sw128_off(row, j0 % 64 + 8)) = pack8(pr + 8);
       }
     }
+    red[256 + wg * 128 + row] = sum;
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -601,16 +658,17 @@ __global__ void __launch_bounds__(128) k_vit_attn(const __nv_bfloat16* __restric
   }
   if (ok) {
     tc_fence_after();
-    float o[64];
-    tmem_ld_cols<64>(trow + 384, o);
+    float o[32];
+    tmem_ld_cols<32>(trow + 384 + wg * 32, o);
     if (valid) {
-      const float inv = 1.0f / sum;
+      const float inv = 1.0f / (red[256 + row] + red[384 + row]);
 #pragma unroll
-      for (int d = 0; d < 64; ++d) o[d] *= inv;
+      for (int d = 0; d < 32; ++d) o[d] *= inv;
       const int grow = img * ag.tokens + qi;
       uint8_t* dst = reinterpret_cast<uint8_t*>(attn_op) + ((size_t)(grow / 128) * kHB + head) * kBlkBytes;
 #pragma unroll
-      for (int d0 = 0; d0 < 64; d0 += 8) *reinterpret_cast<uint4*>(dst + sw128_off(grow % 128, d0)) = pack8(o + d0);
+      for (int d0 = 0; d0 < 32; d0 += 8)
+        *reinterpret_cast<uint4*>(dst + sw128_off(grow % 128, wg * 32 + d0)) = pack8(o + d0);
     }
   }
   tc_fence_before();
@@ -764,7 +822,10 @@ cudaError_t set_gemm_smem() {
 template <int NC, int EPI>
 void launch_gemm(const __nv_bfloat16* A, int kb_n, const __nv_bfloat16* W, int tiles, int chunks, const EpiArgs& ea,
                  uint32_t* status, cudaStream_t st) {
-  const int stages = kb_n < kMaxStages ? kb_n : kMaxStages;
+  // Per-thread epilogues need no staging tile: two operand slots keep two CTAs (and
+  // 2 x 256 TMEM columns) on an SM, so one CTA's epilogue overlaps the other's loads.
+  const int cap = staged_epi(EPI) ? kMaxStages : 2;
+  const int stages = kb_n < cap ? kb_n : cap;
   k_vit_gemm<NC, EPI><<<dim3(tiles, chunks), kGemmThreads, gemm_smem<NC>(stages), st>>>(A, kb_n, W, stages, ea,
                                                                                       status);
 }
@@ -966,8 +1027,11 @@ lewm_status lewm_encoder_create(lewm_encoder** out, const lewm_encoder_desc* des
     if (ce == cudaSuccess) ce = set_gemm_smem<256, EPI_F32>();
     if (ce == cudaSuccess) ce = set_gemm_smem<192, EPI_F32>();
     if (ce == cudaSuccess) {
-      AttnGeom ag{g.tokens, g.ns, g.q_tiles, g.kv_rows, g.kvb};
-      ce = cudaFuncSetAttribute(k_vit_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(ag));
+      // The attribute is per function: size it for the largest supported geometry so an
+      // encoder created later with fewer tokens does not lower it under this one.
+      const int ns_max = (kMaxTok + 15) / 16 * 16, kvb_max = (ns_max + 63) / 64;
+      const AttnGeom big{kMaxTok, ns_max, (kMaxTok + 127) / 128, kvb_max * 64, kvb_max};
+      ce = cudaFuncSetAttribute(k_vit_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(big));
     }
     if (ce != cudaSuccess) {
       efail(nullptr, ce == cudaErrorMemoryAllocation ? LEWM_OUT_OF_MEMORY : LEWM_CUDA_ERROR, "encoder create: %s",
@@ -1057,8 +1121,8 @@ lewm_status lewm_encode(lewm_encoder* e, const float* pixels, int32_t n_images, 
     qa.k = e->k;
     qa.vt = e->vt;
     launch_gemm<192, EPI_QKV>(e->ln_a, kHB, e->w_qkv[l], mt, 3, qa, e->d_status, st);
-    k_vit_attn<<<dim3(g.q_tiles * kHB, n_images), 128, asm_bytes, st>>>(e->q, e->k, e->vt, ag, e->attn_a,
-                                                                        e->d_status);
+    k_vit_attn<<<dim3(g.q_tiles * kHB, n_images), kAttnThreads, asm_bytes, st>>>(e->q, e->k, e->vt, ag,
+                                                                                 e->attn_a, e->d_status);
     EpiArgs ra = ea;
     ra.bias = e->b_out[l];
     ra.ln_g = e->ln2_g[l];  // LN_after of this layer, fused
