@@ -79,16 +79,17 @@ __device__ __forceinline__ uint4 pack8(const float* v) {
 
 template <int NC>
 constexpr int gemm_stage_bytes() { return kBlkBytes + NC * 128; }
-// Operand slots, reused after the MMAs retire as the fp32 staging tile [128][NC + 4] of
-// the row-wise epilogues; the mbarriers sit after the larger of the two.
-template <int NC>
-__host__ __device__ constexpr int gemm_area(int stages) {
-  return stages * gemm_stage_bytes<NC>() > 128 * (NC + 4) * 4 ? stages * gemm_stage_bytes<NC>() : 128 * (NC + 4) * 4;
-}
-template <int NC>
-size_t gemm_smem(int stages) { return 1024 + (size_t)gemm_area<NC>(stages) + 128; }
-
 constexpr bool staged_epi(int epi) { return epi == EPI_PATCH || epi == EPI_RESID || epi == EPI_F32; }
+
+// Operand slots; the row-wise (staged) epilogues reuse them after the MMAs retire as the
+// fp32 staging tile [128][NC + 4]. The mbarriers sit after the larger of the two.
+template <int NC, int EPI>
+__host__ __device__ constexpr int gemm_area(int stages) {
+  return !staged_epi(EPI) || stages * gemm_stage_bytes<NC>() > 128 * (NC + 4) * 4 ? stages * gemm_stage_bytes<NC>()
+                                                                                  : 128 * (NC + 4) * 4;
+}
+template <int NC, int EPI>
+size_t gemm_smem(int stages) { return 1024 + (size_t)gemm_area<NC, EPI>(stages) + 128; }
 
 // Row-wise epilogues from the staging tile, consecutive threads on consecutive float4s of
 // a row (coalesced, and no thread re-reads a sector it has just written): PATCH writes
@@ -302,7 +303,7 @@ __global__ void __launch_bounds__(kGemmThreads) k_vit_gemm(const __nv_bfloat16* 
   static_assert(NC % 64 == 0 && NC <= 256, "N chunk");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + gemm_area<NC>(stages));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + gemm_area<NC, EPI>(stages));
   uint64_t* freed = full + kMaxStages;
   uint64_t* done = freed + kMaxStages;
   uint32_t* slot = reinterpret_cast<uint32_t*>(done + 1);  // [0] TMEM base, [1] wait flag
@@ -816,7 +817,7 @@ size_t weight_count(const lewm_encoder_desc& d) {
 template <int NC, int EPI>
 cudaError_t set_gemm_smem() {
   return cudaFuncSetAttribute(k_vit_gemm<NC, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              (int)gemm_smem<NC>(kMaxStages));
+                              (int)gemm_smem<NC, EPI>(kMaxStages));
 }
 
 template <int NC, int EPI>
@@ -826,7 +827,7 @@ void launch_gemm(const __nv_bfloat16* A, int kb_n, const __nv_bfloat16* W, int t
   // 2 x 256 TMEM columns) on an SM, so one CTA's epilogue overlaps the other's loads.
   const int cap = staged_epi(EPI) ? kMaxStages : 2;
   const int stages = kb_n < cap ? kb_n : cap;
-  k_vit_gemm<NC, EPI><<<dim3(tiles, chunks), kGemmThreads, gemm_smem<NC>(stages), st>>>(A, kb_n, W, stages, ea,
+  k_vit_gemm<NC, EPI><<<dim3(tiles, chunks), kGemmThreads, gemm_smem<NC, EPI>(stages), st>>>(A, kb_n, W, stages, ea,
                                                                                       status);
 }
 
