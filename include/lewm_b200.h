@@ -265,6 +265,16 @@ LEWM_API lewm_status lewm_encoder_create(lewm_encoder** out, const lewm_encoder_
 LEWM_API lewm_status lewm_encode(lewm_encoder* enc, const float* pixels, int32_t n_images, float* emb_out,
                                  void* stream);
 
+/* lewm_encode from raw uint8 frames [n_images][image_size][image_size][channels]
+ * (height, width, channel; device memory): each sample is normalized in the first
+ * kernel as (u * float32(1/255) - mean[c]) / std[c] (mean, std: HOST arrays of
+ * `channels` floats, channels <= 4), the arithmetic of the policy image transform
+ * ToDtype(float32, scale=True) + Normalize (lewm/eval.py:17-26) for frames already at
+ * image_size (its Resize is then the identity). Bit-identical to lewm_encode on the
+ * transformed float pixels, with a quarter of the input bytes. */
+LEWM_API lewm_status lewm_encode_u8(lewm_encoder* enc, const uint8_t* frames, int32_t n_images, const float* mean,
+                                    const float* std, float* emb_out, void* stream);
+
 /* Synchronize `stream`, then read and clear the encoder's device status word. */
 LEWM_API lewm_status lewm_encoder_sync_status(lewm_encoder* enc, void* stream);
 LEWM_API const char* lewm_encoder_last_error(const lewm_encoder* enc);

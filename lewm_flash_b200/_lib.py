@@ -96,6 +96,8 @@ SIGNATURES = {
     "lewm_encoder_create": (C.c_int, [C.POINTER(C.c_void_p), C.POINTER(EncoderDescC), C.c_void_p, C.c_size_t,
                                       C.c_int]),
     "lewm_encode": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p]),
+    "lewm_encode_u8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.POINTER(C.c_float), C.POINTER(C.c_float),
+                                 C.c_void_p, C.c_void_p]),
     "lewm_encoder_sync_status": (C.c_int, [C.c_void_p, C.c_void_p]),
     "lewm_encoder_last_error": (C.c_char_p, [C.c_void_p]),
     "lewm_encoder_destroy": (None, [C.c_void_p]),

@@ -529,6 +529,47 @@ __global__ void __launch_bounds__(256) k_vit_patch_op(const float* __restrict__ 
   *reinterpret_cast<uint4*>(blk + sw128_off(r % 128, (q % 8) * 8)) = pack8(v);
 }
 
+// Per-channel normalization of uint8 frames (at most 4 channels).
+struct FrameNorm {
+  float mean[4];
+  float stdv[4];
+};
+
+// Patch operand straight from uint8 frames [n][img][img][ch] (height, width, channel):
+// each sample becomes (u * float32(1/255) - mean[c]) / std[c], rounded after every
+// step (no contraction), the arithmetic of the policy's image transform ToDtype(float32,
+// scale=True) + Normalize (reference lewm/eval.py:17-26, torchvision v2), so this equals
+// k_vit_patch_op on the transformed float pixels bit for bit. Same row / chunk layout.
+__global__ void __launch_bounds__(256) k_vit_patch_op_u8(const uint8_t* __restrict__ frames, FrameNorm nm,
+                                                         int n_img, int img, int p, int ch, int tokens, int kbp,
+                                                         int total_rows, __nv_bfloat16* __restrict__ out) {
+  const int nchunk = kbp * 8;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)total_rows * nchunk) return;
+  const int r = (int)(idx / nchunk), q = (int)(idx % nchunk);
+  const int gw = img / p, pp2 = p * p, K = ch * pp2;
+  const int im = r / tokens, tok = r % tokens;
+  const bool valid = im < n_img && tok > 0;
+  const int py = valid ? (tok - 1) / gw : 0, px = valid ? (tok - 1) % gw : 0;
+  const float inv255 = __int_as_float(0x3b808081);  // float32 nearest to 1/255
+  float v[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int k = q * 8 + e;
+    float x = 0.f;
+    if (valid && k < K) {
+      const int c = k / pp2, rem = k % pp2, ky = rem / p, kx = rem % p;
+      const float u = (float)frames[(((size_t)im * img + (size_t)(py * p + ky)) * img + px * p + kx) * ch + c];
+      const float mu = c == 0 ? nm.mean[0] : c == 1 ? nm.mean[1] : c == 2 ? nm.mean[2] : nm.mean[3];
+      const float sd = c == 0 ? nm.stdv[0] : c == 1 ? nm.stdv[1] : c == 2 ? nm.stdv[2] : nm.stdv[3];
+      x = __fdiv_rn(__fsub_rn(__fmul_rn(u, inv255), mu), sd);
+    }
+    v[e] = x;
+  }
+  uint8_t* blk = reinterpret_cast<uint8_t*>(out) + ((size_t)(r / 128) * kbp + q / 8) * kBlkBytes;
+  *reinterpret_cast<uint4*>(blk + sw128_off(r % 128, (q % 8) * 8)) = pack8(v);
+}
+
 struct AttnGeom {
   int tokens;    // keys = queries per image
   int ns;        // tokens rounded up to 16: S columns
@@ -1076,11 +1117,17 @@ lewm_status lewm_encoder_create(lewm_encoder** out, const lewm_encoder_desc* des
   return LEWM_OK;
 }
 
-lewm_status lewm_encode(lewm_encoder* e, const float* pixels, int32_t n_images, float* emb_out, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Float pixels (pixels != null) or uint8 frames with their per-channel normalization.
+lewm_status encode_impl(lewm_encoder* e, const float* pixels, const uint8_t* frames, const FrameNorm& nm,
+                        int32_t n_images, float* emb_out, void* stream) {
   if (!e) return efail(nullptr, LEWM_INVALID_ARG, "encoder is NULL");
   if (n_images < 0) return efail(e, LEWM_INVALID_ARG, "n_images < 0");
   if (n_images == 0) return LEWM_OK;
-  if (!pixels || !emb_out) return efail(e, LEWM_INVALID_ARG, "pixels / emb_out is NULL");
+  if ((!pixels && !frames) || !emb_out) return efail(e, LEWM_INVALID_ARG, "pixels / emb_out is NULL");
   if ((reinterpret_cast<uintptr_t>(emb_out) & 15u) != 0)
     return efail(e, LEWM_INVALID_ARG, "emb_out must be 16-byte aligned");
   EncDeviceGuard guard(e->device);
@@ -1093,9 +1140,13 @@ lewm_status lewm_encode(lewm_encoder* e, const float* pixels, int32_t n_images, 
   const float eps = d.ln_eps;
   {
     const long long total = (long long)mt * 128 * g.kbp * 8;
-    k_vit_patch_op<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(pixels, n_images, d.image_size, d.patch_size,
-                                                                    d.channels, g.tokens, g.kbp, mt * 128,
-                                                                    e->patch_a);
+    const unsigned blocks = (unsigned)((total + 255) / 256);
+    if (pixels)
+      k_vit_patch_op<<<blocks, 256, 0, st>>>(pixels, n_images, d.image_size, d.patch_size, d.channels, g.tokens,
+                                             g.kbp, mt * 128, e->patch_a);
+    else
+      k_vit_patch_op_u8<<<blocks, 256, 0, st>>>(frames, nm, n_images, d.image_size, d.patch_size, d.channels,
+                                                g.tokens, g.kbp, mt * 128, e->patch_a);
   }
   EpiArgs ea{};
   ea.rows = rows;
@@ -1173,6 +1224,30 @@ lewm_status lewm_encode(lewm_encoder* e, const float* pixels, int32_t n_images, 
   launch_gemm<192, EPI_F32>(e->ph_a, d.proj_hidden / 64, e->w_p2, mi, 1, oa, e->d_status, st);
   ENC_CK(e, cudaGetLastError());
   return LEWM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+lewm_status lewm_encode(lewm_encoder* e, const float* pixels, int32_t n_images, float* emb_out, void* stream) {
+  if (!pixels && n_images > 0) return efail(e, LEWM_INVALID_ARG, "pixels is NULL");
+  return encode_impl(e, pixels, nullptr, FrameNorm{}, n_images, emb_out, stream);
+}
+
+lewm_status lewm_encode_u8(lewm_encoder* e, const uint8_t* frames, int32_t n_images, const float* mean,
+                           const float* stdv, float* emb_out, void* stream) {
+  if (!e) return efail(nullptr, LEWM_INVALID_ARG, "encoder is NULL");
+  if (e->desc.channels > 4) return efail(e, LEWM_UNSUPPORTED_SHAPE, "uint8 frames support at most 4 channels");
+  if (!mean || !stdv) return efail(e, LEWM_INVALID_ARG, "mean / std is NULL");
+  if (!frames && n_images > 0) return efail(e, LEWM_INVALID_ARG, "frames is NULL");
+  FrameNorm nm{};
+  for (int c = 0; c < e->desc.channels; ++c) {
+    if (!(stdv[c] != 0.f)) return efail(e, LEWM_INVALID_ARG, "std[%d] is zero", c);
+    nm.mean[c] = mean[c];
+    nm.stdv[c] = stdv[c];
+  }
+  return encode_impl(e, nullptr, frames, nm, n_images, emb_out, stream);
 }
 
 lewm_status lewm_encoder_sync_status(lewm_encoder* e, void* stream) {

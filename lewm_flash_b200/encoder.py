@@ -24,6 +24,9 @@ import torch
 from . import _lib
 
 NORMS = ("none", "layernorm", "batchnorm")
+# ImageNet statistics of the policy image transform (reference lewm/eval.py:17-26).
+IMAGENET_MEAN = (0.485, 0.456, 0.406)
+IMAGENET_STD = (0.229, 0.224, 0.225)
 
 
 @dataclass
@@ -211,6 +214,30 @@ class B200Encoder:
         stream = torch.cuda.current_stream(self.device).cuda_stream
         _lib.check_encoder(_lib.lib().lewm_encode(self._enc, C.c_void_p(pix.data_ptr()), n,
                                                   C.c_void_p(out.data_ptr()), C.c_void_p(stream)), self._enc)
+        return out
+
+    def encode_frames(self, frames: torch.Tensor, mean=IMAGENET_MEAN, std=IMAGENET_STD,
+                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Raw uint8 frames (N, H, W, C) -> embeddings: the policy image transform
+        (``ToImage``, ``ToDtype(float32, scale=True)``, ``Normalize``, ``Resize`` to the encoder
+        size; reference ``lewm/eval.py:17-26``) fused into the encoder's first kernel. Frames
+        must already be at the encoder size, where that ``Resize`` is the identity."""
+        d = self.desc
+        if frames.dtype != torch.uint8 or frames.ndim != 4 or tuple(frames.shape[1:]) != (
+                d.image_size, d.image_size, d.channels):
+            raise ValueError(f"frames must be uint8 (N, {d.image_size}, {d.image_size}, {d.channels}), "
+                             f"got {frames.dtype} {tuple(frames.shape)}")
+        if len(mean) != d.channels or len(std) != d.channels:
+            raise ValueError("mean / std need one value per channel")
+        fr = frames.to(self.device).contiguous()
+        n = fr.shape[0]
+        if out is None:
+            out = torch.empty(n, d.proj_out, device=self.device, dtype=torch.float32)
+        m = (C.c_float * d.channels)(*[float(v) for v in mean])
+        sd = (C.c_float * d.channels)(*[float(v) for v in std])
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check_encoder(_lib.lib().lewm_encode_u8(self._enc, C.c_void_p(fr.data_ptr()), n, m, sd,
+                                                     C.c_void_p(out.data_ptr()), C.c_void_p(stream)), self._enc)
         return out
 
     def sync(self) -> None:

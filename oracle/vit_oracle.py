@@ -143,6 +143,23 @@ def encode(vit, proj, desc, pixels: np.ndarray, operand_bf16: bool = False) -> n
     return projector(proj, desc, vit_cls(vit, desc, pixels, operand_bf16), operand_bf16)
 
 
+def img_transform(frames: np.ndarray, mean, std) -> np.ndarray:
+    """Policy image transform (reference ``lewm/eval.py:17-26``: torchvision v2 ``ToImage``,
+    ``ToDtype(float32, scale=True)``, ``Normalize``, ``Resize``) on uint8 frames (N, H, W, C)
+    already at the target size: (u * float32(1/255) - mean) / std per channel, rounded
+    after each float32 step, returned as (N, C, H, W)."""
+    u = np.asarray(frames, dtype=np.uint8).astype(F32).transpose(0, 3, 1, 2)
+    m = np.asarray(mean, dtype=F32).reshape(1, -1, 1, 1)
+    s = np.asarray(std, dtype=F32).reshape(1, -1, 1, 1)
+    return ((u * F32(1.0 / 255.0)) - m) / s
+
+
+def synthetic_frames(n: int, desc, seed: int) -> np.ndarray:
+    """Seeded uint8 frames (N, H, W, C) standing in for rendered observations."""
+    rng = np.random.default_rng(seed)
+    return rng.integers(0, 256, size=(n, desc.image_size, desc.image_size, desc.channels), dtype=np.uint8)
+
+
 def synthetic_pixels(n: int, desc, seed: int) -> np.ndarray:
     """Seeded stand-in for normalized observations: uint8 noise images through the
     ImageNet mean / std normalization the policy applies (values about -2.1 .. 2.6)."""

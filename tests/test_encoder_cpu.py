@@ -134,3 +134,19 @@ def test_desc_round_trips_through_json():
     desc = EncoderDesc(image_size=64, patch_size=16)
     assert EncoderDesc(**json.loads(json.dumps(asdict(desc)))) == desc
     assert desc.tokens == 17
+
+
+def test_img_transform_matches_torchvision_policy_transform():
+    """The oracle's frame normalization equals the reference transform bit for bit
+    (lewm/eval.py:17-26: ToImage, ToDtype(float32, scale=True), Normalize, Resize)."""
+    torch = pytest.importorskip("torch")
+    tv = pytest.importorskip("torchvision.transforms.v2")
+    from lewm_flash_b200.encoder import IMAGENET_MEAN, IMAGENET_STD
+
+    desc = EncoderDesc()
+    frames = vo.synthetic_frames(2, desc, 3)
+    tf = tv.Compose([tv.ToImage(), tv.ToDtype(torch.float32, scale=True),
+                     tv.Normalize(mean=list(IMAGENET_MEAN), std=list(IMAGENET_STD)), tv.Resize(size=desc.image_size)])
+    want = np.stack([tf(f).numpy() for f in frames])
+    got = vo.img_transform(frames, IMAGENET_MEAN, IMAGENET_STD)
+    np.testing.assert_array_equal(got, want)

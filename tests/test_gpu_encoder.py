@@ -123,3 +123,18 @@ def test_install_encoder_routes_model_encode():
     got = info["emb"].cpu().numpy()
     assert got.shape == (2, 2, desc.proj_out)
     assert rel(got.reshape(4, -1), vo.encode(vit, proj, desc, pix)) <= 2e-2
+
+
+def test_uint8_frames_equal_transformed_pixels_bits(full):
+    """lewm_encode_u8 (policy image transform fused into the first kernel) equals lewm_encode
+    on the oracle-transformed float pixels bit for bit, and rejects frames of another size."""
+    from lewm_flash_b200.encoder import IMAGENET_MEAN, IMAGENET_STD
+
+    desc, _, _, enc = full
+    frames = vo.synthetic_frames(3, desc, 14)
+    got = enc.encode_frames(torch.from_numpy(frames).cuda())
+    enc.sync()
+    want = run(enc, vo.img_transform(frames, IMAGENET_MEAN, IMAGENET_STD))
+    np.testing.assert_array_equal(got.cpu().numpy(), want)
+    with pytest.raises(ValueError):
+        enc.encode_frames(torch.zeros(1, 112, 112, 3, dtype=torch.uint8, device="cuda"))
