@@ -214,49 +214,15 @@ __device__ __forceinline__ void staged_epilogue(const EpiArgs& ea, int tile, int
   }
 }
 
-// Epilogue of 16 accumulator columns [c0, c0 + 16) of tile row r.
+// Per-thread epilogue of 16 accumulator columns [c0, c0 + 16) of tile row r, for the
+// epilogues that write bf16 operands (GELU_OP, QKV); the fp32 row-wise ones are staged.
 template <int NC, int EPI>
 __device__ __forceinline__ void gemm_epilogue(const EpiArgs& ea, int tile, int chunk, int r, int c0, float* v) {
+  static_assert(EPI == EPI_GELU_OP || EPI == EPI_QKV, "fp32 row epilogues go through staged_epilogue");
   const int grow = tile * 128 + r;
   if (grow >= ea.rows) return;
   const int col = chunk * NC + c0;  // first output column over all chunks
-  if constexpr (EPI == EPI_PATCH) {
-    const int tok = grow % ea.tokens;
-    float* xr = ea.x + (size_t)grow * kD + c0;
-    const float* pr = ea.pos + (size_t)tok * kD + c0;
-#pragma unroll
-    for (int i = 0; i < 16; i += 4) {
-      float4 o;
-      const float4 p = *reinterpret_cast<const float4*>(pr + i);
-      if (tok == 0) {
-        const float4 c = *reinterpret_cast<const float4*>(ea.cls + c0 + i);
-        o = make_float4(c.x + p.x, c.y + p.y, c.z + p.z, c.w + p.w);
-      } else {
-        const float4 b = *reinterpret_cast<const float4*>(ea.bias + c0 + i);
-        o = make_float4(v[i] + b.x + p.x, v[i + 1] + b.y + p.y, v[i + 2] + b.z + p.z, v[i + 3] + b.w + p.w);
-      }
-      *reinterpret_cast<float4*>(xr + i) = o;
-    }
-  } else if constexpr (EPI == EPI_RESID) {
-    float* xr = ea.x + (size_t)grow * kD + c0;
-#pragma unroll
-    for (int i = 0; i < 16; i += 4) {
-      float4 o = *reinterpret_cast<float4*>(xr + i);
-      const float4 b = *reinterpret_cast<const float4*>(ea.bias + col + i);
-      o.x += v[i] + b.x;
-      o.y += v[i + 1] + b.y;
-      o.z += v[i + 2] + b.z;
-      o.w += v[i + 3] + b.w;
-      *reinterpret_cast<float4*>(xr + i) = o;
-    }
-  } else if constexpr (EPI == EPI_F32) {
-    float* xr = ea.x + (size_t)grow * ea.n_total + col;
-#pragma unroll
-    for (int i = 0; i < 16; i += 4) {
-      const float4 b = *reinterpret_cast<const float4*>(ea.bias + col + i);
-      *reinterpret_cast<float4*>(xr + i) = make_float4(v[i] + b.x, v[i + 1] + b.y, v[i + 2] + b.z, v[i + 3] + b.w);
-    }
-  } else if constexpr (EPI == EPI_GELU_OP) {
+  if constexpr (EPI == EPI_GELU_OP) {
     float bb[16], sc[16];
 #pragma unroll
     for (int i = 0; i < 16; i += 4) {
