@@ -6,12 +6,15 @@ Public surface (drop-ins for the reference antoinenguyen27/lewm-flash):
 * ``B200CEMSolver`` -- ``lewm.solvers.cem_exact.CEMExactSolver``
 * ``run_static_icem_chain`` -- ``lewm.solvers.icem_static_compile.run_static_icem_chain``
 * ``B200ModelCost`` / ``install_model_cost`` -- ``JEPA.get_cost_from_embeddings``
+* ``B200Encoder`` / ``install_encoder`` -- ``JEPA.encode`` (ViT CLS row + projector), and
+  ``B200Encoder.encode_frames`` for raw uint8 frames (the policy image transform fused)
 * ``Runtime`` -- the C ABI (``include/lewm_b200.h``) on one GPU
 
 The compute path is ``liblewm_b200.so`` (sm_100a CUDA); there is no CPU
 fallback.
 """
 
+from .encoder import B200Encoder, EncoderDesc, install_encoder
 from .model import ModelDesc, STRESS_DESC, synthetic_state_dict
 from .runtime import PlanOptions, Runtime, coloring_matrix, sample_counts
 from .solver import (B200CEMSolver, B200ICEMSolver, B200ModelCost, install_model_cost, prepare_init_action,
@@ -20,5 +23,5 @@ from .solver import (B200CEMSolver, B200ICEMSolver, B200ModelCost, install_model
 __all__ = [
     "ModelDesc", "STRESS_DESC", "synthetic_state_dict", "PlanOptions", "Runtime", "coloring_matrix", "sample_counts",
     "B200ICEMSolver", "B200CEMSolver", "B200ModelCost", "install_model_cost", "prepare_init_action",
-    "run_static_icem_chain",
+    "run_static_icem_chain", "B200Encoder", "EncoderDesc", "install_encoder",
 ]
