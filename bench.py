@@ -360,7 +360,27 @@ def encoder_case(n_img: int, repeat: int) -> int:
         b.record()
         enc.sync()
         ms.append(a.elapsed_time(b))
-    print(json.dumps({"case": "encoder", "images": n_img, "ms": ms, "emb0": float(out[0, 0])}))
+    frames = torch.as_tensor(np.random.default_rng(18).integers(0, 256, size=(n_img, 224, 224, 3), dtype=np.uint8),
+                             device=dev)
+    host_f32 = pix.cpu().pin_memory()
+    host_u8 = frames.cpu().pin_memory()
+
+    def ev_ms(fn):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        enc.sync()
+        return a.elapsed_time(b)
+
+    phases = {}
+    for name, fn in (("encode_frames_u8", lambda: enc.encode_frames(frames)),
+                     ("h2d_f32", lambda: host_f32.to(dev, non_blocking=True)),
+                     ("h2d_u8", lambda: host_u8.to(dev, non_blocking=True))):
+        ev_ms(fn)
+        phases[name] = [ev_ms(fn) for _ in range(repeat)]
+    print(json.dumps({"case": "encoder", "images": n_img, "ms": ms, "emb0": float(out[0, 0]), "phases_ms": phases}))
     return 0
 
 
