@@ -69,6 +69,19 @@ def test_encoder_matches_reference_fixture(name):
     assert rel(got, vo.encode(vit, proj, desc, pix, operand_bf16=True)) <= 1e-2
 
 
+@pytest.mark.parametrize("image_size,patch_size", [(224, 16), (112, 14)])
+def test_attention_geometries(image_size, patch_size):
+    """197 tokens (two query tiles, one S MMA of N 208, the second warpgroup on keys 144..207)
+    and 65 tokens (one query tile, N 80) against the oracle."""
+    desc = EncoderDesc(image_size=image_size, patch_size=patch_size, depth=2, proj_hidden=512)
+    vit, proj = synthetic_weights(desc, 15)
+    enc = B200Encoder(desc, flat_weights(vit, proj, desc))
+    pix = vo.synthetic_pixels(3, desc, 16)
+    got = run(enc, pix)
+    assert rel(got, vo.encode(vit, proj, desc, pix, operand_bf16=True)) <= 1e-2
+    assert rel(got, vo.encode(vit, proj, desc, pix)) <= 2e-2
+
+
 def test_more_than_one_tile_of_images_and_workspace_growth():
     """130 images: the CLS / projector GEMMs span two 128-row tiles; the workspace grows
     from a smaller batch and the results do not depend on the history of the encoder."""
