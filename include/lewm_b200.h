@@ -260,8 +260,9 @@ LEWM_API lewm_status lewm_encoder_create(lewm_encoder** out, const lewm_encoder_
 
 /* emb_out[n_images][proj_out] = projector(ViT(pixels)[:, 0]) for pixels
  * [n_images][channels][image_size][image_size] (already normalized, as JEPA.encode
- * receives them). Device pointers; emb_out 16-byte aligned. Asynchronous on
- * `stream`; grows the encoder's workspace on first use of a larger batch. */
+ * receives them). Device pointers; emb_out 16-byte aligned; n_images <= 65535.
+ * Asynchronous on `stream`; grows the encoder's workspace on first use of a larger
+ * batch. */
 LEWM_API lewm_status lewm_encode(lewm_encoder* enc, const float* pixels, int32_t n_images, float* emb_out,
                                  void* stream);
 

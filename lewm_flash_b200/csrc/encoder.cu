@@ -1094,6 +1094,8 @@ lewm_status encode_impl(lewm_encoder* e, const float* pixels, const uint8_t* fra
   if (n_images < 0) return efail(e, LEWM_INVALID_ARG, "n_images < 0");
   if (n_images == 0) return LEWM_OK;
   if ((!pixels && !frames) || !emb_out) return efail(e, LEWM_INVALID_ARG, "pixels / emb_out is NULL");
+  if (n_images > 65535)  // images are the attention grid's y dimension
+    return efail(e, LEWM_UNSUPPORTED_SHAPE, "at most 65535 images per call, got %d", n_images);
   if ((reinterpret_cast<uintptr_t>(emb_out) & 15u) != 0)
     return efail(e, LEWM_INVALID_ARG, "emb_out must be 16-byte aligned");
   EncDeviceGuard guard(e->device);
