@@ -163,7 +163,9 @@ LEWM_API lewm_status lewm_topk_refit(lewm_ctx* ctx, const float* costs, const fl
 /* Candidate sampling alone (tests / diagnostics): candidates of iteration
  * `iter` for the given mean/std, no elite injection. Reference
  * make_colored_noise (lewm/solvers/icem.py:185-250) + :523-527.
- * out (B,S,T,A). */
+ * mean/std (B,T,A), injected_noise (B,S,T,A) or NULL, out (B,S,T,A), with
+ * B = plan->n_envs, T = plan->horizon and A the context's model action_dim
+ * (the buffers are not self-describing: a caller must size them with that A). */
 LEWM_API lewm_status lewm_sample_candidates(lewm_ctx* ctx, const lewm_plan_desc* plan, int32_t S, int32_t iter,
                                    const float* mean, const float* std, const float* injected_noise,
                                    const float* action_low, const float* action_high, float* out, void* stream);

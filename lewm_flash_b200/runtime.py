@@ -283,6 +283,13 @@ class Runtime:
         m = _f32(mean, dev)
         s = _f32(std, dev)
         B, T, A = m.shape
+        # The kernel reads and writes the model's action dim per step: every tensor must match it.
+        if A != self.desc.action_dim:
+            raise ValueError(f"action dim {A} != model action_dim {self.desc.action_dim}")
+        if tuple(s.shape) != (B, T, A):
+            raise ValueError(f"std shape {tuple(s.shape)} != mean shape {(B, T, A)}")
+        if injected_noise is not None and tuple(injected_noise.shape) != (B, n_samples, T, A):
+            raise ValueError(f"injected_noise shape {tuple(injected_noise.shape)} != {(B, n_samples, T, A)}")
         pd = opts.to_c(B, T, 1, plan_index)
         nz = None if injected_noise is None else _f32(injected_noise, dev)
         lo = hi = None
