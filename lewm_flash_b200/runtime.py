@@ -163,6 +163,9 @@ class Runtime:
         H = int(e.shape[-2])
         if H > T:
             raise ValueError(f"history {H} exceeds horizon {T}")
+        if e.shape[-1] != self.desc.dim or goal_emb.shape[-1] != self.desc.dim:
+            raise ValueError(f"emb / goal_emb width must be the model dim {self.desc.dim}, got "
+                             f"{e.shape[-1]} / {goal_emb.shape[-1]}")
         g = goal_emb[..., -1, :]
         if g.ndim == 2:
             g, goal_ps = _f32(g.expand(B, g.shape[-1]), dev), 0
@@ -176,6 +179,18 @@ class Runtime:
         return out
 
     # ------------------------------------------------------------------ full plan
+    def _check_plan_tensors(self, e: torch.Tensor, g: torch.Tensor, m: torch.Tensor, s: torch.Tensor) -> None:
+        """The kernels read every tensor at the model's widths: reject any other shape."""
+        if m.ndim != 3 or m.shape[2] != self.desc.action_dim:
+            raise ValueError(f"mean must be (B,T,{self.desc.action_dim}), got {tuple(m.shape)}")
+        if tuple(s.shape) != tuple(m.shape):
+            raise ValueError(f"std shape {tuple(s.shape)} != mean shape {tuple(m.shape)}")
+        B = m.shape[0]
+        if e.ndim != 3 or e.shape[0] != B or e.shape[2] != self.desc.dim:
+            raise ValueError(f"emb must be (B,H,D) with B={B}, D={self.desc.dim}, got {tuple(e.shape)}")
+        if tuple(g.shape) != (B, self.desc.dim):
+            raise ValueError(f"goal_emb must give (B,D) rows, got {tuple(g.shape)}")
+
     def plan(self, opts: PlanOptions, emb: torch.Tensor, goal_emb: torch.Tensor, mean: torch.Tensor,
              std: torch.Tensor, noise_steps: Optional[Sequence[torch.Tensor]] = None,
              action_low: Optional[torch.Tensor] = None, action_high: Optional[torch.Tensor] = None,
@@ -184,13 +199,10 @@ class Runtime:
         dev = self.device
         m = _f32(mean, dev)
         s = _f32(std, dev)
-        B, T, A = m.shape
         e = _f32(emb, dev)
-        if e.ndim != 3 or e.shape[0] != B:
-            raise ValueError(f"emb must be (B,H,D) with B={B}, got {tuple(e.shape)}")
         g = _f32(goal_emb[..., -1, :] if goal_emb.ndim == 3 else goal_emb, dev)
-        if g.shape != (B, self.desc.dim):
-            raise ValueError(f"goal_emb must give (B,D) rows, got {tuple(goal_emb.shape)}")
+        self._check_plan_tensors(e, g, m, s)
+        B, T, A = m.shape
         if plan_index is None:
             plan_index = self.plans_issued
         self.plans_issued += 1
@@ -214,6 +226,8 @@ class Runtime:
             if action_low is None or action_high is None:
                 raise ValueError("clip_actions needs action_low and action_high")
             lo, hi = _f32(action_low.reshape(-1), dev), _f32(action_high.reshape(-1), dev)
+            if lo.numel() != A or hi.numel() != A:
+                raise ValueError(f"action_low / action_high need {A} values")
         actions = torch.empty(B, T, A, device=dev)
         std_out = torch.empty(B, T, A, device=dev)
         fcost = torch.empty(B, device=dev)
@@ -243,9 +257,10 @@ class Runtime:
         """Per-kernel-class device ms / FLOPs / launches of one plan (``lewm_profile_plan``)."""
         dev = self.device
         m, s = _f32(mean, dev), _f32(std, dev)
-        B, T, _ = m.shape
         e = _f32(emb, dev)
         g = _f32(goal_emb[..., -1, :] if goal_emb.ndim == 3 else goal_emb, dev)
+        self._check_plan_tensors(e, g, m, s)
+        B, T, _ = m.shape
         pd = opts.to_c(B, T, int(e.shape[1]), plan_index)
         n = len(_lib.KERNEL_CLASSES)
         ms = (C.c_double * n)()
@@ -263,7 +278,13 @@ class Runtime:
         dev = self.device
         c = _f32(costs, dev)
         cand = _f32(candidates, dev)
+        if cand.ndim != 4:
+            raise ValueError(f"candidates must be (B,S,T,A), got {tuple(cand.shape)}")
         B, S, T, A = cand.shape
+        if tuple(c.shape) != (B, S):
+            raise ValueError(f"costs must be {(B, S)}, got {tuple(c.shape)}")
+        if tuple(mean.shape) != (B, T, A) or tuple(std.shape) != (B, T, A):
+            raise ValueError(f"mean / std must be {(B, T, A)}, got {tuple(mean.shape)} / {tuple(std.shape)}")
         m = _f32(mean, dev).clone()
         s = _f32(std, dev).clone()
         idx = torch.empty(B, topk, device=dev, dtype=torch.int32)

@@ -114,3 +114,38 @@ def test_create_without_gpu_fails_loudly():
     st = _lib.lib().lewm_create(ctypes.byref(h), ctypes.byref(desc_to_c(desc)), flat.ctypes.data, flat.size, 0)
     assert st == 5 and not h.value
     assert b"CUDA" in _lib.lib().lewm_last_error(None)
+
+
+def _unopened_runtime(desc: ModelDesc) -> Runtime:
+    """A Runtime without a device context: enough for the argument checks, which run first."""
+    rt = object.__new__(Runtime)
+    rt.desc = desc
+    rt.device = torch.device("cpu")
+    rt.plans_issued = 0
+    return rt
+
+
+@pytest.mark.parametrize("case", ["plan_action_dim", "plan_std", "plan_emb_width", "plan_goal_width",
+                                  "cost_emb_width", "refit_costs", "refit_mean", "sample_action_dim",
+                                  "sample_noise"])
+def test_wrappers_reject_tensors_the_kernels_would_overrun(case):
+    """Every kernel reads and writes at the model's widths, so the wrappers reject any other
+    shape with ValueError before anything reaches the device."""
+    desc = ModelDesc()
+    rt = _unopened_runtime(desc)
+    D, A = desc.dim, desc.action_dim
+    z = torch.zeros
+    opts = PlanOptions(num_samples=8, topk=2, n_steps=1)
+    calls = {
+        "plan_action_dim": lambda: rt.plan(opts, z(1, 1, D), z(1, 1, D), z(1, 5, A - 1), z(1, 5, A - 1)),
+        "plan_std": lambda: rt.plan(opts, z(1, 1, D), z(1, 1, D), z(1, 5, A), z(1, 4, A)),
+        "plan_emb_width": lambda: rt.plan(opts, z(1, 1, D - 1), z(1, 1, D), z(1, 5, A), z(1, 5, A)),
+        "plan_goal_width": lambda: rt.plan(opts, z(1, 1, D), z(1, 1, D + 1), z(1, 5, A), z(1, 5, A)),
+        "cost_emb_width": lambda: rt.model_cost(z(1, 1, D - 64), z(1, 1, D), z(1, 4, 5, A)),
+        "refit_costs": lambda: rt.topk_refit(z(1, 3), z(1, 4, 5, A), z(1, 5, A), z(1, 5, A), 2),
+        "refit_mean": lambda: rt.topk_refit(z(1, 4), z(1, 4, 5, A), z(1, 5, 1), z(1, 5, A), 2),
+        "sample_action_dim": lambda: rt.sample_candidates(opts, 4, 0, z(1, 2, 1), z(1, 2, 1)),
+        "sample_noise": lambda: rt.sample_candidates(opts, 4, 0, z(1, 5, A), z(1, 5, A), injected_noise=z(1, 3, 5, A)),
+    }
+    with pytest.raises(ValueError):
+        calls[case]()
