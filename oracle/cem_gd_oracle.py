@@ -97,3 +97,19 @@ def refine(cost_and_grad: Callable, cost: Callable, seed_actions: np.ndarray, se
     out_c = np.where(keep, final_c, seed_c)
     return out_a.astype(F32), out_c.astype(F32), {"accept_count": int(keep.sum()),
                                                   "step_accepted": accepted_any, "model_cost_evals": evals}
+
+
+def model_cost_fns(emb, goal_emb, sd, desc, history_size: int = 3):
+    """``cost`` and ``cost_and_grad`` of the LeWM model cost for ``refine``: the gradient of the
+    mean over (B, K) of the costs, from the reverse-mode restatement in
+    ``oracle/cost_grad_oracle.py`` (float64, returned as float32)."""
+    from oracle import cost_grad_oracle as cg
+
+    def cost_and_grad(a):
+        c, g = cg.cost_and_grad(emb, goal_emb, a, sd, desc, history_size)
+        return c.astype(F32), (g / c.size).astype(F32)
+
+    def cost(a):
+        return cost_and_grad(a)[0]
+
+    return cost, cost_and_grad
