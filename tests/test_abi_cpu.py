@@ -149,3 +149,22 @@ def test_wrappers_reject_tensors_the_kernels_would_overrun(case):
     }
     with pytest.raises(ValueError):
         calls[case]()
+
+
+def test_sample_count_schedule_fuzzed_against_oracle():
+    """The C ABI's schedule (lewm_sample_counts) equals the oracle restatement of
+    ICEMSolver.sample_count_for_step (reference lewm/solvers/icem.py:377-394) on random
+    sample sizes, elite counts, decays and buckets."""
+    hyp = pytest.importorskip("hypothesis")
+    st = hyp.strategies
+    from oracle import icem_oracle as io
+
+    @hyp.settings(max_examples=300, deadline=None, derandomize=True)
+    @hyp.given(S=st.integers(1, 4096), k=st.integers(1, 512), n=st.integers(1, 40),
+               decay=st.sampled_from([1.0, 1.1, 1.25, 1.5, 2.0, 3.0]), bucket=st.integers(0, 700))
+    def check(S, k, n, decay, bucket):
+        hyp.assume(k <= S)
+        opts = PlanOptions(num_samples=S, topk=k, n_steps=n, sample_decay=decay, sample_count_bucket_size=bucket)
+        assert sample_counts(opts) == io.sample_counts(n, S, k, decay, bucket)
+
+    check()
