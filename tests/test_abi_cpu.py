@@ -168,3 +168,17 @@ def test_sample_count_schedule_fuzzed_against_oracle():
         assert sample_counts(opts) == io.sample_counts(n, S, k, decay, bucket)
 
     check()
+
+
+def test_coloring_matrix_fuzzed_against_oracle():
+    """lewm_coloring_matrix equals the oracle's rfft / scale / irfft filter as a matrix
+    (reference lewm/solvers/icem.py:173-182) for every colored length up to 128 and any beta."""
+    hyp = pytest.importorskip("hypothesis")
+    st = hyp.strategies
+
+    @hyp.settings(max_examples=150, deadline=None, derandomize=True)
+    @hyp.given(n=st.integers(2, 128), beta=st.floats(0.0, 3.0, allow_nan=False))
+    def check(n, beta):
+        np.testing.assert_allclose(coloring_matrix(n, beta), io.coloring_matrix(n, beta), rtol=1e-10, atol=1e-11)
+
+    check()
