@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define LEWM_ABI_VERSION 1
+#define LEWM_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define LEWM_API __attribute__((visibility("default")))
@@ -105,7 +105,7 @@ typedef struct lewm_plan_desc {
   int32_t num_samples;      /* S */
   int32_t topk;             /* k */
   int32_t n_steps;          /* iCEM iterations */
-  float sample_decay;       /* >= 1 */
+  double sample_decay;      /* >= 1 (a Python float in the reference) */
   int32_t bucket;           /* sample_count_bucket_size >= 0 */
   int32_t elite_retention;  /* >= 0 */
   float beta;               /* colored-noise exponent: 0 white, 1 pink, 2 brown */
@@ -116,7 +116,16 @@ typedef struct lewm_plan_desc {
   int32_t clip_actions;     /* clamp to action_low/high */
   uint64_t seed;            /* Philox key word 0 */
   uint64_t plan_index;      /* Philox key word 1: a new stream per plan call */
+  /* NULL: the sample count of iteration i follows the schedule of
+   * ICEMSolver.sample_count_for_step (num_samples, sample_decay, bucket).
+   * Else a HOST array of n_steps counts, each in [topk, num_samples], used as
+   * given: the sample counts of an arbitrary list of noise tensors, as the
+   * reference's run_static_icem_chain accepts (lewm/solvers/icem_static_compile.py:61-114). */
+  const int32_t* sample_counts;
 } lewm_plan_desc;
+
+/* LEWM_ABI_VERSION of the loaded library (a binding checks it against the header it was written for). */
+LEWM_API int32_t lewm_abi_version(void);
 
 /* Per-iteration device outputs for solver callbacks / debugging (any may be NULL).
  * i = iteration, S = num_samples (rows past the iteration's sample count are unset). */
@@ -180,7 +189,9 @@ LEWM_API lewm_status lewm_sample_candidates(lewm_ctx* ctx, const lewm_plan_desc*
  *   time length (horizon*action_block for raw time, else horizon) above 128,
  *   or horizon*action_dim above 128, returns LEWM_UNSUPPORTED_SHAPE.
  *   The first call on a device looks up that array's address (and may load
- *   the module there): make it before any stream capture.
+ *   the module there): make it before any stream capture. The address is kept
+ *   for the life of the process: after cudaDeviceReset on a device, do not call
+ *   this entry point on that device again.
  *   Calls that overlap on the GPU (unordered streams) share the scratch and
  *   race; order them on one stream or with events.
  *   Errors: text from lewm_last_error(NULL). */
@@ -209,9 +220,28 @@ LEWM_API lewm_status lewm_profile_plan(lewm_ctx* ctx, const lewm_plan_desc* plan
                                        const float* init_mean, const float* init_std, double* ms_out,
                                        double* flops_out, int32_t* launches_out, void* stream);
 
-/* Synchronize `stream`, then read and clear the device status word of `ctx`
- * (LEWM_DEVICE_TIMEOUT if any bounded wait expired since the last call). */
+/* Synchronize `stream`, then read and clear the device status word of `ctx`:
+ * LEWM_DEVICE_TIMEOUT if any bounded wait expired since the last call, else
+ * LEWM_NUMERIC_NAN if a plan since the last call produced a NaN final cost. */
 LEWM_API lewm_status lewm_sync_status(lewm_ctx* ctx, void* stream);
+
+/* Time limit of every bounded device-side wait (mbarrier phases of bulk copies and
+ * MMA completion) in kernels launched on `ctx` from now on, in nanoseconds of
+ * %globaltimer; 0 restores the default of 2 s. A wait that runs out sets the
+ * timeout bit of the context's status word, the kernel skips its dependent work,
+ * releases its tensor memory and returns; lewm_sync_status then reports
+ * LEWM_DEVICE_TIMEOUT. No reference counterpart (the reference's PyTorch kernels
+ * have no bounded waits). Takes effect for kernels enqueued after it returns; it
+ * synchronizes the context's device. */
+LEWM_API lewm_status lewm_set_wait_limit(lewm_ctx* ctx, uint64_t limit_ns);
+
+/* Failure-detection self-test: enqueue on `stream` one device wait on a barrier that
+ * nothing ever completes, bounded by the context's wait limit. When it runs out the
+ * kernel sets the timeout bit and returns (nothing else is in flight), so the next
+ * lewm_sync_status reports LEWM_DEVICE_TIMEOUT and the context stays usable. Set a
+ * short limit first (lewm_set_wait_limit), or the call takes the 2 s default. No
+ * reference counterpart. */
+LEWM_API lewm_status lewm_wait_selftest(lewm_ctx* ctx, void* stream);
 
 /* ------------------------------------------------------------------ observation encoder
  * The pixels -> embedding step in front of planning: JEPA.encode

@@ -47,10 +47,11 @@ class ModelDescC(C.Structure):
 class PlanDescC(C.Structure):
     _fields_ = [
         ("n_envs", C.c_int32), ("horizon", C.c_int32), ("history", C.c_int32), ("history_size", C.c_int32),
-        ("num_samples", C.c_int32), ("topk", C.c_int32), ("n_steps", C.c_int32), ("sample_decay", C.c_float),
+        ("num_samples", C.c_int32), ("topk", C.c_int32), ("n_steps", C.c_int32), ("sample_decay", C.c_double),
         ("bucket", C.c_int32), ("elite_retention", C.c_int32), ("beta", C.c_float), ("time_axis_raw", C.c_int32),
         ("action_block", C.c_int32), ("momentum_alpha", C.c_float), ("return_best_elite", C.c_int32),
         ("clip_actions", C.c_int32), ("seed", C.c_uint64), ("plan_index", C.c_uint64),
+        ("sample_counts", C.POINTER(C.c_int32)),
     ]
 
 
@@ -67,6 +68,7 @@ class PlanTraceC(C.Structure):
 
 
 _lib = None
+ABI_VERSION = 2  # LEWM_ABI_VERSION of include/lewm_b200.h this binding follows
 
 # name -> (restype, argtypes)
 SIGNATURES = {
@@ -90,6 +92,9 @@ SIGNATURES = {
                                                  C.c_int32, C.c_void_p]),
     "lewm_coloring_matrix": (C.c_int, [C.c_int32, C.c_double, C.c_void_p]),
     "lewm_sync_status": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "lewm_set_wait_limit": (C.c_int, [C.c_void_p, C.c_uint64]),
+    "lewm_wait_selftest": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "lewm_abi_version": (C.c_int32, []),
     "lewm_profile_plan": (C.c_int, [C.c_void_p, C.POINTER(PlanDescC), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "lewm_encoder_weight_count": (C.c_size_t, [C.POINTER(EncoderDescC)]),
@@ -120,6 +125,9 @@ def lib():
         fn = getattr(h, name)
         fn.restype = res
         fn.argtypes = args
+    got = h.lewm_abi_version()
+    if got != ABI_VERSION:
+        raise RuntimeError(f"{LIB_PATH} has C ABI version {got}, this binding needs {ABI_VERSION}; rebuild it")
     _lib = h
     return h
 

@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "../../include/lewm_b200.h"
+#include "lewm_common.cuh"
 #include "lewm_internal.h"
 
 using namespace lewm;
@@ -588,7 +589,12 @@ lewm_status check_plan(lewm_ctx* c, const lewm_plan_desc* p) {
     return fail(c, LEWM_INVALID_ARG, "elite_retention must be non-negative, got %d", p->elite_retention);
   if (!(p->momentum_alpha >= 0.f && p->momentum_alpha < 1.f))
     return fail(c, LEWM_INVALID_ARG, "momentum_alpha must satisfy 0 <= alpha < 1, got %g", p->momentum_alpha);
-  if (!(p->sample_decay >= 1.f)) return fail(c, LEWM_INVALID_ARG, "sample_decay must be >= 1.0, got %g", p->sample_decay);
+  if (!(p->sample_decay >= 1.0)) return fail(c, LEWM_INVALID_ARG, "sample_decay must be >= 1.0, got %g", p->sample_decay);
+  if (p->sample_counts)
+    for (int i = 0; i < p->n_steps; ++i)
+      if (p->sample_counts[i] < p->topk || p->sample_counts[i] > p->num_samples)
+        return fail(c, LEWM_INVALID_ARG, "sample_counts[%d]=%d must lie in [topk=%d, num_samples=%d]", i,
+                    p->sample_counts[i], p->topk, p->num_samples);
   if (p->bucket < 0) return fail(c, LEWM_INVALID_ARG, "sample_count_bucket_size must be non-negative, got %d", p->bucket);
   if (p->action_block <= 0) return fail(c, LEWM_INVALID_ARG, "action_block must be positive, got %d", p->action_block);
   if (!(p->beta >= 0.f)) return fail(c, LEWM_INVALID_ARG, "beta must be >= 0");
@@ -611,13 +617,14 @@ lewm_status check_plan(lewm_ctx* c, const lewm_plan_desc* p) {
 }
 
 std::vector<int> counts_of(const lewm_plan_desc* p) {
+  if (p->sample_counts) return std::vector<int>(p->sample_counts, p->sample_counts + p->n_steps);
   std::vector<int> out(p->n_steps);
   for (int s = 0; s < p->n_steps; ++s) {
     int count;
-    if ((double)p->sample_decay == 1.0) {
+    if (p->sample_decay == 1.0) {
       count = p->num_samples;
     } else {
-      const int decayed = (int)std::ceil(p->num_samples * std::pow((double)p->sample_decay, (double)-s));
+      const int decayed = (int)std::ceil(p->num_samples * std::pow(p->sample_decay, (double)-s));
       count = std::max(decayed, std::min(p->num_samples, 2 * p->topk));
       if (p->bucket > 0)
         count = std::min(p->num_samples, (int)std::ceil((double)count / p->bucket) * p->bucket);
@@ -677,10 +684,14 @@ bool graphs_enabled() {
 }
 
 std::vector<double> plan_key(const lewm_plan_desc* p, int kind, int ncol) {
-  return {(double)p->n_envs, (double)p->horizon, (double)p->history, (double)p->history_size,
-          (double)p->num_samples, (double)p->topk, (double)p->n_steps, (double)p->sample_decay,
-          (double)p->bucket, (double)p->elite_retention, (double)kind, (double)ncol, (double)p->action_block,
-          (double)p->momentum_alpha, (double)p->return_best_elite, (double)p->clip_actions};
+  std::vector<double> key{(double)p->n_envs, (double)p->horizon, (double)p->history, (double)p->history_size,
+                          (double)p->num_samples, (double)p->topk, (double)p->n_steps, p->sample_decay,
+                          (double)p->bucket, (double)p->elite_retention, (double)kind, (double)ncol,
+                          (double)p->action_block, (double)p->momentum_alpha, (double)p->return_best_elite,
+                          (double)p->clip_actions, p->sample_counts ? 1.0 : 0.0};
+  if (p->sample_counts)
+    for (int i = 0; i < p->n_steps; ++i) key.push_back((double)p->sample_counts[i]);
+  return key;
 }
 
 // Every launch of one plan: per iteration sample -> model cost -> top-k/refit.
@@ -739,6 +750,7 @@ lewm_status plan_iterations(lewm_ctx* c, const lewm_plan_desc* p, const std::vec
     rp.final_cost = ws.fcost;
     rp.topk_idx = (trace && trace->topk_idx) ? trace->topk_idx + (size_t)it * B * k : nullptr;
     rp.topk_val = (trace && trace->topk_val) ? trace->topk_val + (size_t)it * B * k : nullptr;
+    rp.nan_status = (it == p->n_steps - 1) ? c->d_status : nullptr;  // the plan's final costs
     c->prof.begin(st);
     LEWM_CK(c, launch_refit(rp, st));
     c->prof.end(KC_REFIT, 0.0, st);
@@ -816,8 +828,9 @@ lewm_status lewm_create(lewm_ctx** out, const lewm_model_desc* desc, const float
     if (v > 0) c->tile_target = v;
   }
   s = pack_weights(c, weights, n_floats);
-  if (s == LEWM_OK && cudaMalloc(&c->d_status, 4) != cudaSuccess) s = fail(c, LEWM_CUDA_ERROR, "status alloc");
-  if (s == LEWM_OK && cudaMemset(c->d_status, 0, 4) != cudaSuccess) s = fail(c, LEWM_CUDA_ERROR, "status memset");
+  if (s == LEWM_OK && cudaMalloc(&c->d_status, kStatusBytes) != cudaSuccess) s = fail(c, LEWM_CUDA_ERROR, "status alloc");
+  if (s == LEWM_OK && cudaMemset(c->d_status, 0, kStatusBytes) != cudaSuccess)
+    s = fail(c, LEWM_CUDA_ERROR, "status memset");
   if (s == LEWM_OK && (cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking) != cudaSuccess ||
                        cudaEventCreateWithFlags(&c->ev_in, cudaEventDisableTiming) != cudaSuccess ||
                        cudaEventCreateWithFlags(&c->ev_out, cudaEventDisableTiming) != cudaSuccess))
@@ -1061,10 +1074,29 @@ lewm_status lewm_sync_status(lewm_ctx* c, void* stream) {
   LEWM_CK(c, cudaMemcpy(&v, c->d_status, 4, cudaMemcpyDeviceToHost));
   if (v) {
     LEWM_CK(c, cudaMemset(c->d_status, 0, 4));
-    return fail(c, LEWM_DEVICE_TIMEOUT, "device status 0x%x: a bounded device wait expired", v);
+    if (v & (LEWM_DEV_TIMEOUT | LEWM_DEV_BADARG))
+      return fail(c, LEWM_DEVICE_TIMEOUT, "device status 0x%x: a bounded device wait expired", v);
+    return fail(c, LEWM_NUMERIC_NAN, "device status 0x%x: a plan produced a NaN final cost", v);
   }
   return LEWM_OK;
 }
+
+lewm_status lewm_set_wait_limit(lewm_ctx* c, uint64_t limit_ns) {
+  if (!c) return fail(nullptr, LEWM_INVALID_ARG, "ctx is NULL");
+  DeviceGuard g(c->device);
+  LEWM_CK(c, cudaDeviceSynchronize());
+  LEWM_CK(c, cudaMemcpy(reinterpret_cast<uint8_t*>(c->d_status) + 8, &limit_ns, 8, cudaMemcpyHostToDevice));
+  return LEWM_OK;
+}
+
+lewm_status lewm_wait_selftest(lewm_ctx* c, void* stream) {
+  if (!c) return fail(nullptr, LEWM_INVALID_ARG, "ctx is NULL");
+  DeviceGuard g(c->device);
+  LEWM_CK(c, launch_wait_selftest(c->d_status, static_cast<cudaStream_t>(stream)));
+  return LEWM_OK;
+}
+
+int32_t lewm_abi_version(void) { return LEWM_ABI_VERSION; }
 
 lewm_status lewm_profile_plan(lewm_ctx* c, const lewm_plan_desc* p, const float* emb, const float* goal,
                               const float* init_mean, const float* init_std, double* ms_out, double* flops_out,

@@ -1025,8 +1025,8 @@ lewm_status lewm_encoder_create(lewm_encoder** out, const lewm_encoder_desc* des
     if (ce == cudaSuccess) ce = cudaMemcpy(e->d_w, hb.data(), bf_bytes, cudaMemcpyHostToDevice);
     if (ce == cudaSuccess)
       ce = cudaMemcpy(static_cast<uint8_t*>(e->d_w) + bf_bytes, fv.data(), fv.size() * 4, cudaMemcpyHostToDevice);
-    if (ce == cudaSuccess) ce = cudaMalloc(&e->d_status, 4);
-    if (ce == cudaSuccess) ce = cudaMemset(e->d_status, 0, 4);
+    if (ce == cudaSuccess) ce = cudaMalloc(&e->d_status, kStatusBytes);  // status word + wait limit
+    if (ce == cudaSuccess) ce = cudaMemset(e->d_status, 0, kStatusBytes);
     if (ce == cudaSuccess) ce = set_gemm_smem<192, EPI_PATCH>();
     if (ce == cudaSuccess) ce = set_gemm_smem<192, EPI_QKV>();
     if (ce == cudaSuccess) ce = set_gemm_smem<192, EPI_RESID>();

@@ -196,7 +196,9 @@ __global__ void __launch_bounds__(kRefitThreads) k_refit(RefitParams p) {
   if (tid == 0) {
     float s = 0.f;
     for (int i = 0; i < p.k; ++i) s += costs[(int)(keys[i] & 0xFFFFFFFFull)];
-    p.final_cost[env] = s / (float)p.k;
+    const float fc = s / (float)p.k;
+    p.final_cost[env] = fc;
+    if (p.nan_status && fc != fc) atomicOr(p.nan_status, LEWM_DEV_NAN);
   }
   for (int e = tid; e < p.R * TA; e += kRefitThreads) {
     const int i = e / TA, d = e - i * TA;
@@ -233,7 +235,23 @@ __global__ void k_set_rng(uint32_t* rng, uint32_t seed, uint32_t plan) {
   rng[1] = plan;
 }
 
+// Bounded-wait self-test: one thread waits on an mbarrier that nothing ever arrives
+// on (no copy or MMA is attached to it), with the wait limit of the context's status
+// block. The wait runs out, sets LEWM_DEV_TIMEOUT in the status word and the kernel
+// returns; nothing else is in flight, so the context stays usable.
+__global__ void k_wait_selftest(uint32_t* status) {
+  __shared__ uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  mbar_wait(&bar, 0, status);
+}
+
 }  // namespace
+
+cudaError_t launch_wait_selftest(uint32_t* status, cudaStream_t st) {
+  k_wait_selftest<<<1, 1, 0, st>>>(status);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_set_rng(uint32_t* rng, uint32_t seed, uint32_t plan, cudaStream_t st) {
   return launch_k(k_set_rng, dim3(1), dim3(1), 0, st, rng, seed, plan);

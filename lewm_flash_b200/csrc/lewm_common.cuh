@@ -4,6 +4,11 @@
 // Every wait here has a time limit (%globaltimer); on expiry it sets
 // LEWM_DEV_TIMEOUT in the context's device status word and returns false so
 // the kernel can release TMEM and exit instead of hanging the GPU.
+//
+// Status block (16 bytes of device memory per context, 8-byte aligned):
+//   word 0      status bits (LEWM_DEV_*), read and cleared by the host
+//   word 1      unused
+//   words 2-3   wait limit in ns (uint64; 0 = kWaitLimitNs), set by the host
 #pragma once
 
 #include <cuda_bf16.h>
@@ -15,7 +20,9 @@ namespace lewm {
 // ----------------------------------------------------------------- status bits
 constexpr uint32_t LEWM_DEV_TIMEOUT = 1u;   // a bounded wait gave up
 constexpr uint32_t LEWM_DEV_BADARG = 2u;    // a kernel saw an impossible index
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
+constexpr uint32_t LEWM_DEV_NAN = 4u;       // a plan's final cost was NaN
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // default: 2 s per wait
+constexpr size_t kStatusBytes = 16;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -56,13 +63,21 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ void named_bar(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
-// Wait for phase `parity` of `bar` to complete, at most kWaitLimitNs.
+// The wait limit stored in the status block (read only once a wait has not
+// completed on its first try).
+__device__ __forceinline__ uint64_t wait_limit_ns(const uint32_t* status) {
+  const uint64_t v = *reinterpret_cast<const volatile uint64_t*>(status + 2);
+  return v ? v : kWaitLimitNs;
+}
+
+// Wait for phase `parity` of `bar` to complete, at most the status block's wait limit.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
+  const uint64_t limit = wait_limit_ns(status);
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > limit) {
       atomicOr(status, LEWM_DEV_TIMEOUT);
       return false;
     }

@@ -238,6 +238,8 @@ struct SampleParams {
 };
 cudaError_t launch_sample(const SampleParams& p, cudaStream_t st);
 cudaError_t launch_set_rng(uint32_t* rng, uint32_t seed, uint32_t plan, cudaStream_t st);
+// One wait on an mbarrier that nothing arrives on: expires after the status block's limit.
+cudaError_t launch_wait_selftest(uint32_t* status, cudaStream_t st);
 
 // Sets the thread's error text that lewm_last_error(NULL) returns (context-free calls).
 void set_noctx_error(const char* msg);
@@ -254,6 +256,7 @@ struct RefitParams {
   float* final_cost;    // (B) out: mean of the k smallest costs
   int32_t* topk_idx;    // (B,k) out or null
   float* topk_val;      // (B,k) out or null
+  uint32_t* nan_status; // status block: LEWM_DEV_NAN is set when a final cost is NaN (or null: no check)
 };
 cudaError_t launch_refit(const RefitParams& p, cudaStream_t st);
 

@@ -18,7 +18,10 @@
 // Set-up: the first call on a device, made with that device current, resolves
 // the scratch array's device address with cudaGetSymbolAddress (this may load
 // the module on that device) and caches it. Make that first call before any
-// stream capture. Later calls only launch two kernels.
+// stream capture. Later calls only launch two kernels. The cached address belongs to
+// the device's primary context: a caller that destroys that context
+// (cudaDeviceReset) must not call this entry point on that device again in the
+// same process, since the cache would hand the kernels a stale address.
 //
 // Zero state: nothing in the scratch has to start at zero. Each call first
 // rewrites every scratch word the sampler will read (the ncol x ncol matrix and
@@ -142,8 +145,9 @@ extern "C" lewm_status lewm_sample_candidates_noalloc(const lewm_plan_desc* p, i
   if (!(p->beta >= 0.f)) return noalloc_fail(LEWM_INVALID_ARG, "beta must be >= 0");
   if (p->clip_actions && (!action_low || !action_high))
     return noalloc_fail(LEWM_INVALID_ARG, "clip_actions needs action_low and action_high");
-  if (p->horizon * action_dim > kMaxTA)
-    return noalloc_fail(LEWM_UNSUPPORTED_SHAPE, "horizon*action_dim=%d exceeds %d", p->horizon * action_dim, kMaxTA);
+  if ((int64_t)p->horizon * action_dim > kMaxTA)
+    return noalloc_fail(LEWM_UNSUPPORTED_SHAPE, "horizon*action_dim=%lld exceeds %d",
+                        (long long)p->horizon * action_dim, kMaxTA);
   if ((int64_t)p->n_envs * S > (int64_t)INT_MAX - 127)
     return noalloc_fail(LEWM_UNSUPPORTED_SHAPE, "n_envs*S too large");
   if (device < 0 || device >= kMaxDevices) return noalloc_fail(LEWM_INVALID_ARG, "bad device %d", device);

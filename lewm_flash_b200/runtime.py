@@ -62,16 +62,28 @@ class PlanOptions:
     clip_actions: bool = False
     history_size: int = 3
     seed: int = 1234
+    # Explicit per-iteration sample counts (one per iteration, each in [topk, num_samples]),
+    # e.g. the sample counts of an arbitrary list of injected noise tensors; None follows
+    # the ICEMSolver schedule of (num_samples, sample_decay, sample_count_bucket_size).
+    counts: Optional[List[int]] = None
 
     def to_c(self, n_envs: int, horizon: int, history: int, plan_index: int = 0) -> _lib.PlanDescC:
         if self.time_axis not in ("block", "raw"):
             raise ValueError(f"colored noise time_axis must be 'block' or 'raw', got {self.time_axis!r}")
-        return _lib.PlanDescC(
+        counts_arr = None
+        if self.counts is not None:
+            if len(self.counts) != self.n_steps:
+                raise ValueError(f"counts has {len(self.counts)} entries, n_steps is {self.n_steps}")
+            counts_arr = (C.c_int32 * len(self.counts))(*[int(v) for v in self.counts])
+        pd = _lib.PlanDescC(
             int(n_envs), int(horizon), int(history), int(self.history_size), int(self.num_samples), int(self.topk),
             int(self.n_steps), float(self.sample_decay), int(self.sample_count_bucket_size),
             int(self.elite_retention), float(self.beta), 1 if self.time_axis == "raw" else 0, int(self.action_block),
             float(self.momentum_alpha), int(bool(self.return_best_elite)), int(bool(self.clip_actions)),
-            int(self.seed) & 0xFFFFFFFFFFFFFFFF, int(plan_index) & 0xFFFFFFFFFFFFFFFF)
+            int(self.seed) & 0xFFFFFFFFFFFFFFFF, int(plan_index) & 0xFFFFFFFFFFFFFFFF,
+            C.cast(counts_arr, C.POINTER(C.c_int32)) if counts_arr is not None else None)
+        pd._counts_keep = counts_arr  # the struct holds a raw pointer into this array
+        return pd
 
 
 def sample_counts(opts: PlanOptions, horizon: int = 5, n_envs: int = 1) -> List[int]:
@@ -138,8 +150,18 @@ class Runtime:
         _lib.check(status, self._h)
 
     def sync(self) -> None:
-        """Synchronize and raise LewmError(LEWM_DEVICE_TIMEOUT) if a device wait expired."""
+        """Synchronize; raise LewmError(LEWM_DEVICE_TIMEOUT) if a device wait expired, or
+        LewmError(LEWM_NUMERIC_NAN) if a plan since the last sync produced a NaN final cost."""
         self._check(_lib.lib().lewm_sync_status(self._h, self._stream()))
+
+    def set_wait_limit(self, limit_ns: int) -> None:
+        """Time limit of every bounded device-side wait of later launches (0: the 2 s default)."""
+        self._check(_lib.lib().lewm_set_wait_limit(self._h, int(limit_ns)))
+
+    def wait_selftest(self) -> None:
+        """Enqueue one bounded device wait that can never complete (``lewm_wait_selftest``);
+        the next ``sync`` raises LEWM_DEVICE_TIMEOUT."""
+        self._check(_lib.lib().lewm_wait_selftest(self._h, self._stream()))
 
     # ------------------------------------------------------------------ model cost
     def model_cost(self, emb: torch.Tensor, goal_emb: torch.Tensor, candidates: torch.Tensor,

@@ -27,12 +27,11 @@ from __future__ import annotations
 
 import math
 import warnings
-from typing import Any, List, Optional, Sequence
+from typing import Any, Optional, Sequence
 
 import numpy as np
 import torch
 
-from . import runtime as rt_mod
 from .runtime import PlanOptions, Runtime
 
 COLORED_NOISE_BETA = {"none": 0.0, "pink": 1.0, "brown": 2.0}
@@ -79,9 +78,19 @@ def prepare_init_action(model: Any, info_dict: dict, init_action: Optional[torch
 
 
 class B200ICEMSolver:
-    """iCEM solver whose whole iteration loop runs on the B200 plan kernels."""
+    """iCEM solver whose whole iteration loop runs on the B200 plan kernels.
+
+    ``noise_source`` (default None) is the hook for reproducing a reference run: a
+    callable ``(batch_size, n_samples) -> (batch_size, n_samples, T, A)`` tensor of
+    post-coloring noise, e.g. the ``_sample_noise`` method of a reference
+    ``ICEMSolver`` built with the same seed. When set, ``solve`` draws every
+    iteration's noise from it in the reference's order (env batch by env batch,
+    iteration by iteration, ``lewm/solvers/icem.py:501-521``) and plans on that
+    injected noise instead of the in-kernel Philox stream.
+    """
 
     defer_cpu_materialization = True
+    noise_source = None
 
     def __init__(
         self,
@@ -261,6 +270,18 @@ class B200ICEMSolver:
             goal = goal[:, 0]
         return emb, goal
 
+    def _injected_noise(self, total_envs: int):
+        """Every iteration's noise from ``noise_source``, drawn in the reference's order."""
+        if self.noise_source is None:
+            return None
+        counts = self.sample_counts()
+        steps = [[] for _ in counts]
+        for start in range(0, total_envs, self.batch_size):
+            bs = min(start + self.batch_size, total_envs) - start
+            for step, n in enumerate(counts):
+                steps[step].append(self.noise_source(bs, n).to(device=self.device, dtype=torch.float32))
+        return [torch.cat(chunks, dim=0) for chunks in steps]
+
     def _plan(self, info_dict: dict, mean: torch.Tensor, var: torch.Tensor, trace: bool):
         total_envs = mean.shape[0]
         emb, goal = self._cost_embeddings(info_dict, total_envs)
@@ -268,8 +289,9 @@ class B200ICEMSolver:
         opts = self.plan_options()
         plan_index = self._solves
         self._solves += 1
-        return rt.plan(opts, emb, goal, mean, var, action_low=self._action_low, action_high=self._action_high,
-                       trace=trace, plan_index=plan_index)
+        return rt.plan(opts, emb, goal, mean, var, noise_steps=self._injected_noise(total_envs),
+                       action_low=self._action_low, action_high=self._action_high, trace=trace,
+                       plan_index=plan_index)
 
     @torch.inference_mode()
     def solve(self, info_dict: dict, init_action: torch.Tensor | None = None) -> dict[str, Any]:
@@ -299,22 +321,36 @@ class B200ICEMSolver:
                 outputs["callbacks"][cb.output_key] = cb.history
         return outputs
 
+    _callback_n_samples = True  # ICEMSolver passes n_samples to its callbacks; CEMExactSolver does not
+
     def _replay_callbacks(self, tr, mean0, var0) -> None:
-        """Feed the per-iteration plan trace to the reference callback protocol (icem.py:565-578)."""
-        for cb in self.callbacks:
-            cb.start_batch()
-        prev_mean, prev_var = mean0, var0
-        for step, n in enumerate(tr["counts"]):
-            cand = tr["candidates"][step][:, :n]
-            costs = tr["costs"][step][:, :n]
-            inds = tr["topk_idx"][step].long()
-            vals = tr["topk_val"][step]
-            topk_cand = torch.gather(cand, 1, inds[:, :, None, None].expand(-1, -1, cand.shape[2], cand.shape[3]))
-            m, v = tr["mean"][step], tr["std"][step]
+        """Feed the per-iteration plan trace to the reference callback protocol.
+
+        Same calls, in the same order and with the same per-env-batch tensors, as the
+        reference's solve loop (``lewm/solvers/icem.py:501-578``): ``start_batch`` once
+        per env batch of ``batch_size`` envs, then one call per iteration.
+        """
+        total = int(mean0.shape[0])
+        for start in range(0, total, self.batch_size):
+            end = min(start + self.batch_size, total)
             for cb in self.callbacks:
-                cb(step=step, candidates=cand, costs=costs, topk_vals=vals, topk_inds=inds,
-                   topk_candidates=topk_cand, mean=m, var=v, prev_mean=prev_mean, prev_var=prev_var, n_samples=n)
-            prev_mean, prev_var = m, v
+                cb.start_batch()
+            prev_mean, prev_var = mean0[start:end], var0[start:end]
+            for step, n in enumerate(tr["counts"]):
+                cand = tr["candidates"][step][start:end, :n]
+                costs = tr["costs"][step][start:end, :n]
+                inds = tr["topk_idx"][step][start:end].long()
+                vals = tr["topk_val"][step][start:end]
+                topk_cand = torch.gather(cand, 1,
+                                         inds[:, :, None, None].expand(-1, -1, cand.shape[2], cand.shape[3]))
+                m, v = tr["mean"][step][start:end], tr["std"][step][start:end]
+                kw = dict(step=step, candidates=cand, costs=costs, topk_vals=vals, topk_inds=inds,
+                          topk_candidates=topk_cand, mean=m, var=v, prev_mean=prev_mean, prev_var=prev_var)
+                if self._callback_n_samples:
+                    kw["n_samples"] = n
+                for cb in self.callbacks:
+                    cb(**kw)
+                prev_mean, prev_var = m, v
 
 
 class B200CEMSolver(B200ICEMSolver):
@@ -333,7 +369,10 @@ class B200CEMSolver(B200ICEMSolver):
         self.warm_start = bool(warm_start)
         self._warm_mean: torch.Tensor | None = None
         self._warm_var: torch.Tensor | None = None
+        self._warm_signature: tuple | None = None
         self._last_warm_start_info = {"enabled": self.warm_start, "used": False, "reset": False, "reset_reason": None}
+
+    _callback_n_samples = False  # CEMExactSolver's callbacks get no n_samples (cem_exact.py:340-351)
 
     def configure(self, *, action_space: Any, n_envs: int, config: Any) -> None:
         super().configure(action_space=action_space, n_envs=n_envs, config=config)
@@ -350,8 +389,15 @@ class B200CEMSolver(B200ICEMSolver):
     def reset_warm_start_state(self, reason: str = "manual") -> None:
         self._warm_mean = None
         self._warm_var = None
+        self._warm_signature = None
         self._last_warm_start_info = {"enabled": self.warm_start, "used": False, "reset": True,
                                       "reset_reason": reason}
+
+    def _distribution_signature(self, mean: torch.Tensor, var: torch.Tensor) -> tuple:
+        """What a remembered distribution must match to warm-start the next solve
+        (``_distribution_signature``, ``cem_exact.py:166-180``)."""
+        return (*map(int, mean.shape), *map(int, var.shape), int(self.batch_size), self.receding_horizon,
+                torch.device(mean.device), mean.dtype, torch.device(var.device), var.dtype)
 
     def _shift(self, mean: torch.Tensor, var: torch.Tensor):
         info = {"enabled": self.warm_start, "used": False, "reset": False, "reset_reason": None,
@@ -365,9 +411,11 @@ class B200CEMSolver(B200ICEMSolver):
             info["reset_reason"] = "no_unexecuted_tail" if shift >= self.horizon else "invalid_shift"
             self._last_warm_start_info = info
             return mean, var
-        if self._warm_mean is None or self._warm_mean.shape != mean.shape:
-            had = self._warm_mean is not None
+        if (self._warm_mean is None or self._warm_var is None
+                or self._warm_signature != self._distribution_signature(mean, var)):
+            had = self._warm_mean is not None or self._warm_var is not None
             self._warm_mean = self._warm_var = None
+            self._warm_signature = None
             info["reset"] = had
             info["reset_reason"] = "signature_mismatch" if had else "no_previous_state"
             self._last_warm_start_info = info
@@ -397,6 +445,7 @@ class B200CEMSolver(B200ICEMSolver):
         out = {"costs": costs, "actions": actions.cpu(), "mean": [actions.cpu()], "var": [std.cpu()],
                "warm_start": self.last_warm_start_info}
         if self.warm_start:
+            self._warm_signature = self._distribution_signature(actions, std)
             self._warm_mean, self._warm_var = actions.detach().clone(), std.detach().clone()
         if self.callbacks:
             out["callbacks"] = {}
@@ -418,33 +467,19 @@ def run_static_icem_chain(model, emb: torch.Tensor, goal_emb: torch.Tensor, mean
     Returns (actions_or_best_elite, std, final_cost) on the device.
     """
     rt = _runtime(model, mean.device if mean.is_cuda else "cuda")
+    noise_steps = list(noise_steps)
+    if not noise_steps:
+        # The reference's loop body never runs and its `assert final_cost is not None` fails.
+        raise AssertionError("run_static_icem_chain needs at least one noise step")
     counts = [int(n.shape[1]) for n in noise_steps]
-    S = max(counts)
-    # The plan derives per-iteration counts from (S, decay, bucket); encode the given
-    # counts through a schedule that reproduces them exactly.
-    opts = PlanOptions(num_samples=S, topk=topk, n_steps=len(counts), elite_retention=elite_retention,
+    # Any list of noise tensors: the plan takes their sample counts as given.
+    opts = PlanOptions(num_samples=max(counts), topk=topk, n_steps=len(counts), elite_retention=elite_retention,
                        momentum_alpha=momentum_alpha, return_best_elite=return_best_elite,
-                       clip_actions=action_low is not None and action_high is not None, history_size=history_size)
-    _fit_schedule(opts, counts)
-    actions, std, fcost, _ = rt.plan(opts, emb, goal_emb, mean, var, noise_steps=list(noise_steps),
+                       clip_actions=action_low is not None and action_high is not None, history_size=history_size,
+                       counts=counts)
+    actions, std, fcost, _ = rt.plan(opts, emb, goal_emb, mean, var, noise_steps=noise_steps,
                                      action_low=action_low, action_high=action_high)
     return actions, std, fcost
-
-
-def _fit_schedule(opts: PlanOptions, counts: List[int]) -> None:
-    """Find (sample_decay, bucket) whose schedule equals ``counts`` (fixed S, or an ICEMSolver schedule)."""
-    S = opts.num_samples
-    if all(c == S for c in counts):
-        opts.sample_decay, opts.sample_count_bucket_size = 1.0, 0
-        return
-    from itertools import product
-
-    for decay, bucket in product([1.25, 1.5, 2.0, 1.1, 1.2, 1.3, 1.75, 3.0], [0] + sorted({c for c in counts})):
-        opts.sample_decay, opts.sample_count_bucket_size = decay, bucket
-        got = rt_mod.sample_counts(opts)
-        if got == counts:
-            return
-    raise ValueError(f"noise step sample counts {counts} do not follow an iCEM schedule")
 
 
 class B200ModelCost:

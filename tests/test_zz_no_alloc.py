@@ -104,6 +104,19 @@ def test_noalloc_sampling_repeats_after_context_use():
     b = noalloc_sample(opts, B, T, A, S, 2, mean, std, plan_index=3).clone()
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+    # Warm calls allocate no device memory: free bytes stay the same over repeated calls
+    # (the output buffer is allocated before the measurement).
+    out = torch.empty(B, S, T, A, device="cuda:0")
+    pd = opts.to_c(B, T, 1, 3)
+    stream = C.c_void_p(torch.cuda.current_stream(0).cuda_stream)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info(0)[0]
+    for it in range(8):
+        st = _lib.lib().lewm_sample_candidates_noalloc(C.byref(pd), A, S, it, _ptr(mean), _ptr(std), None, None, None,
+                                                       _ptr(out), 0, stream)
+        assert st == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(0)[0] == free0
 
 
 def test_noalloc_rejects_sizes_beyond_the_scratch_limits():
@@ -119,3 +132,7 @@ def test_noalloc_rejects_sizes_beyond_the_scratch_limits():
     assert st == 1 and b"not divisible" in lib.lewm_last_error(None)
     st = lib.lewm_sample_candidates_noalloc(None, 10, 8, 0, dummy, dummy, None, None, None, dummy, 0, None)
     assert st == 1
+    # horizon * action_dim = 2**20 * 2**12 wraps to 0 in 32-bit arithmetic; the check is 64-bit.
+    pd = PlanOptions(num_samples=8, topk=4, n_steps=1).to_c(1, 1 << 20, 1)
+    st = lib.lewm_sample_candidates_noalloc(C.byref(pd), 1 << 12, 8, 0, dummy, dummy, None, None, None, dummy, 0, None)
+    assert st == 2 and b"exceeds 128" in lib.lewm_last_error(None)
