@@ -211,7 +211,7 @@ def chain_case(torch, name, desc, seed, solver_kw, n_envs, H, input_seed, clip=F
 
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="reference checkout (its lewm/ is imported)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     import torch
