@@ -2,7 +2,7 @@
 
 Workload (one "step" = one full iCEM plan for one env on each GPU):
   LeWM predictor (width 192, 6 layers, 16 heads x 64, MLP 4x, AdaLN-zero action
-  conditioning, action dim 2 x frameskip 5 = 10), horizon 5, history 1, bucketed
+  conditioning), action dim 2 x frameskip 5 = 10, horizon 5, history 1, bucketed
   iCEM 300 -> 60 samples over 30 iterations (2820 model-cost evaluations), 30
   elites, brown colored noise (beta 2) over raw time, elite retention 3 (10% of
   30), bf16 rollout with fp32 costs / ranking, in-kernel Philox noise.
@@ -10,8 +10,20 @@ Workload (one "step" = one full iCEM plan for one env on each GPU):
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
+Further legs of the same line: ``batched`` (64 envs with history 3 in one plan
+call), ``sharded`` (1024 envs split over the ranks, each rank one batched plan
+call: strong scaling, no collective), ``stress`` (width 384 / 12 layers /
+horizon 10 / 3000 -> 600 samples, 32 envs per rank: 256 envs on 8 GPUs),
+``encoder``, ``reference_gpu`` (the reference's own PyTorch solver on this GPU,
+eager and compiled; 1 GPU only) and ``cpu_baseline`` (the reference's own solver on
+the host cores).
+
 Multi-GPU: one process per GPU (torchrun); each rank plans its own env (weak
 scaling, no collective on the plan path); time is the max over ranks.
+
+--impl reference: the reference's own ICEMSolver.solve (unmodified, from the
+package installed in baseline/_ref) for the same plan on the host cores, fp32,
+all host threads; rank 0 only.
 """
 
 from __future__ import annotations
@@ -41,10 +53,10 @@ F_BLOCK_TOKEN = 2 * (D * 3 * INNER + INNER * D + 2 * D * MLP)  # per token per l
 F_CANON = 9 * L * F_BLOCK_TOKEN + T * L * 2 * D * 6 * D + T * 2 * (A * A + A * 4 * D + 4 * D * D)
 
 
-# DRAM bytes (read + write) of one launch of the dominant kernel classes, from the ncu
-# captures summarised in profiles/k_qkv_attn_s60_w3_6tiles.md, profiles/k_ffn_s60_w3_6tiles.md
-# and profiles/k_partial_gemm_outproj_fc2_s300_w3_8tiles.md (ncu flushes L2 between passes,
-# so these are cold-cache first-touch bytes; the timed run keeps weights in L2).
+# DRAM bytes (read + write) of one launch of the dominant kernel classes, from ncu
+# captures (dram__bytes_read.sum + dram__bytes_write.sum) of one launch at the geometry
+# named beside each figure (ncu flushes L2 between passes, so these are cold-cache
+# first-touch bytes; the timed run keeps weights in L2).
 NCU_TRAFFIC = {
     "qkv_attn": {"bytes": 2121728, "launch": "QKV + attention, 180 rows (60 candidates x window 3), 6 tiles x 16 heads"},
     "ffn": {"bytes": 1268480, "launch": "fused FFN, 180 rows (60 candidates x window 3), 6 tiles x 4 hidden quarters"},
@@ -164,69 +176,53 @@ def cpu_info():
     return platform.processor()
 
 
-def run_cpu_plan(n_plans: int):
-    """The oracle port (numpy) of the reference iCEM chain, on the host cores."""
-    from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
-    from oracle import icem_oracle as io
-    from oracle import lewm_oracle as lo
-
-    desc = ModelDesc()
-    sd = synthetic_state_dict(desc, 0)
-    rng = np.random.default_rng(0)
-    emb = rng.standard_normal((1, 1, desc.dim)).astype(np.float32)
-    goal = rng.standard_normal((1, 1, desc.dim)).astype(np.float32)
-    counts = io.sample_counts(30, 300, 30, 1.25, 60)
-    times = []
-    for _ in range(n_plans):
-        white = [rng.standard_normal((1, c, 2, 25)) for c in counts]
-        noise = [io.color_white_noise(w, 5, 10, 2.0, 5, "raw") for w in white]
-        mean = np.zeros((1, 5, 10), np.float32)
-        var = np.ones_like(mean)
-        t0 = time.perf_counter()
-        io.run_static_icem_chain(lambda e, g, c: lo.get_cost_from_embeddings(e, g, c, sd, desc), emb, goal, mean,
-                                 var, noise, topk=30, elite_retention=3)
-        times.append(time.perf_counter() - t0)
-    return times
+REF_DIR = REPO / "baseline" / "_ref"
+# Solver settings of the bench plan, as ICEMSolver keyword arguments.
+ICEM_KW = dict(num_samples=300, n_steps=30, topk=30, elite_retention=3, colored_noise="brown",
+               colored_noise_time="raw", sample_decay=1.25, sample_count_bucket_size=60, seed=0)
 
 
-def reference_gpu_arm(args):
-    """--impl reference-gpu: the reference's own PyTorch path for the same plan on this GPU.
+def bench_config(world):
+    """The `config` of the headline line; the reference arm prints the same keys."""
+    return {"workload": WORKLOAD, "envs_per_gpu": 1, "candidates_per_plan": 2820, "horizon": 5,
+            "history": 1, "topk": 30, "iterations": 30, "colored_noise": "brown/raw", "elite_retention": 3,
+            "width": 192, "layers": 6, "parallelism": f"env-sharded x{world}, no collective",
+            "l2": "256 MiB write between timed plans"}
 
-    ICEMSolver.solve (lewm/solvers/icem.py) from the installed reference package in
-    baseline/_ref, with the same solver settings, bf16 model-cost autocast and
-    float32 matmul precision "high", timed end to end per plan (CUDA events around
-    solve, batch of one env, p50 over at least 50 plans) eager and with get_cost_from_embeddings under
-    torch.compile(mode="reduce-overhead"), prewarmed on the bucket sizes
-    300/240/180/120/60 as the reference's benchmark does
-    (tools/benchmarks/lewm_plan_benchmark.py:596-700). A comparator for the
-    single-env latency target; the driver's reference arm is the CPU path
-    (--impl reference). Same synthetic weights and latents as the main arm."""
-    ref = REPO / "baseline" / "_ref"
-    if not (ref / "lewm" / "jepa.py").is_file():
-        print(json.dumps({"impl": "reference_gpu", "unavailable": "reference not installed in baseline/_ref"}))
-        return 0
-    sys.path.insert(0, str(ref))
+
+def bench_latents(rank, dim=192):
+    rng = np.random.default_rng(100 + rank)
+    return (rng.standard_normal((1, 1, dim)).astype(np.float32), rng.standard_normal((1, 1, dim)).astype(np.float32))
+
+
+def reference_package():
+    """The unmodified reference (lewm/...) installed in baseline/_ref, or None if absent."""
+    if not (REF_DIR / "lewm" / "jepa.py").is_file():
+        return None
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    from lewm import jepa, module
+    from lewm.solvers import icem
+    return {"jepa": jepa, "module": module, "icem": icem}
+
+
+def reference_solver(ref, device, n_envs=1):
+    """The reference JEPA (synthetic weights, seed 0) and its ICEMSolver at the bench settings."""
     from types import SimpleNamespace
 
     import torch
-    from lewm.jepa import JEPA
-    from lewm.module import ARPredictor, Embedder
-    from lewm.solvers.icem import ICEMSolver
 
     from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
 
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
     desc = ModelDesc()
-    pred = ARPredictor(num_frames=desc.num_frames, depth=desc.depth, heads=desc.heads, mlp_dim=desc.mlp_dim,
-                       input_dim=desc.dim, hidden_dim=desc.dim, dim_head=desc.dim_head)
-    enc = Embedder(input_dim=desc.action_dim, smoothed_dim=desc.smoothed_dim, emb_dim=desc.dim,
-                   mlp_scale=desc.embed_hidden // desc.dim)
-    model = JEPA(encoder=torch.nn.Identity(), predictor=pred, action_encoder=enc, pred_proj=None)
+    pred = ref["module"].ARPredictor(num_frames=desc.num_frames, depth=desc.depth, heads=desc.heads,
+                                     mlp_dim=desc.mlp_dim, input_dim=desc.dim, hidden_dim=desc.dim,
+                                     dim_head=desc.dim_head)
+    enc = ref["module"].Embedder(input_dim=desc.action_dim, smoothed_dim=desc.smoothed_dim, emb_dim=desc.dim,
+                                 mlp_scale=desc.embed_hidden // desc.dim)
+    model = ref["jepa"].JEPA(encoder=torch.nn.Identity(), predictor=pred, action_encoder=enc, pred_proj=None)
     model.load_state_dict({k: torch.from_numpy(v) for k, v in synthetic_state_dict(desc, 0).items()}, strict=True)
-    model = model.to(dev).eval()
-    torch.set_float32_matmul_precision("high")
-    model.set_model_cost_autocast("bf16")
+    model = model.to(device).eval()
     # cached latents: get_cost goes straight to get_cost_from_embeddings
     model.set_embedding_cache(True).set_compile_cost(True)
 
@@ -236,14 +232,86 @@ def reference_gpu_arm(args):
             self.low = -np.inf * np.ones(shape, dtype=np.float32)
             self.high = np.inf * np.ones(shape, dtype=np.float32)
 
-    solver = ICEMSolver(model=model, batch_size=1, num_samples=300, n_steps=30, topk=30, device=dev, seed=0,
-                        elite_retention=3, colored_noise="brown", colored_noise_time="raw", sample_decay=1.25,
-                        sample_count_bucket_size=60)
-    solver.configure(action_space=Box((1, desc.action_dim // 5)), n_envs=1,
+    solver = ref["icem"].ICEMSolver(model=model, batch_size=n_envs, device=device, **ICEM_KW)
+    solver.configure(action_space=Box((n_envs, desc.action_dim // 5)), n_envs=n_envs,
                      config=SimpleNamespace(horizon=5, action_block=5))
-    rng = np.random.default_rng(100)
-    emb = torch.as_tensor(rng.standard_normal((1, 1, desc.dim)), dtype=torch.float32, device=dev)
-    goal = torch.as_tensor(rng.standard_normal((1, 1, desc.dim)), dtype=torch.float32, device=dev)
+    return model, solver
+
+
+def quiet(fn, *a, **kw):
+    """Run a reference call with its progress prints sent to stderr (stdout carries the JSON line)."""
+    import contextlib
+
+    with contextlib.redirect_stdout(sys.stderr):
+        return fn(*a, **kw)
+
+
+def reference_cpu_plans(n_plans: int, warmup: int, rank: int = 0):
+    """The reference's own ICEMSolver.solve on the host cores (fp32, every host thread), the
+    bench plan with the bench's weights and latents. Falls back to the numpy oracle port of
+    the same chain only when the reference package is absent. Returns (seconds per plan, info)."""
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ref = reference_package()
+    emb_np, goal_np = bench_latents(rank)
+    if ref is not None:
+        _, solver = reference_solver(ref, "cpu")
+        info = {"emb": torch.from_numpy(emb_np), "goal_emb": torch.from_numpy(goal_np),
+                "pixels": torch.zeros(1, 1), "goal": torch.zeros(1, 1)}
+        for _ in range(warmup):
+            quiet(solver.solve, dict(info))
+        times = []
+        for _ in range(n_plans):
+            t0 = time.perf_counter()
+            quiet(solver.solve, dict(info))
+            times.append(time.perf_counter() - t0)
+        return times, {"kind": "reference", "cores": threads,
+                       "sample": f"{len(times)} full plans (2820 candidates each) of the reference ICEMSolver.solve "
+                                 f"(fp32, torch {torch.__version__}, {threads} threads) on {cpu_info()}"}
+    # reference package absent: the numpy restatement of the same chain (one thread of numpy)
+    from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
+    from oracle import icem_oracle as io
+    from oracle import lewm_oracle as lo
+
+    desc = ModelDesc()
+    sd = synthetic_state_dict(desc, 0)
+    rng = np.random.default_rng(0)
+    counts = io.sample_counts(30, 300, 30, 1.25, 60)
+    times = []
+    for i in range(warmup + n_plans):
+        noise = [io.color_white_noise(rng.standard_normal((1, c, 2, 25)), 5, 10, 2.0, 5, "raw") for c in counts]
+        mean = np.zeros((1, 5, 10), np.float32)
+        t0 = time.perf_counter()
+        io.run_static_icem_chain(lambda e, g, c: lo.get_cost_from_embeddings(e, g, c, sd, desc), emb_np, goal_np,
+                                 mean, np.ones_like(mean), noise, topk=30, elite_retention=3)
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    return times, {"kind": "port", "cores": 1,
+                   "sample": f"{len(times)} full plans of the numpy oracle port (reference package absent) "
+                             f"on {cpu_info()}"}
+
+
+def reference_gpu_pass(dev, eager_plans=20, compiled_plans=50, warmup=2):
+    """The reference's own PyTorch path for the same plan on this GPU: ICEMSolver.solve from
+    baseline/_ref with the same solver settings, weights and latents, bf16 model-cost autocast
+    and float32 matmul precision "high", one env, CUDA events around each solve; eager, and
+    with get_cost_from_embeddings under torch.compile(mode="reduce-overhead") prewarmed on the
+    bucket sizes 300/240/180/120/60 as the reference's benchmark does
+    (tools/benchmarks/lewm_plan_benchmark.py:596-700). The comparator of the single-env
+    latency target."""
+    import torch
+
+    ref = reference_package()
+    if ref is None:
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    torch.set_float32_matmul_precision("high")
+    model, solver = reference_solver(ref, dev)
+    model.set_model_cost_autocast("bf16")
+    emb_np, goal_np = bench_latents(0)
+    emb = torch.as_tensor(emb_np, device=dev)
+    goal = torch.as_tensor(goal_np, device=dev)
 
     def plans(n):
         ms = []
@@ -252,56 +320,66 @@ def reference_gpu_arm(args):
                     "goal": torch.zeros(1, 1, device=dev)}
             a = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize(dev)
             a.record()
             with torch.inference_mode():
-                solver.solve(info)
+                quiet(solver.solve, info)
             b.record()
             torch.cuda.synchronize(dev)
             ms.append(a.elapsed_time(b))
         return ms
 
-    steps = max(args.steps, 50)  # p50 over at least 50 plans
-    plans(max(args.warmup, 2))
-    eager = plans(steps)
-    out = {"impl": "reference_gpu", "metric": "p50 plan latency (ms), 300-sample iCEM H=5, 1 env",
-           "unit": "ms", "higher_is_better": False, "steps": steps, "warmup": max(args.warmup, 2),
-           "eager_ms": eager, "eager_p50_ms": percentile(eager, 50),
-           "settings": "ICEMSolver.solve, bf16 model-cost autocast, matmul precision high, cached latents"}
+    plans(warmup)
+    eager = plans(eager_plans)
+    out = {"api": "reference ICEMSolver.solve (baseline/_ref), bf16 model-cost autocast, matmul precision high, "
+                  "cached latents, 1 env", "eager_plans": eager_plans, "eager_p50_ms": percentile(eager, 50)}
+    t0 = time.perf_counter()
     try:
         model.get_cost_from_embeddings = torch.compile(model.get_cost_from_embeddings, mode="reduce-overhead",
                                                        fullgraph=False)
         for n in (300, 240, 180, 120, 60):
             with torch.inference_mode():
-                model.get_cost_from_embeddings(torch.zeros(1, 1, desc.dim, device=dev),
-                                               torch.zeros(1, 1, desc.dim, device=dev),
-                                               torch.zeros(1, n, 5, desc.action_dim, device=dev))
+                model.get_cost_from_embeddings(torch.zeros(1, 1, 192, device=dev), torch.zeros(1, 1, 192, device=dev),
+                                               torch.zeros(1, n, 5, 10, device=dev))
         torch.cuda.synchronize(dev)
-        plans(max(args.warmup, 2))
-        comp = plans(steps)
-        out.update({"compiled_ms": comp, "compiled_p50_ms": percentile(comp, 50)})
+        plans(warmup)
+        out["compile_s"] = time.perf_counter() - t0
+        comp = plans(compiled_plans)
+        out.update({"compiled_plans": compiled_plans, "compiled_p50_ms": percentile(comp, 50)})
     except Exception as exc:  # torch.compile unavailable or failing on the box: say so
         out["compiled"] = f"failed: {type(exc).__name__}: {str(exc)[:200]}"
+    del model, solver
+    torch.cuda.empty_cache()
+    return out
+
+
+def reference_gpu_arm(args):
+    """--impl reference-gpu: only the reference_gpu leg, as its own JSON line."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    out = reference_gpu_pass(dev, eager_plans=max(args.steps, 20), compiled_plans=max(args.steps, 50),
+                             warmup=max(args.warmup, 2))
+    out["impl"] = "reference_gpu"
     print(json.dumps(out))
     return 0
 
 
 def reference_arm(args, rank, world):
-    """--impl reference: the reference algorithm's CPU implementation (numpy oracle port) on host cores."""
+    """--impl reference: the reference's own ICEMSolver.solve on the host cores (rank 0 only)."""
     if rank != 0:
         return 0
-    threads = os.cpu_count() or 1
-    run_cpu_plan(1) if args.warmup > 0 else None
-    times = run_cpu_plan(max(args.steps, 1))
+    times, info = reference_cpu_plans(max(args.steps, 1), args.warmup, rank)
     per = float(np.mean(times))
     value = 1.0 / per
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "plans/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3,
         "p50_plan_ms": percentile([t * 1e3 for t in times], 50), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "envs_per_gpu": 1, "candidates_per_plan": 2820},
-        "cpu_baseline": {"value": value, "unit": "plans/s", "cores": threads, "kind": "port",
-                         "sample": f"{len(times)} full plans (2820 candidates each) on {cpu_info()}"},
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (random-init weights, N(0,1) latents)",
+        "config": bench_config(world),
+        "cpu_baseline": dict(info, value=value, unit="plans/s"),
         "e2e": {"value": value, "unit": "plans/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -392,6 +470,9 @@ def main() -> int:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-gpu"])
     ap.add_argument("--cpu-baseline-plans", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true", help="skip the reference PyTorch GPU comparator")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the 1024-env sharded leg")
+    ap.add_argument("--no-stress", action="store_true", help="skip the width-384 stress leg")
     ap.add_argument("--model-cost", type=int, default=0, metavar="S",
                     help="profiling case: time R model-cost calls of S candidates per env (horizon 5; 1 env "
                          "with history 1, or --envs B with history 3) and exit; no bench line")
@@ -437,9 +518,9 @@ def main() -> int:
     desc = ModelDesc()
     rt = Runtime(desc, synthetic_state_dict(desc, 0), dev)
     opts = plan_options()
-    rng = np.random.default_rng(100 + rank)
-    emb = torch.as_tensor(rng.standard_normal((1, 1, desc.dim)), dtype=torch.float32, device=dev)
-    goal = torch.as_tensor(rng.standard_normal((1, 1, desc.dim)), dtype=torch.float32, device=dev)
+    emb_np, goal_np = bench_latents(rank, desc.dim)
+    emb = torch.as_tensor(emb_np, device=dev)
+    goal = torch.as_tensor(goal_np, device=dev)
     mean = torch.zeros(1, 5, 10, device=dev)
     std = torch.ones(1, 5, 10, device=dev)
     flush = torch.zeros(64 * 1024 * 1024, device=dev)  # 256 MiB
@@ -515,6 +596,12 @@ def main() -> int:
     # ---------------------------------------------------------------- batched planning (64 envs, history 3)
     batched = batched_pass(rt, dev, args.steps, args.warmup, flush)
 
+    # ---------------------------------------------------------------- 1024 envs split over the ranks
+    sharded = sharded_pass(rt, dev, rank, world, barrier, dist, flush) if not args.no_sharded else None
+
+    # ---------------------------------------------------------------- width 384 / 12 layers, 32 envs per rank
+    stress = stress_pass(dev, rank, world, barrier, dist, flush) if not args.no_stress else None
+
     # ---------------------------------------------------------------- observation encoder (64 images, 224 px)
     encoder = encoder_pass(dev, args.steps, args.warmup, flush)
 
@@ -527,10 +614,7 @@ def main() -> int:
         "warmup": args.warmup, "ms_per_step": worst_ms / args.steps, "p50_plan_ms": p50,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init weights, N(0,1) latents)",
-        "config": {"workload": WORKLOAD, "envs_per_gpu": 1, "candidates_per_plan": 2820, "horizon": 5,
-                   "history": 1, "topk": 30, "iterations": 30, "colored_noise": "brown/raw", "elite_retention": 3,
-                   "width": 192, "layers": 6, "parallelism": f"env-sharded x{world}, no collective",
-                   "l2": "256 MiB write between timed plans"},
+        "config": bench_config(world),
         "e2e": {"value": e2e_value, "unit": "plans/s", "p50_ms": percentile(e2e_ms, 50),
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "api": "B200ICEMSolver.solve with pinned host emb/goal"},
@@ -542,15 +626,21 @@ def main() -> int:
         "roofline": kinfo["roofline"],
         "kernel_classes": kinfo["classes"],
         "batched": batched,
+        "sharded": sharded,
+        "stress": stress,
         "encoder": encoder,
         "clocks": clocks.summary(),
     }
+    if rank == 0 and world == 1 and not args.no_reference_gpu:
+        ref_gpu = reference_gpu_pass(dev)
+        if "eager_p50_ms" in ref_gpu:
+            ref_gpu["speedup_vs_eager"] = ref_gpu["eager_p50_ms"] / p50
+        if "compiled_p50_ms" in ref_gpu:
+            ref_gpu["speedup_vs_compiled"] = ref_gpu["compiled_p50_ms"] / p50
+        line["reference_gpu"] = ref_gpu
     if rank == 0 and not args.no_cpu_baseline:
-        times = run_cpu_plan(max(args.cpu_baseline_plans, 1))
-        line["cpu_baseline"] = {"value": 1.0 / float(np.mean(times)), "unit": "plans/s",
-                                "cores": os.cpu_count() or 1, "kind": "port",
-                                "sample": f"{len(times)} full plans (2820 candidates) of the numpy oracle port "
-                                          f"on {cpu_info()}"}
+        times, info = reference_cpu_plans(max(args.cpu_baseline_plans, 1), 1, rank)
+        line["cpu_baseline"] = dict(info, value=1.0 / float(np.mean(times)), unit="plans/s")
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -558,6 +648,113 @@ def main() -> int:
         print(json.dumps(line), flush=True)
     rt.close()
     return 0
+
+
+def timed_shard_calls(dev, barrier, dist, flush, plan_call, n_calls):
+    """Time `n_calls` plan calls of this rank (CUDA events, host barrier first, L2 flushed before
+    each) and return the max over ranks of the summed call time in ms."""
+    import torch
+
+    stream = torch.cuda.current_stream(dev)
+    total = 0.0
+    for _ in range(n_calls):
+        l2_flush(flush)
+        barrier()
+        torch.cuda.synchronize(dev)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        plan_call()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        total += a.elapsed_time(b)
+    worst = torch.tensor([total], device=dev)
+    if dist is not None:
+        dist.all_reduce(worst, op=dist.ReduceOp.MAX)
+    return float(worst.item())
+
+
+def sharded_pass(rt, dev, rank, world, barrier, dist, flush, n_envs=1024, history=3, n_calls=3):
+    """1024 independent envs (own N(0,1) latents, history 3) split contiguously over the ranks
+    (lewm_flash_b200.shard.env_range); each rank plans its envs as one batched plan call, with
+    no collective in the timed region. plans/s = 1024 / (max over ranks of the call time):
+    total work fixed, so strong scaling over the GPU count. The plans are gathered to rank 0
+    on the host afterwards (gather_plans, gloo), outside the timed region."""
+    import torch
+
+    from lewm_flash_b200.shard import env_range, gather_plans, plan_shard
+
+    opts = plan_options()
+    rng = np.random.default_rng(3)
+    emb = torch.as_tensor(rng.standard_normal((n_envs, history, 192)), dtype=torch.float32)
+    goal = torch.as_tensor(rng.standard_normal((n_envs, 1, 192)), dtype=torch.float32)
+    s, e = env_range(n_envs, rank, world)
+    inputs = {"emb": emb.to(dev), "goal_emb": goal.to(dev), "mean": torch.zeros(n_envs, 5, 10, device=dev),
+              "std": torch.ones(n_envs, 5, 10, device=dev)}
+    box = {}
+
+    def call(idx=[7000]):
+        idx[0] += 1
+        box["out"] = plan_shard(lambda **t: rt.plan(opts, t["emb"], t["goal_emb"], t["mean"], t["std"],
+                                                    plan_index=idx[0])[:3], inputs, rank, world)
+
+    call()  # warm-up: workspace growth and graph capture for this shape
+    rt.sync()
+    worst_ms = timed_shard_calls(dev, barrier, dist, flush, call, n_calls)
+    rt.sync()
+    per_call = worst_ms / n_calls
+    gathered = None
+    if dist is not None:
+        group = dist.new_group(backend="gloo")
+        res = gather_plans(box["out"], n_envs, [(5, 10), (5, 10), ()], group=group)
+        gathered = None if res is None else int(res[0].shape[0])
+        dist.destroy_process_group(group)
+    else:
+        gathered = int(box["out"][0].shape[0])
+    return {"workload": f"icem_bucketed_300_{n_envs}env_h{history}_bf16", "envs": n_envs, "envs_this_rank": e - s,
+            "history": history, "plans_per_s": n_envs / (per_call / 1e3), "ms_per_call": per_call, "calls": n_calls,
+            "gathered_envs": gathered, "scaling": "strong",
+            "note": "each rank plans its contiguous env range as one batched plan call; time = max over ranks; "
+                    "device-resident inputs, L2 flushed between calls"}
+
+
+def stress_pass(dev, rank, world, barrier, dist, flush, envs_per_rank=32, n_calls=1):
+    """Scaled stress configuration: predictor width 384, 12 layers, 16 heads, MLP 1536, action
+    dim 10, horizon 10, history 3, iCEM 3000 samples / 300 elites / 30 iterations with the
+    bucketed schedule (decay 1.25, bucket 600: 28,200 candidates per env), brown noise, bf16
+    rollout; 32 envs per rank (256 envs on 8 GPUs), one batched plan call per rank."""
+    import torch
+
+    from lewm_flash_b200.model import STRESS_DESC, synthetic_state_dict
+    from lewm_flash_b200.runtime import PlanOptions, Runtime
+
+    rt = Runtime(STRESS_DESC, synthetic_state_dict(STRESS_DESC, 5), dev)
+    opts = PlanOptions(num_samples=3000, topk=300, n_steps=30, sample_decay=1.25, sample_count_bucket_size=600,
+                       elite_retention=30, beta=2.0, time_axis="raw", action_block=5, seed=0)
+    rng = np.random.default_rng(500 + rank)
+    emb = torch.as_tensor(rng.standard_normal((envs_per_rank, 3, 384)), dtype=torch.float32, device=dev)
+    goal = torch.as_tensor(rng.standard_normal((envs_per_rank, 1, 384)), dtype=torch.float32, device=dev)
+    mean = torch.zeros(envs_per_rank, 10, 10, device=dev)
+    std = torch.ones(envs_per_rank, 10, 10, device=dev)
+    idx = [9000]
+
+    def call():
+        idx[0] += 1
+        rt.plan(opts, emb, goal, mean, std, plan_index=idx[0])
+
+    call()
+    rt.sync()
+    worst_ms = timed_shard_calls(dev, barrier, dist, flush, call, n_calls)
+    rt.sync()
+    rt.close()
+    torch.cuda.empty_cache()
+    per_call = worst_ms / n_calls
+    flops = 1809.9e6 * 28200 * envs_per_rank
+    return {"workload": "icem_bucketed_3000_w384_l12_t10_h3_bf16", "envs_per_rank": envs_per_rank,
+            "envs": envs_per_rank * world, "candidates_per_plan": 28200,
+            "plans_per_s": envs_per_rank * world / (per_call / 1e3), "ms_per_call": per_call, "calls": n_calls,
+            "tflops_per_gpu": flops / (per_call / 1e3) / 1e12, "scaling": "weak",
+            "note": "one batched plan call per rank; time = max over ranks; elite retention 30 (10% of 300)"}
 
 
 def batched_pass(rt, dev, steps, warmup, flush, n_envs=64, history=3):

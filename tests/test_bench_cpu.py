@@ -29,7 +29,14 @@ def test_reference_arm_prints_one_contract_line():
     assert d["impl"] == "reference" and d["unit"] == "plans/s" and d["value"] > 0
     assert d["config"]["workload"]
     assert set(d["cpu_baseline"]) >= {"value", "unit", "cores", "kind", "sample"}
-    assert d["cpu_baseline"]["kind"] in ("port", "reference")
+    # The reference's own ICEMSolver.solve when its package is installed, else the labelled port.
+    want_kind = "reference" if (REPO / "baseline" / "_ref" / "lewm" / "jepa.py").is_file() else "port"
+    assert d["cpu_baseline"]["kind"] == want_kind
+    # Same config keys as the B200 arm's line.
+    sys.path.insert(0, str(REPO))
+    import bench
+
+    assert d["config"] == bench.bench_config(d["n_gpus"])
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["value"] == d["value"]
 
 
