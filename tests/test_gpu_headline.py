@@ -148,6 +148,7 @@ def test_full_plan_on_reference_noise_tracks_reference(case, runtimes):
     dev = rt.device
     kw = json.loads(str(d["solver"]))
     k, n = kw["topk"], int(d["n_iters"])
+    retention = kw["elite_retention"]
     opts = _opts(kw)
     assert opts.n_steps == n
     counts = [int(c) for c in d["counts"]]
@@ -171,15 +172,26 @@ def test_full_plan_on_reference_noise_tracks_reference(case, runtimes):
                 np.testing.assert_allclose(cand_dev[i][b], traj[i]["candidates"][b], rtol=1e-5, atol=1e-4)
                 rel = np.max(np.abs(cost_dev[i][b] - ref_c) / np.abs(ref_c))
                 assert rel <= COST_RTOL, f"env {b} iteration {i}: cost rel err {rel:.2e}"
-                if set(idx_dev[i, b].tolist()) != set(d[f"inds_{i}"][b].tolist()):
-                    flip = i
+                # The chain leaves the reference's trajectory when the elite set changes (the
+                # refit moves) or the order of the ranks it carries over changes (the retained
+                # elites and the best elite move).
+                dev_i, ref_i = idx_dev[i, b].tolist(), d[f"inds_{i}"][b].tolist()
+                keep = max(retention, 1)
+                gap = None
+                if set(dev_i) != set(ref_i):
                     s = np.sort(ref_c)
                     gap = (s[k] - s[k - 1]) / abs(s[k - 1])
-                    assert gap <= NEAR_TIE_REL, (
-                        f"env {b}: elite flip at iteration {i} with a reference boundary gap of {gap:.2e}")
-                    report.append(f"env {b}: first elite flip at iteration {i} (reference boundary gap {gap:.1e})")
+                    what = "elite set"
+                elif dev_i[:keep] != ref_i[:keep]:
+                    gap = max(abs(ref_c[a] - ref_c[r]) / abs(ref_c[r])
+                              for a, r in zip(dev_i[:keep], ref_i[:keep]) if a != r)
+                    what = "order of the carried-over elites"
+                if gap is not None:
+                    flip = i
+                    assert gap <= NEAR_TIE_REL, f"env {b}: {what} changed at iteration {i} with a gap of {gap:.2e}"
+                    report.append(f"env {b}: {what} first differs at iteration {i} (reference cost gap {gap:.1e})")
         if flip == n:
-            report.append(f"env {b}: no elite flip in {n} iterations")
+            report.append(f"env {b}: on the reference's trajectory for all {n} iterations")
     # Off the reference's trajectory: the device's costs against the fp32 model on its own candidates.
     for i in (n // 2, n - 1):
         want = lo.get_cost_from_embeddings(d["emb"], d["goal"], cand_dev[i], sd, desc)
