@@ -45,7 +45,10 @@ typedef struct lewm_ctx lewm_ctx;
 /* Predictor + action-encoder shape (reference lewm/module.py:189-285).
  * Supported: dim in {192, 384}, dim_head == 64, heads <= 16, mlp_dim and
  * embed_hidden multiples of 128, action_dim and smoothed_dim <= 16,
- * num_frames <= 8, pred_proj_hidden == 0 (Identity head). */
+ * num_frames <= 8. pred_proj (JEPA.predict, lewm/jepa.py:106-114): Identity
+ * (pred_proj_hidden == 0), or the MLP head of lewm/module.py:217-240 at dim 192
+ * with a hidden width that is a multiple of 256 and LayerNorm / BatchNorm1d
+ * (eval, eps 1e-5) / no norm. */
 typedef struct lewm_model_desc {
   int32_t dim;
   int32_t depth;
@@ -69,6 +72,9 @@ typedef struct lewm_model_desc {
  *     mlp.net.1.weight, .bias, mlp.net.4.weight, .bias
  *   transformer.norm.weight, .bias
  *   action_encoder.patch_embed.weight, .bias, embed.0.weight, .bias, embed.2.weight, .bias
+ *   with an MLP head: pred_proj.net.0.weight, .bias, then net.1.weight, .bias (LayerNorm)
+ *     or net.1.weight, .bias, .running_mean, .running_var (BatchNorm1d), then
+ *     net.3.weight, .bias
  * (host memory). */
 LEWM_API size_t lewm_weight_count(const lewm_model_desc* desc);
 

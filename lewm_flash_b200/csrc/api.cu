@@ -62,6 +62,10 @@ struct Workspace {
   float* fcost = nullptr;
   float* W = nullptr;
   uint32_t* rng = nullptr;   // [seed, plan index]
+  __nv_bfloat16* pp_in = nullptr;   // pred_proj head: operand, hidden operand, LayerNorm rows, output rows
+  __nv_bfloat16* pp_hid = nullptr;
+  float* pp_hid32 = nullptr;
+  float* pp_out = nullptr;
   float* emb_in = nullptr;   // staged plan inputs (graph path)
   float* goal_in = nullptr;
   float* lohi = nullptr;     // action low | high
@@ -99,6 +103,7 @@ struct lewm_ctx {
   std::string err;
   void* d_weights = nullptr;
   DevWeights w{};
+  MlpHead pp{};  // pred_proj MLP head (P == 0: Identity)
   uint32_t* d_status = nullptr;
   Workspace ws;
   WsReq cap{};
@@ -162,8 +167,14 @@ lewm_status check_desc(const lewm_model_desc* d, ModelDims* md) {
   if (d->action_dim > 16 || d->smoothed_dim > 16)
     return fail(nullptr, LEWM_UNSUPPORTED_SHAPE, "action_dim/smoothed_dim must be <= 16");
   if (d->num_frames > 8) return fail(nullptr, LEWM_UNSUPPORTED_SHAPE, "num_frames must be <= 8");
-  if (d->pred_proj_hidden != 0)
-    return fail(nullptr, LEWM_UNSUPPORTED_SHAPE, "pred_proj MLP head not supported (Identity only)");
+  if (d->pred_proj_hidden != 0) {  // MLP head: runs on the 192-wide projector kernels
+    if (d->dim != 192 || d->pred_proj_hidden % 256 != 0)
+      return fail(nullptr, LEWM_UNSUPPORTED_SHAPE,
+                  "pred_proj MLP head needs dim 192 and a hidden width that is a multiple of 256 (got %d, %d)",
+                  d->dim, d->pred_proj_hidden);
+    if (d->pred_proj_norm < 0 || d->pred_proj_norm > 2)
+      return fail(nullptr, LEWM_INVALID_ARG, "pred_proj_norm must be 0, 1 or 2, got %d", d->pred_proj_norm);
+  }
   md->D = d->dim;
   md->L = d->depth;
   md->heads = d->heads;
@@ -173,6 +184,8 @@ lewm_status check_desc(const lewm_model_desc* d, ModelDims* md) {
   md->As = d->smoothed_dim;
   md->eh = d->embed_hidden;
   md->frames = d->num_frames;
+  md->pp_hidden = d->pred_proj_hidden;
+  md->pp_norm = d->pred_proj_norm;
   return LEWM_OK;
 }
 
@@ -184,6 +197,7 @@ size_t weight_count(const ModelDims& m) {
   n += per_layer * m.L;
   n += 2 * D;
   n += (size_t)m.As * m.A + m.As + (size_t)m.eh * m.As + m.eh + D * m.eh + D;
+  if (m.pp_hidden) n += mlp_head_floats(m.pp_hidden, m.pp_norm);
   return n;
 }
 
@@ -238,7 +252,9 @@ lewm_status pack_weights(lewm_ctx* c, const float* wts, size_t n) {
   const float* e1_b = take(m.eh);
   const float* e2_w = take((size_t)D * m.eh);
   const float* e2_b = take(D);
+  const float* pp_w = m.pp_hidden ? take(mlp_head_floats(m.pp_hidden, m.pp_norm)) : nullptr;
   if ((size_t)(p - wts) != n) return fail(c, LEWM_INVALID_ARG, "weight walk mismatch");
+  if (pp_w) LEWM_CK(c, mlp_head_create(&c->pp, pp_w, m.pp_hidden, m.pp_norm, 1e-5f));
 
   std::vector<uint8_t> buf;
   auto alloc = [&](size_t bytes) {
@@ -406,6 +422,11 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   const size_t o_embin = carve(r.B * r.T * (size_t)m.D * 4);
   const size_t o_goalin = carve(r.B * (size_t)m.D * 4);
   const size_t o_lohi = carve(2 * (size_t)m.A * 4);
+  const size_t pp_tiles = m.pp_hidden ? (r.n_cand + 127) / 128 : 0;
+  const size_t o_ppin = carve(pp_tiles * (m.D / 64) * 128 * 64 * 2);
+  const size_t o_pphid = carve(pp_tiles * (size_t)(m.pp_hidden / 64) * 128 * 64 * 2);
+  const size_t o_pph32 = carve(m.pp_norm == 1 ? pp_tiles * 128 * (size_t)m.pp_hidden * 4 : 0);
+  const size_t o_ppout = carve(m.pp_hidden ? r.n_cand * (size_t)m.D * 4 : 0);
   void* base = nullptr;
   LEWM_CK(c, cudaMalloc(&base, off));
   auto* b = static_cast<uint8_t*>(base);
@@ -438,6 +459,10 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   ws.emb_in = reinterpret_cast<float*>(b + o_embin);
   ws.goal_in = reinterpret_cast<float*>(b + o_goalin);
   ws.lohi = reinterpret_cast<float*>(b + o_lohi);
+  ws.pp_in = reinterpret_cast<__nv_bfloat16*>(b + o_ppin);
+  ws.pp_hid = reinterpret_cast<__nv_bfloat16*>(b + o_pphid);
+  ws.pp_hid32 = reinterpret_cast<float*>(b + o_pph32);
+  ws.pp_out = reinterpret_cast<float*>(b + o_ppout);
   c->cap = r;
   c->have_ws = true;
   c->W_n = -1;
@@ -455,7 +480,8 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
   RolloutBufs b{emb,        emb_pc,    goal,      goal_pc, cand,      c->ws.act_a, c->ws.mod,
                 c->ws.x,    c->ws.x2,  c->ws.xs,  c->ws.part_a, c->ws.part_b, c->ws.part_stride, c->ws.a_op,
                 c->ws.attn, c->ws.h,
-                c->ws.pred, costs, c->ws.kvc, kv_positions(H, HS)};
+                c->ws.pred, costs, c->ws.kvc, kv_positions(H, HS),
+                m.pp_hidden ? c->ws.pp_in : nullptr, m.pp_hidden ? c->ws.pp_out : nullptr};
   const int n_calls = T - H + 1;
   auto geom = [&](int k) {
     const int end = H + k;
@@ -548,6 +574,10 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
     b.xn = (k & 1) ? c->ws.x : c->ws.x2;
     if (k == 0) LEWM_CK(c, launch_prep0(m, c->w, g, b, st, &c->prof));
     LEWM_CK(c, launch_call(m, c->w, g, b, c->d_status, st, &c->prof));
+    if (m.pp_hidden) {  // pred_proj on the new predictions (JEPA.predict, lewm/jepa.py:106-114)
+      LEWM_CK(c, mlp_head_run(c->pp, c->ws.pp_in, NC, c->ws.pp_hid, c->ws.pp_hid32, c->ws.pp_out, c->d_status, st));
+      LEWM_CK(c, launch_final_post(m, c->w, g, b, st, &c->prof));
+    }
   }
   return LEWM_OK;
 }
@@ -854,6 +884,7 @@ void lewm_destroy(lewm_ctx* c) {
   if (c->cap_stream) cudaStreamDestroy(c->cap_stream);
   if (c->ws.base) cudaFree(c->ws.base);
   if (c->d_weights) cudaFree(c->d_weights);
+  mlp_head_destroy(&c->pp);
   if (c->d_status) cudaFree(c->d_status);
   delete c;
 }

@@ -34,6 +34,7 @@
 
 #include "lewm_b200.h"
 #include "lewm_common.cuh"
+#include "lewm_internal.h"
 
 namespace lewm {
 namespace vit {
@@ -1246,3 +1247,109 @@ void lewm_encoder_destroy(lewm_encoder* e) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- MLP head (predictor pred_proj)
+// The reference MLP (lewm/module.py:217-240) at input and output width 192: Linear(192 -> P),
+// LayerNorm(P) / BatchNorm1d(P) in eval / no norm, GELU, Linear(P -> 192). The predictor's
+// pred_proj head (JEPA.predict, lewm/jepa.py:106-114) runs on the projector kernels of the
+// encoder: BatchNorm folds into a per-column scale / shift of the first GEMM's accumulator,
+// LayerNorm runs as a row pass over the fp32 hidden (eps 1e-5, nn.LayerNorm's default).
+namespace lewm {
+
+size_t mlp_head_floats(int P, int norm) {
+  return (size_t)P * kD + P + (norm == 1 ? 2 * (size_t)P : norm == 2 ? 4 * (size_t)P : 0) + (size_t)kD * P + kD;
+}
+
+cudaError_t mlp_head_create(MlpHead* h, const float* w, int P, int norm, float eps) {
+  *h = MlpHead{};
+  h->P = P;
+  h->norm = norm;
+  h->eps = eps;
+  // bf16 blocks: W1 as 256-column chunks [P / 256][3][256 x 64], W2 [1][P / 64][192 x 64].
+  const size_t n1 = (size_t)P * kD, n2 = (size_t)kD * P;
+  std::vector<uint16_t> hb(n1 + n2);
+  pack_blocks(w, P, kD, 256, hb, 0);
+  const float* b1 = w + n1;
+  const float* np = b1 + P;
+  std::vector<float> scale(P, 1.f), shift(b1, b1 + P), lng, lnb;
+  const float* w2 = np;
+  if (norm == 1) {
+    lng.assign(np, np + P);
+    lnb.assign(np + P, np + 2 * P);
+    w2 = np + 2 * P;
+  } else if (norm == 2) {
+    const float *gam = np, *bet = np + P, *rm = np + 2 * P, *rv = np + 3 * P;
+    for (int i = 0; i < P; ++i) {
+      const double sc = (double)gam[i] / std::sqrt((double)rv[i] + (double)eps);
+      scale[i] = (float)sc;
+      shift[i] = (float)(((double)b1[i] - (double)rm[i]) * sc + (double)bet[i]);
+    }
+    w2 = np + 4 * P;
+  }
+  pack_blocks(w2, kD, P, kD, hb, n1);
+  const float* b2 = w2 + n2;
+  std::vector<float> fv;
+  auto take = [&](const float* src, size_t n) {
+    const size_t o = fv.size();
+    fv.insert(fv.end(), src, src + n);
+    while (fv.size() % 64) fv.push_back(0.f);  // 256-byte aligned vectors
+    return o;
+  };
+  const size_t o_scale = take(scale.data(), P), o_shift = take(shift.data(), P), o_b2 = take(b2, kD);
+  const size_t o_lng = norm == 1 ? take(lng.data(), P) : 0, o_lnb = norm == 1 ? take(lnb.data(), P) : 0;
+  const size_t bf_bytes = (hb.size() * 2 + 1023) / 1024 * 1024;
+  cudaError_t ce = cudaMalloc(&h->d_w, bf_bytes + fv.size() * 4);
+  if (ce == cudaSuccess) ce = cudaMemcpy(h->d_w, hb.data(), hb.size() * 2, cudaMemcpyHostToDevice);
+  if (ce == cudaSuccess)
+    ce = cudaMemcpy(static_cast<uint8_t*>(h->d_w) + bf_bytes, fv.data(), fv.size() * 4, cudaMemcpyHostToDevice);
+  if (ce == cudaSuccess) ce = set_gemm_smem<256, EPI_GELU_OP>();
+  if (ce == cudaSuccess) ce = set_gemm_smem<256, EPI_F32>();
+  if (ce == cudaSuccess) ce = set_gemm_smem<192, EPI_F32>();
+  if (ce != cudaSuccess) {
+    mlp_head_destroy(h);
+    return ce;
+  }
+  const auto* wb = static_cast<const __nv_bfloat16*>(h->d_w);
+  const auto* wf = reinterpret_cast<const float*>(static_cast<const uint8_t*>(h->d_w) + bf_bytes);
+  h->w1 = wb;
+  h->w2 = wb + n1;
+  h->scale = wf + o_scale;
+  h->shift = wf + o_shift;
+  h->b2 = wf + o_b2;
+  h->ln_g = norm == 1 ? wf + o_lng : nullptr;
+  h->ln_b = norm == 1 ? wf + o_lnb : nullptr;
+  return cudaSuccess;
+}
+
+void mlp_head_destroy(MlpHead* h) {
+  if (h->d_w) cudaFree(h->d_w);
+  *h = MlpHead{};
+}
+
+cudaError_t mlp_head_run(const MlpHead& h, const __nv_bfloat16* in_op, int n_rows, __nv_bfloat16* hid_op,
+                         float* hid32, float* out, uint32_t* status, cudaStream_t st) {
+  const int tiles = (n_rows + 127) / 128;
+  EpiArgs pa{};
+  pa.rows = n_rows;
+  pa.n_total = h.P;
+  if (h.norm == 1) {
+    pa.x = hid32;
+    pa.bias = h.shift;  // the Linear bias (scale 1 without BatchNorm)
+    launch_gemm<256, EPI_F32>(in_op, kHB, h.w1, tiles, h.P / 256, pa, status, st);
+    k_vit_ln_wide<<<tiles * 16, 256, 0, st>>>(hid32, h.P, n_rows, tiles * 128, h.eps, h.ln_g, h.ln_b, 1, hid_op);
+  } else {
+    pa.op = hid_op;
+    pa.scale = h.scale;
+    pa.bias = h.shift;
+    launch_gemm<256, EPI_GELU_OP>(in_op, kHB, h.w1, tiles, h.P / 256, pa, status, st);
+  }
+  EpiArgs oa{};
+  oa.rows = n_rows;
+  oa.n_total = kD;
+  oa.x = out;
+  oa.bias = h.b2;
+  launch_gemm<192, EPI_F32>(hid_op, h.P / 64, h.w2, tiles, 1, oa, status, st);
+  return cudaGetLastError();
+}
+
+}  // namespace lewm

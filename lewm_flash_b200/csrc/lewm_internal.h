@@ -64,6 +64,7 @@ struct DevWeights {
 
 struct ModelDims {
   int D, L, heads, inner, mlp, A, As, eh, frames;
+  int pp_hidden, pp_norm;  // pred_proj MLP head hidden width (0: Identity) and norm kind
 };
 
 // One predictor call of the rollout over every candidate.
@@ -124,6 +125,11 @@ struct RolloutBufs {
   // shared k/v scratch). Null with kvc_pos 0 when no call of the rollout reads it.
   float* kvc;
   int kvc_pos;
+  // pred_proj head (null: Identity): k_final writes the final-LayerNorm rows of the calls'
+  // new predictions into pp_in ([n_cand / 128][D / 64][128 x 64] bf16 operand blocks, row =
+  // candidate); after the head, k_final_post reads the head's fp32 output rows pp_out [n_cand][D].
+  __nv_bfloat16* pp_in;
+  const float* pp_out;
 };
 
 // Optional per-launch event profiler (host side). When `on`, every launch site
@@ -216,6 +222,11 @@ cudaError_t launch_call(const ModelDims& md, const DevWeights& w, const CallGeom
 // Layer-0 residual rows (history + position) of the first predictor call of a rollout.
 cudaError_t launch_prep0(const ModelDims& md, const DevWeights& w, const CallGeom& g, const RolloutBufs& b,
                          cudaStream_t st, Prof* prof);
+// With a pred_proj head: the second half of a call's final step once the head has written
+// b.pp_out (cost on the last call, else the prediction's history slot and the next call's
+// layer-0 rows).
+cudaError_t launch_final_post(const ModelDims& md, const DevWeights& w, const CallGeom& g, const RolloutBufs& b,
+                              cudaStream_t st, Prof* prof);
 
 // iCEM kernels (icem_kernels.cu).
 struct SampleParams {
@@ -240,6 +251,33 @@ cudaError_t launch_sample(const SampleParams& p, cudaStream_t st);
 cudaError_t launch_set_rng(uint32_t* rng, uint32_t seed, uint32_t plan, cudaStream_t st);
 // One wait on an mbarrier that nothing arrives on: expires after the status block's limit.
 cudaError_t launch_wait_selftest(uint32_t* status, cudaStream_t st);
+
+// MLP head at input / output width 192 (reference lewm/module.py:217-240): Linear(192 -> P),
+// LayerNorm / BatchNorm1d (eval) / none, GELU, Linear(P -> 192); the predictor's pred_proj.
+// Runs on the encoder's projector kernels (encoder.cu).
+struct MlpHead {
+  int P = 0;     // hidden width, a multiple of 256
+  int norm = 0;  // 0 none, 1 LayerNorm, 2 BatchNorm1d (folded into scale / shift)
+  float eps = 1e-5f;
+  void* d_w = nullptr;
+  const __nv_bfloat16* w1 = nullptr;  // [P / 256][3][256 x 64] blocks
+  const __nv_bfloat16* w2 = nullptr;  // [P / 64][192 x 64] blocks
+  const float* scale = nullptr;  // [P] BatchNorm scale (1 otherwise)
+  const float* shift = nullptr;  // [P] first Linear's bias, BatchNorm-folded
+  const float* ln_g = nullptr;   // [P] LayerNorm affine (norm == 1)
+  const float* ln_b = nullptr;
+  const float* b2 = nullptr;     // [192]
+};
+// Host weights in state-dict order: net.0.weight [P x 192], net.0.bias, norm parameters
+// (LayerNorm: weight, bias; BatchNorm1d: weight, bias, running_mean, running_var),
+// net.3.weight [192 x P], net.3.bias.
+size_t mlp_head_floats(int P, int norm);
+cudaError_t mlp_head_create(MlpHead* h, const float* w, int P, int norm, float eps);
+void mlp_head_destroy(MlpHead* h);
+// out[n_rows][192] (fp32) = head(rows of in_op), in_op: [ceil(n_rows / 128)][3][128 x 64]
+// bf16 operand blocks; hid_op: [tiles][P / 64][128 x 64]; hid32: [tiles * 128][P] (LayerNorm only).
+cudaError_t mlp_head_run(const MlpHead& h, const __nv_bfloat16* in_op, int n_rows, __nv_bfloat16* hid_op,
+                         float* hid32, float* out, uint32_t* status, cudaStream_t st);
 
 // Sets the thread's error text that lewm_last_error(NULL) returns (context-free calls).
 void set_noctx_error(const char* msg);

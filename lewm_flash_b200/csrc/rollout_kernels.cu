@@ -1782,12 +1782,17 @@ __global__ void __launch_bounds__(kThreads) k_ffn(DevWeights w, ModelDims md, Ca
 // LayerNorm of this call's last token, appends it to the history and prepares its row;
 // the other warps prepare their rows from the history (observation embeddings or
 // earlier predictions), which this call does not change.
+// With a pred_proj head the step runs in two launches around the head's GEMMs: mode 1, a
+// warp per candidate, writes the final-LayerNorm row of the new prediction as bf16 into the
+// head's operand (b.pp_in); mode 2 is the step above with the new prediction read from the
+// head's output rows (b.pp_out). Mode 0: no head (Identity).
 template <int D>
-__global__ void __launch_bounds__(128) k_final(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b) {
+__global__ void __launch_bounds__(128) k_final(DevWeights w, ModelDims md, CallGeom g, RolloutBufs b, int mode) {
   griddep_wait();
   griddep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rows_per_cand = g.last ? 1 : g.next_rpc;  // rows the next call processes per candidate
+  // rows the next call processes per candidate (one warp per candidate in mode 1)
+  const int rows_per_cand = (g.last || mode == 1) ? 1 : g.next_rpc;
   const int item = blockIdx.x * 4 + warp;
   if (item >= g.n_cand * rows_per_cand) return;
   const int cand = item / rows_per_cand, pi = item - cand * rows_per_cand;
@@ -1796,9 +1801,13 @@ __global__ void __launch_bounds__(128) k_final(DevWeights w, ModelDims md, CallG
   const int NPred = g.T - g.H + 1;
   float* pcand = b.pred + (size_t)cand * NPred * D;
   const int j = g.next_start + p;  // history index of this row (unused when last)
-  const bool new_pred = g.last || (j - g.H == g.call);
+  const bool new_pred = mode == 1 || g.last || (j - g.H == g.call);
   float2 v[NP];
-  if (new_pred) {
+  if (new_pred && mode == 2) {  // the head's output row
+    const float* pr = b.pp_out + (size_t)cand * D;
+#pragma unroll
+    for (int i = 0; i < NP; ++i) v[i] = *reinterpret_cast<const float2*>(pr + 64 * i + 2 * lane);
+  } else if (new_pred) {
     // Output of the last layer for the window's last token: s + gate_mlp * ((P0 + P1) + b2),
     // the FC2 update of the last layer still pending.
     const int tile = cand / g.cpt;
@@ -1843,6 +1852,16 @@ __global__ void __launch_bounds__(128) k_final(DevWeights w, ModelDims md, CallG
       v[i].x = (v[i].x - mean) * rstd * fw[i].x + fb[i].x;
       v[i].y = (v[i].y - mean) * rstd * fw[i].y + fb[i].y;
     }
+    if (mode == 1) {  // row `cand` of the head's operand blocks
+      uint8_t* blk = reinterpret_cast<uint8_t*>(b.pp_in) + (size_t)(cand / 128) * NP * kBlk;
+#pragma unroll
+      for (int i = 0; i < NP; ++i)
+        *reinterpret_cast<uint32_t*>(blk + i * kBlk + sw128_off(cand % 128, 2 * lane)) =
+            pack_bf16x2(v[i].x, v[i].y);
+      return;
+    }
+  }
+  if (new_pred) {
     if (g.last) {
       const int e = b.goal_per_cand ? cand : cand / g.S;
       const float* gr = b.goal + (size_t)e * D;
@@ -2097,8 +2116,9 @@ cudaError_t call_impl(const ModelDims& md, const DevWeights& w, const CallGeom& 
     if (prof) prof->end(KC_FC2, 2.0 * rows * md.mlp * D, st);
   }
   if (prof) prof->begin(st);
-  const int final_items = g.n_cand * (g.last ? 1 : g.next_rpc);
-  LEWM_TRY(launch_k(k_final<D>, dim3((final_items + 3) / 4), dim3(128), 0, st, w, md, g, b));
+  const int final_mode = b.pp_in ? 1 : 0;
+  const int final_items = g.n_cand * ((g.last || final_mode == 1) ? 1 : g.next_rpc);
+  LEWM_TRY(launch_k(k_final<D>, dim3((final_items + 3) / 4), dim3(128), 0, st, w, md, g, b, final_mode));
   if (prof) prof->end(KC_FINAL, 0.0, st);
 #undef LEWM_TRY
   return cudaSuccess;
@@ -2125,6 +2145,16 @@ cudaError_t launch_prep0(const ModelDims& md, const DevWeights& w, const CallGeo
   if (md.D == 192) return prep0_impl<192>(md, w, g, b, st, prof);
   if (md.D == 384) return prep0_impl<384>(md, w, g, b, st, prof);
   return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_final_post(const ModelDims& md, const DevWeights& w, const CallGeom& g, const RolloutBufs& b,
+                              cudaStream_t st, Prof* prof) {
+  if (md.D != 192 || !b.pp_out) return cudaErrorInvalidValue;  // the head is built for width 192
+  const int items = g.n_cand * (g.last ? 1 : g.next_rpc);
+  if (prof) prof->begin(st);
+  const cudaError_t e = launch_k(k_final<192>, dim3((items + 3) / 4), dim3(128), 0, st, w, md, g, b, 2);
+  if (prof) prof->end(KC_FINAL, 0.0, st);
+  return e;
 }
 
 cudaError_t launch_call(const ModelDims& md, const DevWeights& w, const CallGeom& g, const RolloutBufs& b,

@@ -29,8 +29,6 @@ def pack_canonical(desc: ModelDesc, state_dict: Mapping[str, np.ndarray]) -> np.
     """Concatenate the state dict in the order ``lewm_create`` reads it."""
     parts = []
     for name, shape in param_shapes(desc).items():
-        if name.startswith("pred_proj."):
-            continue
         arr = np.asarray(state_dict[name], dtype=np.float32)
         if tuple(arr.shape) != tuple(shape):
             raise ValueError(f"{name}: expected {shape}, got {arr.shape}")

@@ -230,6 +230,8 @@ def main() -> int:
     model_cost_case(torch, "full_h3", ModelDesc(), 0, B=2, S=4, T=5, H=3, input_seed=7)
     model_cost_case(torch, "full_ppln", ModelDesc(pred_proj_hidden=2048, pred_proj_norm="layernorm"), 3,
                     B=1, S=4, T=5, H=1, input_seed=8)
+    model_cost_case(torch, "full_ppbn_h3", ModelDesc(pred_proj_hidden=2048, pred_proj_norm="batchnorm"), 4,
+                    B=2, S=5, T=5, H=3, input_seed=10)
     model_cost_case(torch, "stress_h3", STRESS_DESC, 5, B=1, S=2, T=10, H=3, input_seed=9)
     base = dict(num_samples=24, n_steps=5, topk=6, seed=3, var_scale=1.0)
     chain_case(torch, "brown_ret", ModelDesc(), 0,

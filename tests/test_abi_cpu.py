@@ -79,12 +79,15 @@ def test_solver_schedule_and_evals():
     assert B200CEMSolver(model=None).sample_counts() == [300] * 30
 
 
-@pytest.mark.parametrize("desc", [ModelDesc(), STRESS_DESC])
+@pytest.mark.parametrize("desc", [ModelDesc(), STRESS_DESC,
+                                  ModelDesc(pred_proj_hidden=2048, pred_proj_norm="layernorm"),
+                                  ModelDesc(pred_proj_hidden=512, pred_proj_norm="batchnorm"),
+                                  ModelDesc(pred_proj_hidden=256, pred_proj_norm="none")])
 def test_weight_count_matches_reference_state_dict(desc):
     lib = _lib.lib()
     cd = __import__("lewm_flash_b200.runtime", fromlist=["desc_to_c"]).desc_to_c(desc)
     n = lib.lewm_weight_count(ctypes.byref(cd))
-    want = sum(int(np.prod(s)) for k, s in param_shapes(desc).items() if not k.startswith("pred_proj"))
+    want = sum(int(np.prod(s)) for k, s in param_shapes(desc).items())
     assert n == want
     flat = pack_canonical(desc, synthetic_state_dict(desc, 0))
     assert flat.size == n
@@ -94,8 +97,10 @@ def test_unsupported_shapes_are_rejected():
     lib = _lib.lib()
     from lewm_flash_b200.runtime import desc_to_c
 
+    # pred_proj heads run at width 192 with a hidden width that is a multiple of 256
     for bad in (ModelDesc(dim=64, heads=4, dim_head=16, mlp_dim=256, embed_hidden=256), ModelDesc(dim_head=32),
-                ModelDesc(pred_proj_hidden=2048, pred_proj_norm="layernorm")):
+                ModelDesc(pred_proj_hidden=96, pred_proj_norm="layernorm"),
+                STRESS_DESC.replace(pred_proj_hidden=2048, pred_proj_norm="layernorm")):
         assert lib.lewm_weight_count(ctypes.byref(desc_to_c(bad))) == 0
 
 
