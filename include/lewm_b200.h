@@ -212,8 +212,9 @@ LEWM_API lewm_status lewm_sample_candidates_noalloc(const lewm_plan_desc* plan, 
 LEWM_API lewm_status lewm_coloring_matrix(int32_t n, double beta, double* out);
 
 /* Kernel classes reported by lewm_profile_plan, in array order. */
-#define LEWM_KERNEL_CLASSES 12 /* embed, adaln, qkv_attn, out_proj, fc1, fc2, final, sample, refit, prep0, \
-                                  ffn (fused FC1 + GELU + FC2), ln_operand (per-tile GEMM operand) */
+#define LEWM_KERNEL_CLASSES 13 /* embed, adaln, qkv_attn, out_proj, fc1, fc2, final, sample, refit, prep0, \
+                                  ffn (fused FC1 + GELU + FC2), ln_operand (per-tile GEMM operand), \
+                                  tile_call (all layers of a predictor call per row tile) */
 
 /* Run one plan (in-kernel noise) with a CUDA event pair around every kernel
  * launch, synchronize, and report per kernel class: summed device ms,

@@ -108,7 +108,7 @@ SIGNATURES = {
     "lewm_encoder_destroy": (None, [C.c_void_p]),
 }
 KERNEL_CLASSES = ("embed", "adaln", "qkv_attn", "out_proj", "fc1", "fc2", "final", "sample", "refit", "prep0", "ffn",
-                  "ln_operand")
+                  "ln_operand", "tile_call")
 
 
 def lib():

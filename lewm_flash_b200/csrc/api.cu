@@ -113,6 +113,7 @@ struct lewm_ctx {
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;
   std::map<std::vector<double>, cudaGraphExec_t> graphs;  // one executable graph per plan shape
   int tile_target = 1;        // row tiles a small predictor call is spread over
+  int tile_call_min = -1;     // fused call kernel from this many candidates (-1: SMs x 20, 0: never)
   int sm_count = 148;         // streaming multiprocessors of the device
   std::vector<float> W_host;  // last uploaded coloring matrix
   int W_n = -1;
@@ -268,6 +269,9 @@ lewm_status pack_weights(lewm_ctx* c, const float* wts, size_t n) {
   const size_t o_wout_w = D == 192 ? alloc((size_t)L * NKI * D * 128) : 0;
   const size_t o_w1 = alloc((size_t)L * (m.mlp / 128) * KB * blkA);
   const size_t o_w2 = alloc((size_t)L * 4 * NKM * NT * 128);
+  const bool tile_w = D == 192 && m.mlp == 768;  // FC1 / FC2 blocks of the fused call kernel
+  const size_t o_w1s = tile_w ? alloc((size_t)L * 12 * 192 * 128) : 0;
+  const size_t o_w2s = tile_w ? alloc((size_t)L * 12 * 192 * 128) : 0;
   const size_t n_ada_tiles = (size_t)L * 6 * D / NT_ADA;
   const size_t o_wada = alloc(n_ada_tiles * KB * NT_ADA * 128);
   const size_t o_we2 = alloc((size_t)(m.eh / 128) * 2 * D * 128);
@@ -312,6 +316,13 @@ lewm_status pack_weights(lewm_ctx* c, const float* wts, size_t n) {
         uint8_t* dst = buf.data() + o_w2 + ((size_t)(l * 4 + nt) * NKM + kb) * NT * 128;
         pack_block(dst, w2[l], m.mlp, NT, kb, [&](int r) { return nt * NT + r; });
       }
+    if (tile_w)
+      for (int q = 0; q < 4; ++q)
+        for (int kb = 0; kb < 3; ++kb) {
+          const size_t blk = ((size_t)(l * 4 + q) * 3 + kb) * 192 * 128;
+          pack_block(buf.data() + o_w1s + blk, w1[l], D, 192, kb, [&](int r) { return 192 * q + r; });
+          pack_block(buf.data() + o_w2s + blk, w2[l], m.mlp, 192, 3 * q + kb, [&](int r) { return r; });
+        }
   }
   for (size_t t = 0; t < n_ada_tiles; ++t)
     for (int kb = 0; kb < KB; ++kb) {
@@ -342,7 +353,8 @@ lewm_status pack_weights(lewm_ctx* c, const float* wts, size_t n) {
   auto fl = [&](size_t o) { return reinterpret_cast<const float*>(base + o); };
   c->w = DevWeights{bf(o_qkv), bf(o_wout), D == 192 ? bf(o_wout_w) : nullptr, bf(o_w1), bf(o_w2), bf(o_wada), bf(o_we2), fl(o_pos), fl(o_adab),
                     fl(o_alnw), fl(o_alnb), fl(o_outb), fl(o_flnw), fl(o_flnb), fl(o_b1), fl(o_b2), fl(o_finw),
-                    fl(o_finb), fl(o_convw), fl(o_convb), fl(o_e1w), fl(o_e1b), fl(o_e2b)};
+                    fl(o_finb), fl(o_convw), fl(o_convb), fl(o_e1w), fl(o_e1b), fl(o_e2b),
+                    tile_w ? bf(o_w1s) : nullptr, tile_w ? bf(o_w2s) : nullptr};
   return LEWM_OK;
 }
 
@@ -469,6 +481,19 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   return LEWM_OK;
 }
 
+// The fused call kernel (tile_call.cu) covers width 192 / 16 heads / MLP 768 / 6 layers
+// without a pred_proj head, a window full from the first call (history >= window = 3),
+// observation embeddings per env, and calls with enough candidates to fill the SMs
+// (LEWM_TILE_CALL_MIN, default 148 x 40 / 2 candidates; 0 disables it).
+bool use_tile_call(const lewm_ctx* c, int NC, int H, int HS, int emb_pc) {
+  const int min_cand = c->tile_call_min;
+  const ModelDims& m = c->md;
+  if (min_cand == 0) return false;
+  const int need = min_cand > 0 ? min_cand : c->sm_count * tile_call_candidates_per_tile() / 2;
+  return m.D == 192 && m.heads == 16 && m.mlp == 768 && m.pp_hidden == 0 && m.frames >= 3 && HS == 3 && H >= 3 &&
+         !emb_pc && c->w.w1s != nullptr && NC >= need;
+}
+
 // Launch sequence of one model-cost evaluation over n_cand = B*S candidates.
 lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, const float* goal, int goal_pc,
                            const float* cand, int B, int S, int T, int HS, float* costs, cudaStream_t st) {
@@ -483,6 +508,38 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
                 c->ws.pred, costs, c->ws.kvc, kv_positions(H, HS),
                 m.pp_hidden ? c->ws.pp_in : nullptr, m.pp_hidden ? c->ws.pp_out : nullptr};
   const int n_calls = T - H + 1;
+  if (use_tile_call(c, NC, H, HS, emb_pc)) {
+    // Batched regime: one fused kernel per predictor call (all layers per row tile).
+    for (int k = 0; k < n_calls; ++k) {
+      TileCallParams tp{};
+      tp.n_cand = NC;
+      tp.S = S;
+      tp.T = T;
+      tp.H = H;
+      tp.start = H + k - 3;
+      tp.call = k;
+      tp.last = k == n_calls - 1 ? 1 : 0;
+      tp.npred = n_calls;
+      tp.layers = m.L;
+      tp.goal_per_cand = goal_pc;
+      tp.emb = emb;
+      tp.goal = goal;
+      tp.mod = c->ws.mod;
+      tp.pred = c->ws.pred;
+      tp.costs = costs;
+      tp.status = c->d_status;
+      c->prof.begin(st);
+      const cudaError_t te = launch_tile_call(c->w, tp, st);
+      if (te != cudaSuccess) {
+        char info[256];
+        tile_call_describe(info, sizeof info);
+        return fail(c, LEWM_CUDA_ERROR, "fused call kernel launch: %s (%s)", cudaGetErrorString(te), info);
+      }
+      c->prof.end(KC_TILE_CALL, 2.0 * NC * 3 * m.L * (double)(m.D * 3 * m.inner + m.inner * m.D + 2 * m.D * m.mlp),
+                  st);
+    }
+    return LEWM_OK;
+  }
   auto geom = [&](int k) {
     const int end = H + k;
     const int start = std::max(0, end - HS);
@@ -857,6 +914,7 @@ lewm_status lewm_create(lewm_ctx** out, const lewm_model_desc* desc, const float
     const int v = std::atoi(tt);
     if (v > 0) c->tile_target = v;
   }
+  if (const char* tm = std::getenv("LEWM_TILE_CALL_MIN")) c->tile_call_min = std::atoi(tm);  // read per context
   s = pack_weights(c, weights, n_floats);
   if (s == LEWM_OK && cudaMalloc(&c->d_status, kStatusBytes) != cudaSuccess) s = fail(c, LEWM_CUDA_ERROR, "status alloc");
   if (s == LEWM_OK && cudaMemset(c->d_status, 0, kStatusBytes) != cudaSuccess)

@@ -60,6 +60,11 @@ struct DevWeights {
   const float* e1_w;       // [eh][A']
   const float* e1_b;       // [eh]
   const float* e2_b;       // [D]
+  // FC1 / FC2 re-blocked for the fused call kernel (width 192, MLP 768): [L][4 quarters][3]
+  // blocks of [192 x 64]: FC1 rows = the quarter's 192 hidden units over K block kb of D;
+  // FC2 rows = the 192 outputs over hidden columns [192 q + 64 kb, +64).
+  const __nv_bfloat16* w1s;
+  const __nv_bfloat16* w2s;
 };
 
 struct ModelDims {
@@ -136,7 +141,7 @@ struct RolloutBufs {
 // records an event pair and the algorithmic FLOPs of that launch under a kernel
 // class; lewm_profile_plan sums them after a synchronize.
 enum KernelClass { KC_EMBED = 0, KC_ADALN, KC_QKV_ATTN, KC_OUT, KC_FC1, KC_FC2, KC_FINAL, KC_SAMPLE, KC_REFIT,
-                   KC_PREP0, KC_FFN, KC_LN_OP, KC_COUNT };
+                   KC_PREP0, KC_FFN, KC_LN_OP, KC_TILE_CALL, KC_COUNT };
 struct Prof {
   bool on = false;
   struct Rec {
@@ -251,6 +256,29 @@ cudaError_t launch_sample(const SampleParams& p, cudaStream_t st);
 cudaError_t launch_set_rng(uint32_t* rng, uint32_t seed, uint32_t plan, cudaStream_t st);
 // One wait on an mbarrier that nothing arrives on: expires after the status block's limit.
 cudaError_t launch_wait_selftest(uint32_t* status, cudaStream_t st);
+
+// One predictor call, all layers, for tiles of 40 candidates x 3 window rows
+// (tile_call.cu). Width 192, 16 heads, MLP 768, a full window of 3 from the first call.
+struct TileCallParams {
+  int n_cand;         // candidates (envs x samples)
+  int S;              // samples per env
+  int T, H;           // horizon, history rows
+  int start;          // history index of window position 0 (H + call - 3)
+  int call;           // prediction slot this call writes
+  int last;           // 1: write costs instead of the prediction
+  int npred;          // prediction slots per candidate (T - H + 1)
+  int layers;
+  int goal_per_cand;
+  const float* emb;   // (B, H, D)
+  const float* goal;  // (B, D) or (n_cand, D)
+  const __nv_bfloat16* mod;  // AdaLN modulation rows [n_cand * T][L * 6D]
+  float* pred;        // [n_cand][npred][D]
+  float* costs;       // [n_cand]
+  uint32_t* status;
+};
+cudaError_t launch_tile_call(const DevWeights& w, const TileCallParams& p, cudaStream_t st);
+int tile_call_candidates_per_tile();
+void tile_call_describe(char* buf, size_t n);  // launch resources, for error messages
 
 // MLP head at input / output width 192 (reference lewm/module.py:217-240): Linear(192 -> P),
 // LayerNorm / BatchNorm1d (eval) / none, GELU, Linear(P -> 192); the predictor's pred_proj.

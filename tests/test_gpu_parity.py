@@ -25,10 +25,23 @@ COST_RTOL = 1e-2  # bf16 rollout vs fp32 reference, relative, per candidate
 _RT = {}
 
 
-def runtime(desc: ModelDesc, seed: int) -> Runtime:
-    key = (desc, seed)
+def runtime(desc: ModelDesc, seed: int, fused: bool = True) -> Runtime:
+    """fused=False: a context that never uses the fused call kernel (LEWM_TILE_CALL_MIN=0 at
+    creation), for the tests of the per-layer kernels on batches large enough for it."""
+    import os
+
+    key = (desc, seed, fused)
     if key not in _RT:
-        _RT[key] = Runtime(desc, synthetic_state_dict(desc, seed), "cuda:0")
+        old = os.environ.get("LEWM_TILE_CALL_MIN")
+        if not fused:
+            os.environ["LEWM_TILE_CALL_MIN"] = "0"
+        try:
+            _RT[key] = Runtime(desc, synthetic_state_dict(desc, seed), "cuda:0")
+        finally:
+            if old is None:
+                os.environ.pop("LEWM_TILE_CALL_MIN", None)
+            else:
+                os.environ["LEWM_TILE_CALL_MIN"] = old
     return _RT[key]
 
 
@@ -146,7 +159,7 @@ def test_many_tile_fused_ffn_equals_single_env_bits():
     # takes the two-kernel FFN. Same FC2 hidden quarters on both paths: same bits.
     desc = ModelDesc()
     sd = synthetic_state_dict(desc, 0)
-    rt = runtime(desc, 0)
+    rt = runtime(desc, 0, fused=False)
     rng = np.random.default_rng(21)
     B, S = 48, 250
     emb = rng.standard_normal((B, 3, desc.dim)).astype(np.float32)
@@ -334,7 +347,7 @@ def test_many_env_plan_matches_single_env_plan_bits():
     # the fused FFN with GELU from TMEM and the N = 192 out-projection; env 0 alone runs
     # the small-call kernels. Sampling, rollout, top-k and refit give env 0 the same bits.
     desc = ModelDesc()
-    rt = runtime(desc, 0)
+    rt = runtime(desc, 0, fused=False)
     rng = np.random.default_rng(31)
     B = 40
     emb, goal = cuda(rng.standard_normal((B, 3, desc.dim))), cuda(rng.standard_normal((B, 1, desc.dim)))

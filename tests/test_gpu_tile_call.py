@@ -1,0 +1,117 @@
+"""The fused predictor-call kernel (lewm_flash_b200/csrc/tile_call.cu) on batched calls.
+
+A call with enough candidates (at least SMs x 20; width 192, 16 heads, MLP 768, a full
+window of 3 from the first call) runs all layers of the call in one kernel per row tile
+of 40 candidates. Checked through the C ABI against the float32 oracle (the reference's
+fp32 semantics, within the 1e-2 bf16 bound) and against the per-layer kernels (same
+bf16 operands, different accumulation order); bit-identical per candidate whatever the
+batch around it and run to run; inside a full batched plan whose elites and outputs the
+oracle reproduces from the device's costs.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
+from lewm_flash_b200.runtime import PlanOptions, Runtime
+from oracle import icem_oracle as io
+from oracle import lewm_oracle as lo
+
+pytestmark = pytest.mark.gpu
+COST_RTOL = 1e-2
+
+
+def cuda(x):
+    return torch.as_tensor(np.asarray(x), dtype=torch.float32, device="cuda:0")
+
+
+def rel(got, want):
+    return np.abs(np.asarray(got, np.float64) - want) / np.maximum(np.abs(want), 1e-6)
+
+
+def _runtime(desc, sd, tile_min):
+    old = os.environ.get("LEWM_TILE_CALL_MIN")
+    os.environ["LEWM_TILE_CALL_MIN"] = str(tile_min)
+    try:
+        return Runtime(desc, sd, "cuda:0")
+    finally:
+        if old is None:
+            os.environ.pop("LEWM_TILE_CALL_MIN", None)
+        else:
+            os.environ["LEWM_TILE_CALL_MIN"] = old
+
+
+@pytest.fixture(scope="module")
+def model():
+    desc = ModelDesc()
+    sd = synthetic_state_dict(desc, 0)
+    fused = _runtime(desc, sd, 1)       # fused kernel on every call it supports
+    layered = _runtime(desc, sd, 0)     # per-layer kernels only
+    yield desc, sd, fused, layered
+    fused.close()
+    layered.close()
+
+
+@pytest.mark.parametrize("B,S,H,T", [(2, 61, 3, 5), (3, 100, 3, 5), (1, 7, 4, 5), (2, 40, 3, 3)])
+def test_fused_call_matches_oracle_and_per_layer_kernels(model, B, S, H, T):
+    desc, sd, fused, layered = model
+    rng = np.random.default_rng(B * 1000 + S)
+    emb = rng.standard_normal((B, H, desc.dim)).astype(np.float32)
+    goal = rng.standard_normal((B, 1, desc.dim)).astype(np.float32)
+    cand = rng.standard_normal((B, S, T, desc.action_dim)).astype(np.float32)
+    got = fused.model_cost(cuda(emb), cuda(goal), cuda(cand)).cpu().numpy()
+    other = layered.model_cost(cuda(emb), cuda(goal), cuda(cand)).cpu().numpy()
+    fused.sync()
+    layered.sync()
+    want = lo.get_cost_from_embeddings(emb, goal, cand, sd, desc)
+    assert rel(got, want).max() <= COST_RTOL, rel(got, want).max()
+    assert rel(got, other).max() <= COST_RTOL
+    assert np.isfinite(got).all()
+
+
+def test_fused_call_is_deterministic_and_batch_independent(model):
+    desc, sd, fused, _ = model
+    rng = np.random.default_rng(5)
+    B, S = 7, 90  # 630 candidates: 16 tiles, the last one partly filled
+    emb = cuda(rng.standard_normal((B, 3, desc.dim)))
+    goal = cuda(rng.standard_normal((B, 1, desc.dim)))
+    cand = cuda(rng.standard_normal((B, S, 5, desc.action_dim)))
+    a = fused.model_cost(emb, goal, cand)
+    b = fused.model_cost(emb, goal, cand)
+    assert torch.equal(a, b)
+    for e in (0, 3, B - 1):  # an env alone: its candidates land in other tiles and rows
+        single = fused.model_cost(emb[e:e + 1], goal[e:e + 1], cand[e:e + 1])
+        assert torch.equal(single[0], a[e]), e
+    fused.sync()
+
+
+def test_fused_call_plan_matches_oracle_replay(model):
+    desc, sd, fused, _ = model
+    rng = np.random.default_rng(8)
+    B = 6
+    emb = rng.standard_normal((B, 3, desc.dim)).astype(np.float32)
+    goal = rng.standard_normal((B, 1, desc.dim)).astype(np.float32)
+    mean = np.zeros((B, 5, 10), np.float32)
+    std = np.ones_like(mean)
+    opts = PlanOptions(num_samples=120, topk=12, n_steps=3, elite_retention=3, sample_decay=1.25,
+                       sample_count_bucket_size=40, beta=2.0, action_block=5)
+    counts = [120, 120, 80]
+    noise = [rng.standard_normal((B, c, 5, 10)).astype(np.float32) for c in counts]
+    act, sdv, fc, tr = fused.plan(opts, cuda(emb), cuda(goal), cuda(mean), cuda(std),
+                                  noise_steps=[cuda(n) for n in noise], trace=True)
+    fused.sync()
+    i = len(counts) - 1
+    cand_last = tr["candidates"][i, :, :counts[i]].cpu().numpy()
+    want = lo.get_cost_from_embeddings(emb, goal, cand_last, sd, desc)
+    assert rel(tr["costs"][i, :, :counts[i]].cpu().numpy(), want).max() <= COST_RTOL
+    costs = iter([tr["costs"][k, :, :c].cpu().numpy() for k, c in enumerate(counts)])
+    trace = []
+    a_o, s_o, f_o = io.run_static_icem_chain(lambda e, g, cc: next(costs), emb, goal, mean, std, noise, topk=12,
+                                             elite_retention=3, trace=trace)
+    for k, t in enumerate(trace):
+        assert np.array_equal(t["topk_inds"], tr["topk_idx"][k].cpu().numpy()), k
+    np.testing.assert_allclose(act.cpu().numpy(), a_o, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(fc.cpu().numpy(), f_o, rtol=1e-5)
