@@ -50,21 +50,23 @@ constexpr int RING = 4;
 constexpr int B_BLK = 192 * 128;  // bytes of a [192 x 64] bf16 weight block
 constexpr int A_BLK = 128 * 128;  // bytes of a [128 x 64] bf16 operand block
 constexpr int BLOCKS_PER_LAYER = 88;
-constexpr int KV_STRIDE = 272;    // bytes per row of the k / v exchange (16-byte skew per row)
+constexpr int KV_ROW = 256;       // bytes per row of the k / v exchange: k 64 | v 64 bf16
 constexpr uint32_t COL_QKV = 0, COL_OUT = 192, COL_STASH = 384;
 
 constexpr int OFF_A = 0;                              // 3 operand blocks (LayerNorm output)
 constexpr int OFF_RING = OFF_A + 3 * A_BLK;           // weight ring
 constexpr int OFF_SCR = OFF_RING + RING * B_BLK;      // attention scratch | FC2 operand (hidden)
-constexpr int OFF_KV = OFF_SCR;                       // [128][272 B]: k 64 | v 64 bf16
-constexpr int OFF_SO = OFF_SCR + 35840;               // 2 attention-output operand blocks
-constexpr int OFF_SPART = OFF_SO + 2 * A_BLK;         // [4 parts][3 positions][128] partial scores
-constexpr int OFF_STATS = OFF_SPART + 4 * WIN * 128 * 4;  // [2][4 parts][128] row reductions
-constexpr int OFF_BAR = OFF_STATS + 2 * 4 * 128 * 4;
+constexpr int OFF_KV = OFF_SCR;                       // [128][256 B]: k 64 | v 64 bf16, chunks swizzled
+constexpr int OFF_SO = OFF_SCR + 128 * KV_ROW;        // 2 attention-output operand blocks
+// [2 buffers][4 parts][3 positions][128] partial scores; the LayerNorm moments ([2][4][128]
+// float2) share the region (the two phases never overlap).
+constexpr int OFF_SPART = OFF_SO + 2 * A_BLK;
+constexpr int OFF_STATS = OFF_SPART;
+constexpr int OFF_BAR = OFF_SPART + 2 * 4 * WIN * 128 * 4;
 constexpr int SMEM_BYTES = 1024 + OFF_BAR + 256;
 static_assert(OFF_SO % 1024 == 0 && OFF_SCR % 1024 == 0, "operand blocks need 1024-byte alignment");
-static_assert(OFF_KV + 128 * KV_STRIDE <= OFF_SO, "k / v exchange overlaps the output blocks");
-static_assert(3 * A_BLK <= OFF_STATS - OFF_SCR, "hidden operand must fit the scratch region");
+static_assert(2 * 4 * 128 * 8 <= OFF_BAR - OFF_STATS, "moment scratch must fit the score region");
+static_assert(3 * A_BLK <= OFF_BAR - OFF_SCR, "hidden operand must fit the scratch region");
 static_assert(SMEM_BYTES <= 232448, "shared memory");
 
 enum Bar {
@@ -84,7 +86,8 @@ enum Bar {
   B_COUNT = 21
 };
 
-__device__ __forceinline__ void bar_epi() { named_bar(1, EPI_THREADS); }
+// The four warps of one TMEM lane quadrant (the four column parts of the same 32 rows).
+__device__ __forceinline__ void bar_quad(int quad) { named_bar(2 + quad, 128); }
 
 // Bounded wait that gives up at once when another wait of the CTA has expired.
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, uint32_t* status, volatile int* abort) {
@@ -201,18 +204,43 @@ struct RowCtx {
   int tok;      // cand * T + history index (modulation row)
 };
 
-// Sum over the row's four parts (two-buffer reduction scratch; `red` counts uses).
-__device__ __forceinline__ float row_sum(float v, float* stats, int& red, const RowCtx& rc) {
-  float* s = stats + (red & 1) * 512;
+// Row moments from the four parts' own (mean, M2) over 48 columns each (Chan et al.'s
+// pairwise combination): mean of the part means, M2 = sum M2_p + 48 sum (mean_p - mean)^2.
+// One exchange through the two-buffer scratch (`red` counts uses). Returns (mean, var).
+__device__ __forceinline__ float2 row_moments(float mean_p, float m2_p, float* stats, int& red, const RowCtx& rc) {
+  float2* s = reinterpret_cast<float2*>(stats) + (red & 1) * 512;
   ++red;
-  s[rc.part * 128 + rc.r] = v;
-  bar_epi();
-  return (s[rc.r] + s[128 + rc.r]) + (s[256 + rc.r] + s[384 + rc.r]);
+  s[rc.part * 128 + rc.r] = make_float2(mean_p, m2_p);
+  bar_quad(rc.r >> 5);
+  const float2 a = s[rc.r], b = s[128 + rc.r], c = s[256 + rc.r], d = s[384 + rc.r];
+  const float mean = ((a.x + b.x) + (c.x + d.x)) * 0.25f;
+  const float da = a.x - mean, db = b.x - mean, dc = c.x - mean, dd = d.x - mean;
+  const float m2 = ((a.y + b.y) + (c.y + d.y)) + 48.0f * ((da * da + db * db) + (dc * dc + dd * dd));
+  return make_float2(mean, m2 * (1.0f / D));
+}
+// Sum of one value over the row's four parts.
+__device__ __forceinline__ float row_sum(float v, float* stats, int& red, const RowCtx& rc) {
+  float2* s = reinterpret_cast<float2*>(stats) + (red & 1) * 512;
+  ++red;
+  s[rc.part * 128 + rc.r] = make_float2(v, 0.f);
+  bar_quad(rc.r >> 5);
+  return (s[rc.r].x + s[128 + rc.r].x) + (s[256 + rc.r].x + s[384 + rc.r].x);
 }
 
+__device__ __forceinline__ void unpack2(uint32_t u, float* f) {
+  f[0] = __uint_as_float(u << 16);
+  f[1] = __uint_as_float(u & 0xffff0000u);
+}
 __device__ __forceinline__ void unpack8(const uint4 u, float* f) {
-  const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
-  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+  unpack2(u.x, f);
+  unpack2(u.y, f + 2);
+  unpack2(u.z, f + 4);
+  unpack2(u.w, f + 6);
+}
+__device__ __forceinline__ void ldg8(const float* p, float* f) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p + 4));
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
 }
 
 // bf16(LN_{g,b}(LN(x) * (1 + scale) + shift)) into the three operand blocks at `op`:
@@ -236,6 +264,7 @@ __device__ __forceinline__ void ln_modulate_operand(const float* xr, uint32_t ts
                                                     const float* __restrict__ bb, uint8_t* op, float* stats, int& red,
                                                     const RowCtx& rc) {
   const int c0 = 48 * rc.part;
+  // moments of x (two passes over the thread's 48 columns, one exchange)
   float s = 0.f;
 #pragma unroll
   for (int t = 0; t < 3; ++t) {
@@ -244,31 +273,21 @@ __device__ __forceinline__ void ln_modulate_operand(const float* xr, uint32_t ts
 #pragma unroll
     for (int i = 0; i < 16; ++i) s += v[i];
   }
-  const float m1 = row_sum(s, stats, red, rc) * (1.0f / D);
+  const float mp = s * (1.0f / 48);
   float q = 0.f;
 #pragma unroll
   for (int t = 0; t < 3; ++t) {
     float v[16];
     load_chunk(t, xr, ts, v);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) q += (v[i] - m1) * (v[i] - m1);
+    for (int i = 0; i < 16; ++i) q += (v[i] - mp) * (v[i] - mp);
   }
-  const float r1 = rsqrtf(row_sum(q, stats, red, rc) * (1.0f / D) + 1e-6f);
-  float hs = 0.f;
-#pragma unroll
-  for (int t = 0; t < 3; ++t) {
-    float v[16];
-    load_chunk(t, xr, ts, v);
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      float sh[8], sc[8];
-      mod_chunk8(shift, scale, 16 * t + 8 * e, sh, sc);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) hs += (v[8 * e + k] - m1) * r1 * (1.0f + sc[k]) + sh[k];
-    }
-  }
-  const float m2 = row_sum(hs, stats, red, rc) * (1.0f / D);
-  float hq = 0.f;
+  const float2 mv1 = row_moments(mp, q, stats, red, rc);
+  const float m1 = mv1.x, r1 = rsqrtf(mv1.y + 1e-6f);
+  // h = LN(x) * (1 + scale) + shift: its moments in one pass (sum and sum of squares over the
+  // thread's 48 columns, then the exact pairwise combination across parts), recomputed for
+  // the output pass.
+  float hs = 0.f, hss = 0.f;
 #pragma unroll
   for (int t = 0; t < 3; ++t) {
     float v[16];
@@ -279,25 +298,32 @@ __device__ __forceinline__ void ln_modulate_operand(const float* xr, uint32_t ts
       mod_chunk8(shift, scale, 16 * t + 8 * e, sh, sc);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const float h = (v[8 * e + k] - m1) * r1 * (1.0f + sc[k]) + sh[k];
-        hq += (h - m2) * (h - m2);
+        const float y = (v[8 * e + k] - m1) * r1;
+        const float h = fmaf(y, sc[k], y) + sh[k];
+        hs += h;
+        hss = fmaf(h, h, hss);
       }
     }
   }
-  const float r2 = rsqrtf(row_sum(hq, stats, red, rc) * (1.0f / D) + 1e-5f);
+  const float hp = hs * (1.0f / 48);
+  const float2 mv2 = row_moments(hp, fmaxf(hss - hs * hp, 0.f), stats, red, rc);
+  const float m2 = mv2.x, r2 = rsqrtf(mv2.y + 1e-5f);
 #pragma unroll
   for (int t = 0; t < 3; ++t) {
     float v[16];
     load_chunk(t, xr, ts, v);
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      float sh[8], sc[8], o[8];
+      float sh[8], sc[8], gg[8], bv[8], o[8];
       mod_chunk8(shift, scale, 16 * t + 8 * e, sh, sc);
       const int c = c0 + 16 * t + 8 * e;
+      ldg8(g + c, gg);
+      ldg8(bb + c, bv);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const float h = (v[8 * e + k] - m1) * r1 * (1.0f + sc[k]) + sh[k];
-        o[k] = (h - m2) * r2 * __ldg(g + c + k) + __ldg(bb + c + k);
+        const float y = (v[8 * e + k] - m1) * r1;
+        const float h = fmaf(y, sc[k], y) + sh[k];
+        o[k] = fmaf((h - m2) * r2, gg[k], bv[k]);
       }
       const uint4 u = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
                                  pack_bf16x2(o[6], o[7]));
@@ -317,14 +343,15 @@ __device__ __forceinline__ void residual_update(float* xr, uint32_t ts, uint32_t
     load_chunk(t, xr, ts, v);
 #pragma unroll
     for (int e = 0; e < 16; e += 8) {
-      float gt[8];
+      float gt[8], bv[8];
       if (gate)
         unpack8(__ldg(reinterpret_cast<const uint4*>(gate + 16 * t + e)), gt);
       else
 #pragma unroll
         for (int k = 0; k < 8; ++k) gt[k] = 0.f;
+      ldg8(bias + c0 + 16 * t + e, bv);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) v[e + k] += gt[k] * (a[e + k] + __ldg(bias + c0 + 16 * t + e + k));
+      for (int k = 0; k < 8; ++k) v[e + k] = fmaf(gt[k], a[e + k] + bv[k], v[e + k]);
     }
     store_chunk(t, xr, ts, v);
   }
@@ -566,57 +593,75 @@ __global__ void __maxnreg__(96) k_tile_call(DevWeights w, TileCallParams p) {
         tmem_ld8(tr + 128, vv);
         tmem_ld8(tr + 160, vv + 8);
         if (h < HEADS - 1) warp_arrive(&bars[B_QKV_FREE], lane);
-        // k and v of every row, bf16 (the precision of the reference's autocast attention).
-        uint4* kvrow = reinterpret_cast<uint4*>(sKV + rc.r * KV_STRIDE + rc.part * 32);
-        const uint4 k0 = make_uint4(pack_bf16x2(kk[0], kk[1]), pack_bf16x2(kk[2], kk[3]), pack_bf16x2(kk[4], kk[5]),
-                                    pack_bf16x2(kk[6], kk[7]));
-        const uint4 k1 = make_uint4(pack_bf16x2(kk[8], kk[9]), pack_bf16x2(kk[10], kk[11]),
-                                    pack_bf16x2(kk[12], kk[13]), pack_bf16x2(kk[14], kk[15]));
-        const uint4 v0 = make_uint4(pack_bf16x2(vv[0], vv[1]), pack_bf16x2(vv[2], vv[3]), pack_bf16x2(vv[4], vv[5]),
-                                    pack_bf16x2(vv[6], vv[7]));
-        const uint4 v1 = make_uint4(pack_bf16x2(vv[8], vv[9]), pack_bf16x2(vv[10], vv[11]),
-                                    pack_bf16x2(vv[12], vv[13]), pack_bf16x2(vv[14], vv[15]));
-        kvrow[0] = k0;
-        kvrow[1] = k1;
-        kvrow[8] = v0;
-        kvrow[9] = v1;
-        bar_epi();
-        // Partial scores q . k_j over this part's 16 dims for j <= pos.
-#pragma unroll 1
-        for (int jj = 0; jj <= npos; ++jj) {
-          const uint4* kr = reinterpret_cast<const uint4*>(sKV + (base + jj) * KV_STRIDE + rc.part * 32);
-          float kf[16];
-          unpack8(kr[0], kf);
-          unpack8(kr[1], kf + 8);
+        // k and v of every row, bf16 (the precision of the reference's autocast attention) for
+        // the window-mates, fp32 for the row itself, exchanged through shared memory. A candidate's window rows are lanes of this warp
+        // and the part's dims are this warp's, so the exchange needs only warp barriers.
+        uint8_t* kvr = sKV + rc.r * KV_ROW;
+        const int sw = rc.r & 7;  // 16-byte chunk swizzle of the row
+        __syncwarp();             // window-mates are done reading the previous head's k / v
+        *reinterpret_cast<uint4*>(kvr + (((2 * rc.part) ^ sw) << 4)) =
+            make_uint4(pack_bf16x2(kk[0], kk[1]), pack_bf16x2(kk[2], kk[3]), pack_bf16x2(kk[4], kk[5]),
+                       pack_bf16x2(kk[6], kk[7]));
+        *reinterpret_cast<uint4*>(kvr + (((2 * rc.part + 1) ^ sw) << 4)) =
+            make_uint4(pack_bf16x2(kk[8], kk[9]), pack_bf16x2(kk[10], kk[11]), pack_bf16x2(kk[12], kk[13]),
+                       pack_bf16x2(kk[14], kk[15]));
+        *reinterpret_cast<uint4*>(kvr + (((8 + 2 * rc.part) ^ sw) << 4)) =
+            make_uint4(pack_bf16x2(vv[0], vv[1]), pack_bf16x2(vv[2], vv[3]), pack_bf16x2(vv[4], vv[5]),
+                       pack_bf16x2(vv[6], vv[7]));
+        *reinterpret_cast<uint4*>(kvr + (((9 + 2 * rc.part) ^ sw) << 4)) =
+            make_uint4(pack_bf16x2(vv[8], vv[9]), pack_bf16x2(vv[10], vv[11]), pack_bf16x2(vv[12], vv[13]),
+                       pack_bf16x2(vv[14], vv[15]));
+        __syncwarp();
+        float* sp = spart + (h & 1) * (4 * WIN * 128);  // double-buffered partial scores
+        // Partial scores q . k_j over this part's 16 dims for j <= pos (the row's own k from
+        // registers, the window-mates' from the exchange).
+        {
           float d = 0.f;
 #pragma unroll
-          for (int t = 0; t < 16; ++t) d += q[t] * kf[t];
-          spart[(rc.part * WIN + jj) * 128 + rc.r] = d;
+          for (int t = 0; t < 16; ++t) d = fmaf(q[t], kk[t], d);
+          sp[(rc.part * WIN + npos) * 128 + rc.r] = d;
         }
-        bar_epi();
+#pragma unroll 1
+        for (int jj = 0; jj < npos; ++jj) {
+          const int rj = base + jj;
+          const uint8_t* kr = sKV + rj * KV_ROW;
+          float kf[16];
+          unpack8(*reinterpret_cast<const uint4*>(kr + (((2 * rc.part) ^ (rj & 7)) << 4)), kf);
+          unpack8(*reinterpret_cast<const uint4*>(kr + (((2 * rc.part + 1) ^ (rj & 7)) << 4)), kf + 8);
+          float d = 0.f;
+#pragma unroll
+          for (int t = 0; t < 16; ++t) d = fmaf(q[t], kf[t], d);
+          sp[(rc.part * WIN + jj) * 128 + rc.r] = d;
+        }
+        bar_quad(quad);
         // One pass of online softmax (scale 1/8 = dim_head^-0.5) and the weighted sum of v.
         float mx = -INFINITY, den = 0.f, o[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) o[t] = 0.f;
 #pragma unroll 1
         for (int jj = 0; jj <= npos; ++jj) {
-          const float sj = ((spart[(0 * WIN + jj) * 128 + rc.r] + spart[(1 * WIN + jj) * 128 + rc.r]) +
-                            (spart[(2 * WIN + jj) * 128 + rc.r] + spart[(3 * WIN + jj) * 128 + rc.r])) *
+          const float sj = ((sp[(0 * WIN + jj) * 128 + rc.r] + sp[(1 * WIN + jj) * 128 + rc.r]) +
+                            (sp[(2 * WIN + jj) * 128 + rc.r] + sp[(3 * WIN + jj) * 128 + rc.r])) *
                            0.125f;
           const float mnew = fmaxf(mx, sj);
           const float sc = __expf(mx - mnew);
           const float pj = __expf(sj - mnew);
           den = den * sc + pj;
           mx = mnew;
-          const uint4* vr = reinterpret_cast<const uint4*>(sKV + (base + jj) * KV_STRIDE + rc.part * 32) + 8;
           float vf[16];
-          unpack8(vr[0], vf);
-          unpack8(vr[1], vf + 8);
+          if (jj < npos) {
+            const int rj = base + jj;
+            const uint8_t* vr = sKV + rj * KV_ROW;
+            unpack8(*reinterpret_cast<const uint4*>(vr + (((8 + 2 * rc.part) ^ (rj & 7)) << 4)), vf);
+            unpack8(*reinterpret_cast<const uint4*>(vr + (((9 + 2 * rc.part) ^ (rj & 7)) << 4)), vf + 8);
+          } else {
 #pragma unroll
-          for (int t = 0; t < 16; ++t) o[t] = o[t] * sc + pj * vf[t];
+            for (int t = 0; t < 16; ++t) vf[t] = vv[t];
+          }
+#pragma unroll
+          for (int t = 0; t < 16; ++t) o[t] = fmaf(pj, vf[t], o[t] * sc);
         }
         const float inv = rc.valid ? 1.0f / den : 0.f;
-        bar_epi();  // k / v and the partial scores are free for the next head
         const int b = h & 1;
         if (h >= 2) warp_wait(&bars[B_O_FREE + b], (8 * l + (h - 2) / 2) & 1, status, abort, lane);
         uint8_t* ob = sO + b * A_BLK;
@@ -646,9 +691,12 @@ __global__ void __maxnreg__(96) k_tile_call(DevWeights w, TileCallParams p) {
           float a[16];
           tmem_ld16(tlane + COL_QKV + c0 + 16 * t, a);
           const float* b1 = w.b1 + l * MLP + 192 * q + c0 + 16 * t;
+          float bv[16];
+          ldg8(b1, bv);
+          ldg8(b1 + 8, bv + 8);
 #pragma unroll
           for (int e = 0; e < 16; e += 2)
-            hp[8 * t + e / 2] = pack_bf16x2(gelu_f(a[e] + __ldg(b1 + e)), gelu_f(a[e + 1] + __ldg(b1 + e + 1)));
+            hp[8 * t + e / 2] = pack_bf16x2(gelu_f(a[e] + bv[e]), gelu_f(a[e + 1] + bv[e + 1]));
         }
         if (q < 3) warp_arrive(&bars[B_FC1_FREE], lane);
         if (q > 0) warp_wait(&bars[B_HID_FREE], (4 * l + q - 1) & 1, status, abort, lane);
@@ -674,16 +722,17 @@ __global__ void __maxnreg__(96) k_tile_call(DevWeights w, TileCallParams p) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) sum += v[i];
     }
-    const float mean = row_sum(sum, stats, red, rc) * (1.0f / D);
+    const float mpart = sum * (1.0f / 48);
     float qv = 0.f;
 #pragma unroll
     for (int t = 0; t < 3; ++t) {
       float v[16];
       load_chunk(t, xr, tstash, v);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) qv += (v[i] - mean) * (v[i] - mean);
+      for (int i = 0; i < 16; ++i) qv += (v[i] - mpart) * (v[i] - mpart);
     }
-    const float rstd = rsqrtf(row_sum(qv, stats, red, rc) * (1.0f / D) + 1e-5f);
+    const float2 mvf = row_moments(mpart, qv, stats, red, rc);
+    const float mean = mvf.x, rstd = rsqrtf(mvf.y + 1e-5f);
     const bool out_row = rc.valid && rc.pos == WIN - 1;
     float acc = 0.f;
     const float* gr = nullptr;
@@ -698,11 +747,13 @@ __global__ void __maxnreg__(96) k_tile_call(DevWeights w, TileCallParams p) {
     for (int t = 0; t < 3; ++t) {
       float v[16];
       load_chunk(t, xr, tstash, v);
+      float fw[16], fb[16];
+      ldg8(w.fin_w + c0 + 16 * t, fw);
+      ldg8(w.fin_w + c0 + 16 * t + 8, fw + 8);
+      ldg8(w.fin_b + c0 + 16 * t, fb);
+      ldg8(w.fin_b + c0 + 16 * t + 8, fb + 8);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int c = c0 + 16 * t + i;
-        v[i] = (v[i] - mean) * rstd * __ldg(w.fin_w + c) + __ldg(w.fin_b + c);
-      }
+      for (int i = 0; i < 16; ++i) v[i] = fmaf((v[i] - mean) * rstd, fw[i], fb[i]);
       if (gr) {  // cost_from_rollout: squared distance to the goal's last row
 #pragma unroll
         for (int i = 0; i < 16; ++i) acc += (v[i] - gr[16 * t + i]) * (v[i] - gr[16 * t + i]);
