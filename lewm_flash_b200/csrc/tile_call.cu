@@ -89,6 +89,21 @@ enum Bar {
 // The four warps of one TMEM lane quadrant (the four column parts of the same 32 rows).
 __device__ __forceinline__ void bar_quad(int quad) { named_bar(2 + quad, 128); }
 
+// mbarrier.try_wait with a suspend-time hint: the waiting thread sleeps until the phase
+// completes or `hint_ns` elapse, instead of spinning and taking issue slots from the warps
+// that do the work on its sub-partition.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait that gives up at once when another wait of the CTA has expired.
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, uint32_t* status, volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -96,7 +111,7 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, uint32_t
   const uint64_t t0 = global_timer_ns();
   const uint64_t limit = wait_limit_ns(status);
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
     if (*abort) return false;
     if (global_timer_ns() - t0 > limit) {
       atomicOr(status, LEWM_DEV_TIMEOUT);
