@@ -473,6 +473,7 @@ def main() -> int:
     ap.add_argument("--no-reference-gpu", action="store_true", help="skip the reference PyTorch GPU comparator")
     ap.add_argument("--no-sharded", action="store_true", help="skip the 1024-env sharded leg")
     ap.add_argument("--no-stress", action="store_true", help="skip the width-384 stress leg")
+    ap.add_argument("--no-fp32", action="store_true", help="skip the float32 CEM leg")
     ap.add_argument("--model-cost", type=int, default=0, metavar="S",
                     help="profiling case: time R model-cost calls of S candidates per env (horizon 5; 1 env "
                          "with history 1, or --envs B with history 3) and exit; no bench line")
@@ -595,6 +596,7 @@ def main() -> int:
 
     # ---------------------------------------------------------------- batched planning (64 envs, history 3)
     batched = batched_pass(rt, dev, args.steps, args.warmup, flush)
+    fp32_cem = fp32_cem_pass(dev, args.steps, args.warmup, flush) if not args.no_fp32 else None
 
     # ---------------------------------------------------------------- 1024 envs split over the ranks
     sharded = sharded_pass(rt, dev, rank, world, barrier, dist, flush) if not args.no_sharded else None
@@ -626,6 +628,7 @@ def main() -> int:
         "roofline": kinfo["roofline"],
         "kernel_classes": kinfo["classes"],
         "batched": batched,
+        "fp32_cem": fp32_cem,
         "sharded": sharded,
         "stress": stress,
         "encoder": encoder,
@@ -787,6 +790,45 @@ def batched_pass(rt, dev, steps, warmup, flush, n_envs=64, history=3):
     return {"workload": f"icem_bucketed_300_{n_envs}env_h{history}_bf16", "envs": n_envs, "history": history,
             "plans_per_s": n_envs / (p50 / 1e3), "p50_call_ms": p50, "calls": n,
             "note": "one plan call solves all envs; per-GPU throughput, device-resident inputs"}
+
+
+def fp32_cem_pass(dev, steps, warmup, flush, n_envs=1):
+    """The float32 configuration: plain CEM 300 samples / 30 elites / 30 iterations, 1 env,
+    history 1, with the model cost in float32 throughout (model_cost_autocast "none", the
+    reference's default arithmetic). Device-resident inputs, L2 flushed between plans."""
+    import torch
+
+    from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
+    from lewm_flash_b200.runtime import PlanOptions, Runtime
+
+    rt = Runtime(ModelDesc(), synthetic_state_dict(ModelDesc(), 0), dev, model_cost_autocast="none")
+    opts = PlanOptions(num_samples=300, topk=30, n_steps=30, sample_decay=1.0, sample_count_bucket_size=0,
+                       elite_retention=0, beta=0.0, action_block=5, seed=0)
+    emb, goal = (torch.as_tensor(x, device=dev) for x in bench_latents(0))
+    mean = torch.zeros(n_envs, 5, 10, device=dev)
+    std = torch.ones(n_envs, 5, 10, device=dev)
+    for i in range(max(warmup, 1)):
+        rt.plan(opts, emb, goal, mean, std, plan_index=7000 + i)
+    stream = torch.cuda.current_stream(dev)
+    ms = []
+    for i in range(max(1, min(steps, 10))):
+        l2_flush(flush)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        rt.plan(opts, emb, goal, mean, std, plan_index=8000 + i)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        ms.append(a.elapsed_time(b))
+    rt.sync()
+    rt.close()
+    p50 = percentile(ms, 50)
+    flops = F_CANON * 300 * 30 * n_envs
+    return {"workload": "cem_300_30_30_1env_h1_fp32", "envs": n_envs, "plans_per_s": n_envs / (p50 / 1e3),
+            "p50_plan_ms": p50, "plans": len(ms), "tflops_fp32": flops / (p50 / 1e3) / 1e12,
+            "flops_per_plan": flops,
+            "note": "float32 CUDA-core model cost (no tensor cores); canonical FLOPs (window rows the "
+                    "bf16 path computes), the fp32 path recomputes full windows (~1.3x)"}
 
 
 def encoder_pass(dev, steps, warmup, flush, n_img=64):

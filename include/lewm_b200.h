@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define LEWM_ABI_VERSION 2
+#define LEWM_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define LEWM_API __attribute__((visibility("default")))
@@ -88,11 +88,25 @@ LEWM_API void lewm_destroy(lewm_ctx* ctx);
 /* Message of the last failing call on `ctx` ("" if none). NULL ctx: last lewm_create failure. */
 LEWM_API const char* lewm_last_error(const lewm_ctx* ctx);
 
+/* Model-cost arithmetic of a context (reference JEPA.set_model_cost_autocast,
+ * lewm/jepa.py:65-86, whose modes are "none" and "bf16"). */
+#define LEWM_AUTOCAST_NONE 0 /* float32 throughout: the reference without autocast */
+#define LEWM_AUTOCAST_BF16 1 /* bf16 tensor-core GEMMs, fp32 norms / residual / cost (the default) */
+
+/* Select the arithmetic of every later lewm_model_cost / lewm_plan / lewm_profile_plan on
+ * `ctx`. LEWM_AUTOCAST_BF16 (the default of a new context) runs the tcgen05 kernels;
+ * LEWM_AUTOCAST_NONE runs the same model in float32 on CUDA cores (tiled SIMT GEMMs with
+ * fused epilogues, two-pass LayerNorms, erf GELU): the reference's float32 costs within its
+ * 1e-5 exactness tolerance (tools/benchmarks/check_lewm_cache_exactness.py:783-784), at a
+ * fraction of the bf16 throughput. Any other mode: LEWM_INVALID_ARG. Synchronizes the
+ * context's device and drops its captured plan graphs. */
+LEWM_API lewm_status lewm_set_model_cost_autocast(lewm_ctx* ctx, int32_t mode);
+
 /* Terminal latent cost of each action candidate.
  * Replaces JEPA.get_cost_from_embeddings(emb, goal_emb, action_candidates, history_size)
  * (reference lewm/jepa.py:302-317), i.e. rollout_from_embeddings (:262-300) and
  * cost_from_rollout (:246-260), computed with bf16 tensor-core GEMMs and fp32
- * norms/residuals/cost.
+ * norms/residuals/cost, or in float32 throughout under LEWM_AUTOCAST_NONE.
  *   emb   (B,H,D) if emb_per_sample == 0, else (B,S,H,D)
  *   goal  (B,D)   if goal_per_sample == 0, else (B,S,D): the last goal row
  *   cand  (B,S,T,A)
@@ -212,9 +226,10 @@ LEWM_API lewm_status lewm_sample_candidates_noalloc(const lewm_plan_desc* plan, 
 LEWM_API lewm_status lewm_coloring_matrix(int32_t n, double beta, double* out);
 
 /* Kernel classes reported by lewm_profile_plan, in array order. */
-#define LEWM_KERNEL_CLASSES 13 /* embed, adaln, qkv_attn, out_proj, fc1, fc2, final, sample, refit, prep0, \
+#define LEWM_KERNEL_CLASSES 14 /* embed, adaln, qkv_attn, out_proj, fc1, fc2, final, sample, refit, prep0, \
                                   ffn (fused FC1 + GELU + FC2), ln_operand (per-tile GEMM operand), \
-                                  tile_call (all layers of a predictor call per row tile) */
+                                  tile_call (all layers of a predictor call per row tile), \
+                                  fp32_cost (a whole float32 model cost, LEWM_AUTOCAST_NONE) */
 
 /* Run one plan (in-kernel noise) with a CUDA event pair around every kernel
  * launch, synchronize, and report per kernel class: summed device ms,

@@ -68,7 +68,7 @@ class PlanTraceC(C.Structure):
 
 
 _lib = None
-ABI_VERSION = 2  # LEWM_ABI_VERSION of include/lewm_b200.h this binding follows
+ABI_VERSION = 3  # LEWM_ABI_VERSION of include/lewm_b200.h this binding follows
 
 # name -> (restype, argtypes)
 SIGNATURES = {
@@ -93,6 +93,7 @@ SIGNATURES = {
     "lewm_coloring_matrix": (C.c_int, [C.c_int32, C.c_double, C.c_void_p]),
     "lewm_sync_status": (C.c_int, [C.c_void_p, C.c_void_p]),
     "lewm_set_wait_limit": (C.c_int, [C.c_void_p, C.c_uint64]),
+    "lewm_set_model_cost_autocast": (C.c_int, [C.c_void_p, C.c_int32]),
     "lewm_wait_selftest": (C.c_int, [C.c_void_p, C.c_void_p]),
     "lewm_abi_version": (C.c_int32, []),
     "lewm_profile_plan": (C.c_int, [C.c_void_p, C.POINTER(PlanDescC), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -108,7 +109,7 @@ SIGNATURES = {
     "lewm_encoder_destroy": (None, [C.c_void_p]),
 }
 KERNEL_CLASSES = ("embed", "adaln", "qkv_attn", "out_proj", "fc1", "fc2", "final", "sample", "refit", "prep0", "ffn",
-                  "ln_operand", "tile_call")
+                  "ln_operand", "tile_call", "fp32_cost")
 
 
 def lib():

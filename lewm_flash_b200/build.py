@@ -15,7 +15,7 @@ PKG = Path(__file__).resolve().parent
 REPO = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "liblewm_b200.so"
-SOURCES = ["api.cu", "rollout_kernels.cu", "tile_call.cu", "icem_kernels.cu", "noalloc.cu", "encoder.cu"]
+SOURCES = ["api.cu", "rollout_kernels.cu", "tile_call.cu", "fp32_path.cu", "icem_kernels.cu", "noalloc.cu", "encoder.cu"]
 HEADERS = ["lewm_common.cuh", "lewm_internal.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -66,6 +66,7 @@ struct Workspace {
   __nv_bfloat16* pp_hid = nullptr;
   float* pp_hid32 = nullptr;
   float* pp_out = nullptr;
+  F32Work f32{};             // fp32 model-cost activations (carved when the context computes in fp32)
   float* emb_in = nullptr;   // staged plan inputs (graph path)
   float* goal_in = nullptr;
   float* lohi = nullptr;     // action low | high
@@ -73,9 +74,10 @@ struct Workspace {
 
 struct WsReq {
   size_t n_cand, T, A, D, L, tiles, heads, mlp, npred, B, R, ncol, kvpos;
+  size_t f32 = 0;  // 1: carve the fp32 model-cost activations too
   bool operator<=(const WsReq& o) const {
     return n_cand <= o.n_cand && T <= o.T && tiles <= o.tiles && npred <= o.npred && B <= o.B && R <= o.R &&
-           ncol <= o.ncol && kvpos <= o.kvpos;
+           ncol <= o.ncol && kvpos <= o.kvpos && f32 <= o.f32;
   }
 };
 
@@ -103,6 +105,9 @@ struct lewm_ctx {
   std::string err;
   void* d_weights = nullptr;
   DevWeights w{};
+  int autocast = 1;           // model-cost arithmetic: 1 bf16 tensor cores (default), 0 float32
+  void* d_w32 = nullptr;      // float32 weights of the fp32 model cost
+  F32Weights w32;
   MlpHead pp{};  // pred_proj MLP head (P == 0: Identity)
   uint32_t* d_status = nullptr;
   Workspace ws;
@@ -362,6 +367,87 @@ lewm_status pack_weights(lewm_ctx* c, const float* wts, size_t n) {
 // holds whole candidates (at most 128 rows). A call with few candidates is spread
 // over up to `target` tiles (one wave of the one-head-per-CTA QKV kernel), so each
 // CTA of the streamed-operand GEMMs moves fewer rows; a large call uses full tiles.
+// The float32 weights of the fp32 model cost: the canonical host array uploaded as given,
+// plus [2P] per-column scale / shift of a pred_proj head without a LayerNorm (BatchNorm1d in
+// eval folded with the first Linear's bias, computed in double; scale 1, shift = bias with no
+// norm).
+lewm_status upload_f32_weights(lewm_ctx* c, const float* wts, size_t n) {
+  const ModelDims& m = c->md;
+  const size_t D = m.D, P = m.pp_hidden;
+  const size_t n_aff = (P && m.pp_norm != 1) ? 2 * P : 0;
+  LEWM_CK(c, cudaMalloc(&c->d_w32, (n + n_aff) * 4));
+  LEWM_CK(c, cudaMemcpy(c->d_w32, wts, n * 4, cudaMemcpyHostToDevice));
+  const float* base = static_cast<const float*>(c->d_w32);
+  size_t off = 0;
+  auto take = [&](size_t k) {
+    const float* q = base + off;
+    off += k;
+    return q;
+  };
+  F32Weights& w = c->w32;
+  w.pos = take((size_t)m.frames * D);
+  w.layers.resize(m.L);
+  for (int l = 0; l < m.L; ++l) {
+    F32Layer& lw = w.layers[l];
+    lw.ada_w = take(6 * D * D);
+    lw.ada_b = take(6 * D);
+    lw.attn_ln_w = take(D);
+    lw.attn_ln_b = take(D);
+    lw.qkv_w = take(3 * (size_t)m.inner * D);
+    lw.out_w = take(D * m.inner);
+    lw.out_b = take(D);
+    lw.ffn_ln_w = take(D);
+    lw.ffn_ln_b = take(D);
+    lw.w1 = take((size_t)m.mlp * D);
+    lw.b1 = take(m.mlp);
+    lw.w2 = take(D * m.mlp);
+    lw.b2 = take(D);
+  }
+  w.fin_w = take(D);
+  w.fin_b = take(D);
+  w.conv_w = take((size_t)m.As * m.A);
+  w.conv_b = take(m.As);
+  w.e1_w = take((size_t)m.eh * m.As);
+  w.e1_b = take(m.eh);
+  w.e2_w = take(D * m.eh);
+  w.e2_b = take(D);
+  if (P) {  // net.0.weight, net.0.bias, norm parameters, net.3.weight, net.3.bias
+    const size_t o_b1 = off + P * D;
+    w.pp_w1 = take(P * D);
+    w.pp_b1 = take(P);
+    std::vector<float> aff(n_aff);
+    if (m.pp_norm == 1) {
+      w.pp_ln_g = take(P);
+      w.pp_ln_b = take(P);
+    } else if (m.pp_norm == 2) {
+      const float* hb = wts + o_b1;  // Linear bias, then BatchNorm weight, bias, running mean, var
+      const size_t o_bn = off;
+      const float *g = wts + o_bn, *bb = g + P, *mu = bb + P, *var = mu + P;
+      for (size_t j = 0; j < P; ++j) {
+        const double sc = (double)g[j] / std::sqrt((double)var[j] + 1e-5);
+        aff[j] = (float)sc;
+        aff[P + j] = (float)(((double)hb[j] - mu[j]) * sc + bb[j]);
+      }
+      take(4 * P);
+    } else {
+      for (size_t j = 0; j < P; ++j) {
+        aff[j] = 1.f;
+        aff[P + j] = wts[o_b1 + j];
+      }
+    }
+    w.pp_w2 = take(D * P);
+    w.pp_b2 = take(D);
+    if (n_aff) {
+      float* d_aff = static_cast<float*>(c->d_w32) + n;
+      LEWM_CK(c, cudaMemcpy(d_aff, aff.data(), n_aff * 4, cudaMemcpyHostToDevice));
+      w.pp_scale = d_aff;
+      w.pp_shift = d_aff + P;
+    }
+  }
+  if (off != n) return fail(c, LEWM_INVALID_ARG, "fp32 weight walk mismatch");
+  return LEWM_OK;
+}
+
 void tile_geom(int n_cand, int w, int target, int* cpt, int* n_tiles) {
   const int cmax = 128 / w;
   int nt = (n_cand + cmax - 1) / cmax;
@@ -382,7 +468,9 @@ void clear_graphs(lewm_ctx* c) {
   c->graphs.clear();
 }
 
-lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
+lewm_status ensure_ws(lewm_ctx* c, const WsReq& need_in) {
+  WsReq need = need_in;
+  need.f32 = c->autocast == 0 ? 1 : 0;
   if (c->have_ws && need <= c->cap) return LEWM_OK;
   WsReq r = need;
   if (c->have_ws) {  // grow monotonically
@@ -394,6 +482,7 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
     r.R = std::max(r.R, c->cap.R);
     r.ncol = std::max(r.ncol, c->cap.ncol);
     r.kvpos = std::max(r.kvpos, c->cap.kvpos);
+    r.f32 = std::max(r.f32, c->cap.f32);
     clear_graphs(c);
     cudaFree(c->ws.base);
     c->ws = Workspace{};
@@ -439,6 +528,7 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   const size_t o_pphid = carve(pp_tiles * (size_t)(m.pp_hidden / 64) * 128 * 64 * 2);
   const size_t o_pph32 = carve(m.pp_norm == 1 ? pp_tiles * 128 * (size_t)m.pp_hidden * 4 : 0);
   const size_t o_ppout = carve(m.pp_hidden ? r.n_cand * (size_t)m.D * 4 : 0);
+  const size_t o_f32 = carve(r.f32 ? f32_work_floats(m, r.n_cand, r.T) * 4 : 0);
   void* base = nullptr;
   LEWM_CK(c, cudaMalloc(&base, off));
   auto* b = static_cast<uint8_t*>(base);
@@ -475,6 +565,7 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need) {
   ws.pp_hid = reinterpret_cast<__nv_bfloat16*>(b + o_pphid);
   ws.pp_hid32 = reinterpret_cast<float*>(b + o_pph32);
   ws.pp_out = reinterpret_cast<float*>(b + o_ppout);
+  if (r.f32) ws.f32 = f32_work_carve(m, r.n_cand, r.T, reinterpret_cast<float*>(b + o_f32));
   c->cap = r;
   c->have_ws = true;
   c->W_n = -1;
@@ -495,12 +586,32 @@ bool use_tile_call(const lewm_ctx* c, int NC, int H, int HS, int emb_pc) {
          !emb_pc && c->w.w1s != nullptr && NC >= need;
 }
 
+// Algorithmic FLOPs of one model-cost evaluation: the GEMMs over the rows each computes
+// (Embedder and AdaLN over every token; every predictor call over its whole window; the
+// pred_proj head over the new predictions).
+double model_cost_flops(const ModelDims& m, int NC, int T, int H, int HS) {
+  const double NT = (double)NC * T;
+  double f = 2.0 * NT * ((double)m.A * m.As + (double)m.As * m.eh + (double)m.eh * m.D + (double)m.L * 6 * m.D * m.D);
+  for (int k = 0; k < T - H + 1; ++k) {
+    const int end = H + k, w = end - std::max(0, end - HS);
+    f += 2.0 * NC * w * m.L * ((double)m.D * 3 * m.inner + (double)m.inner * m.D + 2.0 * m.D * m.mlp);
+    f += 2.0 * NC * m.D * 2.0 * m.pp_hidden;
+  }
+  return f;
+}
+
 // Launch sequence of one model-cost evaluation over n_cand = B*S candidates.
 lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, const float* goal, int goal_pc,
                            const float* cand, int B, int S, int T, int HS, float* costs, cudaStream_t st) {
   const ModelDims& m = c->md;
   const int NC = B * S;
   const int rows = NC * T;
+  if (c->autocast == 0) {  // float32 arithmetic throughout (no autocast): CUDA-core kernels
+    c->prof.begin(st);
+    LEWM_CK(c, run_model_cost_fp32(m, c->w32, c->ws.f32, emb, emb_pc, H, goal, goal_pc, cand, B, S, T, HS, costs, st));
+    c->prof.end(KC_F32_COST, model_cost_flops(m, NC, T, H, HS), st);
+    return LEWM_OK;
+  }
   LEWM_CK(c, launch_embed(m, c->w, cand, rows, c->ws.eh, c->ws.act_a, c->d_status, st, &c->prof));
   LEWM_CK(c, launch_adaln(m, c->w, rows, c->ws.act_a, c->ws.mod, c->d_status, st, &c->prof));
   RolloutBufs b{emb,        emb_pc,    goal,      goal_pc, cand,      c->ws.act_a, c->ws.mod,
@@ -917,6 +1028,7 @@ lewm_status lewm_create(lewm_ctx** out, const lewm_model_desc* desc, const float
   }
   if (const char* tm = std::getenv("LEWM_TILE_CALL_MIN")) c->tile_call_min = std::atoi(tm);  // read per context
   s = pack_weights(c, weights, n_floats);
+  if (s == LEWM_OK) s = upload_f32_weights(c, weights, n_floats);
   if (s == LEWM_OK && cudaMalloc(&c->d_status, kStatusBytes) != cudaSuccess) s = fail(c, LEWM_CUDA_ERROR, "status alloc");
   if (s == LEWM_OK && cudaMemset(c->d_status, 0, kStatusBytes) != cudaSuccess)
     s = fail(c, LEWM_CUDA_ERROR, "status memset");
@@ -943,6 +1055,7 @@ void lewm_destroy(lewm_ctx* c) {
   if (c->cap_stream) cudaStreamDestroy(c->cap_stream);
   if (c->ws.base) cudaFree(c->ws.base);
   if (c->d_weights) cudaFree(c->d_weights);
+  if (c->d_w32) cudaFree(c->d_w32);
   mlp_head_destroy(&c->pp);
   if (c->d_status) cudaFree(c->d_status);
   delete c;
@@ -1187,6 +1300,19 @@ lewm_status lewm_wait_selftest(lewm_ctx* c, void* stream) {
 }
 
 int32_t lewm_abi_version(void) { return LEWM_ABI_VERSION; }
+
+lewm_status lewm_set_model_cost_autocast(lewm_ctx* c, int32_t mode) {
+  if (!c) return fail(nullptr, LEWM_INVALID_ARG, "ctx is NULL");
+  c->err.clear();
+  if (mode != LEWM_AUTOCAST_NONE && mode != LEWM_AUTOCAST_BF16)
+    return fail(c, LEWM_INVALID_ARG, "Unsupported model_cost_autocast mode: %d (0 none, 1 bf16)", mode);
+  if (mode == c->autocast) return LEWM_OK;
+  DeviceGuard g(c->device);
+  LEWM_CK(c, cudaDeviceSynchronize());
+  clear_graphs(c);  // captured plans hold the other arithmetic's launches
+  c->autocast = mode;
+  return LEWM_OK;
+}
 
 lewm_status lewm_profile_plan(lewm_ctx* c, const lewm_plan_desc* p, const float* emb, const float* goal,
                               const float* init_mean, const float* init_std, double* ms_out, double* flops_out,

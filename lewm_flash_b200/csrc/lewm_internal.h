@@ -141,7 +141,7 @@ struct RolloutBufs {
 // records an event pair and the algorithmic FLOPs of that launch under a kernel
 // class; lewm_profile_plan sums them after a synchronize.
 enum KernelClass { KC_EMBED = 0, KC_ADALN, KC_QKV_ATTN, KC_OUT, KC_FC1, KC_FC2, KC_FINAL, KC_SAMPLE, KC_REFIT,
-                   KC_PREP0, KC_FFN, KC_LN_OP, KC_TILE_CALL, KC_COUNT };
+                   KC_PREP0, KC_FFN, KC_LN_OP, KC_TILE_CALL, KC_F32_COST, KC_COUNT };
 struct Prof {
   bool on = false;
   struct Rec {
@@ -306,6 +306,47 @@ void mlp_head_destroy(MlpHead* h);
 // bf16 operand blocks; hid_op: [tiles][P / 64][128 x 64]; hid32: [tiles * 128][P] (LayerNorm only).
 cudaError_t mlp_head_run(const MlpHead& h, const __nv_bfloat16* in_op, int n_rows, __nv_bfloat16* hid_op,
                          float* hid32, float* out, uint32_t* status, cudaStream_t st);
+
+// fp32 model cost (fp32_path.cu): the predictor's float32 weights as given (row-major
+// state-dict tensors) and the float32 activations of one evaluation.
+struct F32Layer {
+  const float *ada_w, *ada_b;          // [6D][D], [6D]
+  const float *attn_ln_w, *attn_ln_b;  // [D]
+  const float *qkv_w;                  // [3 inner][D]
+  const float *out_w, *out_b;          // [D][inner], [D]
+  const float *ffn_ln_w, *ffn_ln_b;    // [D]
+  const float *w1, *b1;                // [mlp][D], [mlp]
+  const float *w2, *b2;                // [D][mlp], [D]
+};
+struct F32Weights {
+  const float* pos = nullptr;  // [frames][D]
+  std::vector<F32Layer> layers;
+  const float *fin_w = nullptr, *fin_b = nullptr;
+  const float *conv_w = nullptr, *conv_b = nullptr;  // [A'][A], [A']
+  const float *e1_w = nullptr, *e1_b = nullptr;      // [eh][A'], [eh]
+  const float *e2_w = nullptr, *e2_b = nullptr;      // [D][eh], [D]
+  // pred_proj MLP head: first Linear (bias only with LayerNorm), LayerNorm affine, or the
+  // per-column scale / shift of BatchNorm (eval) with the Linear's bias folded in (scale 1,
+  // shift = bias without a norm), second Linear.
+  const float *pp_w1 = nullptr, *pp_b1 = nullptr, *pp_ln_g = nullptr, *pp_ln_b = nullptr;
+  const float *pp_scale = nullptr, *pp_shift = nullptr, *pp_w2 = nullptr, *pp_b2 = nullptr;
+};
+struct F32Work {
+  float *act, *eh, *sact;  // [NC*T] x A' / eh / D: Embedder activations, sact = SiLU(action embedding)
+  float* mod;              // [NC*T][L*6D] AdaLN modulation
+  float *x, *a;            // [NC*w][D] residual stream, LayerNorm-modulated operand
+  float *qkv, *att, *hid;  // [NC*w] x 3 inner / inner / mlp
+  float* y;                // [NC][D] final-LayerNorm (and head) output of a call
+  float* pred;             // [NC][T-H+1][D] predictions appended to the history
+  float* pph;              // [NC][P] pred_proj hidden rows
+  int* row_tok;            // [NC*w] modulation row (candidate * T + history index) of each row
+};
+// Floats of F32Work for n_cand candidates, horizon T, window <= frames (pointers into one block).
+size_t f32_work_floats(const ModelDims& m, size_t n_cand, size_t T);
+F32Work f32_work_carve(const ModelDims& m, size_t n_cand, size_t T, float* base);
+cudaError_t run_model_cost_fp32(const ModelDims& m, const F32Weights& w, const F32Work& ws, const float* emb,
+                                int emb_pc, int H, const float* goal, int goal_pc, const float* cand, int B, int S,
+                                int T, int HS, float* costs, cudaStream_t st);
 
 // Sets the thread's error text that lewm_last_error(NULL) returns (context-free calls).
 void set_noctx_error(const char* msg);

@@ -107,10 +107,14 @@ def _ptr(t: Optional[torch.Tensor]):
     return None if t is None else C.c_void_p(t.data_ptr())
 
 
+AUTOCAST_MODES = {"none": 0, "bf16": 1}  # LEWM_AUTOCAST_NONE / LEWM_AUTOCAST_BF16
+
+
 class Runtime:
     """One packed LeWM predictor on one GPU."""
 
-    def __init__(self, desc: ModelDesc, state_dict: Mapping[str, np.ndarray], device="cuda"):
+    def __init__(self, desc: ModelDesc, state_dict: Mapping[str, np.ndarray], device="cuda",
+                 model_cost_autocast: str = "bf16"):
         self.desc = desc
         self.device = torch.device("cuda", _dev_index(device))
         flat = pack_canonical(desc, state_dict)
@@ -125,6 +129,8 @@ class Runtime:
         _lib.check(lib.lewm_create(C.byref(h), C.byref(cd), flat.ctypes.data, flat.size, self.device.index), None)
         self._h = h
         self.plans_issued = 0
+        self._autocast = "bf16"
+        self.set_model_cost_autocast(model_cost_autocast)
 
     def close(self) -> None:
         if getattr(self, "_h", None):
@@ -160,6 +166,19 @@ class Runtime:
         """Enqueue one bounded device wait that can never complete (``lewm_wait_selftest``);
         the next ``sync`` raises LEWM_DEVICE_TIMEOUT."""
         self._check(_lib.lib().lewm_wait_selftest(self._h, self._stream()))
+
+    def set_model_cost_autocast(self, mode: str = "none") -> "Runtime":
+        """Arithmetic of later model costs and plans (reference ``JEPA.set_model_cost_autocast``,
+        ``lewm/jepa.py:65-69``): "bf16" runs the tensor-core kernels, "none" float32 throughout."""
+        if mode not in AUTOCAST_MODES:
+            raise ValueError(f"Unsupported model_cost_autocast mode: {mode!r}")
+        if mode != self._autocast:
+            self._check(_lib.lib().lewm_set_model_cost_autocast(self._h, AUTOCAST_MODES[mode]))
+            self._autocast = mode
+        return self
+
+    def model_cost_autocast_mode(self) -> str:
+        return self._autocast
 
     # ------------------------------------------------------------------ model cost
     def model_cost(self, emb: torch.Tensor, goal_emb: torch.Tensor, candidates: torch.Tensor,

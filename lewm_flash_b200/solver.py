@@ -15,6 +15,10 @@
 * ``B200ModelCost`` / ``install_model_cost`` replace
   ``JEPA.get_cost_from_embeddings`` (``lewm/jepa.py:302-317``).
 
+The model cost follows the JEPA's ``model_cost_autocast_mode()`` at every call, as
+the reference does: "bf16" runs the tensor-core kernels, "none" (a JEPA's default)
+the float32 kernels.
+
 All envs of a ``solve`` run as one batched device plan; ``batch_size`` is
 accepted for interface compatibility. Noise comes from a counter-based Philox
 stream keyed by (seed, solve index, iteration, env, candidate) instead of the
@@ -54,7 +58,13 @@ def _runtime(model, device) -> Runtime:
 
         desc = infer_desc(model)
         cache[key] = Runtime(desc, extract_state_dict(model, desc), torch.device("cuda", key))
-    return cache[key]
+    rt = cache[key]
+    # The model's model-cost arithmetic, read at every use as JEPA.get_cost_from_embeddings
+    # reads it (lewm/jepa.py:310-317): "none" (a JEPA's default) float32, "bf16" tensor cores.
+    mode_of = getattr(model, "model_cost_autocast_mode", None)
+    if callable(mode_of):
+        rt.set_model_cost_autocast(mode_of())
+    return rt
 
 
 def prepare_init_action(model: Any, info_dict: dict, init_action: Optional[torch.Tensor], horizon: int, *,

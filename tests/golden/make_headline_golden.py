@@ -11,7 +11,10 @@ benchmark:
   elite retention 3, 1 env, history 1, horizon 5;
 * ``icem_headline_cfg2_ret5``: the same with elite retention 5;
 * ``icem_headline_cfg3``: the same solver for 4 envs with history 3 (a subset of
-  the 64-env batched configuration; envs are independent).
+  the 64-env batched configuration; envs are independent);
+* ``icem_headline_cfg1``: plain CEM, 300 samples / 30 elites / 30 iterations
+  (``ICEMSolver`` with white noise, no sample decay, no elite retention), 1 env,
+  history 1: the float32 configuration.
 
 The noise of every iteration is drawn by ``ICEMSolver._sample_noise``; the
 fixture stores it with the reference's per-iteration costs, top-k indices and
@@ -43,6 +46,8 @@ sys.path.insert(0, str(HERE))
 
 from lewm_flash_b200.model import ModelDesc, state_dict_checksum, synthetic_state_dict  # noqa: E402
 
+CEM_SOLVER = dict(num_samples=300, n_steps=30, topk=30, sample_decay=1.0, sample_count_bucket_size=0,
+                  colored_noise="none", colored_noise_time="raw", elite_retention=0, seed=0, var_scale=1.0)
 HEADLINE_SOLVER = dict(num_samples=300, n_steps=30, topk=30, sample_decay=1.25, sample_count_bucket_size=60,
                        colored_noise="brown", colored_noise_time="raw", elite_retention=3, seed=0, var_scale=1.0)
 
@@ -121,14 +126,21 @@ def headline_case(torch, name, solver_kw, n_envs, H, input_seed):
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--reference", required=True, help="reference checkout (its lewm/ is imported)")
+    ap.add_argument("--only", nargs="*", help="case names to (re)generate (default: all)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     import torch
 
     torch.set_num_threads(8)
-    headline_case(torch, "cfg2", HEADLINE_SOLVER, n_envs=1, H=1, input_seed=31)
-    headline_case(torch, "cfg2_ret5", dict(HEADLINE_SOLVER, elite_retention=5), n_envs=1, H=1, input_seed=32)
-    headline_case(torch, "cfg3", HEADLINE_SOLVER, n_envs=4, H=3, input_seed=33)
+    cases = {
+        "cfg2": (HEADLINE_SOLVER, 1, 1, 31),
+        "cfg2_ret5": (dict(HEADLINE_SOLVER, elite_retention=5), 1, 1, 32),
+        "cfg3": (HEADLINE_SOLVER, 4, 3, 33),
+        "cfg1": (CEM_SOLVER, 1, 1, 34),
+    }
+    for name, (kw, n_envs, H, seed) in cases.items():
+        if not args.only or name in args.only:
+            headline_case(torch, name, kw, n_envs=n_envs, H=H, input_seed=seed)
     return 0
 
 

@@ -32,3 +32,16 @@ def weights_of(d):
 
 MODEL_COST_CASES = sorted(p.name for p in GOLDEN.glob("model_cost_*.npz"))
 CHAIN_CASES = sorted(p.name for p in GOLDEN.glob("icem_chain_*.npz"))
+
+
+def assert_same_topk(idx, want, costs, what=""):
+    """Top-k indices equal to the reference's up to the order of exactly equal costs.
+
+    ``torch.topk`` leaves the order of equal values unspecified (its CPU kernel put index
+    239 before 160 at one tie of the CEM fixture); the device and the oracle order ties by
+    the lower index. So: the same index set per row, and the same cost at every rank."""
+    idx, want, costs = np.asarray(idx), np.asarray(want), np.asarray(costs)
+    assert idx.shape == want.shape, what
+    for b in range(idx.shape[0]):
+        assert np.array_equal(np.sort(idx[b]), np.sort(want[b])), f"{what}: elite sets differ in row {b}"
+        assert np.array_equal(costs[b][idx[b]], costs[b][want[b]]), f"{what}: elite order differs in row {b}"

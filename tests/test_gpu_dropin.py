@@ -17,7 +17,10 @@ sides see the same costs and the comparison isolates the solver surface:
   (``lewm/solvers/icem_static_compile.py:61-114``) on a noise list whose sample
   counts follow no iCEM schedule;
 * ``install_model_cost`` / ``B200ModelCost`` against the reference's fp32
-  ``get_cost_from_embeddings`` (bf16 bound 1e-2) and against ``Runtime.model_cost``.
+  ``get_cost_from_embeddings`` and against ``Runtime.model_cost``, following the
+  JEPA's ``model_cost_autocast_mode()``: "none" (the JEPA default, so every solver
+  test here runs the float32 kernels) within the reference's 1e-5 exactness gate,
+  "bf16" within the bf16 bound 1e-2.
 
 Tolerances: the two sides compute candidates with different fp32 operation orders
 (one rounding apart), so outputs agree to 1e-4 relative rather than bit for bit.
@@ -224,3 +227,30 @@ def test_install_model_cost_routes_reference_cost(env):
             "pixels": torch.zeros(2, 24, 1, device=env.dev), "goal": torch.zeros(2, 24, 1, device=env.dev)}
     via_get_cost = env.model.get_cost(info, cand.to(env.dev))
     assert torch.equal(via_get_cost, got)
+
+
+@pytest.mark.gpu
+def test_model_cost_follows_the_models_autocast_mode(env):
+    from lewm_flash_b200.solver import _runtime
+
+    g = torch.Generator().manual_seed(12)
+    emb = torch.randn(2, 3, 192, generator=g)
+    goal = torch.randn(2, 1, 192, generator=g)
+    cand = torch.randn(2, 64, T, 10, generator=g)
+    cpu_model, _ = _jepa(env.ref, torch.device("cpu"))
+    with torch.inference_mode():
+        want = cpu_model.get_cost_from_embeddings(emb, goal, cand)
+    args = (emb.to(env.dev), goal.to(env.dev), cand.to(env.dev))
+    assert env.model.model_cost_autocast_mode() == "none"
+    f32 = env.model.get_cost_from_embeddings(*args)
+    assert _runtime(env.model, env.dev).model_cost_autocast_mode() == "none"
+    assert torch.allclose(f32.cpu(), want, rtol=1e-5, atol=1e-5), (f32.cpu() - want).abs().max()
+    env.model.set_model_cost_autocast("bf16")
+    try:
+        bf16 = env.model.get_cost_from_embeddings(*args)
+        assert _runtime(env.model, env.dev).model_cost_autocast_mode() == "bf16"
+        rel = ((bf16.cpu() - want).abs() / want.abs()).max().item()
+        assert rel <= 1e-2 and not torch.allclose(bf16.cpu(), want, rtol=1e-5, atol=1e-5), rel
+    finally:
+        env.model.set_model_cost_autocast("none")
+    assert torch.equal(env.model.get_cost_from_embeddings(*args), f32)

@@ -1,0 +1,190 @@
+"""The float32 model cost (``model_cost_autocast`` "none", ``LEWM_AUTOCAST_NONE``).
+
+The reference computes its model cost in float32 unless ``JEPA.set_model_cost_autocast``
+("bf16", ``lewm/jepa.py:65-86``) is set; cfg1 (plain CEM 300 / 30 / 30) is quoted in
+float32. Its exactness gate (``tools/benchmarks/check_lewm_cache_exactness.py``) is
+``cost_stats`` (``:224-233``: ``torch.allclose`` at atol = rtol = 1e-5, ``:783-784``), then
+``compare_rankings`` (``:236-246``: argmin and top-k indices equal) and, where they differ,
+``ranking_drift_diagnostics`` (``:249-305``). The device's float32 path is held to it
+through the C ABI:
+
+* model costs of every reference fixture (Identity, LayerNorm, BatchNorm and no-norm
+  ``pred_proj`` heads, histories 1 to 3, width 384 / 12 layers) within 1e-5;
+* teacher-forced on the reference's cfg1 / cfg2 / cfg3 trajectories: the costs of every
+  iteration's candidates within 1e-5, the argmin equal, the top-k equal up to the order of
+  exactly equal costs or explained by near-ties;
+* the full float32 plan on the reference's noise stays on the reference's trajectory (any
+  elite change only at a tie below 1e-5 relative) and, where it stays through the last
+  iteration, returns the reference's actions and final cost;
+* switching between "bf16" and "none" gives each mode's own results, bit for bit.
+"""
+
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
+from lewm_flash_b200.runtime import PlanOptions, Runtime
+from oracle import lewm_oracle as lo
+from tests.golden_io import MODEL_COST_CASES, load, weights_of
+from tests.test_gpu_headline import HEADLINE_CASES, _opts, _reference_trajectory, ranking_drift
+
+pytestmark = pytest.mark.gpu
+ATOL = RTOL = 1e-5  # cost_stats of check_lewm_cache_exactness.py
+TIE_REL = 1e-5      # an elite change of the float32 plan must sit at a gap below this
+
+
+def _t(x, dev="cuda:0"):
+    return torch.as_tensor(np.ascontiguousarray(x), dtype=torch.float32, device=dev)
+
+
+def cost_stats(got, want):
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    return {"allclose": bool(np.allclose(got, want, rtol=RTOL, atol=ATOL)),
+            "max_abs": float(np.abs(got - want).max()),
+            "max_rel": float((np.abs(got - want) / np.maximum(np.abs(want), 1e-12)).max())}
+
+
+@pytest.fixture(scope="module")
+def runtimes():
+    cache = {}
+    yield cache
+    for rt in cache.values():
+        rt.close()
+
+
+def _rt(cache, d):
+    desc, sd = weights_of(d)
+    key = (json.dumps(desc.__dict__, sort_keys=True, default=str), int(d["seed"]))
+    if key not in cache:
+        cache[key] = Runtime(desc, sd, "cuda:0", model_cost_autocast="none")
+    return cache[key], desc, sd
+
+
+@pytest.mark.parametrize("case", MODEL_COST_CASES)
+def test_fp32_model_cost_matches_reference_golden(case, runtimes):
+    d = load(case)
+    rt, desc, sd = _rt(runtimes, d)
+    got = rt.model_cost(_t(d["emb"]), _t(d["goal"]), _t(d["cand"])).cpu().numpy()
+    rt.sync()
+    st = cost_stats(got, d["cost"])
+    print(f"{case}: {st}")
+    assert st["allclose"], st
+
+
+@pytest.mark.parametrize("norm,P,H,S", [("none", 256, 1, 64), ("batchnorm", 512, 2, 200), ("layernorm", 2048, 3, 40)])
+def test_fp32_pred_proj_matches_oracle(norm, P, H, S):
+    desc = ModelDesc(pred_proj_hidden=P, pred_proj_norm=norm)
+    sd = synthetic_state_dict(desc, 23)
+    rt = Runtime(desc, sd, "cuda:0", model_cost_autocast="none")
+    rng = np.random.default_rng(7)
+    emb = rng.standard_normal((2, H, desc.dim)).astype(np.float32)
+    goal = rng.standard_normal((2, 1, desc.dim)).astype(np.float32)
+    cand = rng.standard_normal((2, S, 5, desc.action_dim)).astype(np.float32)
+    got = rt.model_cost(_t(emb), _t(goal), _t(cand)).cpu().numpy()
+    rt.sync()
+    st = cost_stats(got, lo.get_cost_from_embeddings(emb, goal, cand, sd, desc))
+    assert st["allclose"], st
+    rt.close()
+
+
+@pytest.mark.parametrize("case", HEADLINE_CASES)
+def test_fp32_teacher_forced_costs_and_rankings(case, runtimes):
+    d = load(case)
+    rt, desc, sd = _rt(runtimes, d)
+    kw = json.loads(str(d["solver"]))
+    k, n = kw["topk"], int(d["n_iters"])
+    traj = _reference_trajectory(d, k, kw["elite_retention"])
+    emb, goal = _t(d["emb"]), _t(d["goal"])
+    worst, mismatched = 0.0, 0
+    for i in range(n):
+        ref = d[f"cost_{i}"]
+        got = rt.model_cost(emb, goal, _t(traj[i]["candidates"])).cpu().numpy()
+        st = cost_stats(got, ref)
+        worst = max(worst, st["max_rel"])
+        assert st["allclose"], f"iteration {i}: {st}"
+        assert np.array_equal(got.argmin(1), ref.argmin(1)) or np.all(
+            ref[np.arange(ref.shape[0]), got.argmin(1)] == ref.min(1)), f"iteration {i}: argmin differs"
+        drift = ranking_drift(ref, got, k, 2.0 * st["max_abs"])
+        mismatched += drift["topk_mismatch_rows"]
+        assert drift["explained"], f"iteration {i}: {drift}"
+    rt.sync()
+    print(f"{case}: {n} iterations, float32 cost max rel err {worst:.2e}, top-k rows with a tie swap {mismatched}")
+
+
+@pytest.mark.parametrize("case", HEADLINE_CASES)
+def test_fp32_full_plan_on_reference_noise(case, runtimes):
+    d = load(case)
+    rt, desc, sd = _rt(runtimes, d)
+    kw = json.loads(str(d["solver"]))
+    k, n, retention = kw["topk"], int(d["n_iters"]), kw["elite_retention"]
+    counts = [int(c) for c in d["counts"]]
+    act, std, fc, tr = rt.plan(_opts(kw), _t(d["emb"]), _t(d["goal"]), _t(d["mean0"]), _t(d["var0"]),
+                               noise_steps=[_t(d[f"noise_{i}"]) for i in range(n)], trace=True)
+    rt.sync()
+    idx_dev = tr["topk_idx"].cpu().numpy()
+    B = d["emb"].shape[0]
+    keep = max(retention, 1)
+    on_track = []
+    for b in range(B):
+        flip = n
+        for i in range(n):
+            ref_c = d[f"cost_{i}"][b]
+            dev_c = tr["costs"][i, b, :counts[i]].cpu().numpy()
+            assert cost_stats(dev_c, ref_c)["allclose"], f"env {b} iteration {i}"
+            dev_i, ref_i = idx_dev[i, b].tolist(), d[f"inds_{i}"][b].tolist()
+            same_set = set(dev_i) == set(ref_i)
+            same_head = [ref_c[a] for a in dev_i[:keep]] == [ref_c[r] for r in ref_i[:keep]]
+            if not (same_set and same_head):
+                s = np.sort(ref_c)
+                gap = (s[k] - s[k - 1]) / abs(s[k - 1]) if not same_set else 0.0
+                assert gap <= TIE_REL, f"env {b}: elites changed at iteration {i} with a gap of {gap:.2e}"
+                flip = i
+                break
+            if dev_i[:keep] != ref_i[:keep]:  # equal costs carried over in another order
+                flip = i
+                break
+        on_track.append(flip)
+    print(f"{case}: float32 plan on the reference's trajectory for {on_track} of {n} iterations")
+    for b, flip in enumerate(on_track):
+        if flip == n:
+            scale = float(np.abs(d["solve_actions"][b]).max()) + 1.0
+            np.testing.assert_allclose(act[b].cpu().numpy(), d["solve_actions"][b], rtol=1e-4, atol=1e-5 * scale)
+            np.testing.assert_allclose(std[b].cpu().numpy(), d["solve_var"][b], rtol=1e-4, atol=1e-5 * scale)
+            np.testing.assert_allclose(fc[b].cpu().numpy(), d["solve_costs"][b], rtol=RTOL, atol=ATOL)
+
+
+def test_switching_modes_gives_each_modes_results():
+    desc = ModelDesc()
+    sd = synthetic_state_dict(desc, 0)
+    rng = np.random.default_rng(9)
+    emb = _t(rng.standard_normal((2, 1, desc.dim)))
+    goal = _t(rng.standard_normal((2, 1, desc.dim)))
+    cand = _t(rng.standard_normal((2, 300, 5, desc.action_dim)))
+    mean, std = torch.zeros(2, 5, 10, device="cuda:0"), torch.ones(2, 5, 10, device="cuda:0")
+    opts = PlanOptions(num_samples=300, topk=30, n_steps=4, sample_decay=1.25, sample_count_bucket_size=60,
+                       elite_retention=3, beta=2.0)
+    rt = Runtime(desc, sd, "cuda:0")
+    assert rt.model_cost_autocast_mode() == "bf16"
+    c_bf16 = rt.model_cost(emb, goal, cand).clone()
+    p_bf16 = rt.plan(opts, emb, goal, mean, std, plan_index=3)[0].clone()
+    rt.set_model_cost_autocast("none")
+    c_f32 = rt.model_cost(emb, goal, cand).clone()
+    p_f32 = rt.plan(opts, emb, goal, mean, std, plan_index=3)[0].clone()
+    p_f32b = rt.plan(opts, emb, goal, mean, std, plan_index=3)[0].clone()  # graph replay
+    rt.set_model_cost_autocast("bf16")
+    c_bf16b = rt.model_cost(emb, goal, cand)
+    p_bf16b = rt.plan(opts, emb, goal, mean, std, plan_index=3)[0]
+    rt.sync()
+    assert torch.equal(c_bf16, c_bf16b) and torch.equal(p_bf16, p_bf16b)
+    assert torch.equal(p_f32, p_f32b)
+    want = lo.get_cost_from_embeddings(emb.cpu().numpy(), goal.cpu().numpy(), cand.cpu().numpy(), sd, desc)
+    assert cost_stats(c_f32.cpu().numpy(), want)["allclose"]
+    assert not cost_stats(c_bf16.cpu().numpy(), want)["allclose"]  # bf16 sits at its own ~1e-3 bound
+    with pytest.raises(ValueError):
+        rt.set_model_cost_autocast("fp16")
+    rt.close()

@@ -3,7 +3,7 @@
 Fixtures from ``tests/golden/make_headline_golden.py`` (the reference's own
 ``ICEMSolver`` / ``run_static_icem_chain``, fp32 CPU): bucketed iCEM 300 -> 60 over
 30 iterations, brown noise, retention 3 / 5, 1 env with history 1 and 4 envs with
-history 3. The oracle's chain, driven by the reference's per-iteration costs,
+history 3; plain CEM 300 / 30 / 30, 1 env, history 1. The oracle's chain, driven by the reference's per-iteration costs,
 selects the reference's elites in every iteration and reproduces its refit and
 outputs; the oracle's fp32 model cost reproduces the reference's costs of the
 first iteration's 300 candidates.
@@ -16,7 +16,7 @@ import pytest
 
 from oracle import icem_oracle as io
 from oracle import lewm_oracle as lo
-from tests.golden_io import GOLDEN, load, weights_of
+from tests.golden_io import GOLDEN, assert_same_topk, load, weights_of
 
 HEADLINE_CASES = sorted(p.name for p in GOLDEN.glob("icem_headline_*.npz"))
 
@@ -35,7 +35,7 @@ def test_oracle_chain_fed_reference_costs_reproduces_reference(case):
         [d[f"noise_{i}"] for i in range(n)], topk=kw["topk"], elite_retention=kw["elite_retention"], trace=trace)
     np.testing.assert_allclose(trace[0]["candidates"], d["cand_0"], rtol=1e-6, atol=1e-6)
     for i, t in enumerate(trace):
-        assert np.array_equal(t["topk_inds"], d[f"inds_{i}"]), f"elite indices differ at iteration {i}"
+        assert_same_topk(t["topk_inds"], d[f"inds_{i}"], d[f"cost_{i}"], f"iteration {i}")
         scale = float(np.abs(d[f"mean_{i}"]).max()) + 1.0
         np.testing.assert_allclose(t["mean"], d[f"mean_{i}"], rtol=1e-5, atol=1e-6 * scale)
         np.testing.assert_allclose(t["var"], d[f"std_{i}"], rtol=1e-5, atol=1e-6 * scale)
