@@ -367,84 +367,82 @@ lewm_status pack_weights(lewm_ctx* c, const float* wts, size_t n) {
 // holds whole candidates (at most 128 rows). A call with few candidates is spread
 // over up to `target` tiles (one wave of the one-head-per-CTA QKV kernel), so each
 // CTA of the streamed-operand GEMMs moves fewer rows; a large call uses full tiles.
-// The float32 weights of the fp32 model cost: the canonical host array uploaded as given,
-// plus [2P] per-column scale / shift of a pred_proj head without a LayerNorm (BatchNorm1d in
-// eval folded with the first Linear's bias, computed in double; scale 1, shift = bias with no
-// norm).
+// The float32 weights of the fp32 model cost: each tensor of the canonical host array at a
+// 16-byte aligned offset (so the GEMMs' 16-byte loads apply), plus [2P] per-column scale /
+// shift of a pred_proj head without a LayerNorm (BatchNorm1d in eval folded with the first
+// Linear's bias, computed in double; scale 1, shift = bias with no norm).
 lewm_status upload_f32_weights(lewm_ctx* c, const float* wts, size_t n) {
   const ModelDims& m = c->md;
   const size_t D = m.D, P = m.pp_hidden;
-  const size_t n_aff = (P && m.pp_norm != 1) ? 2 * P : 0;
-  LEWM_CK(c, cudaMalloc(&c->d_w32, (n + n_aff) * 4));
-  LEWM_CK(c, cudaMemcpy(c->d_w32, wts, n * 4, cudaMemcpyHostToDevice));
-  const float* base = static_cast<const float*>(c->d_w32);
-  size_t off = 0;
-  auto take = [&](size_t k) {
-    const float* q = base + off;
-    off += k;
-    return q;
+  std::vector<float> stage;
+  size_t src = 0;
+  std::vector<std::pair<const float**, size_t>> fix;  // pointer to set, staged offset
+  auto place = [&](const float* data, size_t k) {
+    const size_t off = round_up(stage.size(), 4);
+    stage.resize(off + k);
+    std::memcpy(stage.data() + off, data, k * 4);
+    return off;
   };
+  auto take = [&](const float** dst, size_t k) {
+    fix.emplace_back(dst, place(wts + src, k));
+    src += k;
+  };
+  auto skip = [&](size_t k) { src += k; };
   F32Weights& w = c->w32;
-  w.pos = take((size_t)m.frames * D);
-  w.layers.resize(m.L);
+  take(&w.pos, (size_t)m.frames * D);
+  w.layers.assign(m.L, F32Layer{});
   for (int l = 0; l < m.L; ++l) {
     F32Layer& lw = w.layers[l];
-    lw.ada_w = take(6 * D * D);
-    lw.ada_b = take(6 * D);
-    lw.attn_ln_w = take(D);
-    lw.attn_ln_b = take(D);
-    lw.qkv_w = take(3 * (size_t)m.inner * D);
-    lw.out_w = take(D * m.inner);
-    lw.out_b = take(D);
-    lw.ffn_ln_w = take(D);
-    lw.ffn_ln_b = take(D);
-    lw.w1 = take((size_t)m.mlp * D);
-    lw.b1 = take(m.mlp);
-    lw.w2 = take(D * m.mlp);
-    lw.b2 = take(D);
+    take(&lw.ada_w, 6 * D * D);
+    take(&lw.ada_b, 6 * D);
+    take(&lw.attn_ln_w, D);
+    take(&lw.attn_ln_b, D);
+    take(&lw.qkv_w, 3 * (size_t)m.inner * D);
+    take(&lw.out_w, D * m.inner);
+    take(&lw.out_b, D);
+    take(&lw.ffn_ln_w, D);
+    take(&lw.ffn_ln_b, D);
+    take(&lw.w1, (size_t)m.mlp * D);
+    take(&lw.b1, m.mlp);
+    take(&lw.w2, D * m.mlp);
+    take(&lw.b2, D);
   }
-  w.fin_w = take(D);
-  w.fin_b = take(D);
-  w.conv_w = take((size_t)m.As * m.A);
-  w.conv_b = take(m.As);
-  w.e1_w = take((size_t)m.eh * m.As);
-  w.e1_b = take(m.eh);
-  w.e2_w = take(D * m.eh);
-  w.e2_b = take(D);
+  take(&w.fin_w, D);
+  take(&w.fin_b, D);
+  take(&w.conv_w, (size_t)m.As * m.A);
+  take(&w.conv_b, m.As);
+  take(&w.e1_w, (size_t)m.eh * m.As);
+  take(&w.e1_b, m.eh);
+  take(&w.e2_w, D * m.eh);
+  take(&w.e2_b, D);
   if (P) {  // net.0.weight, net.0.bias, norm parameters, net.3.weight, net.3.bias
-    const size_t o_b1 = off + P * D;
-    w.pp_w1 = take(P * D);
-    w.pp_b1 = take(P);
-    std::vector<float> aff(n_aff);
+    take(&w.pp_w1, P * D);
+    const float* hb = wts + src;
+    take(&w.pp_b1, P);
     if (m.pp_norm == 1) {
-      w.pp_ln_g = take(P);
-      w.pp_ln_b = take(P);
-    } else if (m.pp_norm == 2) {
-      const float* hb = wts + o_b1;  // Linear bias, then BatchNorm weight, bias, running mean, var
-      const size_t o_bn = off;
-      const float *g = wts + o_bn, *bb = g + P, *mu = bb + P, *var = mu + P;
-      for (size_t j = 0; j < P; ++j) {
-        const double sc = (double)g[j] / std::sqrt((double)var[j] + 1e-5);
-        aff[j] = (float)sc;
-        aff[P + j] = (float)(((double)hb[j] - mu[j]) * sc + bb[j]);
-      }
-      take(4 * P);
+      take(&w.pp_ln_g, P);
+      take(&w.pp_ln_b, P);
     } else {
-      for (size_t j = 0; j < P; ++j) {
-        aff[j] = 1.f;
-        aff[P + j] = wts[o_b1 + j];
+      std::vector<float> scale(P, 1.f), shift(hb, hb + P);
+      if (m.pp_norm == 2) {  // BatchNorm1d weight, bias, running mean, running var
+        const float *g = wts + src, *bb = g + P, *mu = bb + P, *var = mu + P;
+        for (size_t j = 0; j < P; ++j) {
+          const double sc = (double)g[j] / std::sqrt((double)var[j] + 1e-5);
+          scale[j] = (float)sc;
+          shift[j] = (float)(((double)hb[j] - mu[j]) * sc + bb[j]);
+        }
+        skip(4 * P);
       }
+      fix.emplace_back(&w.pp_scale, place(scale.data(), P));
+      fix.emplace_back(&w.pp_shift, place(shift.data(), P));
     }
-    w.pp_w2 = take(D * P);
-    w.pp_b2 = take(D);
-    if (n_aff) {
-      float* d_aff = static_cast<float*>(c->d_w32) + n;
-      LEWM_CK(c, cudaMemcpy(d_aff, aff.data(), n_aff * 4, cudaMemcpyHostToDevice));
-      w.pp_scale = d_aff;
-      w.pp_shift = d_aff + P;
-    }
+    take(&w.pp_w2, D * P);
+    take(&w.pp_b2, D);
   }
-  if (off != n) return fail(c, LEWM_INVALID_ARG, "fp32 weight walk mismatch");
+  if (src != n) return fail(c, LEWM_INVALID_ARG, "fp32 weight walk mismatch");
+  LEWM_CK(c, cudaMalloc(&c->d_w32, stage.size() * 4));
+  LEWM_CK(c, cudaMemcpy(c->d_w32, stage.data(), stage.size() * 4, cudaMemcpyHostToDevice));
+  for (auto& f : fix) *f.first = static_cast<const float*>(c->d_w32) + f.second;
   return LEWM_OK;
 }
 

@@ -16,7 +16,7 @@
 namespace lewm {
 namespace {
 
-constexpr int GB_M = 64, GB_N = 64, GB_K = 16, G_THREADS = 256;
+constexpr int GB_M = 64, GB_N = 64, GB_K = 32, G_THREADS = 256;
 
 enum GemmEpi { GE_BIAS = 0, GE_SILU = 1, GE_GELU = 2, GE_RESID = 3 };
 
@@ -26,27 +26,73 @@ __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + e
 //   GE_BIAS  C = acc + bias                  GE_SILU  C = silu(acc + bias)
 //   GE_GELU  C = gelu(acc + bias)            GE_RESID X += gate . (acc + bias), in place,
 //   gate = mod[row_tok[m] * mod_ld + gate_off + n]
-// 64 x 64 output tile per CTA, 4 x 4 outputs per thread, K in slabs of 16 through shared
-// memory (transposed so the inner loop reads float4s); every output's K order is fixed.
-template <int EPI>
+// 64 x 64 output tile per CTA, 4 x 4 outputs per thread, K in slabs of 32 staged through
+// shared memory (transposed, so the inner loop reads float4s). The next slab's global loads
+// are issued into registers before the current slab's FMAs (one slab in flight: the kernel
+// is bound by load latency at the planner's few hundred rows). VEC: 16-byte loads (K, lda
+// multiples of 4 and 16-byte aligned A / W), else scalar loads. Every output sums its K
+// products in increasing k, one fmaf each, whatever the grid.
+template <int EPI, bool VEC>
 __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A, int lda, const float* __restrict__ W,
                                                      int K, const float* __restrict__ bias, float* __restrict__ C, int ldc,
                                                      int M, int N, const float* __restrict__ mod,
                                                      const int* __restrict__ row_tok, int mod_ld, int gate_off) {
-  __shared__ float sA[GB_K][GB_M + 4];
-  __shared__ float sW[GB_K][GB_N + 4];
+  __shared__ __align__(16) float sA[GB_K][GB_M + 4];
+  __shared__ __align__(16) float sW[GB_K][GB_N + 4];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int m0 = blockIdx.y * GB_M, n0 = blockIdx.x * GB_N;
-  float acc[4][4] = {};
-  for (int k0 = 0; k0 < K; k0 += GB_K) {
-    for (int i = tid; i < GB_M * GB_K; i += G_THREADS) {
-      const int r = i / GB_K, kk = i % GB_K;
-      const int m = m0 + r, k = k0 + kk;
-      sA[kk][r] = (m < M && k < K) ? A[(size_t)m * lda + k] : 0.f;
-      const int n = n0 + r;
-      sW[kk][r] = (n < N && k < K) ? W[(size_t)n * K + k] : 0.f;
+  // Per slab each thread moves 8 A values and 8 W values: VEC as 2 float4 (row s / 8,
+  // k 4 (s % 8)), scalar as 8 floats (row s / 32, k s % 32), s = tid + 256 q.
+  float ra[8], rw[8];
+  auto load = [&](int k0) {
+    if constexpr (VEC) {
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int sl = tid + q * G_THREADS, r = sl >> 3, k = k0 + (sl & 7) * 4;
+        const int m = m0 + r, n = n0 + r;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), w = a;
+        if (m < M && k < K) a = *reinterpret_cast<const float4*>(A + (size_t)m * lda + k);
+        if (n < N && k < K) w = *reinterpret_cast<const float4*>(W + (size_t)n * K + k);
+        ra[4 * q] = a.x, ra[4 * q + 1] = a.y, ra[4 * q + 2] = a.z, ra[4 * q + 3] = a.w;
+        rw[4 * q] = w.x, rw[4 * q + 1] = w.y, rw[4 * q + 2] = w.z, rw[4 * q + 3] = w.w;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int sl = tid + q * G_THREADS, r = sl >> 5, k = k0 + (sl & 31);
+        const int m = m0 + r, n = n0 + r;
+        ra[q] = (m < M && k < K) ? A[(size_t)m * lda + k] : 0.f;
+        rw[q] = (n < N && k < K) ? W[(size_t)n * K + k] : 0.f;
+      }
     }
-    __syncthreads();
+  };
+  auto store = [&]() {
+    if constexpr (VEC) {
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int sl = tid + q * G_THREADS, r = sl >> 3, kk = (sl & 7) * 4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sA[kk + j][r] = ra[4 * q + j];
+          sW[kk + j][r] = rw[4 * q + j];
+        }
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int sl = tid + q * G_THREADS, r = sl >> 5, kk = sl & 31;
+        sA[kk][r] = ra[q];
+        sW[kk][r] = rw[q];
+      }
+    }
+  };
+  float acc[4][4] = {};
+  load(0);
+  store();
+  __syncthreads();
+  for (int k0 = 0; k0 < K; k0 += GB_K) {
+    const bool more = k0 + GB_K < K;
+    if (more) load(k0 + GB_K);
 #pragma unroll
     for (int kk = 0; kk < GB_K; ++kk) {
       const float4 a = *reinterpret_cast<const float4*>(&sA[kk][ty * 4]);
@@ -58,6 +104,10 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
         for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
     __syncthreads();
+    if (more) {
+      store();
+      __syncthreads();
+    }
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -225,7 +275,11 @@ cudaError_t sgemm(const float* A, int lda, const float* W, int K, const float* b
                   cudaStream_t st, const float* mod = nullptr, const int* row_tok = nullptr, int mod_ld = 0,
                   int gate_off = 0) {
   const dim3 grid((N + GB_N - 1) / GB_N, (M + GB_M - 1) / GB_M);
-  k_sgemm<EPI><<<grid, G_THREADS, 0, st>>>(A, lda, W, K, bias, C, ldc, M, N, mod, row_tok, mod_ld, gate_off);
+  const bool vec = K % 4 == 0 && lda % 4 == 0 && (reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W)) % 16 == 0;
+  if (vec)
+    k_sgemm<EPI, true><<<grid, G_THREADS, 0, st>>>(A, lda, W, K, bias, C, ldc, M, N, mod, row_tok, mod_ld, gate_off);
+  else
+    k_sgemm<EPI, false><<<grid, G_THREADS, 0, st>>>(A, lda, W, K, bias, C, ldc, M, N, mod, row_tok, mod_ld, gate_off);
   return cudaGetLastError();
 }
 
