@@ -116,6 +116,23 @@ LEWM_API lewm_status lewm_model_cost(lewm_ctx* ctx, const float* emb, int32_t em
                             int32_t goal_per_sample, const float* cand, int32_t B, int32_t S, int32_t T,
                             int32_t history_size, float* costs_out, void* stream);
 
+/* Model costs and their gradient with respect to the action candidates: the gradient
+ * CEM-GD's refinement steps on (reference lewm/solvers/cem_gd.py:459-606 takes torch
+ * autograd of JEPA.get_cost_from_embeddings, lewm/jepa.py:302-317). Float32 forward and
+ * reverse pass on CUDA cores whatever the context's autocast mode (a bf16 rollout has no
+ * useful gradient at this precision). Arguments as lewm_model_cost, plus
+ *   cost_weights (B,S) device, or NULL for all ones: w in d(sum_c w_c cost_c) / d cand;
+ *     candidates are independent, so grad_out[c] = w_c * d cost_c / d cand_c
+ *   grad_out (B,S,T,A)
+ * The embeddings and the goal are constants (no gradient). Needs an Identity pred_proj
+ * (LEWM_UNSUPPORTED_SHAPE otherwise) and B*S*T <= 2^22. Keeps the forward's activations
+ * in a context buffer that grows to the largest call (about 1.5 MB per candidate at
+ * width 192, T 5, window 3). */
+LEWM_API lewm_status lewm_model_cost_grad(lewm_ctx* ctx, const float* emb, int32_t emb_per_sample, int32_t H,
+                                          const float* goal, int32_t goal_per_sample, const float* cand, int32_t B,
+                                          int32_t S, int32_t T, int32_t history_size, const float* cost_weights,
+                                          float* costs_out, float* grad_out, void* stream);
+
 /* iCEM solver options (reference ICEMSolver.__init__, lewm/solvers/icem.py:258-322). */
 typedef struct lewm_plan_desc {
   int32_t n_envs;           /* B */

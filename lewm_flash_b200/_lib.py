@@ -78,6 +78,9 @@ SIGNATURES = {
     "lewm_last_error": (C.c_char_p, [C.c_void_p]),
     "lewm_model_cost": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_void_p,
                                   C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
+    "lewm_model_cost_grad": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_int32,
+                                       C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
+                                       C.c_void_p, C.c_void_p, C.c_void_p]),
     "lewm_sample_counts": (C.c_int, [C.POINTER(PlanDescC), C.c_void_p, C.c_int32, C.POINTER(C.c_int64)]),
     "lewm_plan": (C.c_int, [C.c_void_p, C.POINTER(PlanDescC), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                             C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,

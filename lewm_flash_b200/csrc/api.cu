@@ -108,6 +108,8 @@ struct lewm_ctx {
   int autocast = 1;           // model-cost arithmetic: 1 bf16 tensor cores (default), 0 float32
   void* d_w32 = nullptr;      // float32 weights of the fp32 model cost
   F32Weights w32;
+  float* d_grad = nullptr;    // tape + gradient buffers of lewm_model_cost_grad
+  size_t grad_floats = 0;
   MlpHead pp{};  // pred_proj MLP head (P == 0: Identity)
   uint32_t* d_status = nullptr;
   Workspace ws;
@@ -391,8 +393,10 @@ lewm_status upload_f32_weights(lewm_ctx* c, const float* wts, size_t n) {
   F32Weights& w = c->w32;
   take(&w.pos, (size_t)m.frames * D);
   w.layers.assign(m.L, F32Layer{});
+  std::vector<const float*> ada_src(m.L);
   for (int l = 0; l < m.L; ++l) {
     F32Layer& lw = w.layers[l];
+    ada_src[l] = wts + src;
     take(&lw.ada_w, 6 * D * D);
     take(&lw.ada_b, 6 * D);
     take(&lw.attn_ln_w, D);
@@ -440,6 +444,12 @@ lewm_status upload_f32_weights(lewm_ctx* c, const float* wts, size_t n) {
     take(&w.pp_b2, D);
   }
   if (src != n) return fail(c, LEWM_INVALID_ARG, "fp32 weight walk mismatch");
+  {  // every layer's adaLN weight stacked, [L * 6D][D], for the reverse pass's single GEMM
+    const size_t per = 6 * D * D, off = round_up(stage.size(), 4);
+    stage.resize(off + per * m.L);
+    for (int l = 0; l < m.L; ++l) std::memcpy(stage.data() + off + per * l, ada_src[l], per * 4);
+    fix.emplace_back(&w.ada_stack, off);
+  }
   LEWM_CK(c, cudaMalloc(&c->d_w32, stage.size() * 4));
   LEWM_CK(c, cudaMemcpy(c->d_w32, stage.data(), stage.size() * 4, cudaMemcpyHostToDevice));
   for (auto& f : fix) *f.first = static_cast<const float*>(c->d_w32) + f.second;
@@ -468,7 +478,7 @@ void clear_graphs(lewm_ctx* c) {
 
 lewm_status ensure_ws(lewm_ctx* c, const WsReq& need_in) {
   WsReq need = need_in;
-  need.f32 = c->autocast == 0 ? 1 : 0;
+  need.f32 = std::max<size_t>(need_in.f32, c->autocast == 0 ? 1 : 0);
   if (c->have_ws && need <= c->cap) return LEWM_OK;
   WsReq r = need;
   if (c->have_ws) {  // grow monotonically
@@ -1054,6 +1064,7 @@ void lewm_destroy(lewm_ctx* c) {
   if (c->ws.base) cudaFree(c->ws.base);
   if (c->d_weights) cudaFree(c->d_weights);
   if (c->d_w32) cudaFree(c->d_w32);
+  if (c->d_grad) cudaFree(c->d_grad);
   mlp_head_destroy(&c->pp);
   if (c->d_status) cudaFree(c->d_status);
   delete c;
@@ -1082,6 +1093,46 @@ lewm_status lewm_model_cost(lewm_ctx* c, const float* emb, int32_t emb_per_sampl
   if (s != LEWM_OK) return s;
   return run_model_cost(c, emb, emb_per_sample != 0, H, goal, goal_per_sample != 0, cand, B, S, T, history_size,
                         costs_out, st);
+}
+
+lewm_status lewm_model_cost_grad(lewm_ctx* c, const float* emb, int32_t emb_per_sample, int32_t H, const float* goal,
+                                 int32_t goal_per_sample, const float* cand, int32_t B, int32_t S, int32_t T,
+                                 int32_t history_size, const float* cost_weights, float* costs_out, float* grad_out,
+                                 void* stream) {
+  if (!c) return fail(nullptr, LEWM_INVALID_ARG, "ctx is NULL");
+  c->err.clear();
+  if (!emb || !goal || !cand || !costs_out || !grad_out) return fail(c, LEWM_INVALID_ARG, "NULL tensor pointer");
+  if (B <= 0 || S <= 0 || T <= 0 || H <= 0 || H > T || history_size <= 0)
+    return fail(c, LEWM_INVALID_ARG, "need B,S,T > 0 and 1 <= H <= T, got B=%d S=%d T=%d H=%d", B, S, T, H);
+  if (history_size > c->md.frames)
+    return fail(c, LEWM_UNSUPPORTED_SHAPE, "history_size=%d exceeds num_frames=%d", history_size, c->md.frames);
+  if (c->md.pp_hidden)
+    return fail(c, LEWM_UNSUPPORTED_SHAPE, "the model-cost gradient covers an Identity pred_proj only");
+  if ((int64_t)B * S * T > (1ll << 22)) return fail(c, LEWM_UNSUPPORTED_SHAPE, "B*S*T too large for the gradient");
+  DeviceGuard g(c->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int NC = B * S;
+  WsReq need{(size_t)NC, (size_t)T, (size_t)c->md.A, (size_t)c->md.D, (size_t)c->md.L,
+             (size_t)max_call_tiles(NC, T, H, history_size, c->tile_target), (size_t)c->md.heads, (size_t)c->md.mlp,
+             (size_t)(T - H + 1), 1, 0, 0, (size_t)kv_positions(H, history_size)};
+  need.f32 = 1;
+  lewm_status s = ensure_ws(c, need);
+  if (s != LEWM_OK) return s;
+  const size_t nf = f32_grad_floats(c->md, NC, T, H, history_size);
+  if (nf > c->grad_floats) {  // grows; cudaFree waits for the work that used the old buffers
+    if (c->d_grad) cudaFree(c->d_grad);
+    c->d_grad = nullptr;
+    c->grad_floats = 0;
+    LEWM_CK(c, cudaMalloc(&c->d_grad, nf * 4));
+    c->grad_floats = nf;
+  }
+  F32Tape tape;
+  F32GradWork gw{};
+  f32_grad_carve(c->md, NC, T, H, history_size, c->d_grad, &tape, &gw);
+  LEWM_CK(c, run_model_cost_grad_fp32(c->md, c->w32, c->ws.f32, tape, gw, emb, emb_per_sample != 0, H, goal,
+                                      goal_per_sample != 0, cand, B, S, T, history_size, cost_weights, costs_out,
+                                      grad_out, st));
+  return LEWM_OK;
 }
 
 lewm_status lewm_sample_counts(const lewm_plan_desc* plan, int32_t* counts_out, int32_t cap, int64_t* evals_out) {

@@ -8,6 +8,7 @@
 // two-pass moments, exact-erf GELU and expf-based SiLU / softmax. It exists for the
 // reference's float32 exactness gate (tools/benchmarks/check_lewm_cache_exactness.py:
 // 783-784) and its fp32 CEM configuration; the bf16 tensor-core path is the fast one.
+#include <algorithm>
 #include <cmath>
 
 #include "lewm_common.cuh"
@@ -26,6 +27,7 @@ __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + e
 //   GE_BIAS  C = acc + bias                  GE_SILU  C = silu(acc + bias)
 //   GE_GELU  C = gelu(acc + bias)            GE_RESID X += gate . (acc + bias), in place,
 //   gate = mod[row_tok[m] * mod_ld + gate_off + n]
+// and, when `save` is set, save[m][n] = acc + bias (an [M][N] array) for the reverse pass.
 // 64 x 64 output tile per CTA, 4 x 4 outputs per thread, K in slabs of 32 staged through
 // shared memory (transposed, so the inner loop reads float4s). The next slab's global loads
 // are issued into registers before the current slab's FMAs (one slab in flight: the kernel
@@ -36,7 +38,8 @@ template <int EPI, bool VEC>
 __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A, int lda, const float* __restrict__ W,
                                                      int K, const float* __restrict__ bias, float* __restrict__ C, int ldc,
                                                      int M, int N, const float* __restrict__ mod,
-                                                     const int* __restrict__ row_tok, int mod_ld, int gate_off) {
+                                                     const int* __restrict__ row_tok, int mod_ld, int gate_off,
+                                                     float* __restrict__ save) {
   __shared__ __align__(16) float sA[GB_K][GB_M + 4];
   __shared__ __align__(16) float sW[GB_K][GB_N + 4];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -118,6 +121,7 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
       const int n = n0 + tx * 4 + j;
       if (n >= N) continue;
       const float v = acc[i][j] + (bias ? bias[n] : 0.f);
+      if (save) save[(size_t)m * N + n] = v;  // pre-activation / branch output for the reverse pass
       if constexpr (EPI == GE_BIAS) C[(size_t)m * ldc + n] = v;
       if constexpr (EPI == GE_SILU) C[(size_t)m * ldc + n] = v / (1.0f + expf(-v));
       if constexpr (EPI == GE_GELU) C[(size_t)m * ldc + n] = gelu_erf(v);
@@ -273,13 +277,15 @@ __global__ void __launch_bounds__(256) k_emit32(const float* __restrict__ y, int
 template <int EPI>
 cudaError_t sgemm(const float* A, int lda, const float* W, int K, const float* bias, float* C, int ldc, int M, int N,
                   cudaStream_t st, const float* mod = nullptr, const int* row_tok = nullptr, int mod_ld = 0,
-                  int gate_off = 0) {
+                  int gate_off = 0, float* save = nullptr) {
   const dim3 grid((N + GB_N - 1) / GB_N, (M + GB_M - 1) / GB_M);
   const bool vec = K % 4 == 0 && lda % 4 == 0 && (reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W)) % 16 == 0;
   if (vec)
-    k_sgemm<EPI, true><<<grid, G_THREADS, 0, st>>>(A, lda, W, K, bias, C, ldc, M, N, mod, row_tok, mod_ld, gate_off);
+    k_sgemm<EPI, true><<<grid, G_THREADS, 0, st>>>(A, lda, W, K, bias, C, ldc, M, N, mod, row_tok, mod_ld, gate_off,
+                                                   save);
   else
-    k_sgemm<EPI, false><<<grid, G_THREADS, 0, st>>>(A, lda, W, K, bias, C, ldc, M, N, mod, row_tok, mod_ld, gate_off);
+    k_sgemm<EPI, false><<<grid, G_THREADS, 0, st>>>(A, lda, W, K, bias, C, ldc, M, N, mod, row_tok, mod_ld, gate_off,
+                                                    save);
   return cudaGetLastError();
 }
 
@@ -293,14 +299,16 @@ cudaError_t sgemm(const float* A, int lda, const float* W, int K, const float* b
 
 cudaError_t run_model_cost_fp32(const ModelDims& m, const F32Weights& w, const F32Work& ws, const float* emb,
                                 int emb_pc, int H, const float* goal, int goal_pc, const float* cand, int B, int S,
-                                int T, int HS, float* costs, cudaStream_t st) {
+                                int T, int HS, float* costs, cudaStream_t st, const F32Tape* tape) {
   const int NC = B * S, NT = NC * T, D = m.D, L = m.L, inner = m.inner;
   const int mod_ld = L * 6 * D;
   // Embedder (lewm/module.py:189-214): Conv1d(k = 1) -> Linear -> SiLU -> Linear; the blocks
   // use SiLU(act_emb) (the first layer of adaLN_modulation), so that is what is kept.
   F32_TRY(sgemm<GE_BIAS>(cand, m.A, w.conv_w, m.A, w.conv_b, ws.act, m.As, NT, m.As, st));
-  F32_TRY(sgemm<GE_SILU>(ws.act, m.As, w.e1_w, m.As, w.e1_b, ws.eh, m.eh, NT, m.eh, st));
-  F32_TRY(sgemm<GE_SILU>(ws.eh, m.eh, w.e2_w, m.eh, w.e2_b, ws.sact, D, NT, D, st));
+  F32_TRY(sgemm<GE_SILU>(ws.act, m.As, w.e1_w, m.As, w.e1_b, ws.eh, m.eh, NT, m.eh, st, nullptr, nullptr, 0, 0,
+                         tape ? tape->h1 : nullptr));
+  F32_TRY(sgemm<GE_SILU>(ws.eh, m.eh, w.e2_w, m.eh, w.e2_b, ws.sact, D, NT, D, st, nullptr, nullptr, 0, 0,
+                         tape ? tape->e : nullptr));
   for (int l = 0; l < L; ++l)  // AdaLN modulation of every token and layer
     F32_TRY(sgemm<GE_BIAS>(ws.sact, D, w.layers[l].ada_w, D, w.layers[l].ada_b, ws.mod + l * 6 * D, mod_ld, NT,
                            6 * D, st));
@@ -308,25 +316,33 @@ cudaError_t run_model_cost_fp32(const ModelDims& m, const F32Weights& w, const F
   for (int k = 0; k < n_calls; ++k) {
     const int end = H + k, start = end > HS ? end - HS : 0, wlen = end - start;
     const int rows = NC * wlen;
+    const F32TapeCall* tc = tape ? &tape->calls[k] : nullptr;
+    int* row_tok = tc ? tc->row_tok : ws.row_tok;
+    const size_t RD = (size_t)rows * D;
     k_rows_init32<<<rows, 64, 0, st>>>(emb, emb_pc, ws.pred, w.pos, NC, S, T, H, wlen, start, n_calls, D, ws.x,
-                                       ws.row_tok);
+                                       row_tok);
     F32_TRY(cudaGetLastError());
     const int lnb = (rows + 7) / 8;
     for (int l = 0; l < L; ++l) {  // ConditionalBlock (lewm/module.py:88-111)
       const F32Layer& lw = w.layers[l];
       const int mo = l * 6 * D;  // shift_msa | scale_msa | gate_msa | shift_mlp | scale_mlp | gate_mlp
-      k_ln_mod32<<<lnb, 256, 0, st>>>(ws.x, rows, D, ws.row_tok, ws.mod, mod_ld, mo, mo + D, lw.attn_ln_w,
-                                      lw.attn_ln_b, ws.a);
-      F32_TRY(sgemm<GE_BIAS>(ws.a, D, lw.qkv_w, D, nullptr, ws.qkv, 3 * inner, rows, 3 * inner, st));
-      k_attn32<<<(rows * m.heads + 7) / 8, 256, 0, st>>>(ws.qkv, rows, wlen, m.heads, ws.att);
-      F32_TRY(sgemm<GE_RESID>(ws.att, inner, lw.out_w, inner, lw.out_b, ws.x, D, rows, D, st, ws.mod, ws.row_tok,
-                              mod_ld, mo + 2 * D));
-      k_ln_mod32<<<lnb, 256, 0, st>>>(ws.x, rows, D, ws.row_tok, ws.mod, mod_ld, mo + 3 * D, mo + 4 * D, lw.ffn_ln_w,
+      float* qkv = tc ? tc->qkv + (size_t)l * rows * 3 * inner : ws.qkv;
+      if (tc) F32_TRY(cudaMemcpyAsync(tc->x_in + l * RD, ws.x, RD * 4, cudaMemcpyDeviceToDevice, st));
+      k_ln_mod32<<<lnb, 256, 0, st>>>(ws.x, rows, D, row_tok, ws.mod, mod_ld, mo, mo + D, lw.attn_ln_w, lw.attn_ln_b,
+                                      ws.a);
+      F32_TRY(sgemm<GE_BIAS>(ws.a, D, lw.qkv_w, D, nullptr, qkv, 3 * inner, rows, 3 * inner, st));
+      k_attn32<<<(rows * m.heads + 7) / 8, 256, 0, st>>>(qkv, rows, wlen, m.heads, ws.att);
+      F32_TRY(sgemm<GE_RESID>(ws.att, inner, lw.out_w, inner, lw.out_b, ws.x, D, rows, D, st, ws.mod, row_tok, mod_ld,
+                              mo + 2 * D, tc ? tc->o + l * RD : nullptr));
+      if (tc) F32_TRY(cudaMemcpyAsync(tc->x_mid + l * RD, ws.x, RD * 4, cudaMemcpyDeviceToDevice, st));
+      k_ln_mod32<<<lnb, 256, 0, st>>>(ws.x, rows, D, row_tok, ws.mod, mod_ld, mo + 3 * D, mo + 4 * D, lw.ffn_ln_w,
                                       lw.ffn_ln_b, ws.a);
-      F32_TRY(sgemm<GE_GELU>(ws.a, D, lw.w1, D, lw.b1, ws.hid, m.mlp, rows, m.mlp, st));
-      F32_TRY(sgemm<GE_RESID>(ws.hid, m.mlp, lw.w2, m.mlp, lw.b2, ws.x, D, rows, D, st, ws.mod, ws.row_tok, mod_ld,
-                              mo + 5 * D));
+      F32_TRY(sgemm<GE_GELU>(ws.a, D, lw.w1, D, lw.b1, ws.hid, m.mlp, rows, m.mlp, st, nullptr, nullptr, 0, 0,
+                             tc ? tc->f1 + (size_t)l * rows * m.mlp : nullptr));
+      F32_TRY(sgemm<GE_RESID>(ws.hid, m.mlp, lw.w2, m.mlp, lw.b2, ws.x, D, rows, D, st, ws.mod, row_tok, mod_ld,
+                              mo + 5 * D, tc ? tc->f2 + l * RD : nullptr));
     }
+    if (tc) F32_TRY(cudaMemcpyAsync(tc->x_out, ws.x, RD * 4, cudaMemcpyDeviceToDevice, st));
     k_final_ln32<<<(NC + 7) / 8, 256, 0, st>>>(ws.x, NC, wlen, D, w.fin_w, w.fin_b, ws.y);
     F32_TRY(cudaGetLastError());
     if (m.pp_hidden) {  // pred_proj MLP head on the new predictions (lewm/jepa.py:106-114)
@@ -344,8 +360,472 @@ cudaError_t run_model_cost_fp32(const ModelDims& m, const F32Weights& w, const F
     k_emit32<<<(NC + 7) / 8, 256, 0, st>>>(ws.y, NC, D, k == n_calls - 1 ? 1 : 0, k, n_calls, ws.pred, goal, goal_pc,
                                            S, costs);
     F32_TRY(cudaGetLastError());
+    if (tape && k == n_calls - 1)
+      F32_TRY(cudaMemcpyAsync(tape->y, ws.y, (size_t)NC * D * 4, cudaMemcpyDeviceToDevice, st));
   }
   return cudaSuccess;
+}
+
+}  // namespace lewm
+
+namespace lewm {
+
+// ------------------------------------------------------------------------------------------
+// Reverse mode: d cost / d action candidates, the gradient CEM-GD steps on (reference
+// lewm/solvers/cem_gd.py:459-606 takes torch autograd of get_cost_from_embeddings,
+// lewm/jepa.py:302-317). Float32 throughout, over the activations the forward recorded.
+namespace {
+
+enum NnEpi { NE_STORE = 0, NE_GELU_BWD = 1, NE_SILU_BWD = 2 };
+
+// d/dx of the exact GELU 0.5 x (1 + erf(x / sqrt 2)): Phi(x) + x phi(x).
+__device__ __forceinline__ float gelu_erf_grad(float x) {
+  const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752f));
+  return cdf + x * 0.39894228040143268f * expf(-0.5f * x * x);
+}
+// d/dx of x sigmoid(x): sigmoid(x) (1 + x (1 - sigmoid(x))).
+__device__ __forceinline__ float silu_grad(float x) {
+  const float sg = 1.0f / (1.0f + expf(-x));
+  return sg * (1.0f + x * (1.0f - sg));
+}
+
+// C[M x Kout] = A[M x Nin] . Bm[Nin x Kout] (Bm row-major with row stride Kout: a Linear's
+// [out][in] weight, so C = dY . W is the input gradient of y = x . W^T), then the epilogue:
+// NE_STORE C = acc; NE_GELU_BWD / NE_SILU_BWD C = acc * f'(pre[m][c]). Same tiling, slab
+// prefetch and fixed summation order as k_sgemm; VEC: 16-byte loads of A and Bm.
+template <int EPI, bool VEC>
+__global__ void __launch_bounds__(G_THREADS) k_sgemm_nn(const float* __restrict__ A, int lda, const float* __restrict__ Bm,
+                                                        int Nin, int Kout, float* __restrict__ C, int ldc, int M,
+                                                        const float* __restrict__ pre, int ldp) {
+  __shared__ __align__(16) float sA[GB_K][GB_M + 4];
+  __shared__ __align__(16) float sB[GB_K][GB_N + 4];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int m0 = blockIdx.y * GB_M, c0 = blockIdx.x * GB_N;
+  float ra[8], rb[8];
+  auto load = [&](int n0) {
+    if constexpr (VEC) {
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int sl = tid + q * G_THREADS;
+        const int r = sl >> 3, n = n0 + (sl & 7) * 4, m = m0 + r;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (m < M && n < Nin) a = *reinterpret_cast<const float4*>(A + (size_t)m * lda + n);
+        ra[4 * q] = a.x, ra[4 * q + 1] = a.y, ra[4 * q + 2] = a.z, ra[4 * q + 3] = a.w;
+        const int rr = sl >> 4, c = c0 + (sl & 15) * 4, nb = n0 + rr;
+        float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (nb < Nin && c < Kout) b = *reinterpret_cast<const float4*>(Bm + (size_t)nb * Kout + c);
+        rb[4 * q] = b.x, rb[4 * q + 1] = b.y, rb[4 * q + 2] = b.z, rb[4 * q + 3] = b.w;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int sl = tid + q * G_THREADS;
+        const int r = sl >> 5, n = n0 + (sl & 31), m = m0 + r;
+        ra[q] = (m < M && n < Nin) ? A[(size_t)m * lda + n] : 0.f;
+        const int rr = sl >> 6, c = c0 + (sl & 63), nb = n0 + rr;
+        rb[q] = (nb < Nin && c < Kout) ? Bm[(size_t)nb * Kout + c] : 0.f;
+      }
+    }
+  };
+  auto store = [&]() {
+    if constexpr (VEC) {
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int sl = tid + q * G_THREADS;
+        const int r = sl >> 3, kk = (sl & 7) * 4, rr = sl >> 4, cc = (sl & 15) * 4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sA[kk + j][r] = ra[4 * q + j];
+          sB[rr][cc + j] = rb[4 * q + j];
+        }
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int sl = tid + q * G_THREADS;
+        sA[sl & 31][sl >> 5] = ra[q];
+        sB[sl >> 6][sl & 63] = rb[q];
+      }
+    }
+  };
+  float acc[4][4] = {};
+  load(0);
+  store();
+  __syncthreads();
+  for (int n0 = 0; n0 < Nin; n0 += GB_K) {
+    const bool more = n0 + GB_K < Nin;
+    if (more) load(n0 + GB_K);
+#pragma unroll
+    for (int kk = 0; kk < GB_K; ++kk) {
+      const float4 a = *reinterpret_cast<const float4*>(&sA[kk][ty * 4]);
+      const float4 b = *reinterpret_cast<const float4*>(&sB[kk][tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+    if (more) {
+      store();
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty * 4 + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = c0 + tx * 4 + j;
+      if (c >= Kout) continue;
+      float v = acc[i][j];
+      if constexpr (EPI == NE_GELU_BWD) v *= gelu_erf_grad(pre[(size_t)m * ldp + c]);
+      if constexpr (EPI == NE_SILU_BWD) v *= silu_grad(pre[(size_t)m * ldp + c]);
+      C[(size_t)m * ldc + c] = v;
+    }
+  }
+}
+
+template <int EPI>
+cudaError_t sgemm_nn(const float* A, int lda, const float* Bm, int Nin, int Kout, float* C, int ldc, int M,
+                     cudaStream_t st, const float* pre = nullptr, int ldp = 0) {
+  const dim3 grid((Kout + GB_N - 1) / GB_N, (M + GB_M - 1) / GB_M);
+  const bool vec = Nin % 4 == 0 && lda % 4 == 0 && Kout % 4 == 0 &&
+                   (reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(Bm)) % 16 == 0;
+  if (vec)
+    k_sgemm_nn<EPI, true><<<grid, G_THREADS, 0, st>>>(A, lda, Bm, Nin, Kout, C, ldc, M, pre, ldp);
+  else
+    k_sgemm_nn<EPI, false><<<grid, G_THREADS, 0, st>>>(A, lda, Bm, Nin, Kout, C, ldc, M, pre, ldp);
+  return cudaGetLastError();
+}
+
+// dY[c] = 2 (y[c] - goal) * weight[c]: d of weight . sum_d (y - goal)^2 (lewm/jepa.py:246-260).
+__global__ void __launch_bounds__(256) k_seed32(const float* __restrict__ y, const float* __restrict__ goal,
+                                                int goal_per_cand, int S, const float* __restrict__ weights,
+                                                int n_cand, int D, float* __restrict__ dY) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_cand * D) return;
+  const int cand = i / D, c = i % D;
+  const float g = goal[(size_t)(goal_per_cand ? cand : cand / S) * D + c];
+  dY[i] = 2.0f * (y[i] - g) * (weights ? weights[cand] : 1.0f);
+}
+
+// Final LayerNorm (affine, eps 1e-5) of each candidate's last window row: dX[last row] =
+// LN backward of dy (row stride dy_ld); the other rows of dX stay as they are (zero).
+__global__ void __launch_bounds__(256) k_final_ln_bwd32(const float* __restrict__ X, int n_cand, int w, int D,
+                                                        const float* __restrict__ g, const float* __restrict__ dy,
+                                                        int dy_ld, float* __restrict__ dX) {
+  const int cand = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (cand >= n_cand) return;
+  const size_t row = (size_t)cand * w + w - 1;
+  const float* x = X + row * D;
+  const float2 mv = warp_moments(x, D);
+  const float rstd = 1.0f / sqrtf(mv.y + 1e-5f);
+  const float* d = dy + (size_t)cand * dy_ld;
+  float sa = 0.f, sb = 0.f;
+  for (int c = lane; c < D; c += 32) {
+    const float dh = d[c] * g[c], xh = (x[c] - mv.x) * rstd;
+    sa += dh;
+    sb += dh * xh;
+  }
+  sa = warp_sum(sa) / D;
+  sb = warp_sum(sb) / D;
+  for (int c = lane; c < D; c += 32) {
+    const float dh = d[c] * g[c], xh = (x[c] - mv.x) * rstd;
+    dX[row * D + c] = rstd * (dh - sa - xh * sb);
+  }
+}
+
+// Gated residual x += gate . F: dF = dX . gate and dmod[token][gate] += dX . F. A call's rows
+// hold distinct tokens, so no two threads of a launch touch one dmod element.
+__global__ void k_gate_bwd32(const float* __restrict__ dX, const float* __restrict__ F, const int* __restrict__ row_tok,
+                             const float* __restrict__ mod, float* __restrict__ dmod, int mod_ld, int gate_off,
+                             int rows, int D, float* __restrict__ dF) {
+  const size_t n = (size_t)rows * D;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / D), c = (int)(i % D);
+    const size_t mi = (size_t)row_tok[r] * mod_ld + gate_off + c;
+    const float dx = dX[i];
+    dF[i] = dx * mod[mi];
+    dmod[mi] += dx * F[i];
+  }
+}
+
+// Reverse of a = LN_{g,b}(LN(x) (1 + scale) + shift) (k_ln_mod32): from dA, recompute u = LN(x)
+// and h, then dmod[shift] += dh, dmod[scale] += dh . u and dX += LN backward of dh . (1 + scale).
+// One warp per row, NV = D / 32 values per lane.
+template <int NV>
+__global__ void __launch_bounds__(256) k_ln_mod_bwd32(const float* __restrict__ X, const float* __restrict__ dA,
+                                                      int rows, const int* __restrict__ row_tok,
+                                                      const float* __restrict__ mod, float* __restrict__ dmod,
+                                                      int mod_ld, int shift_off, int scale_off,
+                                                      const float* __restrict__ g, float* __restrict__ dX) {
+  constexpr int D = NV * 32;
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const float* x = X + (size_t)r * D;
+  const size_t mrow = (size_t)row_tok[r] * mod_ld;
+  const float2 mv = warp_moments(x, D);
+  const float rstd1 = 1.0f / sqrtf(mv.y + 1e-6f);
+  float u[NV], h[NV], sc[NV];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + 32 * i;
+    u[i] = (x[c] - mv.x) * rstd1;
+    sc[i] = mod[mrow + scale_off + c];
+    h[i] = u[i] * (1.0f + sc[i]) + mod[mrow + shift_off + c];
+    s += h[i];
+  }
+  const float mean2 = warp_sum(s) / D;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) q += (h[i] - mean2) * (h[i] - mean2);
+  const float rstd2 = 1.0f / sqrtf(warp_sum(q) / D + 1e-5f);
+  float sa = 0.f, sb = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + 32 * i;
+    const float ah = (h[i] - mean2) * rstd2, dah = dA[(size_t)r * D + c] * g[c];
+    h[i] = ah;  // h now holds the normalised h
+    sa += dah;
+    sb += dah * ah;
+  }
+  sa = warp_sum(sa) / D;
+  sb = warp_sum(sb) / D;
+  float ta = 0.f, tb = 0.f;
+  float du[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + 32 * i;
+    const float dah = dA[(size_t)r * D + c] * g[c];
+    const float dh = rstd2 * (dah - sa - h[i] * sb);
+    dmod[mrow + shift_off + c] += dh;
+    dmod[mrow + scale_off + c] += dh * u[i];
+    du[i] = dh * (1.0f + sc[i]);
+    ta += du[i];
+    tb += du[i] * u[i];
+  }
+  ta = warp_sum(ta) / D;
+  tb = warp_sum(tb) / D;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + 32 * i;
+    dX[(size_t)r * D + c] += rstd1 * (du[i] - ta - u[i] * tb);
+  }
+}
+
+// Reverse of the causal window attention (k_attn32): one warp per (candidate, head) walks
+// the candidate's w rows, recomputes each row's softmax P and accumulates
+// dq = 1/8 sum_j dS_j k_j, dk_j += 1/8 dS_j q, dv_j += P_j dO with dS_j = P_j (dP_j - sum P dP).
+__global__ void __launch_bounds__(256) k_attn_bwd32(const float* __restrict__ qkv, const float* __restrict__ dO,
+                                                    int n_cand, int w, int heads, float* __restrict__ dQKV) {
+  const int item = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (item >= n_cand * heads) return;
+  const int cand = item / heads, hd = item % heads, inner = heads * 64, ld = 3 * inner;
+  const size_t base = (size_t)cand * w;
+  float dk0[8], dk1[8], dv0[8], dv1[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) dk0[j] = dk1[j] = dv0[j] = dv1[j] = 0.f;
+  for (int p = 0; p < w; ++p) {
+    const float* q = qkv + (base + p) * ld + hd * 64;
+    const float q0 = q[lane], q1 = q[32 + lane];
+    float P[8], dP[8];
+    float mx = -INFINITY;
+    for (int j = 0; j <= p; ++j) {
+      const float* k = qkv + (base + j) * ld + inner + hd * 64;
+      P[j] = warp_sum(q0 * k[lane] + q1 * k[32 + lane]) * 0.125f;
+      mx = fmaxf(mx, P[j]);
+    }
+    float den = 0.f;
+    for (int j = 0; j <= p; ++j) {
+      P[j] = expf(P[j] - mx);
+      den += P[j];
+    }
+    const float* o = dO + (base + p) * inner + hd * 64;
+    const float o0 = o[lane], o1 = o[32 + lane];
+    float spd = 0.f;
+    for (int j = 0; j <= p; ++j) {
+      P[j] /= den;
+      const float* v = qkv + (base + j) * ld + 2 * inner + hd * 64;
+      dP[j] = warp_sum(o0 * v[lane] + o1 * v[32 + lane]);
+      spd += P[j] * dP[j];
+    }
+    float dq0 = 0.f, dq1 = 0.f;
+    for (int j = 0; j <= p; ++j) {
+      const float* k = qkv + (base + j) * ld + inner + hd * 64;
+      const float ds = P[j] * (dP[j] - spd) * 0.125f;
+      dq0 = fmaf(ds, k[lane], dq0);
+      dq1 = fmaf(ds, k[32 + lane], dq1);
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj)
+        if (jj == j) {  // register-resident accumulators: static indices only
+          dk0[jj] = fmaf(ds, q0, dk0[jj]);
+          dk1[jj] = fmaf(ds, q1, dk1[jj]);
+          dv0[jj] = fmaf(P[j], o0, dv0[jj]);
+          dv1[jj] = fmaf(P[j], o1, dv1[jj]);
+        }
+    }
+    float* dq = dQKV + (base + p) * ld + hd * 64;
+    dq[lane] = dq0;
+    dq[32 + lane] = dq1;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (j < w) {
+      float* d = dQKV + (base + j) * ld + hd * 64;
+      d[inner + lane] = dk0[j];
+      d[inner + 32 + lane] = dk1[j];
+      d[2 * inner + lane] = dv0[j];
+      d[2 * inner + 32 + lane] = dv1[j];
+    }
+}
+
+// Layer-0 rows were history + position: rows holding an earlier prediction (history index
+// j >= H) pass their gradient to that prediction, dpred[cand][j - H] += dX[row].
+__global__ void k_hist_bwd32(const float* __restrict__ dX, int n_cand, int w, int start, int H, int npred, int D,
+                             float* __restrict__ dpred) {
+  const int r = blockIdx.x;
+  if (r >= n_cand * w) return;
+  const int cand = r / w, j = start + r % w;
+  if (j < H) return;
+  float* dst = dpred + ((size_t)cand * npred + (j - H)) * D;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) dst[c] += dX[(size_t)r * D + c];
+}
+
+cudaError_t ln_mod_bwd(int D, const float* X, const float* dA, int rows, const int* row_tok, const float* mod,
+                       float* dmod, int mod_ld, int shift_off, int scale_off, const float* g, float* dX,
+                       cudaStream_t st) {
+  const int blocks = (rows + 7) / 8;
+  if (D == 192)
+    k_ln_mod_bwd32<6><<<blocks, 256, 0, st>>>(X, dA, rows, row_tok, mod, dmod, mod_ld, shift_off, scale_off, g, dX);
+  else if (D == 384)
+    k_ln_mod_bwd32<12><<<blocks, 256, 0, st>>>(X, dA, rows, row_tok, mod, dmod, mod_ld, shift_off, scale_off, g, dX);
+  else
+    return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+int ew_blocks(size_t n) { return (int)std::min<size_t>((n + 255) / 256, 148 * 16); }
+
+}  // namespace
+
+cudaError_t run_model_cost_grad_fp32(const ModelDims& m, const F32Weights& w, const F32Work& ws, const F32Tape& tape,
+                                     const F32GradWork& gw, const float* emb, int emb_pc, int H, const float* goal,
+                                     int goal_pc, const float* cand, int B, int S, int T, int HS,
+                                     const float* cost_weights, float* costs, float* grad, cudaStream_t st) {
+  if (m.pp_hidden) return cudaErrorInvalidValue;  // the reverse pass covers an Identity pred_proj
+  const int NC = B * S, NT = NC * T, D = m.D, L = m.L, inner = m.inner, mlp = m.mlp;
+  const int mod_ld = L * 6 * D, n_calls = T - H + 1;
+  F32_TRY(run_model_cost_fp32(m, w, ws, emb, emb_pc, H, goal, goal_pc, cand, B, S, T, HS, costs, st, &tape));
+  F32_TRY(cudaMemsetAsync(gw.dmod, 0, (size_t)NT * mod_ld * 4, st));
+  F32_TRY(cudaMemsetAsync(gw.dpred, 0, (size_t)NC * n_calls * D * 4, st));
+  k_seed32<<<(NC * D + 255) / 256, 256, 0, st>>>(tape.y, goal, goal_pc, S, cost_weights, NC, D, gw.dY);
+  F32_TRY(cudaGetLastError());
+  for (int k = n_calls - 1; k >= 0; --k) {  // calls in reverse: later windows read earlier predictions
+    const F32TapeCall& tc = tape.calls[k];
+    const int R = tc.rows;
+    const size_t RD = (size_t)R * D;
+    F32_TRY(cudaMemsetAsync(gw.dX, 0, RD * 4, st));
+    const bool last = k == n_calls - 1;
+    k_final_ln_bwd32<<<(NC + 7) / 8, 256, 0, st>>>(tc.x_out, NC, tc.w, D, w.fin_w, last ? gw.dY : gw.dpred + (size_t)k * D,
+                                                   last ? D : n_calls * D, gw.dX);
+    F32_TRY(cudaGetLastError());
+    for (int l = L - 1; l >= 0; --l) {
+      const F32Layer& lw = w.layers[l];
+      const int mo = l * 6 * D;
+      // x += gate_mlp . FFN(a2): FFN(a2) = GELU(a2 W1^T + b1) W2^T + b2
+      k_gate_bwd32<<<ew_blocks(RD), 256, 0, st>>>(gw.dX, tc.f2 + l * RD, tc.row_tok, ws.mod, gw.dmod, mod_ld,
+                                                  mo + 5 * D, R, D, gw.dF);
+      F32_TRY(cudaGetLastError());
+      F32_TRY(sgemm_nn<NE_GELU_BWD>(gw.dF, D, lw.w2, D, mlp, gw.dF1, mlp, R, st, tc.f1 + (size_t)l * R * mlp, mlp));
+      F32_TRY(sgemm_nn<NE_STORE>(gw.dF1, mlp, lw.w1, mlp, D, gw.dA, D, R, st));
+      F32_TRY(ln_mod_bwd(D, tc.x_mid + l * RD, gw.dA, R, tc.row_tok, ws.mod, gw.dmod, mod_ld, mo + 3 * D, mo + 4 * D,
+                         lw.ffn_ln_w, gw.dX, st));
+      // x += gate_msa . (attention(a) W_out^T + b_out), attention over q | k | v = a W_qkv^T
+      k_gate_bwd32<<<ew_blocks(RD), 256, 0, st>>>(gw.dX, tc.o + l * RD, tc.row_tok, ws.mod, gw.dmod, mod_ld,
+                                                  mo + 2 * D, R, D, gw.dF);
+      F32_TRY(cudaGetLastError());
+      F32_TRY(sgemm_nn<NE_STORE>(gw.dF, D, lw.out_w, D, inner, gw.dAtt, inner, R, st));
+      k_attn_bwd32<<<(NC * m.heads + 7) / 8, 256, 0, st>>>(tc.qkv + (size_t)l * R * 3 * inner, gw.dAtt, NC, tc.w,
+                                                            m.heads, gw.dQKV);
+      F32_TRY(cudaGetLastError());
+      F32_TRY(sgemm_nn<NE_STORE>(gw.dQKV, 3 * inner, lw.qkv_w, 3 * inner, D, gw.dA, D, R, st));
+      F32_TRY(ln_mod_bwd(D, tc.x_in + l * RD, gw.dA, R, tc.row_tok, ws.mod, gw.dmod, mod_ld, mo, mo + D,
+                         lw.attn_ln_w, gw.dX, st));
+    }
+    k_hist_bwd32<<<R, 64, 0, st>>>(gw.dX, NC, tc.w, tc.start, H, n_calls, D, gw.dpred);
+    F32_TRY(cudaGetLastError());
+  }
+  // mod = SiLU(e) W_ada^T + b_ada for every layer; e = SiLU(h1) W_e2^T + b_e2; h1 = a1 W_e1^T + b_e1;
+  // a1 = cand W_conv^T + b_conv (Embedder, lewm/module.py:205-214).
+  F32_TRY(sgemm_nn<NE_SILU_BWD>(gw.dmod, mod_ld, w.ada_stack, mod_ld, D, gw.de, D, NT, st, tape.e, D));
+  F32_TRY(sgemm_nn<NE_SILU_BWD>(gw.de, D, w.e2_w, D, m.eh, gw.dh1, m.eh, NT, st, tape.h1, m.eh));
+  F32_TRY(sgemm_nn<NE_STORE>(gw.dh1, m.eh, w.e1_w, m.eh, m.As, gw.da1, m.As, NT, st));
+  F32_TRY(sgemm_nn<NE_STORE>(gw.da1, m.As, w.conv_w, m.As, m.A, grad, m.A, NT, st));
+  return cudaSuccess;
+}
+
+namespace {
+// Tape and gradient buffers of one evaluation, in carve order (16-float aligned).
+size_t grad_walk(const ModelDims& m, int NC, int T, int H, int HS, float* base, F32Tape* tape, F32GradWork* gw) {
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    float* p = base ? base + off : nullptr;
+    off += (n + 15) / 16 * 16;
+    return p;
+  };
+  const size_t NT = (size_t)NC * T, D = m.D, I = m.inner, L = m.L, mlp = m.mlp;
+  const int n_calls = T - H + 1;
+  F32Tape t;
+  t.h1 = take(NT * m.eh);
+  t.e = take(NT * D);
+  t.y = take((size_t)NC * D);
+  t.calls.resize(n_calls);
+  size_t maxR = 1;
+  for (int k = 0; k < n_calls; ++k) {
+    F32TapeCall& c = t.calls[k];
+    const int end = H + k;
+    c.start = end > HS ? end - HS : 0;
+    c.w = end - c.start;
+    c.rows = NC * c.w;
+    const size_t R = c.rows;
+    maxR = std::max(maxR, R);
+    c.row_tok = reinterpret_cast<int*>(take(R));
+    c.x_in = take(L * R * D);
+    c.qkv = take(L * R * 3 * I);
+    c.o = take(L * R * D);
+    c.x_mid = take(L * R * D);
+    c.f1 = take(L * R * mlp);
+    c.f2 = take(L * R * D);
+    c.x_out = take(R * D);
+  }
+  F32GradWork g{};
+  g.dX = take(maxR * D);
+  g.dF = take(maxR * D);
+  g.dF1 = take(maxR * mlp);
+  g.dA = take(maxR * D);
+  g.dAtt = take(maxR * I);
+  g.dQKV = take(maxR * 3 * I);
+  g.dY = take((size_t)NC * D);
+  g.dpred = take((size_t)NC * n_calls * D);
+  g.dmod = take(NT * L * 6 * D);
+  g.de = take(NT * D);
+  g.dh1 = take(NT * m.eh);
+  g.da1 = take(NT * m.As);
+  if (tape) *tape = std::move(t);
+  if (gw) *gw = g;
+  return off;
+}
+}  // namespace
+
+size_t f32_grad_floats(const ModelDims& m, int NC, int T, int H, int HS) {
+  return grad_walk(m, NC, T, H, HS, nullptr, nullptr, nullptr);
+}
+
+void f32_grad_carve(const ModelDims& m, int NC, int T, int H, int HS, float* base, F32Tape* tape, F32GradWork* gw) {
+  grad_walk(m, NC, T, H, HS, base, tape, gw);
 }
 
 }  // namespace lewm

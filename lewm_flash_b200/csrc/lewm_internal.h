@@ -330,6 +330,7 @@ struct F32Weights {
   // shift = bias without a norm), second Linear.
   const float *pp_w1 = nullptr, *pp_b1 = nullptr, *pp_ln_g = nullptr, *pp_ln_b = nullptr;
   const float *pp_scale = nullptr, *pp_shift = nullptr, *pp_w2 = nullptr, *pp_b2 = nullptr;
+  const float* ada_stack = nullptr;  // [L * 6D][D]: every layer's adaLN Linear weight, stacked (reverse pass)
 };
 struct F32Work {
   float *act, *eh, *sact;  // [NC*T] x A' / eh / D: Embedder activations, sact = SiLU(action embedding)
@@ -344,9 +345,44 @@ struct F32Work {
 // Floats of F32Work for n_cand candidates, horizon T, window <= frames (pointers into one block).
 size_t f32_work_floats(const ModelDims& m, size_t n_cand, size_t T);
 F32Work f32_work_carve(const ModelDims& m, size_t n_cand, size_t T, float* base);
+// What the reverse pass of the fp32 model cost reads, recorded by the forward: per predictor
+// call (rows = candidates x window, row = candidate * w + position), per layer.
+struct F32TapeCall {
+  int rows = 0, w = 0, start = 0;
+  int* row_tok = nullptr;  // [rows] modulation row of each row
+  float* x_in = nullptr;   // [L][rows][D] residual entering the layer
+  float* qkv = nullptr;    // [L][rows][3 inner]
+  float* o = nullptr;      // [L][rows][D] out-projection output (with bias), before its gate
+  float* x_mid = nullptr;  // [L][rows][D] residual after the attention half
+  float* f1 = nullptr;     // [L][rows][mlp] FC1 output (with bias), before GELU
+  float* f2 = nullptr;     // [L][rows][D] FC2 output (with bias), before its gate
+  float* x_out = nullptr;  // [rows][D] residual after the last layer
+};
+struct F32Tape {
+  float* h1 = nullptr;  // [NC*T][eh] Embedder hidden layer before SiLU
+  float* e = nullptr;   // [NC*T][D] action embedding before SiLU
+  float* y = nullptr;   // [NC][D] final-LayerNorm output of the last call
+  std::vector<F32TapeCall> calls;
+};
+// Gradient buffers of the reverse pass (d = d loss / d ...).
+struct F32GradWork {
+  float *dX, *dF, *dF1, *dA, *dAtt, *dQKV;  // [NC*w] x D / D / mlp / D / inner / 3 inner
+  float *dY, *dpred;                        // [NC][D], [NC][T-H+1][D]
+  float *dmod, *de, *dh1, *da1;             // [NC*T] x L*6D / D / eh / A'
+};
+// Floats of the tape + gradient buffers of one evaluation; carve them from `base`.
+size_t f32_grad_floats(const ModelDims& m, int NC, int T, int H, int HS);
+void f32_grad_carve(const ModelDims& m, int NC, int T, int H, int HS, float* base, F32Tape* tape, F32GradWork* gw);
+// `tape` null: plain forward. Else the forward also records the tape (pred_proj Identity).
 cudaError_t run_model_cost_fp32(const ModelDims& m, const F32Weights& w, const F32Work& ws, const float* emb,
                                 int emb_pc, int H, const float* goal, int goal_pc, const float* cand, int B, int S,
-                                int T, int HS, float* costs, cudaStream_t st);
+                                int T, int HS, float* costs, cudaStream_t st, const F32Tape* tape = nullptr);
+// costs and grad (B,S,T,A) = cost_weight[c] * d cost[c] / d cand[c] (weights null: 1), float32 forward
+// and reverse over the recorded tape; pred_proj Identity.
+cudaError_t run_model_cost_grad_fp32(const ModelDims& m, const F32Weights& w, const F32Work& ws, const F32Tape& tape,
+                                     const F32GradWork& gw, const float* emb, int emb_pc, int H, const float* goal,
+                                     int goal_pc, const float* cand, int B, int S, int T, int HS,
+                                     const float* cost_weights, float* costs, float* grad, cudaStream_t st);
 
 // Sets the thread's error text that lewm_last_error(NULL) returns (context-free calls).
 void set_noctx_error(const char* msg);

@@ -184,6 +184,29 @@ class Runtime:
     def model_cost(self, emb: torch.Tensor, goal_emb: torch.Tensor, candidates: torch.Tensor,
                    history_size: int = 3) -> torch.Tensor:
         """``JEPA.get_cost_from_embeddings`` semantics (reference ``lewm/jepa.py:302-317``)."""
+        args = self._cost_args(emb, goal_emb, candidates)
+        out = torch.empty(args["B"], args["S"], device=self.device, dtype=torch.float32)
+        self._check(_lib.lib().lewm_model_cost(self._h, _ptr(args["e"]), args["emb_ps"], args["H"], _ptr(args["g"]),
+                                               args["goal_ps"], _ptr(args["cand"]), args["B"], args["S"], args["T"],
+                                               int(history_size), _ptr(out), self._stream()))
+        return out
+
+    def model_cost_grad(self, emb: torch.Tensor, goal_emb: torch.Tensor, candidates: torch.Tensor,
+                        history_size: int = 3, cost_weights: Optional[torch.Tensor] = None):
+        """Costs (B,S) and d(sum_c w_c cost_c) / d candidates (B,S,T,A), float32 forward and
+        reverse pass (``lewm_model_cost_grad``): the gradient CEM-GD steps on
+        (reference ``lewm/solvers/cem_gd.py:459-606``). ``cost_weights`` (B,S), default ones."""
+        args = self._cost_args(emb, goal_emb, candidates)
+        B, S = args["B"], args["S"]
+        out = torch.empty(B, S, device=self.device, dtype=torch.float32)
+        grad = torch.empty_like(args["cand"])
+        w = None if cost_weights is None else _f32(cost_weights.expand(B, S), self.device)
+        self._check(_lib.lib().lewm_model_cost_grad(
+            self._h, _ptr(args["e"]), args["emb_ps"], args["H"], _ptr(args["g"]), args["goal_ps"], _ptr(args["cand"]),
+            B, S, args["T"], int(history_size), _ptr(w), _ptr(out), _ptr(grad), self._stream()))
+        return out, grad
+
+    def _cost_args(self, emb: torch.Tensor, goal_emb: torch.Tensor, candidates: torch.Tensor) -> dict:
         dev = self.device
         cand = _f32(candidates, dev)
         if cand.ndim != 4:
@@ -212,10 +235,7 @@ class Runtime:
             g, goal_ps = _f32(g.expand(B, S, g.shape[-1]), dev), 1
         else:
             raise ValueError(f"goal_emb must be rank 3 or 4, got {tuple(goal_emb.shape)}")
-        out = torch.empty(B, S, device=dev, dtype=torch.float32)
-        self._check(_lib.lib().lewm_model_cost(self._h, _ptr(e), emb_ps, H, _ptr(g), goal_ps, _ptr(cand), B, S, T,
-                                               int(history_size), _ptr(out), self._stream()))
-        return out
+        return {"e": e, "emb_ps": emb_ps, "H": H, "g": g, "goal_ps": goal_ps, "cand": cand, "B": B, "S": S, "T": T}
 
     # ------------------------------------------------------------------ full plan
     def _check_plan_tensors(self, e: torch.Tensor, g: torch.Tensor, m: torch.Tensor, s: torch.Tensor) -> None:

@@ -492,8 +492,34 @@ def run_static_icem_chain(model, emb: torch.Tensor, goal_emb: torch.Tensor, mean
     return actions, std, fcost
 
 
+class _ModelCostWithGrad(torch.autograd.Function):
+    """Model costs whose gradient with respect to the action candidates is the device's float32
+    reverse pass (``lewm_model_cost_grad``). Candidates are independent, so the pass computes
+    every candidate's d cost_c / d cand_c once in the forward and the backward only scales it
+    by the incoming d loss / d cost_c."""
+
+    @staticmethod
+    def forward(ctx, candidates, rt, emb, goal_emb, history_size):
+        costs, grad = rt.model_cost_grad(emb, goal_emb, candidates, history_size=history_size)
+        ctx.save_for_backward(grad)
+        ctx.cand_meta = (candidates.dtype, candidates.device)
+        return costs
+
+    @staticmethod
+    def backward(ctx, grad_costs):
+        (grad,) = ctx.saved_tensors
+        dtype, device = ctx.cand_meta
+        g = grad * grad_costs.to(grad.dtype)[..., None, None]
+        return g.to(device=device, dtype=dtype), None, None, None, None
+
+
 class B200ModelCost:
-    """``JEPA.get_cost_from_embeddings`` on the B200 kernels (reference ``lewm/jepa.py:302-317``)."""
+    """``JEPA.get_cost_from_embeddings`` on the B200 kernels (reference ``lewm/jepa.py:302-317``).
+
+    Differentiable with respect to ``action_candidates``: under grad mode with candidates that
+    require grad (CEM-GD's refinement, ``lewm/solvers/cem_gd.py:459-606``) the costs come from
+    the float32 forward that records the reverse pass, and ``backward`` returns the device
+    gradient. The embeddings and goal are constants there (they come from the frozen encoder)."""
 
     def __init__(self, model, device="cuda"):
         self.model = model
@@ -505,7 +531,13 @@ class B200ModelCost:
 
     def get_cost_from_embeddings(self, emb: torch.Tensor, goal_emb: torch.Tensor, action_candidates: torch.Tensor,
                                  history_size: int = 3) -> torch.Tensor:
-        return self.runtime.model_cost(emb, goal_emb, action_candidates, history_size=history_size)
+        rt = self.runtime
+        if torch.is_grad_enabled() and action_candidates.requires_grad:
+            if emb.requires_grad or goal_emb.requires_grad:
+                raise NotImplementedError("the B200 model cost differentiates with respect to the action candidates "
+                                          "only; detach emb / goal_emb")
+            return _ModelCostWithGrad.apply(action_candidates, rt, emb.detach(), goal_emb.detach(), int(history_size))
+        return rt.model_cost(emb, goal_emb, action_candidates, history_size=history_size)
 
     __call__ = get_cost_from_embeddings
 

@@ -10,10 +10,12 @@ import pytest
 from lewm_flash_b200.model import synthetic_state_dict
 from oracle import cost_grad_oracle as cg
 from tests.conftest import GOLDEN
-from tests.golden.make_cost_grad_golden import CASES, DESC, WEIGHT_SEED, case_inputs
+from tests.golden.make_cost_grad_golden import (CASES, DESC, FULL_CASES, FULL_DESC, FULL_WEIGHT_SEED, WEIGHT_SEED,
+                                                case_inputs)
 
 FIX = np.load(GOLDEN / "cost_grad.npz")
 SD = synthetic_state_dict(DESC, WEIGHT_SEED)
+FULL_FIX = np.load(GOLDEN / "cost_grad_full.npz")
 
 
 @pytest.mark.parametrize("name", sorted(CASES))
@@ -23,6 +25,17 @@ def test_cost_gradient_matches_reference_autograd(name):
     np.testing.assert_allclose(cost, FIX[f"{name}__cost"], rtol=2e-6)
     want = FIX[f"{name}__grad"]
     # float32 autograd against float64: within 1e-4 of the largest gradient entry
+    assert np.abs(grad - want).max() <= 1e-4 * np.abs(want).max()
+
+
+@pytest.mark.parametrize("name", sorted(FULL_CASES))
+def test_cost_gradient_matches_reference_autograd_full_width(name):
+    """The width-192 / 6-layer predictor the device runs (the fixture its reverse pass is held to)."""
+    sd = synthetic_state_dict(FULL_DESC, FULL_WEIGHT_SEED)
+    emb, goal, cand = case_inputs(*FULL_CASES[name], desc=FULL_DESC)
+    cost, grad = cg.cost_and_grad(emb, goal, cand, sd, FULL_DESC)
+    np.testing.assert_allclose(cost, FULL_FIX[f"{name}__cost"], rtol=2e-6)
+    want = FULL_FIX[f"{name}__grad"]
     assert np.abs(grad - want).max() <= 1e-4 * np.abs(want).max()
 
 
