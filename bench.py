@@ -386,10 +386,12 @@ def reference_arm(args, rank, world):
     return 0
 
 
-def model_cost_case(S, repeat, envs=1):
+def model_cost_case(S, repeat, envs=1, mode="bf16"):
     """R predictor rollouts of S candidates per env: 1 env with history 1 (5 calls x 6 layers,
     windows 1, 2, 3, 3, 3), or B envs with history 3 (3 calls x 6 layers, windows 3, 3, 3).
-    A fixed launch sequence for ncu captures of one kernel at a known geometry."""
+    A fixed launch sequence for ncu captures of one kernel at a known geometry. mode "bf16"
+    (tensor cores), "fp32" (model_cost_autocast "none") or "grad" (the float32 forward and
+    reverse pass, lewm_model_cost_grad)."""
     import torch
 
     from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
@@ -397,7 +399,7 @@ def model_cost_case(S, repeat, envs=1):
 
     dev = torch.device("cuda", 0)
     desc = ModelDesc()
-    rt = Runtime(desc, synthetic_state_dict(desc, 0), dev)
+    rt = Runtime(desc, synthetic_state_dict(desc, 0), dev, model_cost_autocast="none" if mode == "fp32" else "bf16")
     rng = np.random.default_rng(7)
     hist = 1 if envs == 1 else 3
     emb = torch.as_tensor(rng.standard_normal((envs, hist, desc.dim)), dtype=torch.float32, device=dev)
@@ -408,12 +410,13 @@ def model_cost_case(S, repeat, envs=1):
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record()
-        costs = rt.model_cost(emb, goal, cand)
+        costs = rt.model_cost_grad(emb, goal, cand)[0] if mode == "grad" else rt.model_cost(emb, goal, cand)
         b.record()
         torch.cuda.synchronize(dev)
         ms.append(a.elapsed_time(b))
     rt.sync()
-    print(json.dumps({"case": "model_cost", "envs": envs, "samples": S, "ms": ms, "cost0": float(costs[0, 0])}))
+    print(json.dumps({"case": "model_cost", "mode": mode, "envs": envs, "samples": S, "ms": ms,
+                      "cost0": float(costs[0, 0])}))
     return 0
 
 
@@ -473,7 +476,7 @@ def main() -> int:
     ap.add_argument("--no-reference-gpu", action="store_true", help="skip the reference PyTorch GPU comparator")
     ap.add_argument("--no-sharded", action="store_true", help="skip the 1024-env sharded leg")
     ap.add_argument("--no-stress", action="store_true", help="skip the width-384 stress leg")
-    ap.add_argument("--no-fp32", action="store_true", help="skip the float32 CEM leg")
+    ap.add_argument("--no-fp32", action="store_true", help="skip the float32 CEM and CEM-GD gradient legs")
     ap.add_argument("--model-cost", type=int, default=0, metavar="S",
                     help="profiling case: time R model-cost calls of S candidates per env (horizon 5; 1 env "
                          "with history 1, or --envs B with history 3) and exit; no bench line")
@@ -481,10 +484,12 @@ def main() -> int:
                     help="profiling case: run the observation encoder R times on N 224 px images and exit; "
                          "no bench line")
     ap.add_argument("--envs", type=int, default=1)
+    ap.add_argument("--mode", default="bf16", choices=["bf16", "fp32", "grad"],
+                    help="--model-cost arithmetic: bf16, fp32 or the float32 gradient")
     ap.add_argument("--repeat", type=int, default=3)
     args = ap.parse_args()
     if args.model_cost:
-        return model_cost_case(args.model_cost, args.repeat, args.envs)
+        return model_cost_case(args.model_cost, args.repeat, args.envs, args.mode)
     if args.encoder:
         return encoder_case(args.encoder, args.repeat)
 
@@ -597,6 +602,7 @@ def main() -> int:
     # ---------------------------------------------------------------- batched planning (64 envs, history 3)
     batched = batched_pass(rt, dev, args.steps, args.warmup, flush)
     fp32_cem = fp32_cem_pass(dev, args.steps, args.warmup, flush) if not args.no_fp32 else None
+    cem_gd = cem_gd_pass(rt, dev) if world == 1 and not args.no_fp32 else None
 
     # ---------------------------------------------------------------- 1024 envs split over the ranks
     sharded = sharded_pass(rt, dev, rank, world, barrier, dist, flush) if not args.no_sharded else None
@@ -629,6 +635,7 @@ def main() -> int:
         "kernel_classes": kinfo["classes"],
         "batched": batched,
         "fp32_cem": fp32_cem,
+        "cem_gd": cem_gd,
         "sharded": sharded,
         "stress": stress,
         "encoder": encoder,
@@ -829,6 +836,65 @@ def fp32_cem_pass(dev, steps, warmup, flush, n_envs=1):
             "flops_per_plan": flops,
             "note": "float32 CUDA-core model cost (no tensor cores); canonical FLOPs (window rows the "
                     "bf16 path computes), the fp32 path recomputes full windows (~1.3x)"}
+
+
+def cem_gd_pass(rt, dev, n_seeds=30, repeat=20):
+    """The gradient CEM-GD's refinement steps on (reference lewm/solvers/cem_gd.py:459-606): costs
+    and d cost / d actions of 30 seed candidates (1 env, history 1, horizon 5) in float32. The
+    device's forward + reverse pass (lewm_model_cost_grad) against the reference model's own
+    torch autograd of get_cost_from_embeddings (baseline/_ref, float32, matmul precision
+    "highest") on the same GPU and inputs; CUDA events, p50."""
+    import torch
+
+    g = np.random.default_rng(11)
+    emb = torch.as_tensor(g.standard_normal((1, 1, 192)), dtype=torch.float32, device=dev)
+    goal = torch.as_tensor(g.standard_normal((1, 1, 192)), dtype=torch.float32, device=dev)
+    cand = torch.as_tensor(g.standard_normal((1, n_seeds, 5, 10)), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, n):
+        ms = []
+        for _ in range(n):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            ms.append(a.elapsed_time(b))
+        return ms
+
+    timed(lambda: rt.model_cost_grad(emb, goal, cand), 3)
+    dev_ms = percentile(timed(lambda: rt.model_cost_grad(emb, goal, cand), repeat), 50)
+    _, grad = rt.model_cost_grad(emb, goal, cand)
+    rt.sync()
+    out = {"workload": f"cost_grad_1env_{n_seeds}seeds_h1_fp32", "device_p50_ms": dev_ms, "repeat": repeat}
+    ref = reference_package()
+    if ref is None:
+        out["reference"] = "unavailable: reference not installed in baseline/_ref"
+        return out
+    prev = torch.get_float32_matmul_precision()
+    torch.set_float32_matmul_precision("highest")
+    try:
+        model, _ = reference_solver(ref, dev)
+        model.requires_grad_(False)
+        box = {}
+
+        def ref_step():
+            c = cand.clone().requires_grad_(True)
+            model.get_cost_from_embeddings(emb, goal, c).sum().backward()
+            box["grad"] = c.grad
+
+        timed(ref_step, 3)
+        ref_ms = percentile(timed(ref_step, repeat), 50)
+        err = float((grad - box["grad"]).abs().max() / box["grad"].abs().max())
+        out.update({"reference_autograd_p50_ms": ref_ms, "speedup_vs_reference_autograd": ref_ms / dev_ms,
+                    "max_grad_diff_of_max": err,
+                    "reference": "JEPA.get_cost_from_embeddings + backward, eager torch, float32 (baseline/_ref)"})
+        del model
+    finally:
+        torch.set_float32_matmul_precision(prev)
+    return out
 
 
 def encoder_pass(dev, steps, warmup, flush, n_img=64):

@@ -18,6 +18,11 @@ namespace lewm {
 namespace {
 
 constexpr int GB_M = 64, GB_N = 64, GB_K = 32, G_THREADS = 256;
+// K chunks of the gated-residual GEMMs (out-projection K = inner, FC2 K = mlp; N = D): their
+// grids are N / 64 x rows / 64 CTAs, a few dozen at the planner's sizes, each walking K in
+// dependent slabs. Always 4 chunks, whatever the batch, so a row's sum order (and bits) do
+// not depend on the rows around it.
+constexpr int kSplitK = 4;
 
 enum GemmEpi { GE_BIAS = 0, GE_SILU = 1, GE_GELU = 2, GE_RESID = 3 };
 
@@ -39,11 +44,13 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
                                                      int K, const float* __restrict__ bias, float* __restrict__ C, int ldc,
                                                      int M, int N, const float* __restrict__ mod,
                                                      const int* __restrict__ row_tok, int mod_ld, int gate_off,
-                                                     float* __restrict__ save) {
+                                                     float* __restrict__ save, int kc, float* __restrict__ part) {
   __shared__ __align__(16) float sA[GB_K][GB_M + 4];
   __shared__ __align__(16) float sW[GB_K][GB_N + 4];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int m0 = blockIdx.y * GB_M, n0 = blockIdx.x * GB_N;
+  // K range of this CTA: all of K, or chunk blockIdx.z of kc (a multiple of GB_K) when split.
+  const int kbeg = blockIdx.z * kc, kend = min(K, kbeg + kc);
   // Per slab each thread moves 8 A values and 8 W values: VEC as 2 float4 (row s / 8,
   // k 4 (s % 8)), scalar as 8 floats (row s / 32, k s % 32), s = tid + 256 q.
   float ra[8], rw[8];
@@ -54,8 +61,8 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
         const int sl = tid + q * G_THREADS, r = sl >> 3, k = k0 + (sl & 7) * 4;
         const int m = m0 + r, n = n0 + r;
         float4 a = make_float4(0.f, 0.f, 0.f, 0.f), w = a;
-        if (m < M && k < K) a = *reinterpret_cast<const float4*>(A + (size_t)m * lda + k);
-        if (n < N && k < K) w = *reinterpret_cast<const float4*>(W + (size_t)n * K + k);
+        if (m < M && k < kend) a = *reinterpret_cast<const float4*>(A + (size_t)m * lda + k);
+        if (n < N && k < kend) w = *reinterpret_cast<const float4*>(W + (size_t)n * K + k);
         ra[4 * q] = a.x, ra[4 * q + 1] = a.y, ra[4 * q + 2] = a.z, ra[4 * q + 3] = a.w;
         rw[4 * q] = w.x, rw[4 * q + 1] = w.y, rw[4 * q + 2] = w.z, rw[4 * q + 3] = w.w;
       }
@@ -64,8 +71,8 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
       for (int q = 0; q < 8; ++q) {
         const int sl = tid + q * G_THREADS, r = sl >> 5, k = k0 + (sl & 31);
         const int m = m0 + r, n = n0 + r;
-        ra[q] = (m < M && k < K) ? A[(size_t)m * lda + k] : 0.f;
-        rw[q] = (n < N && k < K) ? W[(size_t)n * K + k] : 0.f;
+        ra[q] = (m < M && k < kend) ? A[(size_t)m * lda + k] : 0.f;
+        rw[q] = (n < N && k < kend) ? W[(size_t)n * K + k] : 0.f;
       }
     }
   };
@@ -90,11 +97,11 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
     }
   };
   float acc[4][4] = {};
-  load(0);
+  load(kbeg);
   store();
   __syncthreads();
-  for (int k0 = 0; k0 < K; k0 += GB_K) {
-    const bool more = k0 + GB_K < K;
+  for (int k0 = kbeg; k0 < kend; k0 += GB_K) {
+    const bool more = k0 + GB_K < kend;
     if (more) load(k0 + GB_K);
 #pragma unroll
     for (int kk = 0; kk < GB_K; ++kk) {
@@ -120,6 +127,10 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
     for (int j = 0; j < 4; ++j) {
       const int n = n0 + tx * 4 + j;
       if (n >= N) continue;
+      if (part) {  // split K: this chunk's raw sum; k_splitk_resid32 applies the epilogue
+        part[((size_t)blockIdx.z * M + m) * N + n] = acc[i][j];
+        continue;
+      }
       const float v = acc[i][j] + (bias ? bias[n] : 0.f);
       if (save) save[(size_t)m * N + n] = v;  // pre-activation / branch output for the reverse pass
       if constexpr (EPI == GE_BIAS) C[(size_t)m * ldc + n] = v;
@@ -274,18 +285,44 @@ __global__ void __launch_bounds__(256) k_emit32(const float* __restrict__ y, int
   if (lane == 0) costs[cand] = acc;
 }
 
+// Split-K epilogue of the gated residual: v = bias + sum_z part[z] (z ascending), save = v,
+// X += gate . v (one thread per output).
+__global__ void k_splitk_resid32(const float* __restrict__ part, int splits, int M, int N,
+                                 const float* __restrict__ bias, float* __restrict__ X, int ldc,
+                                 const float* __restrict__ mod, const int* __restrict__ row_tok, int mod_ld,
+                                 int gate_off, float* __restrict__ save) {
+  const size_t n_out = (size_t)M * N;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_out; i += (size_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / N), n = (int)(i % N);
+    float v = part[i];
+    for (int z = 1; z < splits; ++z) v += part[z * n_out + i];
+    v += bias ? bias[n] : 0.f;
+    if (save) save[i] = v;
+    X[(size_t)m * ldc + n] += mod[(size_t)row_tok[m] * mod_ld + gate_off + n] * v;
+  }
+}
+
 template <int EPI>
 cudaError_t sgemm(const float* A, int lda, const float* W, int K, const float* bias, float* C, int ldc, int M, int N,
                   cudaStream_t st, const float* mod = nullptr, const int* row_tok = nullptr, int mod_ld = 0,
-                  int gate_off = 0, float* save = nullptr) {
-  const dim3 grid((N + GB_N - 1) / GB_N, (M + GB_M - 1) / GB_M);
+                  int gate_off = 0, float* save = nullptr, float* part = nullptr, int splits = 1) {
+  if (EPI != GE_RESID || !part) splits = 1;  // split K only where k_splitk_resid32 finishes the epilogue
+  const int kc = splits > 1 ? ((K + splits - 1) / splits + GB_K - 1) / GB_K * GB_K : K;
+  const int nz = (K + kc - 1) / kc;
+  const dim3 grid((N + GB_N - 1) / GB_N, (M + GB_M - 1) / GB_M, nz);
+  float* pp = nz > 1 ? part : nullptr;
   const bool vec = K % 4 == 0 && lda % 4 == 0 && (reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W)) % 16 == 0;
   if (vec)
     k_sgemm<EPI, true><<<grid, G_THREADS, 0, st>>>(A, lda, W, K, bias, C, ldc, M, N, mod, row_tok, mod_ld, gate_off,
-                                                   save);
+                                                   save, kc, pp);
   else
     k_sgemm<EPI, false><<<grid, G_THREADS, 0, st>>>(A, lda, W, K, bias, C, ldc, M, N, mod, row_tok, mod_ld, gate_off,
-                                                    save);
+                                                    save, kc, pp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || !pp) return e;
+  const size_t n_out = (size_t)M * N;
+  const int blocks = (int)std::min<size_t>((n_out + 255) / 256, 148 * 16);
+  k_splitk_resid32<<<blocks, 256, 0, st>>>(pp, nz, M, N, bias, C, ldc, mod, row_tok, mod_ld, gate_off, save);
   return cudaGetLastError();
 }
 
@@ -333,14 +370,14 @@ cudaError_t run_model_cost_fp32(const ModelDims& m, const F32Weights& w, const F
       F32_TRY(sgemm<GE_BIAS>(ws.a, D, lw.qkv_w, D, nullptr, qkv, 3 * inner, rows, 3 * inner, st));
       k_attn32<<<(rows * m.heads + 7) / 8, 256, 0, st>>>(qkv, rows, wlen, m.heads, ws.att);
       F32_TRY(sgemm<GE_RESID>(ws.att, inner, lw.out_w, inner, lw.out_b, ws.x, D, rows, D, st, ws.mod, row_tok, mod_ld,
-                              mo + 2 * D, tc ? tc->o + l * RD : nullptr));
+                              mo + 2 * D, tc ? tc->o + l * RD : nullptr, ws.part, kSplitK));
       if (tc) F32_TRY(cudaMemcpyAsync(tc->x_mid + l * RD, ws.x, RD * 4, cudaMemcpyDeviceToDevice, st));
       k_ln_mod32<<<lnb, 256, 0, st>>>(ws.x, rows, D, row_tok, ws.mod, mod_ld, mo + 3 * D, mo + 4 * D, lw.ffn_ln_w,
                                       lw.ffn_ln_b, ws.a);
       F32_TRY(sgemm<GE_GELU>(ws.a, D, lw.w1, D, lw.b1, ws.hid, m.mlp, rows, m.mlp, st, nullptr, nullptr, 0, 0,
                              tc ? tc->f1 + (size_t)l * rows * m.mlp : nullptr));
       F32_TRY(sgemm<GE_RESID>(ws.hid, m.mlp, lw.w2, m.mlp, lw.b2, ws.x, D, rows, D, st, ws.mod, row_tok, mod_ld,
-                              mo + 5 * D, tc ? tc->f2 + l * RD : nullptr));
+                              mo + 5 * D, tc ? tc->f2 + l * RD : nullptr, ws.part, kSplitK));
     }
     if (tc) F32_TRY(cudaMemcpyAsync(tc->x_out, ws.x, RD * 4, cudaMemcpyDeviceToDevice, st));
     k_final_ln32<<<(NC + 7) / 8, 256, 0, st>>>(ws.x, NC, wlen, D, w.fin_w, w.fin_b, ws.y);
@@ -396,11 +433,13 @@ __device__ __forceinline__ float silu_grad(float x) {
 template <int EPI, bool VEC>
 __global__ void __launch_bounds__(G_THREADS) k_sgemm_nn(const float* __restrict__ A, int lda, const float* __restrict__ Bm,
                                                         int Nin, int Kout, float* __restrict__ C, int ldc, int M,
-                                                        const float* __restrict__ pre, int ldp) {
+                                                        const float* __restrict__ pre, int ldp, int kc,
+                                                        float* __restrict__ part) {
   __shared__ __align__(16) float sA[GB_K][GB_M + 4];
   __shared__ __align__(16) float sB[GB_K][GB_N + 4];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int m0 = blockIdx.y * GB_M, c0 = blockIdx.x * GB_N;
+  const int nbeg = blockIdx.z * kc, nend = min(Nin, nbeg + kc);  // reduction chunk of this CTA
   float ra[8], rb[8];
   auto load = [&](int n0) {
     if constexpr (VEC) {
@@ -409,11 +448,11 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm_nn(const float* __restrict_
         const int sl = tid + q * G_THREADS;
         const int r = sl >> 3, n = n0 + (sl & 7) * 4, m = m0 + r;
         float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (m < M && n < Nin) a = *reinterpret_cast<const float4*>(A + (size_t)m * lda + n);
+        if (m < M && n < nend) a = *reinterpret_cast<const float4*>(A + (size_t)m * lda + n);
         ra[4 * q] = a.x, ra[4 * q + 1] = a.y, ra[4 * q + 2] = a.z, ra[4 * q + 3] = a.w;
         const int rr = sl >> 4, c = c0 + (sl & 15) * 4, nb = n0 + rr;
         float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (nb < Nin && c < Kout) b = *reinterpret_cast<const float4*>(Bm + (size_t)nb * Kout + c);
+        if (nb < nend && c < Kout) b = *reinterpret_cast<const float4*>(Bm + (size_t)nb * Kout + c);
         rb[4 * q] = b.x, rb[4 * q + 1] = b.y, rb[4 * q + 2] = b.z, rb[4 * q + 3] = b.w;
       }
     } else {
@@ -421,9 +460,9 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm_nn(const float* __restrict_
       for (int q = 0; q < 8; ++q) {
         const int sl = tid + q * G_THREADS;
         const int r = sl >> 5, n = n0 + (sl & 31), m = m0 + r;
-        ra[q] = (m < M && n < Nin) ? A[(size_t)m * lda + n] : 0.f;
+        ra[q] = (m < M && n < nend) ? A[(size_t)m * lda + n] : 0.f;
         const int rr = sl >> 6, c = c0 + (sl & 63), nb = n0 + rr;
-        rb[q] = (nb < Nin && c < Kout) ? Bm[(size_t)nb * Kout + c] : 0.f;
+        rb[q] = (nb < nend && c < Kout) ? Bm[(size_t)nb * Kout + c] : 0.f;
       }
     }
   };
@@ -449,11 +488,11 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm_nn(const float* __restrict_
     }
   };
   float acc[4][4] = {};
-  load(0);
+  load(nbeg);
   store();
   __syncthreads();
-  for (int n0 = 0; n0 < Nin; n0 += GB_K) {
-    const bool more = n0 + GB_K < Nin;
+  for (int n0 = nbeg; n0 < nend; n0 += GB_K) {
+    const bool more = n0 + GB_K < nend;
     if (more) load(n0 + GB_K);
 #pragma unroll
     for (int kk = 0; kk < GB_K; ++kk) {
@@ -479,6 +518,10 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm_nn(const float* __restrict_
     for (int j = 0; j < 4; ++j) {
       const int c = c0 + tx * 4 + j;
       if (c >= Kout) continue;
+      if (part) {  // split reduction: this chunk's raw sum; k_splitk_nn32 finishes
+        part[((size_t)blockIdx.z * M + m) * Kout + c] = acc[i][j];
+        continue;
+      }
       float v = acc[i][j];
       if constexpr (EPI == NE_GELU_BWD) v *= gelu_erf_grad(pre[(size_t)m * ldp + c]);
       if constexpr (EPI == NE_SILU_BWD) v *= silu_grad(pre[(size_t)m * ldp + c]);
@@ -487,16 +530,49 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm_nn(const float* __restrict_
   }
 }
 
+// Split-reduction epilogue of k_sgemm_nn: v = sum_z part[z] (z ascending), then the epilogue.
+template <int EPI>
+__global__ void k_splitk_nn32(const float* __restrict__ part, int splits, int M, int Kout, float* __restrict__ C,
+                              int ldc, const float* __restrict__ pre, int ldp) {
+  const size_t n_out = (size_t)M * Kout;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_out; i += (size_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / Kout), c = (int)(i % Kout);
+    float v = part[i];
+    for (int z = 1; z < splits; ++z) v += part[z * n_out + i];
+    if constexpr (EPI == NE_GELU_BWD) v *= gelu_erf_grad(pre[(size_t)m * ldp + c]);
+    if constexpr (EPI == NE_SILU_BWD) v *= silu_grad(pre[(size_t)m * ldp + c]);
+    C[(size_t)m * ldc + c] = v;
+  }
+}
+
+// Reduction chunks of dY . W as a function of the reduction length alone (one chunk per 256,
+// at most kMaxNnSplits), so a row's sum order does not depend on the batch: the long
+// reductions (3 inner, the stacked adaLN 6 D L, mlp) would otherwise walk 24-216 dependent
+// slabs in a few CTAs.
+constexpr int kMaxNnSplits = 16;
+int nn_splits(int Nin) { return std::max(1, std::min(kMaxNnSplits, Nin / 256)); }
+
 template <int EPI>
 cudaError_t sgemm_nn(const float* A, int lda, const float* Bm, int Nin, int Kout, float* C, int ldc, int M,
-                     cudaStream_t st, const float* pre = nullptr, int ldp = 0) {
-  const dim3 grid((Kout + GB_N - 1) / GB_N, (M + GB_M - 1) / GB_M);
+                     cudaStream_t st, const F32GradWork& gw, const float* pre = nullptr, int ldp = 0) {
+  const int splits = nn_splits(Nin);
+  const int kc = ((Nin + splits - 1) / splits + GB_K - 1) / GB_K * GB_K;
+  const int nz = (Nin + kc - 1) / kc;
+  // The partials must fit gw.part; the reductions it is sized for always do (output width D).
+  if (nz > 1 && (size_t)nz * M * Kout > gw.part_floats) return cudaErrorInvalidValue;
+  float* pp = nz > 1 ? gw.part : nullptr;
+  const dim3 grid((Kout + GB_N - 1) / GB_N, (M + GB_M - 1) / GB_M, nz);
   const bool vec = Nin % 4 == 0 && lda % 4 == 0 && Kout % 4 == 0 &&
                    (reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(Bm)) % 16 == 0;
   if (vec)
-    k_sgemm_nn<EPI, true><<<grid, G_THREADS, 0, st>>>(A, lda, Bm, Nin, Kout, C, ldc, M, pre, ldp);
+    k_sgemm_nn<EPI, true><<<grid, G_THREADS, 0, st>>>(A, lda, Bm, Nin, Kout, C, ldc, M, pre, ldp, kc, pp);
   else
-    k_sgemm_nn<EPI, false><<<grid, G_THREADS, 0, st>>>(A, lda, Bm, Nin, Kout, C, ldc, M, pre, ldp);
+    k_sgemm_nn<EPI, false><<<grid, G_THREADS, 0, st>>>(A, lda, Bm, Nin, Kout, C, ldc, M, pre, ldp, kc, pp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || !pp) return e;
+  const size_t n_out = (size_t)M * Kout;
+  const int blocks = (int)std::min<size_t>((n_out + 255) / 256, 148 * 16);
+  k_splitk_nn32<EPI><<<blocks, 256, 0, st>>>(pp, nz, M, Kout, C, ldc, pre, ldp);
   return cudaGetLastError();
 }
 
@@ -739,19 +815,20 @@ cudaError_t run_model_cost_grad_fp32(const ModelDims& m, const F32Weights& w, co
       k_gate_bwd32<<<ew_blocks(RD), 256, 0, st>>>(gw.dX, tc.f2 + l * RD, tc.row_tok, ws.mod, gw.dmod, mod_ld,
                                                   mo + 5 * D, R, D, gw.dF);
       F32_TRY(cudaGetLastError());
-      F32_TRY(sgemm_nn<NE_GELU_BWD>(gw.dF, D, lw.w2, D, mlp, gw.dF1, mlp, R, st, tc.f1 + (size_t)l * R * mlp, mlp));
-      F32_TRY(sgemm_nn<NE_STORE>(gw.dF1, mlp, lw.w1, mlp, D, gw.dA, D, R, st));
+      F32_TRY(sgemm_nn<NE_GELU_BWD>(gw.dF, D, lw.w2, D, mlp, gw.dF1, mlp, R, st, gw, tc.f1 + (size_t)l * R * mlp,
+                                    mlp));
+      F32_TRY(sgemm_nn<NE_STORE>(gw.dF1, mlp, lw.w1, mlp, D, gw.dA, D, R, st, gw));
       F32_TRY(ln_mod_bwd(D, tc.x_mid + l * RD, gw.dA, R, tc.row_tok, ws.mod, gw.dmod, mod_ld, mo + 3 * D, mo + 4 * D,
                          lw.ffn_ln_w, gw.dX, st));
       // x += gate_msa . (attention(a) W_out^T + b_out), attention over q | k | v = a W_qkv^T
       k_gate_bwd32<<<ew_blocks(RD), 256, 0, st>>>(gw.dX, tc.o + l * RD, tc.row_tok, ws.mod, gw.dmod, mod_ld,
                                                   mo + 2 * D, R, D, gw.dF);
       F32_TRY(cudaGetLastError());
-      F32_TRY(sgemm_nn<NE_STORE>(gw.dF, D, lw.out_w, D, inner, gw.dAtt, inner, R, st));
+      F32_TRY(sgemm_nn<NE_STORE>(gw.dF, D, lw.out_w, D, inner, gw.dAtt, inner, R, st, gw));
       k_attn_bwd32<<<(NC * m.heads + 7) / 8, 256, 0, st>>>(tc.qkv + (size_t)l * R * 3 * inner, gw.dAtt, NC, tc.w,
                                                             m.heads, gw.dQKV);
       F32_TRY(cudaGetLastError());
-      F32_TRY(sgemm_nn<NE_STORE>(gw.dQKV, 3 * inner, lw.qkv_w, 3 * inner, D, gw.dA, D, R, st));
+      F32_TRY(sgemm_nn<NE_STORE>(gw.dQKV, 3 * inner, lw.qkv_w, 3 * inner, D, gw.dA, D, R, st, gw));
       F32_TRY(ln_mod_bwd(D, tc.x_in + l * RD, gw.dA, R, tc.row_tok, ws.mod, gw.dmod, mod_ld, mo, mo + D,
                          lw.attn_ln_w, gw.dX, st));
     }
@@ -760,10 +837,10 @@ cudaError_t run_model_cost_grad_fp32(const ModelDims& m, const F32Weights& w, co
   }
   // mod = SiLU(e) W_ada^T + b_ada for every layer; e = SiLU(h1) W_e2^T + b_e2; h1 = a1 W_e1^T + b_e1;
   // a1 = cand W_conv^T + b_conv (Embedder, lewm/module.py:205-214).
-  F32_TRY(sgemm_nn<NE_SILU_BWD>(gw.dmod, mod_ld, w.ada_stack, mod_ld, D, gw.de, D, NT, st, tape.e, D));
-  F32_TRY(sgemm_nn<NE_SILU_BWD>(gw.de, D, w.e2_w, D, m.eh, gw.dh1, m.eh, NT, st, tape.h1, m.eh));
-  F32_TRY(sgemm_nn<NE_STORE>(gw.dh1, m.eh, w.e1_w, m.eh, m.As, gw.da1, m.As, NT, st));
-  F32_TRY(sgemm_nn<NE_STORE>(gw.da1, m.As, w.conv_w, m.As, m.A, grad, m.A, NT, st));
+  F32_TRY(sgemm_nn<NE_SILU_BWD>(gw.dmod, mod_ld, w.ada_stack, mod_ld, D, gw.de, D, NT, st, gw, tape.e, D));
+  F32_TRY(sgemm_nn<NE_SILU_BWD>(gw.de, D, w.e2_w, D, m.eh, gw.dh1, m.eh, NT, st, gw, tape.h1, m.eh));
+  F32_TRY(sgemm_nn<NE_STORE>(gw.dh1, m.eh, w.e1_w, m.eh, m.As, gw.da1, m.As, NT, st, gw));
+  F32_TRY(sgemm_nn<NE_STORE>(gw.da1, m.As, w.conv_w, m.As, m.A, grad, m.A, NT, st, gw));
   return cudaSuccess;
 }
 
@@ -814,6 +891,10 @@ size_t grad_walk(const ModelDims& m, int NC, int T, int H, int HS, float* base, 
   g.de = take(NT * D);
   g.dh1 = take(NT * m.eh);
   g.da1 = take(NT * m.As);
+  // split-reduction partials of dY . W: the split reductions (q|k|v, mlp, stacked adaLN, eh) all
+  // produce rows of width D or A' <= D
+  g.part_floats = (size_t)kMaxNnSplits * std::max(maxR, NT) * std::max<size_t>(D, m.As);
+  g.part = take(g.part_floats);
   if (tape) *tape = std::move(t);
   if (gw) *gw = g;
   return off;
@@ -851,6 +932,7 @@ void f32_layout(const ModelDims& m, size_t NC, size_t T, F&& f) {
   f(10, al(NC * T * m.D));
   f(11, al(NC * (size_t)m.pp_hidden));
   f(12, al(NW));  // row_tok (int32)
+  f(13, al((size_t)kSplitK * NW * m.D));  // split-K partial sums
 }
 }  // namespace
 
@@ -861,7 +943,7 @@ size_t f32_work_floats(const ModelDims& m, size_t n_cand, size_t T) {
 }
 
 F32Work f32_work_carve(const ModelDims& m, size_t n_cand, size_t T, float* base) {
-  float* p[13];
+  float* p[14];
   size_t off = 0;
   f32_layout(m, n_cand, T, [&](int i, size_t k) {
     p[i] = base + off;
@@ -881,6 +963,7 @@ F32Work f32_work_carve(const ModelDims& m, size_t n_cand, size_t T, float* base)
   w.pred = p[10];
   w.pph = p[11];
   w.row_tok = reinterpret_cast<int*>(p[12]);
+  w.part = p[13];
   return w;
 }
 

@@ -341,6 +341,7 @@ struct F32Work {
   float* pred;             // [NC][T-H+1][D] predictions appended to the history
   float* pph;              // [NC][P] pred_proj hidden rows
   int* row_tok;            // [NC*w] modulation row (candidate * T + history index) of each row
+  float* part;             // [4][NC*w][D] split-K partial sums of the gated-residual GEMMs
 };
 // Floats of F32Work for n_cand candidates, horizon T, window <= frames (pointers into one block).
 size_t f32_work_floats(const ModelDims& m, size_t n_cand, size_t T);
@@ -369,6 +370,8 @@ struct F32GradWork {
   float *dX, *dF, *dF1, *dA, *dAtt, *dQKV;  // [NC*w] x D / D / mlp / D / inner / 3 inner
   float *dY, *dpred;                        // [NC][D], [NC][T-H+1][D]
   float *dmod, *de, *dh1, *da1;             // [NC*T] x L*6D / D / eh / A'
+  float* part;                              // split-reduction partial sums of the dY . W GEMMs
+  size_t part_floats;
 };
 // Floats of the tape + gradient buffers of one evaluation; carve them from `base`.
 size_t f32_grad_floats(const ModelDims& m, int NC, int T, int H, int HS);

@@ -10,6 +10,8 @@
   ``lewm_flash_b200.solver.B200ICEMSolver``.
 * ``B200CEMSolver`` is ``CEMExactSolver`` (``lewm/solvers/cem_exact.py:54-383``):
   iCEM with every feature off, plus its receding-horizon warm start.
+* ``B200CEMGDSolver`` is ``CEMGDSolver`` (``lewm/solvers/cem_gd.py:38-711``): the seed
+  search as one device plan, the gradient refinement on the device gradient.
 * ``run_static_icem_chain`` mirrors the reference tensor-only chain
   (``lewm/solvers/icem_static_compile.py:61-114``) with injected noise.
 * ``B200ModelCost`` / ``install_model_cost`` replace
@@ -30,6 +32,7 @@ by injecting the reference's noise (``run_static_icem_chain``).
 from __future__ import annotations
 
 import math
+import time
 import warnings
 from typing import Any, Optional, Sequence
 
@@ -463,6 +466,286 @@ class B200CEMSolver(B200ICEMSolver):
                 cb.end_solve()
                 out["callbacks"][cb.output_key] = cb.history
         return out
+
+
+class B200CEMGDSolver(B200ICEMSolver):
+    """``CEMGDSolver`` (reference ``lewm/solvers/cem_gd.py:38-711``) on the B200 kernels: the
+    CEM / iCEM seed search of every env as one device plan, then CEM-GD's refinement (Adam
+    with 1 / 1/2 / 1/4 / 1/10 backtracking and per-seed acceptance, ``_refine_seed_actions``,
+    ``:459-606``) stepping on the device gradient of the model cost (``lewm_model_cost_grad``).
+
+    Same constructor arguments, ``ValueError`` texts, properties and ``solve`` output (``costs``,
+    ``mean``, ``var``, ``actions``, ``gd_summary``) as the reference. The seed search draws its
+    noise from the in-kernel Philox stream, or from ``noise_source`` (a reference solver's
+    ``_sample_noise``) to reproduce a reference run. The refinement runs env batch by env batch
+    of ``batch_size`` as the reference does (its loss is the mean over a batch's seeds, which
+    Adam's epsilon sees). The gradient step's forward and reverse pass are one device call:
+    ``gd_forward_time_ms_mean`` times it, ``gd_backward_time_ms_mean`` is 0.
+    """
+
+    def __init__(self, model: Any | None = None, batch_size: int = 1, num_samples: int = 300, var_scale: float = 1.0,
+                 n_steps: int = 30, topk: int = 30, device: str | torch.device = "cuda", seed: int = 1234,
+                 elite_retention: int = 0, colored_noise: str = "none", colored_noise_time: str = "raw",
+                 momentum_alpha: float = 0.0, sample_decay: float = 1.0, sample_count_bucket_size: int = 0,
+                 return_best_elite: bool = False, clip_actions: bool = False, gd_seed_solver: str = "cem",
+                 gd_seed_source: str = "best_elite", gd_refine_topk: int = 1, gd_steps: int = 1, gd_lr: float = 0.01,
+                 gd_compile_cost: bool = False, gd_backtracking: bool = True, callbacks: list[Any] | None = None,
+                 history_size: int = 3) -> None:
+        if topk <= 0:
+            raise ValueError(f"topk must be positive, got {topk}")
+        if num_samples < topk:
+            raise ValueError(f"num_samples={num_samples} must be >= topk={topk}")
+        if n_steps <= 0:
+            raise ValueError(f"n_steps must be positive, got {n_steps}")
+        if elite_retention < 0:
+            raise ValueError(f"elite_retention must be non-negative, got {elite_retention}")
+        if colored_noise not in COLORED_NOISE_BETA:
+            raise ValueError(
+                f"colored_noise must be one of {sorted(COLORED_NOISE_BETA)}, got {colored_noise!r}")
+        if not 0.0 <= momentum_alpha < 1.0:
+            raise ValueError(f"momentum_alpha must satisfy 0 <= alpha < 1, got {momentum_alpha}")
+        if sample_decay < 1.0:
+            raise ValueError(f"sample_decay must be >= 1.0, got {sample_decay}")
+        if sample_count_bucket_size < 0:
+            raise ValueError(f"sample_count_bucket_size must be non-negative, got {sample_count_bucket_size}")
+        if gd_seed_solver not in {"cem", "icem"}:
+            raise ValueError(f"gd_seed_solver must be 'cem' or 'icem', got {gd_seed_solver!r}")
+        if gd_seed_source not in {"best_elite", "mean"}:
+            raise ValueError(f"gd_seed_source must be 'best_elite' or 'mean', got {gd_seed_source!r}")
+        if gd_refine_topk <= 0:
+            raise ValueError(f"gd_refine_topk must be positive, got {gd_refine_topk}")
+        if gd_refine_topk > topk:
+            raise ValueError(f"gd_refine_topk={gd_refine_topk} must be <= topk={topk}")
+        if gd_steps < 0:
+            raise ValueError(f"gd_steps must be non-negative, got {gd_steps}")
+        if gd_lr <= 0.0:
+            raise ValueError(f"gd_lr must be positive, got {gd_lr}")
+        super().__init__(model, batch_size=batch_size, num_samples=num_samples, var_scale=var_scale, n_steps=n_steps,
+                         topk=topk, device=device, seed=seed, elite_retention=elite_retention,
+                         colored_noise=colored_noise, colored_noise_time=colored_noise_time,
+                         momentum_alpha=momentum_alpha, sample_decay=sample_decay,
+                         sample_count_bucket_size=sample_count_bucket_size, return_best_elite=return_best_elite,
+                         clip_actions=clip_actions, callbacks=callbacks, history_size=history_size)
+        self.gd_seed_solver = gd_seed_solver
+        self.gd_seed_source = gd_seed_source
+        self.gd_refine_topk = int(gd_refine_topk)
+        self.gd_steps = int(gd_steps)
+        self.gd_lr = float(gd_lr)
+        self.gd_compile_cost = bool(gd_compile_cost)
+        self.gd_backtracking = bool(gd_backtracking)
+
+    def configure(self, *, action_space: Any, n_envs: int, config: Any) -> None:
+        """``CEMGDSolver.configure`` (``cem_gd.py:134-157``): no callback protocol."""
+        self._action_space = action_space
+        self._n_envs = n_envs
+        self._config = config
+        self._action_dim = int(np.prod(action_space.shape[1:]))
+        self._configured = True
+        if "Box" not in type(action_space).__name__:
+            warnings.warn(f"Action space is not Box-like, got {type(action_space)}. "
+                          "CEMGDSolver may not work as expected.", RuntimeWarning, stacklevel=2)
+            return
+        if self.clip_actions and hasattr(action_space, "low") and hasattr(action_space, "high"):
+            self._action_low = torch.as_tensor(action_space.low[0], device=self.device,
+                                               dtype=self.dtype).repeat(self._config.action_block)
+            self._action_high = torch.as_tensor(action_space.high[0], device=self.device,
+                                                dtype=self.dtype).repeat(self._config.action_block)
+
+    def sample_count_for_step(self, step: int) -> int:
+        if self.gd_seed_solver == "cem":
+            return self.num_samples
+        return super().sample_count_for_step(step)
+
+    def plan_options(self) -> PlanOptions:
+        """The seed search: plain CEM (white noise, no decay, retention or momentum) or iCEM
+        (``_run_seed_search_batch``, ``cem_gd.py:370-436``); never the best elite as output."""
+        icem = self.gd_seed_solver == "icem"
+        return PlanOptions(
+            num_samples=self.num_samples, topk=self.topk, n_steps=self.n_steps,
+            sample_decay=self.sample_decay if icem else 1.0,
+            sample_count_bucket_size=self.sample_count_bucket_size if icem else 0,
+            elite_retention=self.elite_retention if icem else 0,
+            beta=COLORED_NOISE_BETA[self.colored_noise] if icem else 0.0, time_axis=self.colored_noise_time,
+            action_block=self.action_block, momentum_alpha=self.momentum_alpha if icem else 0.0,
+            return_best_elite=False, clip_actions=self._action_low is not None, history_size=self.history_size,
+            seed=self.seed, counts=self.sample_counts())
+
+    def _action_saturation_rate(self, actions: torch.Tensor) -> float | None:
+        if self._action_low is None or self._action_high is None:
+            return None
+        low = self._action_low.to(device=actions.device, dtype=actions.dtype)
+        high = self._action_high.to(device=actions.device, dtype=actions.dtype)
+        saturated = (actions - low).abs().le(1e-5) | (actions - high).abs().le(1e-5)
+        return float(saturated.float().mean().detach().cpu().item())
+
+    def _refine_seed_actions(self, seed_actions: torch.Tensor, seed_costs: torch.Tensor, emb: torch.Tensor,
+                             goal_emb: torch.Tensor, *, enable_backtracking: bool | None = None):
+        """``_refine_seed_actions`` (``cem_gd.py:459-606``) with the device gradient."""
+        rt = self.runtime
+        hs = self.history_size
+        params = seed_actions.detach().clone().requires_grad_(True)
+        optimizer = torch.optim.Adam([params], lr=self.gd_lr)
+        current_costs = seed_costs.detach().clone()
+        accepted_any = torch.zeros_like(current_costs, dtype=torch.bool)
+        forward_times: list[float] = []
+        grad_norm_values: list[float] = []
+        grad_norm_max = 0.0
+        nan_or_inf_count = 0
+        refine_width = int(seed_actions.shape[1])
+        backtrack = self.gd_backtracking if enable_backtracking is None else enable_backtracking
+        factors = [1.0, 0.5, 0.25, 0.1] if backtrack else [1.0]
+        evals = 0
+        final_actions = seed_actions.detach()
+        final_costs = seed_costs.detach()
+        n_loss = int(seed_actions.shape[0] * seed_actions.shape[1])  # loss = costs.mean()
+        weights = torch.full(tuple(seed_costs.shape), 1.0 / n_loss, device=seed_actions.device)
+        for _ in range(self.gd_steps):
+            optimizer.zero_grad(set_to_none=True)
+            torch.cuda.synchronize(self.device)
+            t0 = time.perf_counter()
+            costs, grad = rt.model_cost_grad(emb, goal_emb, params.detach(), history_size=hs, cost_weights=weights)
+            loss = costs.mean()
+            torch.cuda.synchronize(self.device)
+            forward_times.append((time.perf_counter() - t0) * 1000.0)
+            evals += refine_width
+            if not torch.isfinite(costs).all() or not torch.isfinite(loss):
+                nan_or_inf_count += int((~torch.isfinite(costs)).sum().item())
+                nan_or_inf_count += int(not bool(torch.isfinite(loss).item()))
+                break
+            if not torch.isfinite(grad).all():
+                nan_or_inf_count += int((~torch.isfinite(grad)).sum().item())
+                break
+            params.grad = grad.to(params.dtype)
+            grad_norms = params.grad.detach().flatten(start_dim=2).norm(dim=2)
+            grad_norm_values.extend(grad_norms.cpu().flatten().tolist())
+            grad_norm_max = max(grad_norm_max, float(grad_norms.max().item()))
+            before = params.detach().clone()
+            previous_costs = current_costs.detach().clone()
+            optimizer.step()
+            update = params.detach().clone() - before
+            best_actions, best_costs = before, previous_costs
+            for factor in factors:
+                candidate_actions = before + factor * update
+                with torch.no_grad():
+                    candidate_costs = rt.model_cost(emb, goal_emb, candidate_actions, history_size=hs)
+                evals += refine_width
+                finite = torch.isfinite(candidate_costs)
+                if not bool(finite.all().item()):
+                    nan_or_inf_count += int((~finite).sum().item())
+                improved = finite & (candidate_costs < best_costs)
+                best_actions = torch.where(improved[..., None, None], candidate_actions, best_actions)
+                best_costs = torch.where(improved, candidate_costs, best_costs)
+            accepted_any |= best_costs < previous_costs
+            current_costs = best_costs.detach()
+            with torch.no_grad():
+                params.copy_(best_actions)
+            final_actions = params.detach().clone()
+            final_costs = current_costs
+        final_accept = torch.isfinite(final_costs) & (final_costs < seed_costs)
+        accepted_actions = torch.where(final_accept[..., None, None], final_actions, seed_actions.detach())
+        accepted_costs = torch.where(final_accept, final_costs, seed_costs.detach())
+        candidate_count = int(seed_actions.shape[0] * seed_actions.shape[1])
+        accept_count = int(final_accept.sum().item())
+        cost_delta = (accepted_costs - seed_costs.detach()).detach()
+        summary = {
+            "gd_seed_solver": self.gd_seed_solver, "gd_seed_source": self.gd_seed_source,
+            "gd_refine_topk": self.gd_refine_topk, "gd_steps": self.gd_steps, "gd_lr": self.gd_lr,
+            "gd_compile_cost": self.gd_compile_cost,
+            "gd_forward_time_ms_mean": sum(forward_times) / len(forward_times) if forward_times else 0.0,
+            "gd_grad_norm_mean": sum(grad_norm_values) / len(grad_norm_values) if grad_norm_values else 0.0,
+            "gd_grad_norm_max": grad_norm_max,
+            "gd_action_saturation_rate": self._action_saturation_rate(accepted_actions),
+            "gd_backward_time_ms_mean": 0.0,
+            "gd_peak_memory_mb": torch.cuda.max_memory_allocated(self.device) / (1024.0 * 1024.0),
+            "gd_cost_delta_mean": float(cost_delta.mean().item()),
+            "gd_accept_rate": accept_count / candidate_count if candidate_count else 0.0,
+            "gd_accept_count": accept_count, "gd_candidate_count": candidate_count,
+            "gd_step_accept_rate": float(accepted_any.float().mean().item()) if accepted_any.numel() else 0.0,
+            "gd_nan_or_inf_count": nan_or_inf_count, "gd_model_cost_evals": evals,
+        }
+        return accepted_actions.detach(), accepted_costs.detach(), summary
+
+    @staticmethod
+    def _combine_gd_summaries(summaries: list[dict[str, Any]]) -> dict[str, Any]:
+        """``_combine_gd_summaries`` (``cem_gd.py:606-657``): per-batch summaries merged."""
+        if not summaries:
+            return {}
+
+        def mean_field(key):
+            values = [float(s[key]) for s in summaries if isinstance(s.get(key), (int, float))]
+            return sum(values) / len(values) if values else None
+
+        candidate_count = sum(int(s.get("gd_candidate_count", 0)) for s in summaries)
+        accept_count = sum(int(s.get("gd_accept_count", 0)) for s in summaries)
+        cost_delta_total = sum(float(s.get("gd_cost_delta_mean", 0.0)) * int(s.get("gd_candidate_count", 0))
+                               for s in summaries)
+        peaks = [float(s["gd_peak_memory_mb"]) for s in summaries
+                 if isinstance(s.get("gd_peak_memory_mb"), (int, float))]
+        first = summaries[0]
+        return {
+            "gd_seed_solver": first.get("gd_seed_solver"), "gd_seed_source": first.get("gd_seed_source"),
+            "gd_refine_topk": first.get("gd_refine_topk"), "gd_steps": first.get("gd_steps"),
+            "gd_lr": first.get("gd_lr"), "gd_compile_cost": first.get("gd_compile_cost"),
+            "gd_forward_time_ms_mean": mean_field("gd_forward_time_ms_mean"),
+            "gd_grad_norm_mean": mean_field("gd_grad_norm_mean"),
+            "gd_grad_norm_max": max(float(s.get("gd_grad_norm_max", 0.0)) for s in summaries),
+            "gd_action_saturation_rate": mean_field("gd_action_saturation_rate"),
+            "gd_backward_time_ms_mean": mean_field("gd_backward_time_ms_mean"),
+            "gd_peak_memory_mb": max(peaks) if peaks else None,
+            "gd_cost_delta_mean": cost_delta_total / candidate_count if candidate_count else 0.0,
+            "gd_accept_rate": accept_count / candidate_count if candidate_count else 0.0,
+            "gd_accept_count": accept_count, "gd_candidate_count": candidate_count,
+            "gd_nan_or_inf_count": sum(int(s.get("gd_nan_or_inf_count", 0)) for s in summaries),
+            "gd_model_cost_evals": max(int(s.get("gd_model_cost_evals", 0)) for s in summaries),
+        }
+
+    def solve(self, info_dict: dict, init_action: torch.Tensor | None = None) -> dict[str, Any]:
+        """``CEMGDSolver.solve`` (``cem_gd.py:660-711``)."""
+        if self.model is None:
+            raise RuntimeError("CEMGDSolver.solve requires a model")
+        outputs: dict[str, Any] = {"costs": [], "mean": [], "var": []}
+        total_envs = len(next(iter(info_dict.values())))
+        with torch.inference_mode():
+            init_action = prepare_init_action(self.model, info_dict, init_action, self.horizon, n_envs=total_envs,
+                                              action_dim=self.action_dim)
+            mean, var = self.init_action_distrib(total_envs, init_action)
+            mean = mean.to(self.device)
+            var = var.to(self.device)
+            emb, goal = self._cost_embeddings(info_dict, total_envs)
+            _, std, _, tr = self._plan(info_dict, mean, var, trace=True)
+        # Clone out of inference mode: the refinement needs ordinary tensors.
+        emb, goal = emb.detach().clone(), goal.detach().clone()
+        last = self.n_steps - 1
+        k = self.gd_refine_topk
+        if self.gd_seed_source == "mean":
+            seed_actions = tr["mean"][last].detach().clone().unsqueeze(1)
+            seed_costs = self.runtime.model_cost(emb, goal, seed_actions, history_size=self.history_size)
+        else:
+            n = tr["counts"][last]
+            cand = tr["candidates"][last][:, :n]
+            idx = tr["topk_idx"][last][:, :k].long()
+            seed_actions = torch.gather(cand, 1, idx[:, :, None, None].expand(-1, -1, cand.shape[2], cand.shape[3]))
+            seed_actions = seed_actions.detach().clone()
+            seed_costs = tr["topk_val"][last][:, :k].detach().clone()
+        final_var = std.detach().clone()
+        final_actions = torch.empty(total_envs, self.horizon, self.action_dim, device=self.device, dtype=self.dtype)
+        summaries = []
+        for start in range(0, total_envs, self.batch_size):
+            end = min(start + self.batch_size, total_envs)
+            refined, refined_costs, summary = self._refine_seed_actions(
+                seed_actions[start:end], seed_costs[start:end], emb[start:end], goal[start:end])
+            summaries.append(summary)
+            best_costs, best_idx = torch.min(refined_costs, dim=1)
+            final_actions[start:end] = refined[torch.arange(end - start, device=self.device), best_idx]
+            outputs["costs"].extend(best_costs.detach().cpu().tolist())
+        self.runtime.sync()
+        outputs["actions"] = final_actions.detach().cpu()
+        outputs["mean"] = [final_actions.detach().cpu()]
+        outputs["var"] = [final_var.detach().cpu()]
+        gd_summary = self._combine_gd_summaries(summaries)
+        gd_summary["gd_seed_model_cost_evals"] = sum(self.sample_counts()) + (1 if self.gd_seed_source == "mean" else 0)
+        outputs["gd_summary"] = gd_summary
+        return outputs
 
 
 def run_static_icem_chain(model, emb: torch.Tensor, goal_emb: torch.Tensor, mean: torch.Tensor, var: torch.Tensor,

@@ -173,3 +173,60 @@ def test_reference_cem_gd_solver_refines_on_device_gradient(backtracking):
     print(f"backtracking={backtracking}: refined costs {np.round(np.asarray(got['costs']), 3).tolist()}, "
           f"accepted {gs['gd_accept_count']} of {gs['gd_candidate_count']}, cost delta {gs['gd_cost_delta_mean']:.4f}, "
           f"actions: {int((~close).sum())} of {close.numel()} coordinates beyond 1e-4 (max {diff.max().item():.1e})")
+
+
+@pytest.mark.skipif(not (REF / "lewm" / "solvers" / "cem_gd.py").is_file(),
+                    reason="reference package not installed in baseline/_ref")
+@pytest.mark.parametrize("seed_solver,source", [("cem", "best_elite"), ("icem", "best_elite"), ("cem", "mean")])
+def test_b200_cem_gd_solver_matches_reference_solver(seed_solver, source):
+    """B200CEMGDSolver (one device seed plan, device-gradient refinement) against the
+    reference's CEMGDSolver on the same model cost and the same seed-search noise (its twin's
+    _sample_noise): 3 envs in env batches of 2."""
+    from types import SimpleNamespace
+
+    from tests.test_gpu_dropin import Box, _jepa, _reference
+
+    from lewm_flash_b200.solver import B200CEMGDSolver, install_model_cost
+
+    ref = _reference()
+    from lewm.solvers.cem_gd import CEMGDSolver
+
+    class CLSFeatures(torch.nn.Module):
+        def forward(self, pixels, interpolate_pos_encoding=True):
+            return SimpleNamespace(last_hidden_state=pixels[:, None, :])
+
+    dev = torch.device("cuda", 0)
+    model, _ = _jepa(ref, dev)
+    model.encoder = CLSFeatures()
+    model.set_embedding_cache(True).set_compile_cost(True)
+    install_model_cost(model, dev)
+    kw = dict(batch_size=2, num_samples=48, n_steps=4, topk=8, seed=17, gd_seed_solver=seed_solver,
+              gd_seed_source=source, gd_refine_topk=3, gd_steps=3, gd_lr=0.05, colored_noise="brown",
+              sample_decay=1.25, sample_count_bucket_size=8, elite_retention=2, momentum_alpha=0.1, clip_actions=True)
+    cfg = SimpleNamespace(horizon=5, action_block=5)
+    g = torch.Generator().manual_seed(43)
+    info = {"pixels": torch.randn(3, 1, 192, generator=g).to(dev), "goal": torch.randn(3, 1, 192, generator=g).to(dev)}
+    ref_solver = CEMGDSolver(model=model, device=dev, **kw)
+    twin = CEMGDSolver(model=model, device=dev, **kw)
+    b200 = B200CEMGDSolver(model, device=dev, **kw)
+    for s in (ref_solver, twin, b200):
+        s.configure(action_space=Box(3, lo=-1.5, hi=1.5), n_envs=3, config=cfg)
+    b200.noise_source = twin._sample_noise
+    want = ref_solver.solve(dict(info))
+    got = b200.solve(dict(info))
+    assert set(got) == set(want)
+    np.testing.assert_allclose(np.asarray(got["costs"]), np.asarray(want["costs"]), rtol=1e-5)
+    torch.testing.assert_close(got["var"][0], want["var"][0], rtol=1e-4, atol=1e-5)
+    diff = (got["actions"] - want["actions"]).abs()
+    close = diff <= 1e-4 * (1.0 + want["actions"].abs())
+    assert close.float().mean().item() >= 0.95 and diff.max().item() <= 2 * kw["gd_lr"] * kw["gd_steps"]
+    gs, ws = got["gd_summary"], want["gd_summary"]
+    assert set(gs) == set(ws)
+    for key in ("gd_accept_count", "gd_candidate_count", "gd_model_cost_evals", "gd_nan_or_inf_count",
+                "gd_seed_model_cost_evals", "gd_seed_solver", "gd_seed_source", "gd_refine_topk", "gd_steps"):
+        assert gs[key] == ws[key], key
+    for key in ("gd_cost_delta_mean", "gd_grad_norm_mean", "gd_grad_norm_max", "gd_accept_rate"):
+        assert abs(gs[key] - ws[key]) <= 1e-4 * (abs(ws[key]) + 1.0), (key, gs[key], ws[key])
+    print(f"{seed_solver}/{source}: costs {np.round(np.asarray(got['costs']), 3).tolist()}, accepted "
+          f"{gs['gd_accept_count']} of {gs['gd_candidate_count']}, {int((~close).sum())} of {close.numel()} action "
+          f"coordinates beyond 1e-4")

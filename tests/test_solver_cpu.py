@@ -104,3 +104,55 @@ def test_warm_start_shift_matches_reference(case):
     assert ours.last_warm_start_info == ref.last_warm_start_info
     if case == "used":
         assert ours.last_warm_start_info["used"] is True
+
+
+CEMGD_BAD_ARGS = [dict(topk=0), dict(num_samples=10, topk=20), dict(n_steps=0), dict(elite_retention=-1),
+                  dict(colored_noise="blue"), dict(momentum_alpha=1.0), dict(sample_decay=0.5),
+                  dict(sample_count_bucket_size=-1), dict(gd_seed_solver="mppi"), dict(gd_seed_source="last"),
+                  dict(gd_refine_topk=0), dict(gd_refine_topk=31), dict(gd_steps=-1), dict(gd_lr=0.0)]
+
+
+@pytest.mark.parametrize("bad", CEMGD_BAD_ARGS)
+def test_cem_gd_solver_rejects_like_reference(bad):
+    """B200CEMGDSolver raises the reference CEMGDSolver's ValueErrors (lewm/solvers/cem_gd.py:67-101)."""
+    from lewm_flash_b200.solver import B200CEMGDSolver
+
+    _ref()
+    from lewm.solvers.cem_gd import CEMGDSolver
+
+    with pytest.raises(ValueError) as want:
+        CEMGDSolver(model=None, **bad)
+    with pytest.raises(ValueError) as got:
+        B200CEMGDSolver(None, **bad)
+    assert str(got.value) == str(want.value)
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(gd_seed_solver="icem", sample_decay=1.25, sample_count_bucket_size=60),
+                                dict(gd_seed_solver="cem", sample_decay=1.25, sample_count_bucket_size=60),
+                                dict(gd_seed_solver="icem", sample_decay=1.1, num_samples=100, topk=10)])
+def test_cem_gd_solver_schedule_and_surface_match_reference(kw):
+    from lewm_flash_b200.solver import B200CEMGDSolver
+
+    _ref()
+    from lewm.solvers.cem_gd import CEMGDSolver
+
+    cfg = SimpleNamespace(horizon=5, action_block=5)
+    ref = CEMGDSolver(model=None, **kw)
+    dev = B200CEMGDSolver(None, **kw)
+    for s in (ref, dev):
+        s.configure(action_space=Box(2), n_envs=2, config=cfg)
+    assert dev.sample_counts() == ref.sample_counts()
+    assert dev.model_cost_evals_per_solve() == ref.model_cost_evals_per_solve()
+    assert (dev.n_envs, dev.action_dim, dev.horizon, dev.action_block) == (
+        ref.n_envs, ref.action_dim, ref.horizon, ref.action_block)
+    m_ref, v_ref = ref.init_action_distrib(2, None)
+    m_dev, v_dev = dev.init_action_distrib(2, None)
+    assert torch.equal(m_ref, m_dev) and torch.equal(v_ref, v_dev)
+    opts = dev.plan_options()
+    assert opts.counts == ref.sample_counts()
+    icem = dev.gd_seed_solver == "icem"
+    assert opts.beta == (COLORED[dev.colored_noise] if icem else 0.0)
+    assert opts.elite_retention == (dev.elite_retention if icem else 0) and not opts.return_best_elite
+
+
+COLORED = {"none": 0.0, "pink": 1.0, "brown": 2.0}
