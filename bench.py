@@ -606,6 +606,9 @@ def main() -> int:
 
     # ---------------------------------------------------------------- 1024 envs split over the ranks
     sharded = sharded_pass(rt, dev, rank, world, barrier, dist, flush) if not args.no_sharded else None
+    # the same 1024 envs with history 1 (5 predictor calls per iteration, windows 1, 2, 3, 3, 3)
+    sharded_h1 = (sharded_pass(rt, dev, rank, world, barrier, dist, flush, history=1, n_calls=2)
+                  if not args.no_sharded else None)
 
     # ---------------------------------------------------------------- width 384 / 12 layers, 32 envs per rank
     stress = stress_pass(dev, rank, world, barrier, dist, flush) if not args.no_stress else None
@@ -637,6 +640,7 @@ def main() -> int:
         "fp32_cem": fp32_cem,
         "cem_gd": cem_gd,
         "sharded": sharded,
+        "sharded_h1": sharded_h1,
         "stress": stress,
         "encoder": encoder,
         "clocks": clocks.summary(),
@@ -648,7 +652,9 @@ def main() -> int:
         if "compiled_p50_ms" in ref_gpu:
             ref_gpu["speedup_vs_compiled"] = ref_gpu["compiled_p50_ms"] / p50
         line["reference_gpu"] = ref_gpu
-    if rank == 0 and not args.no_cpu_baseline:
+    # The host-core baseline runs at N = 1 only: under torchrun the other ranks would wait at the
+    # closing barrier (and spin on their CPU cores) for the whole CPU run.
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         times, info = reference_cpu_plans(max(args.cpu_baseline_plans, 1), 1, rank)
         line["cpu_baseline"] = dict(info, value=1.0 / float(np.mean(times)), unit="plans/s")
     if dist is not None:
