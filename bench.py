@@ -607,7 +607,7 @@ def main() -> int:
     # ---------------------------------------------------------------- 1024 envs split over the ranks
     sharded = sharded_pass(rt, dev, rank, world, barrier, dist, flush) if not args.no_sharded else None
     # the same 1024 envs with history 1 (5 predictor calls per iteration, windows 1, 2, 3, 3, 3)
-    sharded_h1 = (sharded_pass(rt, dev, rank, world, barrier, dist, flush, history=1, n_calls=2)
+    sharded_h1 = (sharded_pass(rt, dev, rank, world, barrier, dist, flush, history=1, n_calls=2, own_runtime=True)
                   if not args.no_sharded else None)
 
     # ---------------------------------------------------------------- width 384 / 12 layers, 32 envs per rank
@@ -690,15 +690,23 @@ def timed_shard_calls(dev, barrier, dist, flush, plan_call, n_calls):
     return float(worst.item())
 
 
-def sharded_pass(rt, dev, rank, world, barrier, dist, flush, n_envs=1024, history=3, n_calls=3):
+def sharded_pass(rt, dev, rank, world, barrier, dist, flush, n_envs=1024, history=3, n_calls=3, own_runtime=False):
     """1024 independent envs (own N(0,1) latents, history 3) split contiguously over the ranks
     (lewm_flash_b200.shard.env_range); each rank plans its envs as one batched plan call, with
     no collective in the timed region. plans/s = 1024 / (max over ranks of the call time):
     total work fixed, so strong scaling over the GPU count. The plans are gathered to rank 0
-    on the host afterwards (gather_plans, gloo), outside the timed region."""
+    on the host afterwards (gather_plans, gloo), outside the timed region. own_runtime:
+    plan on a context of its own, released afterwards (its workspace for 1024 envs does not
+    stay allocated beside the later legs)."""
     import torch
 
     from lewm_flash_b200.shard import env_range, gather_plans, plan_shard
+
+    if own_runtime:
+        from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
+        from lewm_flash_b200.runtime import Runtime
+
+        rt = Runtime(ModelDesc(), synthetic_state_dict(ModelDesc(), 0), dev)
 
     opts = plan_options()
     rng = np.random.default_rng(3)
@@ -727,6 +735,9 @@ def sharded_pass(rt, dev, rank, world, barrier, dist, flush, n_envs=1024, histor
         dist.destroy_process_group(group)
     else:
         gathered = int(box["out"][0].shape[0])
+    box.clear()
+    if own_runtime:
+        rt.close()
     return {"workload": f"icem_bucketed_300_{n_envs}env_h{history}_bf16", "envs": n_envs, "envs_this_rank": e - s,
             "history": history, "plans_per_s": n_envs / (per_call / 1e3), "ms_per_call": per_call, "calls": n_calls,
             "gathered_envs": gathered, "scaling": "strong",

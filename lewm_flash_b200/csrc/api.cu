@@ -74,10 +74,12 @@ struct Workspace {
 
 struct WsReq {
   size_t n_cand, T, A, D, L, tiles, heads, mlp, npred, B, R, ncol, kvpos;
-  size_t f32 = 0;  // 1: carve the fp32 model-cost activations too
+  // fp32 model-cost activations for this many candidates and horizon (0: none), sized by the
+  // float32 requests alone so that bf16 calls of many candidates do not size them
+  size_t f32_nc = 0, f32_T = 0;
   bool operator<=(const WsReq& o) const {
     return n_cand <= o.n_cand && T <= o.T && tiles <= o.tiles && npred <= o.npred && B <= o.B && R <= o.R &&
-           ncol <= o.ncol && kvpos <= o.kvpos && f32 <= o.f32;
+           ncol <= o.ncol && kvpos <= o.kvpos && f32_nc <= o.f32_nc && f32_T <= o.f32_T;
   }
 };
 
@@ -478,7 +480,10 @@ void clear_graphs(lewm_ctx* c) {
 
 lewm_status ensure_ws(lewm_ctx* c, const WsReq& need_in) {
   WsReq need = need_in;
-  need.f32 = std::max<size_t>(need_in.f32, c->autocast == 0 ? 1 : 0);
+  if (c->autocast == 0) {  // float32 model costs of this request
+    need.f32_nc = std::max(need.f32_nc, need.n_cand);
+    need.f32_T = std::max(need.f32_T, need.T);
+  }
   if (c->have_ws && need <= c->cap) return LEWM_OK;
   WsReq r = need;
   if (c->have_ws) {  // grow monotonically
@@ -490,7 +495,8 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need_in) {
     r.R = std::max(r.R, c->cap.R);
     r.ncol = std::max(r.ncol, c->cap.ncol);
     r.kvpos = std::max(r.kvpos, c->cap.kvpos);
-    r.f32 = std::max(r.f32, c->cap.f32);
+    r.f32_nc = std::max(r.f32_nc, c->cap.f32_nc);
+    r.f32_T = std::max(r.f32_T, c->cap.f32_T);
     clear_graphs(c);
     cudaFree(c->ws.base);
     c->ws = Workspace{};
@@ -536,7 +542,7 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need_in) {
   const size_t o_pphid = carve(pp_tiles * (size_t)(m.pp_hidden / 64) * 128 * 64 * 2);
   const size_t o_pph32 = carve(m.pp_norm == 1 ? pp_tiles * 128 * (size_t)m.pp_hidden * 4 : 0);
   const size_t o_ppout = carve(m.pp_hidden ? r.n_cand * (size_t)m.D * 4 : 0);
-  const size_t o_f32 = carve(r.f32 ? f32_work_floats(m, r.n_cand, r.T) * 4 : 0);
+  const size_t o_f32 = carve(r.f32_nc ? f32_work_floats(m, r.f32_nc, r.f32_T) * 4 : 0);
   void* base = nullptr;
   LEWM_CK(c, cudaMalloc(&base, off));
   auto* b = static_cast<uint8_t*>(base);
@@ -573,7 +579,7 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need_in) {
   ws.pp_hid = reinterpret_cast<__nv_bfloat16*>(b + o_pphid);
   ws.pp_hid32 = reinterpret_cast<float*>(b + o_pph32);
   ws.pp_out = reinterpret_cast<float*>(b + o_ppout);
-  if (r.f32) ws.f32 = f32_work_carve(m, r.n_cand, r.T, reinterpret_cast<float*>(b + o_f32));
+  if (r.f32_nc) ws.f32 = f32_work_carve(m, r.f32_nc, r.f32_T, reinterpret_cast<float*>(b + o_f32));
   c->cap = r;
   c->have_ws = true;
   c->W_n = -1;
@@ -1115,7 +1121,8 @@ lewm_status lewm_model_cost_grad(lewm_ctx* c, const float* emb, int32_t emb_per_
   WsReq need{(size_t)NC, (size_t)T, (size_t)c->md.A, (size_t)c->md.D, (size_t)c->md.L,
              (size_t)max_call_tiles(NC, T, H, history_size, c->tile_target), (size_t)c->md.heads, (size_t)c->md.mlp,
              (size_t)(T - H + 1), 1, 0, 0, (size_t)kv_positions(H, history_size)};
-  need.f32 = 1;
+  need.f32_nc = (size_t)NC;
+  need.f32_T = (size_t)T;
   lewm_status s = ensure_ws(c, need);
   if (s != LEWM_OK) return s;
   const size_t nf = f32_grad_floats(c->md, NC, T, H, history_size);
