@@ -157,42 +157,17 @@ __device__ __forceinline__ float2 warp_moments(const float* row, int width) {
   return make_float2(mean, warp_sum(q) / width);
 }
 
-// A gated residual X += gate . (bias + sum_z part[z]) whose split-K partial sums wait for the
-// next kernel that reads X (k_ln_mod32) instead of a launch of their own.
-struct PendingResid {
-  const float* part = nullptr;  // [splits][rows][D]; null: nothing pending
-  int splits = 0;
-  const float* bias = nullptr;
-  int gate_off = 0;
-  float* save = nullptr;        // the branch value (bias + sum), [rows][D], or null
-};
-
 // out = LN_{g,b}(LN(x) * (1 + scale) + shift): AdaLN modulate (eps 1e-6, no affine) then the
-// block's LayerNorm (eps 1e-5), width D; scratch h in `out` between the passes. A pending
-// gated residual is folded into the row of X first (same order of additions as
-// k_splitk_resid32) and written back.
-__global__ void __launch_bounds__(256) k_ln_mod32(float* __restrict__ X, int rows, int D,
+// block's LayerNorm (eps 1e-5), width D; scratch h in `out` between the passes.
+__global__ void __launch_bounds__(256) k_ln_mod32(const float* __restrict__ X, int rows, int D,
                                                   const int* __restrict__ row_tok, const float* __restrict__ mod,
                                                   int mod_ld, int shift_off, int scale_off, const float* __restrict__ g,
-                                                  const float* __restrict__ b, float* __restrict__ out,
-                                                  PendingResid pend) {
+                                                  const float* __restrict__ b, float* __restrict__ out) {
   const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (r >= rows) return;
-  float* x = X + (size_t)r * D;
+  const float* x = X + (size_t)r * D;
   float* o = out + (size_t)r * D;
   const float* mrow = mod + (size_t)row_tok[r] * mod_ld;
-  if (pend.part) {
-    const size_t n_out = (size_t)rows * D;
-    for (int c = lane; c < D; c += 32) {
-      const size_t i = (size_t)r * D + c;
-      float v = pend.part[i];
-      for (int z = 1; z < pend.splits; ++z) v += pend.part[z * n_out + i];
-      v += pend.bias ? pend.bias[c] : 0.f;
-      if (pend.save) pend.save[i] = v;
-      x[c] += mrow[pend.gate_off + c] * v;
-    }
-    __syncwarp();
-  }
   const float2 mv = warp_moments(x, D);
   const float rstd = 1.0f / sqrtf(mv.y + 1e-6f);
   for (int c = lane; c < D; c += 32) {
@@ -330,10 +305,8 @@ __global__ void k_splitk_resid32(const float* __restrict__ part, int splits, int
 template <int EPI>
 cudaError_t sgemm(const float* A, int lda, const float* W, int K, const float* bias, float* C, int ldc, int M, int N,
                   cudaStream_t st, const float* mod = nullptr, const int* row_tok = nullptr, int mod_ld = 0,
-                  int gate_off = 0, float* save = nullptr, float* part = nullptr, int splits = 1,
-                  PendingResid* defer = nullptr) {
+                  int gate_off = 0, float* save = nullptr, float* part = nullptr, int splits = 1) {
   if (EPI != GE_RESID || !part) splits = 1;  // split K only where k_splitk_resid32 finishes the epilogue
-  if (defer) *defer = PendingResid{};
   const int kc = splits > 1 ? ((K + splits - 1) / splits + GB_K - 1) / GB_K * GB_K : K;
   const int nz = (K + kc - 1) / kc;
   const dim3 grid((N + GB_N - 1) / GB_N, (M + GB_M - 1) / GB_M, nz);
@@ -347,10 +320,6 @@ cudaError_t sgemm(const float* A, int lda, const float* W, int K, const float* b
                                                     save, kc, pp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || !pp) return e;
-  if (defer && ldc == N) {  // the next k_ln_mod32 over these rows folds the partials in
-    *defer = PendingResid{pp, nz, bias, gate_off, save};
-    return cudaSuccess;
-  }
   const size_t n_out = (size_t)M * N;
   const int blocks = (int)std::min<size_t>((n_out + 255) / 256, 148 * 16);
   k_splitk_resid32<<<blocks, 256, 0, st>>>(pp, nz, M, N, bias, C, ldc, mod, row_tok, mod_ld, gate_off, save);
@@ -391,31 +360,24 @@ cudaError_t run_model_cost_fp32(const ModelDims& m, const F32Weights& w, const F
                                        row_tok);
     F32_TRY(cudaGetLastError());
     const int lnb = (rows + 7) / 8;
-    // Without a tape, a gated residual's split-K partials are folded into X by the LayerNorm
-    // kernel that reads X next (the next layer's, for FC2); with one, X is recorded in between.
-    PendingResid pend;
-    PendingResid* defer = tc ? nullptr : &pend;
     for (int l = 0; l < L; ++l) {  // ConditionalBlock (lewm/module.py:88-111)
       const F32Layer& lw = w.layers[l];
       const int mo = l * 6 * D;  // shift_msa | scale_msa | gate_msa | shift_mlp | scale_mlp | gate_mlp
       float* qkv = tc ? tc->qkv + (size_t)l * rows * 3 * inner : ws.qkv;
       if (tc) F32_TRY(cudaMemcpyAsync(tc->x_in + l * RD, ws.x, RD * 4, cudaMemcpyDeviceToDevice, st));
       k_ln_mod32<<<lnb, 256, 0, st>>>(ws.x, rows, D, row_tok, ws.mod, mod_ld, mo, mo + D, lw.attn_ln_w, lw.attn_ln_b,
-                                      ws.a, pend);
-      pend = PendingResid{};
+                                      ws.a);
       F32_TRY(sgemm<GE_BIAS>(ws.a, D, lw.qkv_w, D, nullptr, qkv, 3 * inner, rows, 3 * inner, st));
       k_attn32<<<(rows * m.heads + 7) / 8, 256, 0, st>>>(qkv, rows, wlen, m.heads, ws.att);
       F32_TRY(sgemm<GE_RESID>(ws.att, inner, lw.out_w, inner, lw.out_b, ws.x, D, rows, D, st, ws.mod, row_tok, mod_ld,
-                              mo + 2 * D, tc ? tc->o + l * RD : nullptr, ws.part, kSplitK, defer));
+                              mo + 2 * D, tc ? tc->o + l * RD : nullptr, ws.part, kSplitK));
       if (tc) F32_TRY(cudaMemcpyAsync(tc->x_mid + l * RD, ws.x, RD * 4, cudaMemcpyDeviceToDevice, st));
       k_ln_mod32<<<lnb, 256, 0, st>>>(ws.x, rows, D, row_tok, ws.mod, mod_ld, mo + 3 * D, mo + 4 * D, lw.ffn_ln_w,
-                                      lw.ffn_ln_b, ws.a, pend);
-      pend = PendingResid{};
+                                      lw.ffn_ln_b, ws.a);
       F32_TRY(sgemm<GE_GELU>(ws.a, D, lw.w1, D, lw.b1, ws.hid, m.mlp, rows, m.mlp, st, nullptr, nullptr, 0, 0,
                              tc ? tc->f1 + (size_t)l * rows * m.mlp : nullptr));
       F32_TRY(sgemm<GE_RESID>(ws.hid, m.mlp, lw.w2, m.mlp, lw.b2, ws.x, D, rows, D, st, ws.mod, row_tok, mod_ld,
-                              mo + 5 * D, tc ? tc->f2 + l * RD : nullptr, ws.part, kSplitK,
-                              l + 1 < L ? defer : nullptr));
+                              mo + 5 * D, tc ? tc->f2 + l * RD : nullptr, ws.part, kSplitK));
     }
     if (tc) F32_TRY(cudaMemcpyAsync(tc->x_out, ws.x, RD * 4, cudaMemcpyDeviceToDevice, st));
     k_final_ln32<<<(NC + 7) / 8, 256, 0, st>>>(ws.x, NC, wlen, D, w.fin_w, w.fin_b, ws.y);
