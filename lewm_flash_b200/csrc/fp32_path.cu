@@ -285,6 +285,111 @@ __global__ void __launch_bounds__(256) k_emit32(const float* __restrict__ y, int
   if (lane == 0) costs[cand] = acc;
 }
 
+// The same GEMM as k_sgemm for the wide, many-row cases (QKV, AdaLN, FC1, the Embedder):
+// 128 x 128 output tile per 256-thread CTA, 8 x 8 outputs per thread (half the shared-memory
+// loads per FMA of the 4 x 4 tile), K in slabs of 32 with the next slab prefetched into
+// registers. Each output still sums its K products in increasing k with one fmaf each, so
+// the results are bit-identical to k_sgemm's; the launcher picks the tile by grid size only.
+// Epilogues GE_BIAS / GE_SILU / GE_GELU (and `save`).
+constexpr int GL_M = 128, GL_N = 128;
+
+template <int EPI, bool VEC>
+__global__ void __launch_bounds__(G_THREADS, 2) k_sgemm_wide(const float* __restrict__ A, int lda,
+                                                          const float* __restrict__ W, int K,
+                                                          const float* __restrict__ bias, float* __restrict__ C,
+                                                          int ldc, int M, int N, float* __restrict__ save) {
+  __shared__ __align__(16) float sA[GB_K][GL_M + 4];
+  __shared__ __align__(16) float sW[GB_K][GL_N + 4];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int m0 = blockIdx.y * GL_M, n0 = blockIdx.x * GL_N;
+  // Per slab each thread moves 16 A values and 16 W values: VEC as 4 float4 (row s / 8, k
+  // 4 (s % 8)), scalar as 16 floats (row s / 32, k s % 32), s = tid + 256 q.
+  float ra[16], rw[16];
+  auto load = [&](int k0) {
+    if constexpr (VEC) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int sl = tid + q * G_THREADS, r = sl >> 3, k = k0 + (sl & 7) * 4;
+        const int m = m0 + r, n = n0 + r;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), w = a;
+        if (m < M && k < K) a = *reinterpret_cast<const float4*>(A + (size_t)m * lda + k);
+        if (n < N && k < K) w = *reinterpret_cast<const float4*>(W + (size_t)n * K + k);
+        ra[4 * q] = a.x, ra[4 * q + 1] = a.y, ra[4 * q + 2] = a.z, ra[4 * q + 3] = a.w;
+        rw[4 * q] = w.x, rw[4 * q + 1] = w.y, rw[4 * q + 2] = w.z, rw[4 * q + 3] = w.w;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const int sl = tid + q * G_THREADS, r = sl >> 5, k = k0 + (sl & 31);
+        const int m = m0 + r, n = n0 + r;
+        ra[q] = (m < M && k < K) ? A[(size_t)m * lda + k] : 0.f;
+        rw[q] = (n < N && k < K) ? W[(size_t)n * K + k] : 0.f;
+      }
+    }
+  };
+  auto store = [&]() {
+    if constexpr (VEC) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int sl = tid + q * G_THREADS, r = sl >> 3, kk = (sl & 7) * 4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sA[kk + j][r] = ra[4 * q + j];
+          sW[kk + j][r] = rw[4 * q + j];
+        }
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const int sl = tid + q * G_THREADS, r = sl >> 5, kk = sl & 31;
+        sA[kk][r] = ra[q];
+        sW[kk][r] = rw[q];
+      }
+    }
+  };
+  float acc[8][8] = {};
+  load(0);
+  store();
+  __syncthreads();
+  for (int k0 = 0; k0 < K; k0 += GB_K) {
+    const bool more = k0 + GB_K < K;
+    if (more) load(k0 + GB_K);
+#pragma unroll
+    for (int kk = 0; kk < GB_K; ++kk) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&sA[kk][ty * 8]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&sA[kk][ty * 8 + 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&sW[kk][tx * 8]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&sW[kk][tx * 8 + 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+    if (more) {
+      store();
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int m = m0 + ty * 8 + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int n = n0 + tx * 8 + j;
+      if (n >= N) continue;
+      const float v = acc[i][j] + (bias ? bias[n] : 0.f);
+      if (save) save[(size_t)m * N + n] = v;
+      if constexpr (EPI == GE_BIAS) C[(size_t)m * ldc + n] = v;
+      if constexpr (EPI == GE_SILU) C[(size_t)m * ldc + n] = v / (1.0f + expf(-v));
+      if constexpr (EPI == GE_GELU) C[(size_t)m * ldc + n] = gelu_erf(v);
+    }
+  }
+}
+
 // Split-K epilogue of the gated residual: v = bias + sum_z part[z] (z ascending), save = v,
 // X += gate . v (one thread per output).
 __global__ void k_splitk_resid32(const float* __restrict__ part, int splits, int M, int N,
@@ -307,6 +412,19 @@ cudaError_t sgemm(const float* A, int lda, const float* W, int K, const float* b
                   cudaStream_t st, const float* mod = nullptr, const int* row_tok = nullptr, int mod_ld = 0,
                   int gate_off = 0, float* save = nullptr, float* part = nullptr, int splits = 1) {
   if (EPI != GE_RESID || !part) splits = 1;  // split K only where k_splitk_resid32 finishes the epilogue
+  if constexpr (EPI != GE_RESID) {
+    // The 128 x 128 tile where it still fills the SMs (same bits as the 64 x 64 one).
+    const dim3 wide((N + GL_N - 1) / GL_N, (M + GL_M - 1) / GL_M);
+    if ((size_t)wide.x * wide.y >= 2 * 148) {
+      const bool v = K % 4 == 0 && lda % 4 == 0 &&
+                     (reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W)) % 16 == 0;
+      if (v)
+        k_sgemm_wide<EPI, true><<<wide, G_THREADS, 0, st>>>(A, lda, W, K, bias, C, ldc, M, N, save);
+      else
+        k_sgemm_wide<EPI, false><<<wide, G_THREADS, 0, st>>>(A, lda, W, K, bias, C, ldc, M, N, save);
+      return cudaGetLastError();
+    }
+  }
   const int kc = splits > 1 ? ((K + splits - 1) / splits + GB_K - 1) / GB_K * GB_K : K;
   const int nz = (K + kc - 1) / kc;
   const dim3 grid((N + GB_N - 1) / GB_N, (M + GB_M - 1) / GB_M, nz);

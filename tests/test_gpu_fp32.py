@@ -194,3 +194,24 @@ def test_switching_modes_gives_each_modes_results():
     with pytest.raises(ValueError):
         rt.set_model_cost_autocast("fp16")
     rt.close()
+
+
+def test_fp32_costs_do_not_depend_on_the_batch():
+    """An env's float32 costs are the same bits alone (64 x 64 GEMM tiles) and inside a batch
+    of 64 envs x 300 candidates (the 128 x 128 tiles for the wide GEMMs): every output sums
+    its products in the same order whatever the tile."""
+    desc = ModelDesc()
+    sd = synthetic_state_dict(desc, 0)
+    rt = Runtime(desc, sd, "cuda:0", model_cost_autocast="none")
+    rng = np.random.default_rng(12)
+    emb = _t(rng.standard_normal((64, 3, desc.dim)))
+    goal = _t(rng.standard_normal((64, 1, desc.dim)))
+    cand = _t(rng.standard_normal((64, 300, 5, desc.action_dim)))
+    big = rt.model_cost(emb, goal, cand)
+    one = rt.model_cost(emb[5:6], goal[5:6], cand[5:6])
+    rt.sync()
+    assert torch.equal(big[5:6], one)
+    want = lo.get_cost_from_embeddings(emb[5:6].cpu().numpy(), goal[5:6].cpu().numpy(), cand[5:6].cpu().numpy(),
+                                       sd, desc)
+    assert cost_stats(one.cpu().numpy(), want)["allclose"]
+    rt.close()
