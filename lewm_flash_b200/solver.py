@@ -12,6 +12,8 @@
   iCEM with every feature off, plus its receding-horizon warm start.
 * ``B200CEMGDSolver`` is ``CEMGDSolver`` (``lewm/solvers/cem_gd.py:38-711``): the seed
   search as one device plan, the gradient refinement on the device gradient.
+* ``B200ICEMStaticSolver`` is ``ICEMStaticCompileSolver``
+  (``lewm/solvers/icem_static_compile.py:117-373``): the static chain is the device plan.
 * ``run_static_icem_chain`` mirrors the reference tensor-only chain
   (``lewm/solvers/icem_static_compile.py:61-114``) with injected noise.
 * ``B200ModelCost`` / ``install_model_cost`` replace
@@ -34,6 +36,7 @@ from __future__ import annotations
 import math
 import time
 import warnings
+from dataclasses import dataclass
 from typing import Any, Optional, Sequence
 
 import numpy as np
@@ -364,6 +367,72 @@ class B200ICEMSolver:
                 for cb in self.callbacks:
                     cb(**kw)
                 prev_mean, prev_var = m, v
+
+
+@dataclass
+class StaticChainWarmupResult:
+    """``StaticChainWarmupResult`` (reference ``lewm/solvers/icem_static_compile.py:19-26``)."""
+
+    enabled: bool
+    elapsed_s: Optional[float]
+    sample_counts: list
+    mode: str
+    fullgraph: bool
+    input_shapes: Optional[dict]
+
+
+class B200ICEMStaticSolver(B200ICEMSolver):
+    """``ICEMStaticCompileSolver`` (reference ``lewm/solvers/icem_static_compile.py:117-373``) on
+    the B200 kernels. The reference moves the candidate / model-cost / top-k / refit chain into a
+    tensor-only function run eagerly or under ``torch.compile``; here that chain is always the
+    device plan (one CUDA graph per plan shape), so ``static_chain_compile`` only selects what
+    ``warmup_static_chain_compile`` reports, as in the reference. Same extra arguments and
+    ``ValueError``, and ``solve`` adds the reference's ``static_chain`` record."""
+
+    def __init__(self, *args: Any, static_chain_compile: bool = False, static_chain_mode: str = "reduce-overhead",
+                 static_chain_fullgraph: bool = False, static_chain_warmup: bool = True, **kwargs: Any) -> None:
+        super().__init__(*args, **kwargs)
+        if static_chain_mode not in {"default", "reduce-overhead", "max-autotune"}:
+            raise ValueError("static_chain_mode must be one of 'default', 'reduce-overhead', or 'max-autotune', "
+                             f"got {static_chain_mode!r}")
+        self.static_chain_compile = bool(static_chain_compile)
+        self.static_chain_mode = static_chain_mode
+        self.static_chain_fullgraph = bool(static_chain_fullgraph)
+        self.static_chain_warmup = bool(static_chain_warmup)
+        self._static_compile_warmed = False
+
+    def warmup_static_chain_compile(self, *, embed_dim: int, history: int = 1,
+                                    batch_size: int | None = None) -> StaticChainWarmupResult:
+        """Plan once on zero inputs of the given shape, capturing the plan's CUDA graph
+        (``warmup_static_chain_compile``, ``icem_static_compile.py:246-315``)."""
+        counts = self.sample_counts()
+        if not self.static_chain_compile or not self.static_chain_warmup:
+            return StaticChainWarmupResult(False, None, counts, self.static_chain_mode, self.static_chain_fullgraph,
+                                           None)
+        bs = int(batch_size or self.batch_size)
+        emb = torch.zeros(bs, history, embed_dim, device=self.device, dtype=self.dtype)
+        goal = torch.zeros_like(emb)
+        mean = torch.zeros(bs, self.horizon, self.action_dim, device=self.device, dtype=self.dtype)
+        var = self.var_scale * torch.ones_like(mean)
+        started = time.perf_counter()
+        with torch.inference_mode():
+            self.runtime.plan(self.plan_options(), emb, goal, mean, var, action_low=self._action_low,
+                              action_high=self._action_high)
+        torch.cuda.synchronize(self.device)
+        self._static_compile_warmed = True
+        return StaticChainWarmupResult(
+            True, time.perf_counter() - started, counts, self.static_chain_mode, self.static_chain_fullgraph,
+            {"emb": list(emb.shape), "goal_emb": list(goal.shape), "mean": list(mean.shape), "var": list(var.shape),
+             "noise_steps": [[bs, n, self.horizon, self.action_dim] for n in counts]})
+
+    def solve(self, info_dict: dict, init_action: torch.Tensor | None = None) -> dict[str, Any]:
+        outputs = super().solve(info_dict, init_action)
+        outputs["static_chain"] = {
+            "static_chain_compile": self.static_chain_compile, "static_chain_mode": self.static_chain_mode,
+            "static_chain_fullgraph": self.static_chain_fullgraph, "static_chain_warmed": self._static_compile_warmed,
+            "sample_counts_per_step": self.sample_counts(),
+        }
+        return outputs
 
 
 class B200CEMSolver(B200ICEMSolver):

@@ -254,3 +254,31 @@ def test_model_cost_follows_the_models_autocast_mode(env):
     finally:
         env.model.set_model_cost_autocast("none")
     assert torch.equal(env.model.get_cost_from_embeddings(*args), f32)
+
+
+@pytest.mark.gpu
+def test_static_solver_matches_reference_static_solver(env):
+    """B200ICEMStaticSolver against ICEMStaticCompileSolver (eager static chain,
+    lewm/solvers/icem_static_compile.py:317-373) on the same noise, with a warmed graph."""
+    from lewm_flash_b200.solver import B200ICEMStaticSolver
+
+    n_envs, cfg = 3, SimpleNamespace(horizon=T, action_block=BLOCK)
+    kw = dict(ICEM_KW, return_best_elite=False)
+    ref = env.ref.static.ICEMStaticCompileSolver(model=env.model, device=env.dev, **kw)
+    twin = env.ref.static.ICEMStaticCompileSolver(model=env.model, device=env.dev, **kw)
+    b200 = B200ICEMStaticSolver(env.model, device=env.dev, static_chain_compile=True, **kw)
+    for s in (ref, twin, b200):
+        s.configure(action_space=Box(n_envs), n_envs=n_envs, config=cfg)
+    b200.noise_source = twin._sample_noise
+    warm = b200.warmup_static_chain_compile(embed_dim=192, history=1, batch_size=n_envs)
+    assert warm.enabled and warm.sample_counts == ref.sample_counts()
+    out_ref = ref.solve(_info(n_envs, 1, env.dev, 17))
+    out_dev = b200.solve(_info(n_envs, 1, env.dev, 17))
+    assert set(out_dev) == set(out_ref)
+    _close(out_dev["actions"], out_ref["actions"])
+    _close(out_dev["var"][0], out_ref["var"][0])
+    np.testing.assert_allclose(out_dev["costs"], out_ref["costs"], rtol=1e-5)
+    sc_dev, sc_ref = dict(out_dev["static_chain"]), dict(out_ref["static_chain"])
+    assert sc_dev.pop("static_chain_warmed") and not sc_ref.pop("static_chain_warmed")
+    assert sc_dev.pop("static_chain_compile") and not sc_ref.pop("static_chain_compile")
+    assert sc_dev == sc_ref

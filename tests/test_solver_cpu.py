@@ -156,3 +156,28 @@ def test_cem_gd_solver_schedule_and_surface_match_reference(kw):
 
 
 COLORED = {"none": 0.0, "pink": 1.0, "brown": 2.0}
+
+
+def test_static_solver_surface_matches_reference():
+    """B200ICEMStaticSolver: ICEMStaticCompileSolver's extra arguments, ValueError and the
+    disabled-warmup record (lewm/solvers/icem_static_compile.py:117-258)."""
+    from lewm_flash_b200.solver import B200ICEMStaticSolver
+
+    _ref()
+    from lewm.solvers.icem_static_compile import ICEMStaticCompileSolver
+
+    with pytest.raises(ValueError) as want:
+        ICEMStaticCompileSolver(model=None, static_chain_mode="fast")
+    with pytest.raises(ValueError) as got:
+        B200ICEMStaticSolver(None, static_chain_mode="fast")
+    assert str(got.value) == str(want.value)
+    kw = dict(num_samples=300, topk=30, sample_decay=1.25, sample_count_bucket_size=60, static_chain_mode="default")
+    ref = ICEMStaticCompileSolver(model=None, **kw)
+    dev = B200ICEMStaticSolver(None, **kw)
+    cfg = SimpleNamespace(horizon=5, action_block=5)
+    for s in (ref, dev):
+        s.configure(action_space=Box(1), n_envs=1, config=cfg)
+    assert dev.sample_counts() == ref.sample_counts()
+    r, d = ref.warmup_static_chain_compile(embed_dim=192), dev.warmup_static_chain_compile(embed_dim=192)
+    assert (d.enabled, d.elapsed_s, d.sample_counts, d.mode, d.fullgraph, d.input_shapes) == (
+        r.enabled, r.elapsed_s, r.sample_counts, r.mode, r.fullgraph, r.input_shapes)
