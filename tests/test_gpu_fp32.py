@@ -215,3 +215,28 @@ def test_fp32_costs_do_not_depend_on_the_batch():
                                        sd, desc)
     assert cost_stats(one.cpu().numpy(), want)["allclose"]
     rt.close()
+
+
+def test_fp32_profile_and_per_sample_embeddings():
+    """lewm_profile_plan reports a float32 plan's model costs under one class (fp32_cost, with
+    the canonical GEMM FLOPs of the rows it runs); per-candidate embeddings (rank 4, all equal)
+    give the same costs and gradients as per-env ones."""
+    desc = ModelDesc()
+    sd = synthetic_state_dict(desc, 0)
+    rt = Runtime(desc, sd, "cuda:0", model_cost_autocast="none")
+    rng = np.random.default_rng(13)
+    emb = _t(rng.standard_normal((2, 1, desc.dim)))
+    goal = _t(rng.standard_normal((2, 1, desc.dim)))
+    mean, std = torch.zeros(2, 5, 10, device="cuda:0"), torch.ones(2, 5, 10, device="cuda:0")
+    prof = rt.profile_plan(PlanOptions(num_samples=64, topk=8, n_steps=3), emb, goal, mean, std)
+    assert set(prof["classes"]) == {"fp32_cost", "sample", "refit"}, prof["classes"].keys()
+    f32 = prof["classes"]["fp32_cost"]
+    assert f32["launches"] == 3 and f32["ms"] > 0 and f32["flops"] > 0
+    cand = _t(rng.standard_normal((2, 12, 5, desc.action_dim)))
+    emb4 = emb[:, None].expand(2, 12, 1, desc.dim).contiguous()
+    c3, g3 = rt.model_cost_grad(emb, goal, cand)
+    c4, g4 = rt.model_cost_grad(emb4, goal, cand)
+    rt.sync()
+    assert torch.equal(c3, c4) and torch.equal(g3, g4)
+    assert torch.equal(rt.model_cost(emb4, goal, cand), c3)
+    rt.close()
