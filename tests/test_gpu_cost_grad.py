@@ -230,3 +230,19 @@ def test_b200_cem_gd_solver_matches_reference_solver(seed_solver, source):
     print(f"{seed_solver}/{source}: costs {np.round(np.asarray(got['costs']), 3).tolist()}, accepted "
           f"{gs['gd_accept_count']} of {gs['gd_candidate_count']}, {int((~close).sum())} of {close.numel()} action "
           f"coordinates beyond 1e-4")
+
+
+@pytest.mark.parametrize("H,T,B,S", [(3, 3, 2, 5), (1, 1, 1, 4), (2, 7, 1, 3)])
+def test_gradient_edge_shapes_match_oracle(rt, H, T, B, S):
+    """A single predictor call (H = T, the window already full), a one-step horizon, and a
+    horizon of 7 (a sliding window for five calls) against the float64 oracle."""
+    rng = np.random.default_rng(100 + 10 * H + T)
+    emb = rng.standard_normal((B, H, FULL_DESC.dim)).astype(np.float32)
+    goal = rng.standard_normal((B, 1, FULL_DESC.dim)).astype(np.float32)
+    cand = rng.standard_normal((B, S, T, FULL_DESC.action_dim)).astype(np.float32)
+    cost, grad = rt.model_cost_grad(_t(emb), _t(goal), _t(cand))
+    rt.sync()
+    c64, g64 = cg.cost_and_grad(emb, goal, cand, synthetic_state_dict(FULL_DESC, FULL_WEIGHT_SEED), FULL_DESC)
+    np.testing.assert_allclose(cost.cpu().numpy(), c64, rtol=1e-5, atol=1e-5)
+    err = np.abs(grad.cpu().numpy() - g64).max() / max(np.abs(g64).max(), 1e-30)
+    assert err <= GRAD_TOL, err
