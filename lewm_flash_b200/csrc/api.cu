@@ -587,17 +587,19 @@ lewm_status ensure_ws(lewm_ctx* c, const WsReq& need_in) {
 }
 
 // The fused call kernel (tile_call.cu) covers width 192 / 16 heads / MLP 768 / 6 layers
-// without a pred_proj head, a window full from the first call (history >= window = 3),
-// observation embeddings per env, and calls of at least LEWM_TILE_CALL_MIN candidates
-// (default 8000, where it overtakes the per-layer kernels: measured 641 -> 696 plans/s at
-// 64 envs, 669 -> 844 at 256 envs; 0 disables it).
-bool use_tile_call(const lewm_ctx* c, int NC, int H, int HS, int emb_pc) {
+// without a pred_proj head, calls whose window of 3 is full (history index H + k >= 3 at
+// call k: every call when H >= 3, the later calls of a history-1 or -2 rollout, whose
+// earlier growing-window calls stay on the per-layer kernels), observation embeddings per
+// env, and calls of at least LEWM_TILE_CALL_MIN candidates (default 8000, where it
+// overtakes the per-layer kernels: measured 641 -> 696 plans/s at 64 envs, 669 -> 844 at 256
+// envs; 0 disables it).
+bool use_tile_call(const lewm_ctx* c, int NC, int H, int HS, int emb_pc, int call) {
   const int min_cand = c->tile_call_min;
   const ModelDims& m = c->md;
   if (min_cand == 0) return false;
   const int need = min_cand > 0 ? min_cand : 8000;
-  return m.D == 192 && m.heads == 16 && m.mlp == 768 && m.pp_hidden == 0 && m.frames >= 3 && HS == 3 && H >= 3 &&
-         !emb_pc && c->w.w1s != nullptr && NC >= need;
+  return m.D == 192 && m.heads == 16 && m.mlp == 768 && m.pp_hidden == 0 && m.frames >= 3 && HS == 3 &&
+         H + call >= 3 && !emb_pc && c->w.w1s != nullptr && NC >= need;
 }
 
 // Algorithmic FLOPs of one model-cost evaluation: the GEMMs over the rows each computes
@@ -634,35 +636,41 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
                 c->ws.pred, costs, c->ws.kvc, kv_positions(H, HS),
                 m.pp_hidden ? c->ws.pp_in : nullptr, m.pp_hidden ? c->ws.pp_out : nullptr};
   const int n_calls = T - H + 1;
-  if (use_tile_call(c, NC, H, HS, emb_pc)) {
-    // Batched regime: one fused kernel per predictor call (all layers per row tile).
+  // Batched regime: one fused kernel per predictor call with a full window (all layers per
+  // row tile); it builds its layer-0 rows from the embeddings and the earlier predictions.
+  auto tile_call = [&](int k) -> lewm_status {
+    TileCallParams tp{};
+    tp.n_cand = NC;
+    tp.S = S;
+    tp.T = T;
+    tp.H = H;
+    tp.start = H + k - 3;
+    tp.call = k;
+    tp.last = k == n_calls - 1 ? 1 : 0;
+    tp.npred = n_calls;
+    tp.layers = m.L;
+    tp.goal_per_cand = goal_pc;
+    tp.emb = emb;
+    tp.goal = goal;
+    tp.mod = c->ws.mod;
+    tp.pred = c->ws.pred;
+    tp.costs = costs;
+    tp.status = c->d_status;
+    c->prof.begin(st);
+    const cudaError_t te = launch_tile_call(c->w, tp, st);
+    if (te != cudaSuccess) {
+      char info[256];
+      tile_call_describe(info, sizeof info);
+      return fail(c, LEWM_CUDA_ERROR, "fused call kernel launch: %s (%s)", cudaGetErrorString(te), info);
+    }
+    c->prof.end(KC_TILE_CALL, 2.0 * NC * 3 * m.L * (double)(m.D * 3 * m.inner + m.inner * m.D + 2 * m.D * m.mlp),
+                st);
+    return LEWM_OK;
+  };
+  if (use_tile_call(c, NC, H, HS, emb_pc, 0)) {  // every call
     for (int k = 0; k < n_calls; ++k) {
-      TileCallParams tp{};
-      tp.n_cand = NC;
-      tp.S = S;
-      tp.T = T;
-      tp.H = H;
-      tp.start = H + k - 3;
-      tp.call = k;
-      tp.last = k == n_calls - 1 ? 1 : 0;
-      tp.npred = n_calls;
-      tp.layers = m.L;
-      tp.goal_per_cand = goal_pc;
-      tp.emb = emb;
-      tp.goal = goal;
-      tp.mod = c->ws.mod;
-      tp.pred = c->ws.pred;
-      tp.costs = costs;
-      tp.status = c->d_status;
-      c->prof.begin(st);
-      const cudaError_t te = launch_tile_call(c->w, tp, st);
-      if (te != cudaSuccess) {
-        char info[256];
-        tile_call_describe(info, sizeof info);
-        return fail(c, LEWM_CUDA_ERROR, "fused call kernel launch: %s (%s)", cudaGetErrorString(te), info);
-      }
-      c->prof.end(KC_TILE_CALL, 2.0 * NC * 3 * m.L * (double)(m.D * 3 * m.inner + m.inner * m.D + 2 * m.D * m.mlp),
-                  st);
+      const lewm_status ts = tile_call(k);
+      if (ts != LEWM_OK) return ts;
     }
     return LEWM_OK;
   }
@@ -743,6 +751,11 @@ lewm_status run_model_cost(lewm_ctx* c, const float* emb, int emb_pc, int H, con
     return g;
   };
   for (int k = 0; k < n_calls; ++k) {
+    if (use_tile_call(c, NC, H, HS, emb_pc, k)) {  // a full window from this call on
+      const lewm_status ts = tile_call(k);
+      if (ts != LEWM_OK) return ts;
+      continue;
+    }
     CallGeom g = geom(k);
     if (k + 1 < n_calls) {
       const CallGeom gn = geom(k + 1);
