@@ -420,6 +420,36 @@ def model_cost_case(S, repeat, envs=1, mode="bf16"):
     return 0
 
 
+def plan_case(envs: int, repeat: int, history: int = 3) -> int:
+    """``--plan N``: `repeat` bucketed iCEM plans (the bench's settings) of N envs with history 3,
+    in-kernel noise: a fixed launch sequence for ncu captures of the sampling and top-k / refit
+    kernels at a known geometry."""
+    import torch
+
+    from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
+    from lewm_flash_b200.runtime import Runtime
+
+    dev = torch.device("cuda", 0)
+    rt = Runtime(ModelDesc(), synthetic_state_dict(ModelDesc(), 0), dev)
+    rng = np.random.default_rng(7)
+    emb = torch.as_tensor(rng.standard_normal((envs, history, 192)), dtype=torch.float32, device=dev)
+    goal = torch.as_tensor(rng.standard_normal((envs, 1, 192)), dtype=torch.float32, device=dev)
+    mean = torch.zeros(envs, 5, 10, device=dev)
+    std = torch.ones(envs, 5, 10, device=dev)
+    ms = []
+    for i in range(repeat):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        rt.plan(plan_options(), emb, goal, mean, std, plan_index=9000 + i)
+        b.record()
+        torch.cuda.synchronize(dev)
+        ms.append(a.elapsed_time(b))
+    rt.sync()
+    print(json.dumps({"case": "plan", "envs": envs, "history": history, "ms": ms}))
+    return 0
+
+
 def encoder_case(n_img: int, repeat: int) -> int:
     """``--encoder N``: N images through the observation encoder, `repeat` times (for ncu)."""
     import torch
@@ -483,6 +513,8 @@ def main() -> int:
     ap.add_argument("--encoder", type=int, default=0, metavar="N",
                     help="profiling case: run the observation encoder R times on N 224 px images and exit; "
                          "no bench line")
+    ap.add_argument("--plan", type=int, default=0, metavar="N",
+                    help="profiling case: --repeat plans of N envs (history 3) and exit")
     ap.add_argument("--envs", type=int, default=1)
     ap.add_argument("--mode", default="bf16", choices=["bf16", "fp32", "grad"],
                     help="--model-cost arithmetic: bf16, fp32 or the float32 gradient")
@@ -492,6 +524,8 @@ def main() -> int:
         return model_cost_case(args.model_cost, args.repeat, args.envs, args.mode)
     if args.encoder:
         return encoder_case(args.encoder, args.repeat)
+    if args.plan:
+        return plan_case(args.plan, args.repeat)
 
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
