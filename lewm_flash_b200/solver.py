@@ -298,9 +298,9 @@ class B200ICEMSolver:
                 steps[step].append(self.noise_source(bs, n).to(device=self.device, dtype=torch.float32))
         return [torch.cat(chunks, dim=0) for chunks in steps]
 
-    def _plan(self, info_dict: dict, mean: torch.Tensor, var: torch.Tensor, trace: bool):
+    def _plan(self, info_dict: dict, mean: torch.Tensor, var: torch.Tensor, trace: bool, emb_goal=None):
         total_envs = mean.shape[0]
-        emb, goal = self._cost_embeddings(info_dict, total_envs)
+        emb, goal = emb_goal if emb_goal is not None else self._cost_embeddings(info_dict, total_envs)
         rt = self.runtime
         opts = self.plan_options()
         plan_index = self._solves
@@ -781,7 +781,7 @@ class B200CEMGDSolver(B200ICEMSolver):
             mean = mean.to(self.device)
             var = var.to(self.device)
             emb, goal = self._cost_embeddings(info_dict, total_envs)
-            _, std, _, tr = self._plan(info_dict, mean, var, trace=True)
+            _, std, _, tr = self._plan(info_dict, mean, var, trace=True, emb_goal=(emb, goal))
         # Clone out of inference mode: the refinement needs ordinary tensors.
         emb, goal = emb.detach().clone(), goal.detach().clone()
         last = self.n_steps - 1
