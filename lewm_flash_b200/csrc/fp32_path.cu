@@ -206,18 +206,30 @@ __global__ void k_col_affine_gelu32(float* __restrict__ X, size_t n, int width, 
 }
 
 // Causal window attention (scale 1/8, softmax over the window's positions <= the row's):
-// one warp per (row, head), rows = candidate * w + position; qkv rows [3 * inner].
-__global__ void __launch_bounds__(256) k_attn32(const float* __restrict__ qkv, int rows, int w, int heads,
-                                                float* __restrict__ out) {
+// one warp per (row, head); qkv rows [3 * inner]. A call runs rpc rows per candidate, the
+// window positions pos0 .. pos0 + rpc - 1 (row = candidate * rpc + position - pos0); the
+// keys / values of the positions before pos0 come from the cache kv [candidate][kv_pos]
+// [k inner | v inner] of this layer (a growing-window call whose earlier positions the calls
+// before ran with the same inputs).
+__global__ void __launch_bounds__(256) k_attn32(const float* __restrict__ qkv, int rows, int rpc, int pos0, int heads,
+                                                const float* __restrict__ kv, int kv_pos, float* __restrict__ out) {
   const int item = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (item >= rows * heads) return;
   const int r = item / heads, h = item % heads;
-  const int inner = heads * 64, pos = r % w, base = r - pos;
+  const int inner = heads * 64, cand = r / rpc, pos = pos0 + r % rpc, base = r - (pos - pos0);
   const float* q = qkv + (size_t)r * 3 * inner + h * 64;
+  auto key = [&](int j) {
+    return j < pos0 ? kv + ((size_t)cand * kv_pos + j) * 2 * inner + h * 64
+                    : qkv + (size_t)(base + j - pos0) * 3 * inner + inner + h * 64;
+  };
+  auto val = [&](int j) {
+    return j < pos0 ? kv + ((size_t)cand * kv_pos + j) * 2 * inner + inner + h * 64
+                    : qkv + (size_t)(base + j - pos0) * 3 * inner + 2 * inner + h * 64;
+  };
   float s[8];
   float mx = -INFINITY;
   for (int j = 0; j <= pos; ++j) {
-    const float* k = qkv + (size_t)(base + j) * 3 * inner + inner + h * 64;
+    const float* k = key(j);
     const float d = warp_sum(q[lane] * k[lane] + q[32 + lane] * k[32 + lane]) * 0.125f;
     s[j] = d;
     mx = fmaxf(mx, d);
@@ -229,7 +241,7 @@ __global__ void __launch_bounds__(256) k_attn32(const float* __restrict__ qkv, i
   }
   float o0 = 0.f, o1 = 0.f;
   for (int j = 0; j <= pos; ++j) {
-    const float* v = qkv + (size_t)(base + j) * 3 * inner + 2 * inner + h * 64;
+    const float* v = val(j);
     o0 = fmaf(s[j], v[lane], o0);
     o1 = fmaf(s[j], v[32 + lane], o1);
   }
@@ -238,14 +250,28 @@ __global__ void __launch_bounds__(256) k_attn32(const float* __restrict__ qkv, i
   dst[32 + lane] = o1 / den;
 }
 
-// Layer-0 rows of one call: x[cand * w + p] = history entry (observation embedding or an
-// earlier prediction) + position embedding p; row_tok = the token's modulation row.
-__global__ void k_rows_init32(const float* __restrict__ emb, int emb_per_cand, const float* __restrict__ pred,
-                              const float* __restrict__ pos, int n_cand, int S, int T, int H, int w, int start,
-                              int npred, int D, float* __restrict__ X, int* __restrict__ row_tok) {
+// The keys / values of this call's rows at window positions below kv_pos into the cache
+// kv [candidate][kv_pos][k inner | v inner] (one block per row).
+__global__ void k_kv_store32(const float* __restrict__ qkv, int rows, int rpc, int pos0, int inner, int kv_pos,
+                             float* __restrict__ kv) {
   const int r = blockIdx.x;
-  if (r >= n_cand * w) return;
-  const int cand = r / w, p = r % w, j = start + p;
+  if (r >= rows) return;
+  const int cand = r / rpc, pos = pos0 + r % rpc;
+  if (pos >= kv_pos) return;
+  const float* src = qkv + (size_t)r * 3 * inner + inner;
+  float* dst = kv + ((size_t)cand * kv_pos + pos) * 2 * inner;
+  for (int c = threadIdx.x; c < 2 * inner; c += blockDim.x) dst[c] = src[c];
+}
+
+// Layer-0 rows of one call: x[cand * rpc + p - pos0] = history entry (observation embedding
+// or an earlier prediction) + position embedding p for the window positions p = pos0 ..
+// pos0 + rpc - 1 the call runs; row_tok = the token's modulation row.
+__global__ void k_rows_init32(const float* __restrict__ emb, int emb_per_cand, const float* __restrict__ pred,
+                              const float* __restrict__ pos, int n_cand, int S, int T, int H, int rpc, int pos0,
+                              int start, int npred, int D, float* __restrict__ X, int* __restrict__ row_tok) {
+  const int r = blockIdx.x;
+  if (r >= n_cand * rpc) return;
+  const int cand = r / rpc, p = pos0 + r % rpc, j = start + p;
   const float* src = j < H ? emb + ((size_t)(emb_per_cand ? cand : cand / S) * H + j) * D
                            : pred + ((size_t)cand * npred + (j - H)) * D;
   for (int c = threadIdx.x; c < D; c += blockDim.x) X[(size_t)r * D + c] = src[c] + pos[p * D + c];
@@ -468,13 +494,22 @@ cudaError_t run_model_cost_fp32(const ModelDims& m, const F32Weights& w, const F
     F32_TRY(sgemm<GE_BIAS>(ws.sact, D, w.layers[l].ada_w, D, w.layers[l].ada_b, ws.mod + l * 6 * D, mod_ld, NT,
                            6 * D, st));
   const int n_calls = T - H + 1;
+  // Growing-window key / value cache (no tape): while the window only grows, a call's
+  // earlier positions have the inputs, and so the outputs, of the call before (causal
+  // attention, fixed positions), so the call runs only its new last position and reads the
+  // earlier keys / values from the cache the calls before wrote: the same bits as running
+  // the whole window. The taped forward runs every window row (its reverse pass needs them).
+  const int kv_pos = (!tape && H + 1 <= HS) ? HS - 1 : 0;
   for (int k = 0; k < n_calls; ++k) {
     const int end = H + k, start = end > HS ? end - HS : 0, wlen = end - start;
-    const int rows = NC * wlen;
+    const bool kv_read = kv_pos > 0 && k >= 1 && end <= HS;
+    const bool kv_write = kv_pos > 0 && k + 1 < n_calls && end + 1 <= HS;
+    const int rpc = kv_read ? 1 : wlen, pos0 = wlen - rpc;
+    const int rows = NC * rpc;
     const F32TapeCall* tc = tape ? &tape->calls[k] : nullptr;
     int* row_tok = tc ? tc->row_tok : ws.row_tok;
     const size_t RD = (size_t)rows * D;
-    k_rows_init32<<<rows, 64, 0, st>>>(emb, emb_pc, ws.pred, w.pos, NC, S, T, H, wlen, start, n_calls, D, ws.x,
+    k_rows_init32<<<rows, 64, 0, st>>>(emb, emb_pc, ws.pred, w.pos, NC, S, T, H, rpc, pos0, start, n_calls, D, ws.x,
                                        row_tok);
     F32_TRY(cudaGetLastError());
     const int lnb = (rows + 7) / 8;
@@ -486,7 +521,12 @@ cudaError_t run_model_cost_fp32(const ModelDims& m, const F32Weights& w, const F
       k_ln_mod32<<<lnb, 256, 0, st>>>(ws.x, rows, D, row_tok, ws.mod, mod_ld, mo, mo + D, lw.attn_ln_w, lw.attn_ln_b,
                                       ws.a);
       F32_TRY(sgemm<GE_BIAS>(ws.a, D, lw.qkv_w, D, nullptr, qkv, 3 * inner, rows, 3 * inner, st));
-      k_attn32<<<(rows * m.heads + 7) / 8, 256, 0, st>>>(qkv, rows, wlen, m.heads, ws.att);
+      float* kv_l = ws.kv + (size_t)l * NC * kv_pos * 2 * inner;
+      if (kv_write) {
+        k_kv_store32<<<rows, 128, 0, st>>>(qkv, rows, rpc, pos0, inner, kv_pos, kv_l);
+        F32_TRY(cudaGetLastError());
+      }
+      k_attn32<<<(rows * m.heads + 7) / 8, 256, 0, st>>>(qkv, rows, rpc, pos0, m.heads, kv_l, kv_pos, ws.att);
       F32_TRY(sgemm<GE_RESID>(ws.att, inner, lw.out_w, inner, lw.out_b, ws.x, D, rows, D, st, ws.mod, row_tok, mod_ld,
                               mo + 2 * D, tc ? tc->o + l * RD : nullptr, ws.part, kSplitK));
       if (tc) F32_TRY(cudaMemcpyAsync(tc->x_mid + l * RD, ws.x, RD * 4, cudaMemcpyDeviceToDevice, st));
@@ -498,7 +538,7 @@ cudaError_t run_model_cost_fp32(const ModelDims& m, const F32Weights& w, const F
                               mo + 5 * D, tc ? tc->f2 + l * RD : nullptr, ws.part, kSplitK));
     }
     if (tc) F32_TRY(cudaMemcpyAsync(tc->x_out, ws.x, RD * 4, cudaMemcpyDeviceToDevice, st));
-    k_final_ln32<<<(NC + 7) / 8, 256, 0, st>>>(ws.x, NC, wlen, D, w.fin_w, w.fin_b, ws.y);
+    k_final_ln32<<<(NC + 7) / 8, 256, 0, st>>>(ws.x, NC, rpc, D, w.fin_w, w.fin_b, ws.y);
     F32_TRY(cudaGetLastError());
     if (m.pp_hidden) {  // pred_proj MLP head on the new predictions (lewm/jepa.py:106-114)
       const int P = m.pp_hidden;
@@ -1051,6 +1091,7 @@ void f32_layout(const ModelDims& m, size_t NC, size_t T, F&& f) {
   f(11, al(NC * (size_t)m.pp_hidden));
   f(12, al(NW));  // row_tok (int32)
   f(13, al((size_t)kSplitK * NW * m.D));  // split-K partial sums
+  f(14, al((size_t)m.L * NC * (m.frames - 1) * 2 * m.inner));  // growing-window key / value cache
 }
 }  // namespace
 
@@ -1061,7 +1102,7 @@ size_t f32_work_floats(const ModelDims& m, size_t n_cand, size_t T) {
 }
 
 F32Work f32_work_carve(const ModelDims& m, size_t n_cand, size_t T, float* base) {
-  float* p[14];
+  float* p[15];
   size_t off = 0;
   f32_layout(m, n_cand, T, [&](int i, size_t k) {
     p[i] = base + off;
@@ -1082,6 +1123,7 @@ F32Work f32_work_carve(const ModelDims& m, size_t n_cand, size_t T, float* base)
   w.pph = p[11];
   w.row_tok = reinterpret_cast<int*>(p[12]);
   w.part = p[13];
+  w.kv = p[14];
   return w;
 }
 

@@ -342,6 +342,7 @@ struct F32Work {
   float* pph;              // [NC][P] pred_proj hidden rows
   int* row_tok;            // [NC*w] modulation row (candidate * T + history index) of each row
   float* part;             // [4][NC*w][D] split-K partial sums of the gated-residual GEMMs
+  float* kv;               // [L][NC][HS-1][2 inner] keys / values of growing-window positions
 };
 // Floats of F32Work for n_cand candidates, horizon T, window <= frames (pointers into one block).
 size_t f32_work_floats(const ModelDims& m, size_t n_cand, size_t T);
