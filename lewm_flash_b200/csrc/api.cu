@@ -1046,7 +1046,8 @@ lewm_status lewm_create(lewm_ctx** out, const lewm_model_desc* desc, const float
   c->md = md;
   // Small calls spread over about two thirds of one QKV wave (SMs / heads): the SMs
   // left free let the next kernel's CTAs launch early and prefetch their weights
-  // (measured on B200: 6 tiles 24.2 ms/plan, 9 tiles 25.6 ms, 3 tiles 24.9 ms).
+  // (measured on B200, the 1-env 300-sample plan: 6 tiles 18.25 ms, 4 tiles 19.42 ms,
+  // 8 tiles 19.04 ms, 3 tiles 19.70 ms, 12 tiles 22.83 ms).
   c->tile_target = std::max(1, prop.multiProcessorCount / md.heads * 2 / 3);
   c->sm_count = prop.multiProcessorCount;
   if (const char* tt = std::getenv("LEWM_TILE_TARGET")) {  // tuning override
