@@ -240,3 +240,31 @@ def test_fp32_profile_and_per_sample_embeddings():
     assert torch.equal(c3, c4) and torch.equal(g3, g4)
     assert torch.equal(rt.model_cost(emb4, goal, cand), c3)
     rt.close()
+
+
+@pytest.mark.parametrize("seed", range(8))
+def test_fp32_random_shapes_match_oracle(seed):
+    """Seeded random geometries (history 1-4, horizon up to 7, history window 1-3, per-env or
+    per-candidate embeddings): the float32 costs against the oracle at the 1e-5 gate, and the
+    gradient's costs equal to the forward's bit for bit."""
+    rng = np.random.default_rng(1000 + seed)
+    desc = ModelDesc()
+    sd = synthetic_state_dict(desc, 0)
+    rt = _SHARED.setdefault("rt", Runtime(desc, sd, "cuda:0", model_cost_autocast="none"))
+    H = int(rng.integers(1, 5))
+    T = int(rng.integers(H, 8))
+    hs = int(rng.integers(1, 4))
+    B, S = int(rng.integers(1, 4)), int(rng.integers(1, 40))
+    emb = rng.standard_normal((B, H, desc.dim)).astype(np.float32)
+    goal = rng.standard_normal((B, 1, desc.dim)).astype(np.float32)
+    cand = rng.standard_normal((B, S, T, desc.action_dim)).astype(np.float32)
+    got = rt.model_cost(_t(emb), _t(goal), _t(cand), history_size=hs)
+    g_cost, _ = rt.model_cost_grad(_t(emb), _t(goal), _t(cand), history_size=hs)
+    rt.sync()
+    want = lo.get_cost_from_embeddings(emb, goal, cand, sd, desc, history_size=hs)
+    st = cost_stats(got.cpu().numpy(), want)
+    assert st["allclose"], (H, T, hs, B, S, st)
+    assert torch.equal(got, g_cost), (H, T, hs)
+
+
+_SHARED = {}
