@@ -14,6 +14,38 @@
 #include "lewm_common.cuh"
 #include "lewm_internal.h"
 
+#define F32_TRY(x)                            \
+  do {                                        \
+    const cudaError_t e_ = (x);               \
+    if (e_ != cudaSuccess) return e_;         \
+  } while (0)
+
+namespace lewm {
+namespace {
+// Launch of a float32-path kernel. As a programmatic dependent launch (unless LEWM_NO_PDL=1 or
+// LEWM_FP32_PDL=0) the grid is set up while the kernel before drains; every kernel waits for
+// its predecessor (griddepcontrol.wait) before its first access and never triggers early, so
+// the next grid's CTAs take no SM slots while this one runs.
+bool fp32_pdl() {
+  static const bool on = [] {
+    const char* v = std::getenv("LEWM_FP32_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on && pdl_enabled();
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch_f32(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  if (fp32_pdl()) return launch_k(kern, grid, block, smem, st, std::forward<Args>(args)...);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+}  // namespace
+}  // namespace lewm
+
 namespace lewm {
 namespace {
 
@@ -45,6 +77,7 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
                                                      int M, int N, const float* __restrict__ mod,
                                                      const int* __restrict__ row_tok, int mod_ld, int gate_off,
                                                      float* __restrict__ save, int kc, float* __restrict__ part) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   __shared__ __align__(16) float sA[GB_K][GB_M + 4];
   __shared__ __align__(16) float sW[GB_K][GB_N + 4];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -163,6 +196,7 @@ __global__ void __launch_bounds__(256) k_ln_mod32(const float* __restrict__ X, i
                                                   const int* __restrict__ row_tok, const float* __restrict__ mod,
                                                   int mod_ld, int shift_off, int scale_off, const float* __restrict__ g,
                                                   const float* __restrict__ b, float* __restrict__ out) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (r >= rows) return;
   const float* x = X + (size_t)r * D;
@@ -184,6 +218,7 @@ __global__ void __launch_bounds__(256) k_ln_mod32(const float* __restrict__ X, i
 // the pred_proj head's LayerNorm over its hidden width.
 __global__ void __launch_bounds__(256) k_row_ln32(float* __restrict__ X, int rows, int width, float eps,
                                                   const float* __restrict__ g, const float* __restrict__ b, int gelu) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (r >= rows) return;
   float* x = X + (size_t)r * width;
@@ -199,6 +234,7 @@ __global__ void __launch_bounds__(256) k_row_ln32(float* __restrict__ X, int row
 // x = scale . x + shift per column, then GELU (the folded eval BatchNorm1d of a pred_proj head).
 __global__ void k_col_affine_gelu32(float* __restrict__ X, size_t n, int width, const float* __restrict__ scale,
                                     const float* __restrict__ shift) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const int c = (int)(i % width);
     X[i] = gelu_erf(X[i] * scale[c] + shift[c]);
@@ -213,6 +249,7 @@ __global__ void k_col_affine_gelu32(float* __restrict__ X, size_t n, int width, 
 // before ran with the same inputs).
 __global__ void __launch_bounds__(256) k_attn32(const float* __restrict__ qkv, int rows, int rpc, int pos0, int heads,
                                                 const float* __restrict__ kv, int kv_pos, float* __restrict__ out) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   const int item = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (item >= rows * heads) return;
   const int r = item / heads, h = item % heads;
@@ -254,6 +291,7 @@ __global__ void __launch_bounds__(256) k_attn32(const float* __restrict__ qkv, i
 // kv [candidate][kv_pos][k inner | v inner] (one block per row).
 __global__ void k_kv_store32(const float* __restrict__ qkv, int rows, int rpc, int pos0, int inner, int kv_pos,
                              float* __restrict__ kv) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   const int r = blockIdx.x;
   if (r >= rows) return;
   const int cand = r / rpc, pos = pos0 + r % rpc;
@@ -269,6 +307,7 @@ __global__ void k_kv_store32(const float* __restrict__ qkv, int rows, int rpc, i
 __global__ void k_rows_init32(const float* __restrict__ emb, int emb_per_cand, const float* __restrict__ pred,
                               const float* __restrict__ pos, int n_cand, int S, int T, int H, int rpc, int pos0,
                               int start, int npred, int D, float* __restrict__ X, int* __restrict__ row_tok) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   const int r = blockIdx.x;
   if (r >= n_cand * rpc) return;
   const int cand = r / rpc, p = pos0 + r % rpc, j = start + p;
@@ -282,6 +321,7 @@ __global__ void k_rows_init32(const float* __restrict__ emb, int emb_per_cand, c
 __global__ void __launch_bounds__(256) k_final_ln32(const float* __restrict__ X, int n_cand, int w, int D,
                                                     const float* __restrict__ g, const float* __restrict__ b,
                                                     float* __restrict__ y) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   const int cand = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (cand >= n_cand) return;
   const float* x = X + ((size_t)cand * w + w - 1) * D;
@@ -294,6 +334,7 @@ __global__ void __launch_bounds__(256) k_final_ln32(const float* __restrict__ X,
 __global__ void __launch_bounds__(256) k_emit32(const float* __restrict__ y, int n_cand, int D, int last, int call,
                                                 int npred, float* __restrict__ pred, const float* __restrict__ goal,
                                                 int goal_per_cand, int S, float* __restrict__ costs) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   const int cand = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (cand >= n_cand) return;
   const float* yr = y + (size_t)cand * D;
@@ -324,6 +365,7 @@ __global__ void __launch_bounds__(G_THREADS, 2) k_sgemm_wide(const float* __rest
                                                           const float* __restrict__ W, int K,
                                                           const float* __restrict__ bias, float* __restrict__ C,
                                                           int ldc, int M, int N, float* __restrict__ save) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   __shared__ __align__(16) float sA[GB_K][GL_M + 4];
   __shared__ __align__(16) float sW[GB_K][GL_N + 4];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -422,6 +464,7 @@ __global__ void k_splitk_resid32(const float* __restrict__ part, int splits, int
                                  const float* __restrict__ bias, float* __restrict__ X, int ldc,
                                  const float* __restrict__ mod, const int* __restrict__ row_tok, int mod_ld,
                                  int gate_off, float* __restrict__ save) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   const size_t n_out = (size_t)M * N;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_out; i += (size_t)gridDim.x * blockDim.x) {
     const int m = (int)(i / N), n = (int)(i % N);
@@ -445,9 +488,11 @@ cudaError_t sgemm(const float* A, int lda, const float* W, int K, const float* b
       const bool v = K % 4 == 0 && lda % 4 == 0 &&
                      (reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W)) % 16 == 0;
       if (v)
-        k_sgemm_wide<EPI, true><<<wide, G_THREADS, 0, st>>>(A, lda, W, K, bias, C, ldc, M, N, save);
+        F32_TRY(launch_f32(k_sgemm_wide<EPI, true>, dim3(wide), dim3(G_THREADS), 0, st, A, lda, W, K, bias, C, ldc, M,
+                         N, save));
       else
-        k_sgemm_wide<EPI, false><<<wide, G_THREADS, 0, st>>>(A, lda, W, K, bias, C, ldc, M, N, save);
+        F32_TRY(launch_f32(k_sgemm_wide<EPI, false>, dim3(wide), dim3(G_THREADS), 0, st, A, lda, W, K, bias, C, ldc, M,
+                         N, save));
       return cudaGetLastError();
     }
   }
@@ -457,26 +502,21 @@ cudaError_t sgemm(const float* A, int lda, const float* W, int K, const float* b
   float* pp = nz > 1 ? part : nullptr;
   const bool vec = K % 4 == 0 && lda % 4 == 0 && (reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W)) % 16 == 0;
   if (vec)
-    k_sgemm<EPI, true><<<grid, G_THREADS, 0, st>>>(A, lda, W, K, bias, C, ldc, M, N, mod, row_tok, mod_ld, gate_off,
-                                                   save, kc, pp);
+    F32_TRY(launch_f32(k_sgemm<EPI, true>, dim3(grid), dim3(G_THREADS), 0, st, A, lda, W, K, bias, C, ldc, M, N, mod,
+                     row_tok, mod_ld, gate_off, save, kc, pp));
   else
-    k_sgemm<EPI, false><<<grid, G_THREADS, 0, st>>>(A, lda, W, K, bias, C, ldc, M, N, mod, row_tok, mod_ld, gate_off,
-                                                    save, kc, pp);
+    F32_TRY(launch_f32(k_sgemm<EPI, false>, dim3(grid), dim3(G_THREADS), 0, st, A, lda, W, K, bias, C, ldc, M, N, mod,
+                     row_tok, mod_ld, gate_off, save, kc, pp));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || !pp) return e;
   const size_t n_out = (size_t)M * N;
   const int blocks = (int)std::min<size_t>((n_out + 255) / 256, 148 * 16);
-  k_splitk_resid32<<<blocks, 256, 0, st>>>(pp, nz, M, N, bias, C, ldc, mod, row_tok, mod_ld, gate_off, save);
+  F32_TRY(launch_f32(k_splitk_resid32, dim3(blocks), dim3(256), 0, st, pp, nz, M, N, bias, C, ldc, mod, row_tok,
+                   mod_ld, gate_off, save));
   return cudaGetLastError();
 }
 
 }  // namespace
-
-#define F32_TRY(x)                            \
-  do {                                        \
-    const cudaError_t e_ = (x);               \
-    if (e_ != cudaSuccess) return e_;         \
-  } while (0)
 
 cudaError_t run_model_cost_fp32(const ModelDims& m, const F32Weights& w, const F32Work& ws, const float* emb,
                                 int emb_pc, int H, const float* goal, int goal_pc, const float* cand, int B, int S,
@@ -509,52 +549,51 @@ cudaError_t run_model_cost_fp32(const ModelDims& m, const F32Weights& w, const F
     const F32TapeCall* tc = tape ? &tape->calls[k] : nullptr;
     int* row_tok = tc ? tc->row_tok : ws.row_tok;
     const size_t RD = (size_t)rows * D;
-    k_rows_init32<<<rows, 64, 0, st>>>(emb, emb_pc, ws.pred, w.pos, NC, S, T, H, rpc, pos0, start, n_calls, D, ws.x,
-                                       row_tok);
-    F32_TRY(cudaGetLastError());
+    F32_TRY(launch_f32(k_rows_init32, dim3(rows), dim3(64), 0, st, emb, emb_pc, ws.pred, w.pos, NC, S, T, H, rpc, pos0,
+                     start, n_calls, D, ws.x, row_tok));
     const int lnb = (rows + 7) / 8;
     for (int l = 0; l < L; ++l) {  // ConditionalBlock (lewm/module.py:88-111)
       const F32Layer& lw = w.layers[l];
       const int mo = l * 6 * D;  // shift_msa | scale_msa | gate_msa | shift_mlp | scale_mlp | gate_mlp
       float* qkv = tc ? tc->qkv + (size_t)l * rows * 3 * inner : ws.qkv;
       if (tc) F32_TRY(cudaMemcpyAsync(tc->x_in + l * RD, ws.x, RD * 4, cudaMemcpyDeviceToDevice, st));
-      k_ln_mod32<<<lnb, 256, 0, st>>>(ws.x, rows, D, row_tok, ws.mod, mod_ld, mo, mo + D, lw.attn_ln_w, lw.attn_ln_b,
-                                      ws.a);
+      F32_TRY(launch_f32(k_ln_mod32, dim3(lnb), dim3(256), 0, st, ws.x, rows, D, row_tok, ws.mod, mod_ld, mo, mo + D,
+                       lw.attn_ln_w, lw.attn_ln_b, ws.a));
       F32_TRY(sgemm<GE_BIAS>(ws.a, D, lw.qkv_w, D, nullptr, qkv, 3 * inner, rows, 3 * inner, st));
       float* kv_l = ws.kv + (size_t)l * NC * kv_pos * 2 * inner;
       if (kv_write) {
-        k_kv_store32<<<rows, 128, 0, st>>>(qkv, rows, rpc, pos0, inner, kv_pos, kv_l);
-        F32_TRY(cudaGetLastError());
+        F32_TRY(launch_f32(k_kv_store32, dim3(rows), dim3(128), 0, st, qkv, rows, rpc, pos0, inner, kv_pos, kv_l));
       }
-      k_attn32<<<(rows * m.heads + 7) / 8, 256, 0, st>>>(qkv, rows, rpc, pos0, m.heads, kv_l, kv_pos, ws.att);
+      F32_TRY(launch_f32(k_attn32, dim3((rows * m.heads + 7) / 8), dim3(256), 0, st, qkv, rows, rpc, pos0, m.heads,
+                       kv_l, kv_pos, ws.att));
       F32_TRY(sgemm<GE_RESID>(ws.att, inner, lw.out_w, inner, lw.out_b, ws.x, D, rows, D, st, ws.mod, row_tok, mod_ld,
                               mo + 2 * D, tc ? tc->o + l * RD : nullptr, ws.part, kSplitK));
       if (tc) F32_TRY(cudaMemcpyAsync(tc->x_mid + l * RD, ws.x, RD * 4, cudaMemcpyDeviceToDevice, st));
-      k_ln_mod32<<<lnb, 256, 0, st>>>(ws.x, rows, D, row_tok, ws.mod, mod_ld, mo + 3 * D, mo + 4 * D, lw.ffn_ln_w,
-                                      lw.ffn_ln_b, ws.a);
+      F32_TRY(launch_f32(k_ln_mod32, dim3(lnb), dim3(256), 0, st, ws.x, rows, D, row_tok, ws.mod, mod_ld, mo + 3 * D,
+                       mo + 4 * D, lw.ffn_ln_w, lw.ffn_ln_b, ws.a));
       F32_TRY(sgemm<GE_GELU>(ws.a, D, lw.w1, D, lw.b1, ws.hid, m.mlp, rows, m.mlp, st, nullptr, nullptr, 0, 0,
                              tc ? tc->f1 + (size_t)l * rows * m.mlp : nullptr));
       F32_TRY(sgemm<GE_RESID>(ws.hid, m.mlp, lw.w2, m.mlp, lw.b2, ws.x, D, rows, D, st, ws.mod, row_tok, mod_ld,
                               mo + 5 * D, tc ? tc->f2 + l * RD : nullptr, ws.part, kSplitK));
     }
     if (tc) F32_TRY(cudaMemcpyAsync(tc->x_out, ws.x, RD * 4, cudaMemcpyDeviceToDevice, st));
-    k_final_ln32<<<(NC + 7) / 8, 256, 0, st>>>(ws.x, NC, rpc, D, w.fin_w, w.fin_b, ws.y);
-    F32_TRY(cudaGetLastError());
+    F32_TRY(launch_f32(k_final_ln32, dim3((NC + 7) / 8), dim3(256), 0, st, ws.x, NC, rpc, D, w.fin_w, w.fin_b, ws.y));
     if (m.pp_hidden) {  // pred_proj MLP head on the new predictions (lewm/jepa.py:106-114)
       const int P = m.pp_hidden;
       if (m.pp_norm == 1) {
         F32_TRY(sgemm<GE_BIAS>(ws.y, D, w.pp_w1, D, w.pp_b1, ws.pph, P, NC, P, st));
-        k_row_ln32<<<(NC + 7) / 8, 256, 0, st>>>(ws.pph, NC, P, 1e-5f, w.pp_ln_g, w.pp_ln_b, 1);
+        F32_TRY(launch_f32(k_row_ln32, dim3((NC + 7) / 8), dim3(256), 0, st, ws.pph, NC, P, 1e-5f, w.pp_ln_g,
+                         w.pp_ln_b, 1));
       } else {
         F32_TRY(sgemm<GE_BIAS>(ws.y, D, w.pp_w1, D, nullptr, ws.pph, P, NC, P, st));
-        k_col_affine_gelu32<<<1024, 256, 0, st>>>(ws.pph, (size_t)NC * P, P, w.pp_scale, w.pp_shift);
+        F32_TRY(launch_f32(k_col_affine_gelu32, dim3(1024), dim3(256), 0, st, ws.pph, (size_t)NC * P, P, w.pp_scale,
+                         w.pp_shift));
       }
       F32_TRY(cudaGetLastError());
       F32_TRY(sgemm<GE_BIAS>(ws.pph, P, w.pp_w2, P, w.pp_b2, ws.y, D, NC, D, st));
     }
-    k_emit32<<<(NC + 7) / 8, 256, 0, st>>>(ws.y, NC, D, k == n_calls - 1 ? 1 : 0, k, n_calls, ws.pred, goal, goal_pc,
-                                           S, costs);
-    F32_TRY(cudaGetLastError());
+    F32_TRY(launch_f32(k_emit32, dim3((NC + 7) / 8), dim3(256), 0, st, ws.y, NC, D, k == n_calls - 1 ? 1 : 0, k,
+                     n_calls, ws.pred, goal, goal_pc, S, costs));
     if (tape && k == n_calls - 1)
       F32_TRY(cudaMemcpyAsync(tape->y, ws.y, (size_t)NC * D * 4, cudaMemcpyDeviceToDevice, st));
   }
@@ -593,6 +632,7 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm_nn(const float* __restrict_
                                                         int Nin, int Kout, float* __restrict__ C, int ldc, int M,
                                                         const float* __restrict__ pre, int ldp, int kc,
                                                         float* __restrict__ part) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   __shared__ __align__(16) float sA[GB_K][GB_M + 4];
   __shared__ __align__(16) float sB[GB_K][GB_N + 4];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -692,6 +732,7 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm_nn(const float* __restrict_
 template <int EPI>
 __global__ void k_splitk_nn32(const float* __restrict__ part, int splits, int M, int Kout, float* __restrict__ C,
                               int ldc, const float* __restrict__ pre, int ldp) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   const size_t n_out = (size_t)M * Kout;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_out; i += (size_t)gridDim.x * blockDim.x) {
     const int m = (int)(i / Kout), c = (int)(i % Kout);
@@ -723,14 +764,16 @@ cudaError_t sgemm_nn(const float* A, int lda, const float* Bm, int Nin, int Kout
   const bool vec = Nin % 4 == 0 && lda % 4 == 0 && Kout % 4 == 0 &&
                    (reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(Bm)) % 16 == 0;
   if (vec)
-    k_sgemm_nn<EPI, true><<<grid, G_THREADS, 0, st>>>(A, lda, Bm, Nin, Kout, C, ldc, M, pre, ldp, kc, pp);
+    F32_TRY(launch_f32(k_sgemm_nn<EPI, true>, dim3(grid), dim3(G_THREADS), 0, st, A, lda, Bm, Nin, Kout, C, ldc, M,
+                     pre, ldp, kc, pp));
   else
-    k_sgemm_nn<EPI, false><<<grid, G_THREADS, 0, st>>>(A, lda, Bm, Nin, Kout, C, ldc, M, pre, ldp, kc, pp);
+    F32_TRY(launch_f32(k_sgemm_nn<EPI, false>, dim3(grid), dim3(G_THREADS), 0, st, A, lda, Bm, Nin, Kout, C, ldc, M,
+                     pre, ldp, kc, pp));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || !pp) return e;
   const size_t n_out = (size_t)M * Kout;
   const int blocks = (int)std::min<size_t>((n_out + 255) / 256, 148 * 16);
-  k_splitk_nn32<EPI><<<blocks, 256, 0, st>>>(pp, nz, M, Kout, C, ldc, pre, ldp);
+  F32_TRY(launch_f32(k_splitk_nn32<EPI>, dim3(blocks), dim3(256), 0, st, pp, nz, M, Kout, C, ldc, pre, ldp));
   return cudaGetLastError();
 }
 
@@ -738,6 +781,7 @@ cudaError_t sgemm_nn(const float* A, int lda, const float* Bm, int Nin, int Kout
 __global__ void __launch_bounds__(256) k_seed32(const float* __restrict__ y, const float* __restrict__ goal,
                                                 int goal_per_cand, int S, const float* __restrict__ weights,
                                                 int n_cand, int D, float* __restrict__ dY) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n_cand * D) return;
   const int cand = i / D, c = i % D;
@@ -750,6 +794,7 @@ __global__ void __launch_bounds__(256) k_seed32(const float* __restrict__ y, con
 __global__ void __launch_bounds__(256) k_final_ln_bwd32(const float* __restrict__ X, int n_cand, int w, int D,
                                                         const float* __restrict__ g, const float* __restrict__ dy,
                                                         int dy_ld, float* __restrict__ dX) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   const int cand = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (cand >= n_cand) return;
   const size_t row = (size_t)cand * w + w - 1;
@@ -776,6 +821,7 @@ __global__ void __launch_bounds__(256) k_final_ln_bwd32(const float* __restrict_
 __global__ void k_gate_bwd32(const float* __restrict__ dX, const float* __restrict__ F, const int* __restrict__ row_tok,
                              const float* __restrict__ mod, float* __restrict__ dmod, int mod_ld, int gate_off,
                              int rows, int D, float* __restrict__ dF) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   const size_t n = (size_t)rows * D;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const int r = (int)(i / D), c = (int)(i % D);
@@ -795,6 +841,7 @@ __global__ void __launch_bounds__(256) k_ln_mod_bwd32(const float* __restrict__ 
                                                       const float* __restrict__ mod, float* __restrict__ dmod,
                                                       int mod_ld, int shift_off, int scale_off,
                                                       const float* __restrict__ g, float* __restrict__ dX) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   constexpr int D = NV * 32;
   const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (r >= rows) return;
@@ -855,6 +902,7 @@ __global__ void __launch_bounds__(256) k_ln_mod_bwd32(const float* __restrict__ 
 // dq = 1/8 sum_j dS_j k_j, dk_j += 1/8 dS_j q, dv_j += P_j dO with dS_j = P_j (dP_j - sum P dP).
 __global__ void __launch_bounds__(256) k_attn_bwd32(const float* __restrict__ qkv, const float* __restrict__ dO,
                                                     int n_cand, int w, int heads, float* __restrict__ dQKV) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   const int item = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (item >= n_cand * heads) return;
   const int cand = item / heads, hd = item % heads, inner = heads * 64, ld = 3 * inner;
@@ -920,6 +968,7 @@ __global__ void __launch_bounds__(256) k_attn_bwd32(const float* __restrict__ qk
 // j >= H) pass their gradient to that prediction, dpred[cand][j - H] += dX[row].
 __global__ void k_hist_bwd32(const float* __restrict__ dX, int n_cand, int w, int start, int H, int npred, int D,
                              float* __restrict__ dpred) {
+  griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   const int r = blockIdx.x;
   if (r >= n_cand * w) return;
   const int cand = r / w, j = start + r % w;
@@ -933,9 +982,11 @@ cudaError_t ln_mod_bwd(int D, const float* X, const float* dA, int rows, const i
                        cudaStream_t st) {
   const int blocks = (rows + 7) / 8;
   if (D == 192)
-    k_ln_mod_bwd32<6><<<blocks, 256, 0, st>>>(X, dA, rows, row_tok, mod, dmod, mod_ld, shift_off, scale_off, g, dX);
+    F32_TRY(launch_f32(k_ln_mod_bwd32<6>, dim3(blocks), dim3(256), 0, st, X, dA, rows, row_tok, mod, dmod, mod_ld,
+                     shift_off, scale_off, g, dX));
   else if (D == 384)
-    k_ln_mod_bwd32<12><<<blocks, 256, 0, st>>>(X, dA, rows, row_tok, mod, dmod, mod_ld, shift_off, scale_off, g, dX);
+    F32_TRY(launch_f32(k_ln_mod_bwd32<12>, dim3(blocks), dim3(256), 0, st, X, dA, rows, row_tok, mod, dmod, mod_ld,
+                     shift_off, scale_off, g, dX));
   else
     return cudaErrorInvalidValue;
   return cudaGetLastError();
@@ -955,43 +1006,38 @@ cudaError_t run_model_cost_grad_fp32(const ModelDims& m, const F32Weights& w, co
   F32_TRY(run_model_cost_fp32(m, w, ws, emb, emb_pc, H, goal, goal_pc, cand, B, S, T, HS, costs, st, &tape));
   F32_TRY(cudaMemsetAsync(gw.dmod, 0, (size_t)NT * mod_ld * 4, st));
   F32_TRY(cudaMemsetAsync(gw.dpred, 0, (size_t)NC * n_calls * D * 4, st));
-  k_seed32<<<(NC * D + 255) / 256, 256, 0, st>>>(tape.y, goal, goal_pc, S, cost_weights, NC, D, gw.dY);
-  F32_TRY(cudaGetLastError());
+  F32_TRY(launch_f32(k_seed32, dim3((NC * D + 255) / 256), dim3(256), 0, st, tape.y, goal, goal_pc, S, cost_weights,
+                   NC, D, gw.dY));
   for (int k = n_calls - 1; k >= 0; --k) {  // calls in reverse: later windows read earlier predictions
     const F32TapeCall& tc = tape.calls[k];
     const int R = tc.rows;
     const size_t RD = (size_t)R * D;
     F32_TRY(cudaMemsetAsync(gw.dX, 0, RD * 4, st));
     const bool last = k == n_calls - 1;
-    k_final_ln_bwd32<<<(NC + 7) / 8, 256, 0, st>>>(tc.x_out, NC, tc.w, D, w.fin_w, last ? gw.dY : gw.dpred + (size_t)k * D,
-                                                   last ? D : n_calls * D, gw.dX);
-    F32_TRY(cudaGetLastError());
+    F32_TRY(launch_f32(k_final_ln_bwd32, dim3((NC + 7) / 8), dim3(256), 0, st, tc.x_out, NC, tc.w, D, w.fin_w,
+                     last ? gw.dY : gw.dpred + (size_t)k * D, last ? D : n_calls * D, gw.dX));
     for (int l = L - 1; l >= 0; --l) {
       const F32Layer& lw = w.layers[l];
       const int mo = l * 6 * D;
       // x += gate_mlp . FFN(a2): FFN(a2) = GELU(a2 W1^T + b1) W2^T + b2
-      k_gate_bwd32<<<ew_blocks(RD), 256, 0, st>>>(gw.dX, tc.f2 + l * RD, tc.row_tok, ws.mod, gw.dmod, mod_ld,
-                                                  mo + 5 * D, R, D, gw.dF);
-      F32_TRY(cudaGetLastError());
+      F32_TRY(launch_f32(k_gate_bwd32, dim3(ew_blocks(RD)), dim3(256), 0, st, gw.dX, tc.f2 + l * RD, tc.row_tok,
+                       ws.mod, gw.dmod, mod_ld, mo + 5 * D, R, D, gw.dF));
       F32_TRY(sgemm_nn<NE_GELU_BWD>(gw.dF, D, lw.w2, D, mlp, gw.dF1, mlp, R, st, gw, tc.f1 + (size_t)l * R * mlp,
                                     mlp));
       F32_TRY(sgemm_nn<NE_STORE>(gw.dF1, mlp, lw.w1, mlp, D, gw.dA, D, R, st, gw));
       F32_TRY(ln_mod_bwd(D, tc.x_mid + l * RD, gw.dA, R, tc.row_tok, ws.mod, gw.dmod, mod_ld, mo + 3 * D, mo + 4 * D,
                          lw.ffn_ln_w, gw.dX, st));
       // x += gate_msa . (attention(a) W_out^T + b_out), attention over q | k | v = a W_qkv^T
-      k_gate_bwd32<<<ew_blocks(RD), 256, 0, st>>>(gw.dX, tc.o + l * RD, tc.row_tok, ws.mod, gw.dmod, mod_ld,
-                                                  mo + 2 * D, R, D, gw.dF);
-      F32_TRY(cudaGetLastError());
+      F32_TRY(launch_f32(k_gate_bwd32, dim3(ew_blocks(RD)), dim3(256), 0, st, gw.dX, tc.o + l * RD, tc.row_tok, ws.mod,
+                       gw.dmod, mod_ld, mo + 2 * D, R, D, gw.dF));
       F32_TRY(sgemm_nn<NE_STORE>(gw.dF, D, lw.out_w, D, inner, gw.dAtt, inner, R, st, gw));
-      k_attn_bwd32<<<(NC * m.heads + 7) / 8, 256, 0, st>>>(tc.qkv + (size_t)l * R * 3 * inner, gw.dAtt, NC, tc.w,
-                                                            m.heads, gw.dQKV);
-      F32_TRY(cudaGetLastError());
+      F32_TRY(launch_f32(k_attn_bwd32, dim3((NC * m.heads + 7) / 8), dim3(256), 0, st,
+                       tc.qkv + (size_t)l * R * 3 * inner, gw.dAtt, NC, tc.w, m.heads, gw.dQKV));
       F32_TRY(sgemm_nn<NE_STORE>(gw.dQKV, 3 * inner, lw.qkv_w, 3 * inner, D, gw.dA, D, R, st, gw));
       F32_TRY(ln_mod_bwd(D, tc.x_in + l * RD, gw.dA, R, tc.row_tok, ws.mod, gw.dmod, mod_ld, mo, mo + D,
                          lw.attn_ln_w, gw.dX, st));
     }
-    k_hist_bwd32<<<R, 64, 0, st>>>(gw.dX, NC, tc.w, tc.start, H, n_calls, D, gw.dpred);
-    F32_TRY(cudaGetLastError());
+    F32_TRY(launch_f32(k_hist_bwd32, dim3(R), dim3(64), 0, st, gw.dX, NC, tc.w, tc.start, H, n_calls, D, gw.dpred));
   }
   // mod = SiLU(e) W_ada^T + b_ada for every layer; e = SiLU(h1) W_e2^T + b_e2; h1 = a1 W_e1^T + b_e1;
   // a1 = cand W_conv^T + b_conv (Embedder, lewm/module.py:205-214).
