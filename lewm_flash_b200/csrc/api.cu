@@ -446,11 +446,16 @@ lewm_status upload_f32_weights(lewm_ctx* c, const float* wts, size_t n) {
     take(&w.pp_b2, D);
   }
   if (src != n) return fail(c, LEWM_INVALID_ARG, "fp32 weight walk mismatch");
-  {  // every layer's adaLN weight stacked, [L * 6D][D], for the reverse pass's single GEMM
+  {  // every layer's adaLN weight and bias stacked, [L * 6D][D] and [L * 6D]: one GEMM for the
+     // modulation of all layers, and one for its reverse pass
     const size_t per = 6 * D * D, off = round_up(stage.size(), 4);
     stage.resize(off + per * m.L);
     for (int l = 0; l < m.L; ++l) std::memcpy(stage.data() + off + per * l, ada_src[l], per * 4);
     fix.emplace_back(&w.ada_stack, off);
+    const size_t offb = round_up(stage.size(), 4);
+    stage.resize(offb + 6 * D * m.L);
+    for (int l = 0; l < m.L; ++l) std::memcpy(stage.data() + offb + 6 * D * l, ada_src[l] + per, 6 * D * 4);
+    fix.emplace_back(&w.ada_b_stack, offb);
   }
   LEWM_CK(c, cudaMalloc(&c->d_w32, stage.size() * 4));
   LEWM_CK(c, cudaMemcpy(c->d_w32, stage.data(), stage.size() * 4, cudaMemcpyHostToDevice));

@@ -530,9 +530,9 @@ cudaError_t run_model_cost_fp32(const ModelDims& m, const F32Weights& w, const F
                          tape ? tape->h1 : nullptr));
   F32_TRY(sgemm<GE_SILU>(ws.eh, m.eh, w.e2_w, m.eh, w.e2_b, ws.sact, D, NT, D, st, nullptr, nullptr, 0, 0,
                          tape ? tape->e : nullptr));
-  for (int l = 0; l < L; ++l)  // AdaLN modulation of every token and layer
-    F32_TRY(sgemm<GE_BIAS>(ws.sact, D, w.layers[l].ada_w, D, w.layers[l].ada_b, ws.mod + l * 6 * D, mod_ld, NT,
-                           6 * D, st));
+  // AdaLN modulation of every token and layer: one GEMM over the stacked layer weights, whose
+  // output rows are the [L * 6D] modulation rows
+  F32_TRY(sgemm<GE_BIAS>(ws.sact, D, w.ada_stack, D, w.ada_b_stack, ws.mod, mod_ld, NT, mod_ld, st));
   const int n_calls = T - H + 1;
   // Growing-window key / value cache (no tape): while the window only grows, a call's
   // earlier positions have the inputs, and so the outputs, of the call before (causal

@@ -330,7 +330,8 @@ struct F32Weights {
   // shift = bias without a norm), second Linear.
   const float *pp_w1 = nullptr, *pp_b1 = nullptr, *pp_ln_g = nullptr, *pp_ln_b = nullptr;
   const float *pp_scale = nullptr, *pp_shift = nullptr, *pp_w2 = nullptr, *pp_b2 = nullptr;
-  const float* ada_stack = nullptr;  // [L * 6D][D]: every layer's adaLN Linear weight, stacked (reverse pass)
+  const float* ada_stack = nullptr;    // [L * 6D][D]: every layer's adaLN Linear weight, stacked
+  const float* ada_b_stack = nullptr;  // [L * 6D]: their biases
 };
 struct F32Work {
   float *act, *eh, *sact;  // [NC*T] x A' / eh / D: Embedder activations, sact = SiLU(action embedding)
