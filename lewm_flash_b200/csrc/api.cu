@@ -112,6 +112,7 @@ struct lewm_ctx {
   F32Weights w32;
   float* d_grad = nullptr;    // tape + gradient buffers of lewm_model_cost_grad
   size_t grad_floats = 0;
+  std::map<std::vector<int>, cudaGraphExec_t> grad_graphs;  // one executable graph per gradient shape
   MlpHead pp{};  // pred_proj MLP head (P == 0: Identity)
   uint32_t* d_status = nullptr;
   Workspace ws;
@@ -481,6 +482,8 @@ int window_tiles(int n_cand, int w, int target) {
 void clear_graphs(lewm_ctx* c) {
   for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
   c->graphs.clear();
+  for (auto& kv : c->grad_graphs) cudaGraphExecDestroy(kv.second);
+  c->grad_graphs.clear();
 }
 
 lewm_status ensure_ws(lewm_ctx* c, const WsReq& need_in) {
@@ -1146,6 +1149,8 @@ lewm_status lewm_model_cost_grad(lewm_ctx* c, const float* emb, int32_t emb_per_
   if (s != LEWM_OK) return s;
   const size_t nf = f32_grad_floats(c->md, NC, T, H, history_size);
   if (nf > c->grad_floats) {  // grows; cudaFree waits for the work that used the old buffers
+    for (auto& kv : c->grad_graphs) cudaGraphExecDestroy(kv.second);
+    c->grad_graphs.clear();
     if (c->d_grad) cudaFree(c->d_grad);
     c->d_grad = nullptr;
     c->grad_floats = 0;
@@ -1155,9 +1160,49 @@ lewm_status lewm_model_cost_grad(lewm_ctx* c, const float* emb, int32_t emb_per_
   F32Tape tape;
   F32GradWork gw{};
   f32_grad_carve(c->md, NC, T, H, history_size, c->d_grad, &tape, &gw);
-  LEWM_CK(c, run_model_cost_grad_fp32(c->md, c->w32, c->ws.f32, tape, gw, emb, emb_per_sample != 0, H, goal,
-                                      goal_per_sample != 0, cand, B, S, T, history_size, cost_weights, costs_out,
-                                      grad_out, st));
+  const bool emb_pc = emb_per_sample != 0, goal_pc = goal_per_sample != 0;
+  if (c->prof.on || !graphs_enabled()) {
+    LEWM_CK(c, run_model_cost_grad_fp32(c->md, c->w32, c->ws.f32, tape, gw, emb, emb_pc, H, goal, goal_pc, cand, B,
+                                        S, T, history_size, cost_weights, costs_out, grad_out, st));
+    return LEWM_OK;
+  }
+  // Graph path (the pass is ~640 small launches): stage the inputs into the gradient buffer so
+  // the captured pass is pointer-stable, replay the cached graph of this shape, copy out.
+  const ModelDims& m = c->md;
+  const size_t n_emb = (size_t)(emb_pc ? NC : B) * H * m.D, n_goal = (size_t)(goal_pc ? NC : B) * m.D;
+  const size_t n_cand = (size_t)NC * T * m.A;
+  cudaStream_t cs = c->cap_stream;
+  LEWM_CK(c, cudaEventRecord(c->ev_in, st));
+  LEWM_CK(c, cudaStreamWaitEvent(cs, c->ev_in, 0));
+  LEWM_CK(c, cudaMemcpyAsync(gw.in_emb, emb, n_emb * 4, cudaMemcpyDeviceToDevice, cs));
+  LEWM_CK(c, cudaMemcpyAsync(gw.in_goal, goal, n_goal * 4, cudaMemcpyDeviceToDevice, cs));
+  LEWM_CK(c, cudaMemcpyAsync(gw.in_cand, cand, n_cand * 4, cudaMemcpyDeviceToDevice, cs));
+  if (cost_weights) LEWM_CK(c, cudaMemcpyAsync(gw.in_w, cost_weights, (size_t)NC * 4, cudaMemcpyDeviceToDevice, cs));
+  const std::vector<int> key{B, S, T, H, history_size, emb_pc ? 1 : 0, goal_pc ? 1 : 0, cost_weights ? 1 : 0};
+  auto it = c->grad_graphs.find(key);
+  if (it == c->grad_graphs.end()) {
+    cudaGraph_t graph = nullptr;
+    LEWM_CK(c, cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+    const cudaError_t re = run_model_cost_grad_fp32(m, c->w32, c->ws.f32, tape, gw, gw.in_emb, emb_pc, H, gw.in_goal,
+                                                    goal_pc, gw.in_cand, B, S, T, history_size,
+                                                    cost_weights ? gw.in_w : nullptr, gw.out_cost, gw.out_grad, cs);
+    const cudaError_t ce = cudaStreamEndCapture(cs, &graph);
+    if (re != cudaSuccess || ce != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      return fail(c, LEWM_CUDA_ERROR, "gradient graph capture: %s",
+                  cudaGetErrorString(re != cudaSuccess ? re : ce));
+    }
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) return fail(c, LEWM_CUDA_ERROR, "gradient graph instantiate: %s", cudaGetErrorString(ie));
+    it = c->grad_graphs.emplace(key, exec).first;
+  }
+  LEWM_CK(c, cudaGraphLaunch(it->second, cs));
+  LEWM_CK(c, cudaMemcpyAsync(costs_out, gw.out_cost, (size_t)NC * 4, cudaMemcpyDeviceToDevice, cs));
+  LEWM_CK(c, cudaMemcpyAsync(grad_out, gw.out_grad, n_cand * 4, cudaMemcpyDeviceToDevice, cs));
+  LEWM_CK(c, cudaEventRecord(c->ev_out, cs));
+  LEWM_CK(c, cudaStreamWaitEvent(st, c->ev_out, 0));
   return LEWM_OK;
 }
 

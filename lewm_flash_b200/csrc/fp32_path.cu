@@ -1099,6 +1099,12 @@ size_t grad_walk(const ModelDims& m, int NC, int T, int H, int HS, float* base, 
   // produce rows of width D or A' <= D
   g.part_floats = (size_t)kMaxNnSplits * std::max(maxR, NT) * std::max<size_t>(D, m.As);
   g.part = take(g.part_floats);
+  g.in_emb = take((size_t)NC * H * D);  // per-candidate embeddings at most
+  g.in_goal = take((size_t)NC * D);
+  g.in_cand = take(NT * m.A);
+  g.in_w = take((size_t)NC);
+  g.out_cost = take((size_t)NC);
+  g.out_grad = take(NT * m.A);
   if (tape) *tape = std::move(t);
   if (gw) *gw = g;
   return off;

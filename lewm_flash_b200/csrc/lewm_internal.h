@@ -374,6 +374,9 @@ struct F32GradWork {
   float *dmod, *de, *dh1, *da1;             // [NC*T] x L*6D / D / eh / A'
   float* part;                              // split-reduction partial sums of the dY . W GEMMs
   size_t part_floats;
+  // staged inputs and outputs of a graph-replayed pass: emb, goal, candidates, cost weights,
+  // costs, gradient
+  float *in_emb, *in_goal, *in_cand, *in_w, *out_cost, *out_grad;
 };
 // Floats of the tape + gradient buffers of one evaluation; carve them from `base`.
 size_t f32_grad_floats(const ModelDims& m, int NC, int T, int H, int HS);
