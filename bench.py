@@ -507,6 +507,7 @@ def main() -> int:
     ap.add_argument("--no-sharded", action="store_true", help="skip the 1024-env sharded leg")
     ap.add_argument("--no-stress", action="store_true", help="skip the width-384 stress leg")
     ap.add_argument("--no-fp32", action="store_true", help="skip the float32 CEM and CEM-GD gradient legs")
+    ap.add_argument("--no-policy", action="store_true", help="skip the 100-env get_action leg")
     ap.add_argument("--model-cost", type=int, default=0, metavar="S",
                     help="profiling case: time R model-cost calls of S candidates per env (horizon 5; 1 env "
                          "with history 1, or --envs B with history 3) and exit; no bench line")
@@ -650,6 +651,9 @@ def main() -> int:
     # ---------------------------------------------------------------- observation encoder (64 images, 224 px)
     encoder = encoder_pass(dev, args.steps, args.warmup, flush)
 
+    # ---------------------------------------------------------------- policy get_action, 100 envs
+    policy = policy_pass(rt, dev) if not args.no_policy else None
+
     # ---------------------------------------------------------------- per-kernel-class timing pass (diagnostic, last)
     kinfo = kernel_class_pass(rt, opts, emb, goal, mean, std, dev)
     per_plan_launches = kinfo["launches_per_plan"]
@@ -677,6 +681,7 @@ def main() -> int:
         "sharded_h1": sharded_h1,
         "stress": stress,
         "encoder": encoder,
+        "policy": policy,
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_reference_gpu:
@@ -946,6 +951,59 @@ def cem_gd_pass(rt, dev, n_seeds=30, repeat=20):
     finally:
         torch.set_float32_matmul_precision(prev)
     return out
+
+
+def policy_pass(rt, dev, n_envs=100, replans=3):
+    """``get_action`` through ``B200PlanningPolicy`` for ``n_envs`` envs with the eval plan_config
+    (horizon 5, receding_horizon 5, action_block 5: one plan every 25 calls, history 1): uint8
+    224 px observation and goal frames from pinned host memory, the ViT-tiny encoder with the
+    image transform fused, one bucketed iCEM 300 plan of all envs, one device->host read of the
+    actions per plan. get_action returns host actions, so each call is timed on the host clock;
+    p50 / p90 over all calls (the definition of the reference README's get_action figures) and
+    the mean of the planning calls alone."""
+    import time
+
+    import torch
+
+    from lewm_flash_b200.encoder import B200Encoder, EncoderDesc, flat_weights, synthetic_weights
+    from lewm_flash_b200.policy import B200PlanningPolicy
+    from lewm_flash_b200.solver import B200ICEMSolver
+
+    desc = EncoderDesc()
+    vit, proj = synthetic_weights(desc, 0)
+    enc = B200Encoder(desc, flat_weights(vit, proj, desc), dev)
+    solver = B200ICEMSolver(rt, num_samples=300, n_steps=30, topk=30, elite_retention=3, colored_noise="brown",
+                            colored_noise_time="raw", sample_decay=1.25, sample_count_bucket_size=60, seed=0,
+                            history_size=1, device=dev)
+
+    class Box:
+        shape = (n_envs, 2)
+        low = -np.ones((n_envs, 2), np.float32)
+        high = np.ones((n_envs, 2), np.float32)
+
+    cfg = {"horizon": 5, "receding_horizon": 5, "action_block": 5}
+    policy = B200PlanningPolicy(solver, cfg, encoder=enc)
+    policy.set_env(type("Env", (), {"num_envs": n_envs, "action_space": Box()})())
+    rng = np.random.default_rng(23)
+    frames = [{k: torch.as_tensor(rng.integers(0, 256, (n_envs, 1, 224, 224, 3), dtype=np.uint8)).pin_memory()
+               for k in ("pixels", "goal")} for _ in range(2)]
+    per_plan = 25
+    for i in range(per_plan):  # warm-up cycle: graph capture, encoder and plan workspaces
+        policy.get_action(frames[i % 2])
+    ms, plan_ms, serve_ms = [], [], []
+    for i in range(replans * per_plan):
+        plans = policy.solves
+        t0 = time.perf_counter()
+        policy.get_action(frames[i % 2])
+        dt = (time.perf_counter() - t0) * 1e3
+        ms.append(dt)
+        (plan_ms if policy.solves > plans else serve_ms).append(dt)
+    del enc
+    return {"workload": f"get_action_{n_envs}env_icem_bucketed_300_h1_vit_tiny_224_u8", "envs": n_envs,
+            "calls": len(ms), "plans": len(plan_ms), "p50_ms": percentile(ms, 50), "p90_ms": percentile(ms, 90),
+            "plan_call_ms": float(np.mean(plan_ms)), "serve_call_p50_ms": percentile(serve_ms, 50),
+            "h2d_bytes_per_plan": int(2 * n_envs * 224 * 224 * 3),
+            "note": "host-clock time per get_action; planning calls encode obs + goal frames and plan all envs"}
 
 
 def encoder_pass(dev, steps, warmup, flush, n_img=64):
