@@ -887,11 +887,67 @@ def fp32_cem_pass(dev, steps, warmup, flush, n_envs=1):
     rt.close()
     p50 = percentile(ms, 50)
     flops = F_CANON * 300 * 30 * n_envs
-    return {"workload": "cem_300_30_30_1env_h1_fp32", "envs": n_envs, "plans_per_s": n_envs / (p50 / 1e3),
-            "p50_plan_ms": p50, "plans": len(ms), "tflops_fp32": flops / (p50 / 1e3) / 1e12,
-            "flops_per_plan": flops,
-            "note": "float32 CUDA-core model cost (no tensor cores); canonical FLOPs (window rows the "
-                    "bf16 path computes), the fp32 path recomputes full windows (~1.3x)"}
+    out = {"workload": "cem_300_30_30_1env_h1_fp32", "envs": n_envs, "plans_per_s": n_envs / (p50 / 1e3),
+           "p50_plan_ms": p50, "plans": len(ms), "tflops_fp32": flops / (p50 / 1e3) / 1e12,
+           "flops_per_plan": flops,
+           "note": "float32 CUDA-core model cost (no tensor cores); canonical FLOPs (window rows the "
+                   "bf16 path computes), the fp32 path recomputes full windows (~1.3x)"}
+    if n_envs == 1:
+        out["reference_gpu"] = reference_fp32_cem(dev)
+        if "eager_p50_ms" in out["reference_gpu"]:
+            out["reference_gpu"]["speedup"] = out["reference_gpu"]["eager_p50_ms"] / p50
+    return out
+
+
+def reference_fp32_cem(dev, plans=5, warmup=2):
+    """The reference's own CEMExactSolver.solve (baseline/_ref) for the same float32 plan on this
+    GPU: same weights and latents, model cost in float32 (the JEPA default "none"), float32
+    matmul precision "highest" (no TF32), one env, eager, CUDA events around each solve."""
+    from types import SimpleNamespace
+
+    import torch
+
+    ref = reference_package()
+    if ref is None:
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    from lewm.solvers.cem_exact import CEMExactSolver
+
+    prec = torch.get_float32_matmul_precision()
+    torch.set_float32_matmul_precision("highest")
+    try:
+        model, _ = reference_solver(ref, dev)
+        model.set_model_cost_autocast("none")
+        solver = CEMExactSolver(model=model, batch_size=1, num_samples=300, n_steps=30, topk=30, device=dev, seed=0)
+
+        class Box:
+            shape = (1, 2)
+            low = -np.inf * np.ones((1, 2), dtype=np.float32)
+            high = np.inf * np.ones((1, 2), dtype=np.float32)
+
+        solver.configure(action_space=Box(), n_envs=1, config=SimpleNamespace(horizon=5, action_block=5))
+        emb_np, goal_np = bench_latents(0)
+        emb = torch.as_tensor(emb_np, device=dev)
+        goal = torch.as_tensor(goal_np, device=dev)
+        ms = []
+        for i in range(warmup + plans):
+            info = {"emb": emb, "goal_emb": goal, "pixels": torch.zeros(1, 1, device=dev),
+                    "goal": torch.zeros(1, 1, device=dev)}
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize(dev)
+            a.record()
+            with torch.inference_mode():
+                quiet(solver.solve, info)
+            b.record()
+            torch.cuda.synchronize(dev)
+            if i >= warmup:
+                ms.append(a.elapsed_time(b))
+        del model, solver
+        torch.cuda.empty_cache()
+        return {"api": "reference CEMExactSolver.solve (baseline/_ref), float32 model cost, matmul precision "
+                       "highest, cached latents, 1 env, eager", "plans": plans, "eager_p50_ms": percentile(ms, 50)}
+    finally:
+        torch.set_float32_matmul_precision(prec)
 
 
 def cem_gd_pass(rt, dev, n_seeds=30, repeat=20):
