@@ -58,6 +58,12 @@ constexpr int kSplitK = 4;
 
 enum GemmEpi { GE_BIAS = 0, GE_SILU = 1, GE_GELU = 2, GE_RESID = 3 };
 
+// Column of element (k, r) in a transposed K slab [GB_K][rows + 4]: r XOR 4 ((k / 4) % 8).
+// The loaders write 4 consecutive k of one row per thread and 8 threads per row, so without
+// it a warp's 32 stores hit 8 banks (4-way conflicts); with it all 32 banks. The XOR keeps
+// groups of 4 columns together, so the inner loop's float4 reads stay whole.
+__device__ __forceinline__ int slab_col(int k, int r) { return r ^ (((k >> 2) & 7) << 2); }
+
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 
 // C[M x N] = A[M x K] . W[N x K]^T + bias, then the epilogue:
@@ -116,16 +122,16 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
         const int sl = tid + q * G_THREADS, r = sl >> 3, kk = (sl & 7) * 4;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          sA[kk + j][r] = ra[4 * q + j];
-          sW[kk + j][r] = rw[4 * q + j];
+          sA[kk + j][slab_col(kk + j, r)] = ra[4 * q + j];
+          sW[kk + j][slab_col(kk + j, r)] = rw[4 * q + j];
         }
       }
     } else {
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const int sl = tid + q * G_THREADS, r = sl >> 5, kk = sl & 31;
-        sA[kk][r] = ra[q];
-        sW[kk][r] = rw[q];
+        sA[kk][slab_col(kk, r)] = ra[q];
+        sW[kk][slab_col(kk, r)] = rw[q];
       }
     }
   };
@@ -138,8 +144,8 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
     if (more) load(k0 + GB_K);
 #pragma unroll
     for (int kk = 0; kk < GB_K; ++kk) {
-      const float4 a = *reinterpret_cast<const float4*>(&sA[kk][ty * 4]);
-      const float4 b = *reinterpret_cast<const float4*>(&sW[kk][tx * 4]);
+      const float4 a = *reinterpret_cast<const float4*>(&sA[kk][slab_col(kk, ty * 4)]);
+      const float4 b = *reinterpret_cast<const float4*>(&sW[kk][slab_col(kk, tx * 4)]);
       const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i)
@@ -671,16 +677,14 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm_nn(const float* __restrict_
         const int sl = tid + q * G_THREADS;
         const int r = sl >> 3, kk = (sl & 7) * 4, rr = sl >> 4, cc = (sl & 15) * 4;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          sA[kk + j][r] = ra[4 * q + j];
-          sB[rr][cc + j] = rb[4 * q + j];
-        }
+        for (int j = 0; j < 4; ++j) sA[kk + j][slab_col(kk + j, r)] = ra[4 * q + j];
+        *reinterpret_cast<float4*>(&sB[rr][cc]) = make_float4(rb[4 * q], rb[4 * q + 1], rb[4 * q + 2], rb[4 * q + 3]);
       }
     } else {
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const int sl = tid + q * G_THREADS;
-        sA[sl & 31][sl >> 5] = ra[q];
+        sA[sl & 31][slab_col(sl & 31, sl >> 5)] = ra[q];
         sB[sl >> 6][sl & 63] = rb[q];
       }
     }
@@ -694,7 +698,7 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm_nn(const float* __restrict_
     if (more) load(n0 + GB_K);
 #pragma unroll
     for (int kk = 0; kk < GB_K; ++kk) {
-      const float4 a = *reinterpret_cast<const float4*>(&sA[kk][ty * 4]);
+      const float4 a = *reinterpret_cast<const float4*>(&sA[kk][slab_col(kk, ty * 4)]);
       const float4 b = *reinterpret_cast<const float4*>(&sB[kk][tx * 4]);
       const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
