@@ -33,6 +33,15 @@ bool fp32_pdl() {
   }();
   return on && pdl_enabled();
 }
+// 64 x 32 GEMM tiles where 64 x 64 ones number fewer than the SMs (LEWM_FP32_NARROW=0: never;
+// the results are the same bits either way).
+bool narrow_tiles() {
+  static const bool on = [] {
+    const char* v = std::getenv("LEWM_FP32_NARROW");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 template <typename... KArgs, typename... Args>
 cudaError_t launch_f32(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
   if (fp32_pdl()) return launch_k(kern, grid, block, smem, st, std::forward<Args>(args)...);
@@ -71,39 +80,46 @@ __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + e
 //   GE_GELU  C = gelu(acc + bias)            GE_RESID X += gate . (acc + bias), in place,
 //   gate = mod[row_tok[m] * mod_ld + gate_off + n]
 // and, when `save` is set, save[m][n] = acc + bias (an [M][N] array) for the reverse pass.
-// 64 x 64 output tile per CTA, 4 x 4 outputs per thread, K in slabs of 32 staged through
-// shared memory (transposed, so the inner loop reads float4s). The next slab's global loads
-// are issued into registers before the current slab's FMAs (one slab in flight: the kernel
-// is bound by load latency at the planner's few hundred rows). VEC: 16-byte loads (K, lda
-// multiples of 4 and 16-byte aligned A / W), else scalar loads. Every output sums its K
-// products in increasing k, one fmaf each, whatever the grid.
-template <int EPI, bool VEC>
+// 64 x BN output tile per CTA (BN 64, or 32 where 64-wide tiles leave SMs idle), 4 x BN / 16
+// outputs per thread, K in slabs of 32 staged through shared memory (transposed, so the inner
+// loop reads float4s / float2s). The next slab's global loads are issued into registers
+// before the current slab's FMAs (one slab in flight: the kernel is bound by load latency at
+// the planner's few hundred rows). VEC: 16-byte loads (K, lda multiples of 4 and 16-byte
+// aligned A / W), else scalar loads. Every output sums its K products in increasing k, one
+// fmaf each, whatever the grid or the tile width.
+template <int EPI, bool VEC, int BN = GB_N>
 __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A, int lda, const float* __restrict__ W,
                                                      int K, const float* __restrict__ bias, float* __restrict__ C, int ldc,
                                                      int M, int N, const float* __restrict__ mod,
                                                      const int* __restrict__ row_tok, int mod_ld, int gate_off,
                                                      float* __restrict__ save, int kc, float* __restrict__ part) {
+  static_assert(BN == 64 || BN == 32, "tile width");
+  constexpr int TN = BN / 16;       // output columns per thread
+  constexpr int WV = BN / 32;       // W float4 loads per thread and slab (VEC)
   griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
   __shared__ __align__(16) float sA[GB_K][GB_M + 4];
-  __shared__ __align__(16) float sW[GB_K][GB_N + 4];
+  __shared__ __align__(16) float sW[GB_K][BN + 4];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const int m0 = blockIdx.y * GB_M, n0 = blockIdx.x * GB_N;
+  const int m0 = blockIdx.y * GB_M, n0 = blockIdx.x * BN;
   // K range of this CTA: all of K, or chunk blockIdx.z of kc (a multiple of GB_K) when split.
   const int kbeg = blockIdx.z * kc, kend = min(K, kbeg + kc);
-  // Per slab each thread moves 8 A values and 8 W values: VEC as 2 float4 (row s / 8,
-  // k 4 (s % 8)), scalar as 8 floats (row s / 32, k s % 32), s = tid + 256 q.
-  float ra[8], rw[8];
+  // Per slab each thread moves 8 A values and BN / 8 W values: VEC as float4s (row s / 8,
+  // k 4 (s % 8)), scalar as floats (row s / 32, k s % 32), s = tid + 256 q.
+  float ra[8], rw[BN / 8];
   auto load = [&](int k0) {
     if constexpr (VEC) {
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
         const int sl = tid + q * G_THREADS, r = sl >> 3, k = k0 + (sl & 7) * 4;
         const int m = m0 + r, n = n0 + r;
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), w = a;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
         if (m < M && k < kend) a = *reinterpret_cast<const float4*>(A + (size_t)m * lda + k);
-        if (n < N && k < kend) w = *reinterpret_cast<const float4*>(W + (size_t)n * K + k);
         ra[4 * q] = a.x, ra[4 * q + 1] = a.y, ra[4 * q + 2] = a.z, ra[4 * q + 3] = a.w;
-        rw[4 * q] = w.x, rw[4 * q + 1] = w.y, rw[4 * q + 2] = w.z, rw[4 * q + 3] = w.w;
+        if (q < WV) {
+          float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (n < N && k < kend) w = *reinterpret_cast<const float4*>(W + (size_t)n * K + k);
+          rw[4 * q] = w.x, rw[4 * q + 1] = w.y, rw[4 * q + 2] = w.z, rw[4 * q + 3] = w.w;
+        }
       }
     } else {
 #pragma unroll
@@ -111,7 +127,7 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
         const int sl = tid + q * G_THREADS, r = sl >> 5, k = k0 + (sl & 31);
         const int m = m0 + r, n = n0 + r;
         ra[q] = (m < M && k < kend) ? A[(size_t)m * lda + k] : 0.f;
-        rw[q] = (n < N && k < kend) ? W[(size_t)n * K + k] : 0.f;
+        if (q < BN / 8) rw[q] = (n < N && k < kend) ? W[(size_t)n * K + k] : 0.f;
       }
     }
   };
@@ -123,7 +139,7 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           sA[kk + j][slab_col(kk + j, r)] = ra[4 * q + j];
-          sW[kk + j][slab_col(kk + j, r)] = rw[4 * q + j];
+          if (q < WV) sW[kk + j][slab_col(kk + j, r)] = rw[4 * q + j];
         }
       }
     } else {
@@ -131,11 +147,11 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
       for (int q = 0; q < 8; ++q) {
         const int sl = tid + q * G_THREADS, r = sl >> 5, kk = sl & 31;
         sA[kk][slab_col(kk, r)] = ra[q];
-        sW[kk][slab_col(kk, r)] = rw[q];
+        if (q < BN / 8) sW[kk][slab_col(kk, r)] = rw[q];
       }
     }
   };
-  float acc[4][4] = {};
+  float acc[4][TN] = {};
   load(kbeg);
   store();
   __syncthreads();
@@ -145,12 +161,19 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
 #pragma unroll
     for (int kk = 0; kk < GB_K; ++kk) {
       const float4 a = *reinterpret_cast<const float4*>(&sA[kk][slab_col(kk, ty * 4)]);
-      const float4 b = *reinterpret_cast<const float4*>(&sW[kk][slab_col(kk, tx * 4)]);
-      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+      float bv[TN];
+      if constexpr (TN == 4) {
+        const float4 b = *reinterpret_cast<const float4*>(&sW[kk][slab_col(kk, tx * 4)]);
+        bv[0] = b.x, bv[1] = b.y, bv[2] = b.z, bv[3] = b.w;
+      } else {
+        const float2 b = *reinterpret_cast<const float2*>(&sW[kk][slab_col(kk, tx * 2)]);
+        bv[0] = b.x, bv[1] = b.y;
+      }
+      const float av[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
     __syncthreads();
     if (more) {
@@ -163,8 +186,8 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
     const int m = m0 + ty * 4 + i;
     if (m >= M) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = n0 + tx * 4 + j;
+    for (int j = 0; j < TN; ++j) {
+      const int n = n0 + tx * TN + j;
       if (n >= N) continue;
       if (part) {  // split K: this chunk's raw sum; k_splitk_resid32 applies the epilogue
         part[((size_t)blockIdx.z * M + m) * N + n] = acc[i][j];
@@ -507,7 +530,16 @@ cudaError_t sgemm(const float* A, int lda, const float* W, int K, const float* b
   const dim3 grid((N + GB_N - 1) / GB_N, (M + GB_M - 1) / GB_M, nz);
   float* pp = nz > 1 ? part : nullptr;
   const bool vec = K % 4 == 0 && lda % 4 == 0 && (reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W)) % 16 == 0;
-  if (vec)
+  if (narrow_tiles() && (size_t)grid.x * grid.y * grid.z < 148) {
+    // Fewer 64 x 64 tiles than SMs: 64 x 32 tiles, twice the CTAs (same bits).
+    const dim3 g32((N + 31) / 32, grid.y, grid.z);
+    if (vec)
+      F32_TRY(launch_f32(k_sgemm<EPI, true, 32>, g32, dim3(G_THREADS), 0, st, A, lda, W, K, bias, C, ldc, M, N, mod,
+                         row_tok, mod_ld, gate_off, save, kc, pp));
+    else
+      F32_TRY(launch_f32(k_sgemm<EPI, false, 32>, g32, dim3(G_THREADS), 0, st, A, lda, W, K, bias, C, ldc, M, N, mod,
+                         row_tok, mod_ld, gate_off, save, kc, pp));
+  } else if (vec)
     F32_TRY(launch_f32(k_sgemm<EPI, true>, dim3(grid), dim3(G_THREADS), 0, st, A, lda, W, K, bias, C, ldc, M, N, mod,
                      row_tok, mod_ld, gate_off, save, kc, pp));
   else
