@@ -33,8 +33,8 @@ bool fp32_pdl() {
   }();
   return on && pdl_enabled();
 }
-// 64 x 32 GEMM tiles where 64 x 64 ones number fewer than the SMs (LEWM_FP32_NARROW=0: never;
-// the results are the same bits either way).
+// 64 x 32 GEMM tiles where 64 x 64 ones number fewer than the SMs, 32 x 32 where 64 x 32 ones
+// fill fewer than half of them (LEWM_FP32_NARROW=0: never; the same bits either way).
 bool narrow_tiles() {
   static const bool on = [] {
     const char* v = std::getenv("LEWM_FP32_NARROW");
@@ -80,41 +80,45 @@ __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + e
 //   GE_GELU  C = gelu(acc + bias)            GE_RESID X += gate . (acc + bias), in place,
 //   gate = mod[row_tok[m] * mod_ld + gate_off + n]
 // and, when `save` is set, save[m][n] = acc + bias (an [M][N] array) for the reverse pass.
-// 64 x BN output tile per CTA (BN 64, or 32 where 64-wide tiles leave SMs idle), 4 x BN / 16
-// outputs per thread, K in slabs of 32 staged through shared memory (transposed, so the inner
-// loop reads float4s / float2s). The next slab's global loads are issued into registers
+// BM x BN output tile per CTA (64 x 64; 64 x 32 or 32 x 32 where larger tiles leave SMs idle),
+// BM / 16 x BN / 16 outputs per thread, K in slabs of 32 staged through shared memory
+// (transposed, so the inner loop reads float4s / float2s). The next slab's global loads are issued into registers
 // before the current slab's FMAs (one slab in flight: the kernel is bound by load latency at
 // the planner's few hundred rows). VEC: 16-byte loads (K, lda multiples of 4 and 16-byte
 // aligned A / W), else scalar loads. Every output sums its K products in increasing k, one
 // fmaf each, whatever the grid or the tile width.
-template <int EPI, bool VEC, int BN = GB_N>
+template <int EPI, bool VEC, int BN = GB_N, int BM = GB_M>
 __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A, int lda, const float* __restrict__ W,
                                                      int K, const float* __restrict__ bias, float* __restrict__ C, int ldc,
                                                      int M, int N, const float* __restrict__ mod,
                                                      const int* __restrict__ row_tok, int mod_ld, int gate_off,
                                                      float* __restrict__ save, int kc, float* __restrict__ part) {
-  static_assert(BN == 64 || BN == 32, "tile width");
+  static_assert((BN == 64 || BN == 32) && (BM == 64 || BM == 32), "tile shape");
   constexpr int TN = BN / 16;       // output columns per thread
+  constexpr int TM = BM / 16;       // output rows per thread
   constexpr int WV = BN / 32;       // W float4 loads per thread and slab (VEC)
+  constexpr int AV = BM / 32;       // A float4 loads per thread and slab (VEC)
   griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
-  __shared__ __align__(16) float sA[GB_K][GB_M + 4];
+  __shared__ __align__(16) float sA[GB_K][BM + 4];
   __shared__ __align__(16) float sW[GB_K][BN + 4];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const int m0 = blockIdx.y * GB_M, n0 = blockIdx.x * BN;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   // K range of this CTA: all of K, or chunk blockIdx.z of kc (a multiple of GB_K) when split.
   const int kbeg = blockIdx.z * kc, kend = min(K, kbeg + kc);
-  // Per slab each thread moves 8 A values and BN / 8 W values: VEC as float4s (row s / 8,
+  // Per slab each thread moves BM / 8 A values and BN / 8 W values: VEC as float4s (row s / 8,
   // k 4 (s % 8)), scalar as floats (row s / 32, k s % 32), s = tid + 256 q.
-  float ra[8], rw[BN / 8];
+  float ra[BM / 8], rw[BN / 8];
   auto load = [&](int k0) {
     if constexpr (VEC) {
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
         const int sl = tid + q * G_THREADS, r = sl >> 3, k = k0 + (sl & 7) * 4;
         const int m = m0 + r, n = n0 + r;
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (m < M && k < kend) a = *reinterpret_cast<const float4*>(A + (size_t)m * lda + k);
-        ra[4 * q] = a.x, ra[4 * q + 1] = a.y, ra[4 * q + 2] = a.z, ra[4 * q + 3] = a.w;
+        if (q < AV) {
+          float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (m < M && k < kend) a = *reinterpret_cast<const float4*>(A + (size_t)m * lda + k);
+          ra[4 * q] = a.x, ra[4 * q + 1] = a.y, ra[4 * q + 2] = a.z, ra[4 * q + 3] = a.w;
+        }
         if (q < WV) {
           float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
           if (n < N && k < kend) w = *reinterpret_cast<const float4*>(W + (size_t)n * K + k);
@@ -126,7 +130,7 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
       for (int q = 0; q < 8; ++q) {
         const int sl = tid + q * G_THREADS, r = sl >> 5, k = k0 + (sl & 31);
         const int m = m0 + r, n = n0 + r;
-        ra[q] = (m < M && k < kend) ? A[(size_t)m * lda + k] : 0.f;
+        if (q < BM / 8) ra[q] = (m < M && k < kend) ? A[(size_t)m * lda + k] : 0.f;
         if (q < BN / 8) rw[q] = (n < N && k < kend) ? W[(size_t)n * K + k] : 0.f;
       }
     }
@@ -138,7 +142,7 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
         const int sl = tid + q * G_THREADS, r = sl >> 3, kk = (sl & 7) * 4;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          sA[kk + j][slab_col(kk + j, r)] = ra[4 * q + j];
+          if (q < AV) sA[kk + j][slab_col(kk + j, r)] = ra[4 * q + j];
           if (q < WV) sW[kk + j][slab_col(kk + j, r)] = rw[4 * q + j];
         }
       }
@@ -146,12 +150,12 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const int sl = tid + q * G_THREADS, r = sl >> 5, kk = sl & 31;
-        sA[kk][slab_col(kk, r)] = ra[q];
+        if (q < BM / 8) sA[kk][slab_col(kk, r)] = ra[q];
         if (q < BN / 8) sW[kk][slab_col(kk, r)] = rw[q];
       }
     }
   };
-  float acc[4][TN] = {};
+  float acc[TM][TN] = {};
   load(kbeg);
   store();
   __syncthreads();
@@ -160,8 +164,14 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
     if (more) load(k0 + GB_K);
 #pragma unroll
     for (int kk = 0; kk < GB_K; ++kk) {
-      const float4 a = *reinterpret_cast<const float4*>(&sA[kk][slab_col(kk, ty * 4)]);
-      float bv[TN];
+      float av[TM], bv[TN];
+      if constexpr (TM == 4) {
+        const float4 a = *reinterpret_cast<const float4*>(&sA[kk][slab_col(kk, ty * 4)]);
+        av[0] = a.x, av[1] = a.y, av[2] = a.z, av[3] = a.w;
+      } else {
+        const float2 a = *reinterpret_cast<const float2*>(&sA[kk][slab_col(kk, ty * 2)]);
+        av[0] = a.x, av[1] = a.y;
+      }
       if constexpr (TN == 4) {
         const float4 b = *reinterpret_cast<const float4*>(&sW[kk][slab_col(kk, tx * 4)]);
         bv[0] = b.x, bv[1] = b.y, bv[2] = b.z, bv[3] = b.w;
@@ -169,9 +179,8 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
         const float2 b = *reinterpret_cast<const float2*>(&sW[kk][slab_col(kk, tx * 2)]);
         bv[0] = b.x, bv[1] = b.y;
       }
-      const float av[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < TM; ++i)
 #pragma unroll
         for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
@@ -182,8 +191,8 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm(const float* __restrict__ A
     }
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int m = m0 + ty * 4 + i;
+  for (int i = 0; i < TM; ++i) {
+    const int m = m0 + ty * TM + i;
     if (m >= M) continue;
 #pragma unroll
     for (int j = 0; j < TN; ++j) {
@@ -530,15 +539,24 @@ cudaError_t sgemm(const float* A, int lda, const float* W, int K, const float* b
   const dim3 grid((N + GB_N - 1) / GB_N, (M + GB_M - 1) / GB_M, nz);
   float* pp = nz > 1 ? part : nullptr;
   const bool vec = K % 4 == 0 && lda % 4 == 0 && (reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W)) % 16 == 0;
-  if (narrow_tiles() && (size_t)grid.x * grid.y * grid.z < 148) {
-    // Fewer 64 x 64 tiles than SMs: 64 x 32 tiles, twice the CTAs (same bits).
-    const dim3 g32((N + 31) / 32, grid.y, grid.z);
+  const dim3 g6432((N + 31) / 32, grid.y, grid.z), g3232(g6432.x, (M + 31) / 32, grid.z);
+  if (narrow_tiles() && (size_t)g6432.x * g6432.y * g6432.z < 74) {
+    // 64 x 32 tiles would fill fewer than half the SMs: 32 x 32 tiles (same bits). At 120
+    // tiles of 64 x 32 (FC1 and the residual GEMMs of 300 rows) 32 x 32 measured slower.
     if (vec)
-      F32_TRY(launch_f32(k_sgemm<EPI, true, 32>, g32, dim3(G_THREADS), 0, st, A, lda, W, K, bias, C, ldc, M, N, mod,
+      F32_TRY(launch_f32(k_sgemm<EPI, true, 32, 32>, g3232, dim3(G_THREADS), 0, st, A, lda, W, K, bias, C, ldc, M, N,
+                         mod, row_tok, mod_ld, gate_off, save, kc, pp));
+    else
+      F32_TRY(launch_f32(k_sgemm<EPI, false, 32, 32>, g3232, dim3(G_THREADS), 0, st, A, lda, W, K, bias, C, ldc, M,
+                         N, mod, row_tok, mod_ld, gate_off, save, kc, pp));
+  } else if (narrow_tiles() && (size_t)grid.x * grid.y * grid.z < 148) {
+    // Fewer 64 x 64 tiles than SMs: 64 x 32 tiles, twice the CTAs (same bits).
+    if (vec)
+      F32_TRY(launch_f32(k_sgemm<EPI, true, 32>, g6432, dim3(G_THREADS), 0, st, A, lda, W, K, bias, C, ldc, M, N, mod,
                          row_tok, mod_ld, gate_off, save, kc, pp));
     else
-      F32_TRY(launch_f32(k_sgemm<EPI, false, 32>, g32, dim3(G_THREADS), 0, st, A, lda, W, K, bias, C, ldc, M, N, mod,
-                         row_tok, mod_ld, gate_off, save, kc, pp));
+      F32_TRY(launch_f32(k_sgemm<EPI, false, 32>, g6432, dim3(G_THREADS), 0, st, A, lda, W, K, bias, C, ldc, M, N,
+                         mod, row_tok, mod_ld, gate_off, save, kc, pp));
   } else if (vec)
     F32_TRY(launch_f32(k_sgemm<EPI, true>, dim3(grid), dim3(G_THREADS), 0, st, A, lda, W, K, bias, C, ldc, M, N, mod,
                      row_tok, mod_ld, gate_off, save, kc, pp));
