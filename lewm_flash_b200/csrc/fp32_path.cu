@@ -683,40 +683,52 @@ __device__ __forceinline__ float silu_grad(float x) {
 // [out][in] weight, so C = dY . W is the input gradient of y = x . W^T), then the epilogue:
 // NE_STORE C = acc; NE_GELU_BWD / NE_SILU_BWD C = acc * f'(pre[m][c]). Same tiling, slab
 // prefetch and fixed summation order as k_sgemm; VEC: 16-byte loads of A and Bm.
-template <int EPI, bool VEC>
+template <int EPI, bool VEC, int BN = GB_N, int BM = GB_M>
 __global__ void __launch_bounds__(G_THREADS) k_sgemm_nn(const float* __restrict__ A, int lda, const float* __restrict__ Bm,
                                                         int Nin, int Kout, float* __restrict__ C, int ldc, int M,
                                                         const float* __restrict__ pre, int ldp, int kc,
                                                         float* __restrict__ part) {
+  static_assert((BN == 64 || BN == 32) && (BM == 64 || BM == 32), "tile shape");
+  constexpr int TN = BN / 16, TM = BM / 16;  // outputs per thread
+  constexpr int AV = BM / 32, BV = BN / 32;  // float4 loads per thread and slab (VEC)
+  constexpr int BQ = BN / 4;                 // float4s per Bm row of the tile
   griddep_wait();  // launched as a programmatic dependent: wait for the kernel before
-  __shared__ __align__(16) float sA[GB_K][GB_M + 4];
-  __shared__ __align__(16) float sB[GB_K][GB_N + 4];
+  __shared__ __align__(16) float sA[GB_K][BM + 4];
+  __shared__ __align__(16) float sB[GB_K][BN + 4];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const int m0 = blockIdx.y * GB_M, c0 = blockIdx.x * GB_N;
+  const int m0 = blockIdx.y * BM, c0 = blockIdx.x * BN;
   const int nbeg = blockIdx.z * kc, nend = min(Nin, nbeg + kc);  // reduction chunk of this CTA
-  float ra[8], rb[8];
+  float ra[BM / 8], rb[BN / 8];
   auto load = [&](int n0) {
     if constexpr (VEC) {
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
         const int sl = tid + q * G_THREADS;
-        const int r = sl >> 3, n = n0 + (sl & 7) * 4, m = m0 + r;
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (m < M && n < nend) a = *reinterpret_cast<const float4*>(A + (size_t)m * lda + n);
-        ra[4 * q] = a.x, ra[4 * q + 1] = a.y, ra[4 * q + 2] = a.z, ra[4 * q + 3] = a.w;
-        const int rr = sl >> 4, c = c0 + (sl & 15) * 4, nb = n0 + rr;
-        float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (nb < nend && c < Kout) b = *reinterpret_cast<const float4*>(Bm + (size_t)nb * Kout + c);
-        rb[4 * q] = b.x, rb[4 * q + 1] = b.y, rb[4 * q + 2] = b.z, rb[4 * q + 3] = b.w;
+        if (q < AV) {
+          const int r = sl >> 3, n = n0 + (sl & 7) * 4, m = m0 + r;
+          float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (m < M && n < nend) a = *reinterpret_cast<const float4*>(A + (size_t)m * lda + n);
+          ra[4 * q] = a.x, ra[4 * q + 1] = a.y, ra[4 * q + 2] = a.z, ra[4 * q + 3] = a.w;
+        }
+        if (q < BV) {
+          const int rr = sl / BQ, c = c0 + (sl % BQ) * 4, nb = n0 + rr;
+          float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (nb < nend && c < Kout) b = *reinterpret_cast<const float4*>(Bm + (size_t)nb * Kout + c);
+          rb[4 * q] = b.x, rb[4 * q + 1] = b.y, rb[4 * q + 2] = b.z, rb[4 * q + 3] = b.w;
+        }
       }
     } else {
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const int sl = tid + q * G_THREADS;
-        const int r = sl >> 5, n = n0 + (sl & 31), m = m0 + r;
-        ra[q] = (m < M && n < nend) ? A[(size_t)m * lda + n] : 0.f;
-        const int rr = sl >> 6, c = c0 + (sl & 63), nb = n0 + rr;
-        rb[q] = (nb < nend && c < Kout) ? Bm[(size_t)nb * Kout + c] : 0.f;
+        if (q < BM / 8) {
+          const int r = sl >> 5, n = n0 + (sl & 31), m = m0 + r;
+          ra[q] = (m < M && n < nend) ? A[(size_t)m * lda + n] : 0.f;
+        }
+        if (q < BN / 8) {
+          const int rr = sl / BN, c = c0 + (sl % BN), nb = n0 + rr;
+          rb[q] = (nb < nend && c < Kout) ? Bm[(size_t)nb * Kout + c] : 0.f;
+        }
       }
     }
   };
@@ -725,21 +737,25 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm_nn(const float* __restrict_
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
         const int sl = tid + q * G_THREADS;
-        const int r = sl >> 3, kk = (sl & 7) * 4, rr = sl >> 4, cc = (sl & 15) * 4;
+        if (q < AV) {
+          const int r = sl >> 3, kk = (sl & 7) * 4;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) sA[kk + j][slab_col(kk + j, r)] = ra[4 * q + j];
-        *reinterpret_cast<float4*>(&sB[rr][cc]) = make_float4(rb[4 * q], rb[4 * q + 1], rb[4 * q + 2], rb[4 * q + 3]);
+          for (int j = 0; j < 4; ++j) sA[kk + j][slab_col(kk + j, r)] = ra[4 * q + j];
+        }
+        if (q < BV)
+          *reinterpret_cast<float4*>(&sB[sl / BQ][(sl % BQ) * 4]) =
+              make_float4(rb[4 * q], rb[4 * q + 1], rb[4 * q + 2], rb[4 * q + 3]);
       }
     } else {
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const int sl = tid + q * G_THREADS;
-        sA[sl & 31][slab_col(sl & 31, sl >> 5)] = ra[q];
-        sB[sl >> 6][sl & 63] = rb[q];
+        if (q < BM / 8) sA[sl & 31][slab_col(sl & 31, sl >> 5)] = ra[q];
+        if (q < BN / 8) sB[sl / BN][sl % BN] = rb[q];
       }
     }
   };
-  float acc[4][4] = {};
+  float acc[TM][TN] = {};
   load(nbeg);
   store();
   __syncthreads();
@@ -748,13 +764,25 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm_nn(const float* __restrict_
     if (more) load(n0 + GB_K);
 #pragma unroll
     for (int kk = 0; kk < GB_K; ++kk) {
-      const float4 a = *reinterpret_cast<const float4*>(&sA[kk][slab_col(kk, ty * 4)]);
-      const float4 b = *reinterpret_cast<const float4*>(&sB[kk][tx * 4]);
-      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+      float av[TM], bv[TN];
+      if constexpr (TM == 4) {
+        const float4 a = *reinterpret_cast<const float4*>(&sA[kk][slab_col(kk, ty * 4)]);
+        av[0] = a.x, av[1] = a.y, av[2] = a.z, av[3] = a.w;
+      } else {
+        const float2 a = *reinterpret_cast<const float2*>(&sA[kk][slab_col(kk, ty * 2)]);
+        av[0] = a.x, av[1] = a.y;
+      }
+      if constexpr (TN == 4) {
+        const float4 b = *reinterpret_cast<const float4*>(&sB[kk][tx * 4]);
+        bv[0] = b.x, bv[1] = b.y, bv[2] = b.z, bv[3] = b.w;
+      } else {
+        const float2 b = *reinterpret_cast<const float2*>(&sB[kk][tx * 2]);
+        bv[0] = b.x, bv[1] = b.y;
+      }
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < TM; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
     __syncthreads();
     if (more) {
@@ -763,12 +791,12 @@ __global__ void __launch_bounds__(G_THREADS) k_sgemm_nn(const float* __restrict_
     }
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int m = m0 + ty * 4 + i;
+  for (int i = 0; i < TM; ++i) {
+    const int m = m0 + ty * TM + i;
     if (m >= M) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int c = c0 + tx * 4 + j;
+    for (int j = 0; j < TN; ++j) {
+      const int c = c0 + tx * TN + j;
       if (c >= Kout) continue;
       if (part) {  // split reduction: this chunk's raw sum; k_splitk_nn32 finishes
         part[((size_t)blockIdx.z * M + m) * Kout + c] = acc[i][j];
@@ -817,7 +845,23 @@ cudaError_t sgemm_nn(const float* A, int lda, const float* Bm, int Nin, int Kout
   const dim3 grid((Kout + GB_N - 1) / GB_N, (M + GB_M - 1) / GB_M, nz);
   const bool vec = Nin % 4 == 0 && lda % 4 == 0 && Kout % 4 == 0 &&
                    (reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(Bm)) % 16 == 0;
-  if (vec)
+  // Narrower tiles on grids that leave SMs idle, as in sgemm (same bits).
+  const dim3 g6432((Kout + 31) / 32, grid.y, nz), g3232(g6432.x, (M + 31) / 32, nz);
+  if (narrow_tiles() && (size_t)g6432.x * g6432.y * g6432.z < 74) {
+    if (vec)
+      F32_TRY(launch_f32(k_sgemm_nn<EPI, true, 32, 32>, g3232, dim3(G_THREADS), 0, st, A, lda, Bm, Nin, Kout, C, ldc,
+                         M, pre, ldp, kc, pp));
+    else
+      F32_TRY(launch_f32(k_sgemm_nn<EPI, false, 32, 32>, g3232, dim3(G_THREADS), 0, st, A, lda, Bm, Nin, Kout, C,
+                         ldc, M, pre, ldp, kc, pp));
+  } else if (narrow_tiles() && (size_t)grid.x * grid.y * grid.z < 148) {
+    if (vec)
+      F32_TRY(launch_f32(k_sgemm_nn<EPI, true, 32>, g6432, dim3(G_THREADS), 0, st, A, lda, Bm, Nin, Kout, C, ldc, M,
+                         pre, ldp, kc, pp));
+    else
+      F32_TRY(launch_f32(k_sgemm_nn<EPI, false, 32>, g6432, dim3(G_THREADS), 0, st, A, lda, Bm, Nin, Kout, C, ldc,
+                         M, pre, ldp, kc, pp));
+  } else if (vec)
     F32_TRY(launch_f32(k_sgemm_nn<EPI, true>, dim3(grid), dim3(G_THREADS), 0, st, A, lda, Bm, Nin, Kout, C, ldc, M,
                      pre, ldp, kc, pp));
   else
