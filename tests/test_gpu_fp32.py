@@ -268,3 +268,44 @@ def test_fp32_random_shapes_match_oracle(seed):
 
 
 _SHARED = {}
+
+
+_FP32_TILES = """
+import sys, numpy as np, torch
+from lewm_flash_b200.model import ModelDesc, synthetic_state_dict
+from lewm_flash_b200.runtime import Runtime
+d = np.load(sys.argv[1])
+desc = ModelDesc()
+rt = Runtime(desc, synthetic_state_dict(desc, 0), "cuda:0", model_cost_autocast="none")
+t = lambda x: torch.as_tensor(x, device="cuda:0")
+cost = rt.model_cost(t(d["emb"]), t(d["goal"]), t(d["cand"])).cpu().numpy()
+gc, gg = rt.model_cost_grad(t(d["emb"]), t(d["goal"]), t(d["cand"][:, :30]))
+rt.sync()
+np.save(sys.argv[2], np.concatenate([cost.ravel(), gc.cpu().numpy().ravel(), gg.cpu().numpy().ravel()]))
+"""
+
+
+@pytest.mark.parametrize("S,H", [(300, 1), (40, 3)])
+def test_fp32_gemm_tile_shape_does_not_change_bits(tmp_path, S, H):
+    # Small GEMM grids run 64 x 32 or 32 x 32 tiles instead of 64 x 64 (forward and reverse
+    # pass). Every output keeps its k order, so a process with LEWM_FP32_NARROW=0 (64 x 64
+    # tiles everywhere) gives the same costs and gradients bit for bit.
+    import os
+    import subprocess
+    import sys
+
+    rng = np.random.default_rng(S + H)
+    desc = ModelDesc()
+    np.savez(tmp_path / "in.npz", emb=rng.standard_normal((1, H, desc.dim)).astype(np.float32),
+             goal=rng.standard_normal((1, 1, desc.dim)).astype(np.float32),
+             cand=rng.standard_normal((1, S, 5, desc.action_dim)).astype(np.float32))
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    outs = []
+    for flag in ("1", "0"):
+        env = dict(os.environ, LEWM_FP32_NARROW=flag)
+        env["PYTHONPATH"] = root + os.pathsep + env.get("PYTHONPATH", "")
+        out = tmp_path / f"out{flag}.npy"
+        subprocess.run([sys.executable, "-c", _FP32_TILES, str(tmp_path / "in.npz"), str(out)], env=env, cwd=root,
+                       check=True, timeout=600)
+        outs.append(np.load(out))
+    assert np.array_equal(outs[0], outs[1])
