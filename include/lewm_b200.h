@@ -6,7 +6,14 @@
  * contiguous row-major float32. Calls are asynchronous on the given stream
  * (a cudaStream_t passed as void*; NULL = legacy default stream) and the
  * caller owns every buffer. One context per device; a context is not
- * thread-safe without external locking.
+ * thread-safe without external locking, and its calls share its workspace, so
+ * calls on one context must be ordered on the GPU (one stream, or streams the
+ * caller orders with events).
+ *
+ * lewm_plan (without a trace or injected noise) and lewm_model_cost_grad capture
+ * their launches into a CUDA graph on the first call of each shape, on a stream
+ * of the context, and replay that graph on later calls (LEWM_NO_GRAPH=1 turns
+ * this off): do not call them while the given stream is being captured.
  *
  * The reference (antoinenguyen27/lewm-flash) is pure PyTorch and has no FFI;
  * each entry point below replaces one Python interface of its planning path,
