@@ -266,7 +266,7 @@ class Runtime:
             plan_index = self.plans_issued
         self.plans_issued += 1
         pd = opts.to_c(B, T, int(e.shape[1]), plan_index)
-        counts = sample_counts(opts, T, B)
+        counts = sample_counts(opts, T, B) if noise_steps is not None or trace else None
         keep = []
         noise_arr = None
         if noise_steps is not None:

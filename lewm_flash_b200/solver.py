@@ -301,6 +301,10 @@ class B200ICEMSolver:
     def _plan(self, info_dict: dict, mean: torch.Tensor, var: torch.Tensor, trace: bool, emb_goal=None):
         total_envs = mean.shape[0]
         emb, goal = emb_goal if emb_goal is not None else self._cost_embeddings(info_dict, total_envs)
+        # Host embeddings go up without blocking the host: the solve synchronises the stream
+        # before it returns, so the caller's buffers are read before they can change.
+        emb = emb.to(self.device, torch.float32, non_blocking=True)
+        goal = goal.to(self.device, torch.float32, non_blocking=True)
         rt = self.runtime
         opts = self.plan_options()
         plan_index = self._solves
@@ -323,19 +327,35 @@ class B200ICEMSolver:
         actions, std, fcost, tr = self._plan(info_dict, mean, var, trace=bool(self.callbacks))
         if self.callbacks:
             self._replay_callbacks(tr, mean, var)
-        # One device->host read per solve (reference lewm/solvers/icem.py:589-593).
-        outputs["costs"].extend(fcost.cpu().tolist())
+        # One device->host read per solve (reference lewm/solvers/icem.py:589-593): the three
+        # outputs are queued into pinned host buffers on the plan's stream, then one sync.
+        h_cost, h_act, h_std = self._host_outputs(actions, std, fcost)
+        h_cost.copy_(fcost, non_blocking=True)
+        h_act.copy_(actions, non_blocking=True)
+        h_std.copy_(std, non_blocking=True)
         self.runtime.sync()
-        actions_cpu = actions.detach().cpu()
+        outputs["costs"].extend(h_cost.tolist())
+        actions_cpu = h_act.clone()
         outputs["actions"] = actions_cpu
         outputs["mean"] = [actions_cpu.clone()]
-        outputs["var"] = [std.detach().cpu()]
+        outputs["var"] = [h_std.clone()]
         if self.callbacks:
             outputs["callbacks"] = {}
             for cb in self.callbacks:
                 cb.end_solve()
                 outputs["callbacks"][cb.output_key] = cb.history
         return outputs
+
+    def _host_outputs(self, actions: torch.Tensor, std: torch.Tensor, fcost: torch.Tensor):
+        """Pinned host buffers for a solve's final cost, actions and std, kept per shape (the
+        results are cloned out of them before ``solve`` returns)."""
+        cache = self.__dict__.setdefault("_host_out", {})
+        key = (tuple(actions.shape), tuple(fcost.shape))
+        if key not in cache:
+            cache[key] = (torch.empty(fcost.shape, dtype=torch.float32, pin_memory=True),
+                          torch.empty(actions.shape, dtype=torch.float32, pin_memory=True),
+                          torch.empty(std.shape, dtype=torch.float32, pin_memory=True))
+        return cache[key]
 
     _callback_n_samples = True  # ICEMSolver passes n_samples to its callbacks; CEMExactSolver does not
 
